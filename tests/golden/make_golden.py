@@ -1,0 +1,211 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs ONLY where the reference checkout is mounted (default ``/root/reference``,
+override with ``QW_REFERENCE``); the committed ``*.npz`` files are what the tests
+read, on any machine.  Nothing here is imported by the library.
+
+Fixtures:
+  ops_fp32.npz        reference/fused_ops.py functions on seeded float32 inputs
+  ops_lowp.npz        the same functions on bf16 / fp16 inputs (rounding points)
+  topk.npz            torch.topk on tie-heavy float32 rows (the router's selection)
+  tiny_session.npz    FusedTargetModel + FusedTargetSession (fp16, fp32 recurrent
+                      state) on the tiny configuration: greedy decode, then
+                      block verify / commit rounds with seeded proposals.
+
+Usage:  python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("QW_REFERENCE", "/root/reference")
+
+
+def _import_reference():
+    for sub in ("model", "reference"):
+        path = os.path.join(REF, sub)
+        if path not in sys.path:
+            sys.path.insert(0, path)
+    import fused_ops  # reference/fused_ops.py
+    from qwen35_moe_dflash.fused.ops import ModuleFusedOps
+    from qwen35_moe_dflash.fused.model import FusedTargetModel
+    from qwen35_moe_dflash.fused.session import FusedTargetSession
+    return fused_ops, ModuleFusedOps, FusedTargetModel, FusedTargetSession
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().numpy()
+
+
+def make_ops(fused_ops):
+    g = torch.Generator().manual_seed(1234)
+    out = {}
+
+    def rn(*shape, std=1.0, dtype=torch.float32):
+        return (torch.randn(*shape, generator=g) * std).to(dtype)
+
+    for tag, dtype in (("f32", torch.float32), ("bf16", torch.bfloat16), ("f16", torch.float16)):
+        d = {}
+        # rms_norm [3,5,64] and [7,256]
+        for i, shape in enumerate(((3, 5, 64), (7, 256))):
+            x = rn(*shape, dtype=dtype)
+            gamma = (1 + rn(shape[-1], std=0.1)).to(dtype)
+            d[f"rms{i}_x"], d[f"rms{i}_g"] = _np(x), _np(gamma)
+            d[f"rms{i}_y"] = _np(fused_ops.rms_norm(x, gamma, 1e-6))
+        # conv_state_update + causal_conv1d: B=2, S=5, C=24, K=4
+        proj = rn(2, 5, 24, dtype=dtype)
+        hist = rn(2, 24, 3, dtype=dtype)
+        w = rn(24, 1, 4, std=0.3, dtype=dtype)
+        new_hist, padded = fused_ops.conv_state_update(proj, hist)
+        d["conv_proj"], d["conv_hist"], d["conv_w"] = _np(proj), _np(hist), _np(w)
+        d["conv_newhist"], d["conv_padded"] = _np(new_hist), _np(padded)
+        d["conv_out"] = _np(fused_ops.causal_conv1d(padded, w))
+        # cache_update
+        k0, v0 = rn(2, 2, 7, 16, dtype=dtype), rn(2, 2, 7, 16, dtype=dtype)
+        k1, v1 = rn(2, 2, 3, 16, dtype=dtype), rn(2, 2, 3, 16, dtype=dtype)
+        kk, vv = fused_ops.cache_update(k0, v0, k1, v1)
+        d["cache_k0"], d["cache_v0"], d["cache_k1"], d["cache_v1"] = map(_np, (k0, v0, k1, v1))
+        d["cache_k"], d["cache_v"] = _np(kk), _np(vv)
+        # attention: B=2, H=8, Hkv=2, S=5, T=13, D=32
+        q = rn(2, 8, 5, 32, dtype=dtype)
+        kc, vc = rn(2, 2, 13, 32, dtype=dtype), rn(2, 2, 13, 32, dtype=dtype)
+        d["attn_q"], d["attn_k"], d["attn_v"] = _np(q), _np(kc), _np(vc)
+        d["attn_o"] = _np(fused_ops.attention(q, kc, vc, query_start=8, scale=32 ** -0.5))
+        # moe: T=2x5 tokens, H=64, E=16, I=32, top-4; router rows coarsened to force ties
+        hidden = rn(2, 5, 64, dtype=dtype)
+        router = (torch.round(rn(16, 64, std=0.5) * 4) / 4).to(dtype)
+        gate_up = rn(16, 64, 64, std=0.125, dtype=dtype)
+        down = rn(16, 64, 32, std=0.125, dtype=dtype)
+        d["moe_x"], d["moe_router"], d["moe_gu"], d["moe_down"] = map(_np, (hidden, router, gate_up, down))
+        d["moe_y"] = _np(fused_ops.moe(hidden, router, gate_up, down, top_k=4))
+        out[tag] = d
+    # gated delta rule: fp32 and fp16 only (the reference rejects bf16)
+    for tag, dtype in (("f32", torch.float32), ("f16", torch.float16)):
+        d = out[tag]
+        b, s, h, dk, dv = 3, 6, 4, 16, 24
+        q, k = rn(b, s, h, dk, dtype=dtype), rn(b, s, h, dk, dtype=dtype)
+        v = rn(b, s, h, dv, dtype=dtype)
+        gg = (-torch.nn.functional.softplus(rn(b, s, h))).to(dtype)
+        beta = torch.sigmoid(rn(b, s, h)).to(dtype)
+        state = rn(b, h, dk, dv, std=0.1)
+        length = torch.tensor([6, 0, 4], dtype=torch.int16)
+        for norm in (True, False):
+            core, st = fused_ops.chunk_gated_delta_rule(
+                q, k, v, gg, beta, state, length, chunk_size=64, use_qk_l2norm_in_kernel=norm)
+            d[f"gdn_core_{int(norm)}"], d[f"gdn_state_{int(norm)}"] = _np(core), _np(st)
+        d["gdn_q"], d["gdn_k"], d["gdn_v"], d["gdn_g"], d["gdn_beta"] = map(_np, (q, k, v, gg, beta))
+        d["gdn_s0"], d["gdn_len"] = _np(state), length.numpy()
+    np.savez_compressed(os.path.join(HERE, "ops_fp32.npz"), **out["f32"])
+    np.savez_compressed(os.path.join(HERE, "ops_lowp.npz"),
+                        **{f"bf16_{k}": v for k, v in out["bf16"].items()},
+                        **{f"f16_{k}": v for k, v in out["f16"].items()})
+
+
+def make_topk():
+    g = torch.Generator().manual_seed(99)
+    out = {}
+    for e, k in ((256, 8), (16, 4), (64, 6), (256, 1), (128, 8)):
+        logits = torch.randn(256, e, generator=g)
+        logits[::3] = torch.randint(-3, 3, (len(range(0, 256, 3)), e), generator=g).float()
+        logits = logits.to(torch.bfloat16)
+        probs = torch.softmax(logits.float(), -1)
+        _, idx = torch.topk(probs, k, dim=-1)
+        out[f"p_{e}_{k}"] = probs.numpy()
+        out[f"i_{e}_{k}"] = idx.numpy().astype(np.int16)
+    np.savez_compressed(os.path.join(HERE, "topk.npz"), **out)
+
+
+def make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops):
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    from qwen35_dflash_b200 import config as qcfg, synthetic
+    from oracle.numerics import quantize_w4, dequantize_w4
+
+    cfg = qcfg.TINY
+    raw = synthetic.init_weights(cfg, seed=17)
+    weights = {}
+    for name, value in raw.items():
+        if synthetic.is_w4(name):
+            q, s = quantize_w4(value, cfg.quant_group)
+            value = dequantize_w4(q, s, cfg.quant_group)
+        weights[name] = torch.from_numpy(value).to(torch.float16)
+    ops = ModuleFusedOps(fused_ops, allow_reference=True)
+    model = FusedTargetModel(cfg.to_hf_text_config(), weights, feature_layers=cfg.feature_layers,
+                             ops=ops, recurrent_dtype=torch.float32)
+    prompt = np.random.default_rng(17).integers(0, cfg.vocab_size, 64).tolist()
+    # every layer's output on the prompt (teacher-forced per-layer pin)
+    all_layers = tuple(range(cfg.num_hidden_layers))
+    probe = FusedTargetModel(cfg.to_hf_text_config(), weights, feature_layers=all_layers,
+                             ops=ops, recurrent_dtype=torch.float32)
+    layer_hidden = probe(torch.tensor([prompt])).features[0].reshape(64, cfg.num_hidden_layers, -1)
+    layer_hidden = layer_hidden.permute(1, 0, 2).numpy().astype(np.float16)
+    # layer outputs of the last layer are replaced by the final norm; keep the raw one too
+    last = probe._forward_hidden  # noqa: F841  (documented behaviour, fused/model.py:407-409)
+    # ordinary greedy decode: G[i] = prediction after prompt + G[:i]
+    session = FusedTargetSession(model)
+    session.prefill(prompt)
+    greedy = [session.next_token]
+    for _ in range(79):
+        session.step(greedy[-1])
+        greedy.append(session.next_token)
+    # block verify rounds with seeded proposals
+    session = FusedTargetSession(model)
+    pre = session.prefill(prompt)
+    rng = np.random.default_rng(5)
+    committed = 0
+    rounds = {"proposals": [], "expected": [], "accepted": [], "features": []}
+    corrupt_at = [3, 16, 1, 9, 15, 5, 12, 2]
+    for j in corrupt_at:
+        if committed + 16 > len(greedy):
+            break
+        props = list(greedy[committed:committed + 16])
+        if j < 16:
+            props[j] = int((props[j] + 1 + rng.integers(0, cfg.vocab_size - 1)) % cfg.vocab_size)
+        verification = session.verify(props)
+        accepted = verification.max_accepted_prefix
+        rounds["proposals"].append(props)
+        rounds["expected"].append(list(verification.expected_next_tokens))
+        rounds["accepted"].append(accepted)
+        feats = torch.cat([f for _, f in verification._snapshots[1:]], dim=1)[0]
+        rounds["features"].append(feats.float().numpy())
+        verification.commit(accepted)
+        committed += accepted
+    state = session.state
+    sums = []
+    for layer in state.layers:
+        for name in ("conv", "recurrent", "key", "value"):
+            t = getattr(layer, name)
+            if t is not None:
+                sums.append([float(t.double().sum()), float(t.double().square().sum())])
+    np.savez_compressed(
+        os.path.join(HERE, "tiny_session.npz"),
+        prompt=np.asarray(prompt, np.int32), greedy=np.asarray(greedy, np.int32),
+        layer_hidden=layer_hidden,
+        prefill_features=pre.features[0].float().numpy().astype(np.float16),
+        proposals=np.asarray(rounds["proposals"], np.int32),
+        expected=np.asarray(rounds["expected"], np.int32),
+        accepted=np.asarray(rounds["accepted"], np.int32),
+        features=np.asarray(rounds["features"], np.float16),
+        final_position=np.int32(state.position), state_sums=np.asarray(sums, np.float64))
+
+
+def main():
+    fused_ops, ModuleFusedOps, FusedTargetModel, FusedTargetSession = _import_reference()
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    make_ops(fused_ops)
+    make_topk()
+    make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops)
+    for name in sorted(os.listdir(HERE)):
+        if name.endswith(".npz"):
+            print(name, os.path.getsize(os.path.join(HERE, name)))
+
+
+if __name__ == "__main__":
+    main()
