@@ -1,0 +1,190 @@
+/*
+ * qw_b200.h — C ABI of libqw_b200.so, the sm_100a kernels of the Qwen3.5-MoE
+ * block-verify path.
+ *
+ * Conventions (all entry points):
+ *   - pointers are DEVICE pointers unless stated otherwise; sizes are element
+ *     counts; every tensor is dense row-major in the shape given;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - the return value is a qw_status; on failure qw_last_error() returns a
+ *     thread-local message.  Arguments are validated on the host before any
+ *     launch; nothing is allocated, and no entry point synchronizes the stream;
+ *   - outputs are written only through the output pointers named in each
+ *     signature; inputs are never written (the engine entry points document the
+ *     state banks they update in place).
+ *
+ * Each function names the reference interface it replaces (paths relative to the
+ * reference checkout).  The seven operators of the reference's fused-ops adapter
+ * ABI (model/qwen35_moe_dflash/fused/ops.py:24-123, implemented on the host by
+ * reference/fused_ops.py:28-173) keep their argument meaning.
+ */
+#ifndef QW_B200_H
+#define QW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+/* bfloat16 storage in structs: __nv_bfloat16 for CUDA code, its 16-bit pattern in C. */
+#if defined(__CUDACC__)
+#include <cuda_bf16.h>
+typedef __nv_bfloat16 qw_bf16_t;
+#else
+typedef uint16_t qw_bf16_t;
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QW_ABI_VERSION 1
+
+enum qw_status {
+  QW_OK = 0,
+  QW_ERR_ARG = 1,          /* invalid shape / dtype / pointer (Python: ValueError) */
+  QW_ERR_UNSUPPORTED = 2,  /* valid but outside this build's kernels */
+  QW_ERR_CUDA = 3,         /* a CUDA runtime error */
+  QW_ERR_TIMEOUT = 4       /* a bounded device wait expired */
+};
+
+enum qw_dtype { QW_F32 = 0, QW_F16 = 1, QW_BF16 = 2 };
+
+#define QW_MAX_BLOCK 16 /* tokens per sequence in one block verify (GDN kernels) */
+#define QW_MAX_CONV 8   /* largest causal-conv kernel width */
+
+/* Mirrors FUSED_OPS_ABI = 1 (model/qwen35_moe_dflash/fused/ops.py:21). */
+int qw_abi_version(void);
+/* Thread-local message of the last failing call on this host thread. */
+const char* qw_last_error(void);
+
+/* ------------------------------------------------------------------------------
+ * The seven fused-ops roles (reference/fused_ops.py), dtype-preserving.
+ * ---------------------------------------------------------------------------- */
+
+/* rms_norm(x, gamma, eps) — reference/fused_ops.py:28-34.
+ * y = cast_y(cast_x(x * rsqrt(mean(x^2) + eps)) * gamma), x [rows, dim].
+ * y_dtype must equal x_dtype, or be QW_F32 when gamma is QW_F32. */
+int qw_rms_norm(const void* x, int x_dtype, const void* gamma, int gamma_dtype, void* y,
+                int y_dtype, int64_t rows, int64_t dim, float eps, void* stream);
+
+/* conv_state_update(projected, history) — reference/fused_ops.py:37-47.
+ * projected [B,S,C], history [B,C,K-1] -> new_history [B,C,K-1], padded [B,C,S+K-1]. */
+int qw_conv_state_update(const void* projected, const void* history, void* new_history,
+                         void* padded, int dtype, int64_t batch, int64_t seq,
+                         int64_t channels, int64_t hist, void* stream);
+
+/* causal_conv1d(padded, weight) — reference/fused_ops.py:50-56 (no SiLU).
+ * padded [B,C,L], weight [C,1,K] -> out [B,L-K+1,C]. */
+int qw_causal_conv1d(const void* padded, const void* weight, void* out, int dtype,
+                     int64_t batch, int64_t channels, int64_t padded_len, int64_t kernel,
+                     void* stream);
+
+/* chunk_gated_delta_rule(...) — reference/fused_ops.py:59-107 (sequential recurrence).
+ * q,k [B,S,H,Dk], v [B,S,H,Dv], g,beta [B,S,H] (in_dtype), state0 [B,H,Dk,Dv]
+ * (state_dtype F32 or F16), eff_len int16 [B] in [0,S] -> core [B,S,H,Dv] (in_dtype),
+ * state_out [B,H,Dk,Dv] (state_dtype).  Dk,Dv <= 256. */
+int qw_gated_delta_rule(const void* q, const void* k, const void* v, const void* g,
+                        const void* beta, int in_dtype, const void* state0, int state_dtype,
+                        const int16_t* eff_len, void* core, void* state_out, int64_t batch,
+                        int64_t seq, int64_t heads, int64_t dk, int64_t dv, int use_l2norm,
+                        void* stream);
+
+/* cache_update(key, value, new_key, new_value) — reference/fused_ops.py:110-124.
+ * key/value [B,Hkv,T0,D] (may be NULL with t_old == 0), new [B,Hkv,T1,D]
+ * -> out [B,Hkv,T0+T1,D]. */
+int qw_cache_update(const void* key, const void* value, const void* new_key,
+                    const void* new_value, void* out_key, void* out_value, int dtype,
+                    int64_t batch, int64_t kv_heads, int64_t t_old, int64_t t_new,
+                    int64_t dim, void* stream);
+
+/* attention(q, k, v, query_start, scale) — reference/fused_ops.py:127-145.
+ * Causal GQA: q [B,H,S,D], k,v [B,Hkv,T,D] with T = query_start + S -> out [B,H,S,D].
+ * D in {64, 128, 256}. */
+int qw_attention(const void* q, const void* k, const void* v, void* out, int dtype,
+                 int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq, int64_t total,
+                 int64_t dim, int64_t query_start, float scale, void* stream);
+
+/* moe(hidden, router_weight, gate_up, down, top_k) — reference/fused_ops.py:148-173.
+ * Dense expert weights in the activation dtype (bf16 or f16): hidden [T,H],
+ * router [E,H], gate_up [E,2I,H], down [E,H,I] -> out [T,H].  Selection repeats
+ * torch.topk's CPU order exactly (ties included); topk_idx_out (int32 [T,k], may be
+ * NULL) receives it.  H, I multiples of 16. */
+int qw_moe(const void* hidden, const void* router, const void* gate_up, const void* down,
+           void* out, int dtype, int64_t tokens, int64_t hidden_dim, int64_t experts,
+           int64_t inter, int64_t top_k, int32_t* topk_idx_out, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Weight streams.  A W4 stream packs int4 weights (symmetric, bf16 scale per group
+ * of `group` along K) of an [N,K] matrix in the order the tensor-core fragments
+ * consume them: per 16-row tile, per K group, 8*group bytes of nibbles followed by
+ * 32 bytes of scales.  A B16 stream packs a bf16 [N,K] matrix the same way, per
+ * 16-row tile and 64-wide K chunk (2048 bytes).  The packing is done by the Python
+ * package (qwen35_dflash_b200.w4); these give the byte sizes.
+ * Replaces the quantised-linear weight contract of
+ * model/qwen35_moe_dflash/fused/quantization.py:154-165 (W4A8 g256 there).
+ * ---------------------------------------------------------------------------- */
+int64_t qw_w4_stream_bytes(int64_t n, int64_t k, int32_t group);
+int64_t qw_b16_stream_bytes(int64_t n, int64_t k);
+
+/* Output modes of the streaming linear kernels. */
+enum qw_linear_mode {
+  QW_OUT_BF16 = 0,      /* y[t,n] = bf16(acc) */
+  QW_OUT_F32 = 1,       /* y[t,n] = acc */
+  QW_OUT_RESID_BF16 = 2 /* y[t,n] = bf16(y[t,n] + bf16(acc)), in place (residual add) */
+};
+
+/* Quantised linear y = x . W^T with W a W4 stream — fused/quantization.py:154-165,
+ * fused/model.py:197-204.  x bf16 [T,K], N % 16 == 0, K % group == 0,
+ * group in {32,64,128}; y row stride ldy (elements). */
+int qw_w4_linear(const void* x, const void* w_stream, void* y, int mode, int64_t ldy,
+                 int64_t tokens, int64_t n, int64_t k, int32_t group, void* stream);
+
+/* Dense bf16 linear y = x . W^T with W a B16 stream (router, GDN a/b predictors,
+ * shared-expert gate) — fused/model.py:197-204.  K % 64 == 0. */
+int qw_b16_linear(const void* x, const void* w_stream, void* y, int mode, int64_t ldy,
+                  int64_t tokens, int64_t n, int64_t k, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Gated-DeltaNet block verify and commit (engine layer).
+ * One GDN layer's device buffers for a block of `seq` tokens of `batch` sequences;
+ * token row t = b*seq + s.  The recurrent-state bank stores each head column-major,
+ * [slots, v_heads, dv, dk]; `slots[b]` selects sequence b's row of both banks.
+ * Replaces FusedTargetModel._gdn (model/qwen35_moe_dflash/fused/model.py:227-263)
+ * with the operator sequence conv_state_update -> causal_conv1d -> SiLU ->
+ * chunk_gated_delta_rule -> gated RMSNorm (reference/fused_ops.py:37-107).
+ * ---------------------------------------------------------------------------- */
+typedef struct {
+  const qw_bf16_t* proj;     /* [T, ldp]: q | k | v conv channels, then z            */
+  const float* ab;           /* [T, 2*v_heads]: in_proj_b logits, then in_proj_a      */
+  qw_bf16_t* conv_hist;      /* [slots, channels, conv_k-1] conv tail bank            */
+  const qw_bf16_t* conv_w;   /* [channels, conv_k]                                    */
+  const float* A_log;        /* [v_heads]                                             */
+  const float* dt_bias;      /* [v_heads]                                             */
+  const qw_bf16_t* norm_w;   /* [dv] gated-norm weight (effective, no +1)             */
+  float* state;              /* [slots, v_heads, dv, dk] recurrent-state bank         */
+  qw_bf16_t* out;            /* [T, v_heads*dv] gated-norm output (verify only)       */
+} qw_gdn_layer;
+
+typedef struct {
+  int32_t batch, seq, k_heads, v_heads, dk, dv, channels, conv_k, ldp;
+  float eps;                 /* RMSNorm epsilon of the gated norm                    */
+  const int32_t* slots;      /* device [batch]: bank row of each sequence             */
+  const int32_t* accepted;   /* device [batch]: tokens to commit (commit only)        */
+} qw_gdn_dims;
+
+/* Block verify of one layer (`layers_dev[layer]`, a device array): writes out[],
+ * reads the banks, never writes them.  (dk,dv) in {(128,128),(64,64),(128,64)},
+ * 1 <= seq <= QW_MAX_BLOCK. */
+int qw_gdn_verify(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int layer,
+                  void* stream);
+
+/* Commit of `nlayers` layers (device array): the recurrent state and conv tail of
+ * each sequence advance by accepted[b] tokens of the verified block, in place —
+ * TargetVerification.commit (model/qwen35_moe_dflash/fused/session.py:374-387). */
+int qw_gdn_commit(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int nlayers,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QW_B200_H */

@@ -1,0 +1,423 @@
+// Gated DeltaNet kernels.
+//
+//  * qw_gated_delta_rule — the fused-ops ABI operator (reference/fused_ops.py:59-107):
+//    sequential recurrence, one CTA per (sequence, head), state in shared memory.
+//  * qw_gdn_verify / qw_gdn_commit — the block-verify form.  One thread-block cluster
+//    per (sequence, value head); each CTA of the cluster owns Dv/VSPLIT state columns
+//    and keeps them in registers (4 threads per column, Dk/4 rows each) across the
+//    block's tokens.  The prologue fuses conv_state_update + causal_conv1d + SiLU
+//    (fused/model.py:232-239), the q/k L2 norm and the gate math (:243-253); the
+//    epilogue fuses the gated RMSNorm x SiLU(z) (:219-225), with the row sum of squares
+//    exchanged through distributed shared memory.  Verify never writes the recurrent
+//    state: commit recomputes the first r tokens from the same inputs with the same
+//    arithmetic, so the committed state equals the verify's state after r tokens.
+#include <cooperative_groups.h>
+
+#include "qw_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace qw {
+
+using GdnLayer = qw_gdn_layer;
+using GdnDims = qw_gdn_dims;
+
+// =============================================================== fused-ops operator
+template <typename Tin, typename Tst>
+__global__ void gdn_rule_kernel(const Tin* __restrict__ q, const Tin* __restrict__ k,
+                                const Tin* __restrict__ v, const Tin* __restrict__ g,
+                                const Tin* __restrict__ beta, const Tst* __restrict__ s0,
+                                const int16_t* __restrict__ eff_len, Tin* __restrict__ core,
+                                Tst* __restrict__ s_out, int seq, int heads, int dk, int dv,
+                                int use_l2) {
+  extern __shared__ float smem[];
+  float* S = smem;                 // [dk][dv]
+  float* qs = S + dk * dv;         // [dk]
+  float* ks = qs + dk;             // [dk]
+  float* red = ks + dk;            // [64]
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int64_t bh = static_cast<int64_t>(b) * heads + h;
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) S[i] = to_f(s0[bh * dk * dv + i]);
+  const int len = eff_len[b];
+  const float qscale = rsqrtf(static_cast<float>(dk));
+  for (int t = 0; t < seq; ++t) {
+    const int64_t row = (static_cast<int64_t>(b) * seq + t) * heads + h;
+    __syncthreads();
+    float sq = 0.f, sk = 0.f;
+    for (int i = threadIdx.x; i < dk; i += blockDim.x) {
+      float a = to_f(q[row * dk + i]), c = to_f(k[row * dk + i]);
+      qs[i] = a;
+      ks[i] = c;
+      sq += a * a;
+      sk += c * c;
+    }
+    sq = block_sum(sq, red);
+    sk = block_sum(sk, red + 32);
+    const float iq = use_l2 ? rsqrtf(sq + 1e-6f) : 1.f;
+    const float ik = use_l2 ? rsqrtf(sk + 1e-6f) : 1.f;
+    const bool valid = t < len;
+    const float decay = __expf(to_f(g[row]));
+    const float bt = to_f(beta[row]);
+    for (int c = threadIdx.x; c < dv; c += blockDim.x) {
+      float o = 0.f;
+      if (valid) {
+        float pred = 0.f;
+        for (int i = 0; i < dk; ++i) {
+          float sv = S[i * dv + c] * decay;
+          S[i * dv + c] = sv;
+          pred = fmaf(sv, ks[i] * ik, pred);
+        }
+        const float delta = (to_f(v[row * dv + c]) - pred) * bt;
+        for (int i = 0; i < dk; ++i) {
+          float sv = fmaf(ks[i] * ik, delta, S[i * dv + c]);
+          S[i * dv + c] = sv;
+          o = fmaf(sv, qs[i] * iq * qscale, o);
+        }
+      }
+      core[row * dv + c] = from_f<Tin>(o);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < dk * dv; i += blockDim.x) s_out[bh * dk * dv + i] = from_f<Tst>(S[i]);
+}
+
+// =============================================================== block verify / commit
+constexpr int KSPLIT = 4;  // threads per state column
+
+template <int DK, int DV, int VSPLIT>
+struct GdnTile {
+  static constexpr int COLS = DV / VSPLIT;         // state columns per CTA
+  static constexpr int THREADS = COLS * KSPLIT;    // 128 for COLS = 32
+  static constexpr int ROWS = DK / KSPLIT;         // state rows per thread
+};
+
+// Shared-memory layout of one CTA (floats).
+template <int DK, int DV, int VSPLIT>
+struct GdnSmem {
+  static constexpr int COLS = DV / VSPLIT;
+  float q[QW_MAX_BLOCK][DK];
+  float k[QW_MAX_BLOCK][DK];
+  float v[QW_MAX_BLOCK][COLS];
+  float o[QW_MAX_BLOCK][COLS];
+  float g[QW_MAX_BLOCK];
+  float beta[QW_MAX_BLOCK];
+  float sumsq[QW_MAX_BLOCK];
+  float total[QW_MAX_BLOCK];
+};
+
+// conv + SiLU of one channel over the block's tokens, rounded to bf16 after the conv and
+// after the SiLU (the reference's activation tensors, fused/model.py:238-239).
+__device__ __forceinline__ void conv_channel(const GdnDims& d, const GdnLayer& L, int64_t slot,
+                                             int b, int c, int ntok, float* dst, int stride) {
+  const int K = d.conv_k;
+  float win[QW_MAX_CONV];
+  const __nv_bfloat16* hist = L.conv_hist + (slot * d.channels + c) * (K - 1);
+  for (int j = 0; j < K - 1; ++j) win[j] = __bfloat162float(hist[j]);
+  float w[QW_MAX_CONV];
+  for (int j = 0; j < K; ++j) w[j] = __bfloat162float(L.conv_w[c * K + j]);
+  for (int t = 0; t < ntok; ++t) {
+    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
+    win[K - 1] = __bfloat162float(L.proj[row * d.ldp + c]);
+    float acc = 0.f;
+    for (int j = 0; j < K; ++j) acc = fmaf(win[j], w[j], acc);
+    dst[t * stride] = rbf(silu_f(rbf(acc)));
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+  }
+}
+
+template <int DK, int DV, int VSPLIT, bool COMMIT>
+__global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
+    gdn_block_kernel(GdnDims d, const GdnLayer* __restrict__ layers, int layer0) {
+  using Tile = GdnTile<DK, DV, VSPLIT>;
+  constexpr int COLS = Tile::COLS, ROWS = Tile::ROWS, THREADS = Tile::THREADS;
+  __shared__ GdnSmem<DK, DV, VSPLIT> sm;
+  const int rank = blockIdx.x;          // column block within the head (cluster rank)
+  const int h = blockIdx.y;             // value head
+  const int b = blockIdx.z % d.batch;   // sequence within the batch
+  const GdnLayer& L = layers[layer0 + blockIdx.z / d.batch];
+  const int64_t slot = d.slots[b];
+  const int ntok = COMMIT ? d.accepted[b] : d.seq;
+  const int tid = threadIdx.x;
+  const int col = tid / KSPLIT, kq = tid % KSPLIT;
+  const int kh = h / (d.v_heads / d.k_heads);
+  const int kw = d.k_heads * DK;
+  const int vcol0 = rank * COLS;        // first state column of this CTA within the head
+
+  if (COMMIT && ntok <= 0) return;      // nothing accepted: the state stays S0
+
+  // ---- gates (fused/model.py:243-253, fp32)
+  for (int t = tid; t < ntok; t += THREADS) {
+    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
+    const float bl = L.ab[row * 2 * d.v_heads + h];
+    const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
+    sm.beta[t] = sigmoid_f(bl);
+    sm.g[t] = -__expf(L.A_log[h]) * softplus_f(al + L.dt_bias[h]);
+  }
+  // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns
+  {
+    const int nq = COMMIT ? 0 : DK;
+    const int nch = nq + DK + COLS;
+    for (int i = tid; i < nch; i += THREADS) {
+      if (i < nq) {
+        conv_channel(d, L, slot, b, kh * DK + i, ntok, &sm.q[0][i], DK);
+      } else if (i < nq + DK) {
+        const int j = i - nq;
+        conv_channel(d, L, slot, b, kw + kh * DK + j, ntok, &sm.k[0][j], DK);
+      } else {
+        const int j = i - nq - DK;
+        conv_channel(d, L, slot, b, 2 * kw + h * DV + vcol0 + j, ntok, &sm.v[0][j], COLS);
+      }
+    }
+  }
+  __syncthreads();
+  // ---- L2 norm of q and k per token (fused_ops.py:92-95); q also scaled by Dk^-1/2
+  {
+    const int warp = tid / 32, lane = tid % 32;
+    constexpr int NW = THREADS / 32;
+    for (int t = warp; t < ntok; t += NW) {
+      float sk = 0.f, sq = 0.f;
+      for (int i = lane; i < DK; i += 32) {
+        sk += sm.k[t][i] * sm.k[t][i];
+        if (!COMMIT) sq += sm.q[t][i] * sm.q[t][i];
+      }
+      sk = warp_sum(sk);
+      const float ik = rsqrtf(sk + 1e-6f);
+      float iq = 0.f;
+      if (!COMMIT) iq = rsqrtf(warp_sum(sq) + 1e-6f) * rsqrtf(static_cast<float>(DK));
+      for (int i = lane; i < DK; i += 32) {
+        sm.k[t][i] *= ik;
+        if (!COMMIT) sm.q[t][i] *= iq;
+      }
+    }
+  }
+  // ---- state columns into registers (bank layout [slot][head][Dv][Dk], column-major)
+  float st[ROWS];
+  float* scol = L.state + ((slot * d.v_heads + h) * DV + vcol0 + col) * static_cast<int64_t>(DK) + kq * ROWS;
+#pragma unroll
+  for (int i = 0; i < ROWS; i += 4) {
+    float4 v4 = *reinterpret_cast<const float4*>(scol + i);
+    st[i] = v4.x; st[i + 1] = v4.y; st[i + 2] = v4.z; st[i + 3] = v4.w;
+  }
+  __syncthreads();
+  // ---- the recurrence (fused_ops.py:98-106)
+  for (int t = 0; t < ntok; ++t) {
+    const float decay = __expf(sm.g[t]);
+    const float* kt = &sm.k[t][kq * ROWS];
+    float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < ROWS; i += 2) {
+      st[i] *= decay;
+      st[i + 1] *= decay;
+      p0 = fmaf(st[i], kt[i], p0);
+      p1 = fmaf(st[i + 1], kt[i + 1], p1);
+    }
+    float pred = p0 + p1;
+    pred += __shfl_xor_sync(0xffffffffu, pred, 1);
+    pred += __shfl_xor_sync(0xffffffffu, pred, 2);
+    const float delta = (sm.v[t][col] - pred) * sm.beta[t];
+    if (COMMIT) {
+#pragma unroll
+      for (int i = 0; i < ROWS; ++i) st[i] = fmaf(kt[i], delta, st[i]);
+    } else {
+      const float* qt = &sm.q[t][kq * ROWS];
+      float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < ROWS; i += 2) {
+        st[i] = fmaf(kt[i], delta, st[i]);
+        st[i + 1] = fmaf(kt[i + 1], delta, st[i + 1]);
+        o0 = fmaf(st[i], qt[i], o0);
+        o1 = fmaf(st[i + 1], qt[i + 1], o1);
+      }
+      float o = o0 + o1;
+      o += __shfl_xor_sync(0xffffffffu, o, 1);
+      o += __shfl_xor_sync(0xffffffffu, o, 2);
+      if (kq == 0) sm.o[t][col] = rbf(o);   // core tensor in the activation dtype
+    }
+  }
+  if (COMMIT) {
+#pragma unroll
+    for (int i = 0; i < ROWS; i += 4)
+      *reinterpret_cast<float4*>(scol + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
+    return;
+  }
+  __syncthreads();
+  // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225)
+  for (int t = tid / 32; t < ntok; t += THREADS / 32) {
+    float ss = 0.f;
+    for (int c = tid % 32; c < COLS; c += 32) ss += sm.o[t][c] * sm.o[t][c];
+    ss = warp_sum(ss);
+    if (tid % 32 == 0) sm.sumsq[t] = ss;
+  }
+  if constexpr (VSPLIT > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    for (int t = tid; t < ntok; t += THREADS) {
+      float tot = 0.f;
+      for (int r = 0; r < VSPLIT; ++r) tot += cluster.map_shared_rank(&sm.sumsq[0], r)[t];
+      sm.total[t] = tot;
+    }
+    cluster.sync();
+  } else {
+    __syncthreads();
+    for (int t = tid; t < ntok; t += THREADS) sm.total[t] = sm.sumsq[t];
+  }
+  __syncthreads();
+  const int vw = d.v_heads * DV;
+  for (int i = tid; i < ntok * COLS; i += THREADS) {
+    const int t = i / COLS, c = i % COLS;
+    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
+    const int vc = h * DV + vcol0 + c;
+    const float inv = rsqrtf(sm.total[t] / DV + d.eps);
+    const float n = rbf(sm.o[t][c] * inv);
+    const float y = rbf(n * __bfloat162float(L.norm_w[vcol0 + c]));
+    const float z = __bfloat162float(L.proj[row * d.ldp + 2 * kw + vw + vc]);
+    L.out[row * vw + vc] = __float2bfloat16_rn(y * rbf(silu_f(z)));
+  }
+}
+
+// New conv history after r accepted tokens: padded[r : r + K-1] (fused_ops.py:44-47).
+// One thread per (layer, sequence, channel); each channel is owned by one thread, so the
+// update is in place.
+__global__ void gdn_conv_commit_kernel(GdnDims d, const GdnLayer* __restrict__ layers, int nlayers) {
+  const int64_t total = static_cast<int64_t>(nlayers) * d.batch * d.channels;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % d.channels);
+    const int b = static_cast<int>((idx / d.channels) % d.batch);
+    const int l = static_cast<int>(idx / (static_cast<int64_t>(d.channels) * d.batch));
+    const GdnLayer& L = layers[l];
+    const int r = d.accepted[b];
+    if (r <= 0) continue;
+    const int K1 = d.conv_k - 1;
+    __nv_bfloat16* hist = L.conv_hist + (static_cast<int64_t>(d.slots[b]) * d.channels + c) * K1;
+    __nv_bfloat16 nh[QW_MAX_CONV];
+    for (int j = 0; j < K1; ++j) {
+      const int p = r + j;  // index into padded = [hist(K-1) | proj(seq)]
+      nh[j] = p < K1 ? hist[p] : L.proj[(static_cast<int64_t>(b) * d.seq + (p - K1)) * d.ldp + c];
+    }
+    for (int j = 0; j < K1; ++j) hist[j] = nh[j];
+  }
+}
+
+template <int DK, int DV, int VSPLIT, bool COMMIT>
+static int launch_block(const GdnDims& d, const GdnLayer* layers, int layer0, int nlayers,
+                        cudaStream_t s) {
+  using Tile = GdnTile<DK, DV, VSPLIT>;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(VSPLIT, d.v_heads, d.batch * nlayers);
+  cfg.blockDim = dim3(Tile::THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = VSPLIT;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_block_kernel<DK, DV, VSPLIT, COMMIT>, d, layers, layer0);
+  if (e != cudaSuccess) return cuda_status(e, COMMIT ? "gdn_commit" : "gdn_verify");
+  return QW_OK;
+}
+
+template <bool COMMIT>
+static int dispatch_block(const GdnDims& d, const GdnLayer* layers, int layer0, int nlayers,
+                          cudaStream_t s) {
+  if (d.dk == 128 && d.dv == 128) return launch_block<128, 128, 4, COMMIT>(d, layers, layer0, nlayers, s);
+  if (d.dk == 64 && d.dv == 64) return launch_block<64, 64, 2, COMMIT>(d, layers, layer0, nlayers, s);
+  if (d.dk == 128 && d.dv == 64) return launch_block<128, 64, 2, COMMIT>(d, layers, layer0, nlayers, s);
+  return fail(QW_ERR_UNSUPPORTED, "gdn block: head dims (%d,%d) not built", d.dk, d.dv);
+}
+
+static int check_dims(const GdnDims& d) {
+  QW_CHECK_ARG(d.batch >= 1 && d.seq >= 1 && d.seq <= QW_MAX_BLOCK,
+               "gdn block: need 1 <= seq <= %d", QW_MAX_BLOCK);
+  QW_CHECK_ARG(d.v_heads >= 1 && d.k_heads >= 1 && d.v_heads % d.k_heads == 0,
+               "gdn block: value heads must be a multiple of key heads");
+  QW_CHECK_ARG(d.conv_k >= 2 && d.conv_k <= QW_MAX_CONV, "gdn block: conv kernel out of range");
+  QW_CHECK_ARG(d.channels == 2 * d.k_heads * d.dk + d.v_heads * d.dv, "gdn block: channel count");
+  QW_CHECK_ARG(d.ldp >= d.channels + d.v_heads * d.dv, "gdn block: projection row too short");
+  QW_CHECK_ARG(d.slots != nullptr, "gdn block: null slot table");
+  return QW_OK;
+}
+
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" int qw_gated_delta_rule(const void* q, const void* k, const void* v, const void* g,
+                                   const void* beta, int in_dtype, const void* state0,
+                                   int state_dtype, const int16_t* eff_len, void* core,
+                                   void* state_out, int64_t batch, int64_t seq, int64_t heads,
+                                   int64_t dk, int64_t dv, int use_l2norm, void* stream) {
+  QW_CHECK_ARG(q && k && v && g && beta && state0 && eff_len && core && state_out,
+               "chunk_gated_delta_rule: null pointer");
+  QW_CHECK_ARG(batch >= 1 && seq >= 1 && heads >= 1 && dk >= 1 && dv >= 1,
+               "GDN requires compatible [B,S,H,D] tensors and [B,S,H] gates");
+  QW_CHECK_ARG(dk <= 256 && dv <= 256 && dk * dv <= 48 * 1024, "chunk_gated_delta_rule: head too large");
+  QW_CHECK_ARG(batch < 65536 && heads < 65536, "chunk_gated_delta_rule: grid too large");
+  const size_t smem = (static_cast<size_t>(dk) * dv + 2 * dk + 64) * sizeof(float);
+  cudaStream_t s = as_stream(stream);
+  dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  const int threads = 128;
+#define QW_GDN(TIN, TST)                                                                       \
+  do {                                                                                         \
+    auto kern = gdn_rule_kernel<TIN, TST>;                                                     \
+    if (smem > 48 * 1024) {                                                                    \
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                           static_cast<int>(smem));                            \
+      if (e != cudaSuccess) return cuda_status(e, "chunk_gated_delta_rule smem");              \
+    }                                                                                          \
+    kern<<<grid, threads, smem, s>>>(                                                          \
+        static_cast<const TIN*>(q), static_cast<const TIN*>(k), static_cast<const TIN*>(v),    \
+        static_cast<const TIN*>(g), static_cast<const TIN*>(beta),                             \
+        static_cast<const TST*>(state0), eff_len, static_cast<TIN*>(core),                     \
+        static_cast<TST*>(state_out), static_cast<int>(seq), static_cast<int>(heads),          \
+        static_cast<int>(dk), static_cast<int>(dv), use_l2norm);                               \
+  } while (0)
+  if (state_dtype == QW_F32) {
+    switch (in_dtype) {
+      case QW_F32: QW_GDN(float, float); break;
+      case QW_F16: QW_GDN(__half, float); break;
+      case QW_BF16: QW_GDN(__nv_bfloat16, float); break;
+      default: return fail(QW_ERR_ARG, "chunk_gated_delta_rule: bad input dtype");
+    }
+  } else if (state_dtype == QW_F16) {
+    switch (in_dtype) {
+      case QW_F32: QW_GDN(float, __half); break;
+      case QW_F16: QW_GDN(__half, __half); break;
+      case QW_BF16: QW_GDN(__nv_bfloat16, __half); break;
+      default: return fail(QW_ERR_ARG, "chunk_gated_delta_rule: bad input dtype");
+    }
+  } else {
+    return fail(QW_ERR_ARG, "initial_state must be FP16/FP32 [B,H,Dk,Dv]");
+  }
+#undef QW_GDN
+  QW_LAUNCH_CHECK("chunk_gated_delta_rule");
+  return QW_OK;
+}
+
+extern "C" int qw_gdn_verify(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int layer,
+                             void* stream) {
+  QW_CHECK_ARG(dims && layers_dev && layer >= 0, "gdn_verify: null argument");
+  int st = check_dims(*dims);
+  if (st) return st;
+  return dispatch_block<false>(*dims, layers_dev, layer, 1, as_stream(stream));
+}
+
+extern "C" int qw_gdn_commit(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int nlayers,
+                             void* stream) {
+  QW_CHECK_ARG(dims && layers_dev && nlayers >= 1, "gdn_commit: null argument");
+  int st = check_dims(*dims);
+  if (st) return st;
+  QW_CHECK_ARG(dims->accepted != nullptr, "gdn_commit: null accepted counts");
+  cudaStream_t s = as_stream(stream);
+  st = dispatch_block<true>(*dims, layers_dev, 0, nlayers, s);
+  if (st) return st;
+  const int64_t total = static_cast<int64_t>(nlayers) * dims->batch * dims->channels;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  gdn_conv_commit_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(*dims, layers_dev, nlayers);
+  QW_LAUNCH_CHECK("gdn_conv_commit");
+  return QW_OK;
+}

@@ -1,0 +1,176 @@
+// Streaming linear y = x . W^T for the verify block's tokens (W4A16 or bf16 weights).
+// Replaces the quantised / dense projections of fused/model.py:197-204 and
+// fused/quantization.py:154-165.  HBM-bound: each weight byte is read once per
+// 32-token pass; the CTA splits K across its warps and reduces in shared memory, so
+// the result is deterministic and the epilogue can fuse the residual add.
+#include <mutex>
+
+#include "stream_gemm.cuh"
+
+namespace qw {
+
+struct LinArgs {
+  const __nv_bfloat16* x;  // [T, k]
+  const uint8_t* w;        // stream
+  void* y;                 // [T, ldy]
+  int64_t ldy;
+  int tokens, n, k, rt, mode;
+};
+
+template <class Fmt, int NT, int PF>
+__global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int NTOK = NT * 8;
+  const int xstride = a.k + 8;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);
+  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(NTOK) * xstride * 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KS = SG_WARPS / a.rt;
+  const int rt_local = warp / KS, ks = warp % KS;
+  const int ntiles = a.n / 16;
+  const int rt = blockIdx.x * a.rt + rt_local;
+  const bool active = rt < ntiles;
+  const int nch = a.k / Fmt::KCHUNK;
+  const int c0 = ks * nch / KS, c1 = (ks + 1) * nch / KS;
+  const uint8_t* tile = a.w + static_cast<int64_t>(active ? rt : 0) * nch * Fmt::CHB;
+  const __nv_bfloat16* xl = xs_lane_ptr(xs, xstride, lane);
+  const int gid = lane >> 2, tig = lane & 3;
+
+  for (int tp0 = 0; tp0 < a.tokens; tp0 += NTOK) {
+    __syncthreads();
+    // stage the pass's activation rows (zero beyond the last token)
+    const int vec_per_row = a.k / 8;
+    for (int i = threadIdx.x; i < NTOK * vec_per_row; i += blockDim.x) {
+      const int r = i / vec_per_row, c = (i % vec_per_row) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (tp0 + r < a.tokens)
+        v = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tp0 + r) * a.k + c);
+      *reinterpret_cast<uint4*>(xs + r * xstride + c) = v;
+    }
+    __syncthreads();
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    if (active) stream_tile<Fmt, NT, PF>(tile, c0, c1, lane, xl, 16 * xstride, acc);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) red[(warp * NT * 4 + j * 4 + r) * 32 + lane] = acc[j][r];
+    __syncthreads();
+    if (ks == 0 && active) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float v = 0.f;
+          for (int s = 0; s < KS; ++s) v += red[((warp + s) * NT * 4 + j * 4 + r) * 32 + lane];
+          const int t = tp0 + j * 8 + 2 * tig + (r & 1);
+          const int n = rt * 16 + gid + 8 * (r >> 1);
+          if (t < a.tokens) {
+            const int64_t o = static_cast<int64_t>(t) * a.ldy + n;
+            if (a.mode == QW_OUT_F32) {
+              static_cast<float*>(a.y)[o] = v;
+            } else if (a.mode == QW_OUT_BF16) {
+              static_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(v);
+            } else {
+              __nv_bfloat16* y = static_cast<__nv_bfloat16*>(a.y);
+              y[o] = __float2bfloat16_rn(__bfloat162float(y[o]) + rbf(v));
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+static int choose_rt(int ntiles) {
+  // largest row-tile count per CTA that still leaves >= 2 waves of CTAs; K splits
+  // across the remaining warps
+  for (int rt : {8, 4, 2}) {
+    if ((ntiles + rt - 1) / rt >= 296) return rt;
+  }
+  return 1;
+}
+
+template <class Fmt, int NT, int PF>
+static int launch_linear(const LinArgs& a0, cudaStream_t s) {
+  LinArgs a = a0;
+  a.rt = choose_rt(a.n / 16);
+  const size_t smem = static_cast<size_t>(NT * 8) * (a.k + 8) * 2 + SG_WARPS * NT * 4 * 32 * 4;
+  if (smem > 227 * 1024) return fail(QW_ERR_UNSUPPORTED, "linear: K=%d too large", a.k);
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(stream_linear_kernel<Fmt, NT, PF>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (attr_err != cudaSuccess) return cuda_status(attr_err, "linear smem attribute");
+  const int ntiles = a.n / 16;
+  const unsigned grid = static_cast<unsigned>((ntiles + a.rt - 1) / a.rt);
+  stream_linear_kernel<Fmt, NT, PF><<<grid, SG_WARPS * 32, smem, s>>>(a);
+  QW_LAUNCH_CHECK("linear");
+  return QW_OK;
+}
+
+template <class Fmt, int PF>
+static int dispatch_nt(const LinArgs& a, cudaStream_t s) {
+  const bool wide_ok = static_cast<size_t>(32) * (a.k + 8) * 2 <= 150 * 1024;
+  if (a.tokens > 16 && wide_ok) return launch_linear<Fmt, 4, PF>(a, s);
+  return launch_linear<Fmt, 2, PF>(a, s);
+}
+
+static int check_linear(const void* x, const void* w, void* y, int mode, int64_t ldy,
+                        int64_t tokens, int64_t n, int64_t k) {
+  QW_CHECK_ARG(x && w && y, "linear: null pointer");
+  QW_CHECK_ARG(tokens >= 0 && tokens < (1 << 24), "linear: bad token count");
+  QW_CHECK_ARG(n > 0 && n % 16 == 0 && n < (1LL << 30), "linear: N must be a positive multiple of 16");
+  QW_CHECK_ARG(k > 0 && k < (1 << 20), "linear: bad K");
+  QW_CHECK_ARG(ldy >= n, "linear: ldy < N");
+  QW_CHECK_ARG(mode == QW_OUT_BF16 || mode == QW_OUT_F32 || mode == QW_OUT_RESID_BF16,
+               "linear: bad output mode");
+  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
+               "linear: x and w must be 16-byte aligned");
+  return QW_OK;
+}
+
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" int64_t qw_w4_stream_bytes(int64_t n, int64_t k, int32_t group) {
+  if (n <= 0 || k <= 0 || n % 16 || (group != 32 && group != 64 && group != 128) || k % group) return -1;
+  return (n / 16) * (k / group) * (8LL * group + 32);
+}
+
+extern "C" int64_t qw_b16_stream_bytes(int64_t n, int64_t k) {
+  if (n <= 0 || k <= 0 || n % 16 || k % 64) return -1;
+  return (n / 16) * (k / 64) * 2048LL;
+}
+
+extern "C" int qw_w4_linear(const void* x, const void* w_stream, void* y, int mode, int64_t ldy,
+                            int64_t tokens, int64_t n, int64_t k, int32_t group, void* stream) {
+  int st = check_linear(x, w_stream, y, mode, ldy, tokens, n, k);
+  if (st) return st;
+  QW_CHECK_ARG(group == 32 || group == 64 || group == 128, "w4_linear: group must be 32, 64 or 128");
+  QW_CHECK_ARG(k % group == 0, "w4_linear: K %% group != 0");
+  if (tokens == 0) return QW_OK;
+  LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), y, ldy,
+            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, mode};
+  cudaStream_t s = as_stream(stream);
+  switch (group) {
+    case 128: return dispatch_nt<W4Fmt<128>, 4>(a, s);
+    case 64: return dispatch_nt<W4Fmt<64>, 4>(a, s);
+    default: return dispatch_nt<W4Fmt<32>, 8>(a, s);
+  }
+}
+
+extern "C" int qw_b16_linear(const void* x, const void* w_stream, void* y, int mode, int64_t ldy,
+                             int64_t tokens, int64_t n, int64_t k, void* stream) {
+  int st = check_linear(x, w_stream, y, mode, ldy, tokens, n, k);
+  if (st) return st;
+  QW_CHECK_ARG(k % 64 == 0, "b16_linear: K must be a multiple of 64");
+  if (tokens == 0) return QW_OK;
+  LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), y, ldy,
+            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, mode};
+  return dispatch_nt<B16Fmt, 2>(a, as_stream(stream));
+}
