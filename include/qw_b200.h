@@ -98,19 +98,29 @@ int qw_cache_update(const void* key, const void* value, const void* new_key,
 
 /* attention(q, k, v, query_start, scale) — reference/fused_ops.py:127-145.
  * Causal GQA: q [B,H,S,D], k,v [B,Hkv,T,D] with T = query_start + S -> out [B,H,S,D].
- * D in {64, 128, 256}. */
+ * D in {32, 64, 128, 256}; bf16 or fp16; `workspace` holds qw_attn_workspace_bytes. */
 int qw_attention(const void* q, const void* k, const void* v, void* out, int dtype,
                  int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq, int64_t total,
-                 int64_t dim, int64_t query_start, float scale, void* stream);
+                 int64_t dim, int64_t query_start, float scale, void* workspace, void* stream);
+
+/* Scratch (bytes) of qw_attention / qw_attn_paged for keys up to max_len. */
+int64_t qw_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq,
+                                int64_t dim, int64_t max_len);
 
 /* moe(hidden, router_weight, gate_up, down, top_k) — reference/fused_ops.py:148-173.
  * Dense expert weights in the activation dtype (bf16 or f16): hidden [T,H],
  * router [E,H], gate_up [E,2I,H], down [E,H,I] -> out [T,H].  Selection repeats
  * torch.topk's CPU order exactly (ties included); topk_idx_out (int32 [T,k], may be
- * NULL) receives it.  H, I multiples of 16. */
+ * NULL) receives it.  H, I multiples of 16; `workspace` holds qw_moe_workspace_bytes. */
 int qw_moe(const void* hidden, const void* router, const void* gate_up, const void* down,
            void* out, int dtype, int64_t tokens, int64_t hidden_dim, int64_t experts,
-           int64_t inter, int64_t top_k, int32_t* topk_idx_out, void* stream);
+           int64_t inter, int64_t top_k, int32_t* topk_idx_out, void* workspace, void* stream);
+
+/* Device scratch (bytes) the MoE entry points need for `tokens` routed tokens; the
+ * caller allocates it (the library allocates nothing).  1 <= top_k <= 16: torch's
+ * selection order is reproduced for sorts of up to 16 selected entries. */
+int64_t qw_moe_workspace_bytes(int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
+                               int64_t top_k);
 
 /* ------------------------------------------------------------------------------
  * Weight streams.  A W4 stream packs int4 weights (symmetric, bf16 scale per group
@@ -142,6 +152,70 @@ int qw_w4_linear(const void* x, const void* w_stream, void* y, int mode, int64_t
  * shared-expert gate) — fused/model.py:197-204.  K % 64 == 0. */
 int qw_b16_linear(const void* x, const void* w_stream, void* y, int mode, int64_t ldy,
                   int64_t tokens, int64_t n, int64_t k, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * W4A16 routed MoE, in three launches on one workspace — the quantized MoE chain of
+ * model/qwen35_moe_dflash/fused/quantization.py:181-202 (gating top-k softmax ->
+ * init routing -> grouped gate_up -> SwiGLU -> grouped down -> finalize routing),
+ * with the reference's selection and rounding (reference/fused_ops.py:161-172) and
+ * the shared expert of fused/model.py:305-307.
+ * ---------------------------------------------------------------------------- */
+
+/* Routing from router logits [T, ldl] (logit_dtype): fp32 softmax over the first
+ * `experts` columns, torch.topk CPU order, renormalized weights cast to act_dtype;
+ * column `shared_col` (or -1) holds the shared-expert gate logit.  Builds the
+ * per-expert (token, slot) lists in the workspace. */
+int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens,
+                 int64_t experts, int64_t top_k, int64_t shared_col, int act_dtype,
+                 void* workspace, void* stream);
+
+/* Expert FFNs on the routing in `workspace`: x bf16 [T,H]; gate_up / down are W4
+ * streams of [E][2I,H] / [E][H,I] (experts concatenated); the shared expert's
+ * [2I,H] (gate rows then up rows) and [H,I] streams, or both NULL.  Writes each
+ * (token, slot)'s raw fp32 expert output into the workspace. */
+int qw_moe_experts_w4(const void* x, const void* gate_up, const void* down,
+                      const void* shared_gate_up, const void* shared_down, int64_t tokens,
+                      int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
+                      int32_t group, void* workspace, void* stream);
+
+/* Weighted combine in ascending expert order (+ gated shared expert): out bf16 [T,H]
+ * is overwritten, or, with residual != 0, out = bf16(out + moe) in place. */
+int qw_moe_combine(void* workspace, void* out, int residual, int64_t tokens, int64_t hidden,
+                   int64_t experts, int64_t inter, int64_t top_k, int has_shared, void* stream);
+
+/* Host helper: device addresses of the routing results inside a workspace
+ * (part fp32 [T,k+1,H], topk_idx int32 [T,k], topk_w fp32 [T,k], shared_gate fp32 [T]). */
+int qw_moe_partials(void* workspace, int64_t tokens, int64_t hidden, int64_t experts,
+                    int64_t inter, int64_t top_k, const float** part, const int32_t** topk_idx,
+                    const float** topk_w, const float** shared_gate);
+
+/* ------------------------------------------------------------------------------
+ * Full-attention layer of the block verify (engine layer) — FusedTargetModel._attention
+ * (model/qwen35_moe_dflash/fused/model.py:278-294) over a paged bf16 KV cache.
+ * KV cache layout [pages, kv_heads, page_size, dim]; sequence b's position t is in
+ * page pages[b*max_pages + t/page_size]; qpos[b] = tokens already cached before the
+ * block (the block's first position).
+ * ---------------------------------------------------------------------------- */
+
+/* q/k RMSNorm (zero-centred weights, +1), partial RoPE on the first rotary_dim dims
+ * (theta, fp32 angles), and the K/V append of the block (the CacheUpdate role,
+ * reference/fused_ops.py:110-124).  qkv bf16 [B*S, ldq] holds per head [q | gate]
+ * (heads*2*dim), then k (kv_heads*dim), then v.  q_out bf16 [B, heads, S, dim]. */
+int qw_attn_prep(const void* qkv, int64_t ldq, const void* q_norm_w, const void* k_norm_w,
+                 float eps, float rope_theta, int32_t rotary_dim, const int32_t* qpos,
+                 const int32_t* pages, int32_t max_pages, int32_t page_size, void* k_cache,
+                 void* v_cache, void* q_out, int64_t batch, int64_t seq, int64_t heads,
+                 int64_t kv_heads, int64_t dim, void* stream);
+
+/* Causal GQA of q [B,heads,S,dim] against the paged cache (keys <= qpos[b]+s), times
+ * sigmoid(gate) (gate element (b,h,s,d) at gate + (b*S+s)*ldg + h*2*dim + d, or NULL),
+ * -> out bf16 [B*S, heads*dim] (reference/fused_ops.py:127-145, fused/model.py:291-293).
+ * max_len bounds qpos[b]+S over the batch and sizes the key splits. */
+int qw_attn_paged(const void* q, const void* k_cache, const void* v_cache, const int32_t* pages,
+                  int32_t max_pages, int32_t page_size, const int32_t* qpos, int64_t max_len,
+                  const void* gate, int64_t ldg, void* out, int64_t batch, int64_t seq,
+                  int64_t heads, int64_t kv_heads, int64_t dim, float scale, void* workspace,
+                  void* stream);
 
 /* ------------------------------------------------------------------------------
  * Gated-DeltaNet block verify and commit (engine layer).

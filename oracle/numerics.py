@@ -196,6 +196,9 @@ def topk_indices_row(values, k: int) -> list[int]:
     n = len(values)
     if not 0 < k <= n:
         raise ValueError("invalid k")
+    if k - 1 > 16:
+        # std::sort of more than 16 entries switches to introsort; not restated here
+        raise NotImplementedError("top-k order restated for k <= 17 only")
     q = [(float(v), i) for i, v in enumerate(values)]
     if k * 64 <= n:
         _heap_select(q, 0, k, n)

@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
   const bool active = rt < ntiles;
   const int nch = a.k / Fmt::KCHUNK;
   const int c0 = ks * nch / KS, c1 = (ks + 1) * nch / KS;
-  const uint8_t* tile = a.w + static_cast<int64_t>(active ? rt : 0) * nch * Fmt::CHB;
+  const uint8_t* tile = a.w + Fmt::tile_offset(active ? rt : 0, a.k, 0);
   const __nv_bfloat16* xl = xs_lane_ptr(xs, xstride, lane);
   const int gid = lane >> 2, tig = lane & 3;
 
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
     float acc[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    if (active) stream_tile<Fmt, NT, PF>(tile, c0, c1, lane, xl, 16 * xstride, acc);
+    if (active) stream_tile<Fmt, NT, PF>(tile, 0, c0, c1, lane, xl, 16 * xstride, acc);
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll

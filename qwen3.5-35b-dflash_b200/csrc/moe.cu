@@ -1,0 +1,751 @@
+// Routed mixture-of-experts for the verify block (reference/fused_ops.py:148-173,
+// fused/model.py:296-307, fused/quantization.py:181-202).
+//
+//  route   one warp per token: fp32 softmax of the router logits, top-k selection that
+//          reproduces torch.topk's CPU order exactly (below), renormalized weights cast
+//          to the activation dtype; then one CTA-wide pass builds, per active expert in
+//          ascending id, the list of (token, slot) pairs routed to it.
+//  up      CTA = (expert slot, 16-wide intermediate tile): gate and up rows streamed once,
+//          K split over 8 warps, SiLU(gate) * up in the reference's rounding order.
+//  down    CTA = (expert slot, 128 output rows): each pair's raw fp32 expert output goes
+//          to its own (token, slot) row, so the combine (ascending expert order, bf16
+//          rounding at each add as the reference) is deterministic.
+//  Slot 0 is the shared expert (all tokens), slots 1.. the active routed experts.
+//
+// torch.topk order.  The reference selects with torch.topk on CPU
+// (reference/fused_ops.py:163).  ATen copies (value, index) pairs into a queue in index
+// order and, when k*64 > n, runs std::nth_element(k-1) then std::sort of the first k-1
+// entries (GNU libstdc++ introselect: median-of-3 pivot moved to the front, unguarded
+// Hoare partition, insertion sort below 4 elements, heap select past 2*log2(n) levels),
+// else std::partial_sort (heap select + sort heap); comparator a.value > b.value.  Ties
+// therefore resolve by the partition history, not by index.  Each partition is run
+// here in parallel across the warp in closed form: the i-th left stop (value <= pivot,
+// ascending) swaps with the i-th right stop (value >= pivot, descending) while the
+// first is left of the second; the cut is the next left stop, or the last right stop
+// swapped, whichever comes first.  The sequential steps (pivot choice, small sorts,
+// heap fallback) run on lane 0.  Values compared are the bf16 router logits, which
+// order exactly as torch's fp32 probabilities (exp is monotone; equal logits give
+// equal probabilities).
+#include <mutex>
+
+#include "stream_gemm.cuh"
+
+namespace qw {
+
+// ------------------------------------------------------------------ route workspace
+struct RouteView {
+  int32_t* topk_idx;    // [T*k]
+  float* topk_w;        // [T*k]  (value of the activation dtype)
+  float* shared_gate;   // [T]
+  int32_t* n_active;    // [1]
+  int32_t* active;      // [min(E, T*k)]
+  int32_t* pair_off;    // [min(E, T*k) + 1]
+  int32_t* pair_tok;    // [T*k]
+  int32_t* pair_slot;   // [T*k]
+};
+
+__host__ __device__ inline int64_t route_ints(int T, int E, int k) {
+  const int64_t na = (E < T * k) ? E : T * k;
+  return 2LL * T * k + T + 4 + na + na + 1 + 2LL * T * k;
+}
+
+__host__ __device__ inline RouteView route_view(void* ws, int T, int E, int k) {
+  RouteView v;
+  const int64_t na = (E < T * k) ? E : T * k;
+  int32_t* p = static_cast<int32_t*>(ws);
+  v.topk_idx = p; p += T * k;
+  v.topk_w = reinterpret_cast<float*>(p); p += T * k;
+  v.shared_gate = reinterpret_cast<float*>(p); p += T;
+  v.n_active = p; p += 4;
+  v.active = p; p += na;
+  v.pair_off = p; p += na + 1;
+  v.pair_tok = p; p += T * k;
+  v.pair_slot = p;
+  return v;
+}
+
+// ------------------------------------------------------------------ libstdc++ emulation
+struct Q {
+  float* v;
+  int32_t* i;
+  __device__ __forceinline__ bool gt(int a, int b) const { return v[a] > v[b]; }
+  __device__ __forceinline__ void swap(int a, int b) const {
+    float tv = v[a]; v[a] = v[b]; v[b] = tv;
+    int32_t ti = i[a]; i[a] = i[b]; i[b] = ti;
+  }
+};
+
+__device__ void q_move_median_to_first(const Q& q, int result, int a, int b, int c) {
+  if (q.gt(a, b)) {
+    if (q.gt(b, c)) q.swap(result, b);
+    else if (q.gt(a, c)) q.swap(result, c);
+    else q.swap(result, a);
+  } else if (q.gt(a, c)) {
+    q.swap(result, a);
+  } else if (q.gt(b, c)) {
+    q.swap(result, c);
+  } else {
+    q.swap(result, b);
+  }
+}
+
+__device__ void q_insertion_sort(const Q& q, int first, int last) {
+  for (int i = first + 1; i < last; ++i) {
+    const float vv = q.v[i];
+    const int32_t vi = q.i[i];
+    if (vv > q.v[first]) {
+      for (int j = i; j > first; --j) { q.v[j] = q.v[j - 1]; q.i[j] = q.i[j - 1]; }
+      q.v[first] = vv; q.i[first] = vi;
+    } else {
+      int hole = i, prev = i - 1;
+      while (vv > q.v[prev]) { q.v[hole] = q.v[prev]; q.i[hole] = q.i[prev]; hole = prev; --prev; }
+      q.v[hole] = vv; q.i[hole] = vi;
+    }
+  }
+}
+
+__device__ void q_push_heap(const Q& q, int first, int hole, int top, float vv, int32_t vi) {
+  int parent = (hole - 1) / 2;
+  while (hole > top && q.v[first + parent] > vv) {
+    q.v[first + hole] = q.v[first + parent]; q.i[first + hole] = q.i[first + parent];
+    hole = parent;
+    parent = (hole - 1) / 2;
+  }
+  q.v[first + hole] = vv; q.i[first + hole] = vi;
+}
+
+__device__ void q_adjust_heap(const Q& q, int first, int hole, int len, float vv, int32_t vi) {
+  const int top = hole;
+  int child = hole;
+  while (child < (len - 1) / 2) {
+    child = 2 * (child + 1);
+    if (q.v[first + child] > q.v[first + child - 1]) --child;
+    q.v[first + hole] = q.v[first + child]; q.i[first + hole] = q.i[first + child];
+    hole = child;
+  }
+  if ((len & 1) == 0 && child == (len - 2) / 2) {
+    child = 2 * (child + 1);
+    q.v[first + hole] = q.v[first + child - 1]; q.i[first + hole] = q.i[first + child - 1];
+    hole = child - 1;
+  }
+  q_push_heap(q, first, hole, top, vv, vi);
+}
+
+__device__ void q_make_heap(const Q& q, int first, int last) {
+  const int len = last - first;
+  if (len < 2) return;
+  int parent = (len - 2) / 2;
+  while (true) {
+    q_adjust_heap(q, first, parent, len, q.v[first + parent], q.i[first + parent]);
+    if (parent == 0) return;
+    --parent;
+  }
+}
+
+__device__ void q_heap_select(const Q& q, int first, int middle, int last) {
+  q_make_heap(q, first, middle);
+  for (int i = middle; i < last; ++i) {
+    if (q.v[i] > q.v[first]) {
+      const float vv = q.v[i];
+      const int32_t vi = q.i[i];
+      q.v[i] = q.v[first]; q.i[i] = q.i[first];
+      q_adjust_heap(q, first, 0, middle - first, vv, vi);
+    }
+  }
+}
+
+// Parallel unguarded Hoare partition of [a, b) around the pivot at a-1; returns the cut.
+// pos_l / pos_r: per-warp scratch of >= (b - a + 1) entries.
+__device__ int warp_partition(const Q& q, int a, int b, int16_t* pos_l, int16_t* pos_r, int lane) {
+  const float p = q.v[a - 1];
+  int nl = 0, nr = 0;
+  // left stops ascending over [a, b)
+  for (int base = a; base < b; base += 32) {
+    const int i = base + lane;
+    const bool is_l = i < b && !(q.v[i] > p);
+    const unsigned m = __ballot_sync(0xffffffffu, is_l);
+    if (is_l) pos_l[nl + __popc(m & ((1u << lane) - 1))] = static_cast<int16_t>(i);
+    nl += __popc(m);
+  }
+  // right stops descending over [a-1, b)
+  for (int top = b - 1; top >= a - 1; top -= 32) {
+    const int j = top - lane;
+    const bool is_r = j >= a - 1 && !(p > q.v[j]);
+    const unsigned m = __ballot_sync(0xffffffffu, is_r);
+    if (is_r) pos_r[nr + __popc(m & ((1u << lane) - 1))] = static_cast<int16_t>(j);
+    nr += __popc(m);
+  }
+  __syncwarp();
+  // pairs m with L[m] < R[m] form a prefix
+  int mstar = 0;
+  const int lim = nl < nr ? nl : nr;
+  for (int base = 0; base < lim; base += 32) {
+    const int m = base + lane;
+    const bool ok = m < lim && pos_l[m] < pos_r[m];
+    const unsigned bal = __ballot_sync(0xffffffffu, ok);
+    mstar += __popc(bal);
+    if (bal != 0xffffffffu) break;
+  }
+  for (int m = lane; m < mstar; m += 32) q.swap(pos_l[m], pos_r[m]);
+  __syncwarp();
+  if (mstar == 0) return pos_l[0];
+  const int lm = mstar < nl ? pos_l[mstar] : 1 << 30;
+  const int rm = pos_r[mstar - 1];
+  return lm < rm ? lm : rm;
+}
+
+// torch.topk(values, k) order for one row held in q.v / q.i (initialized in index order).
+// Leaves the selected pairs in q[0..k).
+__device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos_r, int lane) {
+  if (k * 64 <= n) {  // std::partial_sort
+    if (lane == 0) {
+      q_heap_select(q, 0, k, n);
+      for (int last = k; last > 1;) {
+        --last;
+        const float vv = q.v[last];
+        const int32_t vi = q.i[last];
+        q.v[last] = q.v[0]; q.i[last] = q.i[0];
+        q_adjust_heap(q, 0, 0, last, vv, vi);
+      }
+    }
+    __syncwarp();
+    return;
+  }
+  int first = 0, last = n;
+  const int nth = k - 1;
+  int depth = 2 * (31 - __clz(n));
+  bool heap_done = false;
+  while (last - first > 3) {
+    if (depth == 0) {
+      if (lane == 0) {
+        q_heap_select(q, first, nth + 1, last);
+        q.swap(first, nth);
+      }
+      heap_done = true;
+      break;
+    }
+    --depth;
+    const int mid = first + (last - first) / 2;
+    if (lane == 0) q_move_median_to_first(q, first, first + 1, mid, last - 1);
+    __syncwarp();
+    const int cut = warp_partition(q, first + 1, last, pos_l, pos_r, lane);
+    if (cut <= nth) first = cut;
+    else last = cut;
+  }
+  if (lane == 0) {
+    if (!heap_done) q_insertion_sort(q, first, last);
+    q_insertion_sort(q, 0, k - 1);
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------------ route kernel
+// One CTA; warp w handles tokens w, w + nwarps, ...  Dynamic smem per warp:
+// E floats + E ints + 2 * (E + 1) int16.
+template <typename LT>
+__global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logits, int64_t ldl, int T,
+                                                     int E, int k, int shared_col, int act_is_f16,
+                                                     void* ws) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  RouteView rv = route_view(ws, T, E, k);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int per_warp = E * 8 + 2 * (E + 2) * 2;
+  uint8_t* base = smem + warp * ((per_warp + 15) / 16 * 16);
+  Q q{reinterpret_cast<float*>(base), reinterpret_cast<int32_t*>(base + E * 4)};
+  int16_t* pos_l = reinterpret_cast<int16_t*>(base + E * 8);
+  int16_t* pos_r = pos_l + E + 2;
+  for (int t = warp; t < T; t += nw) {
+    const LT* row = logits + static_cast<int64_t>(t) * ldl;
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) {
+      const float v = to_f(row[e]);
+      q.v[e] = v;
+      q.i[e] = e;
+      mx = fmaxf(mx, v);
+    }
+    mx = warp_max(mx);
+    float z = 0.f;
+    for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
+    z = warp_sum(z);
+    __syncwarp();
+    warp_topk(q, E, k, pos_l, pos_r, lane);
+    // renormalized weights of the selected (fused_ops.py:162-164)
+    float p = 0.f;
+    if (lane < k) p = __expf(q.v[lane] - mx) / z;
+    float ps = p;
+    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    if (lane < k) {
+      const float w = p / ps;
+      rv.topk_idx[t * k + lane] = q.i[lane];
+      rv.topk_w[t * k + lane] = act_is_f16 ? rnd<__half>(w) : rbf(w);
+    }
+    if (lane == 0) {
+      float sg = 0.f;
+      if (shared_col >= 0) {
+        const float gl = to_f(row[shared_col]);
+        sg = act_is_f16 ? rnd<__half>(sigmoid_f(gl)) : rbf(sigmoid_f(gl));
+      }
+      rv.shared_gate[t] = sg;
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+  // expert -> pair lists (ascending expert, then ascending token)
+  int* cnt = reinterpret_cast<int*>(smem);       // reuse: [E] counts, [E] active position
+  int* apos = cnt + E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int pidx = threadIdx.x; pidx < T * k; pidx += blockDim.x) atomicAdd(&cnt[rv.topk_idx[pidx]], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int na = 0, off = 0;
+    for (int e = 0; e < E; ++e) {
+      if (cnt[e]) {
+        rv.active[na] = e;
+        rv.pair_off[na] = off;
+        apos[e] = off;
+        off += cnt[e];
+        ++na;
+      } else {
+        apos[e] = -1;
+      }
+    }
+    rv.pair_off[na] = off;
+    *rv.n_active = na;
+  }
+  __syncthreads();
+  for (int pidx = threadIdx.x; pidx < T * k; pidx += blockDim.x) {
+    const int t = pidx / k, s = pidx % k;
+    const int e = rv.topk_idx[pidx];
+    int rank = 0;
+    for (int u = 0; u < t; ++u)
+      for (int j = 0; j < k; ++j) rank += (rv.topk_idx[u * k + j] == e);
+    rv.pair_tok[apos[e] + rank] = t;
+    rv.pair_slot[apos[e] + rank] = s;
+  }
+}
+
+// ------------------------------------------------------------------ expert kernels
+template <typename ET>
+struct MoeArgs {
+  const ET* x;              // [T, H] expert input (post-attention RMSNorm output)
+  const uint8_t* gu;        // routed gate_up weights, expert e at gu + e * gu_stride
+  const uint8_t* dn;        // routed down weights
+  int64_t gu_stride, dn_stride;  // bytes per expert
+  int64_t gu_ld, dn_ld;          // row stride in bytes (row format only)
+  const uint8_t* sgu;       // shared expert gate|up ([2I, H]) and down ([H, I]), may be null
+  const uint8_t* sdn;
+  void* ws;                 // route workspace
+  ET* hbuf;                 // [T*k + T, I]
+  float* part;              // [T, k+1, H] raw expert outputs
+  int T, H, I, E, k, has_shared;
+};
+
+// Decode CTA slot -> (weights, number of pairs, pair list base); false if idle.
+template <typename ET>
+__device__ __forceinline__ bool slot_info(const MoeArgs<ET>& a, const RouteView& rv, int slot,
+                                          bool up, const uint8_t*& w, int& npairs, int& pbase) {
+  if (slot == 0) {
+    if (!a.has_shared) return false;
+    w = up ? a.sgu : a.sdn;
+    npairs = a.T;
+    pbase = -1;  // identity token list
+    return true;
+  }
+  const int ai = slot - 1;
+  if (ai >= *rv.n_active) return false;
+  const int e = rv.active[ai];
+  w = up ? a.gu + e * a.gu_stride : a.dn + e * a.dn_stride;
+  pbase = rv.pair_off[ai];
+  npairs = rv.pair_off[ai + 1] - pbase;
+  return true;
+}
+
+template <class Fmt, int PF>
+__global__ void __launch_bounds__(SG_WARPS * 32) moe_up_kernel(MoeArgs<typename Fmt::ET> a) {
+  using ET = typename Fmt::ET;
+  constexpr int NT = 2, NTOK = 16;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  const uint8_t* w;
+  int npairs, pbase;
+  if (!slot_info(a, rv, blockIdx.x, true, w, npairs, pbase)) return;
+  const int xstride = a.H + 8;
+  ET* xs = reinterpret_cast<ET*>(smem);
+  float* red = reinterpret_cast<float*>(smem + NTOK * xstride * 2);  // [8][2][NT*4][32]
+  int* toks = reinterpret_cast<int*>(red + SG_WARPS * 2 * NT * 4 * 32);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int jt = blockIdx.y;  // intermediate tile
+  const int nch = a.H / Fmt::KCHUNK;
+  const int c0 = warp * nch / SG_WARPS, c1 = (warp + 1) * nch / SG_WARPS;
+  const uint8_t* tg = w + Fmt::tile_offset(jt, a.H, a.gu_ld);
+  const uint8_t* tu = w + Fmt::tile_offset(a.I / 16 + jt, a.H, a.gu_ld);
+  const ET* xl = xs_lane_ptr(xs, xstride, lane);
+  for (int p0 = 0; p0 < npairs; p0 += NTOK) {
+    const int np = min(NTOK, npairs - p0);
+    __syncthreads();
+    if (threadIdx.x < NTOK) toks[threadIdx.x] = threadIdx.x < np ? (pbase < 0 ? p0 + threadIdx.x : rv.pair_tok[pbase + p0 + threadIdx.x]) : -1;
+    __syncthreads();
+    const int vpr = a.H / 8;
+    for (int i = threadIdx.x; i < NTOK * vpr; i += blockDim.x) {
+      const int r = i / vpr, c = (i % vpr) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (toks[r] >= 0) v = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(toks[r]) * a.H + c);
+      *reinterpret_cast<uint4*>(xs + r * xstride + c) = v;
+    }
+    __syncthreads();
+    float ag[NT][4], au[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) ag[j][r] = au[j][r] = 0.f;
+    stream_tile<Fmt, NT, PF>(tg, a.gu_ld, c0, c1, lane, xl, 16 * xstride, ag);
+    stream_tile<Fmt, NT, PF>(tu, a.gu_ld, c0, c1, lane, xl, 16 * xstride, au);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        red[((warp * 2 + 0) * NT * 4 + j * 4 + r) * 32 + lane] = ag[j][r];
+        red[((warp * 2 + 1) * NT * 4 + j * 4 + r) * 32 + lane] = au[j][r];
+      }
+    __syncthreads();
+    // warp 0 reduces and applies SiLU(gate) * up with the reference's rounding points
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float g = 0.f, u = 0.f;
+          for (int s = 0; s < SG_WARPS; ++s) {
+            g += red[((s * 2 + 0) * NT * 4 + j * 4 + r) * 32 + lane];
+            u += red[((s * 2 + 1) * NT * 4 + j * 4 + r) * 32 + lane];
+          }
+          const int tl = frag_tok(lane, j, r);
+          if (tl < np) {
+            const float gr = rnd<ET>(g), ur = rnd<ET>(u);
+            const float h = rnd<ET>(rnd<ET>(silu_f(gr)) * ur);
+            const int64_t hrow = pbase < 0 ? static_cast<int64_t>(a.T) * a.k + p0 + tl : pbase + p0 + tl;
+            a.hbuf[hrow * a.I + jt * 16 + frag_row(lane, r)] = from_f<ET>(h);
+          }
+        }
+    }
+  }
+}
+
+template <class Fmt, int PF>
+__global__ void __launch_bounds__(SG_WARPS * 32) moe_down_kernel(MoeArgs<typename Fmt::ET> a) {
+  using ET = typename Fmt::ET;
+  constexpr int NT = 2, NTOK = 16;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  const uint8_t* w;
+  int npairs, pbase;
+  if (!slot_info(a, rv, blockIdx.x, false, w, npairs, pbase)) return;
+  const int xstride = a.I + 8;
+  ET* xs = reinterpret_cast<ET*>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rt = blockIdx.y * SG_WARPS + warp;   // output row tile
+  const bool active = rt < a.H / 16;
+  const int nch = a.I / Fmt::KCHUNK;
+  const uint8_t* tile = w + Fmt::tile_offset(active ? rt : 0, a.I, a.dn_ld);
+  const ET* xl = xs_lane_ptr(xs, xstride, lane);
+  const int64_t hbase = pbase < 0 ? static_cast<int64_t>(a.T) * a.k : pbase;
+  for (int p0 = 0; p0 < npairs; p0 += NTOK) {
+    const int np = min(NTOK, npairs - p0);
+    __syncthreads();
+    const int vpr = a.I / 8;
+    for (int i = threadIdx.x; i < NTOK * vpr; i += blockDim.x) {
+      const int r = i / vpr, c = (i % vpr) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < np) v = *reinterpret_cast<const uint4*>(a.hbuf + (hbase + p0 + r) * a.I + c);
+      *reinterpret_cast<uint4*>(xs + r * xstride + c) = v;
+    }
+    __syncthreads();
+    if (!active) continue;
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    stream_tile<Fmt, NT, PF>(tile, a.dn_ld, 0, nch, lane, xl, 16 * xstride, acc);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int tl = frag_tok(lane, j, r);
+        if (tl < np) {
+          int tok, slot;
+          if (pbase < 0) { tok = p0 + tl; slot = a.k; }
+          else { tok = rv.pair_tok[pbase + p0 + tl]; slot = rv.pair_slot[pbase + p0 + tl]; }
+          a.part[(static_cast<int64_t>(tok) * (a.k + 1) + slot) * a.H + rt * 16 + frag_row(lane, r)] = acc[j][r];
+        }
+      }
+  }
+}
+
+// Combine (fused/model.py:296-307 with fused_ops.py:165-172): per token, the routed
+// experts in ascending id, each raw output rounded to the activation dtype, times its
+// weight (rounded), added with a rounding; then + round(round(shared) * gate) when a
+// shared expert is present; then, in residual mode, out = round(out + moe) in place.
+template <typename ET>
+__global__ void moe_combine_kernel(const float* __restrict__ part, void* ws, ET* __restrict__ out,
+                                   int T, int H, int E, int k, int has_shared, int residual) {
+  const RouteView rv = route_view(ws, T, E, k);
+  const int t = blockIdx.x;
+  int order[32];
+  for (int j = 0; j < k; ++j) order[j] = j;
+  for (int i = 1; i < k; ++i)
+    for (int j = i; j > 0 && rv.topk_idx[t * k + order[j]] < rv.topk_idx[t * k + order[j - 1]]; --j) {
+      int tmp = order[j]; order[j] = order[j - 1]; order[j - 1] = tmp;
+    }
+  const float sg = has_shared ? rv.shared_gate[t] : 0.f;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int s = order[j];
+      const float y = rnd<ET>(part[(static_cast<int64_t>(t) * (k + 1) + s) * H + c]);
+      acc = rnd<ET>(acc + rnd<ET>(y * rv.topk_w[t * k + s]));
+    }
+    if (has_shared) {
+      const float y = rnd<ET>(part[(static_cast<int64_t>(t) * (k + 1) + k) * H + c]);
+      acc = rnd<ET>(acc + rnd<ET>(y * sg));
+    }
+    ET* o = out + static_cast<int64_t>(t) * H + c;
+    *o = from_f<ET>(residual ? to_f(*o) + acc : acc);
+  }
+}
+
+// Router logits of the fused-ops operator: dense [E, H] weights, one warp per (t, e),
+// fp32 accumulate, one rounding to the activation dtype.
+template <typename ET>
+__global__ void router_dense_kernel(const ET* __restrict__ x, const ET* __restrict__ w, ET* __restrict__ out,
+                                    int T, int H, int E) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (gw >= T * E) return;
+  const int t = gw / E, e = gw % E;
+  float acc = 0.f;
+  for (int c = lane; c < H; c += 32) acc = fmaf(to_f(x[static_cast<int64_t>(t) * H + c]), to_f(w[static_cast<int64_t>(e) * H + c]), acc);
+  acc = warp_sum(acc);
+  if (lane == 0) out[static_cast<int64_t>(t) * E + e] = from_f<ET>(acc);
+}
+
+// ------------------------------------------------------------------ host launchers
+template <typename LT>
+static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, int shared_col,
+                        int act_is_f16, void* ws, cudaStream_t s) {
+  const int nw = T < 32 ? T : 32;
+  const int per_warp = ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16;
+  size_t smem = static_cast<size_t>(nw) * per_warp;
+  if (smem < static_cast<size_t>(E) * 8) smem = static_cast<size_t>(E) * 8;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(route_kernel<LT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (err != cudaSuccess) return cuda_status(err, "route smem attribute");
+  if (smem > 200 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
+  route_kernel<LT><<<1, nw * 32, smem, s>>>(static_cast<const LT*>(logits), ldl, T, E, k, shared_col,
+                                            act_is_f16, ws);
+  QW_LAUNCH_CHECK("moe route");
+  return QW_OK;
+}
+
+template <class Fmt, int PF>
+static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s) {
+  constexpr int NTOK = 16, NT = 2;
+  const int slots = 1 + (a.E < a.T * a.k ? a.E : a.T * a.k);
+  const size_t smem_up = NTOK * (a.H + 8) * 2 + SG_WARPS * 2 * NT * 4 * 32 * 4 + NTOK * 4;
+  const size_t smem_dn = NTOK * (a.I + 8) * 2;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(moe_up_kernel<Fmt, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (err == cudaSuccess)
+      err = cudaFuncSetAttribute(moe_down_kernel<Fmt, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  });
+  if (err != cudaSuccess) return cuda_status(err, "moe smem attribute");
+  if (smem_up > 200 * 1024 || smem_dn > 200 * 1024) return fail(QW_ERR_UNSUPPORTED, "moe: hidden size too large");
+  moe_up_kernel<Fmt, PF><<<dim3(slots, a.I / 16), SG_WARPS * 32, smem_up, s>>>(a);
+  QW_LAUNCH_CHECK("moe up");
+  moe_down_kernel<Fmt, PF><<<dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS), SG_WARPS * 32, smem_dn, s>>>(a);
+  QW_LAUNCH_CHECK("moe down");
+  return QW_OK;
+}
+
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" int64_t qw_moe_workspace_bytes(int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
+                                          int64_t top_k) {
+  if (tokens < 0 || hidden <= 0 || experts <= 0 || inter <= 0 || top_k <= 0) return -1;
+  const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
+  int64_t b = route_ints(T, E, k) * 4;
+  b = (b + 255) / 256 * 256;
+  b += (static_cast<int64_t>(T) * k + T) * inter * 2;          // hbuf (16-bit)
+  b = (b + 255) / 256 * 256;
+  b += static_cast<int64_t>(T) * (k + 1) * hidden * 4;          // part
+  b += static_cast<int64_t>(T) * experts * 2 + 256;             // dense-router logits
+  return b;
+}
+
+struct WsParts {
+  void* route;
+  void* hbuf;
+  float* part;
+  void* logits;
+};
+
+static WsParts split_ws(void* ws, int T, int H, int E, int I, int k) {
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  WsParts w;
+  w.route = p;
+  int64_t off = (route_ints(T, E, k) * 4 + 255) / 256 * 256;
+  w.hbuf = p + off;
+  off += (static_cast<int64_t>(T) * k + T) * I * 2;
+  off = (off + 255) / 256 * 256;
+  w.part = reinterpret_cast<float*>(p + off);
+  off += static_cast<int64_t>(T) * (k + 1) * H * 4;
+  w.logits = p + off;
+  return w;
+}
+
+extern "C" int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
+                            int64_t top_k, int64_t shared_col, int act_dtype, void* workspace, void* stream) {
+  QW_CHECK_ARG(logits && workspace, "moe_route: null pointer");
+  QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && experts >= 1 && experts <= 1024 && top_k >= 1 &&
+                   top_k <= 16 && top_k <= experts && ldl >= experts,
+               "MoE needs compatible expert weights and a valid top_k");
+  QW_CHECK_ARG(act_dtype == QW_BF16 || act_dtype == QW_F16, "moe_route: activation dtype");
+  const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
+  cudaStream_t s = as_stream(stream);
+  if (logit_dtype == QW_BF16)
+    return launch_route<__nv_bfloat16>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
+  if (logit_dtype == QW_F16)
+    return launch_route<__half>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
+  if (logit_dtype == QW_F32)
+    return launch_route<float>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
+  return fail(QW_ERR_ARG, "moe_route: bad logit dtype");
+}
+
+extern "C" int qw_moe_experts_w4(const void* x, const void* gate_up, const void* down,
+                                 const void* shared_gate_up, const void* shared_down, int64_t tokens,
+                                 int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
+                                 int32_t group, void* workspace, void* stream) {
+  QW_CHECK_ARG(x && gate_up && down && workspace, "moe_experts: null pointer");
+  QW_CHECK_ARG((shared_gate_up == nullptr) == (shared_down == nullptr), "moe_experts: shared expert pointers");
+  QW_CHECK_ARG(group == 32 || group == 64 || group == 128, "moe_experts: group must be 32, 64 or 128");
+  QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && hidden % group == 0 && inter % group == 0 && inter % 16 == 0 &&
+                   hidden % 16 == 0 && top_k >= 1 && top_k <= 32 && experts >= top_k,
+               "moe_experts: invalid shape");
+  const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
+            I = static_cast<int>(inter), k = static_cast<int>(top_k);
+  WsParts w = split_ws(workspace, T, H, E, I, k);
+  MoeArgs<__nv_bfloat16> a{};
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.gu = static_cast<const uint8_t*>(gate_up);
+  a.dn = static_cast<const uint8_t*>(down);
+  a.gu_stride = qw_w4_stream_bytes(2 * inter, hidden, group);
+  a.dn_stride = qw_w4_stream_bytes(hidden, inter, group);
+  a.sgu = static_cast<const uint8_t*>(shared_gate_up);
+  a.sdn = static_cast<const uint8_t*>(shared_down);
+  a.ws = w.route;
+  a.hbuf = static_cast<__nv_bfloat16*>(w.hbuf);
+  a.part = w.part;
+  a.T = T; a.H = H; a.I = I; a.E = E; a.k = k;
+  a.has_shared = shared_gate_up != nullptr;
+  cudaStream_t s = as_stream(stream);
+  switch (group) {
+    case 128: return launch_experts<W4Fmt<128>, 4>(a, s);
+    case 64: return launch_experts<W4Fmt<64>, 4>(a, s);
+    default: return launch_experts<W4Fmt<32>, 8>(a, s);
+  }
+}
+
+extern "C" int qw_moe_partials(void* workspace, int64_t tokens, int64_t hidden, int64_t experts,
+                               int64_t inter, int64_t top_k, const float** part, const int32_t** topk_idx,
+                               const float** topk_w, const float** shared_gate) {
+  QW_CHECK_ARG(workspace, "moe_partials: null workspace");
+  const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
+  WsParts w = split_ws(workspace, T, static_cast<int>(hidden), E, static_cast<int>(inter), k);
+  RouteView rv = route_view(w.route, T, E, k);
+  if (part) *part = w.part;
+  if (topk_idx) *topk_idx = rv.topk_idx;
+  if (topk_w) *topk_w = rv.topk_w;
+  if (shared_gate) *shared_gate = rv.shared_gate;
+  return QW_OK;
+}
+
+extern "C" int qw_moe_combine(void* workspace, void* out, int residual, int64_t tokens, int64_t hidden,
+                              int64_t experts, int64_t inter, int64_t top_k, int has_shared, void* stream) {
+  QW_CHECK_ARG(workspace && out, "moe_combine: null pointer");
+  QW_CHECK_ARG(tokens >= 1 && top_k >= 1 && top_k <= 32 && hidden > 0, "moe_combine: invalid shape");
+  const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
+            I = static_cast<int>(inter), k = static_cast<int>(top_k);
+  WsParts w = split_ws(workspace, T, H, E, I, k);
+  moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, as_stream(stream)>>>(
+      w.part, w.route, static_cast<__nv_bfloat16*>(out), T, H, E, k, has_shared, residual);
+  QW_LAUNCH_CHECK("moe combine");
+  return QW_OK;
+}
+
+extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_up, const void* down, void* out,
+                      int dtype, int64_t tokens, int64_t hidden_dim, int64_t experts, int64_t inter,
+                      int64_t top_k, int32_t* topk_idx_out, void* workspace, void* stream) {
+  QW_CHECK_ARG(hidden && router && gate_up && down && out && workspace, "moe: null pointer");
+  QW_CHECK_ARG(dtype == QW_BF16 || dtype == QW_F16, "moe: bf16 or fp16 tensors required");
+  QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && experts >= 1 && experts <= 1024 && top_k >= 1 && top_k <= 16 &&
+                   top_k <= experts && hidden_dim % 16 == 0 && inter % 16 == 0 && hidden_dim > 0 && inter > 0,
+               "MoE needs compatible expert weights and a valid top_k");
+  const int T = static_cast<int>(tokens), H = static_cast<int>(hidden_dim), E = static_cast<int>(experts),
+            I = static_cast<int>(inter), k = static_cast<int>(top_k);
+  cudaStream_t s = as_stream(stream);
+  WsParts w = split_ws(workspace, T, H, E, I, k);
+  const int warps = T * E;
+  const unsigned rblocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  int st;
+  if (dtype == QW_BF16) {
+    router_dense_kernel<__nv_bfloat16><<<rblocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(router),
+        static_cast<__nv_bfloat16*>(w.logits), T, H, E);
+    QW_LAUNCH_CHECK("moe router");
+    st = launch_route<__nv_bfloat16>(w.logits, E, T, E, k, -1, 0, w.route, s);
+  } else {
+    router_dense_kernel<__half><<<rblocks, 256, 0, s>>>(static_cast<const __half*>(hidden),
+                                                        static_cast<const __half*>(router),
+                                                        static_cast<__half*>(w.logits), T, H, E);
+    QW_LAUNCH_CHECK("moe router");
+    st = launch_route<__half>(w.logits, E, T, E, k, -1, 1, w.route, s);
+  }
+  if (st) return st;
+  if (dtype == QW_BF16) {
+    MoeArgs<__nv_bfloat16> a{};
+    a.x = static_cast<const __nv_bfloat16*>(hidden);
+    a.gu = static_cast<const uint8_t*>(gate_up);
+    a.dn = static_cast<const uint8_t*>(down);
+    a.gu_stride = 2LL * I * H * 2; a.dn_stride = 1LL * H * I * 2;
+    a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
+    a.ws = w.route; a.hbuf = static_cast<__nv_bfloat16*>(w.hbuf); a.part = w.part;
+    a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
+    st = launch_experts<RowFmt<__nv_bfloat16>, 4>(a, s);
+    if (st) return st;
+    moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__nv_bfloat16*>(out), T, H, E, k, 0, 0);
+  } else {
+    MoeArgs<__half> a{};
+    a.x = static_cast<const __half*>(hidden);
+    a.gu = static_cast<const uint8_t*>(gate_up);
+    a.dn = static_cast<const uint8_t*>(down);
+    a.gu_stride = 2LL * I * H * 2; a.dn_stride = 1LL * H * I * 2;
+    a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
+    a.ws = w.route; a.hbuf = static_cast<__half*>(w.hbuf); a.part = w.part;
+    a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
+    st = launch_experts<RowFmt<__half>, 4>(a, s);
+    if (st) return st;
+    moe_combine_kernel<__half><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__half*>(out), T, H, E, k, 0, 0);
+  }
+  QW_LAUNCH_CHECK("moe combine");
+  if (topk_idx_out) {
+    RouteView rv = route_view(w.route, T, E, k);
+    cudaError_t e = cudaMemcpyAsync(topk_idx_out, rv.topk_idx, sizeof(int32_t) * T * k, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_status(e, "moe topk copy");
+  }
+  return QW_OK;
+}

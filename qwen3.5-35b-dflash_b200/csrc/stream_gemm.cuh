@@ -17,6 +17,9 @@
 //
 //   B16 stream (bf16), per 16-row tile and 64-wide K chunk 2048 bytes: 4 k16-steps x
 //   32 lanes x one 16-byte vector holding the lane's 4 A-fragment registers.
+//
+//   Row format: a plain row-major [N, K] 16-bit matrix (the fused-ops ABI passes dense
+//   expert weights); fragments are gathered with 32-bit loads.
 #pragma once
 
 #include "qw_common.cuh"
@@ -27,6 +30,7 @@ constexpr int SG_WARPS = 8;
 
 template <int G>
 struct W4Fmt {
+  using ET = __nv_bfloat16;
   static constexpr int KCHUNK = G;
   static constexpr int STEPS = G / 16;
   static constexpr int WORDS = STEPS;              // 32-bit words per lane per chunk
@@ -35,8 +39,13 @@ struct W4Fmt {
   static constexpr int CHB = 8 * G + 32;
   static constexpr bool SCALED = true;
 
-  __device__ __forceinline__ static void load(const uint8_t* chunk, int lane, uint32_t (&w)[WORDS],
-                                              uint32_t& sc) {
+  // byte offset of row tile `rt` of a matrix with `k` columns (ld unused)
+  __host__ __device__ static int64_t tile_offset(int64_t rt, int k, int64_t /*ld*/) {
+    return rt * (k / G) * static_cast<int64_t>(CHB);
+  }
+  __device__ __forceinline__ static void load(const uint8_t* tile, int c, int lane, int64_t /*ld*/,
+                                              uint32_t (&w)[WORDS], uint32_t& sc) {
+    const uint8_t* chunk = tile + static_cast<int64_t>(c) * CHB;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       const uint8_t* p = chunk + v * (32 * VW * 4) + lane * (VW * 4);
@@ -58,14 +67,19 @@ struct W4Fmt {
 };
 
 struct B16Fmt {
+  using ET = __nv_bfloat16;
   static constexpr int KCHUNK = 64;
   static constexpr int STEPS = 4;
   static constexpr int WORDS = 16;
   static constexpr int CHB = 2048;
   static constexpr bool SCALED = false;
 
-  __device__ __forceinline__ static void load(const uint8_t* chunk, int lane, uint32_t (&w)[WORDS],
-                                              uint32_t& sc) {
+  __host__ __device__ static int64_t tile_offset(int64_t rt, int k, int64_t /*ld*/) {
+    return rt * (k / 64) * static_cast<int64_t>(CHB);
+  }
+  __device__ __forceinline__ static void load(const uint8_t* tile, int c, int lane, int64_t /*ld*/,
+                                              uint32_t (&w)[WORDS], uint32_t& sc) {
+    const uint8_t* chunk = tile + static_cast<int64_t>(c) * CHB;
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
       uint4 u = ldg_stream(chunk + s * 512 + lane * 16);
@@ -78,32 +92,58 @@ struct B16Fmt {
   }
 };
 
+// Row-major 16-bit matrix [N, K] with row stride `ld` bytes; K chunk of 16.
+template <typename ET_>
+struct RowFmt {
+  using ET = ET_;
+  static constexpr int KCHUNK = 16;
+  static constexpr int STEPS = 1;
+  static constexpr int WORDS = 4;
+  static constexpr bool SCALED = false;
+
+  __host__ __device__ static int64_t tile_offset(int64_t rt, int /*k*/, int64_t ld) {
+    return rt * 16 * ld;
+  }
+  __device__ __forceinline__ static void load(const uint8_t* tile, int c, int lane, int64_t ld,
+                                              uint32_t (&w)[WORDS], uint32_t& sc) {
+    const int gid = lane >> 2, tig = lane & 3;
+    const uint8_t* p = tile + static_cast<int64_t>(gid) * ld + (c * 16 + 2 * tig) * 2;
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+    w[1] = __ldg(reinterpret_cast<const uint32_t*>(p + 8 * ld));
+    w[2] = __ldg(reinterpret_cast<const uint32_t*>(p + 16));
+    w[3] = __ldg(reinterpret_cast<const uint32_t*>(p + 8 * ld + 16));
+    sc = 0;
+  }
+  __device__ __forceinline__ static void afrag(const uint32_t (&w)[WORDS], int /*s*/, uint32_t (&a)[4]) {
+    a[0] = w[0]; a[1] = w[1]; a[2] = w[2]; a[3] = w[3];
+  }
+};
+
 // Accumulate one chunk of one 16-row weight tile against NT n-tiles (8 tokens each) of
-// activations held in shared memory as xs[token][k] (row stride `xstride` elements).
-// `xrow` points to the row-address table of this lane for ldmatrix.x4 (token block 0).
+// activations held in shared memory as xs[token][k].  `xs_lane` is this lane's
+// ldmatrix.x4 row address for token block 0 at k = 0; token block j is `j * xstride16`
+// elements further.
 template <class Fmt, int NT>
 __device__ __forceinline__ void mma_chunk(const uint32_t (&w)[Fmt::WORDS], uint32_t sc,
-                                          const __nv_bfloat16* xs_lane, int xstride16, int kbase,
+                                          const typename Fmt::ET* xs_lane, int xstride16, int kbase,
                                           float (&acc)[NT][4]) {
-  float part[NT][4];
-  float(&dst)[NT][4] = Fmt::SCALED ? part : acc;
+  using ET = typename Fmt::ET;
   if constexpr (Fmt::SCALED) {
+    float part[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.f;
-  }
 #pragma unroll
-  for (int s = 0; s < Fmt::STEPS; ++s) {
-    uint32_t a[4];
-    Fmt::afrag(w, s, a);
+    for (int s = 0; s < Fmt::STEPS; ++s) {
+      uint32_t a[4];
+      Fmt::afrag(w, s, a);
 #pragma unroll
-    for (int j = 0; j < NT / 2; ++j) {
-      uint32_t b[4];
-      ldmatrix_x4(b, xs_lane + j * xstride16 + kbase + s * 16);
-      mma_bf16_16816(dst[2 * j], a, b[0], b[1]);
-      mma_bf16_16816(dst[2 * j + 1], a, b[2], b[3]);
+      for (int j = 0; j < NT / 2; ++j) {
+        uint32_t b[4];
+        ldmatrix_x4(b, xs_lane + j * xstride16 + kbase + s * 16);
+        mma16816<ET>(part[2 * j], a, b[0], b[1]);
+        mma16816<ET>(part[2 * j + 1], a, b[2], b[3]);
+      }
     }
-  }
-  if constexpr (Fmt::SCALED) {
     const float2 s2 = bf162_to_f2(sc);  // (row gid, row gid + 8)
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
@@ -112,38 +152,53 @@ __device__ __forceinline__ void mma_chunk(const uint32_t (&w)[Fmt::WORDS], uint3
       acc[j][2] = fmaf(part[j][2], s2.y, acc[j][2]);
       acc[j][3] = fmaf(part[j][3], s2.y, acc[j][3]);
     }
+  } else {
+#pragma unroll
+    for (int s = 0; s < Fmt::STEPS; ++s) {
+      uint32_t a[4];
+      Fmt::afrag(w, s, a);
+#pragma unroll
+      for (int j = 0; j < NT / 2; ++j) {
+        uint32_t b[4];
+        ldmatrix_x4(b, xs_lane + j * xstride16 + kbase + s * 16);
+        mma16816<ET>(acc[2 * j], a, b[0], b[1]);
+        mma16816<ET>(acc[2 * j + 1], a, b[2], b[3]);
+      }
+    }
   }
 }
 
-// Stream chunks [c0, c1) of one row tile (chunk pointer base `tile`) with a PF-deep
-// register prefetch ring.
+// Stream chunks [c0, c1) of one row tile with a PF-deep register prefetch ring.
 template <class Fmt, int NT, int PF>
-__device__ __forceinline__ void stream_tile(const uint8_t* tile, int c0, int c1, int lane,
-                                            const __nv_bfloat16* xs_lane, int xstride16,
+__device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int c0, int c1, int lane,
+                                            const typename Fmt::ET* xs_lane, int xstride16,
                                             float (&acc)[NT][4]) {
   uint32_t w[PF][Fmt::WORDS];
   uint32_t sc[PF];
 #pragma unroll
   for (int p = 0; p < PF; ++p)
-    if (c0 + p < c1) Fmt::load(tile + static_cast<int64_t>(c0 + p) * Fmt::CHB, lane, w[p], sc[p]);
+    if (c0 + p < c1) Fmt::load(tile, c0 + p, lane, ld, w[p], sc[p]);
   for (int c = c0; c < c1; c += PF) {
 #pragma unroll
     for (int p = 0; p < PF; ++p) {
       if (c + p < c1) {
         mma_chunk<Fmt, NT>(w[p], sc[p], xs_lane, xstride16, (c + p) * Fmt::KCHUNK, acc);
-        if (c + p + PF < c1)
-          Fmt::load(tile + static_cast<int64_t>(c + p + PF) * Fmt::CHB, lane, w[p], sc[p]);
+        if (c + p + PF < c1) Fmt::load(tile, c + p + PF, lane, ld, w[p], sc[p]);
       }
     }
   }
 }
 
 // Address of this lane's ldmatrix.x4 row for token block 0 (tokens 0..15) at k = 0.
-__device__ __forceinline__ const __nv_bfloat16* xs_lane_ptr(const __nv_bfloat16* xs, int xstride,
-                                                            int lane) {
+template <typename ET>
+__device__ __forceinline__ const ET* xs_lane_ptr(const ET* xs, int xstride, int lane) {
   const int tok = ((lane >> 4) << 3) + (lane & 7);
   const int kof = ((lane >> 3) & 1) << 3;
   return xs + tok * xstride + kof;
 }
+
+// Fragment element r (0..3) of n-tile j: (row within the 16-row tile, token).
+__device__ __forceinline__ int frag_row(int lane, int r) { return (lane >> 2) + 8 * (r >> 1); }
+__device__ __forceinline__ int frag_tok(int lane, int j, int r) { return j * 8 + 2 * (lane & 3) + (r & 1); }
 
 }  // namespace qw

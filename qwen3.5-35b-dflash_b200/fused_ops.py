@@ -177,9 +177,13 @@ def attention(query: Tensor, key: Tensor, value: Tensor, *, query_start: int,
     b, h, s, d = query.shape
     q, k, v = query.contiguous(), key.contiguous(), value.contiguous()
     out = torch.empty_like(q)
+    nbytes = lib.load().qw_attn_workspace_bytes(b, h, key.shape[1], s, d, key.shape[-2])
+    if nbytes < 0:
+        raise ValueError("attention requires causal append-only GQA [B,H,S,D] inputs")
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
     lib.call("qw_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
              lib.dtype_code(q.dtype), b, h, key.shape[1], s, key.shape[-2], d, query_start,
-             float(scale), _s(q))
+             float(scale), ws.data_ptr(), _s(q))
     return out
 
 
@@ -211,8 +215,10 @@ def moe_with_routing(hidden: Tensor, router_weight: Tensor, gate_up: Tensor, dow
     out = torch.empty_like(flat)
     idx = torch.empty(t, top_k, dtype=torch.int32, device=hidden.device)
     r, gu, dn = router_weight.contiguous(), gate_up.contiguous(), down.contiguous()
+    nbytes = lib.load().qw_moe_workspace_bytes(t, hdim, e, two_i // 2, top_k)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=hidden.device)
     lib.call("qw_moe", flat.data_ptr(), r.data_ptr(), gu.data_ptr(), dn.data_ptr(), out.data_ptr(),
-             lib.dtype_code(dt), t, hdim, e, two_i // 2, top_k, idx.data_ptr(), _s(flat))
+             lib.dtype_code(dt), t, hdim, e, two_i // 2, top_k, idx.data_ptr(), ws.data_ptr(), _s(flat))
     return out.reshape_as(hidden), idx
 
 

@@ -45,8 +45,19 @@ SIGNATURES = {
     "qw_gated_delta_rule": (_c.c_int, [P, P, P, P, P, _c.c_int, P, _c.c_int, P, P, P,
                                        I64, I64, I64, I64, I64, _c.c_int, P]),
     "qw_cache_update": (_c.c_int, [P, P, P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, P]),
-    "qw_attention": (_c.c_int, [P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, I64, I64, F32, P]),
-    "qw_moe": (_c.c_int, [P, P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, P, P]),
+    "qw_attention": (_c.c_int, [P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, I64, I64, F32, P, P]),
+    "qw_attn_workspace_bytes": (I64, [I64, I64, I64, I64, I64, I64]),
+    "qw_attn_prep": (_c.c_int, [P, I64, P, P, F32, F32, I32, P, P, I32, I32, P, P, P, I64, I64, I64,
+                                I64, I64, P]),
+    "qw_attn_paged": (_c.c_int, [P, P, P, P, I32, I32, P, I64, P, I64, P, I64, I64, I64, I64, I64,
+                                 F32, P, P]),
+    "qw_moe": (_c.c_int, [P, P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, P, P, P]),
+    "qw_moe_workspace_bytes": (I64, [I64, I64, I64, I64, I64]),
+    "qw_moe_route": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, P]),
+    "qw_moe_experts_w4": (_c.c_int, [P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P]),
+    "qw_moe_combine": (_c.c_int, [P, P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P]),
+    "qw_moe_partials": (_c.c_int, [P, I64, I64, I64, I64, I64, _c.POINTER(P), _c.POINTER(P),
+                                   _c.POINTER(P), _c.POINTER(P)]),
     "qw_w4_stream_bytes": (I64, [I64, I64, I32]),
     "qw_b16_stream_bytes": (I64, [I64, I64]),
     "qw_w4_linear": (_c.c_int, [P, P, P, _c.c_int, I64, I64, I64, I64, I32, P]),

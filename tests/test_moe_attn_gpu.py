@@ -1,0 +1,207 @@
+"""MoE routing/experts and attention kernels vs the oracle and the reference (GPU)."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, to_np, bf16_tensor
+from oracle import fused_ops_np as F
+from oracle.model_np import OracleTarget
+from oracle.numerics import bf16_round
+
+pytestmark = pytest.mark.gpu
+
+DT = {"bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def _t(a, dtype):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda().to(dtype)
+
+
+def _lowp(golden, tag):
+    return {k[len(tag) + 1:]: v for k, v in golden("ops_lowp.npz").items() if k.startswith(tag + "_")}
+
+
+@pytest.mark.parametrize("tag", ["bf16", "f16"])
+def test_moe_operator_matches_reference(golden, cuda_lib, tag):
+    from qwen35_dflash_b200 import fused_ops as Q
+    d = _lowp(golden, tag)
+    ulp = 2 ** -8 if tag == "bf16" else 2 ** -11
+    out, idx = Q.moe_with_routing(_t(d["moe_x"], DT[tag]), _t(d["moe_router"], DT[tag]),
+                                  _t(d["moe_gu"], DT[tag]), _t(d["moe_down"], DT[tag]), top_k=4)
+    assert out.dtype == DT[tag]
+    assert_close(to_np(out), d["moe_y"], 4 * ulp, 4 * ulp, "moe")
+    _, sel, _ = F.moe(d["moe_x"], d["moe_router"], d["moe_gu"], d["moe_down"], top_k=4, dtype=tag,
+                      return_routing=True)
+    np.testing.assert_array_equal(idx.cpu().numpy(), sel)
+
+
+def _tie_heavy_logits(t, e, seed):
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(t, e, generator=g)
+    logits[::4] = torch.randint(-3, 3, (len(range(0, t, 4)), e), generator=g).float()
+    return logits.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("t,e,k", [(16, 256, 8), (256, 256, 8), (64, 16, 4), (33, 128, 8), (40, 256, 2)])
+def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k):
+    """Router selection equals torch.topk on CPU (the reference's call) element for element."""
+    from qwen35_dflash_b200 import lib
+    logits = _tie_heavy_logits(t, e, seed=t * 7 + e)
+    probs = torch.softmax(logits.float(), -1)
+    _, want = torch.topk(probs, k, dim=-1)
+    dev = logits.cuda()
+    nbytes = cuda_lib.qw_moe_workspace_bytes(t, 256, e, 128, k)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    lib.call("qw_moe_route", dev.data_ptr(), lib.QW_BF16, e, t, e, k, -1, lib.QW_BF16, ws.data_ptr(),
+             lib.stream_ptr())
+    idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu()
+    np.testing.assert_array_equal(idx.numpy(), want.numpy())
+    w = ws[t * k * 4: 2 * t * k * 4].view(torch.float32).view(t, k).cpu()
+    sel = torch.gather(probs, 1, want.long())
+    ref_w = (sel / sel.sum(-1, keepdim=True)).to(torch.bfloat16).float()
+    assert_close(w.numpy(), ref_w.numpy(), 2 ** -8, 2 ** -7, "route weights")
+
+
+class _LazyDequant:
+    def __init__(self, q, s, group):
+        self.q, self.s, self.group = q, s, group
+
+    def __getitem__(self, e):
+        return (self.q[e].astype(np.float32) * np.repeat(self.s[e], self.group, -1)).astype(np.float32)
+
+
+@pytest.mark.parametrize("t", [16, 64])
+def test_moe_w4a16_matches_oracle(cuda_lib, t):
+    """Config-2 microbench shape: H 2048, 256 experts top-8 + shared, I 512, W4 g128."""
+    from qwen35_dflash_b200 import lib, w4
+    torch.manual_seed(t)
+    h, e, k, inter, g = 2048, 256, 8, 512, 128
+    x = torch.randn(t, h, device="cuda").to(torch.bfloat16)
+    logits = torch.cat([_tie_heavy_logits(t, e, seed=t).cuda(),
+                        torch.randn(t, 1, device="cuda").to(torch.bfloat16)], 1).contiguous()
+    qgu = torch.randint(-8, 8, (e, 2 * inter, h), dtype=torch.int8, device="cuda")
+    sgu = (torch.rand(e, 2 * inter, h // g, device="cuda") * 0.015 + 0.005).to(torch.bfloat16)
+    qdn = torch.randint(-8, 8, (e, h, inter), dtype=torch.int8, device="cuda")
+    sdn = (torch.rand(e, h, inter // g, device="cuda") * 0.015 + 0.005).to(torch.bfloat16)
+    qsgu = torch.randint(-8, 8, (2 * inter, h), dtype=torch.int8, device="cuda")
+    ssgu = (torch.rand(2 * inter, h // g, device="cuda") * 0.015 + 0.005).to(torch.bfloat16)
+    qsdn = torch.randint(-8, 8, (h, inter), dtype=torch.int8, device="cuda")
+    ssdn = (torch.rand(h, inter // g, device="cuda") * 0.015 + 0.005).to(torch.bfloat16)
+    gu_s, dn_s = w4.pack_w4(qgu, sgu, g), w4.pack_w4(qdn, sdn, g)
+    sgu_s, sdn_s = w4.pack_w4(qsgu, ssgu, g), w4.pack_w4(qsdn, ssdn, g)
+    ws = torch.zeros(cuda_lib.qw_moe_workspace_bytes(t, h, e, inter, k), dtype=torch.uint8, device="cuda")
+    out = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+    st = lib.stream_ptr()
+    lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws.data_ptr(), st)
+    lib.call("qw_moe_experts_w4", x.data_ptr(), gu_s.data_ptr(), dn_s.data_ptr(), sgu_s.data_ptr(),
+             sdn_s.data_ptr(), t, h, e, inter, k, g, ws.data_ptr(), st)
+    lib.call("qw_moe_combine", ws.data_ptr(), out.data_ptr(), 0, t, h, e, inter, k, 1, st)
+    torch.cuda.synchronize()
+    # oracle (bf16 rounding points of fused_ops.moe + the shared expert of fused/model.py:305-307)
+    xn = to_np(x)
+    ln = to_np(logits)
+    routed, sel, _ = F.moe(xn, None, _LazyDequant(qgu.cpu().numpy(), sgu.float().cpu().numpy(), g),
+                           _LazyDequant(qdn.cpu().numpy(), sdn.float().cpu().numpy(), g), top_k=k,
+                           dtype="bf16", logits=ln[:, :e], return_routing=True)
+    wsg = to_np(w4.dequantize(qsgu, ssgu, g))
+    wsd = to_np(w4.dequantize(qsdn, ssdn, g))
+    gate = bf16_round(xn @ wsg[:inter].T)
+    up = bf16_round(xn @ wsg[inter:].T)
+    act = bf16_round(bf16_round(F.silu(gate)) * up)
+    shared = bf16_round(act @ wsd.T)
+    sgate = bf16_round(F.sigmoid(ln[:, e:e + 1]))
+    want = bf16_round(routed + bf16_round(shared * sgate))
+    idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
+    np.testing.assert_array_equal(idx, sel)
+    assert_close(to_np(out), want, what="moe w4a16", row_scale=True, strict_frac=0.999)
+
+
+@pytest.mark.parametrize("tag", ["bf16", "f16"])
+def test_attention_operator_matches_reference(golden, cuda_lib, tag):
+    from qwen35_dflash_b200 import fused_ops as Q
+    d = _lowp(golden, tag)
+    ulp = 2 ** -8 if tag == "bf16" else 2 ** -11
+    out = Q.attention(_t(d["attn_q"], DT[tag]), _t(d["attn_k"], DT[tag]), _t(d["attn_v"], DT[tag]),
+                      query_start=8, scale=32 ** -0.5)
+    assert_close(to_np(out), d["attn_o"], 4 * ulp, 4 * ulp, "attention")
+
+
+@pytest.mark.parametrize("b,h,hkv,s,ctx,dim", [(1, 16, 2, 16, 4096, 256), (2, 4, 1, 16, 100, 64),
+                                               (1, 8, 2, 64, 64, 128), (3, 16, 2, 1, 37, 256)])
+def test_attention_operator_shapes(cuda_lib, b, h, hkv, s, ctx, dim):
+    from qwen35_dflash_b200 import fused_ops as Q
+    rng = np.random.default_rng(ctx + s)
+    q = bf16_round(rng.normal(0, 1, (b, h, s, dim)))
+    k = bf16_round(rng.normal(0, 1, (b, hkv, ctx + s, dim)))
+    v = bf16_round(rng.normal(0, 1, (b, hkv, ctx + s, dim)))
+    want = F.attention(q, k, v, query_start=ctx, scale=dim ** -0.5, dtype="bf16")
+    got = Q.attention(bf16_tensor(q), bf16_tensor(k), bf16_tensor(v), query_start=ctx, scale=dim ** -0.5)
+    assert_close(to_np(got), want, what="attention")
+
+
+@pytest.mark.parametrize("b,ctx", [(1, 4096), (3, 40)])
+def test_paged_attention_layer_matches_oracle(cuda_lib, b, ctx):
+    """q/k norm + RoPE + paged KV append + causal GQA + sigmoid gate (fused/model.py:278-293)."""
+    from qwen35_dflash_b200 import lib
+    h, hkv, dim, s, page = 16, 2, 256, 16, 16
+    rot, theta, eps = 64, 1e7, 1e-6
+    rng = np.random.default_rng(b + ctx)
+    ldq = h * 2 * dim + 2 * hkv * dim
+    qkv = bf16_round(rng.normal(0, 1, (b, s, ldq)))
+    qn = bf16_round(rng.normal(0, 0.1, (dim,)))
+    kn = bf16_round(rng.normal(0, 0.1, (dim,)))
+    qpos = np.array([ctx - 7 * i for i in range(b)], np.int32)
+    max_len = int(qpos.max()) + s
+    max_pages = (max_len + page - 1) // page
+    npages = b * max_pages + 3
+    perm = rng.permutation(npages)[: b * max_pages].reshape(b, max_pages).astype(np.int32)
+    kcache = bf16_round(rng.normal(0, 1, (npages, hkv, page, dim)))
+    vcache = bf16_round(rng.normal(0, 1, (npages, hkv, page, dim)))
+    # oracle
+    cfg = {"head_dim": dim, "rope_parameters": {"partial_rotary_factor": rot / dim, "rope_theta": theta}}
+    orc = OracleTarget(cfg, {}, (0,), act="bf16", rope="f32")
+    want = np.zeros((b, s, h * dim), np.float32)
+    new_k = np.zeros((b, hkv, s, dim), np.float32)
+    new_v = np.zeros((b, hkv, s, dim), np.float32)
+    for i in range(b):
+        x = qkv[i]
+        qg = x[:, : h * 2 * dim].reshape(s, h, 2 * dim)
+        qh, gate = qg[..., :dim], qg[..., dim:]
+        qh = F.rms_norm(qh, bf16_round(qn + 1), eps, "bf16").transpose(1, 0, 2)[None]
+        kh = F.rms_norm(x[:, h * 2 * dim: h * 2 * dim + hkv * dim].reshape(s, hkv, dim), bf16_round(kn + 1),
+                        eps, "bf16").transpose(1, 0, 2)[None]
+        vh = x[:, h * 2 * dim + hkv * dim:].reshape(s, hkv, dim).transpose(1, 0, 2)[None]
+        qh, kh = orc.rotary(qh, int(qpos[i])), orc.rotary(kh, int(qpos[i]))
+        new_k[i], new_v[i] = kh[0], vh[0]
+        pos = np.arange(qpos[i])
+        old_k = kcache[perm[i][pos // page], :, pos % page].transpose(1, 0, 2)[None]
+        old_v = vcache[perm[i][pos // page], :, pos % page].transpose(1, 0, 2)[None]
+        kk, vv = F.cache_update(old_k, old_v, kh, vh)
+        o = F.attention(qh, kk, vv, query_start=int(qpos[i]), scale=dim ** -0.5, dtype="bf16")
+        o = o[0].transpose(1, 0, 2).reshape(s, h * dim)
+        want[i] = bf16_round(o * bf16_round(F.sigmoid(gate.reshape(s, h * dim))))
+    # device
+    qkv_d = bf16_tensor(qkv.reshape(b * s, ldq))
+    kc, vc = bf16_tensor(kcache), bf16_tensor(vcache)
+    pages_d = torch.from_numpy(perm).cuda()
+    qpos_d = torch.from_numpy(qpos).cuda()
+    qout = torch.empty(b, h, s, dim, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(b * s, h * dim, dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(cuda_lib.qw_attn_workspace_bytes(b, h, hkv, s, dim, max_len), dtype=torch.uint8, device="cuda")
+    st = lib.stream_ptr()
+    qn_d, kn_d = bf16_tensor(qn), bf16_tensor(kn)  # keep the tensors alive across the launch
+    lib.call("qw_attn_prep", qkv_d.data_ptr(), ldq, qn_d.data_ptr(), kn_d.data_ptr(), eps,
+             theta, rot, qpos_d.data_ptr(), pages_d.data_ptr(), max_pages, page, kc.data_ptr(), vc.data_ptr(),
+             qout.data_ptr(), b, s, h, hkv, dim, st)
+    gate_ptr = qkv_d.data_ptr() + dim * 2
+    lib.call("qw_attn_paged", qout.data_ptr(), kc.data_ptr(), vc.data_ptr(), pages_d.data_ptr(), max_pages, page,
+             qpos_d.data_ptr(), max_len, gate_ptr, ldq, out.data_ptr(), b, s, h, hkv, dim, dim ** -0.5,
+             ws.data_ptr(), st)
+    torch.cuda.synchronize()
+    kc_h = to_np(kc)
+    for i in range(b):
+        pos = qpos[i] + np.arange(s)
+        got_k = kc_h[perm[i][pos // page], :, pos % page].transpose(1, 0, 2)
+        assert_close(got_k, new_k[i], what="k append")
+        np.testing.assert_array_equal(to_np(vc)[perm[i][pos // page], :, pos % page].transpose(1, 0, 2), new_v[i])
+    assert_close(to_np(out).reshape(b, s, h * dim), want, what="paged attention")
