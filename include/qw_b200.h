@@ -257,6 +257,40 @@ int qw_gdn_verify(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int l
 int qw_gdn_commit(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int nlayers,
                   void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Layer boundaries and the verify decision (engine layer).
+ * ---------------------------------------------------------------------------- */
+
+/* Residual-stream RMSNorm of FusedTargetModel._norm (fused/model.py:206-217) with a
+ * zero-centred weight: normed = bf16(bf16(h*rsqrt(mean(h^2)+eps)) * bf16(gamma+1)).
+ * With ids (int32 [T]) the stream is first set to embed[ids] (:346-347).  With tap,
+ * the residual stream (or, tap_normed != 0, the normed output) is also copied to
+ * tap[t*ldf + i] (the feature taps of :405-409). */
+int qw_residual_norm(void* hidden, const int32_t* ids, const void* embed, const void* gamma,
+                     void* normed, void* tap, int64_t ldf, int tap_normed, int64_t tokens,
+                     int64_t hidden_dim, float eps, void* stream);
+
+/* lm_head + argmax of fused/model.py:410-417: x bf16 [T,K] (T <= 16), W a B16 stream
+ * of [N,K]; writes one (value, index) key per CTA and token into keys (u64
+ * [qw_lmhead_blocks(N), T]) and, when logits != NULL, bf16 logits [T,N]. */
+int64_t qw_lmhead_blocks(int64_t n);
+int qw_lmhead_argmax(const void* x, const void* w_stream, void* logits, void* keys,
+                     int64_t tokens, int64_t n, int64_t k, void* stream);
+
+/* Acceptance of a verified block (fused/session.py:316-341, execution/runtime.py:83-95):
+ * top1[t] = argmax of row t (ties -> lowest id); max_accepted[b] = longest prefix of
+ * proposals[b*seq..] equal to (next_token[b], top1[b*seq], ...).  With auto_commit,
+ * accepted[b] = max_accepted[b], next_token[b] = top1 of row accepted-1, qpos[b] +=
+ * accepted (all device-side: no host synchronization). */
+int qw_accept(const void* keys, int64_t nblk, const int32_t* proposals, int32_t* top1,
+              int32_t* max_accepted, int32_t* next_token, int32_t* accepted, int32_t* qpos,
+              int64_t batch, int64_t seq, int auto_commit, void* stream);
+
+/* Commit bookkeeping for host-chosen accepted counts (TargetVerification.commit,
+ * fused/session.py:374-387): next_token and qpos advance as in qw_accept. */
+int qw_apply_commit(const int32_t* accepted, const int32_t* top1, int32_t* next_token,
+                    int32_t* qpos, int64_t batch, int64_t seq, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

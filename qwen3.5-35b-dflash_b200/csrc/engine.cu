@@ -1,0 +1,149 @@
+// Layer-boundary kernels of the block verify: residual RMSNorm (with the embedding
+// gather and the DFlash feature taps) and the acceptance step.
+//
+//  residual_norm  fused/model.py:398, :403, :407 — normed = round(round(h * rsqrt(mean h^2
+//                 + eps)) * round(w + 1)) (zero-centred weights, :206-217); on the first
+//                 layer h = embed[ids] (:346-347); a tap copies the residual stream after
+//                 a feature layer (:405-406, target_features.py) into its feature slot, or
+//                 the final-norm output when the tapped layer is the last (:407-409).
+//  accept         the verify decision of fused/session.py:316-341 for a whole block:
+//                 expected[0] = the pre-block prediction, expected[i] = argmax row i-1;
+//                 proposal i is accepted while it equals expected[i].  The lm_head
+//                 argmax keys are reduced here (ties -> lowest token id).
+//  apply_commit   the bookkeeping of TargetVerification.commit (session.py:374-387):
+//                 next prediction = row accepted-1 (or unchanged), position += accepted.
+#include "qw_common.cuh"
+
+namespace qw {
+
+struct NormArgs {
+  __nv_bfloat16* hidden;          // [T, H] residual stream (in/out)
+  const int32_t* ids;             // [T] token ids, or null
+  const __nv_bfloat16* embed;     // [V, H]
+  const __nv_bfloat16* gamma;     // [H] zero-centred weight
+  __nv_bfloat16* normed;          // [T, H]
+  __nv_bfloat16* tap;             // feature slot base (row stride ldf), or null
+  int64_t ldf;
+  int tap_normed, T, H;
+  float eps;
+};
+
+__global__ void residual_norm_kernel(NormArgs a) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  __nv_bfloat16* h = a.hidden + static_cast<int64_t>(t) * a.H;
+  if (a.ids) {
+    const __nv_bfloat16* e = a.embed + static_cast<int64_t>(a.ids[t]) * a.H;
+    for (int i = threadIdx.x; i < a.H; i += blockDim.x) h[i] = e[i];
+    __syncthreads();
+  }
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+    const float v = __bfloat162float(h[i]);
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / a.H + a.eps);
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+    const __nv_bfloat16 hv = h[i];
+    const float g = rbf(__bfloat162float(a.gamma[i]) + 1.f);
+    const __nv_bfloat16 y = __float2bfloat16_rn(rbf(__bfloat162float(hv) * inv) * g);
+    a.normed[static_cast<int64_t>(t) * a.H + i] = y;
+    if (a.tap) a.tap[static_cast<int64_t>(t) * a.ldf + i] = a.tap_normed ? y : hv;
+  }
+}
+
+// One warp per token reduces the lm_head argmax keys; then one thread per sequence
+// evaluates acceptance.
+__global__ void accept_kernel(const unsigned long long* __restrict__ keys, int nblk, int T, int S, int B,
+                              const int32_t* __restrict__ proposals, int32_t* __restrict__ top1,
+                              int32_t* __restrict__ max_accepted, int32_t* __restrict__ next_token,
+                              int32_t* __restrict__ accepted, int32_t* __restrict__ qpos, int auto_commit) {
+  __shared__ int32_t s_top1[QW_MAX_BLOCK * 64];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int t = warp; t < T; t += nw) {
+    unsigned long long best = 0ull;
+    for (int i = lane; i < nblk; i += 32) {
+      const unsigned long long k = keys[static_cast<int64_t>(i) * T + t];
+      best = k > best ? k : best;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) {
+      const int32_t tok = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+      top1[t] = tok;
+      s_top1[t] = tok;
+    }
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    int acc = 0;
+    int expected = next_token[b];
+    for (int i = 0; i < S; ++i) {
+      if (proposals[b * S + i] != expected) break;
+      ++acc;
+      expected = s_top1[b * S + i];
+    }
+    max_accepted[b] = acc;
+    if (auto_commit) {
+      accepted[b] = acc;
+      if (acc > 0) next_token[b] = s_top1[b * S + acc - 1];
+      qpos[b] += acc;
+    }
+  }
+}
+
+__global__ void apply_commit_kernel(const int32_t* __restrict__ accepted, const int32_t* __restrict__ top1,
+                                    int32_t* __restrict__ next_token, int32_t* __restrict__ qpos, int B, int S) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int acc = accepted[b];
+  if (acc > 0) next_token[b] = top1[b * S + acc - 1];
+  qpos[b] += acc;
+}
+
+}  // namespace qw
+
+using namespace qw;
+
+extern "C" int qw_residual_norm(void* hidden, const int32_t* ids, const void* embed, const void* gamma,
+                                void* normed, void* tap, int64_t ldf, int tap_normed, int64_t tokens,
+                                int64_t hidden_dim, float eps, void* stream) {
+  QW_CHECK_ARG(hidden && gamma && normed && (ids == nullptr || embed != nullptr), "residual_norm: null pointer");
+  QW_CHECK_ARG(tokens >= 0 && hidden_dim > 0 && eps > 0.f && (tap == nullptr || ldf >= hidden_dim),
+               "residual_norm: invalid shape");
+  if (tokens == 0) return QW_OK;
+  NormArgs a{static_cast<__nv_bfloat16*>(hidden), ids, static_cast<const __nv_bfloat16*>(embed),
+             static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(normed),
+             static_cast<__nv_bfloat16*>(tap), ldf, tap_normed, static_cast<int>(tokens),
+             static_cast<int>(hidden_dim), eps};
+  residual_norm_kernel<<<static_cast<unsigned>(tokens), 256, 0, as_stream(stream)>>>(a);
+  QW_LAUNCH_CHECK("residual_norm");
+  return QW_OK;
+}
+
+extern "C" int qw_accept(const void* keys, int64_t nblk, const int32_t* proposals, int32_t* top1,
+                         int32_t* max_accepted, int32_t* next_token, int32_t* accepted, int32_t* qpos,
+                         int64_t batch, int64_t seq, int auto_commit, void* stream) {
+  QW_CHECK_ARG(keys && proposals && top1 && max_accepted && next_token, "accept: null pointer");
+  QW_CHECK_ARG(!auto_commit || (accepted && qpos), "accept: auto commit needs accepted and qpos");
+  QW_CHECK_ARG(batch >= 1 && seq >= 1 && seq <= QW_MAX_BLOCK && batch * seq <= QW_MAX_BLOCK * 64 && nblk >= 1,
+               "accept: invalid shape");
+  accept_kernel<<<1, 512, 0, as_stream(stream)>>>(static_cast<const unsigned long long*>(keys),
+                                                   static_cast<int>(nblk), static_cast<int>(batch * seq),
+                                                   static_cast<int>(seq), static_cast<int>(batch), proposals,
+                                                   top1, max_accepted, next_token, accepted, qpos, auto_commit);
+  QW_LAUNCH_CHECK("accept");
+  return QW_OK;
+}
+
+extern "C" int qw_apply_commit(const int32_t* accepted, const int32_t* top1, int32_t* next_token, int32_t* qpos,
+                               int64_t batch, int64_t seq, void* stream) {
+  QW_CHECK_ARG(accepted && top1 && next_token && qpos && batch >= 1 && seq >= 1, "apply_commit: invalid argument");
+  apply_commit_kernel<<<static_cast<unsigned>((batch + 127) / 128), 128, 0, as_stream(stream)>>>(
+      accepted, top1, next_token, qpos, static_cast<int>(batch), static_cast<int>(seq));
+  QW_LAUNCH_CHECK("apply_commit");
+  return QW_OK;
+}

@@ -12,12 +12,19 @@ namespace qw {
 struct LinArgs {
   const __nv_bfloat16* x;  // [T, k]
   const uint8_t* w;        // stream
-  void* y;                 // [T, ldy]
+  void* y;                 // [T, ldy] (argmax: optional bf16 logits)
   int64_t ldy;
   int tokens, n, k, rt, mode;
+  unsigned long long* keys;  // argmax: [gridDim.x, tokens] best (value, index) key per CTA
 };
 
-template <class Fmt, int NT, int PF>
+// Argmax key of logit `v` (rounded to bf16, the reference's logits dtype) at row n:
+// larger value wins, then the lower index (torch argmax returns the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
+  return (static_cast<unsigned long long>(float_key(rbf(v))) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
+}
+
+template <class Fmt, int NT, int PF, bool ARGMAX = false>
 __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int NTOK = NT * 8;
@@ -57,7 +64,50 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
 #pragma unroll
       for (int r = 0; r < 4; ++r) red[(warp * NT * 4 + j * 4 + r) * 32 + lane] = acc[j][r];
     __syncthreads();
-    if (ks == 0 && active) {
+    if constexpr (ARGMAX) {
+      // per-token best over this CTA's rows: lanes hold (row gid / gid+8, token), reduce
+      // over gid with shuffles, then across the CTA's row tiles in shared memory
+      unsigned long long* best = reinterpret_cast<unsigned long long*>(red + SG_WARPS * NT * 4 * 32);
+      if (threadIdx.x < NTOK * SG_WARPS) best[threadIdx.x] = 0ull;
+      __syncthreads();
+      if (ks == 0) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // token parity (r & 1)
+            unsigned long long key = 0ull;
+            const int t = tp0 + j * 8 + 2 * tig + h;
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+              const int r = rr * 2 + h;
+              float v = 0.f;
+              for (int s = 0; s < KS; ++s) v += red[((warp + s) * NT * 4 + j * 4 + r) * 32 + lane];
+              const int n = rt * 16 + gid + 8 * rr;
+              if (active && t < a.tokens) {
+                const unsigned long long kk = argmax_key(v, n);
+                key = kk > key ? kk : key;
+                if (a.y) static_cast<__nv_bfloat16*>(a.y)[static_cast<int64_t>(t) * a.ldy + n] = __float2bfloat16_rn(v);
+              }
+            }
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+              const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+              key = other > key ? other : key;
+            }
+            if (gid == 0) best[rt_local * NTOK + j * 8 + 2 * tig + h] = key;
+          }
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x < NTOK && tp0 + threadIdx.x < a.tokens) {
+        unsigned long long key = 0ull;
+        for (int r = 0; r < a.rt; ++r) {
+          const unsigned long long kk = best[r * NTOK + threadIdx.x];
+          key = kk > key ? kk : key;
+        }
+        a.keys[static_cast<int64_t>(blockIdx.x) * a.tokens + tp0 + threadIdx.x] = key;
+      }
+    } else if (ks == 0 && active) {
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -92,22 +142,23 @@ static int choose_rt(int ntiles) {
   return 1;
 }
 
-template <class Fmt, int NT, int PF>
+template <class Fmt, int NT, int PF, bool ARGMAX = false>
 static int launch_linear(const LinArgs& a0, cudaStream_t s) {
   LinArgs a = a0;
   a.rt = choose_rt(a.n / 16);
-  const size_t smem = static_cast<size_t>(NT * 8) * (a.k + 8) * 2 + SG_WARPS * NT * 4 * 32 * 4;
+  const size_t smem = static_cast<size_t>(NT * 8) * (a.k + 8) * 2 + SG_WARPS * NT * 4 * 32 * 4 +
+                      (ARGMAX ? SG_WARPS * NT * 8 * 8 : 0);
   if (smem > 227 * 1024) return fail(QW_ERR_UNSUPPORTED, "linear: K=%d too large", a.k);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(stream_linear_kernel<Fmt, NT, PF>,
+    attr_err = cudaFuncSetAttribute(stream_linear_kernel<Fmt, NT, PF, ARGMAX>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "linear smem attribute");
   const int ntiles = a.n / 16;
   const unsigned grid = static_cast<unsigned>((ntiles + a.rt - 1) / a.rt);
-  stream_linear_kernel<Fmt, NT, PF><<<grid, SG_WARPS * 32, smem, s>>>(a);
+  stream_linear_kernel<Fmt, NT, PF, ARGMAX><<<grid, SG_WARPS * 32, smem, s>>>(a);
   QW_LAUNCH_CHECK("linear");
   return QW_OK;
 }
@@ -173,4 +224,22 @@ extern "C" int qw_b16_linear(const void* x, const void* w_stream, void* y, int m
   LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), y, ldy,
             static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, mode};
   return dispatch_nt<B16Fmt, 2>(a, as_stream(stream));
+}
+
+extern "C" int64_t qw_lmhead_blocks(int64_t n) {
+  if (n <= 0 || n % 16) return -1;
+  const int rt = choose_rt(static_cast<int>(n / 16));
+  return (n / 16 + rt - 1) / rt;
+}
+
+extern "C" int qw_lmhead_argmax(const void* x, const void* w_stream, void* logits, void* keys, int64_t tokens,
+                                int64_t n, int64_t k, void* stream) {
+  int st = check_linear(x, w_stream, keys, QW_OUT_BF16, n, tokens, n, k);
+  if (st) return st;
+  QW_CHECK_ARG(k % 64 == 0, "lmhead: K must be a multiple of 64");
+  if (tokens == 0) return QW_OK;
+  LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), logits, n,
+            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, QW_OUT_BF16,
+            static_cast<unsigned long long*>(keys)};
+  return launch_linear<B16Fmt, 2, 2, true>(a, as_stream(stream));
 }

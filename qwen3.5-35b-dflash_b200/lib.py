@@ -64,6 +64,11 @@ SIGNATURES = {
     "qw_b16_linear": (_c.c_int, [P, P, P, _c.c_int, I64, I64, I64, I64, P]),
     "qw_gdn_verify": (_c.c_int, [_c.POINTER(GdnDims), P, _c.c_int, P]),
     "qw_gdn_commit": (_c.c_int, [_c.POINTER(GdnDims), P, _c.c_int, P]),
+    "qw_residual_norm": (_c.c_int, [P, P, P, P, P, P, I64, _c.c_int, I64, I64, F32, P]),
+    "qw_lmhead_blocks": (I64, [I64]),
+    "qw_lmhead_argmax": (_c.c_int, [P, P, P, P, I64, I64, I64, P]),
+    "qw_accept": (_c.c_int, [P, I64, P, P, P, P, P, P, I64, I64, _c.c_int, P]),
+    "qw_apply_commit": (_c.c_int, [P, P, P, P, I64, I64, P]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,230 @@
+"""The 40-layer-style block verify engine on the tiny configuration vs the oracle (GPU)."""
+import dataclasses
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, to_np
+from oracle.model_np import OracleTarget, verify as oracle_verify, commit as oracle_commit
+from oracle.numerics import quantize_w4, dequantize_w4, bf16_round
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny(feature_layers=None, seed=17):
+    from qwen35_dflash_b200 import config as qcfg, synthetic
+    cfg = qcfg.TINY
+    if feature_layers is not None:
+        cfg = dataclasses.replace(cfg, feature_layers=tuple(feature_layers))
+    raw = synthetic.init_weights(cfg, seed=seed)
+    deq = {}
+    for name, value in raw.items():
+        if synthetic.is_w4(name):
+            q, s = quantize_w4(value, cfg.quant_group)
+            value = dequantize_w4(q, s, cfg.quant_group)
+        deq[name] = value
+    oracle = OracleTarget(cfg.to_hf_text_config(), deq, cfg.feature_layers, act="bf16", rope="f32")
+    return cfg, raw, oracle
+
+
+def _engine(cfg, raw, batch=1, capacity=256):
+    from qwen35_dflash_b200 import engine as E
+    weights = E.weights_from_arrays(cfg, raw)
+    return E.TargetEngine(cfg, weights, batch=batch, block=16, capacity=capacity)
+
+
+def _oracle_state_from_engine(oracle, eng, b=0):
+    """The engine's committed banks of sequence b as an oracle State (teacher forcing)."""
+    from oracle.model_np import LayerState, State
+    cfg = eng.cfg
+    pos = int(eng.qpos[b].item())
+    layers = []
+    for l, kind in enumerate(cfg.layer_types):
+        if kind == "linear_attention":
+            gi = eng.gdn_idx[l]
+            layers.append(LayerState(conv=to_np(eng.conv_hist[gi, b:b + 1]),
+                                     recurrent=to_np(eng.state[gi, b:b + 1]).transpose(0, 1, 3, 2).copy()))
+        else:
+            ai = eng.attn_idx[l]
+            t = np.arange(pos)
+            pg = eng.pages[b].cpu().numpy()[t // eng.P]
+            k = to_np(eng.k_cache[ai])[pg, :, t % eng.P].transpose(1, 0, 2)[None]
+            v = to_np(eng.v_cache[ai])[pg, :, t % eng.P].transpose(1, 0, 2)[None]
+            layers.append(LayerState(key=k, value=v))
+    return State(pos, layers)
+
+
+def test_layers_teacher_forced(cuda_lib):
+    """Every layer's output from the engine (taps on all layers) equals the oracle layer
+    applied to the engine's previous-layer output and the engine's committed state
+    (64-token prompt in 4 blocks, each committed)."""
+    cfg, raw, oracle = _tiny(feature_layers=(0, 1, 2, 3))
+    eng = _engine(cfg, raw)
+    prompt = np.random.default_rng(17).integers(0, cfg.vocab_size, 64)
+    H = cfg.hidden_size
+    for blk in range(4):
+        ostate = _oracle_state_from_engine(oracle, eng)
+        ids = prompt[blk * 16:(blk + 1) * 16]
+        eng.tokens.copy_(torch.from_numpy(ids.astype(np.int32)))
+        eng.forward()
+        eng.accept(auto_commit=False)
+        feats = to_np(eng.features)
+        x = oracle.w["target.embed_tokens.weight"][ids][None]
+        for layer in range(cfg.num_hidden_layers):
+            out, _ = oracle.layer(layer, x, ostate.layers[layer], ostate.position)
+            if layer == cfg.num_hidden_layers - 1:
+                out = oracle.norm(out, "target.norm.weight")
+            got = feats[:, layer * H:(layer + 1) * H]
+            assert_close(got, out[0], 2e-2, 1e-2, f"block {blk} layer {layer}", row_scale=True, strict_frac=0.98)
+            x = got[None]
+        eng.commit([16])
+
+
+def test_session_rounds_match_oracle(cuda_lib, golden):
+    """prefill + block verify/commit rounds vs the bf16 oracle run from the engine's own
+    committed state each round (per-step identity).  A prediction may differ only where
+    the oracle's two candidate logits are within four bf16 ulps (2^-7 relative each: the
+    bf16 residual stream of two implementations that round at the same points but sum in
+    different fp32 orders drifts by a few ulps over the layers); the accepted counts must
+    match on >= 99% of rounds."""
+    from qwen35_dflash_b200.session import TargetSession
+    cfg, raw, oracle = _tiny()
+    eng = _engine(cfg, raw)
+    sess = TargetSession(eng)
+    d = golden("tiny_session.npz")
+    prompt = [int(t) for t in d["prompt"]]
+    sess.prefill(prompt)
+    top1, feats, _, _ = oracle.forward(np.asarray([prompt]))
+    assert sess.next_token == int(top1[0, -1])
+    assert_close(to_np(sess.last_features[0]), feats[0, -1:], 2e-2, 1e-2, "prefill features", row_scale=True)
+    agree = total = same_acc = rounds = 0
+    rng = np.random.default_rng(11)
+    greedy = [int(t) for t in d["greedy"]]
+    for r in range(12):
+        next_token = sess.next_token
+        ostate = _oracle_state_from_engine(oracle, eng)
+        # proposals: the oracle's own greedy continuation with one seeded corruption
+        cont = [next_token]
+        o_top, _, _, _ = oracle.forward(np.asarray([[next_token]]), ostate.copy())
+        props = [next_token] + [int(t) for t in rng.integers(0, cfg.vocab_size, 15)]
+        j = int(rng.integers(1, 17))
+        if r % 2 == 0:
+            # accept-friendly rounds: proposals follow the oracle's predictions up to j
+            state = ostate.copy()
+            tok = next_token
+            for i in range(1, 16):
+                t1, _, state, _ = oracle.forward(np.asarray([[tok]]), state)
+                tok = int(t1[0, 0])
+                props[i] = tok if i < j else props[i]
+        v = sess.verify(props)
+        o_top1, _, _, logits = oracle.forward(np.asarray([props]), ostate.copy(), return_logits=True)
+        exp = (next_token,) + tuple(int(t) for t in o_top1[0])
+        for i, (a, b) in enumerate(zip(v.expected_next_tokens, exp)):
+            total += 1
+            if a == b:
+                agree += 1
+            else:
+                row = logits[0, i - 1]
+                margin = abs(float(row[a]) - float(row[b]))
+                assert margin <= 4 * 2 ** -7 * max(1.0, abs(float(row[b]))), (r, i, a, b, margin)
+        acc = 0
+        for i, t in enumerate(props):
+            if t != exp[i]:
+                break
+            acc += 1
+        same_acc += int(v.max_accepted_prefix == acc)
+        rounds += 1
+        v.commit(v.max_accepted_prefix)
+    assert agree >= 0.95 * total, (agree, total)
+    assert same_acc >= 0.99 * rounds, (same_acc, rounds)
+
+
+def test_verification_semantics(cuda_lib):
+    from qwen35_dflash_b200.session import TargetSession
+    cfg, raw, _ = _tiny()
+    sess = TargetSession(_engine(cfg, raw))
+    with pytest.raises(RuntimeError):
+        sess.verify([1, 2])
+    sess.prefill(list(range(20)))
+    assert sess.position == 20
+    v1 = sess.verify([sess.next_token, 5, 6])
+    v2 = sess.verify([sess.next_token, 7])
+    assert v1.max_accepted_prefix >= 1 and v2.max_accepted_prefix >= 1
+    with pytest.raises(ValueError):
+        v1.commit(v1.max_accepted_prefix + 1)
+    v1.commit(1)             # v2 was the engine's last block: v1 is re-run before commit
+    assert sess.position == 21
+    with pytest.raises(RuntimeError):
+        v2.commit(1)         # stale after v1 committed
+    with pytest.raises(ValueError):
+        sess.verify([])
+
+
+def test_device_commit_equals_host_commit(cuda_lib):
+    """The graph-capturable step (device-side accept + commit) equals verify + commit(max)."""
+    cfg, raw, _ = _tiny()
+    a = _engine(cfg, raw, batch=2, capacity=128)
+    b = _engine(cfg, raw, batch=2, capacity=128)
+    for e in (a, b):
+        e.set_random_context(40, seed=5)
+    rng = np.random.default_rng(0)
+    for it in range(3):
+        props = torch.from_numpy(rng.integers(0, cfg.vocab_size, (2, 16)).astype(np.int32)).cuda()
+        props[:, 0] = a.next_token
+        props[1, 1:4] = a.top1.view(2, 16)[1, :3] if it else props[1, 1:4]
+        for e in (a, b):
+            e.tokens.copy_(props.view(-1))
+        a.step()
+        b.forward()
+        b.accept(auto_commit=False)
+        b.commit(b.max_accepted.clone())
+        torch.cuda.synchronize()
+        assert torch.equal(a.accepted, b.accepted)
+        assert torch.equal(a.qpos, b.qpos) and torch.equal(a.next_token, b.next_token)
+        assert torch.equal(a.state, b.state) and torch.equal(a.conv_hist, b.conv_hist)
+
+
+def test_cuda_graph_replay_matches_eager(cuda_lib):
+    cfg, raw, _ = _tiny()
+    a = _engine(cfg, raw, batch=2, capacity=128)
+    b = _engine(cfg, raw, batch=2, capacity=128)
+    for e in (a, b):
+        e.set_random_context(30, seed=9)
+    a.capture()
+    for it in range(3):
+        props = torch.randint(0, cfg.vocab_size, (32,), dtype=torch.int32, device="cuda")
+        for e in (a, b):
+            e.tokens.copy_(props)
+        a.replay()
+        b.step()
+        torch.cuda.synchronize()
+        assert torch.equal(a.top1, b.top1) and torch.equal(a.qpos, b.qpos)
+        assert torch.equal(a.state, b.state) and torch.equal(a.features, b.features)
+
+
+@pytest.mark.parametrize("batch", [3])
+def test_batched_sequences_are_independent(cuda_lib, batch):
+    """Sequences of one batch at different positions give the single-sequence results."""
+    cfg, raw, _ = _tiny()
+    big = _engine(cfg, raw, batch=batch, capacity=128)
+    big.set_random_context(0, seed=1)
+    ctx = [20, 33, 47]
+    big.qpos.copy_(torch.tensor(ctx, dtype=torch.int32))
+    props = torch.randint(0, cfg.vocab_size, (batch, 16), dtype=torch.int32, device="cuda")
+    big.tokens.copy_(props.view(-1))
+    big.forward()
+    big.accept(auto_commit=False)
+    for i in range(batch):
+        one = _engine(cfg, raw, batch=1, capacity=128)
+        one.state.copy_(big.state[:, i:i + 1])
+        one.conv_hist.copy_(big.conv_hist[:, i:i + 1])
+        mp = big.max_pages
+        one.k_cache.copy_(big.k_cache[:, i * mp:(i + 1) * mp])
+        one.v_cache.copy_(big.v_cache[:, i * mp:(i + 1) * mp])
+        one.qpos.fill_(ctx[i])
+        one.tokens.copy_(props[i])
+        one.forward()
+        one.accept(auto_commit=False)
+        assert torch.equal(one.top1, big.top1.view(batch, 16)[i])
+        assert torch.equal(one.features, big.features.view(batch, 16, -1)[i])
