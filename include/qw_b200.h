@@ -178,6 +178,19 @@ int qw_moe_experts_w4(const void* x, const void* gate_up, const void* down,
                       int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
                       int32_t group, void* workspace, void* stream);
 
+/* The two halves of qw_moe_experts_w4 (same arguments), for timing each launch:
+ * up = gate_up + SiLU*up into the workspace, down = down projection. */
+int qw_moe_up_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
+                 const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts,
+                 int64_t inter, int64_t top_k, int32_t group, void* workspace, void* stream);
+int qw_moe_down_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
+                   const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts,
+                   int64_t inter, int64_t top_k, int32_t group, void* workspace, void* stream);
+
+/* Byte offset, inside a MoE workspace, of the int32 count of active routed experts
+ * written by qw_moe_route (for measuring the experts actually streamed). */
+int32_t qw_moe_active_experts(const void* workspace, int64_t tokens, int64_t experts, int64_t top_k);
+
 /* Weighted combine in ascending expert order (+ gated shared expert): out bf16 [T,H]
  * is overwritten, or, with residual != 0, out = bf16(out + moe) in place. */
 int qw_moe_combine(void* workspace, void* out, int residual, int64_t tokens, int64_t hidden,

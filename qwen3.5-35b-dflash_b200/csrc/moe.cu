@@ -549,11 +549,7 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
 }
 
 template <class Fmt, int PF>
-static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s) {
-  constexpr int NTOK = 16, NT = 2;
-  const int slots = 1 + (a.E < a.T * a.k ? a.E : a.T * a.k);
-  const size_t smem_up = NTOK * (a.H + 8) * 2 + SG_WARPS * 2 * NT * 4 * 32 * 4 + NTOK * 4;
-  const size_t smem_dn = NTOK * (a.I + 8) * 2;
+static int set_moe_attrs() {
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
@@ -562,11 +558,26 @@ static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s) {
       err = cudaFuncSetAttribute(moe_down_kernel<Fmt, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
   if (err != cudaSuccess) return cuda_status(err, "moe smem attribute");
+  return QW_OK;
+}
+
+template <class Fmt, int PF>
+static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
+  constexpr int NTOK = 16, NT = 2;
+  const int slots = 1 + (a.E < a.T * a.k ? a.E : a.T * a.k);
+  const size_t smem_up = NTOK * (a.H + 8) * 2 + SG_WARPS * 2 * NT * 4 * 32 * 4 + NTOK * 4;
+  const size_t smem_dn = NTOK * (a.I + 8) * 2;
+  int st = set_moe_attrs<Fmt, PF>();
+  if (st) return st;
   if (smem_up > 200 * 1024 || smem_dn > 200 * 1024) return fail(QW_ERR_UNSUPPORTED, "moe: hidden size too large");
-  moe_up_kernel<Fmt, PF><<<dim3(slots, a.I / 16), SG_WARPS * 32, smem_up, s>>>(a);
-  QW_LAUNCH_CHECK("moe up");
-  moe_down_kernel<Fmt, PF><<<dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS), SG_WARPS * 32, smem_dn, s>>>(a);
-  QW_LAUNCH_CHECK("moe down");
+  if (up) {
+    moe_up_kernel<Fmt, PF><<<dim3(slots, a.I / 16), SG_WARPS * 32, smem_up, s>>>(a);
+    QW_LAUNCH_CHECK("moe up");
+  }
+  if (down) {
+    moe_down_kernel<Fmt, PF><<<dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS), SG_WARPS * 32, smem_dn, s>>>(a);
+    QW_LAUNCH_CHECK("moe down");
+  }
   return QW_OK;
 }
 
@@ -626,15 +637,14 @@ extern "C" int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, in
   return fail(QW_ERR_ARG, "moe_route: bad logit dtype");
 }
 
-extern "C" int qw_moe_experts_w4(const void* x, const void* gate_up, const void* down,
-                                 const void* shared_gate_up, const void* shared_down, int64_t tokens,
-                                 int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
-                                 int32_t group, void* workspace, void* stream) {
+static int experts_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
+                      const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
+                      int64_t top_k, int32_t group, void* workspace, void* stream, bool up, bool dn) {
   QW_CHECK_ARG(x && gate_up && down && workspace, "moe_experts: null pointer");
   QW_CHECK_ARG((shared_gate_up == nullptr) == (shared_down == nullptr), "moe_experts: shared expert pointers");
   QW_CHECK_ARG(group == 32 || group == 64 || group == 128, "moe_experts: group must be 32, 64 or 128");
   QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && hidden % group == 0 && inter % group == 0 && inter % 16 == 0 &&
-                   hidden % 16 == 0 && top_k >= 1 && top_k <= 32 && experts >= top_k,
+                   hidden % 16 == 0 && top_k >= 1 && top_k <= 16 && experts >= top_k,
                "moe_experts: invalid shape");
   const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
             I = static_cast<int>(inter), k = static_cast<int>(top_k);
@@ -654,10 +664,39 @@ extern "C" int qw_moe_experts_w4(const void* x, const void* gate_up, const void*
   a.has_shared = shared_gate_up != nullptr;
   cudaStream_t s = as_stream(stream);
   switch (group) {
-    case 128: return launch_experts<W4Fmt<128>, 4>(a, s);
-    case 64: return launch_experts<W4Fmt<64>, 4>(a, s);
-    default: return launch_experts<W4Fmt<32>, 8>(a, s);
+    case 128: return launch_experts<W4Fmt<128>, 4>(a, s, up, dn);
+    case 64: return launch_experts<W4Fmt<64>, 4>(a, s, up, dn);
+    default: return launch_experts<W4Fmt<32>, 8>(a, s, up, dn);
   }
+}
+
+extern "C" int qw_moe_experts_w4(const void* x, const void* gate_up, const void* down,
+                                 const void* shared_gate_up, const void* shared_down, int64_t tokens,
+                                 int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
+                                 int32_t group, void* workspace, void* stream) {
+  return experts_w4(x, gate_up, down, shared_gate_up, shared_down, tokens, hidden, experts, inter, top_k, group,
+                    workspace, stream, true, true);
+}
+
+extern "C" int qw_moe_up_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
+                            const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts,
+                            int64_t inter, int64_t top_k, int32_t group, void* workspace, void* stream) {
+  return experts_w4(x, gate_up, down, shared_gate_up, shared_down, tokens, hidden, experts, inter, top_k, group,
+                    workspace, stream, true, false);
+}
+
+extern "C" int qw_moe_down_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
+                              const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts,
+                              int64_t inter, int64_t top_k, int32_t group, void* workspace, void* stream) {
+  return experts_w4(x, gate_up, down, shared_gate_up, shared_down, tokens, hidden, experts, inter, top_k, group,
+                    workspace, stream, false, true);
+}
+
+extern "C" int32_t qw_moe_active_experts(const void* workspace, int64_t tokens, int64_t experts, int64_t top_k) {
+  // host helper for measurement: byte offset of the active-expert count in the workspace
+  (void)workspace;
+  const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
+  return static_cast<int32_t>((2LL * T * k + T) * 4 + 0 * E);
 }
 
 extern "C" int qw_moe_partials(void* workspace, int64_t tokens, int64_t hidden, int64_t experts,
@@ -725,7 +764,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
     a.ws = w.route; a.hbuf = static_cast<__nv_bfloat16*>(w.hbuf); a.part = w.part;
     a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
-    st = launch_experts<RowFmt<__nv_bfloat16>, 4>(a, s);
+    st = launch_experts<RowFmt<__nv_bfloat16>, 4>(a, s, true, true);
     if (st) return st;
     moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__nv_bfloat16*>(out), T, H, E, k, 0, 0);
   } else {
@@ -737,7 +776,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
     a.ws = w.route; a.hbuf = static_cast<__half*>(w.hbuf); a.part = w.part;
     a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
-    st = launch_experts<RowFmt<__half>, 4>(a, s);
+    st = launch_experts<RowFmt<__half>, 4>(a, s, true, true);
     if (st) return st;
     moe_combine_kernel<__half><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__half*>(out), T, H, E, k, 0, 0);
   }

@@ -83,8 +83,8 @@ def pack_weights(cfg: TargetConfig, get, device) -> tuple[dict, list[LayerWeight
     def experts(name):
         t = get(name)
         out = []
-        for e0 in range(0, t.shape[0], 16):
-            q, s = w4.quantize(t[e0:e0 + 16].float(), g)
+        for e0 in range(0, t.shape[0], 64):
+            q, s = w4.quantize(t[e0:e0 + 64].float(), g)
             out.append(w4.pack_w4(q, s, g))
         return torch.cat(out)
 
@@ -237,8 +237,10 @@ class TargetEngine:
         return None
 
     # ------------------------------------------------------------------ the block
-    def forward(self):
-        """All layers + final norm + lm_head argmax keys for the tokens in ``self.tokens``."""
+    def forward(self, after_moe_route=None):
+        """All layers + final norm + lm_head argmax keys for the tokens in ``self.tokens``.
+
+        ``after_moe_route(layer)`` (eager use only) is called after each layer's routing."""
         c, T, H, st = self.cfg, self.T, self.cfg.hidden_size, self._st()
         eps = c.rms_norm_eps
         L = c.num_hidden_layers
@@ -281,6 +283,8 @@ class TargetEngine:
             E, k, I = c.num_experts, c.num_experts_per_tok, c.moe_intermediate_size
             self._call("qw_moe_route", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
                        lib.QW_BF16, self.moe_ws.data_ptr(), st)
+            if after_moe_route is not None:
+                after_moe_route(l)
             self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                        lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
                        self.moe_ws.data_ptr(), st)
@@ -315,6 +319,52 @@ class TargetEngine:
         self.forward()
         self.accept(auto_commit=True)
         self.commit_states()
+
+    def active_experts(self) -> int:
+        """Distinct routed experts of the last routed layer (reads the workspace; syncs)."""
+        c = self.cfg
+        off = self.lib.qw_moe_active_experts(None, self.T, c.num_experts, c.num_experts_per_tok)
+        return int(self.moe_ws[off:off + 4].view(torch.int32).item())
+
+    def algorithmic_bytes(self, active_per_layer) -> dict:
+        """Bytes one verify step must move at least once (weights read once, the
+        recurrent state read and written once, the KV context read once), given the
+        distinct routed experts of each layer."""
+        c = self.cfg
+        g = c.quant_group
+        w4b = lambda n, k: n * k // 2 + n * (k // g) * 2  # noqa: E731
+        H, I, E = c.hidden_size, c.moe_intermediate_size, c.num_experts
+        expert = w4b(2 * I, H) + w4b(H, I)
+        ctx = int(self.qpos.float().mean().item()) + self.S
+        parts = {"gdn_weights": 0, "attn_weights": 0, "moe_fixed": 0, "routed_experts": 0, "state": 0,
+                 "kv": 0, "lm_head": 0}
+        for l, kind in enumerate(c.layer_types):
+            if kind == "linear_attention":
+                parts["gdn_weights"] += (w4b(c.conv_channels + c.value_width, H) + 2 * c.linear_num_value_heads * H * 2
+                                         + c.conv_channels * c.linear_conv_kernel_dim * 2 + w4b(H, c.value_width))
+                parts["state"] += self.B * (2 * c.linear_num_value_heads * c.linear_key_head_dim
+                                            * c.linear_value_head_dim * 4
+                                            + 2 * c.conv_channels * (c.linear_conv_kernel_dim - 1) * 2)
+            else:
+                D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_key_value_heads
+                parts["attn_weights"] += w4b(Hq * 2 * D + 2 * Hkv * D, H) + w4b(H, Hq * D)
+                parts["kv"] += self.B * 2 * Hkv * D * 2 * ctx
+            parts["moe_fixed"] += (E + 1) * H * 2 + expert
+            parts["routed_experts"] += active_per_layer[l] * expert
+        parts["lm_head"] = c.vocab_size * H * 2
+        parts["total"] = sum(parts.values())
+        return parts
+
+    def serve_step(self, host_tokens: torch.Tensor, host_out: torch.Tensor):
+        """Public serving step: pinned host proposals [B*S] int32 in, device-side verify
+        + accept + commit (the captured graph), then [accepted (B), next_token (B)] back
+        into the pinned host buffer; returns after the copy completes."""
+        self.tokens.copy_(host_tokens, non_blocking=True)
+        self.graph.replay()
+        host_out[: self.B].copy_(self.accepted, non_blocking=True)
+        host_out[self.B: 2 * self.B].copy_(self.next_token, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return host_out
 
     # ------------------------------------------------------------------ graph
     def capture(self):

@@ -48,8 +48,10 @@ def _lane_maps(steps: int, device):
 
 def pack_w4(q: torch.Tensor, scale: torch.Tensor, group: int) -> torch.Tensor:
     """int8 q [N, K] (or [E, N, K]) + scales -> uint8 W4 stream (experts concatenated)."""
-    if q.dim() == 3:
-        return torch.cat([pack_w4(q[e], scale[e], group) for e in range(q.shape[0])])
+    if q.dim() == 3:  # expert bank: per-expert streams back to back == one [E*N, K] stream
+        if q.shape[1] % TILE:
+            raise ValueError("pack_w4 needs N % 16 == 0")
+        return pack_w4(q.reshape(-1, q.shape[-1]), scale.reshape(-1, scale.shape[-1]), group)
     n, k = q.shape
     if n % TILE or k % group or group not in (32, 64, 128):
         raise ValueError("pack_w4 needs N % 16 == 0, K % group == 0, group in {32,64,128}")
@@ -100,7 +102,9 @@ def unpack_w4(stream: torch.Tensor, n: int, k: int, group: int) -> tuple[torch.T
 def pack_b16(weight: torch.Tensor) -> torch.Tensor:
     """bf16 [N, K] (or [E, N, K]) -> uint8 B16 stream; N % 16 == 0, K % 64 == 0."""
     if weight.dim() == 3:
-        return torch.cat([pack_b16(weight[e]) for e in range(weight.shape[0])])
+        if weight.shape[1] % TILE:
+            raise ValueError("pack_b16 needs N % 16 == 0")
+        return pack_b16(weight.reshape(-1, weight.shape[-1]))
     n, k = weight.shape
     if n % TILE or k % 64:
         raise ValueError("pack_b16 needs N % 16 == 0 and K % 64 == 0")
