@@ -28,9 +28,7 @@ template <class Fmt, int NT, int PF, bool ARGMAX = false>
 __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int NTOK = NT * 8;
-  const int xstride = a.k + 8;
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem);
-  float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(NTOK) * xstride * 2);
+  float* red = reinterpret_cast<float*>(smem);  // [SG_WARPS][NT*4][32]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KS = SG_WARPS / a.rt;
   const int rt_local = warp / KS, ks = warp % KS;
@@ -40,25 +38,20 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
   const int nch = a.k / Fmt::KCHUNK;
   const int c0 = ks * nch / KS, c1 = (ks + 1) * nch / KS;
   const uint8_t* tile = a.w + Fmt::tile_offset(active ? rt : 0, a.k, 0);
-  const __nv_bfloat16* xl = xs_lane_ptr(xs, xstride, lane);
   const int gid = lane >> 2, tig = lane & 3;
 
   for (int tp0 = 0; tp0 < a.tokens; tp0 += NTOK) {
-    __syncthreads();
-    // stage the pass's activation rows (zero beyond the last token)
-    const int vec_per_row = a.k / 8;
-    for (int i = threadIdx.x; i < NTOK * vec_per_row; i += blockDim.x) {
-      const int r = i / vec_per_row, c = (i % vec_per_row) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (tp0 + r < a.tokens)
-        v = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(tp0 + r) * a.k + c);
-      *reinterpret_cast<uint4*>(xs + r * xstride + c) = v;
+    XRows<__nv_bfloat16, NT> xr;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int t = min(tp0 + j * 8 + gid, a.tokens - 1);  // rows past the last token: any valid row
+      xr.r[j] = a.x + static_cast<int64_t>(t) * a.k;
     }
-    __syncthreads();
     float acc[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    if (active) stream_tile<Fmt, NT, PF>(tile, 0, c0, c1, lane, xl, 16 * xstride, acc);
+    if (active) stream_tile<Fmt, NT, PF>(tile, 0, c0, c1, lane, xr, acc);
+    if (tp0 > 0) __syncthreads();  // previous pass's reduction reads are done
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -68,8 +61,6 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
       // per-token best over this CTA's rows: lanes hold (row gid / gid+8, token), reduce
       // over gid with shuffles, then across the CTA's row tiles in shared memory
       unsigned long long* best = reinterpret_cast<unsigned long long*>(red + SG_WARPS * NT * 4 * 32);
-      if (threadIdx.x < NTOK * SG_WARPS) best[threadIdx.x] = 0ull;
-      __syncthreads();
       if (ks == 0) {
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
@@ -146,9 +137,7 @@ template <class Fmt, int NT, int PF, bool ARGMAX = false>
 static int launch_linear(const LinArgs& a0, cudaStream_t s) {
   LinArgs a = a0;
   a.rt = choose_rt(a.n / 16);
-  const size_t smem = static_cast<size_t>(NT * 8) * (a.k + 8) * 2 + SG_WARPS * NT * 4 * 32 * 4 +
-                      (ARGMAX ? SG_WARPS * NT * 8 * 8 : 0);
-  if (smem > 227 * 1024) return fail(QW_ERR_UNSUPPORTED, "linear: K=%d too large", a.k);
+  const size_t smem = SG_WARPS * NT * 4 * 32 * 4 + (ARGMAX ? SG_WARPS * NT * 8 * 8 : 0);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
@@ -165,8 +154,7 @@ static int launch_linear(const LinArgs& a0, cudaStream_t s) {
 
 template <class Fmt, int PF>
 static int dispatch_nt(const LinArgs& a, cudaStream_t s) {
-  const bool wide_ok = static_cast<size_t>(32) * (a.k + 8) * 2 <= 150 * 1024;
-  if (a.tokens > 16 && wide_ok) return launch_linear<Fmt, 4, PF>(a, s);
+  if (a.tokens > 16) return launch_linear<Fmt, 4, PF>(a, s);
   return launch_linear<Fmt, 2, PF>(a, s);
 }
 
@@ -181,6 +169,7 @@ static int check_linear(const void* x, const void* w, void* y, int mode, int64_t
                "linear: bad output mode");
   QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
                "linear: x and w must be 16-byte aligned");
+  QW_CHECK_ARG(k % 32 == 0, "linear: K must be a multiple of 32");
   return QW_OK;
 }
 
@@ -211,7 +200,7 @@ extern "C" int qw_w4_linear(const void* x, const void* w_stream, void* y, int mo
   switch (group) {
     case 128: return dispatch_nt<W4Fmt<128>, 4>(a, s);
     case 64: return dispatch_nt<W4Fmt<64>, 4>(a, s);
-    default: return dispatch_nt<W4Fmt<32>, 8>(a, s);
+    default: return dispatch_nt<W4Fmt<32>, 4>(a, s);
   }
 }
 
@@ -223,7 +212,7 @@ extern "C" int qw_b16_linear(const void* x, const void* w_stream, void* y, int m
   if (tokens == 0) return QW_OK;
   LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), y, ldy,
             static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, mode};
-  return dispatch_nt<B16Fmt, 2>(a, as_stream(stream));
+  return dispatch_nt<B16Fmt, 4>(a, as_stream(stream));
 }
 
 extern "C" int64_t qw_lmhead_blocks(int64_t n) {
@@ -241,5 +230,5 @@ extern "C" int qw_lmhead_argmax(const void* x, const void* w_stream, void* logit
   LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), logits, n,
             static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, QW_OUT_BF16,
             static_cast<unsigned long long*>(keys)};
-  return launch_linear<B16Fmt, 2, 2, true>(a, as_stream(stream));
+  return launch_linear<B16Fmt, 2, 4, true>(a, as_stream(stream));
 }

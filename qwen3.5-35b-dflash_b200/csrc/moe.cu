@@ -361,68 +361,57 @@ __device__ __forceinline__ bool slot_info(const MoeArgs<ET>& a, const RouteView&
   return true;
 }
 
-template <class Fmt, int PF>
-__global__ void __launch_bounds__(SG_WARPS * 32) moe_up_kernel(MoeArgs<typename Fmt::ET> a) {
+// CTA = (expert slot, 4 intermediate tiles); warp w streams one whole row tile (gate
+// rows of tile w/2 when w is even, the matching up rows when odd) over all of K through
+// a PF-deep register ring, so every warp keeps PF chunks in flight for the CTA's whole
+// life; gate/up pairs meet in shared memory for SiLU(gate) * up.
+constexpr int UP_JT = 4;
+
+template <class Fmt, int NT, int PF>
+__global__ void __launch_bounds__(SG_WARPS * 32, 2) moe_up_kernel(MoeArgs<typename Fmt::ET> a) {
   using ET = typename Fmt::ET;
-  constexpr int NT = 2, NTOK = 16;
-  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int NTOK = NT * 8;
+  __shared__ float gsm[UP_JT][NT * 4][32];
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   const uint8_t* w;
   int npairs, pbase;
   if (!slot_info(a, rv, blockIdx.x, true, w, npairs, pbase)) return;
-  const int xstride = a.H + 8;
-  ET* xs = reinterpret_cast<ET*>(smem);
-  float* red = reinterpret_cast<float*>(smem + NTOK * xstride * 2);  // [8][2][NT*4][32]
-  int* toks = reinterpret_cast<int*>(red + SG_WARPS * 2 * NT * 4 * 32);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int jt = blockIdx.y;  // intermediate tile
+  const int jl = warp >> 1, role = warp & 1;
+  const int jt = blockIdx.y * UP_JT + jl;  // intermediate tile
+  const bool active = jt < a.I / 16;
   const int nch = a.H / Fmt::KCHUNK;
-  const int c0 = warp * nch / SG_WARPS, c1 = (warp + 1) * nch / SG_WARPS;
-  const uint8_t* tg = w + Fmt::tile_offset(jt, a.H, a.gu_ld);
-  const uint8_t* tu = w + Fmt::tile_offset(a.I / 16 + jt, a.H, a.gu_ld);
-  const ET* xl = xs_lane_ptr(xs, xstride, lane);
+  const uint8_t* tile = w + Fmt::tile_offset(role * (a.I / 16) + (active ? jt : 0), a.H, a.gu_ld);
+  const int gid = lane >> 2;
   for (int p0 = 0; p0 < npairs; p0 += NTOK) {
     const int np = min(NTOK, npairs - p0);
-    __syncthreads();
-    if (threadIdx.x < NTOK) toks[threadIdx.x] = threadIdx.x < np ? (pbase < 0 ? p0 + threadIdx.x : rv.pair_tok[pbase + p0 + threadIdx.x]) : -1;
-    __syncthreads();
-    const int vpr = a.H / 8;
-    for (int i = threadIdx.x; i < NTOK * vpr; i += blockDim.x) {
-      const int r = i / vpr, c = (i % vpr) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (toks[r] >= 0) v = *reinterpret_cast<const uint4*>(a.x + static_cast<int64_t>(toks[r]) * a.H + c);
-      *reinterpret_cast<uint4*>(xs + r * xstride + c) = v;
+    XRows<ET, NT> xr;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int pi = p0 + min(j * 8 + gid, np - 1);
+      const int tok = pbase < 0 ? pi : rv.pair_tok[pbase + pi];
+      xr.r[j] = a.x + static_cast<int64_t>(tok) * a.H;
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    if (active) stream_tile<Fmt, NT, PF>(tile, a.gu_ld, 0, nch, lane, xr, acc);
+    if (p0 > 0) __syncthreads();
+    if (role == 0) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) gsm[jl][j * 4 + r][lane] = acc[j][r];
     }
     __syncthreads();
-    float ag[NT][4], au[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) ag[j][r] = au[j][r] = 0.f;
-    stream_tile<Fmt, NT, PF>(tg, a.gu_ld, c0, c1, lane, xl, 16 * xstride, ag);
-    stream_tile<Fmt, NT, PF>(tu, a.gu_ld, c0, c1, lane, xl, 16 * xstride, au);
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        red[((warp * 2 + 0) * NT * 4 + j * 4 + r) * 32 + lane] = ag[j][r];
-        red[((warp * 2 + 1) * NT * 4 + j * 4 + r) * 32 + lane] = au[j][r];
-      }
-    __syncthreads();
-    // warp 0 reduces and applies SiLU(gate) * up with the reference's rounding points
-    if (warp == 0) {
+    if (role == 1 && active) {
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          float g = 0.f, u = 0.f;
-          for (int s = 0; s < SG_WARPS; ++s) {
-            g += red[((s * 2 + 0) * NT * 4 + j * 4 + r) * 32 + lane];
-            u += red[((s * 2 + 1) * NT * 4 + j * 4 + r) * 32 + lane];
-          }
           const int tl = frag_tok(lane, j, r);
           if (tl < np) {
-            const float gr = rnd<ET>(g), ur = rnd<ET>(u);
+            const float gr = rnd<ET>(gsm[jl][j * 4 + r][lane]), ur = rnd<ET>(acc[j][r]);
             const float h = rnd<ET>(rnd<ET>(silu_f(gr)) * ur);
             const int64_t hrow = pbase < 0 ? static_cast<int64_t>(a.T) * a.k + p0 + tl : pbase + p0 + tl;
             a.hbuf[hrow * a.I + jt * 16 + frag_row(lane, r)] = from_f<ET>(h);
@@ -432,40 +421,30 @@ __global__ void __launch_bounds__(SG_WARPS * 32) moe_up_kernel(MoeArgs<typename 
   }
 }
 
-template <class Fmt, int PF>
-__global__ void __launch_bounds__(SG_WARPS * 32) moe_down_kernel(MoeArgs<typename Fmt::ET> a) {
+template <class Fmt, int NT, int PF>
+__global__ void __launch_bounds__(SG_WARPS * 32, 2) moe_down_kernel(MoeArgs<typename Fmt::ET> a) {
   using ET = typename Fmt::ET;
-  constexpr int NT = 2, NTOK = 16;
-  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int NTOK = NT * 8;
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   const uint8_t* w;
   int npairs, pbase;
   if (!slot_info(a, rv, blockIdx.x, false, w, npairs, pbase)) return;
-  const int xstride = a.I + 8;
-  ET* xs = reinterpret_cast<ET*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rt = blockIdx.y * SG_WARPS + warp;   // output row tile
-  const bool active = rt < a.H / 16;
+  if (rt >= a.H / 16) return;
   const int nch = a.I / Fmt::KCHUNK;
-  const uint8_t* tile = w + Fmt::tile_offset(active ? rt : 0, a.I, a.dn_ld);
-  const ET* xl = xs_lane_ptr(xs, xstride, lane);
+  const uint8_t* tile = w + Fmt::tile_offset(rt, a.I, a.dn_ld);
   const int64_t hbase = pbase < 0 ? static_cast<int64_t>(a.T) * a.k : pbase;
+  const int gid = lane >> 2;
   for (int p0 = 0; p0 < npairs; p0 += NTOK) {
     const int np = min(NTOK, npairs - p0);
-    __syncthreads();
-    const int vpr = a.I / 8;
-    for (int i = threadIdx.x; i < NTOK * vpr; i += blockDim.x) {
-      const int r = i / vpr, c = (i % vpr) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (r < np) v = *reinterpret_cast<const uint4*>(a.hbuf + (hbase + p0 + r) * a.I + c);
-      *reinterpret_cast<uint4*>(xs + r * xstride + c) = v;
-    }
-    __syncthreads();
-    if (!active) continue;
+    XRows<ET, NT> xr;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) xr.r[j] = a.hbuf + (hbase + p0 + min(j * 8 + gid, np - 1)) * a.I;
     float acc[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    stream_tile<Fmt, NT, PF>(tile, a.dn_ld, 0, nch, lane, xl, 16 * xstride, acc);
+    stream_tile<Fmt, NT, PF>(tile, a.dn_ld, 0, nch, lane, xr, acc);
 #pragma unroll
     for (int j = 0; j < NT; ++j)
 #pragma unroll
@@ -548,37 +527,27 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   return QW_OK;
 }
 
-template <class Fmt, int PF>
-static int set_moe_attrs() {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    err = cudaFuncSetAttribute(moe_up_kernel<Fmt, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (err == cudaSuccess)
-      err = cudaFuncSetAttribute(moe_down_kernel<Fmt, PF>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-  });
-  if (err != cudaSuccess) return cuda_status(err, "moe smem attribute");
-  return QW_OK;
-}
-
-template <class Fmt, int PF>
-static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
-  constexpr int NTOK = 16, NT = 2;
+template <class Fmt, int NT, int PF>
+static int launch_experts_nt(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
   const int slots = 1 + (a.E < a.T * a.k ? a.E : a.T * a.k);
-  const size_t smem_up = NTOK * (a.H + 8) * 2 + SG_WARPS * 2 * NT * 4 * 32 * 4 + NTOK * 4;
-  const size_t smem_dn = NTOK * (a.I + 8) * 2;
-  int st = set_moe_attrs<Fmt, PF>();
-  if (st) return st;
-  if (smem_up > 200 * 1024 || smem_dn > 200 * 1024) return fail(QW_ERR_UNSUPPORTED, "moe: hidden size too large");
   if (up) {
-    moe_up_kernel<Fmt, PF><<<dim3(slots, a.I / 16), SG_WARPS * 32, smem_up, s>>>(a);
+    const int jb = (a.I / 16 + UP_JT - 1) / UP_JT;
+    moe_up_kernel<Fmt, NT, PF><<<dim3(slots, jb), SG_WARPS * 32, 0, s>>>(a);
     QW_LAUNCH_CHECK("moe up");
   }
   if (down) {
-    moe_down_kernel<Fmt, PF><<<dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS), SG_WARPS * 32, smem_dn, s>>>(a);
+    moe_down_kernel<Fmt, NT, PF><<<dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS), SG_WARPS * 32, 0, s>>>(a);
     QW_LAUNCH_CHECK("moe down");
   }
   return QW_OK;
+}
+
+// Activation tile width: 8 tokens when routed experts average at most ~2 tokens (the
+// block-verify case: 16 tokens x top-8 over 256 experts), else 16.
+template <class Fmt, int PF>
+static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
+  if (static_cast<int64_t>(a.T) * a.k <= 2LL * a.E) return launch_experts_nt<Fmt, 1, PF>(a, s, up, down);
+  return launch_experts_nt<Fmt, 2, PF>(a, s, up, down);
 }
 
 }  // namespace qw
@@ -666,7 +635,7 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   switch (group) {
     case 128: return launch_experts<W4Fmt<128>, 4>(a, s, up, dn);
     case 64: return launch_experts<W4Fmt<64>, 4>(a, s, up, dn);
-    default: return launch_experts<W4Fmt<32>, 8>(a, s, up, dn);
+    default: return launch_experts<W4Fmt<32>, 4>(a, s, up, dn);
   }
 }
 
@@ -764,7 +733,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
     a.ws = w.route; a.hbuf = static_cast<__nv_bfloat16*>(w.hbuf); a.part = w.part;
     a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
-    st = launch_experts<RowFmt<__nv_bfloat16>, 4>(a, s, true, true);
+    st = launch_experts<RowFmt<__nv_bfloat16>, 2>(a, s, true, true);
     if (st) return st;
     moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__nv_bfloat16*>(out), T, H, E, k, 0, 0);
   } else {
@@ -776,7 +745,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
     a.ws = w.route; a.hbuf = static_cast<__half*>(w.hbuf); a.part = w.part;
     a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
-    st = launch_experts<RowFmt<__half>, 4>(a, s, true, true);
+    st = launch_experts<RowFmt<__half>, 2>(a, s, true, true);
     if (st) return st;
     moe_combine_kernel<__half><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__half*>(out), T, H, E, k, 0, 0);
   }

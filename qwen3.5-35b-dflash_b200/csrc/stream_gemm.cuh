@@ -2,10 +2,16 @@
 //
 // y[t, n] = sum_k x[t, k] * W[n, k] for a handful of tokens t (a verify block) and a
 // weight matrix streamed once from HBM.  The weight is the tensor-core A operand
-// (16 output rows per warp tile), the tokens are the B operand (8 per n-tile), so one
-// 128-bit weight load per lane feeds several mma.sync.m16n8k16 without any shared-
-// memory round trip for the weights.  Weights are pre-packed ("streams") so that each
-// lane's 16-byte loads are exactly its A fragments:
+// (16 output rows per warp tile), the tokens are the B operand (8 per n-tile).  Nothing
+// is staged in shared memory: every lane loads its own fragments from global memory
+// with 16-byte loads, so each warp issues all of its loads at once and runs without a
+// CTA barrier until the cross-warp K reduction.
+//
+// K permutation.  The dot product is invariant under any permutation of k applied to
+// both operands.  Within every 32-wide block of K the weight streams are packed in the
+// order that makes lane (gid, tig)'s B fragments of two consecutive k16-steps the 8
+// contiguous activations x[t, 32p + 8*tig .. +7]: mma-logical k = 16*(2p+h) + 2*tig + e
+// (+8 for the second register) is physical k = 32p + 8*tig + 4h + e (+2).
 //
 //   W4 stream (int4 symmetric, bf16 scale per G-wide K group), per 16-row tile and per
 //   group a chunk of 8*G + 32 bytes: G/16 k16-steps x 32 lanes x one 32-bit word (eight
@@ -19,7 +25,7 @@
 //   32 lanes x one 16-byte vector holding the lane's 4 A-fragment registers.
 //
 //   Row format: a plain row-major [N, K] 16-bit matrix (the fused-ops ABI passes dense
-//   expert weights); fragments are gathered with 32-bit loads.
+//   expert weights); fragments use the natural k order and 32-bit loads.
 #pragma once
 
 #include "qw_common.cuh"
@@ -38,8 +44,8 @@ struct W4Fmt {
   static constexpr int NV = STEPS / VW;
   static constexpr int CHB = 8 * G + 32;
   static constexpr bool SCALED = true;
+  static constexpr bool PERMUTED_K = true;
 
-  // byte offset of row tile `rt` of a matrix with `k` columns (ld unused)
   __host__ __device__ static int64_t tile_offset(int64_t rt, int k, int64_t /*ld*/) {
     return rt * (k / G) * static_cast<int64_t>(CHB);
   }
@@ -52,11 +58,9 @@ struct W4Fmt {
       if constexpr (VW == 4) {
         uint4 u = ldg_stream(p);
         w[v * 4 + 0] = u.x; w[v * 4 + 1] = u.y; w[v * 4 + 2] = u.z; w[v * 4 + 3] = u.w;
-      } else if constexpr (VW == 2) {
+      } else {
         uint2 u = ldg_stream2(p);
         w[v * 2 + 0] = u.x; w[v * 2 + 1] = u.y;
-      } else {
-        w[v] = __ldg(reinterpret_cast<const uint32_t*>(p));
       }
     }
     sc = __ldg(reinterpret_cast<const uint32_t*>(chunk + 8 * G + (lane >> 2) * 4));
@@ -73,6 +77,7 @@ struct B16Fmt {
   static constexpr int WORDS = 16;
   static constexpr int CHB = 2048;
   static constexpr bool SCALED = false;
+  static constexpr bool PERMUTED_K = true;
 
   __host__ __device__ static int64_t tile_offset(int64_t rt, int k, int64_t /*ld*/) {
     return rt * (k / 64) * static_cast<int64_t>(CHB);
@@ -92,14 +97,15 @@ struct B16Fmt {
   }
 };
 
-// Row-major 16-bit matrix [N, K] with row stride `ld` bytes; K chunk of 16.
+// Row-major 16-bit matrix [N, K] with row stride `ld` bytes; natural k order.
 template <typename ET_>
 struct RowFmt {
   using ET = ET_;
-  static constexpr int KCHUNK = 16;
-  static constexpr int STEPS = 1;
-  static constexpr int WORDS = 4;
+  static constexpr int KCHUNK = 32;
+  static constexpr int STEPS = 2;
+  static constexpr int WORDS = 8;
   static constexpr bool SCALED = false;
+  static constexpr bool PERMUTED_K = false;
 
   __host__ __device__ static int64_t tile_offset(int64_t rt, int /*k*/, int64_t ld) {
     return rt * 16 * ld;
@@ -107,26 +113,68 @@ struct RowFmt {
   __device__ __forceinline__ static void load(const uint8_t* tile, int c, int lane, int64_t ld,
                                               uint32_t (&w)[WORDS], uint32_t& sc) {
     const int gid = lane >> 2, tig = lane & 3;
-    const uint8_t* p = tile + static_cast<int64_t>(gid) * ld + (c * 16 + 2 * tig) * 2;
-    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
-    w[1] = __ldg(reinterpret_cast<const uint32_t*>(p + 8 * ld));
-    w[2] = __ldg(reinterpret_cast<const uint32_t*>(p + 16));
-    w[3] = __ldg(reinterpret_cast<const uint32_t*>(p + 8 * ld + 16));
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const uint8_t* p = tile + static_cast<int64_t>(gid) * ld + (c * 32 + s * 16 + 2 * tig) * 2;
+      w[s * 4 + 0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+      w[s * 4 + 1] = __ldg(reinterpret_cast<const uint32_t*>(p + 8 * ld));
+      w[s * 4 + 2] = __ldg(reinterpret_cast<const uint32_t*>(p + 16));
+      w[s * 4 + 3] = __ldg(reinterpret_cast<const uint32_t*>(p + 8 * ld + 16));
+    }
     sc = 0;
   }
-  __device__ __forceinline__ static void afrag(const uint32_t (&w)[WORDS], int /*s*/, uint32_t (&a)[4]) {
-    a[0] = w[0]; a[1] = w[1]; a[2] = w[2]; a[3] = w[3];
+  __device__ __forceinline__ static void afrag(const uint32_t (&w)[WORDS], int s, uint32_t (&a)[4]) {
+    a[0] = w[s * 4 + 0]; a[1] = w[s * 4 + 1]; a[2] = w[s * 4 + 2]; a[3] = w[s * 4 + 3];
   }
 };
 
-// Accumulate one chunk of one 16-row weight tile against NT n-tiles (8 tokens each) of
-// activations held in shared memory as xs[token][k].  `xs_lane` is this lane's
-// ldmatrix.x4 row address for token block 0 at k = 0; token block j is `j * xstride16`
-// elements further.
+// Activation rows of the lane's n-tiles: n-tile j covers tokens j*8 .. j*8+7, the lane
+// reads token j*8 + gid.  Rows are element pointers to x[token, 0].
+template <typename ET, int NT>
+struct XRows {
+  const ET* r[NT];
+};
+
+// Weight fragments of one chunk, and the activation fragments of one chunk.
+template <class Fmt>
+struct WFrag {
+  uint32_t w[Fmt::WORDS];
+  uint32_t sc;
+};
 template <class Fmt, int NT>
-__device__ __forceinline__ void mma_chunk(const uint32_t (&w)[Fmt::WORDS], uint32_t sc,
-                                          const typename Fmt::ET* xs_lane, int xstride16, int kbase,
-                                          float (&acc)[NT][4]) {
+struct BFrag {
+  uint32_t b[Fmt::KCHUNK / 32][NT][4];
+};
+
+template <class Fmt>
+__device__ __forceinline__ void load_w(WFrag<Fmt>& f, const uint8_t* tile, int c, int lane, int64_t ld) {
+  Fmt::load(tile, c, lane, ld, f.w, f.sc);
+}
+
+template <class Fmt, int NT>
+__device__ __forceinline__ void load_b(BFrag<Fmt, NT>& f, int c, int lane, const XRows<typename Fmt::ET, NT>& x) {
+  const int kb = c * Fmt::KCHUNK;
+  const int tig = lane & 3;
+#pragma unroll
+  for (int q = 0; q < Fmt::KCHUNK / 32; ++q) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      if constexpr (Fmt::PERMUTED_K) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(x.r[j] + kb + 32 * q + 8 * tig));
+        f.b[q][j][0] = v.x; f.b[q][j][1] = v.y; f.b[q][j][2] = v.z; f.b[q][j][3] = v.w;
+      } else {
+        const typename Fmt::ET* p = x.r[j] + kb + 32 * q + 2 * tig;
+        f.b[q][j][0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+        f.b[q][j][1] = __ldg(reinterpret_cast<const uint32_t*>(p + 8));
+        f.b[q][j][2] = __ldg(reinterpret_cast<const uint32_t*>(p + 16));
+        f.b[q][j][3] = __ldg(reinterpret_cast<const uint32_t*>(p + 24));
+      }
+    }
+  }
+}
+
+template <class Fmt, int NT>
+__device__ __forceinline__ void mma_frag(const WFrag<Fmt>& wf, const BFrag<Fmt, NT>& bf, float (&acc)[NT][4]) {
   using ET = typename Fmt::ET;
   if constexpr (Fmt::SCALED) {
     float part[NT][4];
@@ -135,16 +183,12 @@ __device__ __forceinline__ void mma_chunk(const uint32_t (&w)[Fmt::WORDS], uint3
 #pragma unroll
     for (int s = 0; s < Fmt::STEPS; ++s) {
       uint32_t a[4];
-      Fmt::afrag(w, s, a);
+      Fmt::afrag(wf.w, s, a);
 #pragma unroll
-      for (int j = 0; j < NT / 2; ++j) {
-        uint32_t b[4];
-        ldmatrix_x4(b, xs_lane + j * xstride16 + kbase + s * 16);
-        mma16816<ET>(part[2 * j], a, b[0], b[1]);
-        mma16816<ET>(part[2 * j + 1], a, b[2], b[3]);
-      }
+      for (int j = 0; j < NT; ++j)
+        mma16816<ET>(part[j], a, bf.b[s >> 1][j][(s & 1) * 2], bf.b[s >> 1][j][(s & 1) * 2 + 1]);
     }
-    const float2 s2 = bf162_to_f2(sc);  // (row gid, row gid + 8)
+    const float2 s2 = bf162_to_f2(wf.sc);  // (row gid, row gid + 8)
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       acc[j][0] = fmaf(part[j][0], s2.x, acc[j][0]);
@@ -156,45 +200,54 @@ __device__ __forceinline__ void mma_chunk(const uint32_t (&w)[Fmt::WORDS], uint3
 #pragma unroll
     for (int s = 0; s < Fmt::STEPS; ++s) {
       uint32_t a[4];
-      Fmt::afrag(w, s, a);
+      Fmt::afrag(wf.w, s, a);
 #pragma unroll
-      for (int j = 0; j < NT / 2; ++j) {
-        uint32_t b[4];
-        ldmatrix_x4(b, xs_lane + j * xstride16 + kbase + s * 16);
-        mma16816<ET>(acc[2 * j], a, b[0], b[1]);
-        mma16816<ET>(acc[2 * j + 1], a, b[2], b[3]);
-      }
+      for (int j = 0; j < NT; ++j)
+        mma16816<ET>(acc[j], a, bf.b[s >> 1][j][(s & 1) * 2], bf.b[s >> 1][j][(s & 1) * 2 + 1]);
     }
   }
 }
 
-// Stream chunks [c0, c1) of one row tile with a PF-deep register prefetch ring.
-template <class Fmt, int NT, int PF>
-__device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int c0, int c1, int lane,
-                                            const typename Fmt::ET* xs_lane, int xstride16,
-                                            float (&acc)[NT][4]) {
-  uint32_t w[PF][Fmt::WORDS];
-  uint32_t sc[PF];
+// Stream chunks [c0, c1) of NTILES row tiles that share the activations: the weights
+// run PF chunks ahead in a register ring (issued first, before anything else, so the
+// HBM latency overlaps the caller's setup), the activations (L1/L2 hits) one chunk
+// ahead.  PF must be even.
+template <class Fmt, int NT, int PF, int NTILES>
+__device__ __forceinline__ void stream_tiles(const uint8_t* const (&tiles)[NTILES], int64_t ld, int c0, int c1,
+                                             int lane, const XRows<typename Fmt::ET, NT>& x,
+                                             float (&acc)[NTILES][NT][4]) {
+  static_assert(PF % 2 == 0, "PF must be even");
+  WFrag<Fmt> w[PF][NTILES];
+  BFrag<Fmt, NT> b[2];
 #pragma unroll
   for (int p = 0; p < PF; ++p)
-    if (c0 + p < c1) Fmt::load(tile, c0 + p, lane, ld, w[p], sc[p]);
+    if (c0 + p < c1) {
+#pragma unroll
+      for (int t = 0; t < NTILES; ++t) load_w<Fmt>(w[p][t], tiles[t], c0 + p, lane, ld);
+    }
+  if (c0 < c1) load_b<Fmt, NT>(b[0], c0, lane, x);
   for (int c = c0; c < c1; c += PF) {
 #pragma unroll
     for (int p = 0; p < PF; ++p) {
       if (c + p < c1) {
-        mma_chunk<Fmt, NT>(w[p], sc[p], xs_lane, xstride16, (c + p) * Fmt::KCHUNK, acc);
-        if (c + p + PF < c1) Fmt::load(tile, c + p + PF, lane, ld, w[p], sc[p]);
+        if (c + p + 1 < c1) load_b<Fmt, NT>(b[(p + 1) & 1], c + p + 1, lane, x);
+#pragma unroll
+        for (int t = 0; t < NTILES; ++t) mma_frag<Fmt, NT>(w[p][t], b[p & 1], acc[t]);
+        if (c + p + PF < c1) {
+#pragma unroll
+          for (int t = 0; t < NTILES; ++t) load_w<Fmt>(w[p][t], tiles[t], c + p + PF, lane, ld);
+        }
       }
     }
   }
 }
 
-// Address of this lane's ldmatrix.x4 row for token block 0 (tokens 0..15) at k = 0.
-template <typename ET>
-__device__ __forceinline__ const ET* xs_lane_ptr(const ET* xs, int xstride, int lane) {
-  const int tok = ((lane >> 4) << 3) + (lane & 7);
-  const int kof = ((lane >> 3) & 1) << 3;
-  return xs + tok * xstride + kof;
+template <class Fmt, int NT, int PF>
+__device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int c0, int c1, int lane,
+                                            const XRows<typename Fmt::ET, NT>& x, float (&acc)[NT][4]) {
+  const uint8_t* const tiles[1] = {tile};
+  float (&a1)[1][NT][4] = *reinterpret_cast<float (*)[1][NT][4]>(&acc);
+  stream_tiles<Fmt, NT, PF, 1>(tiles, ld, c0, c1, lane, x, a1);
 }
 
 // Fragment element r (0..3) of n-tile j: (row within the 16-row tile, token).

@@ -10,7 +10,8 @@ exactly q * scale.
 
 Stream layouts (see csrc/stream_gemm.cuh): every function here is a pure
 permutation / bit packing implemented with torch tensor ops, so it runs on the
-device that holds the weights.
+device that holds the weights.  K is permuted within 32-wide blocks
+(``physical_k``) so that the kernels read activations with 16-byte loads.
 """
 from __future__ import annotations
 
@@ -35,14 +36,21 @@ def dequantize(q: torch.Tensor, scale: torch.Tensor, group: int) -> torch.Tensor
     return (q.float() * scale.float().repeat_interleave(group, -1))
 
 
+def physical_k(step, tig, second, e):
+    """Physical K offset (within the chunk) of the mma-logical element k = 16*step + 2*tig
+    + 8*second + e.  Within each 32-wide block the streams are permuted so that lane tig's
+    B fragments of steps 2p and 2p+1 are the 8 contiguous activations 32p + 8*tig .. +7."""
+    return 32 * (step // 2) + 8 * tig + 4 * (step % 2) + 2 * second + e
+
+
 def _lane_maps(steps: int, device):
-    """Row-in-tile and column-in-group of nibble j of word (lane, step)."""
+    """Row-in-tile and (physical) column-in-group of nibble j of word (lane, step)."""
     lane = torch.arange(32, device=device).view(32, 1, 1)
     s = torch.arange(steps, device=device).view(1, steps, 1)
     j = torch.arange(8, device=device).view(1, 1, 8)
     gid, tig = lane // 4, lane % 4
     row = gid + 8 * (j & 1)
-    col = s * 16 + 2 * tig + 8 * ((j >> 1) & 1) + (j >> 2)
+    col = physical_k(s, tig, (j >> 1) & 1, j >> 2)
     return row.expand(32, steps, 8), col.expand(32, steps, 8)
 
 
@@ -118,7 +126,7 @@ def pack_b16(weight: torch.Tensor) -> torch.Tensor:
     half = torch.arange(2, device=dev).view(1, 1, 1, 2)
     gid, tig = lane // 4, lane % 4
     row = gid + 8 * (reg & 1)
-    col = s * 16 + 2 * tig + 8 * (reg >> 1) + half
+    col = physical_k(s, tig, reg >> 1, half)
     row, col = torch.broadcast_tensors(row, col)
     vals = w[:, :, row, col]                                    # [nt, nc, 32, 4(step), 4(reg), 2]
     vals = vals.permute(0, 1, 3, 2, 4, 5).contiguous()          # [nt, nc, step, lane, reg, 2]

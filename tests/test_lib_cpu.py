@@ -70,7 +70,9 @@ def test_w4_stream_fragment_layout():
             word = words[(step // 4) * 128 + lane * 4 + step % 4]
             for j in range(8):
                 row = gid + 8 * (j & 1)
-                col = step * 16 + 2 * tig + 8 * ((j >> 1) & 1) + (j >> 2)
+                # mma-logical k = 16*step + 2*tig + 8*second + e, stored permuted in 32-blocks
+                second, e = (j >> 1) & 1, j >> 2
+                col = 32 * (step // 2) + 8 * tig + 4 * (step % 2) + 2 * second + e
                 assert (word >> (4 * j)) & 15 == int(q[row, col]) + 8
 
 
@@ -84,7 +86,7 @@ def test_b16_stream_fragment_layout():
             base = step * 256 + lane * 8
             for reg in range(4):
                 row = gid + 8 * (reg & 1)
-                col = step * 16 + 2 * tig + 8 * (reg >> 1)
+                col = 32 * (step // 2) + 8 * tig + 4 * (step % 2) + 2 * (reg >> 1)
                 assert st[base + reg * 2] == float(w[row, col])
                 assert st[base + reg * 2 + 1] == float(w[row, col + 1])
 
@@ -99,6 +101,12 @@ def test_quantizer_matches_oracle():
     qo, so = quantize_w4(w, 128)
     np.testing.assert_array_equal(q.numpy(), qo)
     np.testing.assert_array_equal(s.float().numpy(), so)
+
+
+def test_k_permutation_is_a_bijection_per_block():
+    from qwen35_dflash_b200 import w4
+    cols = sorted(w4.physical_k(s, t, sec, e) for s in range(2) for t in range(4) for sec in range(2) for e in range(2))
+    assert cols == list(range(32))
 
 
 def test_fused_ops_module_binds_like_the_reference_adapter():
