@@ -91,16 +91,36 @@ def test_layers_teacher_forced(cuda_lib):
     assert rows_ok >= 0.97 * rows, (rows_ok, rows)
 
 
+def _greedy_chain(sess, next_token, n=16):
+    """Proposals equal to the engine's own greedy continuation from the committed state:
+    iterate verify until the block is self-consistent (p[i+1] = prediction after p[i])."""
+    props = [next_token] + [0] * (n - 1)
+    for _ in range(n):
+        v = sess.verify(props)
+        new = [next_token] + list(v.expected_next_tokens[1:n])
+        v.abort()
+        if new == props:
+            break
+        props = new
+    return props
+
+
+def _near_tie(row, a, b, ulps=4):
+    """Oracle logits of tokens a and b within ``ulps`` bf16 ulps (2^-7 relative) of each other."""
+    return abs(float(row[a]) - float(row[b])) <= ulps * 2 ** -7 * max(1.0, abs(float(row[b])))
+
+
 def test_session_rounds_match_oracle(cuda_lib, golden):
-    """prefill + block verify/commit rounds vs the bf16 oracle run from the engine's own
-    committed state each round (per-step identity).  A prediction may differ only where
-    the oracle's two candidate logits are within four bf16 ulps (2^-7 relative each: the
-    bf16 residual stream of two implementations that round at the same points but sum in
-    different fp32 orders drifts by a few ulps over the layers); the accepted counts must
-    match on >= 99% of rounds."""
+    """DFlash rounds (the engine's own greedy chain with a seeded corruption, then commit
+    of the accepted prefix) vs the bf16 oracle run from the engine's own committed state
+    each round.  A predicted token may differ from the oracle's only where the oracle's
+    two candidate logits are within four bf16 ulps (2^-7 relative each: two
+    implementations that round at the same points but sum in different fp32 orders drift
+    by a few ulps over the layers), and an accepted count only where the first such
+    near-tie sits inside the accepted prefix; >= 95% of the predictions must agree."""
     from qwen35_dflash_b200.session import TargetSession
     cfg, raw, oracle = _tiny()
-    eng = _engine(cfg, raw)
+    eng = _engine(cfg, raw, capacity=2048)
     sess = TargetSession(eng)
     d = golden("tiny_session.npz")
     prompt = [int(t) for t in d["prompt"]]
@@ -108,46 +128,42 @@ def test_session_rounds_match_oracle(cuda_lib, golden):
     top1, feats, _, _ = oracle.forward(np.asarray([prompt]))
     assert sess.next_token == int(top1[0, -1])
     assert_close(to_np(sess.last_features[0]), feats[0, -1:], 2e-2, 1e-2, "prefill features", row_scale=True)
-    agree = total = same_acc = rounds = 0
+    agree = total = same_acc = tie_acc = 0
     rng = np.random.default_rng(11)
-    greedy = [int(t) for t in d["greedy"]]
-    for r in range(12):
+    rounds = 48
+    for r in range(rounds):
         next_token = sess.next_token
+        props = _greedy_chain(sess, next_token)
+        j = int(rng.integers(1, 18))
+        if j < 16:
+            props[j] = int((props[j] + 1 + rng.integers(0, cfg.vocab_size - 1)) % cfg.vocab_size)
         ostate = _oracle_state_from_engine(oracle, eng)
-        # proposals: the oracle's own greedy continuation with one seeded corruption
-        cont = [next_token]
-        o_top, _, _, _ = oracle.forward(np.asarray([[next_token]]), ostate.copy())
-        props = [next_token] + [int(t) for t in rng.integers(0, cfg.vocab_size, 15)]
-        j = int(rng.integers(1, 17))
-        if r % 2 == 0:
-            # accept-friendly rounds: proposals follow the oracle's predictions up to j
-            state = ostate.copy()
-            tok = next_token
-            for i in range(1, 16):
-                t1, _, state, _ = oracle.forward(np.asarray([[tok]]), state)
-                tok = int(t1[0, 0])
-                props[i] = tok if i < j else props[i]
         v = sess.verify(props)
-        o_top1, _, _, logits = oracle.forward(np.asarray([props]), ostate.copy(), return_logits=True)
+        o_top1, _, _, logits = oracle.forward(np.asarray([props]), ostate, return_logits=True)
         exp = (next_token,) + tuple(int(t) for t in o_top1[0])
+        ties = set()
         for i, (a, b) in enumerate(zip(v.expected_next_tokens, exp)):
             total += 1
             if a == b:
                 agree += 1
             else:
-                row = logits[0, i - 1]
-                margin = abs(float(row[a]) - float(row[b]))
-                assert margin <= 4 * 2 ** -7 * max(1.0, abs(float(row[b]))), (r, i, a, b, margin)
+                assert i > 0 and _near_tie(logits[0, i - 1], a, b), (r, i, a, b)
+                ties.add(i)
         acc = 0
         for i, t in enumerate(props):
             if t != exp[i]:
                 break
             acc += 1
-        same_acc += int(v.max_accepted_prefix == acc)
-        rounds += 1
-        v.commit(v.max_accepted_prefix)
+        got = v.max_accepted_prefix
+        if got == acc:
+            same_acc += 1
+        else:
+            # the decisions part at the first position where the predictions differ
+            assert min(got, acc) in ties, (r, got, acc, sorted(ties))
+            tie_acc += 1
+        v.commit(got)
     assert agree >= 0.95 * total, (agree, total)
-    assert same_acc >= 0.99 * rounds, (same_acc, rounds)
+    assert same_acc + tie_acc == rounds and same_acc >= 0.75 * rounds, (same_acc, tie_acc, rounds)
 
 
 def test_verification_semantics(cuda_lib):
