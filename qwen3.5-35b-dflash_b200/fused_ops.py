@@ -11,8 +11,8 @@ defines the seven operators with the signatures, argument meaning, validation er
 tensors; outputs are new tensors and inputs are never written.  There is no CPU or
 dtype fallback: a missing library or a CPU tensor raises.
 
-Extra entry points (ignored by ModuleFusedOps): ``qlinear_w4a16``, ``linear_b16``,
-``moe_w4a16``.
+Extra entry points (ignored by ModuleFusedOps): ``moe_with_routing``, ``qlinear_w4a16``,
+``linear_b16``.
 """
 from __future__ import annotations
 
