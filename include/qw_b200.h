@@ -107,6 +107,23 @@ int qw_attention(const void* q, const void* k, const void* v, void* out, int dty
 int64_t qw_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq,
                                 int64_t dim, int64_t max_len);
 
+/* qw_attention without a workspace argument.  No counterpart in the reference: it is
+ * an addition for callers that cannot allocate device memory per call (a host runtime
+ * that owns all device memory through its own pool, or a thread on which a cudaMalloc
+ * would synchronise the device).  The split-K scratch is a fixed array of
+ * QW_ATTN_NOALLOC_SCRATCH_BYTES in this library's device memory, held on every GPU that
+ * loads the library until the process exits; shapes whose qw_attn_workspace_bytes
+ * exceeds it are rejected with QW_ERR_ARG.  Nothing is allocated.  The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress, with that device
+ * current), so make that first call before any stream capture.  All calls on a device
+ * share the one array: calls that overlap on the GPU (other streams, other host threads)
+ * race and corrupt each other's results; serialise them.  Nothing in the array needs
+ * clearing between calls.  Same arguments and results as qw_attention. */
+#define QW_ATTN_NOALLOC_SCRATCH_BYTES (16 * 1024 * 1024)
+int qw_attention_noalloc(const void* q, const void* k, const void* v, void* out, int dtype,
+                         int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq, int64_t total,
+                         int64_t dim, int64_t query_start, float scale, void* stream);
+
 /* moe(hidden, router_weight, gate_up, down, top_k) — reference/fused_ops.py:148-173.
  * Dense expert weights in the activation dtype (bf16 or f16): hidden [T,H],
  * router [E,H], gate_up [E,2I,H], down [E,H,I] -> out [T,H].  Selection repeats

@@ -463,3 +463,88 @@ extern "C" int qw_attn_paged(const void* q, const void* k_cache, const void* v_c
                                       H * D, static_cast<const __nv_bfloat16*>(gate), S * ldg, 2 * D, ldg,
                                       as_stream(stream));
 }
+
+// ------------------------------------------------------------------ allocation-free variant
+// qw_attention_noalloc: qw_attention with its split-K scratch taken from a fixed array
+// in this library's device memory instead of a caller-supplied workspace, for callers
+// that cannot allocate device memory (a host runtime with its own pool and no hook for
+// per-call scratch, a driver thread that must not call cudaMalloc because it would
+// synchronise the device).  The array is a file-scope __device__ variable: every GPU
+// that loads this module holds QW_ATTN_NOALLOC_SCRATCH_BYTES of it until the process
+// exits.  Host code never uses the array's name as a pointer (on the host it is only a
+// stand-in symbol); the device address comes from cudaGetSymbolAddress, looked up once
+// per device, with that device current, on the first call made on it.
+namespace qw {
+
+static __device__ __align__(256) float g_attn_noalloc_scratch[QW_ATTN_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static float* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// Device address of the scratch array on the current device (looked up on first use).
+static int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_status(err, "attention_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES)
+    return fail(QW_ERR_UNSUPPORTED, "attention_noalloc: device %d beyond the %d this build tracks", dev,
+                NOALLOC_MAX_DEVICES);
+  std::lock_guard<std::mutex> guard(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (err != cudaSuccess) return cuda_status(err, "attention_noalloc: cudaGetSymbolAddress of the scratch");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return QW_OK;
+}
+
+}  // namespace qw
+
+extern "C" int qw_attention_noalloc(const void* q, const void* k, const void* v, void* out, int dtype,
+                                    int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq, int64_t total,
+                                    int64_t dim, int64_t query_start, float scale, void* stream) {
+  QW_CHECK_ARG(q && k && v && out, "attention_noalloc: null pointer");
+  QW_CHECK_ARG(batch >= 1 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && seq >= 1 &&
+                   query_start >= 0 && query_start + seq == total && scale > 0.f && batch < 65536,
+               "attention_noalloc requires causal append-only GQA [B,H,S,D] inputs");
+  QW_CHECK_ARG(dtype == QW_BF16 || dtype == QW_F16, "attention_noalloc: bf16 or fp16 required");
+  if (dim != 32 && dim != 64 && dim != 128 && dim != 256)
+    return fail(QW_ERR_UNSUPPORTED, "attention_noalloc: head dim %lld not built (32, 64, 128, 256)",
+                static_cast<long long>(dim));
+  SplitPlan p = plan_splits(static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(kv_heads),
+                            static_cast<int>(seq), static_cast<int>(total));
+  const int64_t need = static_cast<int64_t>(p.nsplit) * batch * heads * seq * (dim + 2) * 4;
+  QW_CHECK_ARG(need <= static_cast<int64_t>(QW_ATTN_NOALLOC_SCRATCH_BYTES),
+               "attention_noalloc: this shape needs %lld scratch bytes, the static scratch holds %lld "
+               "(use qw_attention with a caller workspace)",
+               static_cast<long long>(need), static_cast<long long>(QW_ATTN_NOALLOC_SCRATCH_BYTES));
+  float* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != QW_OK) return rc;
+  // Nothing in the scratch has to start at zero: the split kernel writes every
+  // (split, row) partial and max/sum pair that the combine kernel then reads, so the
+  // previous call's contents are never observed.
+  const int64_t S = seq, D = dim, T = total;
+  cudaStream_t st = as_stream(stream);
+  float* opart = scratch;
+  float* ml = opart + static_cast<int64_t>(p.nsplit) * batch * heads * seq * dim;
+#define QW_ATT_NA(ET)                                                                               \
+  do {                                                                                              \
+    AttnArgs<ET> a{};                                                                               \
+    a.q = static_cast<const ET*>(q); a.qb = heads * S * D; a.qh = S * D; a.qs = D;                 \
+    a.k = static_cast<const ET*>(k); a.v = static_cast<const ET*>(v);                              \
+    a.pages = nullptr; a.max_pages = 1; a.P = static_cast<int>(T);                                  \
+    a.qpos = nullptr; a.qpos_scalar = static_cast<int>(query_start);                                \
+    a.B = static_cast<int>(batch); a.H = static_cast<int>(heads); a.Hkv = static_cast<int>(kv_heads); \
+    a.S = static_cast<int>(seq); a.kc = p.kc; a.nsplit = p.nsplit; a.rowgroups = p.rowgroups;       \
+    a.scale = scale; a.opart = opart; a.ml = ml;                                                    \
+    return dispatch_attn<ET>(static_cast<int>(dim), a, static_cast<ET*>(out), heads * S * D, S * D, D, \
+                             nullptr, 0, 0, 0, st);                                                 \
+  } while (0)
+  if (dtype == QW_BF16) QW_ATT_NA(__nv_bfloat16);
+  QW_ATT_NA(__half);
+#undef QW_ATT_NA
+}

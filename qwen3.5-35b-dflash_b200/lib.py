@@ -19,6 +19,7 @@ QW_OK, QW_ERR_ARG, QW_ERR_UNSUPPORTED, QW_ERR_CUDA, QW_ERR_TIMEOUT = range(5)
 QW_F32, QW_F16, QW_BF16 = 0, 1, 2
 QW_OUT_BF16, QW_OUT_F32, QW_OUT_RESID_BF16 = 0, 1, 2
 QW_MAX_BLOCK = 16
+QW_ATTN_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024  # static scratch of qw_attention_noalloc
 
 _c = ctypes
 P, I32, I64, F32 = _c.c_void_p, _c.c_int32, _c.c_int64, _c.c_float
@@ -47,6 +48,7 @@ SIGNATURES = {
     "qw_cache_update": (_c.c_int, [P, P, P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, P]),
     "qw_attention": (_c.c_int, [P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, I64, I64, F32, P, P]),
     "qw_attn_workspace_bytes": (I64, [I64, I64, I64, I64, I64, I64]),
+    "qw_attention_noalloc": (_c.c_int, [P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, I64, I64, F32, P]),
     "qw_attn_prep": (_c.c_int, [P, I64, P, P, F32, F32, I32, P, P, I32, I32, P, P, P, I64, I64, I64,
                                 I64, I64, P]),
     "qw_attn_paged": (_c.c_int, [P, P, P, P, I32, I32, P, I64, P, I64, P, I64, I64, I64, I64, I64,
