@@ -217,6 +217,7 @@ def run_ours(args, rank, world, local_rank):
     alg = eng.algorithmic_bytes([active[l] for l in range(cfg.num_hidden_layers)])
 
     eng.capture()
+    launches = eng.launches_per_step()
     gen = torch.Generator(device=dev)
     gen.manual_seed(11 + rank)
     props = torch.randint(0, cfg.vocab_size, (total_steps, B * S), generator=gen, device=dev, dtype=torch.int32)
@@ -309,7 +310,7 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": round(tok / (e2e_ms * 1e-3), 2), "unit": "tok/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 2 * B * 4,
                     "api": "TargetEngine.serve_step (pinned host proposals -> graph -> accepted/next tokens)"},
-            "gpu_launches": gpu_launch_count(cfg),
+            "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": "moe_up_kernel (routed + shared expert gate/up, W4A16)",
                          "achieved": round(rl_achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(rl_achieved / hbm, 4), "peak_kind": f"{peak_kind} burst copy",
@@ -355,17 +356,6 @@ def time_moe_up(eng, cfg, dev, iters: int = 50):
     w4b = 2 * I * H // 2 + 2 * I * (H // g) * 2
     nbytes = (active + 1) * w4b + T * H * 2 + (T * k + T) * I * 2
     return {"us": statistics.median(times), "bytes": nbytes, "active": active}
-
-
-def gpu_launch_count(cfg) -> int:
-    """Kernels of this library launched per timed step (graph nodes of ours)."""
-    per_gdn = 1 + 1 + 1 + 1 + 1          # norm, qkvz, ab, gdn verify, out_proj(+residual)
-    per_attn = 1 + 1 + 1 + 2 + 1         # norm, qkv, prep, attention split + combine, o_proj
-    per_moe = 1 + 1 + 1 + 2 + 1          # post norm, router, route, up + down, combine
-    n = len(cfg.gdn_layers) * per_gdn + len(cfg.attn_layers) * per_attn + cfg.num_hidden_layers * per_moe
-    n += 1 + 1 + 1                       # final norm, lm_head argmax, accept
-    n += 2 if cfg.gdn_layers else 0      # GDN state commit + conv tail commit
-    return n
 
 
 def run_reference(args, rank, world):

@@ -213,6 +213,17 @@ int32_t qw_moe_active_experts(const void* workspace, int64_t tokens, int64_t exp
 int qw_moe_combine(void* workspace, void* out, int residual, int64_t tokens, int64_t hidden,
                    int64_t experts, int64_t inter, int64_t top_k, int has_shared, void* stream);
 
+/* qw_moe_combine (residual form, bf16) fused with the RMSNorm that follows it at a
+ * layer boundary (fused/model.py:386-409: the next layer's input norm, or the final
+ * norm): hidden = bf16(hidden + moe) in place, then normed = rms_norm(hidden) with the
+ * +1 gamma convention as qw_residual_norm, and, when tap != NULL, the feature tap
+ * (hidden, or normed with tap_normed != 0) at tap[t*ldf + i].  hidden, normed, gamma
+ * and tap 8-byte aligned, hidden_dim and ldf multiples of 4; top_k <= 16. */
+int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens, int64_t hidden_dim,
+                        int64_t experts, int64_t inter, int64_t top_k, int has_shared,
+                        const void* gamma, void* normed, float eps, void* tap, int64_t ldf,
+                        int tap_normed, void* stream);
+
 /* Host helper: device addresses of the routing results inside a workspace
  * (part fp32 [T,k+1,H], topk_idx int32 [T,k], topk_w fp32 [T,k], shared_gate fp32 [T]). */
 int qw_moe_partials(void* workspace, int64_t tokens, int64_t hidden, int64_t experts,
@@ -277,7 +288,7 @@ typedef struct {
 
 /* Block verify of one layer (`layers_dev[layer]`, a device array): writes out[],
  * reads the banks, never writes them.  (dk,dv) in {(128,128),(64,64),(128,64)},
- * 1 <= seq <= QW_MAX_BLOCK. */
+ * 1 <= seq <= QW_MAX_BLOCK; proj 16-byte aligned with ldp a multiple of 8. */
 int qw_gdn_verify(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int layer,
                   void* stream);
 

@@ -63,6 +63,11 @@ class OracleTarget:
         inv = 1.0 / (theta ** (np.arange(0, rot, 2, dtype=np.float32) / rot))
         self.inv_freq = inv.astype(np.float32)
         self.rotary_dim = rot
+        # when a list: each MoE call appends, per token, the gap between the k-th and
+        # (k+1)-th largest router logits in bf16 ulps of the k-th (a routing near-tie
+        # is a gap of a few ulps; two implementations that sum the router GEMV in
+        # different orders may select differently there)
+        self.router_gaps = None
 
     # helpers -------------------------------------------------------------------------
     def r(self, x):
@@ -165,6 +170,14 @@ class OracleTarget:
 
     def moe(self, x, p):
         c = self.c
+        if self.router_gaps is not None:
+            flat = np.asarray(x, np.float32).reshape(-1, x.shape[-1])
+            lg = self.r(flat @ self.w[p + ".gate.weight"].T)
+            srt = -np.sort(-lg, -1)
+            k = c["num_experts_per_tok"]
+            top, nxt = srt[:, k - 1], srt[:, min(k, srt.shape[-1] - 1)]
+            ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(top), 1e-30))) - 7)
+            self.router_gaps.append((top - nxt) / ulp)
         routed = F.moe(x, self.w[p + ".gate.weight"], self.w[p + ".experts.gate_up_proj"],
                        self.w[p + ".experts.down_proj"], top_k=c["num_experts_per_tok"],
                        dtype=self.act, emulate_rounding=True)

@@ -26,6 +26,9 @@ namespace qw {
 
 constexpr int ATT_KT = 32;       // keys per tile
 constexpr int ATT_MAXROWS = 128; // query rows per CTA
+constexpr int ATT_NST = 3;        // K/V tile stages in flight
+constexpr int ATT_MIN_KC = 256;   // keys per split at least (partials cost as much as the keys)
+constexpr int ATT_PGCAP = 64;     // page indices staged per CTA
 
 template <typename ET>
 struct AttnArgs {
@@ -41,6 +44,7 @@ struct AttnArgs {
   float scale;
   float* opart;                // [nsplit, B, H, S, D]
   float* ml;                   // [nsplit, B, H, S, 2]
+  int pgcap;                   // page indices a CTA may stage in shared memory
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
@@ -57,8 +61,8 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   constexpr int XS = D + 8;  // smem row stride (elements)
   extern __shared__ __align__(16) uint8_t smem[];
   ET* qsm = reinterpret_cast<ET*>(smem);                 // [128][XS]
-  ET* ksm = qsm + ATT_MAXROWS * XS;                      // [32][XS]
-  ET* vsm = ksm + ATT_KT * XS;                           // [32][XS]
+  ET* ksm = qsm + ATT_MAXROWS * XS;                      // ATT_NST stages of K [32][XS], V [32][XS]
+  int* pg = reinterpret_cast<int*>(ksm + ATT_NST * 2 * ATT_KT * XS);  // [pgcap] page of each key page
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / a.rowgroups, rg = blockIdx.y % a.rowgroups;
   const int b = blockIdx.z;
@@ -76,16 +80,39 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   const int gid = lane >> 2, tig = lane & 3;
   const bool f16 = std::is_same<ET, __half>::value;
 
-  // Q rows -> smem (row r: head kvh*G + (row0+r)/S, position (row0+r)%S)
+  // Q rows -> smem (row r: head kvh*G + (row0+r)/S, position (row0+r)%S), first cp.async group
   for (int i = threadIdx.x; i < nwarps * 16 * (D / 8); i += blockDim.x) {
     const int r = i / (D / 8), c = (i % (D / 8)) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < nrows) {
-      const int rr = row0 + r;
-      const int h = kvh * G + rr / a.S, s = rr % a.S;
-      v = *reinterpret_cast<const uint4*>(a.q + b * a.qb + h * a.qh + s * a.qs + c);
+    const bool valid = r < nrows;
+    const int rr = row0 + (valid ? r : 0);
+    const int h = kvh * G + rr / a.S, s = rr % a.S;
+    cp_async16(qsm + r * XS + c, a.q + b * a.qb + h * a.qh + s * a.qs + c, valid);
+  }
+  // page of every key page this CTA reads (staged when it fits)
+  const int p0 = k0 / a.P, npg = (k1 - 1) / a.P - p0 + 1;
+  const bool staged = npg <= a.pgcap;
+  if (staged)
+    for (int i = threadIdx.x; i < npg; i += blockDim.x) pg[i] = a.pages ? a.pages[b * a.max_pages + p0 + i] : b;
+  __syncthreads();
+  // K/V tile t0.. -> stage st (keys past k1 zero-filled)
+  auto load_tile = [&](int st, int t0) {
+    ET* kd = ksm + st * 2 * ATT_KT * XS;
+    ET* vd = kd + ATT_KT * XS;
+    for (int i = threadIdx.x; i < ATT_KT * (D / 8); i += blockDim.x) {
+      const int r = i / (D / 8), c = (i % (D / 8)) * 8;
+      const bool valid = t0 + r < k1;
+      const int t = valid ? t0 + r : k0;
+      const int page = staged ? pg[t / a.P - p0] : (a.pages ? a.pages[b * a.max_pages + t / a.P] : b);
+      const int64_t off = ((static_cast<int64_t>(page) * a.Hkv + kvh) * a.P + t % a.P) * D + c;
+      cp_async16(kd + r * XS + c, a.k + off, valid);
+      cp_async16(vd + r * XS + c, a.v + off, valid);
     }
-    *reinterpret_cast<uint4*>(qsm + r * XS + c) = v;
+  };
+  const int ntiles = (k1 - k0 + ATT_KT - 1) / ATT_KT;
+#pragma unroll
+  for (int st = 0; st < ATT_NST - 1; ++st) {
+    if (st < ntiles) load_tile(st, k0 + st * ATT_KT);
+    cp_async_commit();
   }
 
   float o[D / 8][4];
@@ -107,23 +134,18 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   const int vb_key = ((lane >> 3) & 1) * 8 + (lane & 7);
   const int vb_col = (lane >> 4) * 8;
 
-  for (int t0 = k0; t0 < k1; t0 += ATT_KT) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < ATT_KT * (D / 8); i += blockDim.x) {
-      const int r = i / (D / 8), c = (i % (D / 8)) * 8;
-      const int t = t0 + r;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (t < k1) {
-        const int page = a.pages ? a.pages[b * a.max_pages + t / a.P] : b;
-        const int64_t off = ((static_cast<int64_t>(page) * a.Hkv + kvh) * a.P + t % a.P) * D + c;
-        kv = *reinterpret_cast<const uint4*>(a.k + off);
-        vv = *reinterpret_cast<const uint4*>(a.v + off);
-      }
-      *reinterpret_cast<uint4*>(ksm + r * XS + c) = kv;
-      *reinterpret_cast<uint4*>(vsm + r * XS + c) = vv;
+  for (int it = 0; it < ntiles; ++it) {
+    const int t0 = k0 + it * ATT_KT;
+    cp_async_wait<ATT_NST - 2>();
+    __syncthreads();  // tile it landed for every thread; stage (it - 1) % NST is free
+    {
+      const int nt = it + ATT_NST - 1;
+      if (nt < ntiles) load_tile(nt % ATT_NST, k0 + nt * ATT_KT);
+      cp_async_commit();
     }
-    __syncthreads();
     if (wrow >= nrows) continue;
+    const ET* kst = ksm + (it % ATT_NST) * 2 * ATT_KT * XS;
+    const ET* vst = kst + ATT_KT * XS;
     // S = Q K^T for 16 rows x 32 keys
     float sc[4][4];
 #pragma unroll
@@ -135,7 +157,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
 #pragma unroll
       for (int jp = 0; jp < 2; ++jp) {
         uint32_t bf[4];
-        ldmatrix_x4(bf, ksm + (jp * 16 + kb_key) * XS + ks * 16 + kb_col);
+        ldmatrix_x4(bf, kst + (jp * 16 + kb_key) * XS + ks * 16 + kb_col);
         mma16816<ET>(sc[2 * jp], af, bf[0], bf[1]);
         mma16816<ET>(sc[2 * jp + 1], af, bf[2], bf[3]);
       }
@@ -194,7 +216,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
 #pragma unroll
       for (int dp = 0; dp < D / 16; ++dp) {
         uint32_t vf[4];
-        ldmatrix_x4_trans(vf, vsm + (kk * 16 + vb_key) * XS + dp * 16 + vb_col);
+        ldmatrix_x4_trans(vf, vst + (kk * 16 + vb_key) * XS + dp * 16 + vb_col);
         mma16816<ET>(o[2 * dp], pf, vf[0], vf[1]);
         mma16816<ET>(o[2 * dp + 1], pf, vf[2], vf[3]);
       }
@@ -223,29 +245,55 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
 }
 
 // out element (b, h, s, d) at out + b*ob + h*oh + s*os + d; gate (optional) likewise.
+// One CTA per (b, h, s): warp 0 turns the splits' (max, sum) pairs into per-split
+// weights exp(m - M) (0 for a split with no visible key) and the total L; then every
+// thread sums its output columns over the splits in split order.
+constexpr int ATT_MAXSPLIT = 64;
+
 template <typename ET, int D>
 __global__ void attn_combine_kernel(const float* __restrict__ opart, const float* __restrict__ ml,
                                     ET* __restrict__ out, int64_t ob, int64_t oh, int64_t os,
                                     const ET* __restrict__ gate, int64_t gb, int64_t gh, int64_t gs,
                                     const int32_t* __restrict__ qposv, int qpos_scalar, int B, int H,
                                     int S, int kc) {
+  __shared__ float s_w[ATT_MAXSPLIT];
+  __shared__ float s_l;
   const int s = blockIdx.x % S, h = (blockIdx.x / S) % H, b = blockIdx.x / (S * H);
   const int qpos = qposv ? qposv[b] : qpos_scalar;
   const int nsp = (qpos + S + kc - 1) / kc;
-  float M = -INFINITY;
-  for (int sp = 0; sp < nsp; ++sp) M = fmaxf(M, ml[((((int64_t)sp * B + b) * H + h) * S + s) * 2]);
-  float L = 0.f;
-  for (int sp = 0; sp < nsp; ++sp) {
-    const int64_t base = (((int64_t)sp * B + b) * H + h) * S + s;
-    const float m = ml[base * 2];
-    if (m != -INFINITY) L += __expf(m - M) * ml[base * 2 + 1];
+  const int64_t row = (static_cast<int64_t>(b) * H + h) * S + s;   // row index within one split
+  const int64_t split_stride = static_cast<int64_t>(B) * H * S;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float m[2], l[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int sp = lane + 32 * u;
+      m[u] = -INFINITY; l[u] = 0.f;
+      if (sp < nsp) { m[u] = ml[(sp * split_stride + row) * 2]; l[u] = ml[(sp * split_stride + row) * 2 + 1]; }
+    }
+    const float M = warp_max(fmaxf(m[0], m[1]));
+    float L = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int sp = lane + 32 * u;
+      const float w = (m[u] == -INFINITY) ? 0.f : __expf(m[u] - M);
+      if (sp < nsp) s_w[sp] = w;
+      L += w * l[u];
+    }
+    L = warp_sum(L);
+    if (lane == 0) s_l = L;
   }
+  __syncthreads();
+  const float L = s_l;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
+    const float* op = opart + row * D + d;
+#pragma unroll 8
     for (int sp = 0; sp < nsp; ++sp) {
-      const int64_t base = (((int64_t)sp * B + b) * H + h) * S + s;
-      const float m = ml[base * 2];
-      if (m != -INFINITY) acc += __expf(m - M) * opart[base * D + d];
+      const float w = s_w[sp];
+      const float v = op[sp * split_stride * D];
+      if (w != 0.f) acc += w * v;
     }
     float y = rnd<ET>(acc / L);
     if (gate) y = rnd<ET>(y * rnd<ET>(sigmoid_f(to_f(gate[b * gb + h * gh + s * gs + d]))));
@@ -322,6 +370,7 @@ static SplitPlan plan_splits(int B, int H, int Hkv, int S, int max_len) {
   if (target > max_tiles) target = max_tiles;
   if (target < 1) target = 1;
   int kc = (max_len + target - 1) / target;
+  if (kc < ATT_MIN_KC) kc = ATT_MIN_KC;
   kc = (kc + ATT_KT - 1) / ATT_KT * ATT_KT;
   p.kc = kc;
   p.nsplit = (max_len + kc - 1) / kc;
@@ -335,13 +384,16 @@ static int launch_attn(AttnArgs<ET> a, ET* out, int64_t ob, int64_t oh, int64_t 
   const int R = G * a.S;
   const int rows_cta = R < ATT_MAXROWS ? R : ATT_MAXROWS;
   const int warps = (rows_cta + 15) / 16;
-  const size_t smem = (static_cast<size_t>(warps * 16 > ATT_MAXROWS ? warps * 16 : ATT_MAXROWS) + 2 * ATT_KT) * (D + 8) * sizeof(ET);
+  const size_t smem = (static_cast<size_t>(ATT_MAXROWS) + ATT_NST * 2 * ATT_KT) * (D + 8) * sizeof(ET) +
+                     ATT_PGCAP * sizeof(int);
+  a.pgcap = ATT_PGCAP;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
     err = cudaFuncSetAttribute(attn_split_kernel<ET, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   });
   if (err != cudaSuccess) return cuda_status(err, "attention smem attribute");
+  if (a.nsplit > ATT_MAXSPLIT) return fail(QW_ERR_UNSUPPORTED, "attention: %d key splits", a.nsplit);
   attn_split_kernel<ET, D><<<dim3(a.nsplit, a.Hkv * a.rowgroups, a.B), warps * 32, smem, st>>>(a);
   QW_LAUNCH_CHECK("attention split");
   attn_combine_kernel<ET, D><<<a.B * a.H * a.S, D < 256 ? D : 256, 0, st>>>(

@@ -103,25 +103,46 @@ struct GdnSmem {
   float beta[QW_MAX_BLOCK];
   float sumsq[QW_MAX_BLOCK];
   float total[QW_MAX_BLOCK];
+  // the block's projections of this CTA's channels: q [0, DK), k [DK, 2DK), v [2DK, 2DK+COLS)
+  __align__(16) __nv_bfloat16 xin[QW_MAX_BLOCK][2 * DK + COLS];
+  __align__(16) __nv_bfloat16 zin[QW_MAX_BLOCK][COLS];   // output gate inputs
 };
 
+// Position in shared memory of q/k element j: the thread owning state rows
+// [kq * ROWS, (kq + 1) * ROWS) reads its elements i..i+3 (i a multiple of 4) as one
+// 16-byte vector at (i / 4) * 4 * KSPLIT + 4 * kq, so the KSPLIT threads of a column
+// read consecutive vectors (no bank conflicts).
+template <int DK>
+__device__ __forceinline__ int kperm(int j) {
+  constexpr int ROWS = DK / KSPLIT;
+  const int kq = j / ROWS, i = j % ROWS;
+  return (i / 4) * (4 * KSPLIT) + kq * 4 + (i % 4);
+}
+
 // conv + SiLU of one channel over the block's tokens, rounded to bf16 after the conv and
-// after the SiLU (the reference's activation tensors, fused/model.py:238-239).
-__device__ __forceinline__ void conv_channel(const GdnDims& d, const GdnLayer& L, int64_t slot,
-                                             int b, int c, int ntok, float* dst, int stride) {
-  const int K = d.conv_k;
-  float win[QW_MAX_CONV];
-  const __nv_bfloat16* hist = L.conv_hist + (slot * d.channels + c) * (K - 1);
-  for (int j = 0; j < K - 1; ++j) win[j] = __bfloat162float(hist[j]);
-  float w[QW_MAX_CONV];
-  for (int j = 0; j < K; ++j) w[j] = __bfloat162float(L.conv_w[c * K + j]);
-  for (int t = 0; t < ntok; ++t) {
-    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
-    win[K - 1] = __bfloat162float(L.proj[row * d.ldp + c]);
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) acc = fmaf(win[j], w[j], acc);
-    dst[t * stride] = rbf(silu_f(rbf(acc)));
-    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+// after the SiLU (the reference's activation tensors, fused/model.py:238-239).  hist /
+// w hold the channel's conv tail and taps, the block inputs come from shared memory
+// (src[t * sstride]).
+constexpr int GDN_CONV_K = 4;  // conv taps of the block kernels
+
+__device__ __forceinline__ void conv_channel(const float (&hist)[GDN_CONV_K - 1], const float (&w)[GDN_CONV_K],
+                                             const __nv_bfloat16* src, int sstride, int ntok, float* dst,
+                                             int stride) {
+  constexpr int K = GDN_CONV_K;
+  float win[K];
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) win[j] = hist[j];
+#pragma unroll
+  for (int t = 0; t < QW_MAX_BLOCK; ++t) {
+    if (t < ntok) {
+      win[K - 1] = __bfloat162float(src[t * sstride]);
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) acc = fmaf(win[j], w[j], acc);
+      dst[t * stride] = rbf(silu_f(rbf(acc)));
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
+    }
   }
 }
 
@@ -145,6 +166,15 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
 
   if (COMMIT && ntok <= 0) return;      // nothing accepted: the state stays S0
 
+  // ---- state columns into registers (bank layout [slot][head][Dv][Dk], column-major);
+  // issued first so their latency overlaps the staging below
+  float st[ROWS];
+  float* scol = L.state + ((slot * d.v_heads + h) * DV + vcol0 + col) * static_cast<int64_t>(DK) + kq * ROWS;
+#pragma unroll
+  for (int i = 0; i < ROWS; i += 4) {
+    float4 v4 = *reinterpret_cast<const float4*>(scol + i);
+    st[i] = v4.x; st[i + 1] = v4.y; st[i + 2] = v4.z; st[i + 3] = v4.w;
+  }
   // ---- gates (fused/model.py:243-253, fp32)
   for (int t = tid; t < ntok; t += THREADS) {
     const int64_t row = static_cast<int64_t>(b) * d.seq + t;
@@ -153,19 +183,65 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     sm.beta[t] = sigmoid_f(bl);
     sm.g[t] = -__expf(L.A_log[h]) * softplus_f(al + L.dt_bias[h]);
   }
-  // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns
+  // ---- stage the block's projections of this CTA's channels (and z) in shared memory:
+  // per token 8-element vectors of the q, k, v (and z) segments, all loads in flight at once
   {
+    const int vw = d.v_heads * DV;
+    constexpr int QV = DK / 8, KV = DK / 8, VV = COLS / 8;
+    constexpr int PER = QV + KV + VV + VV;
+    const int64_t segq = kh * DK, segk = kw + kh * DK, segv = 2 * kw + h * DV + vcol0,
+                  segz = 2 * kw + vw + h * DV + vcol0;
+    for (int i = tid; i < ntok * PER; i += THREADS) {
+      const int t = i / PER, v = i % PER;
+      if (COMMIT && (v < QV || v >= QV + KV + VV)) continue;   // commit needs k and v only
+      const __nv_bfloat16* rowp = L.proj + (static_cast<int64_t>(b) * d.seq + t) * d.ldp;
+      const __nv_bfloat16* src;
+      __nv_bfloat16* dst;
+      if (v < QV) { src = rowp + segq + v * 8; dst = &sm.xin[t][v * 8]; }
+      else if (v < QV + KV) { src = rowp + segk + (v - QV) * 8; dst = &sm.xin[t][DK + (v - QV) * 8]; }
+      else if (v < QV + KV + VV) { src = rowp + segv + (v - QV - KV) * 8; dst = &sm.xin[t][2 * DK + (v - QV - KV) * 8]; }
+      else { src = rowp + segz + (v - QV - KV - VV) * 8; dst = &sm.zin[t][(v - QV - KV - VV) * 8]; }
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+  }
+  __syncthreads();
+  // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns; each thread's
+  // channels' conv tails and taps are loaded together first
+  {
+    constexpr int K = GDN_CONV_K;
+    constexpr int XS = 2 * DK + COLS;
+    constexpr int CPT = (2 * DK + COLS + THREADS - 1) / THREADS;  // channels per thread
     const int nq = COMMIT ? 0 : DK;
     const int nch = nq + DK + COLS;
-    for (int i = tid; i < nch; i += THREADS) {
+    float hreg[CPT][K - 1], wreg[CPT][K];
+    int chan[CPT];
+#pragma unroll
+    for (int r = 0; r < CPT; ++r) {
+      const int i = tid + r * THREADS;
+      if (i < nq) chan[r] = kh * DK + i;
+      else if (i < nq + DK) chan[r] = kw + kh * DK + (i - nq);
+      else chan[r] = 2 * kw + h * DV + vcol0 + (i - nq - DK);
+      if (i < nch) {
+        const __nv_bfloat16* hist = L.conv_hist + (slot * d.channels + chan[r]) * (K - 1);
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j) hreg[r][j] = __bfloat162float(hist[j]);
+#pragma unroll
+        for (int j = 0; j < K; ++j) wreg[r][j] = __bfloat162float(L.conv_w[chan[r] * K + j]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < CPT; ++r) {
+      const int i = tid + r * THREADS;
+      if (i >= nch) continue;
+      // q and k are stored with row j at kperm(j) (see the recurrence)
       if (i < nq) {
-        conv_channel(d, L, slot, b, kh * DK + i, ntok, &sm.q[0][i], DK);
+        conv_channel(hreg[r], wreg[r], &sm.xin[0][i], XS, ntok, &sm.q[0][kperm<DK>(i)], DK);
       } else if (i < nq + DK) {
         const int j = i - nq;
-        conv_channel(d, L, slot, b, kw + kh * DK + j, ntok, &sm.k[0][j], DK);
+        conv_channel(hreg[r], wreg[r], &sm.xin[0][DK + j], XS, ntok, &sm.k[0][kperm<DK>(j)], DK);
       } else {
         const int j = i - nq - DK;
-        conv_channel(d, L, slot, b, 2 * kw + h * DV + vcol0 + j, ntok, &sm.v[0][j], COLS);
+        conv_channel(hreg[r], wreg[r], &sm.xin[0][2 * DK + j], XS, ntok, &sm.v[0][j], COLS);
       }
     }
   }
@@ -190,26 +266,24 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
       }
     }
   }
-  // ---- state columns into registers (bank layout [slot][head][Dv][Dk], column-major)
-  float st[ROWS];
-  float* scol = L.state + ((slot * d.v_heads + h) * DV + vcol0 + col) * static_cast<int64_t>(DK) + kq * ROWS;
-#pragma unroll
-  for (int i = 0; i < ROWS; i += 4) {
-    float4 v4 = *reinterpret_cast<const float4*>(scol + i);
-    st[i] = v4.x; st[i + 1] = v4.y; st[i + 2] = v4.z; st[i + 3] = v4.w;
-  }
   __syncthreads();
   // ---- the recurrence (fused_ops.py:98-106)
   for (int t = 0; t < ntok; ++t) {
     const float decay = __expf(sm.g[t]);
-    const float* kt = &sm.k[t][kq * ROWS];
+    const float* kt = &sm.k[t][kq * 4];
+    float kr[ROWS];
     float p0 = 0.f, p1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < ROWS; i += 2) {
-      st[i] *= decay;
-      st[i + 1] *= decay;
-      p0 = fmaf(st[i], kt[i], p0);
-      p1 = fmaf(st[i + 1], kt[i + 1], p1);
+    for (int i = 0; i < ROWS; i += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kt + (i / 4) * 4 * KSPLIT);
+      kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        st[i + e] *= decay;
+        st[i + e + 1] *= decay;
+        p0 = fmaf(st[i + e], kr[i + e], p0);
+        p1 = fmaf(st[i + e + 1], kr[i + e + 1], p1);
+      }
     }
     float pred = p0 + p1;
     pred += __shfl_xor_sync(0xffffffffu, pred, 1);
@@ -217,16 +291,21 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     const float delta = (sm.v[t][col] - pred) * sm.beta[t];
     if (COMMIT) {
 #pragma unroll
-      for (int i = 0; i < ROWS; ++i) st[i] = fmaf(kt[i], delta, st[i]);
+      for (int i = 0; i < ROWS; ++i) st[i] = fmaf(kr[i], delta, st[i]);
     } else {
-      const float* qt = &sm.q[t][kq * ROWS];
+      const float* qt = &sm.q[t][kq * 4];
       float o0 = 0.f, o1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < ROWS; i += 2) {
-        st[i] = fmaf(kt[i], delta, st[i]);
-        st[i + 1] = fmaf(kt[i + 1], delta, st[i + 1]);
-        o0 = fmaf(st[i], qt[i], o0);
-        o1 = fmaf(st[i + 1], qt[i + 1], o1);
+      for (int i = 0; i < ROWS; i += 4) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qt + (i / 4) * 4 * KSPLIT);
+        const float qr[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          st[i + e] = fmaf(kr[i + e], delta, st[i + e]);
+          st[i + e + 1] = fmaf(kr[i + e + 1], delta, st[i + e + 1]);
+          o0 = fmaf(st[i + e], qr[e], o0);
+          o1 = fmaf(st[i + e + 1], qr[e + 1], o1);
+        }
       }
       float o = o0 + o1;
       o += __shfl_xor_sync(0xffffffffu, o, 1);
@@ -270,7 +349,7 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     const float inv = rsqrtf(sm.total[t] / DV + d.eps);
     const float n = rbf(sm.o[t][c] * inv);
     const float y = rbf(n * __bfloat162float(L.norm_w[vcol0 + c]));
-    const float z = __bfloat162float(L.proj[row * d.ldp + 2 * kw + vw + vc]);
+    const float z = __bfloat162float(sm.zin[t][c]);
     L.out[row * vw + vc] = __float2bfloat16_rn(y * rbf(silu_f(z)));
   }
 }
@@ -335,8 +414,11 @@ static int check_dims(const GdnDims& d) {
   QW_CHECK_ARG(d.v_heads >= 1 && d.k_heads >= 1 && d.v_heads % d.k_heads == 0,
                "gdn block: value heads must be a multiple of key heads");
   QW_CHECK_ARG(d.conv_k >= 2 && d.conv_k <= QW_MAX_CONV, "gdn block: conv kernel out of range");
+  if (d.conv_k != GDN_CONV_K)
+    return fail(QW_ERR_UNSUPPORTED, "gdn block: conv kernel width %d not built (%d)", d.conv_k, GDN_CONV_K);
   QW_CHECK_ARG(d.channels == 2 * d.k_heads * d.dk + d.v_heads * d.dv, "gdn block: channel count");
   QW_CHECK_ARG(d.ldp >= d.channels + d.v_heads * d.dv, "gdn block: projection row too short");
+  QW_CHECK_ARG(d.ldp % 8 == 0, "gdn block: the projection row stride must be a multiple of 8 elements");
   QW_CHECK_ARG(d.slots != nullptr, "gdn block: null slot table");
   return QW_OK;
 }

@@ -28,6 +28,7 @@
 // equal probabilities).
 #include <mutex>
 
+#include "bulk_ring.cuh"
 #include "stream_gemm.cuh"
 
 namespace qw {
@@ -37,7 +38,7 @@ struct RouteView {
   int32_t* topk_idx;    // [T*k]
   float* topk_w;        // [T*k]  (value of the activation dtype)
   float* shared_gate;   // [T]
-  int32_t* n_active;    // [1]
+  int32_t* n_active;    // [4]: [0] active experts, [1] device status (sticky, bulk_ring.cuh)
   int32_t* active;      // [min(E, T*k)]
   int32_t* pair_off;    // [min(E, T*k) + 1]
   int32_t* pair_tok;    // [T*k]
@@ -240,8 +241,17 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
 }
 
 // ------------------------------------------------------------------ route kernel
-// One CTA; warp w handles tokens w, w + nwarps, ...  Dynamic smem per warp:
-// E floats + E ints + 2 * (E + 1) int16.
+// One CTA; warp w handles tokens w, w + nwarps, ...
+//
+// Selection.  When the k+1 largest logits of a row are strictly ordered
+// (v0 > v1 > ... > v_{k-1} > v_k), every correct top-k returns the same indices in the
+// same (descending) order, torch.topk's included, so the warp extracts them directly
+// from registers (k+1 rounds of a warp arg-max).  A row with any tie among them (or
+// more than 256 experts) runs the libstdc++ emulation above, which reproduces the order
+// torch.topk gives tied values.  Dynamic smem per warp (emulation rows):
+// E floats + E ints + 2 * (E + 2) int16.
+constexpr int ROUTE_MAXJ = 8;  // logits per lane on the fast path (E <= 256)
+
 template <typename LT>
 __global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logits, int64_t ldl, int T,
                                                      int E, int k, int shared_col, int act_is_f16,
@@ -256,27 +266,73 @@ __global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logi
   int16_t* pos_r = pos_l + E + 2;
   for (int t = warp; t < T; t += nw) {
     const LT* row = logits + static_cast<int64_t>(t) * ldl;
-    float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) {
-      const float v = to_f(row[e]);
-      q.v[e] = v;
-      q.i[e] = e;
-      mx = fmaxf(mx, v);
+    float sel_v = -INFINITY;   // lane r < k: value of the r-th selected expert
+    int sel_i = 0;             //             and its index
+    float mx, z;
+    bool exact = E > 32 * ROUTE_MAXJ;
+    if (!exact) {
+      float v[ROUTE_MAXJ];
+      mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < ROUTE_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = e < E ? to_f(row[e]) : -INFINITY;
+        mx = fmaxf(mx, v[j]);
+      }
+      mx = warp_max(mx);
+      z = 0.f;
+#pragma unroll
+      for (int j = 0; j < ROUTE_MAXJ; ++j)
+        if (lane + 32 * j < E) z += __expf(v[j] - mx);
+      z = warp_sum(z);
+      unsigned taken = 0u;
+      float prev = 0.f;
+      const int rounds = k < E ? k + 1 : k;
+      for (int r = 0; r < rounds; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < ROUTE_MAXJ; ++j) {
+          const int e = lane + 32 * j;
+          if (e < E && !(taken >> j & 1u) && (bv < v[j] || bi == 0x7fffffff)) { bv = v[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        // a tie (or a NaN) anywhere among the k+1 largest: use the exact emulation
+        if (r > 0 && !(prev > bv)) { exact = true; break; }
+        prev = bv;
+        if (r < k && lane == r) { sel_v = bv; sel_i = bi; }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      }
     }
-    mx = warp_max(mx);
-    float z = 0.f;
-    for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
-    z = warp_sum(z);
-    __syncwarp();
-    warp_topk(q, E, k, pos_l, pos_r, lane);
+    if (exact) {
+      mx = -INFINITY;
+      for (int e = lane; e < E; e += 32) {
+        const float v = to_f(row[e]);
+        q.v[e] = v;
+        q.i[e] = e;
+        mx = fmaxf(mx, v);
+      }
+      mx = warp_max(mx);
+      z = 0.f;
+      for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
+      z = warp_sum(z);
+      __syncwarp();
+      warp_topk(q, E, k, pos_l, pos_r, lane);
+      if (lane < k) { sel_v = q.v[lane]; sel_i = q.i[lane]; }
+    }
     // renormalized weights of the selected (fused_ops.py:162-164)
     float p = 0.f;
-    if (lane < k) p = __expf(q.v[lane] - mx) / z;
+    if (lane < k) p = __expf(sel_v - mx) / z;
     float ps = p;
     for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
     if (lane < k) {
       const float w = p / ps;
-      rv.topk_idx[t * k + lane] = q.i[lane];
+      rv.topk_idx[t * k + lane] = sel_i;
       rv.topk_w[t * k + lane] = act_is_f16 ? rnd<__half>(w) : rbf(w);
     }
     if (lane == 0) {
@@ -291,37 +347,63 @@ __global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logi
   }
   __syncthreads();
   // expert -> pair lists (ascending expert, then ascending token)
-  int* cnt = reinterpret_cast<int*>(smem);       // reuse: [E] counts, [E] active position
-  int* apos = cnt + E;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  const int nthr = blockDim.x;
+  int* cnt = reinterpret_cast<int*>(smem);       // reuse: [E] counts
+  int* apos = cnt + E;                           // [E] next free position of each expert's list
+  unsigned* bits = reinterpret_cast<unsigned*>(apos + E);  // [E] token bits of one 32-token chunk
+  int* red = reinterpret_cast<int*>(bits + E);   // [64] scan partials
+  for (int e = threadIdx.x; e < E; e += nthr) cnt[e] = 0;
   __syncthreads();
-  for (int pidx = threadIdx.x; pidx < T * k; pidx += blockDim.x) atomicAdd(&cnt[rv.topk_idx[pidx]], 1);
+  for (int pidx = threadIdx.x; pidx < T * k; pidx += nthr) atomicAdd(&cnt[rv.topk_idx[pidx]], 1);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int na = 0, off = 0;
-    for (int e = 0; e < E; ++e) {
-      if (cnt[e]) {
-        rv.active[na] = e;
-        rv.pair_off[na] = off;
-        apos[e] = off;
-        off += cnt[e];
-        ++na;
-      } else {
-        apos[e] = -1;
-      }
+  // exclusive scans of (active flag, count) over experts: thread i owns a contiguous run
+  const int per = (E + nthr - 1) / nthr;
+  const int e0 = threadIdx.x * per, e1 = min(E, e0 + per);
+  int my_a = 0, my_c = 0;
+  for (int e = e0; e < e1; ++e) { my_a += cnt[e] > 0; my_c += cnt[e]; }
+  int inc_a = my_a, inc_c = my_c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ua = __shfl_up_sync(0xffffffffu, inc_a, o), uc = __shfl_up_sync(0xffffffffu, inc_c, o);
+    if (lane >= o) { inc_a += ua; inc_c += uc; }
+  }
+  if (lane == 31) { red[warp] = inc_a; red[32 + warp] = inc_c; }
+  __syncthreads();
+  int wa = 0, wc = 0;
+  for (int w = 0; w < warp; ++w) { wa += red[w]; wc += red[32 + w]; }
+  int na = wa + inc_a - my_a, off = wc + inc_c - my_c;
+  for (int e = e0; e < e1; ++e) {
+    if (cnt[e]) {
+      rv.active[na] = e;
+      rv.pair_off[na] = off;
+      apos[e] = off;
+      off += cnt[e];
+      ++na;
     }
+  }
+  if (threadIdx.x == nthr - 1) {
     rv.pair_off[na] = off;
     *rv.n_active = na;
   }
   __syncthreads();
-  for (int pidx = threadIdx.x; pidx < T * k; pidx += blockDim.x) {
-    const int t = pidx / k, s = pidx % k;
-    const int e = rv.topk_idx[pidx];
-    int rank = 0;
-    for (int u = 0; u < t; ++u)
-      for (int j = 0; j < k; ++j) rank += (rv.topk_idx[u * k + j] == e);
-    rv.pair_tok[apos[e] + rank] = t;
-    rv.pair_slot[apos[e] + rank] = s;
+  // ranks within each expert's list, 32 tokens at a time
+  for (int t0 = 0; t0 < T; t0 += 32) {
+    const int tn = min(32, T - t0);
+    for (int e = threadIdx.x; e < E; e += nthr) bits[e] = 0u;
+    __syncthreads();
+    for (int pidx = threadIdx.x; pidx < tn * k; pidx += nthr)
+      atomicOr(&bits[rv.topk_idx[t0 * k + pidx]], 1u << (pidx / k));
+    __syncthreads();
+    for (int pidx = threadIdx.x; pidx < tn * k; pidx += nthr) {
+      const int tl = pidx / k, s = pidx % k;
+      const int e = rv.topk_idx[t0 * k + pidx];
+      const int at = apos[e] + __popc(bits[e] & ((1u << tl) - 1u));
+      rv.pair_tok[at] = t0 + tl;
+      rv.pair_slot[at] = s;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += nthr) apos[e] += __popc(bits[e]);
+    __syncthreads();
   }
 }
 
@@ -460,6 +542,322 @@ __global__ void __launch_bounds__(SG_WARPS * 32, 2) moe_down_kernel(MoeArgs<type
   }
 }
 
+// ------------------------------------------------------------------ bulk-copy expert kernels
+// Verify-block form (T <= 16 tokens) of the gate/up and down kernels: persistent CTAs
+// (one per SM) of XT_WARPS warps, each warp streaming its weight tiles from HBM through
+// its own ring of shared-memory stages with bulk copies (bulk_ring.cuh).  The expert
+// inputs sit in shared memory, so the loop waits on nothing but the weight stream; the
+// arithmetic (and its order) is that of moe_up_kernel / moe_down_kernel, so the results
+// are the same bits.
+constexpr int XT_WARPS = 8;
+constexpr int XT_NST = 2;        // stages per warp ring
+constexpr int XT_MAXT = 16;      // tokens of the block
+constexpr int XT_BAR_BYTES = (XT_WARPS * XT_NST * 8 + 127) / 128 * 128;
+constexpr int XT_PAD = 32;       // bf16 of row padding: 16-byte fragment loads hit distinct banks
+constexpr int XT_CPS = 8;        // W4 chunks per stage (at most)
+
+// Route lists of the block staged in shared memory.
+struct XtRoute {
+  int n_active;
+  int active[XT_MAXT * 16];
+  int off[XT_MAXT * 16 + 1];
+  int tok[XT_MAXT * 16];
+  int slot[XT_MAXT * 16];
+};
+
+__device__ __forceinline__ void xt_load_route(XtRoute& r, const RouteView& rv, int T, int k) {
+  const int np = T * k;
+  if (threadIdx.x == 0) {
+    const int cap = min(np, XT_MAXT * 16);
+    r.n_active = max(0, min(*rv.n_active, cap));
+  }
+  __syncthreads();
+  const int na = r.n_active;
+  for (int i = threadIdx.x; i < na; i += blockDim.x) r.active[i] = rv.active[i];
+  for (int i = threadIdx.x; i <= na; i += blockDim.x) r.off[i] = rv.pair_off[i];
+  for (int i = threadIdx.x; i < np; i += blockDim.x) { r.tok[i] = rv.pair_tok[i]; r.slot[i] = rv.pair_slot[i]; }
+}
+
+// Slot sl of the block: 0 the shared expert (when present), then the active experts.
+template <typename A>
+__device__ __forceinline__ void xt_slot(const A& a, const XtRoute& r, int sl, bool up, const uint8_t*& w,
+                                        int& np, int& pbase) {
+  if (a.has_shared && sl == 0) {
+    w = up ? a.sgu : a.sdn;
+    np = a.T;
+    pbase = -1;
+    return;
+  }
+  const int ai = sl - a.has_shared;
+  const int e = r.active[ai];
+  w = up ? a.gu + e * a.gu_stride : a.dn + e * a.dn_stride;
+  pbase = r.off[ai];
+  np = r.off[ai + 1] - pbase;
+}
+
+// acc[nt] += W4 chunk (16 rows x G) . x rows (token of lane gid in n-tile nt at xr[nt]).
+template <int G>
+__device__ __forceinline__ void xt_chunk(const uint8_t* chunk, const __nv_bfloat16* const (&xr)[2], int k0,
+                                         int lane, bool two, float (&acc)[2][4]) {
+  using Fmt = W4Fmt<G>;
+  uint32_t w[Fmt::WORDS];
+#pragma unroll
+  for (int v = 0; v < Fmt::NV; ++v) {
+    const uint8_t* p = chunk + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
+    if constexpr (Fmt::VW == 4) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p);
+      w[v * 4 + 0] = u.x; w[v * 4 + 1] = u.y; w[v * 4 + 2] = u.z; w[v * 4 + 3] = u.w;
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(p);
+      w[v * 2 + 0] = u.x; w[v * 2 + 1] = u.y;
+    }
+  }
+  const uint32_t sc = *reinterpret_cast<const uint32_t*>(chunk + 8 * G + (lane >> 2) * 4);
+  const int tig = lane & 3;
+  float part[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.f;
+#pragma unroll
+  for (int q = 0; q < G / 32; ++q) {
+    uint32_t b[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (j == 0 || two) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + 32 * q + 8 * tig);
+        b[j][0] = v.x; b[j][1] = v.y; b[j][2] = v.z; b[j][3] = v.w;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t a[4];
+      dequant_w4_word(w[2 * q + h], a);
+      mma16816<__nv_bfloat16>(part[0], a, b[0][2 * h], b[0][2 * h + 1]);
+      if (two) mma16816<__nv_bfloat16>(part[1], a, b[1][2 * h], b[1][2 * h + 1]);
+    }
+  }
+  const float2 s2 = bf162_to_f2(sc);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    acc[j][0] = fmaf(part[j][0], s2.x, acc[j][0]);
+    acc[j][1] = fmaf(part[j][1], s2.x, acc[j][1]);
+    acc[j][2] = fmaf(part[j][2], s2.y, acc[j][2]);
+    acc[j][3] = fmaf(part[j][3], s2.y, acc[j][3]);
+  }
+}
+
+struct XtArgs {
+  MoeArgs<__nv_bfloat16> m;
+  int32_t* status;
+  long long limit;
+};
+
+// Gate/up.  Unit = (slot, intermediate tile j): the gate row tile j then the up row tile
+// I/16 + j, each cut into stages of up to XT_CPS chunks; unit u goes to warp u mod (all
+// warps).  x [T, H] is staged once per CTA.
+template <int G>
+__global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs args) {
+  using Fmt = W4Fmt<G>;
+  const MoeArgs<__nv_bfloat16>& a = args.m;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  XtRoute& rt = *reinterpret_cast<XtRoute*>(smem + XT_BAR_BYTES);
+  const int H = a.H, I = a.I, T = a.T;
+  const int XS = H + XT_PAD;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(xs) + ((static_cast<size_t>(T) * XS * 2 + 127) / 128) * 128;
+  const int nch = H / G, cps = nch < XT_CPS ? nch : XT_CPS, spt = nch / cps;
+  const uint32_t sbytes = cps * Fmt::CHB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
+  if (lane == 0)
+    for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
+  fence_barrier_init();
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  xt_load_route(rt, rv, T, a.k);
+  // x -> shared memory (cp.async), overlapped with the first weight stages below
+  for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
+    const int r = i / (H / 8), c = (i % (H / 8)) * 8;
+    cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(r) * H + c, true);
+  }
+  cp_async_commit();
+  __syncthreads();
+  const int J = I / 16;
+  const int nslots = a.has_shared + rt.n_active;
+  const int nu = nslots * J;
+  const int gw = blockIdx.x * XT_WARPS + warp, nw = gridDim.x * XT_WARPS;
+  const int my_units = gw < nu ? (nu - 1 - gw) / nw + 1 : 0;
+  const int Q = my_units * 2 * spt;
+  auto src = [&](int q) -> const uint8_t* {
+    const int u = gw + (q / (2 * spt)) * nw, part = q % (2 * spt);
+    const uint8_t* w;
+    int np, pb;
+    xt_slot(a, rt, u / J, true, w, np, pb);
+    const int tile = (part / spt) * J + u % J;
+    return w + Fmt::tile_offset(tile, H, 0) + static_cast<int64_t>(part % spt) * sbytes;
+  };
+  if (lane == 0)
+    for (int q = 0; q < XT_NST && q < Q; ++q) ring.issue(q, src(q), sbytes);
+  cp_async_wait<0>();
+  __syncthreads();
+  const int gid = lane >> 2;
+  int q = 0;
+  for (int i = 0; i < my_units; ++i) {
+    const int u = gw + i * nw, j = u % J;
+    const uint8_t* w;
+    int np, pb;
+    xt_slot(a, rt, u / J, true, w, np, pb);
+    const bool two = np > 8;
+    const __nv_bfloat16* xr[2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int idx = min(nt * 8 + gid, np - 1);
+      xr[nt] = xs + (pb < 0 ? idx : rt.tok[pb + idx]) * XS;
+    }
+    float acc[2][2][4];
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) acc[g][nt][0] = acc[g][nt][1] = acc[g][nt][2] = acc[g][nt][3] = 0.f;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      for (int sub = 0; sub < spt; ++sub, ++q) {
+        if (!ring.wait(q, args.status)) {
+          if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
+          return;
+        }
+        const uint8_t* st = ring.stage(q);
+        for (int c = 0; c < cps; ++c) xt_chunk<G>(st + c * Fmt::CHB, xr, (sub * cps + c) * G, lane, two, acc[g]);
+        __syncwarp();
+        if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
+      }
+    }
+    // h = silu(gate) * up in the reference's rounding order
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int tl = frag_tok(lane, nt, r);
+        if (tl < np) {
+          const float gr = rbf(acc[0][nt][r]), ur = rbf(acc[1][nt][r]);
+          const float h = rbf(rbf(silu_f(gr)) * ur);
+          const int64_t hrow = pb < 0 ? static_cast<int64_t>(T) * a.k + tl : pb + tl;
+          a.hbuf[hrow * I + j * 16 + frag_row(lane, r)] = __float2bfloat16_rn(h);
+        }
+      }
+  }
+}
+
+// Down.  Unit = (slot, block of XT_WARPS * spw row tiles); the CTA's warps share the
+// unit, each streaming spw... stages of tiles; the unit's rows of h are staged in shared
+// memory (double-buffered across units).  Units go to CTAs round-robin.
+template <int G>
+__global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs args, int tiles_per_stage,
+                                                                         int stages_per_warp) {
+  using Fmt = W4Fmt<G>;
+  const MoeArgs<__nv_bfloat16>& a = args.m;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  XtRoute& rt = *reinterpret_cast<XtRoute*>(smem + XT_BAR_BYTES);
+  const int H = a.H, I = a.I, T = a.T;
+  const int HS = I + XT_PAD;
+  __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
+  const size_t hbytes = ((static_cast<size_t>(XT_MAXT) * HS * 2 + 127) / 128) * 128;
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(hs) + 2 * hbytes;
+  const int cpt = I / G;                         // chunks per row tile
+  const int tps = tiles_per_stage, spw = stages_per_warp;
+  const uint32_t sbytes = tps * cpt * Fmt::CHB;
+  const int rb_tiles = XT_WARPS * spw * tps;     // row tiles per unit
+  const int nrb = (H / 16) / rb_tiles;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
+  if (lane == 0)
+    for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
+  fence_barrier_init();
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  xt_load_route(rt, rv, T, a.k);
+  __syncthreads();
+  const int nslots = a.has_shared + rt.n_active;
+  const int nu = nslots * nrb;
+  const int my_units = blockIdx.x < nu ? (nu - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int Q = my_units * spw;
+  auto src = [&](int q) -> const uint8_t* {
+    const int u = blockIdx.x + (q / spw) * gridDim.x, l = q % spw;
+    const uint8_t* w;
+    int np, pb;
+    xt_slot(a, rt, u / nrb, false, w, np, pb);
+    const int tile = (u % nrb) * rb_tiles + (warp * spw + l) * tps;
+    return w + Fmt::tile_offset(tile, I, 0);
+  };
+  if (lane == 0)
+    for (int q = 0; q < XT_NST && q < Q; ++q) ring.issue(q, src(q), sbytes);
+  // h rows of unit i -> buffer i & 1
+  auto stage_h = [&](int i) {
+    const int u = blockIdx.x + i * gridDim.x;
+    const uint8_t* w;
+    int np, pb;
+    xt_slot(a, rt, u / nrb, false, w, np, pb);
+    const int64_t hb = pb < 0 ? static_cast<int64_t>(T) * a.k : pb;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(hs) + (i & 1) * hbytes);
+    for (int e = threadIdx.x; e < np * (I / 8); e += blockDim.x) {
+      const int r = e / (I / 8), c = (e % (I / 8)) * 8;
+      cp_async16(dst + r * HS + c, a.hbuf + (hb + r) * I + c, true);
+    }
+  };
+  if (my_units > 0) stage_h(0);
+  cp_async_commit();
+  const int gid = lane >> 2;
+  int q = 0;
+  bool ok = true;
+  for (int i = 0; i < my_units; ++i) {
+    if (i + 1 < my_units) stage_h(i + 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int u = blockIdx.x + i * gridDim.x;
+    const uint8_t* w;
+    int np, pb;
+    xt_slot(a, rt, u / nrb, false, w, np, pb);
+    const bool two = np > 8;
+    const __nv_bfloat16* hbuf_s =
+        reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<const uint8_t*>(hs) + (i & 1) * hbytes);
+    const __nv_bfloat16* xr[2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) xr[nt] = hbuf_s + min(nt * 8 + gid, np - 1) * HS;
+    for (int l = 0; l < spw && ok; ++l, ++q) {
+      if (!ring.wait(q, args.status)) {
+        if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
+        ok = false;
+        break;
+      }
+      const uint8_t* st = ring.stage(q);
+      for (int t = 0; t < tps; ++t) {
+        float acc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        for (int c = 0; c < cpt; ++c) xt_chunk<G>(st + (t * cpt + c) * Fmt::CHB, xr, c * G, lane, two, acc);
+        const int row0 = ((u % nrb) * rb_tiles + (warp * spw + l) * tps + t) * 16;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int tl = frag_tok(lane, nt, r);
+            if (tl < np) {
+              int tok, slot;
+              if (pb < 0) { tok = tl; slot = a.k; }
+              else { tok = rt.tok[pb + tl]; slot = rt.slot[pb + tl]; }
+              a.part[(static_cast<int64_t>(tok) * (a.k + 1) + slot) * H + row0 + frag_row(lane, r)] = acc[nt][r];
+            }
+          }
+      }
+      __syncwarp();
+      if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
+    }
+    // a warp that timed out keeps taking part in the CTA barriers until the end
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+}
+
 // Combine (fused/model.py:296-307 with fused_ops.py:165-172): per token, the routed
 // experts in ascending id, each raw output rounded to the activation dtype, times its
 // weight (rounded), added with a rounding; then + round(round(shared) * gate) when a
@@ -492,6 +890,94 @@ __global__ void moe_combine_kernel(const float* __restrict__ part, void* ws, ET*
   }
 }
 
+// Combine fused with the next RMSNorm (the boundary between decoder layers): per token
+// t, hidden[t] = bf16(hidden[t] + moe(t)) with moe(t) summed as moe_combine_kernel does
+// (ascending expert, rounding at each add, then the gated shared expert), then
+// normed[t] = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * bf16(gamma + 1)) as
+// residual_norm_kernel, and the optional feature tap (h, or the normed row).
+// One CTA per token; each thread owns runs of 4 columns (16-byte loads of the fp32
+// expert outputs, all k + 1 slots of a run issued before the ordered sum).
+constexpr int CN_THREADS = 256;
+
+template <int KMAX>
+__global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
+    const float* __restrict__ part, void* ws, __nv_bfloat16* __restrict__ hidden, int T, int H, int E, int k,
+    int has_shared, const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ normed, float eps,
+    __nv_bfloat16* __restrict__ tap, int64_t ldf, int tap_normed) {
+  __shared__ int s_slot[KMAX];
+  __shared__ float s_w[KMAX];
+  __shared__ float red[32];
+  const RouteView rv = route_view(ws, T, E, k);
+  const int t = blockIdx.x;
+  if (threadIdx.x < k) {
+    const int e = rv.topk_idx[t * k + threadIdx.x];
+    int rank = 0;
+    for (int j = 0; j < k; ++j) rank += rv.topk_idx[t * k + j] < e;
+    s_slot[rank] = threadIdx.x;
+    s_w[rank] = rv.topk_w[t * k + threadIdx.x];
+  }
+  __syncthreads();
+  const float sg = has_shared ? rv.shared_gate[t] : 0.f;
+  const float* pt = part + static_cast<int64_t>(t) * (k + 1) * H;
+  __nv_bfloat16* h = hidden + static_cast<int64_t>(t) * H;
+  float ss = 0.f;
+  for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
+    float4 y[KMAX + 1];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j)
+      if (j < k) y[j] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(s_slot[j]) * H + c);
+    if (has_shared) y[KMAX] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(k) * H + c);
+    const uint2 hraw = *reinterpret_cast<const uint2*>(h + c);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j < k) {
+        const float w = s_w[j];
+        acc[0] = rbf(acc[0] + rbf(rbf(y[j].x) * w));
+        acc[1] = rbf(acc[1] + rbf(rbf(y[j].y) * w));
+        acc[2] = rbf(acc[2] + rbf(rbf(y[j].z) * w));
+        acc[3] = rbf(acc[3] + rbf(rbf(y[j].w) * w));
+      }
+    }
+    if (has_shared) {
+      acc[0] = rbf(acc[0] + rbf(rbf(y[KMAX].x) * sg));
+      acc[1] = rbf(acc[1] + rbf(rbf(y[KMAX].y) * sg));
+      acc[2] = rbf(acc[2] + rbf(rbf(y[KMAX].z) * sg));
+      acc[3] = rbf(acc[3] + rbf(rbf(y[KMAX].w) * sg));
+    }
+    const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&hraw);
+    const float2 h01 = __bfloat1622float2(hp[0]), h23 = __bfloat1622float2(hp[1]);
+    const __nv_bfloat162 n01 = __floats2bfloat162_rn(h01.x + acc[0], h01.y + acc[1]);
+    const __nv_bfloat162 n23 = __floats2bfloat162_rn(h23.x + acc[2], h23.y + acc[3]);
+    uint2 out;
+    out.x = *reinterpret_cast<const uint32_t*>(&n01);
+    out.y = *reinterpret_cast<const uint32_t*>(&n23);
+    *reinterpret_cast<uint2*>(h + c) = out;
+    const float2 f01 = __bfloat1622float2(n01), f23 = __bfloat1622float2(n23);
+    ss += f01.x * f01.x + f01.y * f01.y + f23.x * f23.x + f23.y * f23.y;
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / H + eps);
+  for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
+    const uint2 hraw = *reinterpret_cast<const uint2*>(h + c);
+    const uint2 graw = *reinterpret_cast<const uint2*>(gamma + c);
+    const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&hraw);
+    const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&graw);
+    __nv_bfloat16 yv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float g = rbf(__bfloat162float(gv[i]) + 1.f);
+      yv[i] = __float2bfloat16_rn(rbf(__bfloat162float(hv[i]) * inv) * g);
+    }
+    const uint2 yraw = *reinterpret_cast<const uint2*>(yv);
+    *reinterpret_cast<uint2*>(normed + static_cast<int64_t>(t) * H + c) = yraw;
+    if (tap) {
+      // 8-byte stores need ldf and the tap column to be multiples of 4
+      *reinterpret_cast<uint2*>(tap + static_cast<int64_t>(t) * ldf + c) = tap_normed ? yraw : hraw;
+    }
+  }
+}
+
 // Router logits of the fused-ops operator: dense [E, H] weights, one warp per (t, e),
 // fp32 accumulate, one rounding to the activation dtype.
 template <typename ET>
@@ -513,7 +999,7 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   const int nw = T < 32 ? T : 32;
   const int per_warp = ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16;
   size_t smem = static_cast<size_t>(nw) * per_warp;
-  if (smem < static_cast<size_t>(E) * 8) smem = static_cast<size_t>(E) * 8;
+  if (smem < static_cast<size_t>(E) * 12 + 256) smem = static_cast<size_t>(E) * 12 + 256;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
@@ -548,6 +1034,100 @@ template <class Fmt, int PF>
 static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
   if (static_cast<int64_t>(a.T) * a.k <= 2LL * a.E) return launch_experts_nt<Fmt, 1, PF>(a, s, up, down);
   return launch_experts_nt<Fmt, 2, PF>(a, s, up, down);
+}
+
+static int sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
+constexpr size_t XT_SMEM_LIMIT = 227 * 1024;
+
+static size_t xt_route_bytes() { return XT_BAR_BYTES + (sizeof(XtRoute) + 127) / 128 * 128; }
+
+// Shapes the bulk-copy kernels take: the verify block (T <= 16), and stage geometry
+// that tiles the weights exactly.
+struct XtPlan {
+  bool up_ok, down_ok;
+  int down_tps, down_spw;
+  size_t up_smem, down_smem;
+};
+
+template <int G>
+static XtPlan xt_plan(const MoeArgs<__nv_bfloat16>& a) {
+  XtPlan p{};
+  constexpr int CHB = W4Fmt<G>::CHB;
+  const bool small = a.T <= XT_MAXT && static_cast<int64_t>(a.T) * a.k <= XT_MAXT * 16 && a.H % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.hbuf) & 15) == 0;
+  const int nch = a.H / G;
+  const int cps = nch < XT_CPS ? nch : XT_CPS;
+  p.up_smem = xt_route_bytes() + (static_cast<size_t>(a.T) * (a.H + XT_PAD) * 2 + 127) / 128 * 128 +
+              static_cast<size_t>(XT_WARPS) * XT_NST * cps * CHB;
+  p.up_ok = small && nch % cps == 0 && p.up_smem <= XT_SMEM_LIMIT;
+  const int cpt = a.I / G;
+  p.down_ok = false;
+  if (small && cpt >= 1 && cpt <= XT_CPS && XT_CPS % cpt == 0) {
+    p.down_tps = XT_CPS / cpt;
+    const int tiles = a.H / 16;
+    p.down_spw = 0;
+    for (int spw = 2; spw >= 1; --spw)
+      if (tiles % (XT_WARPS * spw * p.down_tps) == 0) { p.down_spw = spw; break; }
+    p.down_smem = xt_route_bytes() + 2 * ((static_cast<size_t>(XT_MAXT) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
+                  static_cast<size_t>(XT_WARPS) * XT_NST * p.down_tps * cpt * CHB;
+    p.down_ok = p.down_spw > 0 && p.down_smem <= XT_SMEM_LIMIT;
+  }
+  return p;
+}
+
+template <int G>
+static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p, cudaStream_t s, bool up,
+                               bool down, int32_t* status) {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(moe_up_bulk_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(XT_SMEM_LIMIT));
+    if (err == cudaSuccess)
+      err = cudaFuncSetAttribute(moe_down_bulk_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(XT_SMEM_LIMIT));
+  });
+  if (err != cudaSuccess) return cuda_status(err, "moe bulk smem attribute");
+  XtArgs xa{a, status, QW_WAIT_LIMIT};
+  const int grid = sm_count();
+  if (up) {
+    moe_up_bulk_kernel<G><<<grid, XT_WARPS * 32, p.up_smem, s>>>(xa);
+    QW_LAUNCH_CHECK("moe up (bulk)");
+  }
+  if (down) {
+    moe_down_bulk_kernel<G><<<grid, XT_WARPS * 32, p.down_smem, s>>>(xa, p.down_tps, p.down_spw);
+    QW_LAUNCH_CHECK("moe down (bulk)");
+  }
+  return QW_OK;
+}
+
+template <int G>
+static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bool up, bool down) {
+  const XtPlan p = xt_plan<G>(a);
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  int32_t* status = rv.n_active + 1;
+  if (up) {
+    const int rc = p.up_ok ? launch_experts_bulk<G>(a, p, s, true, false, status)
+                           : launch_experts<W4Fmt<G>, 4>(a, s, true, false);
+    if (rc != QW_OK) return rc;
+  }
+  if (down) {
+    const int rc = p.down_ok ? launch_experts_bulk<G>(a, p, s, false, true, status)
+                             : launch_experts<W4Fmt<G>, 4>(a, s, false, true);
+    if (rc != QW_OK) return rc;
+  }
+  return QW_OK;
 }
 
 }  // namespace qw
@@ -633,9 +1213,9 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   a.has_shared = shared_gate_up != nullptr;
   cudaStream_t s = as_stream(stream);
   switch (group) {
-    case 128: return launch_experts<W4Fmt<128>, 4>(a, s, up, dn);
-    case 64: return launch_experts<W4Fmt<64>, 4>(a, s, up, dn);
-    default: return launch_experts<W4Fmt<32>, 4>(a, s, up, dn);
+    case 128: return launch_experts_w4<128>(a, s, up, dn);
+    case 64: return launch_experts_w4<64>(a, s, up, dn);
+    default: return launch_experts_w4<32>(a, s, up, dn);
   }
 }
 
@@ -692,6 +1272,37 @@ extern "C" int qw_moe_combine(void* workspace, void* out, int residual, int64_t 
   moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, as_stream(stream)>>>(
       w.part, w.route, static_cast<__nv_bfloat16*>(out), T, H, E, k, has_shared, residual);
   QW_LAUNCH_CHECK("moe combine");
+  return QW_OK;
+}
+
+extern "C" int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens, int64_t hidden_dim,
+                                   int64_t experts, int64_t inter, int64_t top_k, int has_shared,
+                                   const void* gamma, void* normed, float eps, void* tap, int64_t ldf,
+                                   int tap_normed, void* stream) {
+  QW_CHECK_ARG(workspace && hidden && gamma && normed, "moe_combine_norm: null pointer");
+  QW_CHECK_ARG(tokens >= 1 && top_k >= 1 && top_k <= 16 && hidden_dim > 0 && hidden_dim % 4 == 0 && eps > 0.f,
+               "moe_combine_norm: invalid shape");
+  QW_CHECK_ARG(!tap || (ldf >= hidden_dim && ldf % 4 == 0 && (reinterpret_cast<uintptr_t>(tap) & 7) == 0),
+               "moe_combine_norm: tap rows must be 8-byte aligned (ldf a multiple of 4)");
+  QW_CHECK_ARG(((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(normed) |
+                 reinterpret_cast<uintptr_t>(gamma)) & 7) == 0,
+               "moe_combine_norm: hidden, normed and gamma must be 8-byte aligned");
+  const int T = static_cast<int>(tokens), H = static_cast<int>(hidden_dim), E = static_cast<int>(experts),
+            I = static_cast<int>(inter), k = static_cast<int>(top_k);
+  WsParts w = split_ws(workspace, T, H, E, I, k);
+  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(w.part) & 15) == 0, "moe_combine_norm: workspace alignment");
+  cudaStream_t s = as_stream(stream);
+  auto* hp = static_cast<__nv_bfloat16*>(hidden);
+  auto* gp = static_cast<const __nv_bfloat16*>(gamma);
+  auto* np_ = static_cast<__nv_bfloat16*>(normed);
+  auto* tp = static_cast<__nv_bfloat16*>(tap);
+  if (k <= 8)
+    moe_combine_norm_kernel<8><<<T, CN_THREADS, 0, s>>>(w.part, w.route, hp, T, H, E, k, has_shared, gp, np_, eps,
+                                                        tp, ldf, tap_normed);
+  else
+    moe_combine_norm_kernel<16><<<T, CN_THREADS, 0, s>>>(w.part, w.route, hp, T, H, E, k, has_shared, gp, np_,
+                                                         eps, tp, ldf, tap_normed);
+  QW_LAUNCH_CHECK("moe combine_norm");
   return QW_OK;
 }
 

@@ -221,13 +221,26 @@ class TargetEngine:
                                     c.linear_conv_kernel_dim, self.ldp, c.rms_norm_eps,
                                     self.slots.data_ptr(), self.accepted.data_ptr())
         self.graph = None
+        self._recording = None
+        self.captured_calls = {}
 
     # ------------------------------------------------------------------ helpers
     def _st(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
     def _call(self, name, *args):
+        if self._recording is not None:
+            self._recording[name] = self._recording.get(name, 0) + 1
         lib.check(getattr(self.lib, name)(*args), name)
+
+    # kernels each entry point launches (all others launch one)
+    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2}
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library in the captured step (counted from the entry calls)."""
+        if not self.captured_calls:
+            raise RuntimeError("capture() first")
+        return sum(n * self.KERNELS_PER_CALL.get(name, 1) for name, n in self.captured_calls.items())
 
     def _tap(self, layer: int):
         c = self.cfg
@@ -245,11 +258,12 @@ class TargetEngine:
         eps = c.rms_norm_eps
         L = c.num_hidden_layers
         for l, lw in enumerate(self.layers):
-            # input RMSNorm (+ embedding on layer 0, + tap of the previous layer)
-            self._call("qw_residual_norm", self.hidden.data_ptr(),
-                       self.tokens.data_ptr() if l == 0 else None, self.glob["embed"].data_ptr(),
-                       lw.in_norm.data_ptr(), self.normed.data_ptr(), self._tap(l - 1), c.feature_width, 0,
-                       T, H, eps, st)
+            if l == 0:
+                # embedding + input RMSNorm; later layers' input norms are fused into the
+                # previous layer's MoE combine
+                self._call("qw_residual_norm", self.hidden.data_ptr(), self.tokens.data_ptr(),
+                           self.glob["embed"].data_ptr(), lw.in_norm.data_ptr(), self.normed.data_ptr(),
+                           None, c.feature_width, 0, T, H, eps, st)
             if lw.kind == "linear_attention":
                 gi = self.gdn_idx[l]
                 self._call("qw_w4_linear", self.normed.data_ptr(), lw.qkvz.data_ptr(), self.proj[gi].data_ptr(),
@@ -288,10 +302,12 @@ class TargetEngine:
             self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                        lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
                        self.moe_ws.data_ptr(), st)
-            self._call("qw_moe_combine", self.moe_ws.data_ptr(), self.hidden.data_ptr(), 1, T, H, E, I, k, 1, st)
-        last_tap = self._tap(L - 1)
-        self._call("qw_residual_norm", self.hidden.data_ptr(), None, None, self.glob["final_norm"].data_ptr(),
-                   self.normed.data_ptr(), last_tap, c.feature_width, 1, T, H, eps, st)
+            # residual add of the MoE output + the next RMSNorm (next layer's input norm, or
+            # the final norm) + the feature tap of this layer (normed after the last layer)
+            last = l == L - 1
+            gamma = self.glob["final_norm"] if last else self.layers[l + 1].in_norm
+            self._call("qw_moe_combine_norm", self.moe_ws.data_ptr(), self.hidden.data_ptr(), T, H, E, I, k, 1,
+                       gamma.data_ptr(), self.normed.data_ptr(), eps, self._tap(l), c.feature_width, int(last), st)
         self._call("qw_lmhead_argmax", self.normed.data_ptr(), self.glob["lm_head"].data_ptr(), None,
                    self.keys.data_ptr(), T, self.vocab_pad, H, st)
 
@@ -379,8 +395,12 @@ class TargetEngine:
         torch.cuda.synchronize(self.device)
         self.restore(snapshot)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
-            self.step()
+        self._recording = {}
+        try:
+            with torch.cuda.graph(g, stream=s):
+                self.step()
+        finally:
+            self.captured_calls, self._recording = self._recording, None
         torch.cuda.synchronize(self.device)
         self.graph = g
         return g

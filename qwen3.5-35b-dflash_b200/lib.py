@@ -61,6 +61,7 @@ SIGNATURES = {
     "qw_moe_down_w4": (_c.c_int, [P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P]),
     "qw_moe_active_experts": (I32, [P, I64, I64, I64]),
     "qw_moe_combine": (_c.c_int, [P, P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P]),
+    "qw_moe_combine_norm": (_c.c_int, [P, P, I64, I64, I64, I64, I64, _c.c_int, P, P, F32, P, I64, _c.c_int, P]),
     "qw_moe_partials": (_c.c_int, [P, I64, I64, I64, I64, I64, _c.POINTER(P), _c.POINTER(P),
                                    _c.POINTER(P), _c.POINTER(P)]),
     "qw_w4_stream_bytes": (I64, [I64, I64, I32]),

@@ -117,7 +117,12 @@ def test_session_rounds_match_oracle(cuda_lib, golden):
     two candidate logits are within four bf16 ulps (2^-7 relative each: two
     implementations that round at the same points but sum in different fp32 orders drift
     by a few ulps over the layers), and an accepted count only where the first such
-    near-tie sits inside the accepted prefix; >= 95% of the predictions must agree."""
+    near-tie sits inside the accepted prefix; >= 95% of the predictions must agree.
+    A prediction may also differ where a token of the block at or before it sits on a
+    routing near-tie (k-th and (k+1)-th router logits within two bf16 ulps in some
+    layer of the oracle): the engine's router GEMV sums in another order and may pick
+    the other expert, which moves that token's hidden state by more than a few ulps.
+    Such rounds are counted and must stay rare."""
     from qwen35_dflash_b200.session import TargetSession
     cfg, raw, oracle = _tiny()
     eng = _engine(cfg, raw, capacity=2048)
@@ -128,7 +133,7 @@ def test_session_rounds_match_oracle(cuda_lib, golden):
     top1, feats, _, _ = oracle.forward(np.asarray([prompt]))
     assert sess.next_token == int(top1[0, -1])
     assert_close(to_np(sess.last_features[0]), feats[0, -1:], 2e-2, 1e-2, "prefill features", row_scale=True)
-    agree = total = same_acc = tie_acc = 0
+    agree = total = same_acc = tie_acc = route_flips = 0
     rng = np.random.default_rng(11)
     rounds = 48
     for r in range(rounds):
@@ -139,16 +144,24 @@ def test_session_rounds_match_oracle(cuda_lib, golden):
             props[j] = int((props[j] + 1 + rng.integers(0, cfg.vocab_size - 1)) % cfg.vocab_size)
         ostate = _oracle_state_from_engine(oracle, eng)
         v = sess.verify(props)
+        oracle.router_gaps = []
         o_top1, _, _, logits = oracle.forward(np.asarray([props]), ostate, return_logits=True)
+        gaps = np.min(np.stack(oracle.router_gaps), 0)     # per token, over the MoE layers
+        oracle.router_gaps = None
         exp = (next_token,) + tuple(int(t) for t in o_top1[0])
         ties = set()
+        flipped = False
         for i, (a, b) in enumerate(zip(v.expected_next_tokens, exp)):
             total += 1
             if a == b:
                 agree += 1
             else:
-                assert i > 0 and _near_tie(logits[0, i - 1], a, b), (r, i, a, b)
+                assert i > 0, (r, i, a, b)
+                if not _near_tie(logits[0, i - 1], a, b):
+                    assert gaps[:i].min() <= 2.0, (r, i, a, b, gaps[:i].min())
+                    flipped = True
                 ties.add(i)
+        route_flips += int(flipped)
         acc = 0
         for i, t in enumerate(props):
             if t != exp[i]:
@@ -164,6 +177,7 @@ def test_session_rounds_match_oracle(cuda_lib, golden):
         v.commit(got)
     assert agree >= 0.95 * total, (agree, total)
     assert same_acc + tie_acc == rounds and same_acc >= 0.75 * rounds, (same_acc, tie_acc, rounds)
+    assert route_flips <= 0.1 * rounds, (route_flips, rounds)
 
 
 def test_verification_semantics(cuda_lib):

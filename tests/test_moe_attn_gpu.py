@@ -60,6 +60,23 @@ def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k):
     sel = torch.gather(probs, 1, want.long())
     ref_w = (sel / sel.sum(-1, keepdim=True)).to(torch.bfloat16).float()
     assert_close(w.numpy(), ref_w.numpy(), 2 ** -8, 2 ** -7, "route weights")
+    # expert -> (token, slot) lists: active experts ascending, tokens ascending in each
+    ints = ws.view(torch.int32).cpu().numpy()
+    na_max = min(e, t * k)
+    o = 2 * t * k + t
+    n_active = int(ints[o])
+    active = ints[o + 4: o + 4 + na_max]
+    off = ints[o + 4 + na_max: o + 5 + 2 * na_max]
+    ptok = ints[o + 5 + 2 * na_max: o + 5 + 2 * na_max + t * k]
+    pslot = ints[o + 5 + 2 * na_max + t * k: o + 5 + 2 * na_max + 2 * t * k]
+    sel_np = want.numpy()
+    experts = sorted(set(sel_np.ravel().tolist()))
+    assert n_active == len(experts) and active[:n_active].tolist() == experts
+    assert off[0] == 0 and off[n_active] == t * k
+    for a, ex in enumerate(experts):
+        toks, slots = np.nonzero(sel_np == ex)
+        assert ptok[off[a]:off[a + 1]].tolist() == toks.tolist()
+        assert pslot[off[a]:off[a + 1]].tolist() == slots.tolist()
 
 
 class _LazyDequant:
