@@ -544,17 +544,19 @@ __global__ void __launch_bounds__(SG_WARPS * 32, 2) moe_down_kernel(MoeArgs<type
 
 // ------------------------------------------------------------------ bulk-copy expert kernels
 // Verify-block form (T <= 16 tokens) of the gate/up and down kernels: persistent CTAs
-// (one per SM) of XT_WARPS warps, each warp streaming its weight tiles from HBM through
+// (one per SM) of XT_UP_WARPS / XT_DN_WARPS warps, each warp streaming its weight tiles from HBM through
 // its own ring of shared-memory stages with bulk copies (bulk_ring.cuh).  The expert
 // inputs sit in shared memory, so the loop waits on nothing but the weight stream; the
 // arithmetic (and its order) is that of moe_up_kernel / moe_down_kernel, so the results
 // are the same bits.
-constexpr int XT_WARPS = 8;
+constexpr int XT_UP_WARPS = 8;   // gate/up: whole (gate, up) tile pairs per warp
+constexpr int XT_UP_CPS = 8;     // gate/up: W4 chunks per stage (at most)
+constexpr int XT_DN_WARPS = 16;  // down: row blocks shared by the CTA
+constexpr int XT_DN_CPS = 4;     // down: W4 chunks per stage (at most)
 constexpr int XT_NST = 2;        // stages per warp ring
 constexpr int XT_MAXT = 16;      // tokens of the block
-constexpr int XT_BAR_BYTES = (XT_WARPS * XT_NST * 8 + 127) / 128 * 128;
-constexpr int XT_PAD = 32;       // bf16 of row padding: 16-byte fragment loads hit distinct banks
-constexpr int XT_CPS = 8;        // W4 chunks per stage (at most)
+constexpr int XT_BAR_BYTES = (16 * XT_NST * 8 + 127) / 128 * 128;   // up to 16 warps
+constexpr int XT_PAD = 32;       // 16-bit elements of row padding: fragment loads hit distinct banks
 
 // Route lists of the block staged in shared memory.
 struct XtRoute {
@@ -595,53 +597,84 @@ __device__ __forceinline__ void xt_slot(const A& a, const XtRoute& r, int sl, bo
   np = r.off[ai + 1] - pbase;
 }
 
-// acc[nt] += W4 chunk (16 rows x G) . x rows (token of lane gid in n-tile nt at xr[nt]).
-template <int G>
-__device__ __forceinline__ void xt_chunk(const uint8_t* chunk, const __nv_bfloat16* const (&xr)[2], int k0,
-                                         int lane, bool two, float (&acc)[2][4]) {
+// acc[nt] += W4 chunks c0 .. c0+NC-1 (16 rows x G each, consecutive in shared memory)
+// . x rows (token of lane gid in n-tile nt at xr[nt]).  NC chunks are decoded and
+// multiplied interleaved (independent instruction streams for one warp) and their
+// scaled partial sums are added to acc in chunk order, as one chunk at a time would.
+// Both operands are fp16: the weights are small integers and the activations are bf16
+// values, exact in fp16 (|x| in [2^-14, 65504]), so the products equal the bf16 ones and
+// the decode needs no conversion-unit instructions (dequant_w4_word_f16).
+template <int G, int NC, int NT>
+__device__ __forceinline__ void xt_chunks(const uint8_t* chunk, const __half* const (&xr)[2], int k0,
+                                          int lane, float (&acc)[2][4]) {
   using Fmt = W4Fmt<G>;
-  uint32_t w[Fmt::WORDS];
+  uint32_t w[NC][Fmt::WORDS];
+  uint32_t sc[NC];
 #pragma unroll
-  for (int v = 0; v < Fmt::NV; ++v) {
-    const uint8_t* p = chunk + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
-    if constexpr (Fmt::VW == 4) {
-      const uint4 u = *reinterpret_cast<const uint4*>(p);
-      w[v * 4 + 0] = u.x; w[v * 4 + 1] = u.y; w[v * 4 + 2] = u.z; w[v * 4 + 3] = u.w;
-    } else {
-      const uint2 u = *reinterpret_cast<const uint2*>(p);
-      w[v * 2 + 0] = u.x; w[v * 2 + 1] = u.y;
-    }
-  }
-  const uint32_t sc = *reinterpret_cast<const uint32_t*>(chunk + 8 * G + (lane >> 2) * 4);
-  const int tig = lane & 3;
-  float part[2][4];
+  for (int c = 0; c < NC; ++c) {
 #pragma unroll
-  for (int j = 0; j < 2; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.f;
-#pragma unroll
-  for (int q = 0; q < G / 32; ++q) {
-    uint32_t b[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      if (j == 0 || two) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + 32 * q + 8 * tig);
-        b[j][0] = v.x; b[j][1] = v.y; b[j][2] = v.z; b[j][3] = v.w;
+    for (int v = 0; v < Fmt::NV; ++v) {
+      const uint8_t* p = chunk + c * Fmt::CHB + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
+      if constexpr (Fmt::VW == 4) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        w[c][v * 4 + 0] = u.x; w[c][v * 4 + 1] = u.y; w[c][v * 4 + 2] = u.z; w[c][v * 4 + 3] = u.w;
+      } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(p);
+        w[c][v * 2 + 0] = u.x; w[c][v * 2 + 1] = u.y;
       }
     }
+    sc[c] = *reinterpret_cast<const uint32_t*>(chunk + c * Fmt::CHB + 8 * G + (lane >> 2) * 4);
+  }
+  const int tig = lane & 3;
+  float part[NC][NT][4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t a[4];
-      dequant_w4_word(w[2 * q + h], a);
-      mma16816<__nv_bfloat16>(part[0], a, b[0][2 * h], b[0][2 * h + 1]);
-      if (two) mma16816<__nv_bfloat16>(part[1], a, b[1][2 * h], b[1][2 * h + 1]);
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) part[c][j][0] = part[c][j][1] = part[c][j][2] = part[c][j][3] = 0.f;
+#pragma unroll
+  for (int q = 0; q < G / 32; ++q) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      uint32_t b[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + c * G + 32 * q + 8 * tig);
+        b[j][0] = v.x; b[j][1] = v.y; b[j][2] = v.z; b[j][3] = v.w;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t a[4];
+        dequant_w4_word_f16(w[c][2 * q + h], a);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) mma16816<__half>(part[c][j], a, b[j][2 * h], b[j][2 * h + 1]);
+      }
     }
   }
-  const float2 s2 = bf162_to_f2(sc);
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    acc[j][0] = fmaf(part[j][0], s2.x, acc[j][0]);
-    acc[j][1] = fmaf(part[j][1], s2.x, acc[j][1]);
-    acc[j][2] = fmaf(part[j][2], s2.y, acc[j][2]);
-    acc[j][3] = fmaf(part[j][3], s2.y, acc[j][3]);
+  for (int c = 0; c < NC; ++c) {
+    const float2 s2 = bf162_to_f2(sc[c]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      acc[j][0] = fmaf(part[c][j][0], s2.x, acc[j][0]);
+      acc[j][1] = fmaf(part[c][j][1], s2.x, acc[j][1]);
+      acc[j][2] = fmaf(part[c][j][2], s2.y, acc[j][2]);
+      acc[j][3] = fmaf(part[c][j][3], s2.y, acc[j][3]);
+    }
+  }
+}
+
+// n consecutive chunks, two at a time; NT = 2 n-tiles only when the unit has > 8 tokens.
+template <int G>
+__device__ __forceinline__ void xt_run(const uint8_t* chunk, int n, const __half* const (&xr)[2], int k0, int lane,
+                                       bool two, float (&acc)[2][4]) {
+  constexpr int CHB = W4Fmt<G>::CHB;
+  int c = 0;
+  if (two) {
+    for (; c + 2 <= n; c += 2) xt_chunks<G, 2, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+    if (c < n) xt_chunks<G, 1, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+  } else {
+    for (; c + 2 <= n; c += 2) xt_chunks<G, 2, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+    if (c < n) xt_chunks<G, 1, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
   }
 }
 
@@ -652,10 +685,12 @@ struct XtArgs {
 };
 
 // Gate/up.  Unit = (slot, intermediate tile j): the gate row tile j then the up row tile
-// I/16 + j, each cut into stages of up to XT_CPS chunks; unit u goes to warp u mod (all
-// warps).  x [T, H] is staged once per CTA.
+// I/16 + j, each cut into stages of up to XT_UP_CPS chunks; unit u goes to warp u mod (all
+// warps).  x [T, H] is staged once per CTA.  (Splitting a unit's K range over two warps
+// was measured no faster, and would change the fp32 summation order against the
+// streaming kernels that serve larger blocks.)
 template <int G>
-__global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs args) {
+__global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs args) {
   using Fmt = W4Fmt<G>;
   const MoeArgs<__nv_bfloat16>& a = args.m;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -663,9 +698,9 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs ar
   XtRoute& rt = *reinterpret_cast<XtRoute*>(smem + XT_BAR_BYTES);
   const int H = a.H, I = a.I, T = a.T;
   const int XS = H + XT_PAD;
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
+  __half* xs = reinterpret_cast<__half*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(xs) + ((static_cast<size_t>(T) * XS * 2 + 127) / 128) * 128;
-  const int nch = H / G, cps = nch < XT_CPS ? nch : XT_CPS, spt = nch / cps;
+  const int nch = H / G, cps = nch < XT_UP_CPS ? nch : XT_UP_CPS, spt = nch / cps;
   const uint32_t sbytes = cps * Fmt::CHB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
@@ -684,7 +719,7 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs ar
   const int J = I / 16;
   const int nslots = a.has_shared + rt.n_active;
   const int nu = nslots * J;
-  const int gw = blockIdx.x * XT_WARPS + warp, nw = gridDim.x * XT_WARPS;
+  const int gw = blockIdx.x * XT_UP_WARPS + warp, nw = gridDim.x * XT_UP_WARPS;
   const int my_units = gw < nu ? (nu - 1 - gw) / nw + 1 : 0;
   const int Q = my_units * 2 * spt;
   auto src = [&](int q) -> const uint8_t* {
@@ -698,6 +733,11 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs ar
   if (lane == 0)
     for (int q = 0; q < XT_NST && q < Q; ++q) ring.issue(q, src(q), sbytes);
   cp_async_wait<0>();
+  // x: bf16 -> fp16 in place (each thread converts the vectors it copied)
+  for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
+    uint4* p = reinterpret_cast<uint4*>(xs + (i / (H / 8)) * XS + (i % (H / 8)) * 8);
+    *p = bf16x8_to_f16x8(*p);
+  }
   __syncthreads();
   const int gid = lane >> 2;
   int q = 0;
@@ -707,7 +747,7 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs ar
     int np, pb;
     xt_slot(a, rt, u / J, true, w, np, pb);
     const bool two = np > 8;
-    const __nv_bfloat16* xr[2];
+    const __half* xr[2];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const int idx = min(nt * 8 + gid, np - 1);
@@ -725,8 +765,7 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs ar
           if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
           return;
         }
-        const uint8_t* st = ring.stage(q);
-        for (int c = 0; c < cps; ++c) xt_chunk<G>(st + c * Fmt::CHB, xr, (sub * cps + c) * G, lane, two, acc[g]);
+        xt_run<G>(ring.stage(q), cps, xr, sub * cps * G, lane, two, acc[g]);
         __syncwarp();
         if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
       }
@@ -741,17 +780,18 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs ar
           const float gr = rbf(acc[0][nt][r]), ur = rbf(acc[1][nt][r]);
           const float h = rbf(rbf(silu_f(gr)) * ur);
           const int64_t hrow = pb < 0 ? static_cast<int64_t>(T) * a.k + tl : pb + tl;
-          a.hbuf[hrow * I + j * 16 + frag_row(lane, r)] = __float2bfloat16_rn(h);
+          // h is a bf16 value; stored as fp16 (exact) for the bulk down kernel's operand
+          reinterpret_cast<__half*>(a.hbuf)[hrow * I + j * 16 + frag_row(lane, r)] = __float2half_rn(h);
         }
       }
   }
 }
 
-// Down.  Unit = (slot, block of XT_WARPS * spw row tiles); the CTA's warps share the
+// Down.  Unit = (slot, block of XT_DN_WARPS * spw row tiles); the CTA's warps share the
 // unit, each streaming spw... stages of tiles; the unit's rows of h are staged in shared
 // memory (double-buffered across units).  Units go to CTAs round-robin.
 template <int G>
-__global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs args, int tiles_per_stage,
+__global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs args, int tiles_per_stage,
                                                                          int stages_per_warp) {
   using Fmt = W4Fmt<G>;
   const MoeArgs<__nv_bfloat16>& a = args.m;
@@ -760,13 +800,13 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs 
   XtRoute& rt = *reinterpret_cast<XtRoute*>(smem + XT_BAR_BYTES);
   const int H = a.H, I = a.I, T = a.T;
   const int HS = I + XT_PAD;
-  __nv_bfloat16* hs = reinterpret_cast<__nv_bfloat16*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
+  __half* hs = reinterpret_cast<__half*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
   const size_t hbytes = ((static_cast<size_t>(XT_MAXT) * HS * 2 + 127) / 128) * 128;
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(hs) + 2 * hbytes;
   const int cpt = I / G;                         // chunks per row tile
   const int tps = tiles_per_stage, spw = stages_per_warp;
   const uint32_t sbytes = tps * cpt * Fmt::CHB;
-  const int rb_tiles = XT_WARPS * spw * tps;     // row tiles per unit
+  const int rb_tiles = XT_DN_WARPS * spw * tps;     // row tiles per unit
   const int nrb = (H / 16) / rb_tiles;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
@@ -797,10 +837,11 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs 
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
     const int64_t hb = pb < 0 ? static_cast<int64_t>(T) * a.k : pb;
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(hs) + (i & 1) * hbytes);
+    __half* dst = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(hs) + (i & 1) * hbytes);
+    const __half* hsrc = reinterpret_cast<const __half*>(a.hbuf);
     for (int e = threadIdx.x; e < np * (I / 8); e += blockDim.x) {
       const int r = e / (I / 8), c = (e % (I / 8)) * 8;
-      cp_async16(dst + r * HS + c, a.hbuf + (hb + r) * I + c, true);
+      cp_async16(dst + r * HS + c, hsrc + (hb + r) * I + c, true);
     }
   };
   if (my_units > 0) stage_h(0);
@@ -818,9 +859,8 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs 
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
     const bool two = np > 8;
-    const __nv_bfloat16* hbuf_s =
-        reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<const uint8_t*>(hs) + (i & 1) * hbytes);
-    const __nv_bfloat16* xr[2];
+    const __half* hbuf_s = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(hs) + (i & 1) * hbytes);
+    const __half* xr[2];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) xr[nt] = hbuf_s + min(nt * 8 + gid, np - 1) * HS;
     for (int l = 0; l < spw && ok; ++l, ++q) {
@@ -834,7 +874,7 @@ __global__ void __launch_bounds__(XT_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs 
         float acc[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-        for (int c = 0; c < cpt; ++c) xt_chunk<G>(st + (t * cpt + c) * Fmt::CHB, xr, c * G, lane, two, acc);
+        xt_run<G>(st + t * cpt * Fmt::CHB, cpt, xr, 0, lane, two, acc);
         const int row0 = ((u % nrb) * rb_tiles + (warp * spw + l) * tps + t) * 16;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
@@ -1067,20 +1107,20 @@ static XtPlan xt_plan(const MoeArgs<__nv_bfloat16>& a) {
   const bool small = a.T <= XT_MAXT && static_cast<int64_t>(a.T) * a.k <= XT_MAXT * 16 && a.H % 8 == 0 &&
                      (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.hbuf) & 15) == 0;
   const int nch = a.H / G;
-  const int cps = nch < XT_CPS ? nch : XT_CPS;
+  const int cps = nch < XT_UP_CPS ? nch : XT_UP_CPS;
   p.up_smem = xt_route_bytes() + (static_cast<size_t>(a.T) * (a.H + XT_PAD) * 2 + 127) / 128 * 128 +
-              static_cast<size_t>(XT_WARPS) * XT_NST * cps * CHB;
+              static_cast<size_t>(XT_UP_WARPS) * XT_NST * cps * CHB;
   p.up_ok = small && nch % cps == 0 && p.up_smem <= XT_SMEM_LIMIT;
   const int cpt = a.I / G;
   p.down_ok = false;
-  if (small && cpt >= 1 && cpt <= XT_CPS && XT_CPS % cpt == 0) {
-    p.down_tps = XT_CPS / cpt;
+  if (small && cpt >= 1 && cpt <= XT_DN_CPS && XT_DN_CPS % cpt == 0) {
+    p.down_tps = XT_DN_CPS / cpt;
     const int tiles = a.H / 16;
     p.down_spw = 0;
     for (int spw = 2; spw >= 1; --spw)
-      if (tiles % (XT_WARPS * spw * p.down_tps) == 0) { p.down_spw = spw; break; }
+      if (tiles % (XT_DN_WARPS * spw * p.down_tps) == 0) { p.down_spw = spw; break; }
     p.down_smem = xt_route_bytes() + 2 * ((static_cast<size_t>(XT_MAXT) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
-                  static_cast<size_t>(XT_WARPS) * XT_NST * p.down_tps * cpt * CHB;
+                  static_cast<size_t>(XT_DN_WARPS) * XT_NST * p.down_tps * cpt * CHB;
     p.down_ok = p.down_spw > 0 && p.down_smem <= XT_SMEM_LIMIT;
   }
   return p;
@@ -1102,11 +1142,11 @@ static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p,
   XtArgs xa{a, status, QW_WAIT_LIMIT};
   const int grid = sm_count();
   if (up) {
-    moe_up_bulk_kernel<G><<<grid, XT_WARPS * 32, p.up_smem, s>>>(xa);
+    moe_up_bulk_kernel<G><<<grid, XT_UP_WARPS * 32, p.up_smem, s>>>(xa);
     QW_LAUNCH_CHECK("moe up (bulk)");
   }
   if (down) {
-    moe_down_bulk_kernel<G><<<grid, XT_WARPS * 32, p.down_smem, s>>>(xa, p.down_tps, p.down_spw);
+    moe_down_bulk_kernel<G><<<grid, XT_DN_WARPS * 32, p.down_smem, s>>>(xa, p.down_tps, p.down_spw);
     QW_LAUNCH_CHECK("moe down (bulk)");
   }
   return QW_OK;
@@ -1117,17 +1157,10 @@ static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bo
   const XtPlan p = xt_plan<G>(a);
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   int32_t* status = rv.n_active + 1;
-  if (up) {
-    const int rc = p.up_ok ? launch_experts_bulk<G>(a, p, s, true, false, status)
-                           : launch_experts<W4Fmt<G>, 4>(a, s, true, false);
-    if (rc != QW_OK) return rc;
-  }
-  if (down) {
-    const int rc = p.down_ok ? launch_experts_bulk<G>(a, p, s, false, true, status)
-                             : launch_experts<W4Fmt<G>, 4>(a, s, false, true);
-    if (rc != QW_OK) return rc;
-  }
-  return QW_OK;
+  // the bulk pair keeps h (the down input) in fp16, the streaming pair in bf16: both
+  // halves of one MoE always come from the same pair
+  if (p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);
+  return launch_experts<W4Fmt<G>, 4>(a, s, up, down);
 }
 
 }  // namespace qw

@@ -182,6 +182,39 @@ __device__ __forceinline__ void dequant_w4_word(uint32_t w, uint32_t (&a)[4]) {
   }
 }
 
+// The same word decoded to fp16 A fragments with no conversion-unit work: masking
+// nibbles into the mantissa of fp16 1024.0 (0x6400) gives 1024 + u (nibbles 0, 2 of
+// each half) or 1024 + 16u (nibbles 1, 3, left in place), then one HADD2 / HFMA2
+// leaves q exactly.  Register j again holds nibbles (j, j + 4).
+__device__ __forceinline__ void dequant_w4_word_f16(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u, EXP = 0x64006400u;
+  const uint32_t w8 = w >> 8;
+  uint32_t r[4] = {lop3_and_or(w, LO, EXP), lop3_and_or(w, HI, EXP), lop3_and_or(w8, LO, EXP),
+                   lop3_and_or(w8, HI, EXP)};
+  const __half2 sub_lo = __halves2half2(__ushort_as_half(0xE408u), __ushort_as_half(0xE408u));   // -1032
+  const __half2 mul_hi = __halves2half2(__ushort_as_half(0x2C00u), __ushort_as_half(0x2C00u));   // 1/16
+  const __half2 sub_hi = __halves2half2(__ushort_as_half(0xD480u), __ushort_as_half(0xD480u));   // -72
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 v = *reinterpret_cast<__half2*>(&r[j]);
+    v = (j & 1) ? __hfma2(v, mul_hi, sub_hi) : __hadd2(v, sub_lo);
+    a[j] = *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// bf16 -> fp16 of 8 packed values (exact for |x| in [2^-14, 65504]; saturates beyond).
+__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 u) {
+  uint32_t in[4] = {u.x, u.y, u.z, u.w}, out[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = fminf(fmaxf(__uint_as_float(in[i] << 16), -65504.f), 65504.f);
+    const float hi = fminf(fmaxf(__uint_as_float(in[i] & 0xFFFF0000u), -65504.f), 65504.f);
+    const __half2 h = __floats2half2_rn(lo, hi);
+    out[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 __device__ __forceinline__ float2 bf162_to_f2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);
