@@ -180,11 +180,17 @@ int qw_b16_linear(const void* x, const void* w_stream, void* y, int mode, int64_
 
 /* Routing from router logits [T, ldl] (logit_dtype): fp32 softmax over the first
  * `experts` columns, torch.topk CPU order, renormalized weights cast to act_dtype;
- * column `shared_col` (or -1) holds the shared-expert gate logit.  Builds the
- * per-expert (token, slot) lists in the workspace. */
+ * column `shared_col` (or -1) holds the shared-expert gate logit.  Writes the top-k
+ * indices and weights into the workspace; the per-expert (token, slot) lists are
+ * built by the expert entry points (or qw_moe_route_lists). */
 int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens,
                  int64_t experts, int64_t top_k, int64_t shared_col, int act_dtype,
                  void* workspace, void* stream);
+
+/* The per-expert lists of a routed block in the workspace: active experts in
+ * ascending id, and for each its (token, slot) pairs in ascending token (the order in
+ * which fused_ops.py:165-172 visits them). */
+int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t experts, int64_t top_k, void* stream);
 
 /* Expert FFNs on the routing in `workspace`: x bf16 [T,H]; gate_up / down are W4
  * streams of [E][2I,H] / [E][H,I] (experts concatenated); the shared expert's
@@ -205,7 +211,8 @@ int qw_moe_down_w4(const void* x, const void* gate_up, const void* down, const v
                    int64_t inter, int64_t top_k, int32_t group, void* workspace, void* stream);
 
 /* Byte offset, inside a MoE workspace, of the int32 count of active routed experts
- * written by qw_moe_route (for measuring the experts actually streamed). */
+ * (valid after qw_moe_route_lists or an expert entry point; for measuring the experts
+ * actually streamed). */
 int32_t qw_moe_active_experts(const void* workspace, int64_t tokens, int64_t experts, int64_t top_k);
 
 /* Weighted combine in ascending expert order (+ gated shared expert): out bf16 [T,H]

@@ -124,9 +124,11 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
   }
 }
 
+// Row tiles per CTA (the K split is SG_WARPS / rt): the largest count that still leaves
+// >= 2 waves of CTAs.  The partition (and so the fp32 summation order) depends on the
+// weight shape only, never on the token count, so a token's output has the same bits
+// whichever block size computes it.
 static int choose_rt(int ntiles) {
-  // largest row-tile count per CTA that still leaves >= 2 waves of CTAs; K splits
-  // across the remaining warps
   for (int rt : {8, 4, 2}) {
     if ((ntiles + rt - 1) / rt >= 296) return rt;
   }
@@ -136,7 +138,7 @@ static int choose_rt(int ntiles) {
 template <class Fmt, int NT, int PF, bool ARGMAX = false>
 static int launch_linear(const LinArgs& a0, cudaStream_t s) {
   LinArgs a = a0;
-  a.rt = choose_rt(a.n / 16);
+  if (a.rt <= 0) a.rt = choose_rt(a.n / 16);
   const size_t smem = SG_WARPS * NT * 4 * 32 * 4 + (ARGMAX ? SG_WARPS * NT * 8 * 8 : 0);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -195,7 +197,7 @@ extern "C" int qw_w4_linear(const void* x, const void* w_stream, void* y, int mo
   QW_CHECK_ARG(k % group == 0, "w4_linear: K %% group != 0");
   if (tokens == 0) return QW_OK;
   LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), y, ldy,
-            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, mode};
+            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 0, mode};
   cudaStream_t s = as_stream(stream);
   switch (group) {
     case 128: return dispatch_nt<W4Fmt<128>, 4>(a, s);
@@ -211,14 +213,17 @@ extern "C" int qw_b16_linear(const void* x, const void* w_stream, void* y, int m
   QW_CHECK_ARG(k % 64 == 0, "b16_linear: K must be a multiple of 64");
   if (tokens == 0) return QW_OK;
   LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), y, ldy,
-            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, mode};
+            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 0, mode};
   return dispatch_nt<B16Fmt, 4>(a, as_stream(stream));
 }
 
+// The lm_head streams 8 row tiles per CTA (each warp a whole tile, all of K): fewer
+// argmax partials per token for the accept reduction.
+constexpr int LMHEAD_RT = 8;
+
 extern "C" int64_t qw_lmhead_blocks(int64_t n) {
   if (n <= 0 || n % 16) return -1;
-  const int rt = choose_rt(static_cast<int>(n / 16));
-  return (n / 16 + rt - 1) / rt;
+  return (n / 16 + LMHEAD_RT - 1) / LMHEAD_RT;
 }
 
 extern "C" int qw_lmhead_argmax(const void* x, const void* w_stream, void* logits, void* keys, int64_t tokens,
@@ -228,7 +233,7 @@ extern "C" int qw_lmhead_argmax(const void* x, const void* w_stream, void* logit
   QW_CHECK_ARG(k % 64 == 0, "lmhead: K must be a multiple of 64");
   if (tokens == 0) return QW_OK;
   LinArgs a{static_cast<const __nv_bfloat16*>(x), static_cast<const uint8_t*>(w_stream), logits, n,
-            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 1, QW_OUT_BF16,
+            static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), LMHEAD_RT, QW_OUT_BF16,
             static_cast<unsigned long long*>(keys)};
   return launch_linear<B16Fmt, 2, 4, true>(a, as_stream(stream));
 }

@@ -240,121 +240,121 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
   __syncwarp();
 }
 
-// ------------------------------------------------------------------ route kernel
-// One CTA; warp w handles tokens w, w + nwarps, ...
+// ------------------------------------------------------------------ route kernels
+// route_topk_kernel: one warp (CTA) per token.
 //
 // Selection.  When the k+1 largest logits of a row are strictly ordered
 // (v0 > v1 > ... > v_{k-1} > v_k), every correct top-k returns the same indices in the
 // same (descending) order, torch.topk's included, so the warp extracts them directly
 // from registers (k+1 rounds of a warp arg-max).  A row with any tie among them (or
 // more than 256 experts) runs the libstdc++ emulation above, which reproduces the order
-// torch.topk gives tied values.  Dynamic smem per warp (emulation rows):
-// E floats + E ints + 2 * (E + 2) int16.
+// torch.topk gives tied values.  Dynamic smem (emulation rows): E floats + E ints +
+// 2 * (E + 2) int16.
 constexpr int ROUTE_MAXJ = 8;  // logits per lane on the fast path (E <= 256)
 
 template <typename LT>
-__global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logits, int64_t ldl, int T,
-                                                     int E, int k, int shared_col, int act_is_f16,
-                                                     void* ws) {
+__global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ logits, int64_t ldl, int T, int E,
+                                                       int k, int shared_col, int act_is_f16, void* ws) {
   extern __shared__ __align__(16) uint8_t smem[];
   RouteView rv = route_view(ws, T, E, k);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const int per_warp = E * 8 + 2 * (E + 2) * 2;
-  uint8_t* base = smem + warp * ((per_warp + 15) / 16 * 16);
-  Q q{reinterpret_cast<float*>(base), reinterpret_cast<int32_t*>(base + E * 4)};
-  int16_t* pos_l = reinterpret_cast<int16_t*>(base + E * 8);
+  const int lane = threadIdx.x;
+  Q q{reinterpret_cast<float*>(smem), reinterpret_cast<int32_t*>(smem + E * 4)};
+  int16_t* pos_l = reinterpret_cast<int16_t*>(smem + E * 8);
   int16_t* pos_r = pos_l + E + 2;
-  for (int t = warp; t < T; t += nw) {
-    const LT* row = logits + static_cast<int64_t>(t) * ldl;
-    float sel_v = -INFINITY;   // lane r < k: value of the r-th selected expert
-    int sel_i = 0;             //             and its index
-    float mx, z;
-    bool exact = E > 32 * ROUTE_MAXJ;
-    if (!exact) {
-      float v[ROUTE_MAXJ];
-      mx = -INFINITY;
+  const int t = blockIdx.x;
+  const LT* row = logits + static_cast<int64_t>(t) * ldl;
+  float sel_v = -INFINITY;   // lane r < k: value of the r-th selected expert
+  int sel_i = 0;             //             and its index
+  float mx, z;
+  bool exact = E > 32 * ROUTE_MAXJ;
+  if (!exact) {
+    float v[ROUTE_MAXJ];
+    mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < ROUTE_MAXJ; ++j) {
+      const int e = lane + 32 * j;
+      v[j] = e < E ? to_f(row[e]) : -INFINITY;
+      mx = fmaxf(mx, v[j]);
+    }
+    mx = warp_max(mx);
+    z = 0.f;
+#pragma unroll
+    for (int j = 0; j < ROUTE_MAXJ; ++j)
+      if (lane + 32 * j < E) z += __expf(v[j] - mx);
+    z = warp_sum(z);
+    unsigned taken = 0u;
+    float prev = 0.f;
+    const int rounds = k < E ? k + 1 : k;
+    for (int r = 0; r < rounds; ++r) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
 #pragma unroll
       for (int j = 0; j < ROUTE_MAXJ; ++j) {
         const int e = lane + 32 * j;
-        v[j] = e < E ? to_f(row[e]) : -INFINITY;
-        mx = fmaxf(mx, v[j]);
+        if (e < E && !(taken >> j & 1u) && (bv < v[j] || bi == 0x7fffffff)) { bv = v[j]; bi = e; }
       }
-      mx = warp_max(mx);
-      z = 0.f;
 #pragma unroll
-      for (int j = 0; j < ROUTE_MAXJ; ++j)
-        if (lane + 32 * j < E) z += __expf(v[j] - mx);
-      z = warp_sum(z);
-      unsigned taken = 0u;
-      float prev = 0.f;
-      const int rounds = k < E ? k + 1 : k;
-      for (int r = 0; r < rounds; ++r) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < ROUTE_MAXJ; ++j) {
-          const int e = lane + 32 * j;
-          if (e < E && !(taken >> j & 1u) && (bv < v[j] || bi == 0x7fffffff)) { bv = v[j]; bi = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
-        }
-        // a tie (or a NaN) anywhere among the k+1 largest: use the exact emulation
-        if (r > 0 && !(prev > bv)) { exact = true; break; }
-        prev = bv;
-        if (r < k && lane == r) { sel_v = bv; sel_i = bi; }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
       }
+      // a tie (or a NaN) anywhere among the k+1 largest: use the exact emulation
+      if (r > 0 && !(prev > bv)) { exact = true; break; }
+      prev = bv;
+      if (r < k && lane == r) { sel_v = bv; sel_i = bi; }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
     }
-    if (exact) {
-      mx = -INFINITY;
-      for (int e = lane; e < E; e += 32) {
-        const float v = to_f(row[e]);
-        q.v[e] = v;
-        q.i[e] = e;
-        mx = fmaxf(mx, v);
-      }
-      mx = warp_max(mx);
-      z = 0.f;
-      for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
-      z = warp_sum(z);
-      __syncwarp();
-      warp_topk(q, E, k, pos_l, pos_r, lane);
-      if (lane < k) { sel_v = q.v[lane]; sel_i = q.i[lane]; }
-    }
-    // renormalized weights of the selected (fused_ops.py:162-164)
-    float p = 0.f;
-    if (lane < k) p = __expf(sel_v - mx) / z;
-    float ps = p;
-    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-    if (lane < k) {
-      const float w = p / ps;
-      rv.topk_idx[t * k + lane] = sel_i;
-      rv.topk_w[t * k + lane] = act_is_f16 ? rnd<__half>(w) : rbf(w);
-    }
-    if (lane == 0) {
-      float sg = 0.f;
-      if (shared_col >= 0) {
-        const float gl = to_f(row[shared_col]);
-        sg = act_is_f16 ? rnd<__half>(sigmoid_f(gl)) : rbf(sigmoid_f(gl));
-      }
-      rv.shared_gate[t] = sg;
-    }
-    __syncwarp();
   }
-  __syncthreads();
-  // expert -> pair lists (ascending expert, then ascending token)
-  const int nthr = blockDim.x;
-  int* cnt = reinterpret_cast<int*>(smem);       // reuse: [E] counts
-  int* apos = cnt + E;                           // [E] next free position of each expert's list
-  unsigned* bits = reinterpret_cast<unsigned*>(apos + E);  // [E] token bits of one 32-token chunk
-  int* red = reinterpret_cast<int*>(bits + E);   // [64] scan partials
+  if (exact) {
+    mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) {
+      const float v = to_f(row[e]);
+      q.v[e] = v;
+      q.i[e] = e;
+      mx = fmaxf(mx, v);
+    }
+    mx = warp_max(mx);
+    z = 0.f;
+    for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
+    z = warp_sum(z);
+    __syncwarp();
+    warp_topk(q, E, k, pos_l, pos_r, lane);
+    if (lane < k) { sel_v = q.v[lane]; sel_i = q.i[lane]; }
+  }
+  // renormalized weights of the selected (fused_ops.py:162-164)
+  float p = 0.f;
+  if (lane < k) p = __expf(sel_v - mx) / z;
+  float ps = p;
+  for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+  if (lane < k) {
+    const float w = p / ps;
+    rv.topk_idx[t * k + lane] = sel_i;
+    rv.topk_w[t * k + lane] = act_is_f16 ? rnd<__half>(w) : rbf(w);
+  }
+  if (lane == 0) {
+    float sg = 0.f;
+    if (shared_col >= 0) {
+      const float gl = to_f(row[shared_col]);
+      sg = act_is_f16 ? rnd<__half>(sigmoid_f(gl)) : rbf(sigmoid_f(gl));
+    }
+    rv.shared_gate[t] = sg;
+  }
+}
+
+// Expert -> (token, slot) lists of a block from its top-k indices idx[T * k]: the
+// active experts in ascending id with their pair ranges (off), and in each range the
+// pairs in ascending token.  Called by every thread of a CTA; scratch holds 3E ints,
+// red 64 ints.  Outputs may live in shared or global memory.
+__device__ void build_route_lists(const int* idx, int T, int E, int k, int* scratch, int* red, int* n_active,
+                                  int* active, int* off, int* tok, int* slot) {
+  const int nthr = blockDim.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int* cnt = scratch;                                  // [E] pairs per expert
+  int* apos = scratch + E;                             // [E] next free position of each list
+  unsigned* bits = reinterpret_cast<unsigned*>(scratch + 2 * E);   // [E] token bits of one 32-token chunk
   for (int e = threadIdx.x; e < E; e += nthr) cnt[e] = 0;
   __syncthreads();
-  for (int pidx = threadIdx.x; pidx < T * k; pidx += nthr) atomicAdd(&cnt[rv.topk_idx[pidx]], 1);
+  for (int i = threadIdx.x; i < T * k; i += nthr) atomicAdd(&cnt[idx[i]], 1);
   __syncthreads();
   // exclusive scans of (active flag, count) over experts: thread i owns a contiguous run
   const int per = (E + nthr - 1) / nthr;
@@ -371,19 +371,19 @@ __global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logi
   __syncthreads();
   int wa = 0, wc = 0;
   for (int w = 0; w < warp; ++w) { wa += red[w]; wc += red[32 + w]; }
-  int na = wa + inc_a - my_a, off = wc + inc_c - my_c;
+  int na = wa + inc_a - my_a, o = wc + inc_c - my_c;
   for (int e = e0; e < e1; ++e) {
     if (cnt[e]) {
-      rv.active[na] = e;
-      rv.pair_off[na] = off;
-      apos[e] = off;
-      off += cnt[e];
+      active[na] = e;
+      off[na] = o;
+      apos[e] = o;
+      o += cnt[e];
       ++na;
     }
   }
   if (threadIdx.x == nthr - 1) {
-    rv.pair_off[na] = off;
-    *rv.n_active = na;
+    off[na] = o;
+    *n_active = na;
   }
   __syncthreads();
   // ranks within each expert's list, 32 tokens at a time
@@ -391,20 +391,28 @@ __global__ void __launch_bounds__(1024) route_kernel(const LT* __restrict__ logi
     const int tn = min(32, T - t0);
     for (int e = threadIdx.x; e < E; e += nthr) bits[e] = 0u;
     __syncthreads();
-    for (int pidx = threadIdx.x; pidx < tn * k; pidx += nthr)
-      atomicOr(&bits[rv.topk_idx[t0 * k + pidx]], 1u << (pidx / k));
+    for (int i = threadIdx.x; i < tn * k; i += nthr) atomicOr(&bits[idx[t0 * k + i]], 1u << (i / k));
     __syncthreads();
-    for (int pidx = threadIdx.x; pidx < tn * k; pidx += nthr) {
-      const int tl = pidx / k, s = pidx % k;
-      const int e = rv.topk_idx[t0 * k + pidx];
+    for (int i = threadIdx.x; i < tn * k; i += nthr) {
+      const int tl = i / k, s = i % k;
+      const int e = idx[t0 * k + i];
       const int at = apos[e] + __popc(bits[e] & ((1u << tl) - 1u));
-      rv.pair_tok[at] = t0 + tl;
-      rv.pair_slot[at] = s;
+      tok[at] = t0 + tl;
+      slot[at] = s;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += nthr) apos[e] += __popc(bits[e]);
     __syncthreads();
   }
+}
+
+// Lists of the routing workspace (one CTA).  Dynamic smem: 3E + 64 ints.
+__global__ void __launch_bounds__(1024) route_lists_kernel(int T, int E, int k, void* ws) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  RouteView rv = route_view(ws, T, E, k);
+  int* scratch = reinterpret_cast<int*>(smem);
+  build_route_lists(rv.topk_idx, T, E, k, scratch, scratch + 3 * E, rv.n_active, rv.active, rv.pair_off,
+                    rv.pair_tok, rv.pair_slot);
 }
 
 // ------------------------------------------------------------------ expert kernels
@@ -558,26 +566,41 @@ constexpr int XT_MAXT = 16;      // tokens of the block
 constexpr int XT_BAR_BYTES = (16 * XT_NST * 8 + 127) / 128 * 128;   // up to 16 warps
 constexpr int XT_PAD = 32;       // 16-bit elements of row padding: fragment loads hit distinct banks
 
-// Route lists of the block staged in shared memory.
+// Route lists of the block, built in shared memory from the top-k indices.
 struct XtRoute {
   int n_active;
+  int idx[XT_MAXT * 16];
   int active[XT_MAXT * 16];
   int off[XT_MAXT * 16 + 1];
   int tok[XT_MAXT * 16];
   int slot[XT_MAXT * 16];
 };
 
-__device__ __forceinline__ void xt_load_route(XtRoute& r, const RouteView& rv, int T, int k) {
+// Every thread of the CTA: the block's lists into r (scratch: 3E + 64 ints of shared
+// memory).  With publish, the lists are also written to the routing workspace (for the
+// host and for kernels that read the workspace lists).
+__device__ __forceinline__ void xt_build_route(XtRoute& r, int* scratch, const RouteView& rv, int T, int E, int k,
+                                               bool publish) {
   const int np = T * k;
-  if (threadIdx.x == 0) {
-    const int cap = min(np, XT_MAXT * 16);
-    r.n_active = max(0, min(*rv.n_active, cap));
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int e = rv.topk_idx[i];
+    r.idx[i] = (e >= 0 && e < E) ? e : 0;   // the route kernel writes valid ids; stay in bounds regardless
   }
   __syncthreads();
-  const int na = r.n_active;
-  for (int i = threadIdx.x; i < na; i += blockDim.x) r.active[i] = rv.active[i];
-  for (int i = threadIdx.x; i <= na; i += blockDim.x) r.off[i] = rv.pair_off[i];
-  for (int i = threadIdx.x; i < np; i += blockDim.x) { r.tok[i] = rv.pair_tok[i]; r.slot[i] = rv.pair_slot[i]; }
+  build_route_lists(r.idx, T, E, k, scratch, scratch + 3 * E, &r.n_active, r.active, r.off, r.tok, r.slot);
+  if (publish) {
+    const int na = r.n_active;
+    if (threadIdx.x == 0) *rv.n_active = na;
+    for (int i = threadIdx.x; i < na; i += blockDim.x) rv.active[i] = r.active[i];
+    for (int i = threadIdx.x; i <= na; i += blockDim.x) rv.pair_off[i] = r.off[i];
+    for (int i = threadIdx.x; i < np; i += blockDim.x) { rv.pair_tok[i] = r.tok[i]; rv.pair_slot[i] = r.slot[i]; }
+  }
+}
+
+// Bytes of shared memory ahead of a bulk kernel's operand buffers: barriers, lists and
+// the list-building scratch.
+__host__ __device__ inline size_t xt_head_bytes(int E) {
+  return XT_BAR_BYTES + (sizeof(XtRoute) + 127) / 128 * 128 + ((3 * static_cast<size_t>(E) + 64) * 4 + 127) / 128 * 128;
 }
 
 // Slot sl of the block: 0 the shared expert (when present), then the active experts.
@@ -595,87 +618,6 @@ __device__ __forceinline__ void xt_slot(const A& a, const XtRoute& r, int sl, bo
   w = up ? a.gu + e * a.gu_stride : a.dn + e * a.dn_stride;
   pbase = r.off[ai];
   np = r.off[ai + 1] - pbase;
-}
-
-// acc[nt] += W4 chunks c0 .. c0+NC-1 (16 rows x G each, consecutive in shared memory)
-// . x rows (token of lane gid in n-tile nt at xr[nt]).  NC chunks are decoded and
-// multiplied interleaved (independent instruction streams for one warp) and their
-// scaled partial sums are added to acc in chunk order, as one chunk at a time would.
-// Both operands are fp16: the weights are small integers and the activations are bf16
-// values, exact in fp16 (|x| in [2^-14, 65504]), so the products equal the bf16 ones and
-// the decode needs no conversion-unit instructions (dequant_w4_word_f16).
-template <int G, int NC, int NT>
-__device__ __forceinline__ void xt_chunks(const uint8_t* chunk, const __half* const (&xr)[2], int k0,
-                                          int lane, float (&acc)[2][4]) {
-  using Fmt = W4Fmt<G>;
-  uint32_t w[NC][Fmt::WORDS];
-  uint32_t sc[NC];
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-#pragma unroll
-    for (int v = 0; v < Fmt::NV; ++v) {
-      const uint8_t* p = chunk + c * Fmt::CHB + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
-      if constexpr (Fmt::VW == 4) {
-        const uint4 u = *reinterpret_cast<const uint4*>(p);
-        w[c][v * 4 + 0] = u.x; w[c][v * 4 + 1] = u.y; w[c][v * 4 + 2] = u.z; w[c][v * 4 + 3] = u.w;
-      } else {
-        const uint2 u = *reinterpret_cast<const uint2*>(p);
-        w[c][v * 2 + 0] = u.x; w[c][v * 2 + 1] = u.y;
-      }
-    }
-    sc[c] = *reinterpret_cast<const uint32_t*>(chunk + c * Fmt::CHB + 8 * G + (lane >> 2) * 4);
-  }
-  const int tig = lane & 3;
-  float part[NC][NT][4];
-#pragma unroll
-  for (int c = 0; c < NC; ++c)
-#pragma unroll
-    for (int j = 0; j < NT; ++j) part[c][j][0] = part[c][j][1] = part[c][j][2] = part[c][j][3] = 0.f;
-#pragma unroll
-  for (int q = 0; q < G / 32; ++q) {
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      uint32_t b[NT][4];
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + c * G + 32 * q + 8 * tig);
-        b[j][0] = v.x; b[j][1] = v.y; b[j][2] = v.z; b[j][3] = v.w;
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t a[4];
-        dequant_w4_word_f16(w[c][2 * q + h], a);
-#pragma unroll
-        for (int j = 0; j < NT; ++j) mma16816<__half>(part[c][j], a, b[j][2 * h], b[j][2 * h + 1]);
-      }
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const float2 s2 = bf162_to_f2(sc[c]);
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      acc[j][0] = fmaf(part[c][j][0], s2.x, acc[j][0]);
-      acc[j][1] = fmaf(part[c][j][1], s2.x, acc[j][1]);
-      acc[j][2] = fmaf(part[c][j][2], s2.y, acc[j][2]);
-      acc[j][3] = fmaf(part[c][j][3], s2.y, acc[j][3]);
-    }
-  }
-}
-
-// n consecutive chunks, two at a time; NT = 2 n-tiles only when the unit has > 8 tokens.
-template <int G>
-__device__ __forceinline__ void xt_run(const uint8_t* chunk, int n, const __half* const (&xr)[2], int k0, int lane,
-                                       bool two, float (&acc)[2][4]) {
-  constexpr int CHB = W4Fmt<G>::CHB;
-  int c = 0;
-  if (two) {
-    for (; c + 2 <= n; c += 2) xt_chunks<G, 2, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
-    if (c < n) xt_chunks<G, 1, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
-  } else {
-    for (; c + 2 <= n; c += 2) xt_chunks<G, 2, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
-    if (c < n) xt_chunks<G, 1, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
-  }
 }
 
 struct XtArgs {
@@ -696,9 +638,10 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
   extern __shared__ __align__(16) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   XtRoute& rt = *reinterpret_cast<XtRoute*>(smem + XT_BAR_BYTES);
+  int* scratch = reinterpret_cast<int*>(smem + XT_BAR_BYTES + (sizeof(XtRoute) + 127) / 128 * 128);
   const int H = a.H, I = a.I, T = a.T;
   const int XS = H + XT_PAD;
-  __half* xs = reinterpret_cast<__half*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
+  __half* xs = reinterpret_cast<__half*>(smem + xt_head_bytes(a.E));
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(xs) + ((static_cast<size_t>(T) * XS * 2 + 127) / 128) * 128;
   const int nch = H / G, cps = nch < XT_UP_CPS ? nch : XT_UP_CPS, spt = nch / cps;
   const uint32_t sbytes = cps * Fmt::CHB;
@@ -708,13 +651,14 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
     for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
   fence_barrier_init();
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
-  xt_load_route(rt, rv, T, a.k);
-  // x -> shared memory (cp.async), overlapped with the first weight stages below
+  // x -> shared memory (cp.async), overlapped with the list building and the first
+  // weight stages below
   for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
     const int r = i / (H / 8), c = (i % (H / 8)) * 8;
     cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(r) * H + c, true);
   }
   cp_async_commit();
+  xt_build_route(rt, scratch, rv, T, a.E, a.k, blockIdx.x == 0);
   __syncthreads();
   const int J = I / 16;
   const int nslots = a.has_shared + rt.n_active;
@@ -765,7 +709,7 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
           if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
           return;
         }
-        xt_run<G>(ring.stage(q), cps, xr, sub * cps * G, lane, two, acc[g]);
+        w4_smem_run<G>(ring.stage(q), cps, xr, sub * cps * G, lane, two, acc[g]);
         __syncwarp();
         if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
       }
@@ -798,9 +742,10 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   extern __shared__ __align__(16) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   XtRoute& rt = *reinterpret_cast<XtRoute*>(smem + XT_BAR_BYTES);
+  int* scratch = reinterpret_cast<int*>(smem + XT_BAR_BYTES + (sizeof(XtRoute) + 127) / 128 * 128);
   const int H = a.H, I = a.I, T = a.T;
   const int HS = I + XT_PAD;
-  __half* hs = reinterpret_cast<__half*>(smem + XT_BAR_BYTES + ((sizeof(XtRoute) + 127) / 128) * 128);
+  __half* hs = reinterpret_cast<__half*>(smem + xt_head_bytes(a.E));
   const size_t hbytes = ((static_cast<size_t>(XT_MAXT) * HS * 2 + 127) / 128) * 128;
   uint8_t* ring_base = reinterpret_cast<uint8_t*>(hs) + 2 * hbytes;
   const int cpt = I / G;                         // chunks per row tile
@@ -814,7 +759,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
     for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
   fence_barrier_init();
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
-  xt_load_route(rt, rv, T, a.k);
+  xt_build_route(rt, scratch, rv, T, a.E, a.k, false);
   __syncthreads();
   const int nslots = a.has_shared + rt.n_active;
   const int nu = nslots * nrb;
@@ -874,7 +819,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
         float acc[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-        xt_run<G>(st + t * cpt * Fmt::CHB, cpt, xr, 0, lane, two, acc);
+        w4_smem_run<G>(st + t * cpt * Fmt::CHB, cpt, xr, 0, lane, two, acc);
         const int row0 = ((u % nrb) * rb_tiles + (warp * spw + l) * tps + t) * 16;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
@@ -1036,20 +981,30 @@ __global__ void router_dense_kernel(const ET* __restrict__ x, const ET* __restri
 template <typename LT>
 static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, int shared_col,
                         int act_is_f16, void* ws, cudaStream_t s) {
-  const int nw = T < 32 ? T : 32;
-  const int per_warp = ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16;
-  size_t smem = static_cast<size_t>(nw) * per_warp;
-  if (smem < static_cast<size_t>(E) * 12 + 256) smem = static_cast<size_t>(E) * 12 + 256;
+  const size_t smem = ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
-    err = cudaFuncSetAttribute(route_kernel<LT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    err = cudaFuncSetAttribute(route_topk_kernel<LT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
   });
   if (err != cudaSuccess) return cuda_status(err, "route smem attribute");
-  if (smem > 200 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
-  route_kernel<LT><<<1, nw * 32, smem, s>>>(static_cast<const LT*>(logits), ldl, T, E, k, shared_col,
-                                            act_is_f16, ws);
+  if (smem > 64 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
+  route_topk_kernel<LT><<<T, 32, smem, s>>>(static_cast<const LT*>(logits), ldl, T, E, k, shared_col, act_is_f16,
+                                             ws);
   QW_LAUNCH_CHECK("moe route");
+  return QW_OK;
+}
+
+static int launch_route_lists(int T, int E, int k, void* ws, cudaStream_t s) {
+  const size_t smem = (3 * static_cast<size_t>(E) + 64) * sizeof(int);
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(route_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  });
+  if (err != cudaSuccess) return cuda_status(err, "route lists smem attribute");
+  route_lists_kernel<<<1, 1024, smem, s>>>(T, E, k, ws);
+  QW_LAUNCH_CHECK("moe route lists");
   return QW_OK;
 }
 
@@ -1090,7 +1045,7 @@ static int sm_count() {
 
 constexpr size_t XT_SMEM_LIMIT = 227 * 1024;
 
-static size_t xt_route_bytes() { return XT_BAR_BYTES + (sizeof(XtRoute) + 127) / 128 * 128; }
+
 
 // Shapes the bulk-copy kernels take: the verify block (T <= 16), and stage geometry
 // that tiles the weights exactly.
@@ -1108,7 +1063,7 @@ static XtPlan xt_plan(const MoeArgs<__nv_bfloat16>& a) {
                      (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.hbuf) & 15) == 0;
   const int nch = a.H / G;
   const int cps = nch < XT_UP_CPS ? nch : XT_UP_CPS;
-  p.up_smem = xt_route_bytes() + (static_cast<size_t>(a.T) * (a.H + XT_PAD) * 2 + 127) / 128 * 128 +
+  p.up_smem = xt_head_bytes(a.E) + (static_cast<size_t>(a.T) * (a.H + XT_PAD) * 2 + 127) / 128 * 128 +
               static_cast<size_t>(XT_UP_WARPS) * XT_NST * cps * CHB;
   p.up_ok = small && nch % cps == 0 && p.up_smem <= XT_SMEM_LIMIT;
   const int cpt = a.I / G;
@@ -1119,7 +1074,7 @@ static XtPlan xt_plan(const MoeArgs<__nv_bfloat16>& a) {
     p.down_spw = 0;
     for (int spw = 2; spw >= 1; --spw)
       if (tiles % (XT_DN_WARPS * spw * p.down_tps) == 0) { p.down_spw = spw; break; }
-    p.down_smem = xt_route_bytes() + 2 * ((static_cast<size_t>(XT_MAXT) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
+    p.down_smem = xt_head_bytes(a.E) + 2 * ((static_cast<size_t>(XT_MAXT) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
                   static_cast<size_t>(XT_DN_WARPS) * XT_NST * p.down_tps * cpt * CHB;
     p.down_ok = p.down_spw > 0 && p.down_smem <= XT_SMEM_LIMIT;
   }
@@ -1160,7 +1115,14 @@ static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bo
   // the bulk pair keeps h (the down input) in fp16, the streaming pair in bf16: both
   // halves of one MoE always come from the same pair
   if (p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);
-  return launch_experts<W4Fmt<G>, 4>(a, s, up, down);
+  // the streaming kernels read the lists from the workspace (built once, before gate/up)
+  if (up) {
+    const int rc = launch_route_lists(a.T, a.E, a.k, a.ws, s);
+    if (rc != QW_OK) return rc;
+  }
+  // fp16 operands, as the bulk kernels: a token's expert outputs have the same bits
+  // whichever kernels (block size) compute them
+  return launch_experts<W4Fmt<G, __half>, 4>(a, s, up, down);
 }
 
 }  // namespace qw
@@ -1217,6 +1179,14 @@ extern "C" int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, in
   if (logit_dtype == QW_F32)
     return launch_route<float>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
   return fail(QW_ERR_ARG, "moe_route: bad logit dtype");
+}
+
+extern "C" int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t experts, int64_t top_k, void* stream) {
+  QW_CHECK_ARG(workspace, "moe_route_lists: null pointer");
+  QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && experts >= 1 && experts <= 1024 && top_k >= 1 && top_k <= 16 &&
+                   top_k <= experts, "moe_route_lists: invalid shape");
+  return launch_route_lists(static_cast<int>(tokens), static_cast<int>(experts), static_cast<int>(top_k), workspace,
+                            as_stream(stream));
 }
 
 static int experts_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
@@ -1367,6 +1337,8 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     QW_LAUNCH_CHECK("moe router");
     st = launch_route<__half>(w.logits, E, T, E, k, -1, 1, w.route, s);
   }
+  if (st) return st;
+  st = launch_route_lists(T, E, k, w.route, s);
   if (st) return st;
   if (dtype == QW_BF16) {
     MoeArgs<__nv_bfloat16> a{};

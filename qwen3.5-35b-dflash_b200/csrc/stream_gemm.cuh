@@ -34,9 +34,13 @@ namespace qw {
 
 constexpr int SG_WARPS = 8;
 
-template <int G>
+// OT_ is the tensor-core operand type: bf16 (the activations as stored), or fp16 (exact
+// for the int4 weights and for bf16 activations in [2^-14, 65504]; the decode then needs
+// no conversion-unit work, but the activations are converted as they are loaded).
+template <int G, typename OT_ = __nv_bfloat16>
 struct W4Fmt {
-  using ET = __nv_bfloat16;
+  using ET = __nv_bfloat16;   // activation storage
+  using OT = OT_;
   static constexpr int KCHUNK = G;
   static constexpr int STEPS = G / 16;
   static constexpr int WORDS = STEPS;              // 32-bit words per lane per chunk
@@ -66,12 +70,14 @@ struct W4Fmt {
     sc = __ldg(reinterpret_cast<const uint32_t*>(chunk + 8 * G + (lane >> 2) * 4));
   }
   __device__ __forceinline__ static void afrag(const uint32_t (&w)[WORDS], int s, uint32_t (&a)[4]) {
-    dequant_w4_word(w[s], a);
+    if constexpr (std::is_same<OT, __half>::value) dequant_w4_word_f16(w[s], a);
+    else dequant_w4_word(w[s], a);
   }
 };
 
 struct B16Fmt {
   using ET = __nv_bfloat16;
+  using OT = __nv_bfloat16;
   static constexpr int KCHUNK = 64;
   static constexpr int STEPS = 4;
   static constexpr int WORDS = 16;
@@ -101,6 +107,7 @@ struct B16Fmt {
 template <typename ET_>
 struct RowFmt {
   using ET = ET_;
+  using OT = ET_;
   static constexpr int KCHUNK = 32;
   static constexpr int STEPS = 2;
   static constexpr int WORDS = 8;
@@ -160,7 +167,8 @@ __device__ __forceinline__ void load_b(BFrag<Fmt, NT>& f, int c, int lane, const
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       if constexpr (Fmt::PERMUTED_K) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(x.r[j] + kb + 32 * q + 8 * tig));
+        uint4 v = __ldg(reinterpret_cast<const uint4*>(x.r[j] + kb + 32 * q + 8 * tig));
+        if constexpr (!std::is_same<typename Fmt::ET, typename Fmt::OT>::value) v = bf16x8_to_f16x8(v);
         f.b[q][j][0] = v.x; f.b[q][j][1] = v.y; f.b[q][j][2] = v.z; f.b[q][j][3] = v.w;
       } else {
         const typename Fmt::ET* p = x.r[j] + kb + 32 * q + 2 * tig;
@@ -175,7 +183,7 @@ __device__ __forceinline__ void load_b(BFrag<Fmt, NT>& f, int c, int lane, const
 
 template <class Fmt, int NT>
 __device__ __forceinline__ void mma_frag(const WFrag<Fmt>& wf, const BFrag<Fmt, NT>& bf, float (&acc)[NT][4]) {
-  using ET = typename Fmt::ET;
+  using ET = typename Fmt::OT;
   if constexpr (Fmt::SCALED) {
     float part[NT][4];
 #pragma unroll
@@ -248,6 +256,110 @@ __device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int
   const uint8_t* const tiles[1] = {tile};
   float (&a1)[1][NT][4] = *reinterpret_cast<float (*)[1][NT][4]>(&acc);
   stream_tiles<Fmt, NT, PF, 1>(tiles, ld, c0, c1, lane, x, a1);
+}
+
+// acc[nt] += W4 chunks c0 .. c0+NC-1 (16 rows x G each, consecutive in shared memory)
+// . x rows (token of lane gid in n-tile nt at xr[nt]).  NC chunks are decoded and
+// multiplied interleaved (independent instruction streams for one warp) and their
+// scaled partial sums are added to acc in chunk order, as one chunk at a time would.
+// Both operands are fp16: the weights are small integers and the activations are bf16
+// values, exact in fp16 (|x| in [2^-14, 65504]), so the products equal the bf16 ones and
+// the decode needs no conversion-unit instructions (dequant_w4_word_f16).
+template <int G, int NC, int NT>
+__device__ __forceinline__ void w4_smem_chunks(const uint8_t* chunk, const __half* const (&xr)[2], int k0,
+                                          int lane, float (&acc)[2][4]) {
+  using Fmt = W4Fmt<G>;
+  uint32_t w[NC][Fmt::WORDS];
+  uint32_t sc[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int v = 0; v < Fmt::NV; ++v) {
+      const uint8_t* p = chunk + c * Fmt::CHB + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
+      if constexpr (Fmt::VW == 4) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        w[c][v * 4 + 0] = u.x; w[c][v * 4 + 1] = u.y; w[c][v * 4 + 2] = u.z; w[c][v * 4 + 3] = u.w;
+      } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(p);
+        w[c][v * 2 + 0] = u.x; w[c][v * 2 + 1] = u.y;
+      }
+    }
+    sc[c] = *reinterpret_cast<const uint32_t*>(chunk + c * Fmt::CHB + 8 * G + (lane >> 2) * 4);
+  }
+  const int tig = lane & 3;
+  float part[NC][NT][4];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) part[c][j][0] = part[c][j][1] = part[c][j][2] = part[c][j][3] = 0.f;
+#pragma unroll
+  for (int q = 0; q < G / 32; ++q) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      uint32_t b[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + c * G + 32 * q + 8 * tig);
+        b[j][0] = v.x; b[j][1] = v.y; b[j][2] = v.z; b[j][3] = v.w;
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t a[4];
+        dequant_w4_word_f16(w[c][2 * q + h], a);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) mma16816<__half>(part[c][j], a, b[j][2 * h], b[j][2 * h + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const float2 s2 = bf162_to_f2(sc[c]);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      acc[j][0] = fmaf(part[c][j][0], s2.x, acc[j][0]);
+      acc[j][1] = fmaf(part[c][j][1], s2.x, acc[j][1]);
+      acc[j][2] = fmaf(part[c][j][2], s2.y, acc[j][2]);
+      acc[j][3] = fmaf(part[c][j][3], s2.y, acc[j][3]);
+    }
+  }
+}
+
+// n consecutive chunks, two at a time; NT = 2 n-tiles only when the unit has > 8 tokens.
+template <int G>
+__device__ __forceinline__ void w4_smem_run(const uint8_t* chunk, int n, const __half* const (&xr)[2], int k0, int lane,
+                                       bool two, float (&acc)[2][4]) {
+  constexpr int CHB = W4Fmt<G>::CHB;
+  int c = 0;
+  if (two) {
+    for (; c + 2 <= n; c += 2) w4_smem_chunks<G, 2, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+    if (c < n) w4_smem_chunks<G, 1, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+  } else {
+    for (; c + 2 <= n; c += 2) w4_smem_chunks<G, 2, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+    if (c < n) w4_smem_chunks<G, 1, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+  }
+}
+
+// acc[nt] += B16 chunk (16 rows x 64, in shared memory) . x rows (bf16 activations,
+// permuted-K fragment order as the W4 chunks), accumulated like mma_frag (no scales).
+template <int NT>
+__device__ __forceinline__ void b16_smem_chunk(const uint8_t* chunk, const __nv_bfloat16* const (&xr)[2], int k0,
+                                               int lane, float (&acc)[2][4]) {
+  const int tig = lane & 3;
+  uint32_t b[2][NT][4];
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + 32 * q + 8 * tig);
+      b[q][j][0] = v.x; b[q][j][1] = v.y; b[q][j][2] = v.z; b[q][j][3] = v.w;
+    }
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {
+    const uint4 u = *reinterpret_cast<const uint4*>(chunk + st * 512 + lane * 16);
+    const uint32_t a[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < NT; ++j) mma16816<__nv_bfloat16>(acc[j], a, b[st >> 1][j][(st & 1) * 2], b[st >> 1][j][(st & 1) * 2 + 1]);
+  }
 }
 
 // Fragment element r (0..3) of n-tile j: (row within the 16-row tile, token).

@@ -253,7 +253,8 @@ class TargetEngine:
     def forward(self, after_moe_route=None):
         """All layers + final norm + lm_head argmax keys for the tokens in ``self.tokens``.
 
-        ``after_moe_route(layer)`` (eager use only) is called after each layer's routing."""
+        ``after_moe_route(layer)`` (eager use only) is called after each layer's experts
+        (the routing lists, e.g. ``active_experts()``, are valid then)."""
         c, T, H, st = self.cfg, self.T, self.cfg.hidden_size, self._st()
         eps = c.rms_norm_eps
         L = c.num_hidden_layers
@@ -297,11 +298,11 @@ class TargetEngine:
             E, k, I = c.num_experts, c.num_experts_per_tok, c.moe_intermediate_size
             self._call("qw_moe_route", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
                        lib.QW_BF16, self.moe_ws.data_ptr(), st)
-            if after_moe_route is not None:
-                after_moe_route(l)
             self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                        lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
                        self.moe_ws.data_ptr(), st)
+            if after_moe_route is not None:
+                after_moe_route(l)
             # residual add of the MoE output + the next RMSNorm (next layer's input norm, or
             # the final norm) + the feature tap of this layer (normed after the last layer)
             last = l == L - 1

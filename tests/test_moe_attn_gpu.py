@@ -61,6 +61,7 @@ def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k):
     ref_w = (sel / sel.sum(-1, keepdim=True)).to(torch.bfloat16).float()
     assert_close(w.numpy(), ref_w.numpy(), 2 ** -8, 2 ** -7, "route weights")
     # expert -> (token, slot) lists: active experts ascending, tokens ascending in each
+    lib.call("qw_moe_route_lists", ws.data_ptr(), t, e, k, lib.stream_ptr())
     ints = ws.view(torch.int32).cpu().numpy()
     na_max = min(e, t * k)
     o = 2 * t * k + t
