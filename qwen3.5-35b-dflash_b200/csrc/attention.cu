@@ -25,9 +25,9 @@
 namespace qw {
 
 constexpr int ATT_KT = 32;       // keys per tile
-constexpr int ATT_MAXROWS = 128; // query rows per CTA
+constexpr int ATT_MAXROWS = 64;  // query rows per CTA
 constexpr int ATT_NST = 3;        // K/V tile stages in flight
-constexpr int ATT_MIN_KC = 256;   // keys per split at least (partials cost as much as the keys)
+constexpr int ATT_MIN_KC = 128;   // keys per split at least (partials cost about as much as the keys)
 constexpr int ATT_PGCAP = 64;     // page indices staged per CTA
 
 template <typename ET>
