@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   ET* qsm = reinterpret_cast<ET*>(smem);                 // [128][XS]
   ET* ksm = qsm + ATT_MAXROWS * XS;                      // ATT_NST stages of K [32][XS], V [32][XS]
   int* pg = reinterpret_cast<int*>(ksm + ATT_NST * 2 * ATT_KT * XS);  // [pgcap] page of each key page
+  pdl_wait();   // q and the block's keys come from the predecessor (prep)
+  pdl_trigger();
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / a.rowgroups, rg = blockIdx.y % a.rowgroups;
   const int b = blockIdx.z;
@@ -258,6 +260,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ opart, const float
                                     int S, int kc) {
   __shared__ float s_w[ATT_MAXSPLIT];
   __shared__ float s_l;
+  pdl_wait();
+  pdl_trigger();
   const int s = blockIdx.x % S, h = (blockIdx.x / S) % H, b = blockIdx.x / (S * H);
   const int qpos = qposv ? qposv[b] : qpos_scalar;
   const int nsp = (qpos + S + kc - 1) / kc;
@@ -310,6 +314,8 @@ __global__ void attn_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t 
                                  const int32_t* __restrict__ pages, int max_pages, int P,
                                  __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                  __nv_bfloat16* __restrict__ qout, int S, int H, int Hkv) {
+  pdl_wait();   // qkv comes from the predecessor (the projection)
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ float xr[D];
   const int t = blockIdx.x;  // token row b*S + s
@@ -394,11 +400,11 @@ static int launch_attn(AttnArgs<ET> a, ET* out, int64_t ob, int64_t oh, int64_t 
   });
   if (err != cudaSuccess) return cuda_status(err, "attention smem attribute");
   if (a.nsplit > ATT_MAXSPLIT) return fail(QW_ERR_UNSUPPORTED, "attention: %d key splits", a.nsplit);
-  attn_split_kernel<ET, D><<<dim3(a.nsplit, a.Hkv * a.rowgroups, a.B), warps * 32, smem, st>>>(a);
-  QW_LAUNCH_CHECK("attention split");
-  attn_combine_kernel<ET, D><<<a.B * a.H * a.S, D < 256 ? D : 256, 0, st>>>(
-      a.opart, a.ml, out, ob, oh, os, gate, gb, gh, gs, a.qpos, a.qpos_scalar, a.B, a.H, a.S, a.kc);
-  QW_LAUNCH_CHECK("attention combine");
+  QW_LAUNCH_PDL("attention split", attn_split_kernel<ET, D>, dim3(a.nsplit, a.Hkv * a.rowgroups, a.B),
+                dim3(warps * 32), smem, st, a);
+  QW_LAUNCH_PDL("attention combine", attn_combine_kernel<ET, D>, dim3(a.B * a.H * a.S), dim3(D < 256 ? D : 256), 0,
+                st, static_cast<const float*>(a.opart), static_cast<const float*>(a.ml), out, ob, oh, os, gate, gb,
+                gh, gs, a.qpos, a.qpos_scalar, a.B, a.H, a.S, a.kc);
   return QW_OK;
 }
 
@@ -472,7 +478,7 @@ extern "C" int qw_attn_prep(const void* qkv, int64_t ldq, const void* q_norm_w, 
   const dim3 grid(static_cast<unsigned>(batch * seq), static_cast<unsigned>(heads + kv_heads));
   cudaStream_t st = as_stream(stream);
 #define QW_PREP(DD)                                                                                     \
-  attn_prep_kernel<DD><<<grid, 128, 0, st>>>(                                                           \
+  QW_LAUNCH_PDL("attn_prep", attn_prep_kernel<DD>, grid, dim3(128), 0, st,                              \
       static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<const __nv_bfloat16*>(q_norm_w),        \
       static_cast<const __nv_bfloat16*>(k_norm_w), eps, rope_theta, rotary_dim, qpos, pages, max_pages, \
       page_size, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),            \

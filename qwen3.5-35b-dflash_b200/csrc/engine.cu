@@ -30,6 +30,8 @@ struct NormArgs {
 
 __global__ void residual_norm_kernel(NormArgs a) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   __nv_bfloat16* h = a.hidden + static_cast<int64_t>(t) * a.H;
   if (a.ids) {
@@ -59,11 +61,14 @@ __global__ void accept_kernel(const unsigned long long* __restrict__ keys, int n
                               const int32_t* __restrict__ proposals, int32_t* __restrict__ top1,
                               int32_t* __restrict__ max_accepted, int32_t* __restrict__ next_token,
                               int32_t* __restrict__ accepted, int32_t* __restrict__ qpos, int auto_commit) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int32_t s_top1[QW_MAX_BLOCK * 64];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int t = warp; t < T; t += nw) {
     unsigned long long best = 0ull;
-    for (int i = lane; i < nblk; i += 32) {
+#pragma unroll 8
+    for (int i = lane; i < nblk; i += 32) {   // unrolled: the partial keys load together
       const unsigned long long k = keys[static_cast<int64_t>(i) * T + t];
       best = k > best ? k : best;
     }
@@ -97,6 +102,8 @@ __global__ void accept_kernel(const unsigned long long* __restrict__ keys, int n
 
 __global__ void apply_commit_kernel(const int32_t* __restrict__ accepted, const int32_t* __restrict__ top1,
                                     int32_t* __restrict__ next_token, int32_t* __restrict__ qpos, int B, int S) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int acc = accepted[b];
@@ -119,8 +126,8 @@ extern "C" int qw_residual_norm(void* hidden, const int32_t* ids, const void* em
              static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(normed),
              static_cast<__nv_bfloat16*>(tap), ldf, tap_normed, static_cast<int>(tokens),
              static_cast<int>(hidden_dim), eps};
-  residual_norm_kernel<<<static_cast<unsigned>(tokens), 256, 0, as_stream(stream)>>>(a);
-  QW_LAUNCH_CHECK("residual_norm");
+  QW_LAUNCH_PDL("residual_norm", residual_norm_kernel, dim3(static_cast<unsigned>(tokens)), dim3(256), 0,
+                as_stream(stream), a);
   return QW_OK;
 }
 
@@ -131,19 +138,18 @@ extern "C" int qw_accept(const void* keys, int64_t nblk, const int32_t* proposal
   QW_CHECK_ARG(!auto_commit || (accepted && qpos), "accept: auto commit needs accepted and qpos");
   QW_CHECK_ARG(batch >= 1 && seq >= 1 && seq <= QW_MAX_BLOCK && batch * seq <= QW_MAX_BLOCK * 64 && nblk >= 1,
                "accept: invalid shape");
-  accept_kernel<<<1, 512, 0, as_stream(stream)>>>(static_cast<const unsigned long long*>(keys),
-                                                   static_cast<int>(nblk), static_cast<int>(batch * seq),
-                                                   static_cast<int>(seq), static_cast<int>(batch), proposals,
-                                                   top1, max_accepted, next_token, accepted, qpos, auto_commit);
-  QW_LAUNCH_CHECK("accept");
+  QW_LAUNCH_PDL("accept", accept_kernel, dim3(1), dim3(512), 0, as_stream(stream),
+                static_cast<const unsigned long long*>(keys), static_cast<int>(nblk),
+                static_cast<int>(batch * seq), static_cast<int>(seq), static_cast<int>(batch), proposals, top1,
+                max_accepted, next_token, accepted, qpos, auto_commit);
   return QW_OK;
 }
 
 extern "C" int qw_apply_commit(const int32_t* accepted, const int32_t* top1, int32_t* next_token, int32_t* qpos,
                                int64_t batch, int64_t seq, void* stream) {
   QW_CHECK_ARG(accepted && top1 && next_token && qpos && batch >= 1 && seq >= 1, "apply_commit: invalid argument");
-  apply_commit_kernel<<<static_cast<unsigned>((batch + 127) / 128), 128, 0, as_stream(stream)>>>(
-      accepted, top1, next_token, qpos, static_cast<int>(batch), static_cast<int>(seq));
-  QW_LAUNCH_CHECK("apply_commit");
+  QW_LAUNCH_PDL("apply_commit", apply_commit_kernel, dim3(static_cast<unsigned>((batch + 127) / 128)), dim3(128), 0,
+                as_stream(stream), accepted, top1, next_token, qpos, static_cast<int>(batch),
+                static_cast<int>(seq));
   return QW_OK;
 }

@@ -157,6 +157,12 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   const int b = blockIdx.z % d.batch;   // sequence within the batch
   const GdnLayer& L = layers[layer0 + blockIdx.z / d.batch];
   const int64_t slot = d.slots[b];
+  // commit: the accepted counts come from the predecessor (accept); verify reads the
+  // banks and the projections of earlier kernels first and waits before the gates
+  if constexpr (COMMIT) {
+    pdl_wait();
+    pdl_trigger();
+  }
   const int ntok = COMMIT ? d.accepted[b] : d.seq;
   const int tid = threadIdx.x;
   const int col = tid / KSPLIT, kq = tid % KSPLIT;
@@ -174,14 +180,6 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   for (int i = 0; i < ROWS; i += 4) {
     float4 v4 = *reinterpret_cast<const float4*>(scol + i);
     st[i] = v4.x; st[i + 1] = v4.y; st[i + 2] = v4.z; st[i + 3] = v4.w;
-  }
-  // ---- gates (fused/model.py:243-253, fp32)
-  for (int t = tid; t < ntok; t += THREADS) {
-    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
-    const float bl = L.ab[row * 2 * d.v_heads + h];
-    const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
-    sm.beta[t] = sigmoid_f(bl);
-    sm.g[t] = -__expf(L.A_log[h]) * softplus_f(al + L.dt_bias[h]);
   }
   // ---- stage the block's projections of this CTA's channels (and z) in shared memory:
   // per token 8-element vectors of the q, k, v (and z) segments, all loads in flight at once
@@ -203,6 +201,18 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
       else { src = rowp + segz + (v - QV - KV - VV) * 8; dst = &sm.zin[t][(v - QV - KV - VV) * 8]; }
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
     }
+  }
+  if constexpr (!COMMIT) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  // ---- gates (fused/model.py:243-253, fp32)
+  for (int t = tid; t < ntok; t += THREADS) {
+    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
+    const float bl = L.ab[row * 2 * d.v_heads + h];
+    const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
+    sm.beta[t] = sigmoid_f(bl);
+    sm.g[t] = -__expf(L.A_log[h]) * softplus_f(al + L.dt_bias[h]);
   }
   __syncthreads();
   // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns; each thread's
@@ -358,6 +368,8 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
 // One thread per (layer, sequence, channel); each channel is owned by one thread, so the
 // update is in place.
 __global__ void gdn_conv_commit_kernel(GdnDims d, const GdnLayer* __restrict__ layers, int nlayers) {
+  pdl_wait();   // the state commit (predecessor) still reads the conv tails
+  pdl_trigger();
   const int64_t total = static_cast<int64_t>(nlayers) * d.batch * d.channels;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -387,13 +399,15 @@ static int launch_block(const GdnDims& d, const GdnLayer* layers, int layer0, in
   cfg.blockDim = dim3(Tile::THREADS);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = VSPLIT;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gdn_block_kernel<DK, DV, VSPLIT, COMMIT>, d, layers, layer0);
   if (e != cudaSuccess) return cuda_status(e, COMMIT ? "gdn_commit" : "gdn_verify");
   return QW_OK;
@@ -499,7 +513,7 @@ extern "C" int qw_gdn_commit(const qw_gdn_dims* dims, const qw_gdn_layer* layers
   const int64_t total = static_cast<int64_t>(nlayers) * dims->batch * dims->channels;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  gdn_conv_commit_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(*dims, layers_dev, nlayers);
-  QW_LAUNCH_CHECK("gdn_conv_commit");
+  QW_LAUNCH_PDL("gdn_conv_commit", gdn_conv_commit_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
+                *dims, layers_dev, nlayers);
   return QW_OK;
 }

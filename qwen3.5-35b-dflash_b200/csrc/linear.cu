@@ -50,7 +50,9 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
     float acc[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    if (active) stream_tile<Fmt, NT, PF>(tile, 0, c0, c1, lane, xr, acc);
+    if (active) stream_tile<Fmt, NT, PF, true>(tile, 0, c0, c1, lane, xr, acc);
+    pdl_wait();                    // (idle warps) before any write of this kernel
+    pdl_trigger();
     if (tp0 > 0) __syncthreads();  // previous pass's reduction reads are done
 #pragma unroll
     for (int j = 0; j < NT; ++j)
@@ -149,8 +151,7 @@ static int launch_linear(const LinArgs& a0, cudaStream_t s) {
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "linear smem attribute");
   const int ntiles = a.n / 16;
   const unsigned grid = static_cast<unsigned>((ntiles + a.rt - 1) / a.rt);
-  stream_linear_kernel<Fmt, NT, PF, ARGMAX><<<grid, SG_WARPS * 32, smem, s>>>(a);
-  QW_LAUNCH_CHECK("linear");
+  QW_LAUNCH_PDL("linear", stream_linear_kernel<Fmt, NT, PF, ARGMAX>, dim3(grid), dim3(SG_WARPS * 32), smem, s, a);
   return QW_OK;
 }
 

@@ -256,6 +256,8 @@ template <typename LT>
 __global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ logits, int64_t ldl, int T, int E,
                                                        int k, int shared_col, int act_is_f16, void* ws) {
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_wait();   // the router logits come from the predecessor
+  pdl_trigger();
   RouteView rv = route_view(ws, T, E, k);
   const int lane = threadIdx.x;
   Q q{reinterpret_cast<float*>(smem), reinterpret_cast<int32_t*>(smem + E * 4)};
@@ -409,6 +411,8 @@ __device__ void build_route_lists(const int* idx, int T, int E, int k, int* scra
 // Lists of the routing workspace (one CTA).  Dynamic smem: 3E + 64 ints.
 __global__ void __launch_bounds__(1024) route_lists_kernel(int T, int E, int k, void* ws) {
   extern __shared__ __align__(16) uint8_t smem[];
+  pdl_wait();
+  pdl_trigger();
   RouteView rv = route_view(ws, T, E, k);
   int* scratch = reinterpret_cast<int*>(smem);
   build_route_lists(rv.topk_idx, T, E, k, scratch, scratch + 3 * E, rv.n_active, rv.active, rv.pair_off,
@@ -462,6 +466,8 @@ __global__ void __launch_bounds__(SG_WARPS * 32, 2) moe_up_kernel(MoeArgs<typena
   using ET = typename Fmt::ET;
   constexpr int NTOK = NT * 8;
   __shared__ float gsm[UP_JT][NT * 4][32];
+  pdl_wait();
+  pdl_trigger();
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   const uint8_t* w;
   int npairs, pbase;
@@ -515,6 +521,8 @@ template <class Fmt, int NT, int PF>
 __global__ void __launch_bounds__(SG_WARPS * 32, 2) moe_down_kernel(MoeArgs<typename Fmt::ET> a) {
   using ET = typename Fmt::ET;
   constexpr int NTOK = NT * 8;
+  pdl_wait();
+  pdl_trigger();
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   const uint8_t* w;
   int npairs, pbase;
@@ -658,6 +666,8 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
     cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(r) * H + c, true);
   }
   cp_async_commit();
+  pdl_wait();   // the top-k indices come from the predecessor (route); x is older
+  pdl_trigger();
   xt_build_route(rt, scratch, rv, T, a.E, a.k, blockIdx.x == 0);
   __syncthreads();
   const int J = I / 16;
@@ -789,6 +799,8 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
       cp_async16(dst + r * HS + c, hsrc + (hb + r) * I + c, true);
     }
   };
+  pdl_wait();   // h comes from the predecessor (gate/up); the lists and weights do not
+  pdl_trigger();
   if (my_units > 0) stage_h(0);
   cp_async_commit();
   const int gid = lane >> 2;
@@ -892,6 +904,8 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
   __shared__ int s_slot[KMAX];
   __shared__ float s_w[KMAX];
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const RouteView rv = route_view(ws, T, E, k);
   const int t = blockIdx.x;
   if (threadIdx.x < k) {
@@ -989,9 +1003,8 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   });
   if (err != cudaSuccess) return cuda_status(err, "route smem attribute");
   if (smem > 64 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
-  route_topk_kernel<LT><<<T, 32, smem, s>>>(static_cast<const LT*>(logits), ldl, T, E, k, shared_col, act_is_f16,
-                                             ws);
-  QW_LAUNCH_CHECK("moe route");
+  QW_LAUNCH_PDL("moe route", route_topk_kernel<LT>, dim3(T), dim3(32), smem, s, static_cast<const LT*>(logits), ldl,
+                T, E, k, shared_col, act_is_f16, ws);
   return QW_OK;
 }
 
@@ -1003,8 +1016,7 @@ static int launch_route_lists(int T, int E, int k, void* ws, cudaStream_t s) {
     err = cudaFuncSetAttribute(route_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
   });
   if (err != cudaSuccess) return cuda_status(err, "route lists smem attribute");
-  route_lists_kernel<<<1, 1024, smem, s>>>(T, E, k, ws);
-  QW_LAUNCH_CHECK("moe route lists");
+  QW_LAUNCH_PDL("moe route lists", route_lists_kernel, dim3(1), dim3(1024), smem, s, T, E, k, ws);
   return QW_OK;
 }
 
@@ -1013,12 +1025,11 @@ static int launch_experts_nt(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s,
   const int slots = 1 + (a.E < a.T * a.k ? a.E : a.T * a.k);
   if (up) {
     const int jb = (a.I / 16 + UP_JT - 1) / UP_JT;
-    moe_up_kernel<Fmt, NT, PF><<<dim3(slots, jb), SG_WARPS * 32, 0, s>>>(a);
-    QW_LAUNCH_CHECK("moe up");
+    QW_LAUNCH_PDL("moe up", moe_up_kernel<Fmt, NT, PF>, dim3(slots, jb), dim3(SG_WARPS * 32), 0, s, a);
   }
   if (down) {
-    moe_down_kernel<Fmt, NT, PF><<<dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS), SG_WARPS * 32, 0, s>>>(a);
-    QW_LAUNCH_CHECK("moe down");
+    QW_LAUNCH_PDL("moe down", moe_down_kernel<Fmt, NT, PF>, dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS),
+                  dim3(SG_WARPS * 32), 0, s, a);
   }
   return QW_OK;
 }
@@ -1097,12 +1108,11 @@ static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p,
   XtArgs xa{a, status, QW_WAIT_LIMIT};
   const int grid = sm_count();
   if (up) {
-    moe_up_bulk_kernel<G><<<grid, XT_UP_WARPS * 32, p.up_smem, s>>>(xa);
-    QW_LAUNCH_CHECK("moe up (bulk)");
+    QW_LAUNCH_PDL("moe up (bulk)", moe_up_bulk_kernel<G>, dim3(grid), dim3(XT_UP_WARPS * 32), p.up_smem, s, xa);
   }
   if (down) {
-    moe_down_bulk_kernel<G><<<grid, XT_DN_WARPS * 32, p.down_smem, s>>>(xa, p.down_tps, p.down_spw);
-    QW_LAUNCH_CHECK("moe down (bulk)");
+    QW_LAUNCH_PDL("moe down (bulk)", moe_down_bulk_kernel<G>, dim3(grid), dim3(XT_DN_WARPS * 32), p.down_smem, s, xa,
+                  p.down_tps, p.down_spw);
   }
   return QW_OK;
 }
@@ -1299,13 +1309,13 @@ extern "C" int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens
   auto* gp = static_cast<const __nv_bfloat16*>(gamma);
   auto* np_ = static_cast<__nv_bfloat16*>(normed);
   auto* tp = static_cast<__nv_bfloat16*>(tap);
+  const float* part = w.part;
   if (k <= 8)
-    moe_combine_norm_kernel<8><<<T, CN_THREADS, 0, s>>>(w.part, w.route, hp, T, H, E, k, has_shared, gp, np_, eps,
-                                                        tp, ldf, tap_normed);
+    QW_LAUNCH_PDL("moe combine_norm", moe_combine_norm_kernel<8>, dim3(T), dim3(CN_THREADS), 0, s, part, w.route, hp,
+                  T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed);
   else
-    moe_combine_norm_kernel<16><<<T, CN_THREADS, 0, s>>>(w.part, w.route, hp, T, H, E, k, has_shared, gp, np_,
-                                                         eps, tp, ldf, tap_normed);
-  QW_LAUNCH_CHECK("moe combine_norm");
+    QW_LAUNCH_PDL("moe combine_norm", moe_combine_norm_kernel<16>, dim3(T), dim3(CN_THREADS), 0, s, part, w.route,
+                  hp, T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed);
   return QW_OK;
 }
 

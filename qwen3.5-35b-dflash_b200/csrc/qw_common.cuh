@@ -7,6 +7,7 @@
 #include <stdint.h>
 #include <string>
 #include <type_traits>
+#include <utility>
 
 #include "../../include/qw_b200.h"
 
@@ -29,6 +30,38 @@ int cuda_status(cudaError_t err, const char* what);
   } while (0)
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------------ programmatic launch
+// Kernels of the verify step are launched with programmatic stream serialization: a
+// kernel may start while its predecessor on the stream drains, runs its independent
+// prologue (weights, which no kernel writes; data of kernels before the predecessor),
+// then pdl_wait() blocks until the predecessor has completed and its writes are
+// visible.  pdl_trigger() (only after pdl_wait) lets the successor start early in turn.
+// Without a programmatic predecessor both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+#define QW_LAUNCH_PDL(what, ...)                                                  \
+  do {                                                                            \
+    cudaError_t _e = ::qw::launch_pdl(__VA_ARGS__);                               \
+    if (_e != cudaSuccess) return ::qw::cuda_status(_e, what);                    \
+  } while (0)
 
 // ------------------------------------------------------------------ dtype helpers
 template <typename T> struct DT;

@@ -220,7 +220,9 @@ __device__ __forceinline__ void mma_frag(const WFrag<Fmt>& wf, const BFrag<Fmt, 
 // run PF chunks ahead in a register ring (issued first, before anything else, so the
 // HBM latency overlaps the caller's setup), the activations (L1/L2 hits) one chunk
 // ahead.  PF must be even.
-template <class Fmt, int NT, int PF, int NTILES>
+// With PDL the first weight chunks are requested before pdl_wait(): weights are never
+// written by a kernel, the activations come from the predecessor.
+template <class Fmt, int NT, int PF, int NTILES, bool PDL = false>
 __device__ __forceinline__ void stream_tiles(const uint8_t* const (&tiles)[NTILES], int64_t ld, int c0, int c1,
                                              int lane, const XRows<typename Fmt::ET, NT>& x,
                                              float (&acc)[NTILES][NT][4]) {
@@ -233,6 +235,10 @@ __device__ __forceinline__ void stream_tiles(const uint8_t* const (&tiles)[NTILE
 #pragma unroll
       for (int t = 0; t < NTILES; ++t) load_w<Fmt>(w[p][t], tiles[t], c0 + p, lane, ld);
     }
+  if constexpr (PDL) {
+    pdl_wait();
+    pdl_trigger();
+  }
   if (c0 < c1) load_b<Fmt, NT>(b[0], c0, lane, x);
   for (int c = c0; c < c1; c += PF) {
 #pragma unroll
@@ -250,12 +256,12 @@ __device__ __forceinline__ void stream_tiles(const uint8_t* const (&tiles)[NTILE
   }
 }
 
-template <class Fmt, int NT, int PF>
+template <class Fmt, int NT, int PF, bool PDL = false>
 __device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int c0, int c1, int lane,
                                             const XRows<typename Fmt::ET, NT>& x, float (&acc)[NT][4]) {
   const uint8_t* const tiles[1] = {tile};
   float (&a1)[1][NT][4] = *reinterpret_cast<float (*)[1][NT][4]>(&acc);
-  stream_tiles<Fmt, NT, PF, 1>(tiles, ld, c0, c1, lane, x, a1);
+  stream_tiles<Fmt, NT, PF, 1, PDL>(tiles, ld, c0, c1, lane, x, a1);
 }
 
 // acc[nt] += W4 chunks c0 .. c0+NC-1 (16 rows x G each, consecutive in shared memory)
