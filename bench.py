@@ -374,6 +374,89 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_kernels(args):
+    """Per-kernel CUDA-event timings of the verify step's kernels on a 4-layer model of
+    the full width (about 2 GB of weights on the device): each launch cycles through the
+    4 layers' weights so successive launches stream from HBM, not L2.  The small case
+    for ncu captures (``--kernels --kernel-reps 1``)."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from qwen35_dflash_b200 import config, engine as E, lib
+    cfg = config.with_layers(config.QWEN35_35B_A3B, 4)
+    eng = E.TargetEngine(cfg, E.weights_random(cfg, seed=2), batch=1, block=16, capacity=args.ctx + 64)
+    eng.set_random_context(args.ctx, seed=3)
+    so, T, H = eng.lib, eng.T, cfg.hidden_size
+    Ex, k, I, g = cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size, cfg.quant_group
+    st = torch.cuda.Stream()
+    s = st.cuda_stream
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    x = torch.randn(T, H, device="cuda", generator=gen).to(torch.bfloat16)
+    logits = torch.randn(T, eng.nrouter, device="cuda", generator=gen).to(torch.bfloat16)
+    ws = eng.moe_ws
+    L = eng.layers
+    gl = [lw for lw in L if lw.kind == "linear_attention"]
+
+    def chk(rc):
+        lib.check(rc)
+
+    def route():
+        chk(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, Ex, k, Ex, lib.QW_BF16, ws.data_ptr(), s))
+
+    def up(lw):
+        return lambda: chk(so.qw_moe_up_w4(x.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
+                                           lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, Ex, I, k, g,
+                                           ws.data_ptr(), s))
+
+    def down(lw):
+        return lambda: chk(so.qw_moe_down_w4(x.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
+                                             lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, Ex, I, k, g,
+                                             ws.data_ptr(), s))
+
+    def qkvz(lw):
+        return lambda: chk(so.qw_w4_linear(x.data_ptr(), lw.qkvz.data_ptr(), eng.proj[0].data_ptr(), lib.QW_OUT_BF16,
+                                           eng.ldp, T, eng.ldp, H, g, s))
+
+    def gdn(gi):
+        return lambda: chk(so.qw_gdn_verify(eng.gdn_dims, eng.gdn_desc.data_ptr(), gi, s))
+
+    with torch.cuda.stream(st):
+        route()
+        up(L[0])()
+    torch.cuda.synchronize()
+    active = eng.active_experts()
+    w4 = lambda n, kk: n * kk // 2 + n * (kk // g) * 2
+    cases = [("route", [route], 0), ("moe_up", [up(lw) for lw in L], (active + 1) * w4(2 * I, H)),
+             ("moe_down", [down(lw) for lw in L], (active + 1) * w4(H, I)),
+             ("w4_qkvz", [qkvz(lw) for lw in gl], w4(eng.ldp, H)),
+             ("gdn_verify", [gdn(i) for i in range(len(gl))], 0)]
+    out = {"kernels": {}, "active_experts": active, "ctx": args.ctx}
+    for name, fns, nbytes in cases:
+        with torch.cuda.stream(st):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for _ in range(args.kernel_reps):
+                for f in fns:
+                    f()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()           # graph.replay() runs on the current stream
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (args.kernel_reps * len(fns))
+        entry = {"us": round(us, 2)}
+        if nbytes:
+            entry.update(bytes=nbytes, gbs=round(nbytes / us / 1e3, 1))
+        out["kernels"][name] = entry
+        del graph
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -386,7 +469,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="run warm-up then one step inside cudaProfilerStart/Stop and exit (for ncu)")
+    ap.add_argument("--kernels", action="store_true",
+                    help="per-kernel timings on a 4-layer model of the full width (the small case for ncu)")
+    ap.add_argument("--kernel-reps", type=int, default=5)
     args = ap.parse_args()
+    if args.kernels:
+        run_kernels(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -330,18 +330,17 @@ __device__ __forceinline__ void w4_smem_chunks(const uint8_t* chunk, const __hal
   }
 }
 
-// n consecutive chunks, two at a time; NT = 2 n-tiles only when the unit has > 8 tokens.
+// n consecutive chunks; NT = 2 n-tiles only when the unit has > 8 tokens.
 template <int G>
 __device__ __forceinline__ void w4_smem_run(const uint8_t* chunk, int n, const __half* const (&xr)[2], int k0, int lane,
                                        bool two, float (&acc)[2][4]) {
   constexpr int CHB = W4Fmt<G>::CHB;
-  int c = 0;
+  // one chunk per iteration: a small loop body (instruction fetch was the top stall with
+  // two interleaved chunks, which gave no more issue parallelism)
   if (two) {
-    for (; c + 2 <= n; c += 2) w4_smem_chunks<G, 2, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
-    if (c < n) w4_smem_chunks<G, 1, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+    for (int c = 0; c < n; ++c) w4_smem_chunks<G, 1, 2>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
   } else {
-    for (; c + 2 <= n; c += 2) w4_smem_chunks<G, 2, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
-    if (c < n) w4_smem_chunks<G, 1, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
+    for (int c = 0; c < n; ++c) w4_smem_chunks<G, 1, 1>(chunk + c * CHB, xr, k0 + c * G, lane, acc);
   }
 }
 
