@@ -82,7 +82,7 @@ __global__ void gdn_rule_kernel(const Tin* __restrict__ q, const Tin* __restrict
 }
 
 // =============================================================== block verify / commit
-constexpr int KSPLIT = 4;  // threads per state column
+constexpr int KSPLIT = 8;  // threads per state column
 
 template <int DK, int DV, int VSPLIT>
 struct GdnTile {
@@ -99,6 +99,7 @@ struct GdnSmem {
   float k[QW_MAX_BLOCK][DK];
   float v[QW_MAX_BLOCK][COLS];
   float o[QW_MAX_BLOCK][COLS];
+  float opart[QW_MAX_BLOCK][COLS][KSPLIT];   // per-thread partial outputs, reduced after the recurrence
   float g[QW_MAX_BLOCK];
   float beta[QW_MAX_BLOCK];
   float sumsq[QW_MAX_BLOCK];
@@ -132,17 +133,18 @@ __device__ __forceinline__ void conv_channel(const float (&hist)[GDN_CONV_K - 1]
   float win[K];
 #pragma unroll
   for (int j = 0; j < K - 1; ++j) win[j] = hist[j];
+  // every row of the block buffer is computed (rows past ntok hold stale, in-bounds
+  // values) so the unrolled tokens interleave; only the real ones are stored
 #pragma unroll
   for (int t = 0; t < QW_MAX_BLOCK; ++t) {
-    if (t < ntok) {
-      win[K - 1] = __bfloat162float(src[t * sstride]);
-      float acc = 0.f;
+    win[K - 1] = __bfloat162float(src[t * sstride]);
+    float acc = 0.f;
 #pragma unroll
-      for (int j = 0; j < K; ++j) acc = fmaf(win[j], w[j], acc);
-      dst[t * stride] = rbf(silu_f(rbf(acc)));
+    for (int j = 0; j < K; ++j) acc = fmaf(win[j], w[j], acc);
+    const float y = rbf(silu_f(rbf(acc)));
+    if (t < ntok) dst[t * stride] = y;
 #pragma unroll
-      for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
-    }
+    for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
   }
 }
 
@@ -199,9 +201,35 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
       else if (v < QV + KV) { src = rowp + segk + (v - QV) * 8; dst = &sm.xin[t][DK + (v - QV) * 8]; }
       else if (v < QV + KV + VV) { src = rowp + segv + (v - QV - KV) * 8; dst = &sm.xin[t][2 * DK + (v - QV - KV) * 8]; }
       else { src = rowp + segz + (v - QV - KV - VV) * 8; dst = &sm.zin[t][(v - QV - KV - VV) * 8]; }
-      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      cp_async16(dst, src, true);
+    }
+    cp_async_commit();
+  }
+  // ---- each thread's conv channels: tails and taps (older than the predecessor)
+  constexpr int K = GDN_CONV_K;
+  constexpr int XS = 2 * DK + COLS;
+  constexpr int CPT = (2 * DK + COLS + THREADS - 1) / THREADS;  // channels per thread
+  const int nq = COMMIT ? 0 : DK;
+  const int nch = nq + DK + COLS;
+  float hreg[CPT][K - 1], wreg[CPT][K];
+  int chan[CPT];
+#pragma unroll
+  for (int r = 0; r < CPT; ++r) {
+    const int i = tid + r * THREADS;
+    if (i < nq) chan[r] = kh * DK + i;
+    else if (i < nq + DK) chan[r] = kw + kh * DK + (i - nq);
+    else chan[r] = 2 * kw + h * DV + vcol0 + (i - nq - DK);
+    if (i < nch) {
+      const __nv_bfloat16* hist = L.conv_hist + (slot * d.channels + chan[r]) * (K - 1);
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) hreg[r][j] = __bfloat162float(hist[j]);
+#pragma unroll
+      for (int j = 0; j < K; ++j) wreg[r][j] = __bfloat162float(L.conv_w[chan[r] * K + j]);
     }
   }
+  // per-thread constants of the gates and of the gated norm
+  const float neg_a = -__expf(L.A_log[h]), dtb = L.dt_bias[h];
+  const float norm_w = COMMIT ? 0.f : __bfloat162float(L.norm_w[vcol0 + tid % COLS]);
   if constexpr (!COMMIT) {
     pdl_wait();
     pdl_trigger();
@@ -212,33 +240,13 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     const float bl = L.ab[row * 2 * d.v_heads + h];
     const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
     sm.beta[t] = sigmoid_f(bl);
-    sm.g[t] = -__expf(L.A_log[h]) * softplus_f(al + L.dt_bias[h]);
+    sm.g[t] = __expf(neg_a * softplus_f(al + dtb));   // the decay exp(g) of the recurrence
   }
+  cp_async_wait<0>();
   __syncthreads();
-  // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns; each thread's
-  // channels' conv tails and taps are loaded together first
+  // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns (taps and tails
+  // loaded above, before the wait)
   {
-    constexpr int K = GDN_CONV_K;
-    constexpr int XS = 2 * DK + COLS;
-    constexpr int CPT = (2 * DK + COLS + THREADS - 1) / THREADS;  // channels per thread
-    const int nq = COMMIT ? 0 : DK;
-    const int nch = nq + DK + COLS;
-    float hreg[CPT][K - 1], wreg[CPT][K];
-    int chan[CPT];
-#pragma unroll
-    for (int r = 0; r < CPT; ++r) {
-      const int i = tid + r * THREADS;
-      if (i < nq) chan[r] = kh * DK + i;
-      else if (i < nq + DK) chan[r] = kw + kh * DK + (i - nq);
-      else chan[r] = 2 * kw + h * DV + vcol0 + (i - nq - DK);
-      if (i < nch) {
-        const __nv_bfloat16* hist = L.conv_hist + (slot * d.channels + chan[r]) * (K - 1);
-#pragma unroll
-        for (int j = 0; j < K - 1; ++j) hreg[r][j] = __bfloat162float(hist[j]);
-#pragma unroll
-        for (int j = 0; j < K; ++j) wreg[r][j] = __bfloat162float(L.conv_w[chan[r] * K + j]);
-      }
-    }
 #pragma unroll
     for (int r = 0; r < CPT; ++r) {
       const int i = tid + r * THREADS;
@@ -256,21 +264,29 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     }
   }
   __syncthreads();
-  // ---- L2 norm of q and k per token (fused_ops.py:92-95); q also scaled by Dk^-1/2
+  // ---- L2 norm of q and k per token (fused_ops.py:92-95); q also scaled by Dk^-1/2:
+  // 8 threads per token, all tokens at once
   {
-    const int warp = tid / 32, lane = tid % 32;
-    constexpr int NW = THREADS / 32;
-    for (int t = warp; t < ntok; t += NW) {
-      float sk = 0.f, sq = 0.f;
-      for (int i = lane; i < DK; i += 32) {
+    static_assert(THREADS >= 8 * QW_MAX_BLOCK, "the l2 norm needs 8 threads per token");
+    const int t = tid / 8, part = tid % 8;
+    float sk = 0.f, sq = 0.f;
+    if (t < ntok) {
+#pragma unroll
+      for (int i = part; i < DK; i += 8) {
         sk += sm.k[t][i] * sm.k[t][i];
         if (!COMMIT) sq += sm.q[t][i] * sm.q[t][i];
       }
-      sk = warp_sum(sk);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      if (!COMMIT) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    }
+    if (t < ntok) {
       const float ik = rsqrtf(sk + 1e-6f);
-      float iq = 0.f;
-      if (!COMMIT) iq = rsqrtf(warp_sum(sq) + 1e-6f) * rsqrtf(static_cast<float>(DK));
-      for (int i = lane; i < DK; i += 32) {
+      const float iq = COMMIT ? 0.f : rsqrtf(sq + 1e-6f) * rsqrtf(static_cast<float>(DK));
+#pragma unroll
+      for (int i = part; i < DK; i += 8) {
         sm.k[t][i] *= ik;
         if (!COMMIT) sm.q[t][i] *= iq;
       }
@@ -279,48 +295,43 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   __syncthreads();
   // ---- the recurrence (fused_ops.py:98-106)
   for (int t = 0; t < ntok; ++t) {
-    const float decay = __expf(sm.g[t]);
+    const float decay = sm.g[t];
     const float* kt = &sm.k[t][kq * 4];
     float kr[ROWS];
-    float p0 = 0.f, p1 = 0.f;
+    float p[4] = {0.f, 0.f, 0.f, 0.f};   // four chains: short dependent FMA sequences
 #pragma unroll
     for (int i = 0; i < ROWS; i += 4) {
       const float4 k4 = *reinterpret_cast<const float4*>(kt + (i / 4) * 4 * KSPLIT);
       kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
+      for (int e = 0; e < 4; ++e) {
         st[i + e] *= decay;
-        st[i + e + 1] *= decay;
-        p0 = fmaf(st[i + e], kr[i + e], p0);
-        p1 = fmaf(st[i + e + 1], kr[i + e + 1], p1);
+        p[e] = fmaf(st[i + e], kr[i + e], p[e]);
       }
     }
-    float pred = p0 + p1;
-    pred += __shfl_xor_sync(0xffffffffu, pred, 1);
-    pred += __shfl_xor_sync(0xffffffffu, pred, 2);
+    float pred = (p[0] + p[1]) + (p[2] + p[3]);
+#pragma unroll
+    for (int sh = 1; sh < KSPLIT; sh <<= 1) pred += __shfl_xor_sync(0xffffffffu, pred, sh);
     const float delta = (sm.v[t][col] - pred) * sm.beta[t];
     if (COMMIT) {
 #pragma unroll
       for (int i = 0; i < ROWS; ++i) st[i] = fmaf(kr[i], delta, st[i]);
     } else {
       const float* qt = &sm.q[t][kq * 4];
-      float o0 = 0.f, o1 = 0.f;
+      float oo[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < ROWS; i += 4) {
         const float4 q4 = *reinterpret_cast<const float4*>(qt + (i / 4) * 4 * KSPLIT);
         const float qr[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (int e = 0; e < 4; e += 2) {
+        for (int e = 0; e < 4; ++e) {
           st[i + e] = fmaf(kr[i + e], delta, st[i + e]);
-          st[i + e + 1] = fmaf(kr[i + e + 1], delta, st[i + e + 1]);
-          o0 = fmaf(st[i + e], qr[e], o0);
-          o1 = fmaf(st[i + e + 1], qr[e + 1], o1);
+          oo[e] = fmaf(st[i + e], qr[e], oo[e]);
         }
       }
-      float o = o0 + o1;
-      o += __shfl_xor_sync(0xffffffffu, o, 1);
-      o += __shfl_xor_sync(0xffffffffu, o, 2);
-      if (kq == 0) sm.o[t][col] = rbf(o);   // core tensor in the activation dtype
+      // the output sum over the KSPLIT threads is not on the state's critical path:
+      // partials go to shared memory and are reduced after the loop
+      sm.opart[t][col][kq] = (oo[0] + oo[1]) + (oo[2] + oo[3]);
     }
   }
   if (COMMIT) {
@@ -328,6 +339,14 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     for (int i = 0; i < ROWS; i += 4)
       *reinterpret_cast<float4*>(scol + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
     return;
+  }
+  __syncthreads();
+  for (int i = tid; i < ntok * COLS; i += THREADS) {
+    const int t = i / COLS, c = i % COLS;
+    float o = 0.f;
+#pragma unroll
+    for (int q = 0; q < KSPLIT; ++q) o += sm.opart[t][c][q];
+    sm.o[t][c] = rbf(o);   // core tensor in the activation dtype
   }
   __syncthreads();
   // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225)
@@ -358,7 +377,7 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     const int vc = h * DV + vcol0 + c;
     const float inv = rsqrtf(sm.total[t] / DV + d.eps);
     const float n = rbf(sm.o[t][c] * inv);
-    const float y = rbf(n * __bfloat162float(L.norm_w[vcol0 + c]));
+    const float y = rbf(n * norm_w);   // c == tid % COLS for every i of this thread
     const float z = __bfloat162float(sm.zin[t][c]);
     L.out[row * vw + vc] = __float2bfloat16_rn(y * rbf(silu_f(z)));
   }

@@ -85,8 +85,13 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float
 template <typename T> __device__ __forceinline__ float rnd(float x) { return to_f(from_f<T>(x)); }
 __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// SiLU and sigmoid with the fast reciprocal-multiply division (within 2 ulp of the
+// correctly rounded quotient, far below the bf16 rounding that follows every use): the
+// IEEE division sequence dominated the GDN conv prologue.  __fdividef returns 0 when the
+// denominator exceeds 2^126 (x < -87), where both functions are 0 to float precision
+// after rounding.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
