@@ -40,6 +40,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "verify tok/s & step latency (block 16, W4 MoE+GDN); % HBM roofline"
 
+# DRAM bytes (read + write) of one moe_up_bulk_kernel launch from an ncu capture of the
+# same routing (16 tokens of N(0,1) router logits, seed 17 -> 103 active experts):
+# profiles/moe_up_bulk_T16.md
+MOE_UP_NCU_TRAFFIC = {"bytes": 112_624_896 + 3_246_336, "active": 103, "profile": "profiles/moe_up_bulk_T16.md"}
+
 
 def _peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -311,10 +316,12 @@ def run_ours(args, rank, world, local_rank):
                     "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 2 * B * 4,
                     "api": "TargetEngine.serve_step (pinned host proposals -> graph -> accepted/next tokens)"},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "moe_up_kernel (routed + shared expert gate/up, W4A16)",
+            "roofline": {"bound": "hbm", "kernel": "moe_up_bulk_kernel (routed + shared expert gate/up, W4A16)",
                          "achieved": round(rl_achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(rl_achieved / hbm, 4), "peak_kind": f"{peak_kind} burst copy",
-                         "traffic": None, "bytes_per_launch": rl["bytes"], "us_per_launch": round(rl["us"], 2),
+                         "traffic": MOE_UP_NCU_TRAFFIC["bytes"] if rl["active"] == MOE_UP_NCU_TRAFFIC["active"] else None,
+                         "traffic_source": MOE_UP_NCU_TRAFFIC["profile"],
+                         "bytes_per_launch": rl["bytes"], "us_per_launch": round(rl["us"], 2),
                          "active_experts": rl["active"]},
             "clocks": clocks.summary(),
         }

@@ -4,10 +4,17 @@
 // 32-token pass; the CTA splits K across its warps and reduces in shared memory, so
 // the result is deterministic and the epilogue can fuse the residual add.
 #include <mutex>
+#include <utility>
+#include <vector>
 
+#include <cooperative_groups.h>
+
+#include "bulk_ring.cuh"
 #include "stream_gemm.cuh"
 
 namespace qw {
+
+namespace cg = cooperative_groups;
 
 struct LinArgs {
   const __nv_bfloat16* x;  // [T, k]
@@ -126,16 +133,290 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
   }
 }
 
-// Row tiles per CTA (the K split is SG_WARPS / rt): the largest count that still leaves
-// >= 2 waves of CTAs.  The partition (and so the fp32 summation order) depends on the
-// weight shape only, never on the token count, so a token's output has the same bits
-// whichever block size computes it.
-static int choose_rt(int ntiles) {
-  for (int rt : {8, 4, 2}) {
-    if ((ntiles + rt - 1) / rt >= 296) return rt;
-  }
-  return 1;
+// ------------------------------------------------------------------ cluster linear
+// Verify-block form (T <= 16 tokens).  Clusters of CL_SIZE CTAs split K: CTA rank r
+// owns the K chunks [r * nch / CL_SIZE, (r + 1) * nch / CL_SIZE) of every row tile the
+// cluster handles (row tile t goes to cluster t mod clusters), so it stages only its
+// slice of the activations.  Its warps take whole tiles of the slice (tile i to warp
+// i mod CL_WARPS) and stream them from HBM through per-warp rings of bulk copies, all
+// requested before the PDL wait.  Partials meet through distributed shared memory: each
+// CTA stores its partial of tile i into the shared memory of rank i mod CL_SIZE, which
+// adds the CL_SIZE partials of its tiles in rank order after one cluster barrier: the
+// order (and partition) of the streaming kernel's K split with rt = 1, so every output
+// has the streaming kernel's bits.
+constexpr int CL_SIZE = 8;
+constexpr int CL_WARPS = 8;
+constexpr int CL_MAXT = 16;
+constexpr int CL_PAD = 32;      // 16-bit elements of row padding (conflict-free fragment loads)
+constexpr int CL_MAXS = 8;      // ring stages per warp, at most
+
+__device__ int32_t g_linear_wait_status;   // sticky: a bounded wait in a cluster linear expired
+
+struct ClArgs {
+  const __nv_bfloat16* x;
+  const uint8_t* w;
+  void* y;
+  int64_t ldy;
+  int tokens, n, k, mode;
+  int tpc;        // row tiles per cluster, at most (partials buffer)
+  int nst;        // ring stages per warp
+  long long limit;
+};
+
+__host__ __device__ inline size_t cl_head_bytes(int tpc) {
+  const size_t owned = (tpc + CL_SIZE - 1) / CL_SIZE;   // tiles a CTA finishes, at most
+  return CL_WARPS * CL_MAXS * 8 + owned * CL_SIZE * 32 * 8 * sizeof(float);
 }
+
+template <class Fmt>
+__global__ void __launch_bounds__(CL_WARPS * 32, 1) cluster_linear_kernel(ClArgs a) {
+  using OT = typename Fmt::OT;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int cid = blockIdx.x / CL_SIZE, ncl = gridDim.x / CL_SIZE;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int K = a.k, T = a.tokens;
+  const int nch = K / Fmt::KCHUNK;
+  const int c0 = rank * nch / CL_SIZE, c1 = (rank + 1) * nch / CL_SIZE, ncs = c1 - c0;
+  const int maxc = (nch + CL_SIZE - 1) / CL_SIZE;
+  const uint32_t sbytes = maxc * Fmt::CHB, wbytes = ncs * Fmt::CHB;
+  const int ntiles = a.n / 16;
+  const int my_tiles = cid < ntiles ? (ntiles - 1 - cid) / ncl + 1 : 0;
+  const int XS = maxc * Fmt::KCHUNK + CL_PAD;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  // partials received for the tiles this CTA finishes: [tpc / CL_SIZE][CL_SIZE][32][8]
+  float* part = reinterpret_cast<float*>(smem + CL_WARPS * CL_MAXS * 8);
+  OT* xs = reinterpret_cast<OT*>(smem + cl_head_bytes(a.tpc));                     // [T][XS]
+  uint8_t* ring = reinterpret_cast<uint8_t*>(xs) + (static_cast<size_t>(T) * XS * 2 + 127) / 128 * 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nst = a.nst;
+  uint8_t* wring = ring + static_cast<size_t>(warp) * nst * sbytes;
+  uint64_t* wbar = bars + warp * CL_MAXS;
+  const int my_w = warp < my_tiles ? (my_tiles - 1 - warp) / CL_WARPS + 1 : 0;   // tiles of this warp
+  if (lane == 0)
+    for (int i = 0; i < nst; ++i) mbar_init(wbar + i, 1);
+  fence_barrier_init();
+  __syncthreads();
+  auto src = [&](int j) {
+    const int t = cid + (warp + j * CL_WARPS) * ncl;
+    return a.w + Fmt::tile_offset(t, K, 0) + static_cast<int64_t>(c0) * Fmt::CHB;
+  };
+  auto issue = [&](int j) {
+    uint64_t* b = wbar + (j % nst);
+    fence_proxy_async();
+    mbar_arrive_expect_tx(b, wbytes);
+    bulk_g2s(wring + (j % nst) * sbytes, src(j), wbytes, b);
+  };
+  if (lane == 0 && wbytes)
+    for (int j = 0; j < nst && j < my_w; ++j) issue(j);   // weights: before the wait
+  pdl_wait();
+  pdl_trigger();
+  // this CTA's slice of the activations
+  const int xw = ncs * Fmt::KCHUNK;
+  for (int i = threadIdx.x; i < T * (xw / 8); i += blockDim.x) {
+    const int r = i / (xw / 8), c = (i % (xw / 8)) * 8;
+    cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(r) * K + c0 * Fmt::KCHUNK + c, true);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  if constexpr (!std::is_same<OT, __nv_bfloat16>::value) {
+    // fp16 operands: convert the slice once (each thread the vectors it copied)
+    for (int i = threadIdx.x; i < T * (xw / 8); i += blockDim.x) {
+      uint4* p = reinterpret_cast<uint4*>(xs + (i / (xw / 8)) * XS + (i % (xw / 8)) * 8);
+      *p = bf16x8_to_f16x8(*p);
+    }
+  }
+  __syncthreads();
+  const int gid = lane >> 2;
+  const bool two = T > 8;
+  const OT* xr[2];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) xr[nt] = xs + min(nt * 8 + gid, T - 1) * XS;
+  bool ok = true;
+  for (int j = 0; j < my_w; ++j) {
+    float acc[2][4];
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) acc[jj][0] = acc[jj][1] = acc[jj][2] = acc[jj][3] = 0.f;
+    if (wbytes && ok) {
+      if (!mbar_wait(wbar + (j % nst), static_cast<uint32_t>((j / nst) & 1), &g_linear_wait_status, a.limit)) {
+        if (lane == 0) {   // wait (bounded) for this warp's other copies in flight before giving up
+          for (int q = j + 1; q < min(j + nst, my_w); ++q) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(wbar + (q % nst), static_cast<uint32_t>((q / nst) & 1)))
+              if (clock64() - t0 > a.limit) break;
+          }
+        }
+        ok = false;
+      }
+      if (ok) {
+        const uint8_t* st = wring + (j % nst) * sbytes;
+        if constexpr (Fmt::SCALED) {
+          if (two) {
+            for (int c = 0; c < ncs; ++c) w4_smem_chunks<Fmt::KCHUNK, 1, 2, OT>(st + c * Fmt::CHB, xr, c * Fmt::KCHUNK, lane, acc);
+          } else {
+            for (int c = 0; c < ncs; ++c) w4_smem_chunks<Fmt::KCHUNK, 1, 1, OT>(st + c * Fmt::CHB, xr, c * Fmt::KCHUNK, lane, acc);
+          }
+        } else {
+          for (int c = 0; c < ncs; ++c) {
+            if (two) b16_smem_chunk<2>(st + c * Fmt::CHB, xr, c * Fmt::KCHUNK, lane, acc);
+            else b16_smem_chunk<1>(st + c * Fmt::CHB, xr, c * Fmt::KCHUNK, lane, acc);
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && j + nst < my_w) issue(j + nst);
+      }
+    }
+    // push the partial to the owner of tile i (rank i mod CL_SIZE), into its slot for
+    // this rank: remote stores, no round trip
+    const int i = warp + j * CL_WARPS;
+    float* dst = cluster.map_shared_rank(part, i % CL_SIZE) +
+                 ((static_cast<size_t>(i / CL_SIZE) * CL_SIZE + rank) * 32 + lane) * 8;
+    reinterpret_cast<float4*>(dst)[0] = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+  }
+  cluster.sync();   // every partial has reached its owner
+  {
+    const int l = threadIdx.x >> 3, e = threadIdx.x & 7;   // fragment lane, value
+    const int jj = e >> 2, r = e & 3;
+    const int t = jj * 8 + 2 * (l & 3) + (r & 1);
+    const int row = (l >> 2) + 8 * (r >> 1);
+    for (int i = rank; i < my_tiles; i += CL_SIZE) {
+      float v = 0.f;
+#pragma unroll
+      for (int sr = 0; sr < CL_SIZE; ++sr)
+        v += part[((static_cast<size_t>(i / CL_SIZE) * CL_SIZE + sr) * 32 + l) * 8 + e];
+      if (t < T) {
+        const int64_t o = static_cast<int64_t>(t) * a.ldy + (cid + i * ncl) * 16 + row;
+        if (a.mode == QW_OUT_F32) {
+          static_cast<float*>(a.y)[o] = v;
+        } else if (a.mode == QW_OUT_BF16) {
+          static_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(v);
+        } else {
+          __nv_bfloat16* y = static_cast<__nv_bfloat16*>(a.y);
+          y[o] = __float2bfloat16_rn(__bfloat162float(y[o]) + rbf(v));
+        }
+      }
+    }
+  }
+}
+
+static int cl_sm_count() {
+  static int counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
+struct ClPlan {
+  int ncl, tpc, nst;
+  size_t smem;
+};
+
+template <class Fmt>
+static bool cl_plan(const LinArgs& l, int ncl, ClPlan& p) {
+  constexpr size_t LIMIT = 227 * 1024;
+  const int ntiles = l.n / 16;
+  p.ncl = ncl;
+  p.tpc = (ntiles + ncl - 1) / ncl;
+  const int nch = l.k / Fmt::KCHUNK;
+  const int maxc = (nch + CL_SIZE - 1) / CL_SIZE;
+  const size_t sbytes = static_cast<size_t>(maxc) * Fmt::CHB;
+  const size_t fixed = cl_head_bytes(p.tpc) +
+                       (static_cast<size_t>(l.tokens) * (maxc * Fmt::KCHUNK + CL_PAD) * 2 + 127) / 128 * 128;
+  const int tpw = (p.tpc + CL_WARPS - 1) / CL_WARPS;   // tiles per warp, at most
+  p.nst = tpw < CL_MAXS ? tpw : CL_MAXS;
+  while (p.nst > 1 && fixed + CL_WARPS * p.nst * sbytes > LIMIT) --p.nst;
+  p.smem = fixed + CL_WARPS * p.nst * sbytes;
+  return p.smem <= LIMIT;
+}
+
+// Clusters of this kernel and shared-memory size that can be resident at once (8-CTA
+// clusters must fit in one GPC); cached per (device, kernel, size).
+template <class Fmt>
+static int cl_resident(size_t smem) {
+  static std::mutex mu;
+  static std::vector<std::pair<long long, int>> cache;
+  int dev = 0;
+  (void)cudaGetDevice(&dev);
+  const long long key = (static_cast<long long>(dev) << 40) | static_cast<long long>(smem);
+  std::lock_guard<std::mutex> guard(mu);
+  for (const auto& kv : cache)
+    if (kv.first == key) return kv.second;
+  cudaLaunchConfig_t occ = {};
+  occ.gridDim = dim3(CL_SIZE);
+  occ.blockDim = dim3(CL_WARPS * 32);
+  occ.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL_SIZE;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  occ.attrs = attr;
+  occ.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, cluster_linear_kernel<Fmt>, &occ) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = cl_sm_count() / CL_SIZE;
+  }
+  cache.emplace_back(key, n);
+  return n;
+}
+
+// The cluster linear when the block fits (T <= 16, aligned activations); otherwise
+// QW_ERR_UNSUPPORTED, and the caller streams.
+template <class Fmt>
+static int launch_linear_cluster(const LinArgs& l, cudaStream_t s) {
+  constexpr size_t LIMIT = 227 * 1024;
+  if (l.tokens < 1 || l.tokens > CL_MAXT || l.k % (8 * CL_SIZE) || (reinterpret_cast<uintptr_t>(l.x) & 15))
+    return QW_ERR_UNSUPPORTED;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(cluster_linear_kernel<Fmt>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(LIMIT));
+  });
+  if (err != cudaSuccess) return cuda_status(err, "cluster linear smem attribute");
+  const int ntiles = l.n / 16;
+  int ncl = cl_sm_count() / CL_SIZE;
+  if (ncl > ntiles) ncl = ntiles;
+  if (ncl < 1) return QW_ERR_UNSUPPORTED;
+  ClPlan p{};
+  if (!cl_plan<Fmt>(l, ncl, p)) return QW_ERR_UNSUPPORTED;
+  // no second wave of clusters: shrink to the resident count (more tiles per cluster)
+  for (int it = 0; it < 3; ++it) {
+    const int res = cl_resident<Fmt>(p.smem);
+    if (res >= p.ncl) break;
+    if (!cl_plan<Fmt>(l, res, p)) return QW_ERR_UNSUPPORTED;
+  }
+  ClArgs a{l.x, l.w, l.y, l.ldy, l.tokens, l.n, l.k, l.mode, p.tpc, p.nst, QW_WAIT_LIMIT};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.ncl * CL_SIZE);
+  cfg.blockDim = dim3(CL_WARPS * 32);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL_SIZE;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, cluster_linear_kernel<Fmt>, a);
+  if (e != cudaSuccess) return cuda_status(e, "linear (cluster)");
+  return QW_OK;
+}
+
+// One row tile per CTA, K split over its SG_WARPS warps: the partition (and the order
+// in which the partial sums are added) of the cluster kernel, so a token's output has
+// the same bits whichever kernel (block size) computes it.
+static int choose_rt(int /*ntiles*/) { return 1; }
 
 template <class Fmt, int NT, int PF, bool ARGMAX = false>
 static int launch_linear(const LinArgs& a0, cudaStream_t s) {
@@ -157,6 +438,9 @@ static int launch_linear(const LinArgs& a0, cudaStream_t s) {
 
 template <class Fmt, int PF>
 static int dispatch_nt(const LinArgs& a, cudaStream_t s) {
+  static_assert(SG_WARPS == CL_SIZE, "the streaming and cluster kernels share the 8-way K partition");
+  const int rc = launch_linear_cluster<Fmt>(a, s);
+  if (rc != QW_ERR_UNSUPPORTED) return rc;
   if (a.tokens > 16) return launch_linear<Fmt, 4, PF>(a, s);
   return launch_linear<Fmt, 2, PF>(a, s);
 }
@@ -201,9 +485,10 @@ extern "C" int qw_w4_linear(const void* x, const void* w_stream, void* y, int mo
             static_cast<int>(tokens), static_cast<int>(n), static_cast<int>(k), 0, mode};
   cudaStream_t s = as_stream(stream);
   switch (group) {
-    case 128: return dispatch_nt<W4Fmt<128>, 4>(a, s);
-    case 64: return dispatch_nt<W4Fmt<64>, 4>(a, s);
-    default: return dispatch_nt<W4Fmt<32>, 4>(a, s);
+    // fp16 MMA operands: the int4 decode then needs no conversion-unit work
+    case 128: return dispatch_nt<W4Fmt<128, __half>, 4>(a, s);
+    case 64: return dispatch_nt<W4Fmt<64, __half>, 4>(a, s);
+    default: return dispatch_nt<W4Fmt<32, __half>, 4>(a, s);
   }
 }
 

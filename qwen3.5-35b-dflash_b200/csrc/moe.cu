@@ -195,6 +195,67 @@ __device__ int warp_partition(const Q& q, int a, int b, int16_t* pos_l, int16_t*
   return lm < rm ? lm : rm;
 }
 
+// The same partition for ranges of at most 288 elements (b - (a - 1) <= 288, so every
+// router of <= 256 experts): all ballots first, then the stop positions from prefix
+// counts, then the pair scan unrolled, so no loop carries a memory dependency.
+__device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, int16_t* pos_r, int lane) {
+  constexpr int IT = 9;
+  const float p = q.v[a - 1];
+  const unsigned lt = (1u << lane) - 1u;
+  unsigned mL[IT], mR[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int i = a + 32 * it + lane;
+    mL[it] = __ballot_sync(0xffffffffu, i < b && !(q.v[i] > p));
+    const int j = b - 1 - 32 * it - lane;
+    mR[it] = __ballot_sync(0xffffffffu, j >= a - 1 && !(p > q.v[j]));
+  }
+  int nl = 0, nr = 0;
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    if ((mL[it] >> lane) & 1u) pos_l[nl + __popc(mL[it] & lt)] = static_cast<int16_t>(a + 32 * it + lane);
+    nl += __popc(mL[it]);
+    if ((mR[it] >> lane) & 1u) pos_r[nr + __popc(mR[it] & lt)] = static_cast<int16_t>(b - 1 - 32 * it - lane);
+    nr += __popc(mR[it]);
+  }
+  __syncwarp();
+  // pairs m with L[m] < R[m] form a prefix: its length is the first failing m
+  const int lim = nl < nr ? nl : nr;
+  int mstar = lim;
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int m = 32 * it + lane;
+    const unsigned bad = __ballot_sync(0xffffffffu, m < lim && !(pos_l[m] < pos_r[m]));
+    if (bad && mstar == lim) mstar = 32 * it + __ffs(bad) - 1;
+  }
+  for (int m = lane; m < mstar; m += 32) q.swap(pos_l[m], pos_r[m]);
+  __syncwarp();
+  if (mstar == 0) return pos_l[0];
+  const int lm = mstar < nl ? pos_l[mstar] : 1 << 30;
+  const int rm = pos_r[mstar - 1];
+  return lm < rm ? lm : rm;
+}
+
+// libstdc++ __insertion_sort of [first, first + n) under a > b, n <= 32, in parallel: it
+// is a stable descending sort, so element i goes to the number of elements greater than
+// it plus the number of equal ones before it.
+__device__ void warp_stable_sort_desc(const Q& q, int first, int n, int lane) {
+  float vi = 0.f;
+  int32_t ii = 0;
+  int rank = 0;
+  if (lane < n) {
+    vi = q.v[first + lane];
+    ii = q.i[first + lane];
+    for (int j = 0; j < n; ++j) {
+      const float vj = q.v[first + j];
+      rank += (vj > vi) || (j < lane && !(vj > vi) && !(vi > vj));
+    }
+  }
+  __syncwarp();
+  if (lane < n) { q.v[first + rank] = vi; q.i[first + rank] = ii; }
+  __syncwarp();
+}
+
 // torch.topk(values, k) order for one row held in q.v / q.i (initialized in index order).
 // Leaves the selected pairs in q[0..k).
 __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos_r, int lane) {
@@ -229,15 +290,18 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
     const int mid = first + (last - first) / 2;
     if (lane == 0) q_move_median_to_first(q, first, first + 1, mid, last - 1);
     __syncwarp();
-    const int cut = warp_partition(q, first + 1, last, pos_l, pos_r, lane);
+    const int cut = last - first <= 288 ? warp_partition_small(q, first + 1, last, pos_l, pos_r, lane)
+                                        : warp_partition(q, first + 1, last, pos_l, pos_r, lane);
     if (cut <= nth) first = cut;
     else last = cut;
   }
-  if (lane == 0) {
-    if (!heap_done) q_insertion_sort(q, first, last);
-    q_insertion_sort(q, 0, k - 1);
+  if (!heap_done) warp_stable_sort_desc(q, first, last - first, lane);
+  if (k - 1 <= 32) {
+    warp_stable_sort_desc(q, 0, k - 1, lane);
+  } else {
+    if (lane == 0) q_insertion_sort(q, 0, k - 1);
+    __syncwarp();
   }
-  __syncwarp();
 }
 
 // ------------------------------------------------------------------ route kernels

@@ -271,8 +271,8 @@ __device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int
 // Both operands are fp16: the weights are small integers and the activations are bf16
 // values, exact in fp16 (|x| in [2^-14, 65504]), so the products equal the bf16 ones and
 // the decode needs no conversion-unit instructions (dequant_w4_word_f16).
-template <int G, int NC, int NT>
-__device__ __forceinline__ void w4_smem_chunks(const uint8_t* chunk, const __half* const (&xr)[2], int k0,
+template <int G, int NC, int NT, typename OT = __half>
+__device__ __forceinline__ void w4_smem_chunks(const uint8_t* chunk, const OT* const (&xr)[2], int k0,
                                           int lane, float (&acc)[2][4]) {
   using Fmt = W4Fmt<G>;
   uint32_t w[NC][Fmt::WORDS];
@@ -311,9 +311,10 @@ __device__ __forceinline__ void w4_smem_chunks(const uint8_t* chunk, const __hal
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t a[4];
-        dequant_w4_word_f16(w[c][2 * q + h], a);
+        if constexpr (std::is_same<OT, __half>::value) dequant_w4_word_f16(w[c][2 * q + h], a);
+        else dequant_w4_word(w[c][2 * q + h], a);
 #pragma unroll
-        for (int j = 0; j < NT; ++j) mma16816<__half>(part[c][j], a, b[j][2 * h], b[j][2 * h + 1]);
+        for (int j = 0; j < NT; ++j) mma16816<OT>(part[c][j], a, b[j][2 * h], b[j][2 * h + 1]);
       }
     }
   }
