@@ -40,12 +40,14 @@ __global__ void residual_norm_kernel(NormArgs a) {
     __syncthreads();
   }
   float ss = 0.f;
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+#pragma unroll 8
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {   // unrolled: the row loads are in flight together
     const float v = __bfloat162float(h[i]);
     ss += v * v;
   }
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / a.H + a.eps);
+#pragma unroll 8
   for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
     const __nv_bfloat16 hv = h[i];
     const float g = rbf(__bfloat162float(a.gamma[i]) + 1.f);

@@ -958,7 +958,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ part, void* ws, ET*
 // residual_norm_kernel, and the optional feature tap (h, or the normed row).
 // One CTA per token; each thread owns runs of 4 columns (16-byte loads of the fp32
 // expert outputs, all k + 1 slots of a run issued before the ordered sum).
-constexpr int CN_THREADS = 256;
+constexpr int CN_THREADS = 512;
 
 template <int KMAX>
 __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
