@@ -54,6 +54,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // hint (ns) passes; a waiting warp then does not take issue slots from computing warps.
 constexpr uint32_t QW_SUSPEND_NS = 100000;
 
+// The same copy with an L2 cache policy (e.g. evict-first for weights read once).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy) : "memory");
+}
+
+// L2 policy: lines of this access are evicted first.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -89,12 +104,13 @@ struct WarpRing {
 
   __device__ __forceinline__ uint8_t* stage(int q) const { return buf + (q % NST) * stage_bytes; }
 
-  // Lane 0: start the copy of stage q (bytes <= stage_bytes) from src.
+  // Lane 0: start the copy of stage q (bytes <= stage_bytes) from src; weights read once
+  // are copied with an evict-first L2 policy so they do not displace prefetched lines.
   __device__ __forceinline__ void issue(int q, const void* src, uint32_t bytes) const {
     uint64_t* b = bar + (q % NST);
     fence_proxy_async();
     mbar_arrive_expect_tx(b, bytes);
-    bulk_g2s(stage(q), src, bytes, b);
+    bulk_g2s_hint(stage(q), src, bytes, b, l2_evict_first_policy());
   }
   // Whole warp: wait until stage q landed (bounded).
   __device__ __forceinline__ bool wait(int q, int32_t* status) const {
