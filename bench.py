@@ -343,8 +343,8 @@ def time_moe_up(eng, cfg, dev, iters: int = 50):
     ws = eng.moe_ws
     st = torch.cuda.current_stream(dev).cuda_stream
     so = eng.lib
-    lib.check(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, E, k, E, lib.QW_BF16,
-                              ws.data_ptr(), st))
+    lib.check(so.qw_moe_route_x(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, E, k, E, lib.QW_BF16,
+                                x.data_ptr(), H, g, ws.data_ptr(), st))
     args = (x.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(), lw.shared_gu.data_ptr(),
             lw.shared_down.data_ptr(), T, H, E, I, k, g, ws.data_ptr(), st)
     for _ in range(5):
@@ -408,7 +408,8 @@ def run_kernels(args):
         lib.check(rc)
 
     def route():
-        chk(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, Ex, k, Ex, lib.QW_BF16, ws.data_ptr(), s))
+        chk(so.qw_moe_route_x(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, Ex, k, Ex, lib.QW_BF16, x.data_ptr(), H,
+                              g, ws.data_ptr(), s))
 
     def up(lw):
         return lambda: chk(so.qw_moe_up_w4(x.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),

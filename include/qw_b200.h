@@ -187,6 +187,17 @@ int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t token
                  int64_t experts, int64_t top_k, int64_t shared_col, int act_dtype,
                  void* workspace, void* stream);
 
+/* qw_moe_route that also stages the expert input x (bf16 [T, hidden], the x the next
+ * expert call on this workspace receives; it must not change in between) for the
+ * gate/up kernel: fp16 copy and per-group sums, written once per block instead of by
+ * every gate/up CTA.  hidden and group as in that call; staged only for blocks of
+ * <= 16 tokens with hidden a multiple of 256 and x 16-byte aligned (otherwise this is
+ * qw_moe_route and the expert call converts x itself).  No counterpart in the
+ * reference: qw_moe_route's extra work, same outputs. */
+int qw_moe_route_x(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens,
+                   int64_t experts, int64_t top_k, int64_t shared_col, int act_dtype,
+                   const void* x, int64_t hidden, int32_t group, void* workspace, void* stream);
+
 /* The per-expert lists of a routed block in the workspace: active experts in
  * ascending id, and for each its (token, slot) pairs in ascending token (the order in
  * which fused_ops.py:165-172 visits them). */

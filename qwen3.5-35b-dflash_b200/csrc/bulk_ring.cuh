@@ -112,6 +112,15 @@ struct WarpRing {
     mbar_arrive_expect_tx(b, bytes);
     bulk_g2s_hint(stage(q), src, bytes, b, l2_evict_first_policy());
   }
+  // Lane 0: stage q from two sources, `bytes` each, into its two halves.
+  __device__ __forceinline__ void issue2(int q, const void* src0, const void* src1, uint32_t bytes) const {
+    uint64_t* b = bar + (q % NST);
+    fence_proxy_async();
+    mbar_arrive_expect_tx(b, 2 * bytes);
+    const uint64_t pol = l2_evict_first_policy();
+    bulk_g2s_hint(stage(q), src0, bytes, b, pol);
+    bulk_g2s_hint(stage(q) + bytes, src1, bytes, b, pol);
+  }
   // Whole warp: wait until stage q landed (bounded).
   __device__ __forceinline__ bool wait(int q, int32_t* status) const {
     return mbar_wait(bar + (q % NST), static_cast<uint32_t>((q / NST) & 1), status, limit);

@@ -65,6 +65,34 @@ __host__ __device__ inline RouteView route_view(void* ws, int T, int E, int k) {
   return v;
 }
 
+// Staged gate/up input of a routed block, right after the routing ints: a 256-byte
+// header (the x pointer and a shape key it was staged for), x16 [T, H] (the bf16
+// activations as fp16, saturated) and xsum [T, H / G] (group_xsum_f16 of each token's
+// K groups; room for G >= 32).  qw_moe_route_x writes it once per block so that the
+// gate/up kernel's CTAs need not each convert and sum x.
+__host__ __device__ inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
+__host__ __device__ inline int64_t stage_off(int T, int E, int k) { return align256(route_ints(T, E, k) * 4); }
+__host__ __device__ inline int64_t stage_bytes(int T, int H) {
+  return 256 + align256(static_cast<int64_t>(T) * H * 2) + align256(static_cast<int64_t>(T) * (H / 32) * 4);
+}
+__host__ __device__ inline unsigned long long stage_key(int T, int H, int G) {
+  return (static_cast<unsigned long long>(T) << 40) | (static_cast<unsigned long long>(H) << 8) |
+         static_cast<unsigned long long>(G);
+}
+struct StageView {
+  unsigned long long* tag;   // [0] x pointer (0: nothing staged), [1] stage_key
+  __half* x16;
+  float* xsum;
+};
+__host__ __device__ inline StageView stage_view(void* ws, int T, int E, int k, int H) {
+  uint8_t* p = static_cast<uint8_t*>(ws) + stage_off(T, E, k);
+  StageView v;
+  v.tag = reinterpret_cast<unsigned long long*>(p);
+  v.x16 = reinterpret_cast<__half*>(p + 256);
+  v.xsum = reinterpret_cast<float*>(p + 256 + align256(static_cast<int64_t>(T) * H * 2));
+  return v;
+}
+
 // ------------------------------------------------------------------ libstdc++ emulation
 struct Q {
   float* v;
@@ -76,18 +104,14 @@ struct Q {
   }
 };
 
-__device__ void q_move_median_to_first(const Q& q, int result, int a, int b, int c) {
-  if (q.gt(a, b)) {
-    if (q.gt(b, c)) q.swap(result, b);
-    else if (q.gt(a, c)) q.swap(result, c);
-    else q.swap(result, a);
-  } else if (q.gt(a, c)) {
-    q.swap(result, a);
-  } else if (q.gt(b, c)) {
-    q.swap(result, c);
-  } else {
-    q.swap(result, b);
-  }
+// libstdc++ __move_median_to_first under a > b: every lane makes the choice from one
+// parallel read of the three values, lane 0 swaps (the warp synchronizes after).
+__device__ __forceinline__ void warp_move_median_to_first(const Q& q, int result, int a, int b, int c, int lane) {
+  const float va = q.v[a], vb = q.v[b], vc = q.v[c];
+  int m;
+  if (va > vb) m = vb > vc ? b : (va > vc ? c : a);
+  else m = va > vc ? a : (vb > vc ? c : b);
+  if (lane == 0) q.swap(result, m);
 }
 
 __device__ void q_insertion_sort(const Q& q, int first, int last) {
@@ -202,21 +226,28 @@ __device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, in
   constexpr int IT = 9;
   const float p = q.v[a - 1];
   const unsigned lt = (1u << lane) - 1u;
+  const int itn = (b - a + 32) / 32;   // 32-wide passes over [a - 1, b)
   unsigned mL[IT], mR[IT];
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    const int i = a + 32 * it + lane;
-    mL[it] = __ballot_sync(0xffffffffu, i < b && !(q.v[i] > p));
-    const int j = b - 1 - 32 * it - lane;
-    mR[it] = __ballot_sync(0xffffffffu, j >= a - 1 && !(p > q.v[j]));
+    if (it < itn) {
+      const int i = a + 32 * it + lane;
+      mL[it] = __ballot_sync(0xffffffffu, i < b && !(q.v[i] > p));
+      const int j = b - 1 - 32 * it - lane;
+      mR[it] = __ballot_sync(0xffffffffu, j >= a - 1 && !(p > q.v[j]));
+    } else {
+      mL[it] = mR[it] = 0u;
+    }
   }
   int nl = 0, nr = 0;
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    if ((mL[it] >> lane) & 1u) pos_l[nl + __popc(mL[it] & lt)] = static_cast<int16_t>(a + 32 * it + lane);
-    nl += __popc(mL[it]);
-    if ((mR[it] >> lane) & 1u) pos_r[nr + __popc(mR[it] & lt)] = static_cast<int16_t>(b - 1 - 32 * it - lane);
-    nr += __popc(mR[it]);
+    if (it < itn) {
+      if ((mL[it] >> lane) & 1u) pos_l[nl + __popc(mL[it] & lt)] = static_cast<int16_t>(a + 32 * it + lane);
+      nl += __popc(mL[it]);
+      if ((mR[it] >> lane) & 1u) pos_r[nr + __popc(mR[it] & lt)] = static_cast<int16_t>(b - 1 - 32 * it - lane);
+      nr += __popc(mR[it]);
+    }
   }
   __syncwarp();
   // pairs m with L[m] < R[m] form a prefix: its length is the first failing m
@@ -224,9 +255,11 @@ __device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, in
   int mstar = lim;
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    const int m = 32 * it + lane;
-    const unsigned bad = __ballot_sync(0xffffffffu, m < lim && !(pos_l[m] < pos_r[m]));
-    if (bad && mstar == lim) mstar = 32 * it + __ffs(bad) - 1;
+    if (32 * it < lim) {
+      const int m = 32 * it + lane;
+      const unsigned bad = __ballot_sync(0xffffffffu, m < lim && !(pos_l[m] < pos_r[m]));
+      if (bad && mstar == lim) mstar = 32 * it + __ffs(bad) - 1;
+    }
   }
   for (int m = lane; m < mstar; m += 32) q.swap(pos_l[m], pos_r[m]);
   __syncwarp();
@@ -288,7 +321,7 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
     }
     --depth;
     const int mid = first + (last - first) / 2;
-    if (lane == 0) q_move_median_to_first(q, first, first + 1, mid, last - 1);
+    warp_move_median_to_first(q, first, first + 1, mid, last - 1, lane);
     __syncwarp();
     const int cut = last - first <= 288 ? warp_partition_small(q, first + 1, last, pos_l, pos_r, lane)
                                         : warp_partition(q, first + 1, last, pos_l, pos_r, lane);
@@ -316,14 +349,45 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
 // 2 * (E + 2) int16.
 constexpr int ROUTE_MAXJ = 8;  // logits per lane on the fast path (E <= 256)
 
+// One token's row of x -> x16 and its group sums (warp, lanes = 8-element segments).
+template <int G>
+__device__ __forceinline__ void stage_row(const __nv_bfloat16* xr, __half* dst, float* xs, int H, int lane) {
+  for (int b = 0; b < H / 256; ++b) {
+    const int seg = b * 32 + lane;
+    const uint4 v = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(xr + seg * 8)));
+    *reinterpret_cast<uint4*>(dst + seg * 8) = v;
+    const float xg = warp_group_xsum_f16<G>(sum8_f16(v), lane);
+    if (lane % (G / 8) == 0) xs[seg * 8 / G] = xg;
+  }
+}
+
 template <typename LT>
 __global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ logits, int64_t ldl, int T, int E,
-                                                       int k, int shared_col, int act_is_f16, void* ws) {
+                                                       int k, int shared_col, int act_is_f16, void* ws,
+                                                       const __nv_bfloat16* __restrict__ x, int H, int G) {
   extern __shared__ __align__(16) uint8_t smem[];
+  const int lane = threadIdx.x;
+  // x (older than the router logits) is staged for the gate/up kernel before the wait;
+  // the header is rewritten on every call so that nothing stale is taken for staged
+  {
+    const StageView sv = stage_view(ws, T, E, k, H);
+    const int t = blockIdx.x;
+    if (x != nullptr) {
+      const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * H;
+      __half* dst = sv.x16 + static_cast<int64_t>(t) * H;
+      float* xs = sv.xsum + static_cast<int64_t>(t) * (H / G);
+      if (G == 128) stage_row<128>(xr, dst, xs, H, lane);
+      else if (G == 64) stage_row<64>(xr, dst, xs, H, lane);
+      else stage_row<32>(xr, dst, xs, H, lane);
+    }
+    if (t == 0 && lane == 0) {
+      sv.tag[0] = reinterpret_cast<unsigned long long>(x);
+      sv.tag[1] = x != nullptr ? stage_key(T, H, G) : 0ull;
+    }
+  }
   pdl_wait();   // the router logits come from the predecessor
   pdl_trigger();
   RouteView rv = route_view(ws, T, E, k);
-  const int lane = threadIdx.x;
   Q q{reinterpret_cast<float*>(smem), reinterpret_cast<int32_t*>(smem + E * 4)};
   int16_t* pos_l = reinterpret_cast<int16_t*>(smem + E * 8);
   int16_t* pos_r = pos_l + E + 2;
@@ -331,58 +395,115 @@ __global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ l
   const LT* row = logits + static_cast<int64_t>(t) * ldl;
   float sel_v = -INFINITY;   // lane r < k: value of the r-th selected expert
   int sel_i = 0;             //             and its index
-  float mx, z;
+  float mx = -INFINITY, z = 0.f;
   bool exact = E > 32 * ROUTE_MAXJ;
+  float v[ROUTE_MAXJ];
   if (!exact) {
-    float v[ROUTE_MAXJ];
-    mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < ROUTE_MAXJ; ++j) {
       const int e = lane + 32 * j;
       v[j] = e < E ? to_f(row[e]) : -INFINITY;
-      mx = fmaxf(mx, v[j]);
     }
-    mx = warp_max(mx);
-    z = 0.f;
-#pragma unroll
-    for (int j = 0; j < ROUTE_MAXJ; ++j)
-      if (lane + 32 * j < E) z += __expf(v[j] - mx);
-    z = warp_sum(z);
-    unsigned taken = 0u;
-    float prev = 0.f;
     const int rounds = k < E ? k + 1 : k;
-    for (int r = 0; r < rounds; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
+    if constexpr (sizeof(LT) == 2) {
+      // 16-bit logits: (value, index) packed in one word, the value's float_key with its
+      // 12 low bits cleared (they are all zeros or all ones for a 16-bit type, so order
+      // and equality of values are kept) above 4095 - index, so that each arg-max round
+      // is one redux.sync; 0 is below every packed value and marks taken entries
+      uint32_t pk[ROUTE_MAXJ];
+      bool nan = false;
 #pragma unroll
       for (int j = 0; j < ROUTE_MAXJ; ++j) {
         const int e = lane + 32 * j;
-        if (e < E && !(taken >> j & 1u) && (bv < v[j] || bi == 0x7fffffff)) { bv = v[j]; bi = e; }
+        nan |= e < E && isnan(v[j]);
+        const float vc = v[j] == 0.f ? 0.f : v[j];   // -0 and +0 compare equal: one key
+        pk[j] = e < E ? ((float_key(vc) & 0xFFFFF000u) | (0xFFFu - static_cast<uint32_t>(e))) : 0u;
       }
+      if (__any_sync(0xffffffffu, nan)) {
+        exact = true;   // NaN among the logits: the emulation reproduces their order
+      } else {
+        uint32_t prev = 0u;
+        for (int r = 0; r < rounds; ++r) {
+          uint32_t loc = 0u;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+          for (int j = 0; j < ROUTE_MAXJ; ++j) loc = max(loc, pk[j]);
+          const uint32_t best = __reduce_max_sync(0xffffffffu, loc);
+          // a tie anywhere among the k+1 largest: use the exact emulation
+          if (r > 0 && (best >> 12) == (prev >> 12)) { exact = true; break; }
+          prev = best;
+          const int e = 0xFFF - static_cast<int>(best & 0xFFFu);
+          const uint32_t kv = best & 0xFFFFF000u;
+          const float bv = __uint_as_float((kv & 0x80000000u) ? (kv ^ 0x80000000u) : ~(kv | 0xFFFu));
+          if (r == 0) mx = bv;
+          if (r < k && lane == r) { sel_v = bv; sel_i = e; }
+          if ((e & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < ROUTE_MAXJ; ++j)
+              if (j == (e >> 5)) pk[j] = 0u;
+          }
+        }
       }
-      // a tie (or a NaN) anywhere among the k+1 largest: use the exact emulation
-      if (r > 0 && !(prev > bv)) { exact = true; break; }
-      prev = bv;
-      if (r < k && lane == r) { sel_v = bv; sel_i = bi; }
-      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    } else {
+#pragma unroll
+      for (int j = 0; j < ROUTE_MAXJ; ++j) mx = fmaxf(mx, v[j]);
+      mx = warp_max(mx);
+      unsigned taken = 0u;
+      float prev = 0.f;
+      for (int r = 0; r < rounds; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < ROUTE_MAXJ; ++j) {
+          const int e = lane + 32 * j;
+          if (e < E && !(taken >> j & 1u) && (bv < v[j] || bi == 0x7fffffff)) { bv = v[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+        }
+        // a tie (or a NaN) anywhere among the k+1 largest: use the exact emulation
+        if (r > 0 && !(prev > bv)) { exact = true; break; }
+        prev = bv;
+        if (r < k && lane == r) { sel_v = bv; sel_i = bi; }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      }
+    }
+    if (!exact) {
+#pragma unroll
+      for (int j = 0; j < ROUTE_MAXJ; ++j)
+        if (lane + 32 * j < E) z += __expf(v[j] - mx);
+      z = warp_sum(z);
     }
   }
   if (exact) {
+    // the row into shared memory: from the registers when the fast path loaded it
+    const bool in_regs = E <= 32 * ROUTE_MAXJ;
     mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) {
-      const float v = to_f(row[e]);
-      q.v[e] = v;
-      q.i[e] = e;
-      mx = fmaxf(mx, v);
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < ROUTE_MAXJ; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) { q.v[e] = v[j]; q.i[e] = e; mx = fmaxf(mx, v[j]); }
+      }
+    } else {
+      for (int e = lane; e < E; e += 32) {
+        const float ve = to_f(row[e]);
+        q.v[e] = ve;
+        q.i[e] = e;
+        mx = fmaxf(mx, ve);
+      }
     }
     mx = warp_max(mx);
     z = 0.f;
-    for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < ROUTE_MAXJ; ++j)
+        if (lane + 32 * j < E) z += __expf(v[j] - mx);
+    } else {
+      for (int e = lane; e < E; e += 32) z += __expf(q.v[e] - mx);
+    }
     z = warp_sum(z);
     __syncwarp();
     warp_topk(q, E, k, pos_l, pos_r, lane);
@@ -713,9 +834,10 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
   int* scratch = reinterpret_cast<int*>(smem + XT_BAR_BYTES + (sizeof(XtRoute) + 127) / 128 * 128);
   const int H = a.H, I = a.I, T = a.T;
   const int XS = H + XT_PAD;
+  const int nch = H / G, cps = nch < XT_UP_CPS ? nch : XT_UP_CPS;
   __half* xs = reinterpret_cast<__half*>(smem + xt_head_bytes(a.E));
-  uint8_t* ring_base = reinterpret_cast<uint8_t*>(xs) + ((static_cast<size_t>(T) * XS * 2 + 127) / 128) * 128;
-  const int nch = H / G, cps = nch < XT_UP_CPS ? nch : XT_UP_CPS, spt = nch / cps;
+  float* xsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + ((static_cast<size_t>(T) * XS * 2 + 127) / 128) * 128);
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(xsum) + ((static_cast<size_t>(T) * nch * 4 + 127) / 128) * 128;
   const uint32_t sbytes = cps * Fmt::CHB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
@@ -723,15 +845,30 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
     for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
   fence_barrier_init();
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  pdl_wait();   // the top-k indices and the staged x come from the predecessor (route)
+  pdl_trigger();
   // x -> shared memory (cp.async), overlapped with the list building and the first
-  // weight stages below
-  for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
-    const int r = i / (H / 8), c = (i % (H / 8)) * 8;
-    cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(r) * H + c, true);
+  // weight stages below: as fp16 with its group sums when the route kernel staged this
+  // x (qw_moe_route_x), else as bf16, converted and summed here
+  const StageView sv = stage_view(a.ws, T, a.E, a.k, H);
+  const bool staged = sv.tag[0] == reinterpret_cast<unsigned long long>(a.x) && sv.tag[1] == stage_key(T, H, G);
+  if (staged) {
+    for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
+      const int r = i / (H / 8), c = (i % (H / 8)) * 8;
+      cp_async16(xs + r * XS + c, sv.x16 + static_cast<int64_t>(r) * H + c, true);
+    }
+    if ((T * nch) % 4 == 0) {
+      for (int i = threadIdx.x; i < T * nch / 4; i += blockDim.x) cp_async16(xsum + 4 * i, sv.xsum + 4 * i, true);
+    } else {
+      for (int i = threadIdx.x; i < T * nch; i += blockDim.x) xsum[i] = sv.xsum[i];
+    }
+  } else {
+    for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
+      const int r = i / (H / 8), c = (i % (H / 8)) * 8;
+      cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(r) * H + c, true);
+    }
   }
   cp_async_commit();
-  pdl_wait();   // the top-k indices come from the predecessor (route); x is older
-  pdl_trigger();
   xt_build_route(rt, scratch, rv, T, a.E, a.k, blockIdx.x == 0);
   __syncthreads();
   const int J = I / 16;
@@ -739,25 +876,58 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
   const int nu = nslots * J;
   const int gw = blockIdx.x * XT_UP_WARPS + warp, nw = gridDim.x * XT_UP_WARPS;
   const int my_units = gw < nu ? (nu - 1 - gw) / nw + 1 : 0;
-  const int Q = my_units * 2 * spt;
-  auto src = [&](int q) -> const uint8_t* {
-    const int u = gw + (q / (2 * spt)) * nw, part = q % (2 * spt);
-    const uint8_t* w;
-    int np, pb;
-    xt_slot(a, rt, u / J, true, w, np, pb);
-    const int tile = (part / spt) * J + u % J;
-    return w + Fmt::tile_offset(tile, H, 0) + static_cast<int64_t>(part % spt) * sbytes;
+  // stage s of a unit: the gate chunks [s * hc, s * hc + hc) and the up chunks of the
+  // same k range (two copies, the up half second); spu stages per unit
+  const int hc = cps / 2, spu = nch / hc;
+  const uint32_t hbytes = hc * Fmt::CHB;
+  const int64_t tbytes = Fmt::tile_offset(1, H, 0);   // one row tile, all chunks
+  const int Q = my_units * spu;
+  // lane 0's copy cursor: the warp's unit cu_i, its stage cu_s, the unit's gate tile
+  int cu_i = 0, cu_s = 0;
+  const uint8_t* cu_w = nullptr;
+  auto cursor_unit = [&]() {
+    const int u = gw + cu_i * nw;
+    int np_, pb_;
+    xt_slot(a, rt, u / J, true, cu_w, np_, pb_);
+    cu_w += Fmt::tile_offset(u % J, H, 0);
   };
-  if (lane == 0)
-    for (int q = 0; q < XT_NST && q < Q; ++q) ring.issue(q, src(q), sbytes);
-  cp_async_wait<0>();
-  // x: bf16 -> fp16 in place (each thread converts the vectors it copied)
-  for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
-    uint4* p = reinterpret_cast<uint4*>(xs + (i / (H / 8)) * XS + (i % (H / 8)) * 8);
-    *p = bf16x8_to_f16x8(*p);
+  auto issue_next = [&](int qq) {
+    ring.issue2(qq, cu_w + cu_s * hbytes, cu_w + J * tbytes + cu_s * hbytes, hbytes);
+    if (++cu_s == spu) {
+      cu_s = 0;
+      if (++cu_i < my_units) cursor_unit();
+    }
+  };
+  if (lane == 0 && my_units > 0) {
+    cursor_unit();
+    for (int qq = 0; qq < XT_NST && qq < Q; ++qq) issue_next(qq);
   }
-  __syncthreads();
-  const int gid = lane >> 2;
+  cp_async_wait<0>();
+  // unstaged x: bf16 -> fp16 in place (each thread converts the vectors it copied), and
+  // the per (token, K group) activation sums of the nibble MMA's offset term: with H a
+  // multiple of 256 a warp holds whole groups of one row and sums them with shuffles
+  if (staged) {
+    __syncthreads();
+  } else if (H % 256 == 0) {
+    for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
+      const int r = i / (H / 8), sg = i % (H / 8);
+      uint4* p = reinterpret_cast<uint4*>(xs + r * XS + sg * 8);
+      const uint4 v = bf16x8_to_f16x8(*p);
+      *p = v;
+      const float xg = warp_group_xsum_f16<G>(sum8_f16(v), lane);
+      if (sg % (G / 8) == 0) xsum[r * nch + sg / (G / 8)] = xg;
+    }
+    __syncthreads();
+  } else {
+    for (int i = threadIdx.x; i < T * (H / 8); i += blockDim.x) {
+      uint4* p = reinterpret_cast<uint4*>(xs + (i / (H / 8)) * XS + (i % (H / 8)) * 8);
+      *p = bf16x8_to_f16x8(*p);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * nch; i += blockDim.x) xsum[i] = group_xsum_f16<G>(xs + (i / nch) * XS + (i % nch) * G);
+    __syncthreads();
+  }
+  const int gid = lane >> 2, tig = lane & 3;
   int q = 0;
   for (int i = 0; i < my_units; ++i) {
     const int u = gw + i * nw, j = u % J;
@@ -766,27 +936,37 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
     xt_slot(a, rt, u / J, true, w, np, pb);
     const bool two = np > 8;
     const __half* xr[2];
+    const float* xq[2][2];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const int idx = min(nt * 8 + gid, np - 1);
       xr[nt] = xs + (pb < 0 ? idx : rt.tok[pb + idx]) * XS;
-    }
-    float acc[2][2][4];
 #pragma unroll
-    for (int g = 0; g < 2; ++g)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) acc[g][nt][0] = acc[g][nt][1] = acc[g][nt][2] = acc[g][nt][3] = 0.f;
-#pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      for (int sub = 0; sub < spt; ++sub, ++q) {
-        if (!ring.wait(q, args.status)) {
-          if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
-          return;
-        }
-        w4_smem_run<G>(ring.stage(q), cps, xr, sub * cps * G, lane, two, acc[g]);
-        __syncwarp();
-        if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
+      for (int e = 0; e < 2; ++e) {
+        const int ci = min(nt * 8 + 2 * tig + e, np - 1);
+        xq[nt][e] = xsum + (pb < 0 ? ci : rt.tok[pb + ci]) * nch;
       }
+    }
+    float accg[2][4], accu[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) accg[nt][r] = accu[nt][r] = 0.f;
+    for (int s = 0; s < spu; ++s, ++q) {
+      if (!ring.wait(q, args.status)) {
+        if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
+        return;
+      }
+      const uint8_t* st = ring.stage(q);
+      for (int c = 0; c < hc; ++c)
+        w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[0], (s * hc + c) * G, xq[0][0], xq[0][1],
+                         s * hc + c, lane, accg[0], accu[0]);
+      if (two)
+        for (int c = 0; c < hc; ++c)
+          w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[1], (s * hc + c) * G, xq[1][0],
+                           xq[1][1], s * hc + c, lane, accg[1], accu[1]);
+      __syncwarp();
+      if (lane == 0 && q + XT_NST < Q) issue_next(q + XT_NST);
     }
     // h = silu(gate) * up in the reference's rounding order
 #pragma unroll
@@ -795,7 +975,7 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
       for (int r = 0; r < 4; ++r) {
         const int tl = frag_tok(lane, nt, r);
         if (tl < np) {
-          const float gr = rbf(acc[0][nt][r]), ur = rbf(acc[1][nt][r]);
+          const float gr = rbf(accg[nt][r]), ur = rbf(accu[nt][r]);
           const float h = rbf(rbf(silu_f(gr)) * ur);
           const int64_t hrow = pb < 0 ? static_cast<int64_t>(T) * a.k + tl : pb + tl;
           // h is a bf16 value; stored as fp16 (exact) for the bulk down kernel's operand
@@ -1058,7 +1238,7 @@ __global__ void router_dense_kernel(const ET* __restrict__ x, const ET* __restri
 // ------------------------------------------------------------------ host launchers
 template <typename LT>
 static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, int shared_col,
-                        int act_is_f16, void* ws, cudaStream_t s) {
+                        int act_is_f16, void* ws, const void* x, int H, int G, cudaStream_t s) {
   const size_t smem = ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
@@ -1068,7 +1248,7 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   if (err != cudaSuccess) return cuda_status(err, "route smem attribute");
   if (smem > 64 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
   QW_LAUNCH_PDL("moe route", route_topk_kernel<LT>, dim3(T), dim3(32), smem, s, static_cast<const LT*>(logits), ldl,
-                T, E, k, shared_col, act_is_f16, ws);
+                T, E, k, shared_col, act_is_f16, ws, static_cast<const __nv_bfloat16*>(x), H, G);
   return QW_OK;
 }
 
@@ -1139,8 +1319,8 @@ static XtPlan xt_plan(const MoeArgs<__nv_bfloat16>& a) {
   const int nch = a.H / G;
   const int cps = nch < XT_UP_CPS ? nch : XT_UP_CPS;
   p.up_smem = xt_head_bytes(a.E) + (static_cast<size_t>(a.T) * (a.H + XT_PAD) * 2 + 127) / 128 * 128 +
-              static_cast<size_t>(XT_UP_WARPS) * XT_NST * cps * CHB;
-  p.up_ok = small && nch % cps == 0 && p.up_smem <= XT_SMEM_LIMIT;
+              (static_cast<size_t>(a.T) * nch * 4 + 127) / 128 * 128 + static_cast<size_t>(XT_UP_WARPS) * XT_NST * cps * CHB;
+  p.up_ok = small && nch % cps == 0 && cps % 2 == 0 && p.up_smem <= XT_SMEM_LIMIT;
   const int cpt = a.I / G;
   p.down_ok = false;
   if (small && cpt >= 1 && cpt <= XT_DN_CPS && XT_DN_CPS % cpt == 0) {
@@ -1207,8 +1387,7 @@ extern "C" int64_t qw_moe_workspace_bytes(int64_t tokens, int64_t hidden, int64_
                                           int64_t top_k) {
   if (tokens < 0 || hidden <= 0 || experts <= 0 || inter <= 0 || top_k <= 0) return -1;
   const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
-  int64_t b = route_ints(T, E, k) * 4;
-  b = (b + 255) / 256 * 256;
+  int64_t b = stage_off(T, E, k) + stage_bytes(T, static_cast<int>(hidden));   // routing ints, staged x
   b += (static_cast<int64_t>(T) * k + T) * inter * 2;          // hbuf (16-bit)
   b = (b + 255) / 256 * 256;
   b += static_cast<int64_t>(T) * (k + 1) * hidden * 4;          // part
@@ -1227,7 +1406,7 @@ static WsParts split_ws(void* ws, int T, int H, int E, int I, int k) {
   uint8_t* p = static_cast<uint8_t*>(ws);
   WsParts w;
   w.route = p;
-  int64_t off = (route_ints(T, E, k) * 4 + 255) / 256 * 256;
+  int64_t off = stage_off(T, E, k) + stage_bytes(T, H);
   w.hbuf = p + off;
   off += (static_cast<int64_t>(T) * k + T) * I * 2;
   off = (off + 255) / 256 * 256;
@@ -1237,22 +1416,46 @@ static WsParts split_ws(void* ws, int T, int H, int E, int I, int k) {
   return w;
 }
 
-extern "C" int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
-                            int64_t top_k, int64_t shared_col, int act_dtype, void* workspace, void* stream) {
+static int route_entry(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
+                       int64_t top_k, int64_t shared_col, int act_dtype, const void* x, int64_t hidden,
+                       int32_t group, void* workspace, void* stream) {
   QW_CHECK_ARG(logits && workspace, "moe_route: null pointer");
   QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && experts >= 1 && experts <= 1024 && top_k >= 1 &&
                    top_k <= 16 && top_k <= experts && ldl >= experts,
                "MoE needs compatible expert weights and a valid top_k");
   QW_CHECK_ARG(act_dtype == QW_BF16 || act_dtype == QW_F16, "moe_route: activation dtype");
   const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
+  int H = 0, G = 0;
+  if (x != nullptr) {
+    QW_CHECK_ARG(hidden >= 256 && hidden <= (1 << 20) && (group == 32 || group == 64 || group == 128),
+                 "moe_route_x: invalid hidden / group");
+    H = static_cast<int>(hidden);
+    G = group;
+    // staged only where the gate/up kernel that reads it runs (blocks of <= 16 tokens)
+    // and the row layout suits a warp per token; otherwise the header says "nothing"
+    if (!(T <= XT_MAXT && H % 256 == 0 && act_dtype == QW_BF16 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)) x = nullptr;
+  }
+  if (x == nullptr) H = 256, G = 32;   // header only
   cudaStream_t s = as_stream(stream);
-  if (logit_dtype == QW_BF16)
-    return launch_route<__nv_bfloat16>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
-  if (logit_dtype == QW_F16)
-    return launch_route<__half>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
-  if (logit_dtype == QW_F32)
-    return launch_route<float>(logits, ldl, T, E, k, static_cast<int>(shared_col), act_dtype == QW_F16, workspace, s);
+  const int sc = static_cast<int>(shared_col), f16 = act_dtype == QW_F16;
+  if (logit_dtype == QW_BF16) return launch_route<__nv_bfloat16>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s);
+  if (logit_dtype == QW_F16) return launch_route<__half>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s);
+  if (logit_dtype == QW_F32) return launch_route<float>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s);
   return fail(QW_ERR_ARG, "moe_route: bad logit dtype");
+}
+
+extern "C" int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
+                            int64_t top_k, int64_t shared_col, int act_dtype, void* workspace, void* stream) {
+  return route_entry(logits, logit_dtype, ldl, tokens, experts, top_k, shared_col, act_dtype, nullptr, 0, 0,
+                     workspace, stream);
+}
+
+extern "C" int qw_moe_route_x(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
+                              int64_t top_k, int64_t shared_col, int act_dtype, const void* x, int64_t hidden,
+                              int32_t group, void* workspace, void* stream) {
+  QW_CHECK_ARG(x != nullptr, "moe_route_x: null x");
+  return route_entry(logits, logit_dtype, ldl, tokens, experts, top_k, shared_col, act_dtype, x, hidden, group,
+                     workspace, stream);
 }
 
 extern "C" int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t experts, int64_t top_k, void* stream) {
@@ -1403,13 +1606,13 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
         static_cast<const __nv_bfloat16*>(hidden), static_cast<const __nv_bfloat16*>(router),
         static_cast<__nv_bfloat16*>(w.logits), T, H, E);
     QW_LAUNCH_CHECK("moe router");
-    st = launch_route<__nv_bfloat16>(w.logits, E, T, E, k, -1, 0, w.route, s);
+    st = launch_route<__nv_bfloat16>(w.logits, E, T, E, k, -1, 0, w.route, nullptr, 256, 32, s);
   } else {
     router_dense_kernel<__half><<<rblocks, 256, 0, s>>>(static_cast<const __half*>(hidden),
                                                         static_cast<const __half*>(router),
                                                         static_cast<__half*>(w.logits), T, H, E);
     QW_LAUNCH_CHECK("moe router");
-    st = launch_route<__half>(w.logits, E, T, E, k, -1, 1, w.route, s);
+    st = launch_route<__half>(w.logits, E, T, E, k, -1, 1, w.route, nullptr, 256, 32, s);
   }
   if (st) return st;
   st = launch_route_lists(T, E, k, w.route, s);

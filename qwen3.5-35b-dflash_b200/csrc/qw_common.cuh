@@ -220,6 +220,22 @@ __device__ __forceinline__ void dequant_w4_word(uint32_t w, uint32_t (&a)[4]) {
   }
 }
 
+// The same word as fp16 A fragments with no arithmetic at all: each fp16 lane keeps its
+// stored nibble n in place, so nibbles 0, 2 (bits 0-3 of a half) read as the subnormal
+// n * 2^-24 and nibbles 1, 3 (bits 4-7) as n * 2^-20 -- exact values the MMA multiplies
+// exactly.  Register j holds nibbles (j, j + 4) as in dequant_w4_word_f16, so registers
+// 0, 2 (A rows gid) carry the 2^-24 lanes and registers 1, 3 (rows gid + 8) the 2^-20
+// lanes; the caller restores q = n - 8 per row from the MMA sum P and the activation
+// sum X of the same k range: sum (n - 8) x = 2^24 P - 8 X (rows gid), 2^20 P - 8 X
+// (rows gid + 8).
+__device__ __forceinline__ void w4_nibbles_f16(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t w8 = w >> 8;
+  a[0] = w & 0x000F000Fu;
+  a[1] = w & 0x00F000F0u;
+  a[2] = w8 & 0x000F000Fu;
+  a[3] = w8 & 0x00F000F0u;
+}
+
 // The same word decoded to fp16 A fragments with no conversion-unit work: masking
 // nibbles into the mantissa of fp16 1024.0 (0x6400) gives 1024 + u (nibbles 0, 2 of
 // each half) or 1024 + 16u (nibbles 1, 3, left in place), then one HADD2 / HFMA2

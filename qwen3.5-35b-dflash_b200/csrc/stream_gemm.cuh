@@ -264,6 +264,170 @@ __device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int
   stream_tiles<Fmt, NT, PF, 1, PDL>(tiles, ld, c0, c1, lane, x, a1);
 }
 
+// Sum of 8 packed fp16 values in fp32, in order.
+__device__ __forceinline__ float sum8_f16(uint4 v) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
+    s += f.x;
+    s += f.y;
+  }
+  return s;
+}
+
+// Sum X of one token's G fp16 activations of one K group, in fp32 and in a fixed order
+// that the lanes of an MMA fragment group (and a warp converting the activations)
+// reproduce: p(q, t) = the 8 values at k = 32q + 8t .. +7 summed in order, S_t = p(0, t)
+// + p(1, t) + ... in order of q, X = (S0 + S1) + (S2 + S3).  p: 16-byte aligned.
+template <int G>
+__device__ __forceinline__ float group_xsum_f16(const __half* p) {
+  float s[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    s[t] = sum8_f16(*reinterpret_cast<const uint4*>(p + 8 * t));
+#pragma unroll
+    for (int q = 1; q < G / 32; ++q) s[t] += sum8_f16(*reinterpret_cast<const uint4*>(p + 32 * q + 8 * t));
+  }
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+// The same sum from a warp whose lane l holds the 8 values of segment l (k = 8l .. 8l+7
+// of 256 consecutive activations of one token, i.e. 256 / G whole groups): returns X of
+// the lane's group on the lanes holding a group's first segment.  All lanes call it.
+template <int G>
+__device__ __forceinline__ float warp_group_xsum_f16(float p, int lane) {
+  float s = p;
+#pragma unroll
+  for (int q = 1; q < G / 32; ++q) s += __shfl_down_sync(0xffffffffu, p, 4 * q);
+  const float a = s + __shfl_xor_sync(0xffffffffu, s, 1);
+  return a + __shfl_xor_sync(0xffffffffu, a, 2);
+}
+
+// acc[nt] += W4 chunk (16 rows x G, shared memory) . x rows, the weights entering the MMA
+// as their raw nibbles (w4_nibbles_f16: no decode arithmetic) and the offset and nibble
+// position restored per chunk: d = 2^24 P - 8 X (rows gid) or 2^20 P - 8 X (rows gid + 8),
+// acc += d * scale.  xq[nt][e]: the chunk sums (group_xsum_f16) of the token of
+// accumulator column 2 tig + e of n-tile nt, indexed by the global chunk cg.
+template <int G, int NT>
+__device__ __forceinline__ void w4n_smem_chunk(const uint8_t* chunk, const __half* const (&xr)[2], int k0,
+                                               const float* const (&xq)[2][2], int cg, int lane,
+                                               float (&acc)[2][4]) {
+  using Fmt = W4Fmt<G>;
+  uint32_t w[Fmt::WORDS];
+#pragma unroll
+  for (int v = 0; v < Fmt::NV; ++v) {
+    const uint8_t* p = chunk + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
+    if constexpr (Fmt::VW == 4) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p);
+      w[v * 4 + 0] = u.x; w[v * 4 + 1] = u.y; w[v * 4 + 2] = u.z; w[v * 4 + 3] = u.w;
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(p);
+      w[v * 2 + 0] = u.x; w[v * 2 + 1] = u.y;
+    }
+  }
+  const uint32_t sc = *reinterpret_cast<const uint32_t*>(chunk + 8 * G + (lane >> 2) * 4);
+  const int tig = lane & 3;
+  float part[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.f;
+#pragma unroll
+  for (int q = 0; q < G / 32; ++q) {
+    uint32_t b[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr[j] + k0 + 32 * q + 8 * tig);
+      b[j][0] = v.x; b[j][1] = v.y; b[j][2] = v.z; b[j][3] = v.w;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t a[4];
+      w4_nibbles_f16(w[2 * q + h], a);
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma_f16_16816(part[j], a, b[j][2 * h], b[j][2 * h + 1]);
+    }
+  }
+  const float2 s2 = bf162_to_f2(sc);
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const float x0 = -8.f * xq[j][0][cg], x1 = -8.f * xq[j][1][cg];
+    acc[j][0] = fmaf(fmaf(part[j][0], 0x1p24f, x0), s2.x, acc[j][0]);
+    acc[j][1] = fmaf(fmaf(part[j][1], 0x1p24f, x1), s2.x, acc[j][1]);
+    acc[j][2] = fmaf(fmaf(part[j][2], 0x1p20f, x0), s2.y, acc[j][2]);
+    acc[j][3] = fmaf(fmaf(part[j][3], 0x1p20f, x1), s2.y, acc[j][3]);
+  }
+}
+
+// The same for two tiles over the same k range at once (an expert's gate and up rows):
+// one x fragment load feeds two independent MMA chains.  Per tile the MMA sequence and
+// the epilogue are those of w4n_smem_chunk, so each result has the same bits.  One
+// n-tile: xr the lane's B-fragment token row, xq0 / xq1 the chunk sums of the tokens of
+// accumulator columns 2 tig, 2 tig + 1.
+template <int G>
+__device__ __forceinline__ void w4n_smem_pair(const uint8_t* ca, const uint8_t* cb, const __half* xr, int k0,
+                                              const float* xq0, const float* xq1, int cg, int lane,
+                                              float (&acca)[4], float (&accb)[4]) {
+  using Fmt = W4Fmt<G>;
+  uint32_t wa[Fmt::WORDS], wb[Fmt::WORDS];
+#pragma unroll
+  for (int v = 0; v < Fmt::NV; ++v) {
+    const int off = v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
+    if constexpr (Fmt::VW == 4) {
+      const uint4 u = *reinterpret_cast<const uint4*>(ca + off);
+      const uint4 t = *reinterpret_cast<const uint4*>(cb + off);
+      wa[v * 4 + 0] = u.x; wa[v * 4 + 1] = u.y; wa[v * 4 + 2] = u.z; wa[v * 4 + 3] = u.w;
+      wb[v * 4 + 0] = t.x; wb[v * 4 + 1] = t.y; wb[v * 4 + 2] = t.z; wb[v * 4 + 3] = t.w;
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(ca + off);
+      const uint2 t = *reinterpret_cast<const uint2*>(cb + off);
+      wa[v * 2 + 0] = u.x; wa[v * 2 + 1] = u.y;
+      wb[v * 2 + 0] = t.x; wb[v * 2 + 1] = t.y;
+    }
+  }
+  const uint32_t sca = *reinterpret_cast<const uint32_t*>(ca + 8 * G + (lane >> 2) * 4);
+  const uint32_t scb = *reinterpret_cast<const uint32_t*>(cb + 8 * G + (lane >> 2) * 4);
+  const int tig = lane & 3;
+  float pa[4] = {0.f, 0.f, 0.f, 0.f}, pb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < G / 32; ++q) {
+    const uint4 v = *reinterpret_cast<const uint4*>(xr + k0 + 32 * q + 8 * tig);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t b0 = h ? v.z : v.x, b1 = h ? v.w : v.y;
+      uint32_t a[4];
+      w4_nibbles_f16(wa[2 * q + h], a);
+      mma_f16_16816(pa, a, b0, b1);
+      w4_nibbles_f16(wb[2 * q + h], a);
+      mma_f16_16816(pb, a, b0, b1);
+    }
+  }
+  const float x0 = -8.f * xq0[cg], x1 = -8.f * xq1[cg];
+  const float2 s2a = bf162_to_f2(sca), s2b = bf162_to_f2(scb);
+  acca[0] = fmaf(fmaf(pa[0], 0x1p24f, x0), s2a.x, acca[0]);
+  acca[1] = fmaf(fmaf(pa[1], 0x1p24f, x1), s2a.x, acca[1]);
+  acca[2] = fmaf(fmaf(pa[2], 0x1p20f, x0), s2a.y, acca[2]);
+  acca[3] = fmaf(fmaf(pa[3], 0x1p20f, x1), s2a.y, acca[3]);
+  accb[0] = fmaf(fmaf(pb[0], 0x1p24f, x0), s2b.x, accb[0]);
+  accb[1] = fmaf(fmaf(pb[1], 0x1p24f, x1), s2b.x, accb[1]);
+  accb[2] = fmaf(fmaf(pb[2], 0x1p20f, x0), s2b.y, accb[2]);
+  accb[3] = fmaf(fmaf(pb[3], 0x1p20f, x1), s2b.y, accb[3]);
+}
+
+// n consecutive chunks (global chunk index cg0 + c) through w4n_smem_chunk; NT = 2 only
+// when the unit has > 8 tokens.
+template <int G>
+__device__ __forceinline__ void w4n_smem_run(const uint8_t* chunk, int n, const __half* const (&xr)[2], int k0,
+                                             const float* const (&xq)[2][2], int cg0, int lane, bool two,
+                                             float (&acc)[2][4]) {
+  constexpr int CHB = W4Fmt<G>::CHB;
+  if (two) {
+    for (int c = 0; c < n; ++c) w4n_smem_chunk<G, 2>(chunk + c * CHB, xr, k0 + c * G, xq, cg0 + c, lane, acc);
+  } else {
+    for (int c = 0; c < n; ++c) w4n_smem_chunk<G, 1>(chunk + c * CHB, xr, k0 + c * G, xq, cg0 + c, lane, acc);
+  }
+}
+
 // acc[nt] += W4 chunks c0 .. c0+NC-1 (16 rows x G each, consecutive in shared memory)
 // . x rows (token of lane gid in n-tile nt at xr[nt]).  NC chunks are decoded and
 // multiplied interleaved (independent instruction streams for one warp) and their

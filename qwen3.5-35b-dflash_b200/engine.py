@@ -296,8 +296,8 @@ class TargetEngine:
             self._call("qw_b16_linear", self.normed.data_ptr(), lw.router.data_ptr(),
                        self.router_logits.data_ptr(), lib.QW_OUT_BF16, self.nrouter, T, self.nrouter, H, st)
             E, k, I = c.num_experts, c.num_experts_per_tok, c.moe_intermediate_size
-            self._call("qw_moe_route", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
-                       lib.QW_BF16, self.moe_ws.data_ptr(), st)
+            self._call("qw_moe_route_x", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
+                       lib.QW_BF16, self.normed.data_ptr(), H, c.quant_group, self.moe_ws.data_ptr(), st)
             self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                        lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
                        self.moe_ws.data_ptr(), st)

@@ -42,17 +42,28 @@ def _tie_heavy_logits(t, e, seed):
     return logits.to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("t,e,k", [(16, 256, 8), (256, 256, 8), (64, 16, 4), (33, 128, 8), (40, 256, 2)])
-def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k):
-    """Router selection equals torch.topk on CPU (the reference's call) element for element."""
+@pytest.mark.parametrize("t,e,k,dt", [(16, 256, 8, "bf16"), (256, 256, 8, "bf16"), (64, 16, 4, "bf16"),
+                                      (33, 128, 8, "bf16"), (40, 256, 2, "bf16"), (48, 256, 8, "f16"),
+                                      (16, 256, 8, "f32")])
+def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k, dt):
+    """Router selection equals torch.topk on CPU (the reference's call) element for element,
+    ties included (integer-valued rows, and rows whose largest logits are +0.0 and -0.0)."""
     from qwen35_dflash_b200 import lib
-    logits = _tie_heavy_logits(t, e, seed=t * 7 + e)
+    logits = _tie_heavy_logits(t, e, seed=t * 7 + e).float()
+    for r in range(2, t, 8):   # signed zeros on top: equal values for the selection
+        logits[r] = -1.0 - torch.rand(e, generator=torch.Generator().manual_seed(r))
+        logits[r, r % e] = 0.0
+        logits[r, (3 * r + 1) % e] = -0.0
+        logits[r, (5 * r + 2) % e] = -0.0
+    torch_dt = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dt]
+    code = {"bf16": lib.QW_BF16, "f16": lib.QW_F16, "f32": lib.QW_F32}[dt]
+    logits = logits.to(torch_dt)
     probs = torch.softmax(logits.float(), -1)
     _, want = torch.topk(probs, k, dim=-1)
     dev = logits.cuda()
     nbytes = cuda_lib.qw_moe_workspace_bytes(t, 256, e, 128, k)
     ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
-    lib.call("qw_moe_route", dev.data_ptr(), lib.QW_BF16, e, t, e, k, -1, lib.QW_BF16, ws.data_ptr(),
+    lib.call("qw_moe_route", dev.data_ptr(), code, e, t, e, k, -1, lib.QW_BF16, ws.data_ptr(),
              lib.stream_ptr())
     idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu()
     np.testing.assert_array_equal(idx.numpy(), want.numpy())
@@ -132,6 +143,45 @@ def test_moe_w4a16_matches_oracle(cuda_lib, t):
     idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
     np.testing.assert_array_equal(idx, sel)
     assert_close(to_np(out), want, what="moe w4a16", row_scale=True, strict_frac=0.999)
+
+
+@pytest.mark.parametrize("t,g", [(16, 128), (5, 64), (16, 32)])
+def test_moe_route_x_staging_is_bit_identical(cuda_lib, t, g):
+    """qw_moe_route_x stages x for the gate/up kernel; the experts' output must be the
+    bits of the unstaged path (qw_moe_route), and a different x than the staged one
+    must be converted afresh, not taken from the stage."""
+    from qwen35_dflash_b200 import lib, w4
+    torch.manual_seed(t + g)
+    h, e, k, inter = 2048, 64, 8, 256
+    x = torch.randn(t, h, device="cuda").to(torch.bfloat16)
+    x2 = torch.randn(t, h, device="cuda").to(torch.bfloat16)
+    logits = torch.randn(t, e + 1, device="cuda").to(torch.bfloat16)
+    gu = w4.pack_w4(torch.randint(-8, 8, (e, 2 * inter, h), dtype=torch.int8, device="cuda"),
+                    (torch.rand(e, 2 * inter, h // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    dn = w4.pack_w4(torch.randint(-8, 8, (e, h, inter), dtype=torch.int8, device="cuda"),
+                    (torch.rand(e, h, inter // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    sgu = w4.pack_w4(torch.randint(-8, 8, (2 * inter, h), dtype=torch.int8, device="cuda"),
+                     (torch.rand(2 * inter, h // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    sdn = w4.pack_w4(torch.randint(-8, 8, (h, inter), dtype=torch.int8, device="cuda"),
+                     (torch.rand(h, inter // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    st = lib.stream_ptr()
+
+    def run(stage_x, x_in):
+        ws = torch.zeros(cuda_lib.qw_moe_workspace_bytes(t, h, e, inter, k), dtype=torch.uint8, device="cuda")
+        out = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+        if stage_x is None:
+            lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws.data_ptr(), st)
+        else:
+            lib.call("qw_moe_route_x", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16,
+                     stage_x.data_ptr(), h, g, ws.data_ptr(), st)
+        lib.call("qw_moe_experts_w4", x_in.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(),
+                 sdn.data_ptr(), t, h, e, inter, k, g, ws.data_ptr(), st)
+        lib.call("qw_moe_combine", ws.data_ptr(), out.data_ptr(), 0, t, h, e, inter, k, 1, st)
+        torch.cuda.synchronize()
+        return out
+
+    assert torch.equal(run(x, x), run(None, x))
+    assert torch.equal(run(x, x2), run(None, x2))
 
 
 @pytest.mark.parametrize("tag", ["bf16", "f16"])
