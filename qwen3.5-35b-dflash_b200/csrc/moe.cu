@@ -1264,12 +1264,12 @@ static int launch_route_lists(int T, int E, int k, void* ws, cudaStream_t s) {
   return QW_OK;
 }
 
-template <class Fmt, int NT, int PF>
+template <class Fmt, int NT, int PF, class FmtUp = Fmt>
 static int launch_experts_nt(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
   const int slots = 1 + (a.E < a.T * a.k ? a.E : a.T * a.k);
   if (up) {
     const int jb = (a.I / 16 + UP_JT - 1) / UP_JT;
-    QW_LAUNCH_PDL("moe up", moe_up_kernel<Fmt, NT, PF>, dim3(slots, jb), dim3(SG_WARPS * 32), 0, s, a);
+    QW_LAUNCH_PDL("moe up", moe_up_kernel<FmtUp, NT, PF>, dim3(slots, jb), dim3(SG_WARPS * 32), 0, s, a);
   }
   if (down) {
     QW_LAUNCH_PDL("moe down", moe_down_kernel<Fmt, NT, PF>, dim3(slots, (a.H / 16 + SG_WARPS - 1) / SG_WARPS),
@@ -1280,10 +1280,10 @@ static int launch_experts_nt(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s,
 
 // Activation tile width: 8 tokens when routed experts average at most ~2 tokens (the
 // block-verify case: 16 tokens x top-8 over 256 experts), else 16.
-template <class Fmt, int PF>
+template <class Fmt, int PF, class FmtUp = Fmt>
 static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
-  if (static_cast<int64_t>(a.T) * a.k <= 2LL * a.E) return launch_experts_nt<Fmt, 1, PF>(a, s, up, down);
-  return launch_experts_nt<Fmt, 2, PF>(a, s, up, down);
+  if (static_cast<int64_t>(a.T) * a.k <= 2LL * a.E) return launch_experts_nt<Fmt, 1, PF, FmtUp>(a, s, up, down);
+  return launch_experts_nt<Fmt, 2, PF, FmtUp>(a, s, up, down);
 }
 
 static int sm_count() {
@@ -1374,9 +1374,9 @@ static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bo
     const int rc = launch_route_lists(a.T, a.E, a.k, a.ws, s);
     if (rc != QW_OK) return rc;
   }
-  // fp16 operands, as the bulk kernels: a token's expert outputs have the same bits
-  // whichever kernels (block size) compute them
-  return launch_experts<W4Fmt<G, __half>, 4>(a, s, up, down);
+  // the arithmetic of the bulk kernels (raw-nibble gate/up, fp16 down): a token's expert
+  // outputs have the same bits whichever kernels (block size) compute them
+  return launch_experts<W4Fmt<G, __half>, 4, W4NibFmt<G>>(a, s, up, down);
 }
 
 }  // namespace qw

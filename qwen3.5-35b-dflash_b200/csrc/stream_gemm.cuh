@@ -49,6 +49,7 @@ struct W4Fmt {
   static constexpr int CHB = 8 * G + 32;
   static constexpr bool SCALED = true;
   static constexpr bool PERMUTED_K = true;
+  static constexpr bool NIB = false;
 
   __host__ __device__ static int64_t tile_offset(int64_t rt, int k, int64_t /*ld*/) {
     return rt * (k / G) * static_cast<int64_t>(CHB);
@@ -75,6 +76,17 @@ struct W4Fmt {
   }
 };
 
+// W4 chunks entering the MMA as raw nibbles (w4_nibbles_f16), the offset restored per
+// chunk from the activation sums exactly as w4n_smem_chunk / w4n_smem_pair compute it, so
+// the streaming and the shared-memory kernels give a token the same bits.
+template <int G>
+struct W4NibFmt : W4Fmt<G, __half> {
+  static constexpr bool NIB = true;
+  __device__ __forceinline__ static void afrag(const uint32_t (&w)[G / 16], int s, uint32_t (&a)[4]) {
+    w4_nibbles_f16(w[s], a);
+  }
+};
+
 struct B16Fmt {
   using ET = __nv_bfloat16;
   using OT = __nv_bfloat16;
@@ -84,6 +96,7 @@ struct B16Fmt {
   static constexpr int CHB = 2048;
   static constexpr bool SCALED = false;
   static constexpr bool PERMUTED_K = true;
+  static constexpr bool NIB = false;
 
   __host__ __device__ static int64_t tile_offset(int64_t rt, int k, int64_t /*ld*/) {
     return rt * (k / 64) * static_cast<int64_t>(CHB);
@@ -113,6 +126,7 @@ struct RowFmt {
   static constexpr int WORDS = 8;
   static constexpr bool SCALED = false;
   static constexpr bool PERMUTED_K = false;
+  static constexpr bool NIB = false;
 
   __host__ __device__ static int64_t tile_offset(int64_t rt, int /*k*/, int64_t ld) {
     return rt * 16 * ld;
@@ -134,6 +148,47 @@ struct RowFmt {
     a[0] = w[s * 4 + 0]; a[1] = w[s * 4 + 1]; a[2] = w[s * 4 + 2]; a[3] = w[s * 4 + 3];
   }
 };
+
+// Sum of 8 packed fp16 values in fp32, in order.
+__device__ __forceinline__ float sum8_f16(uint4 v) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
+    s += f.x;
+    s += f.y;
+  }
+  return s;
+}
+
+// Sum X of one token's G fp16 activations of one K group, in fp32 and in a fixed order
+// that the lanes of an MMA fragment group (and a warp converting the activations)
+// reproduce: p(q, t) = the 8 values at k = 32q + 8t .. +7 summed in order, S_t = p(0, t)
+// + p(1, t) + ... in order of q, X = (S0 + S1) + (S2 + S3).  p: 16-byte aligned.
+template <int G>
+__device__ __forceinline__ float group_xsum_f16(const __half* p) {
+  float s[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    s[t] = sum8_f16(*reinterpret_cast<const uint4*>(p + 8 * t));
+#pragma unroll
+    for (int q = 1; q < G / 32; ++q) s[t] += sum8_f16(*reinterpret_cast<const uint4*>(p + 32 * q + 8 * t));
+  }
+  return (s[0] + s[1]) + (s[2] + s[3]);
+}
+
+// The same sum from a warp whose lane l holds the 8 values of segment l (k = 8l .. 8l+7
+// of 256 consecutive activations of one token, i.e. 256 / G whole groups): returns X of
+// the lane's group on the lanes holding a group's first segment.  All lanes call it.
+template <int G>
+__device__ __forceinline__ float warp_group_xsum_f16(float p, int lane) {
+  float s = p;
+#pragma unroll
+  for (int q = 1; q < G / 32; ++q) s += __shfl_down_sync(0xffffffffu, p, 4 * q);
+  const float a = s + __shfl_xor_sync(0xffffffffu, s, 1);
+  return a + __shfl_xor_sync(0xffffffffu, a, 2);
+}
 
 // Activation rows of the lane's n-tiles: n-tile j covers tokens j*8 .. j*8+7, the lane
 // reads token j*8 + gid.  Rows are element pointers to x[token, 0].
@@ -184,7 +239,39 @@ __device__ __forceinline__ void load_b(BFrag<Fmt, NT>& f, int c, int lane, const
 template <class Fmt, int NT>
 __device__ __forceinline__ void mma_frag(const WFrag<Fmt>& wf, const BFrag<Fmt, NT>& bf, float (&acc)[NT][4]) {
   using ET = typename Fmt::OT;
-  if constexpr (Fmt::SCALED) {
+  if constexpr (Fmt::NIB) {
+    float part[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < Fmt::STEPS; ++s) {
+      uint32_t a[4];
+      Fmt::afrag(wf.w, s, a);
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+        mma_f16_16816(part[j], a, bf.b[s >> 1][j][(s & 1) * 2], bf.b[s >> 1][j][(s & 1) * 2 + 1]);
+    }
+    // the chunk's activation sums in group_xsum_f16's order: this lane's running sum
+    // over its 8-value segments, then the fragment group's four lanes combined, then
+    // moved to the lanes holding each accumulator column
+    const int tig = threadIdx.x & 3;
+    const float2 s2 = bf162_to_f2(wf.sc);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      float sx = sum8_f16(make_uint4(bf.b[0][j][0], bf.b[0][j][1], bf.b[0][j][2], bf.b[0][j][3]));
+#pragma unroll
+      for (int q = 1; q < Fmt::KCHUNK / 32; ++q)
+        sx += sum8_f16(make_uint4(bf.b[q][j][0], bf.b[q][j][1], bf.b[q][j][2], bf.b[q][j][3]));
+      const float pa = sx + __shfl_xor_sync(0xffffffffu, sx, 1);
+      const float xg = pa + __shfl_xor_sync(0xffffffffu, pa, 2);
+      const float x0 = -8.f * __shfl_sync(0xffffffffu, xg, 8 * tig);
+      const float x1 = -8.f * __shfl_sync(0xffffffffu, xg, 8 * tig + 4);
+      acc[j][0] = fmaf(fmaf(part[j][0], 0x1p24f, x0), s2.x, acc[j][0]);
+      acc[j][1] = fmaf(fmaf(part[j][1], 0x1p24f, x1), s2.x, acc[j][1]);
+      acc[j][2] = fmaf(fmaf(part[j][2], 0x1p20f, x0), s2.y, acc[j][2]);
+      acc[j][3] = fmaf(fmaf(part[j][3], 0x1p20f, x1), s2.y, acc[j][3]);
+    }
+  } else if constexpr (Fmt::SCALED) {
     float part[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.f;
@@ -262,47 +349,6 @@ __device__ __forceinline__ void stream_tile(const uint8_t* tile, int64_t ld, int
   const uint8_t* const tiles[1] = {tile};
   float (&a1)[1][NT][4] = *reinterpret_cast<float (*)[1][NT][4]>(&acc);
   stream_tiles<Fmt, NT, PF, 1, PDL>(tiles, ld, c0, c1, lane, x, a1);
-}
-
-// Sum of 8 packed fp16 values in fp32, in order.
-__device__ __forceinline__ float sum8_f16(uint4 v) {
-  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-  float s = 0.f;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
-    s += f.x;
-    s += f.y;
-  }
-  return s;
-}
-
-// Sum X of one token's G fp16 activations of one K group, in fp32 and in a fixed order
-// that the lanes of an MMA fragment group (and a warp converting the activations)
-// reproduce: p(q, t) = the 8 values at k = 32q + 8t .. +7 summed in order, S_t = p(0, t)
-// + p(1, t) + ... in order of q, X = (S0 + S1) + (S2 + S3).  p: 16-byte aligned.
-template <int G>
-__device__ __forceinline__ float group_xsum_f16(const __half* p) {
-  float s[4];
-#pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    s[t] = sum8_f16(*reinterpret_cast<const uint4*>(p + 8 * t));
-#pragma unroll
-    for (int q = 1; q < G / 32; ++q) s[t] += sum8_f16(*reinterpret_cast<const uint4*>(p + 32 * q + 8 * t));
-  }
-  return (s[0] + s[1]) + (s[2] + s[3]);
-}
-
-// The same sum from a warp whose lane l holds the 8 values of segment l (k = 8l .. 8l+7
-// of 256 consecutive activations of one token, i.e. 256 / G whole groups): returns X of
-// the lane's group on the lanes holding a group's first segment.  All lanes call it.
-template <int G>
-__device__ __forceinline__ float warp_group_xsum_f16(float p, int lane) {
-  float s = p;
-#pragma unroll
-  for (int q = 1; q < G / 32; ++q) s += __shfl_down_sync(0xffffffffu, p, 4 * q);
-  const float a = s + __shfl_xor_sync(0xffffffffu, s, 1);
-  return a + __shfl_xor_sync(0xffffffffu, a, 2);
 }
 
 // acc[nt] += W4 chunk (16 rows x G, shared memory) . x rows, the weights entering the MMA
