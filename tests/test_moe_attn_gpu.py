@@ -73,6 +73,12 @@ def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k, dt):
     assert_close(w.numpy(), ref_w.numpy(), 2 ** -8, 2 ** -7, "route weights")
     # expert -> (token, slot) lists: active experts ascending, tokens ascending in each
     lib.call("qw_moe_route_lists", ws.data_ptr(), t, e, k, lib.stream_ptr())
+    _check_lists(ws, t, e, k, want.numpy())
+
+
+def _check_lists(ws, t, e, k, sel_np):
+    """The workspace's per-expert lists against the top-k indices sel_np [t, k]."""
+    torch.cuda.synchronize()
     ints = ws.view(torch.int32).cpu().numpy()
     na_max = min(e, t * k)
     o = 2 * t * k + t
@@ -81,7 +87,6 @@ def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k, dt):
     off = ints[o + 4 + na_max: o + 5 + 2 * na_max]
     ptok = ints[o + 5 + 2 * na_max: o + 5 + 2 * na_max + t * k]
     pslot = ints[o + 5 + 2 * na_max + t * k: o + 5 + 2 * na_max + 2 * t * k]
-    sel_np = want.numpy()
     experts = sorted(set(sel_np.ravel().tolist()))
     assert n_active == len(experts) and active[:n_active].tolist() == experts
     assert off[0] == 0 and off[n_active] == t * k
@@ -142,6 +147,7 @@ def test_moe_w4a16_matches_oracle(cuda_lib, t):
     want = bf16_round(routed + bf16_round(shared * sgate))
     idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
     np.testing.assert_array_equal(idx, sel)
+    _check_lists(ws, t, e, k, sel)   # as the expert kernels built (and published) them
     assert_close(to_np(out), want, what="moe w4a16", row_scale=True, strict_frac=0.999)
 
 
