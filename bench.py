@@ -43,7 +43,7 @@ METRIC = "verify tok/s & step latency (block 16, W4 MoE+GDN); % HBM roofline"
 # DRAM bytes (read + write) of one moe_up_bulk_kernel launch from an ncu capture of the
 # same routing (16 tokens of N(0,1) router logits, seed 17 -> 103 active experts):
 # profiles/moe_up_bulk_T16.md
-MOE_UP_NCU_TRAFFIC = {"bytes": 112_624_896 + 3_246_336, "active": 103, "profile": "profiles/moe_up_bulk_T16.md"}
+MOE_UP_NCU_TRAFFIC = {"bytes": 112_579_584 + 3_767_552, "active": 103, "profile": "profiles/moe_up_bulk_T16.md"}
 
 
 def _peaks():
