@@ -236,7 +236,9 @@ int qw_moe_combine(void* workspace, void* out, int residual, int64_t tokens, int
  * norm): hidden = bf16(hidden + moe) in place, then normed = rms_norm(hidden) with the
  * +1 gamma convention as qw_residual_norm, and, when tap != NULL, the feature tap
  * (hidden, or normed with tap_normed != 0) at tap[t*ldf + i].  hidden, normed, gamma
- * and tap 8-byte aligned, hidden_dim and ldf multiples of 4; top_k <= 16. */
+ * and tap 8-byte aligned, hidden_dim and ldf multiples of 4; top_k <= 16.  The kernel
+ * reads hidden, gamma and the routing before it waits for the launch ahead of it (the
+ * expert call), so that launch must not be the one that wrote hidden. */
 int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens, int64_t hidden_dim,
                         int64_t experts, int64_t inter, int64_t top_k, int has_shared,
                         const void* gamma, void* normed, float eps, void* tap, int64_t ldf,

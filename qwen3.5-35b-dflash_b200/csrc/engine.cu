@@ -30,6 +30,17 @@ struct NormArgs {
 
 __global__ void residual_norm_kernel(NormArgs a) {
   __shared__ float red[32];
+  constexpr int NV = 8;   // row values per thread held in registers (H <= NV * blockDim.x)
+  const bool regs = a.H <= NV * static_cast<int>(blockDim.x);
+  float g[NV];
+  if (regs) {
+    // the norm weight is no kernel's output: read before the wait
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      g[j] = i < a.H ? rbf(__bfloat162float(a.gamma[i]) + 1.f) : 0.f;
+    }
+  }
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
@@ -39,21 +50,35 @@ __global__ void residual_norm_kernel(NormArgs a) {
     for (int i = threadIdx.x; i < a.H; i += blockDim.x) h[i] = e[i];
     __syncthreads();
   }
+  __nv_bfloat16* out = a.normed + static_cast<int64_t>(t) * a.H;
+  __nv_bfloat16* tap = a.tap ? a.tap + static_cast<int64_t>(t) * a.ldf : nullptr;
+  if (!regs) {
+    rms_norm_row<false>(h, a.gamma, out, tap, a.tap_normed, a.H, a.eps, red);
+    return;
+  }
+  // rms_norm_row's arithmetic with the row read once into registers
+  __nv_bfloat16 hv[NV];
   float ss = 0.f;
-#pragma unroll 8
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {   // unrolled: the row loads are in flight together
-    const float v = __bfloat162float(h[i]);
-    ss += v * v;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    hv[j] = i < a.H ? h[i] : __float2bfloat16_rn(0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const float v = __bfloat162float(hv[j]);
+    if (threadIdx.x + j * blockDim.x < a.H) ss += v * v;
   }
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / a.H + a.eps);
-#pragma unroll 8
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
-    const __nv_bfloat16 hv = h[i];
-    const float g = rbf(__bfloat162float(a.gamma[i]) + 1.f);
-    const __nv_bfloat16 y = __float2bfloat16_rn(rbf(__bfloat162float(hv) * inv) * g);
-    a.normed[static_cast<int64_t>(t) * a.H + i] = y;
-    if (a.tap) a.tap[static_cast<int64_t>(t) * a.ldf + i] = a.tap_normed ? y : hv;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < a.H) {
+      const __nv_bfloat16 y = __float2bfloat16_rn(rbf(__bfloat162float(hv[j]) * inv) * g[j]);
+      out[i] = y;
+      if (tap) tap[i] = a.tap_normed ? y : hv[j];
+    }
   }
 }
 

@@ -1148,8 +1148,9 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
   __shared__ int s_slot[KMAX];
   __shared__ float s_w[KMAX];
   __shared__ float red[32];
-  pdl_wait();
-  pdl_trigger();
+  // before the wait: everything but the expert outputs -- the routing (from the route
+  // kernel), the residual row (from the mixer's projection) and the norm weight are
+  // older than the predecessor (the down projection)
   const RouteView rv = route_view(ws, T, E, k);
   const int t = blockIdx.x;
   if (threadIdx.x < k) {
@@ -1159,10 +1160,18 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     s_slot[rank] = threadIdx.x;
     s_w[rank] = rv.topk_w[t * k + threadIdx.x];
   }
-  __syncthreads();
   const float sg = has_shared ? rv.shared_gate[t] : 0.f;
-  const float* pt = part + static_cast<int64_t>(t) * (k + 1) * H;
   __nv_bfloat16* h = hidden + static_cast<int64_t>(t) * H;
+  const bool one = H <= 4 * CN_THREADS;   // each thread at most one 4-column chunk
+  uint2 h0 = make_uint2(0u, 0u), g0 = make_uint2(0u, 0u), n0 = make_uint2(0u, 0u);
+  if (one && 4 * static_cast<int>(threadIdx.x) < H) {
+    h0 = *reinterpret_cast<const uint2*>(h + 4 * threadIdx.x);
+    g0 = *reinterpret_cast<const uint2*>(gamma + 4 * threadIdx.x);
+  }
+  pdl_wait();
+  pdl_trigger();
+  __syncthreads();
+  const float* pt = part + static_cast<int64_t>(t) * (k + 1) * H;
   float ss = 0.f;
   for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
     float4 y[KMAX + 1];
@@ -1170,7 +1179,7 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     for (int j = 0; j < KMAX; ++j)
       if (j < k) y[j] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(s_slot[j]) * H + c);
     if (has_shared) y[KMAX] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(k) * H + c);
-    const uint2 hraw = *reinterpret_cast<const uint2*>(h + c);
+    const uint2 hraw = one ? h0 : *reinterpret_cast<const uint2*>(h + c);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < KMAX; ++j) {
@@ -1196,14 +1205,15 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     out.x = *reinterpret_cast<const uint32_t*>(&n01);
     out.y = *reinterpret_cast<const uint32_t*>(&n23);
     *reinterpret_cast<uint2*>(h + c) = out;
+    n0 = out;
     const float2 f01 = __bfloat1622float2(n01), f23 = __bfloat1622float2(n23);
     ss += f01.x * f01.x + f01.y * f01.y + f23.x * f23.x + f23.y * f23.y;
   }
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / H + eps);
   for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
-    const uint2 hraw = *reinterpret_cast<const uint2*>(h + c);
-    const uint2 graw = *reinterpret_cast<const uint2*>(gamma + c);
+    const uint2 hraw = one ? n0 : *reinterpret_cast<const uint2*>(h + c);
+    const uint2 graw = one ? g0 : *reinterpret_cast<const uint2*>(gamma + c);
     const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&hraw);
     const __nv_bfloat16* gv = reinterpret_cast<const __nv_bfloat16*>(&graw);
     __nv_bfloat16 yv[4];

@@ -122,6 +122,32 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return red[0];
 }
 
+// RMSNorm of one token's row with the +1 gamma convention of qw_residual_norm:
+// out = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * bf16(gamma + 1)), and the feature tap
+// (h, or out with tap_normed) when tap != null.  Every thread of the CTA calls it; the
+// same thread count gives the same bits.  CG: h was written by other CTAs of this
+// launch, so it is read through L2 only.
+template <bool CG>
+__device__ __forceinline__ void rms_norm_row(const __nv_bfloat16* h, const __nv_bfloat16* gamma, __nv_bfloat16* out,
+                                             __nv_bfloat16* tap, int tap_normed, int H, float eps, float* red) {
+  float ss = 0.f;
+#pragma unroll 8
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {   // unrolled: the row loads are in flight together
+    const float v = __bfloat162float(CG ? __ldcg(h + i) : h[i]);
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / H + eps);
+#pragma unroll 8
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const __nv_bfloat16 hv = CG ? __ldcg(h + i) : h[i];
+    const float g = rbf(__bfloat162float(gamma[i]) + 1.f);
+    const __nv_bfloat16 y = __float2bfloat16_rn(rbf(__bfloat162float(hv) * inv) * g);
+    out[i] = y;
+    if (tap) tap[i] = tap_normed ? y : hv;
+  }
+}
+
 // ------------------------------------------------------------------ tensor-core helpers
 // mma.sync m16n8k16 bf16 x bf16 -> f32 (row.col).  A: 4 x b32, B: 2 x b32, C/D: 4 x f32.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
