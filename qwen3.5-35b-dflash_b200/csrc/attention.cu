@@ -63,8 +63,9 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   ET* qsm = reinterpret_cast<ET*>(smem);                 // [128][XS]
   ET* ksm = qsm + ATT_MAXROWS * XS;                      // ATT_NST stages of K [32][XS], V [32][XS]
   int* pg = reinterpret_cast<int*>(ksm + ATT_NST * 2 * ATT_KT * XS);  // [pgcap] page of each key page
-  pdl_wait();   // q and the block's keys come from the predecessor (prep)
-  pdl_trigger();
+  // q and the block's own keys come from the predecessor (prep); the page table, the
+  // query positions and the keys of earlier steps are older, so the first K/V tiles of
+  // the context are requested before the wait
   const int split = blockIdx.x;
   const int kvh = blockIdx.y / a.rowgroups, rg = blockIdx.y % a.rowgroups;
   const int b = blockIdx.z;
@@ -82,14 +83,6 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   const int gid = lane >> 2, tig = lane & 3;
   const bool f16 = std::is_same<ET, __half>::value;
 
-  // Q rows -> smem (row r: head kvh*G + (row0+r)/S, position (row0+r)%S), first cp.async group
-  for (int i = threadIdx.x; i < nwarps * 16 * (D / 8); i += blockDim.x) {
-    const int r = i / (D / 8), c = (i % (D / 8)) * 8;
-    const bool valid = r < nrows;
-    const int rr = row0 + (valid ? r : 0);
-    const int h = kvh * G + rr / a.S, s = rr % a.S;
-    cp_async16(qsm + r * XS + c, a.q + b * a.qb + h * a.qh + s * a.qs + c, valid);
-  }
   // page of every key page this CTA reads (staged when it fits)
   const int p0 = k0 / a.P, npg = (k1 - 1) / a.P - p0 + 1;
   const bool staged = npg <= a.pgcap;
@@ -111,11 +104,30 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
     }
   };
   const int ntiles = (k1 - k0 + ATT_KT - 1) / ATT_KT;
-#pragma unroll
-  for (int st = 0; st < ATT_NST - 1; ++st) {
+  // the first ATT_NST - 1 tiles, one cp.async group each: those wholly before qpos now
+  int pre = 0;
+  while (pre < ATT_NST - 1 && pre < ntiles && k0 + (pre + 1) * ATT_KT <= qpos) {
+    load_tile(pre, k0 + pre * ATT_KT);
+    cp_async_commit();
+    ++pre;
+  }
+  pdl_wait();
+  pdl_trigger();
+  for (int st = pre; st < ATT_NST - 1; ++st) {
     if (st < ntiles) load_tile(st, k0 + st * ATT_KT);
     cp_async_commit();
   }
+  // Q rows -> smem (row r: head kvh*G + (row0+r)/S, position (row0+r)%S)
+  for (int i = threadIdx.x; i < nwarps * 16 * (D / 8); i += blockDim.x) {
+    const int r = i / (D / 8), c = (i % (D / 8)) * 8;
+    const bool valid = r < nrows;
+    const int rr = row0 + (valid ? r : 0);
+    const int h = kvh * G + rr / a.S, s = rr % a.S;
+    cp_async16(qsm + r * XS + c, a.q + b * a.qb + h * a.qh + s * a.qs + c, valid);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
 
   float o[D / 8][4];
 #pragma unroll
