@@ -227,41 +227,50 @@ __device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, in
   const float p = q.v[a - 1];
   const unsigned lt = (1u << lane) - 1u;
   const int itn = (b - a + 32) / 32;   // 32-wide passes over [a - 1, b)
+  // every value load first, indices clamped into [a - 1, b) and the out-of-range lanes
+  // masked in the ballots: one shared-memory round trip instead of one per pass
+  float vl[IT], vr[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    vl[it] = q.v[min(a + 32 * it + lane, b - 1)];
+    vr[it] = q.v[max(b - 1 - 32 * it - lane, a - 1)];
+  }
   unsigned mL[IT], mR[IT];
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    if (it < itn) {
-      const int i = a + 32 * it + lane;
-      mL[it] = __ballot_sync(0xffffffffu, i < b && !(q.v[i] > p));
-      const int j = b - 1 - 32 * it - lane;
-      mR[it] = __ballot_sync(0xffffffffu, j >= a - 1 && !(p > q.v[j]));
-    } else {
-      mL[it] = mR[it] = 0u;
-    }
+    mL[it] = __ballot_sync(0xffffffffu, it < itn && a + 32 * it + lane < b && !(vl[it] > p));
+    mR[it] = __ballot_sync(0xffffffffu, it < itn && b - 1 - 32 * it - lane >= a - 1 && !(p > vr[it]));
   }
   int nl = 0, nr = 0;
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    if (it < itn) {
-      if ((mL[it] >> lane) & 1u) pos_l[nl + __popc(mL[it] & lt)] = static_cast<int16_t>(a + 32 * it + lane);
-      nl += __popc(mL[it]);
-      if ((mR[it] >> lane) & 1u) pos_r[nr + __popc(mR[it] & lt)] = static_cast<int16_t>(b - 1 - 32 * it - lane);
-      nr += __popc(mR[it]);
-    }
+    if ((mL[it] >> lane) & 1u) pos_l[nl + __popc(mL[it] & lt)] = static_cast<int16_t>(a + 32 * it + lane);
+    nl += __popc(mL[it]);
+    if ((mR[it] >> lane) & 1u) pos_r[nr + __popc(mR[it] & lt)] = static_cast<int16_t>(b - 1 - 32 * it - lane);
+    nr += __popc(mR[it]);
   }
   __syncwarp();
-  // pairs m with L[m] < R[m] form a prefix: its length is the first failing m
+  // pairs m with L[m] < R[m] form a prefix: its length is the first failing m (the stop
+  // lists are read once, every pass at once, and kept for the swaps)
   const int lim = nl < nr ? nl : nr;
+  const int mcap = lim > 0 ? lim - 1 : 0;
+  int pl[IT], pr[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int m = min(32 * it + lane, mcap);
+    pl[it] = pos_l[m];
+    pr[it] = pos_r[m];
+  }
   int mstar = lim;
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    if (32 * it < lim) {
-      const int m = 32 * it + lane;
-      const unsigned bad = __ballot_sync(0xffffffffu, m < lim && !(pos_l[m] < pos_r[m]));
-      if (bad && mstar == lim) mstar = 32 * it + __ffs(bad) - 1;
-    }
+    const int m = 32 * it + lane;
+    const unsigned bad = __ballot_sync(0xffffffffu, m < lim && !(pl[it] < pr[it]));
+    if (bad && mstar == lim && 32 * it < lim) mstar = 32 * it + __ffs(bad) - 1;
   }
-  for (int m = lane; m < mstar; m += 32) q.swap(pos_l[m], pos_r[m]);
+#pragma unroll
+  for (int it = 0; it < IT; ++it)
+    if (32 * it + lane < mstar) q.swap(pl[it], pr[it]);
   __syncwarp();
   if (mstar == 0) return pos_l[0];
   const int lm = mstar < nl ? pos_l[mstar] : 1 << 30;
