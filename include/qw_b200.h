@@ -342,7 +342,9 @@ int qw_lmhead_argmax(const void* x, const void* w_stream, void* logits, void* ke
  * top1[t] = argmax of row t (ties -> lowest id); max_accepted[b] = longest prefix of
  * proposals[b*seq..] equal to (next_token[b], top1[b*seq], ...).  With auto_commit,
  * accepted[b] = max_accepted[b], next_token[b] = top1 of row accepted-1, qpos[b] +=
- * accepted (all device-side: no host synchronization). */
+ * accepted (all device-side: no host synchronization).  One CTA per row; the last to
+ * finish decides acceptance through a counter inside the library, so calls on one GPU
+ * must not overlap. */
 int qw_accept(const void* keys, int64_t nblk, const int32_t* proposals, int32_t* top1,
               int32_t* max_accepted, int32_t* next_token, int32_t* accepted, int32_t* qpos,
               int64_t batch, int64_t seq, int auto_commit, void* stream);

@@ -82,46 +82,54 @@ __global__ void residual_norm_kernel(NormArgs a) {
   }
 }
 
-// One warp per token reduces the lm_head argmax keys; then one thread per sequence
-// evaluates acceptance.
+// One CTA per token reduces its lm_head argmax keys; the CTA that finishes last (a
+// ticket that wraps to 0 with the last token, so it is 0 again for the next launch;
+// launches must not overlap) then evaluates acceptance for every sequence.
+__device__ unsigned g_accept_ticket;
+
 __global__ void accept_kernel(const unsigned long long* __restrict__ keys, int nblk, int T, int S, int B,
                               const int32_t* __restrict__ proposals, int32_t* __restrict__ top1,
                               int32_t* __restrict__ max_accepted, int32_t* __restrict__ next_token,
                               int32_t* __restrict__ accepted, int32_t* __restrict__ qpos, int auto_commit) {
+  __shared__ unsigned long long s_best[32];
+  __shared__ int s_last;
   pdl_wait();
   pdl_trigger();
-  __shared__ int32_t s_top1[QW_MAX_BLOCK * 64];
+  const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int t = warp; t < T; t += nw) {
-    unsigned long long best = 0ull;
+  unsigned long long best = 0ull;
 #pragma unroll 8
-    for (int i = lane; i < nblk; i += 32) {   // unrolled: the partial keys load together
-      const unsigned long long k = keys[static_cast<int64_t>(i) * T + t];
-      best = k > best ? k : best;
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-      best = other > best ? other : best;
-    }
-    if (lane == 0) {
-      const int32_t tok = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
-      top1[t] = tok;
-      s_top1[t] = tok;
-    }
+  for (int i = threadIdx.x; i < nblk; i += blockDim.x) {   // unrolled: the partial keys load together
+    const unsigned long long k = keys[static_cast<int64_t>(i) * T + t];
+    best = k > best ? k : best;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if (lane == 0) s_best[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < nw; ++w) best = s_best[w] > best ? s_best[w] : best;
+    top1[t] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+    __threadfence();
+    s_last = atomicInc(&g_accept_ticket, static_cast<unsigned>(T - 1)) == static_cast<unsigned>(T - 1);
   }
   __syncthreads();
+  if (!s_last) return;
+  __threadfence();
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     int acc = 0;
     int expected = next_token[b];
     for (int i = 0; i < S; ++i) {
       if (proposals[b * S + i] != expected) break;
       ++acc;
-      expected = s_top1[b * S + i];
+      expected = __ldcg(top1 + b * S + i);
     }
     max_accepted[b] = acc;
     if (auto_commit) {
       accepted[b] = acc;
-      if (acc > 0) next_token[b] = s_top1[b * S + acc - 1];
+      if (acc > 0) next_token[b] = __ldcg(top1 + b * S + acc - 1);
       qpos[b] += acc;
     }
   }
@@ -165,7 +173,7 @@ extern "C" int qw_accept(const void* keys, int64_t nblk, const int32_t* proposal
   QW_CHECK_ARG(!auto_commit || (accepted && qpos), "accept: auto commit needs accepted and qpos");
   QW_CHECK_ARG(batch >= 1 && seq >= 1 && seq <= QW_MAX_BLOCK && batch * seq <= QW_MAX_BLOCK * 64 && nblk >= 1,
                "accept: invalid shape");
-  QW_LAUNCH_PDL("accept", accept_kernel, dim3(1), dim3(512), 0, as_stream(stream),
+  QW_LAUNCH_PDL("accept", accept_kernel, dim3(static_cast<unsigned>(batch * seq)), dim3(256), 0, as_stream(stream),
                 static_cast<const unsigned long long*>(keys), static_cast<int>(nblk),
                 static_cast<int>(batch * seq), static_cast<int>(seq), static_cast<int>(batch), proposals, top1,
                 max_accepted, next_token, accepted, qpos, auto_commit);
