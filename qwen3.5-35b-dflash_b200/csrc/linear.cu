@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(SG_WARPS * 32) stream_linear_kernel(LinArgs a)
 // order (and partition) of the streaming kernel's K split with rt = 1, so every output
 // has the streaming kernel's bits.
 constexpr int CL_SIZE = 8;
-constexpr int CL_WARPS = 8;
+constexpr int CL_WARPS = 16;
 constexpr int CL_MAXT = 16;
 constexpr int CL_PAD = 32;      // 16-bit elements of row padding (conflict-free fragment loads)
 constexpr int CL_MAXS = 8;      // ring stages per warp, at most
@@ -276,11 +276,12 @@ __global__ void __launch_bounds__(CL_WARPS * 32, 1) cluster_linear_kernel(ClArgs
   }
   cluster.sync();   // every partial has reached its owner
   {
-    const int l = threadIdx.x >> 3, e = threadIdx.x & 7;   // fragment lane, value
+    // 256 threads per owned tile (fragment lane l, value e); CL_WARPS / 8 tiles at a time
+    const int l = (threadIdx.x & 255) >> 3, e = threadIdx.x & 7;
     const int jj = e >> 2, r = e & 3;
     const int t = jj * 8 + 2 * (l & 3) + (r & 1);
     const int row = (l >> 2) + 8 * (r >> 1);
-    for (int i = rank; i < my_tiles; i += CL_SIZE) {
+    for (int i = rank + CL_SIZE * (threadIdx.x >> 8); i < my_tiles; i += CL_SIZE * (CL_WARPS / 8)) {
       float v = 0.f;
 #pragma unroll
       for (int sr = 0; sr < CL_SIZE; ++sr)
