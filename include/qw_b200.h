@@ -221,6 +221,41 @@ int qw_moe_down_w4(const void* x, const void* gate_up, const void* down, const v
                    const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts,
                    int64_t inter, int64_t top_k, int32_t group, void* workspace, void* stream);
 
+/* qw_moe_experts_w4 for the routed experts [expert_lo, expert_lo + expert_count) of the
+ * routing only (gate_up / down hold those experts' streams, indexed e - expert_lo; pairs
+ * of other experts are left out, expert_count 0 computes only the shared expert).  The
+ * expert-parallel building block; no counterpart in the reference. */
+int qw_moe_experts_w4_range(const void* x, const void* gate_up, const void* down,
+                            const void* shared_gate_up, const void* shared_down, int64_t tokens,
+                            int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
+                            int32_t group, int64_t expert_lo, int64_t expert_count, void* workspace,
+                            void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Expert parallelism (experts [g E/G, (g+1) E/G) on rank g; dispatch and combine by
+ * the host's all-to-all): the source rank packs each routed (token, slot) pair's row
+ * for its expert's rank (qw_moe_ep_pack: send_rows bf16 [ranks][cap][hidden],
+ * send_meta int32 [ranks][cap + 1], cap >= tokens * top_k); after the all-to-all the
+ * receiving rank routes what it got (qw_moe_ep_recv_route into a workspace of
+ * qw_moe_ep_recv_workspace_bytes), runs qw_moe_experts_w4_range over ranks * cap rows
+ * (top_k 1, its experts, no shared expert), packs the outputs (qw_moe_ep_pack_out) and
+ * the all-to-all returns them; qw_moe_ep_scatter writes them into the source routing's
+ * per-(token, slot) outputs for qw_moe_combine(_norm).  Bit-identical to the one-GPU
+ * MoE.  No counterpart in the reference (its plan for multi-GPU serving).
+ * ---------------------------------------------------------------------------- */
+int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+                                       int64_t inter);
+int qw_moe_ep_pack(const void* workspace, const void* x, int64_t tokens, int64_t hidden, int64_t experts,
+                   int64_t top_k, int64_t ranks, int64_t cap, void* send_rows, int32_t* send_meta,
+                   void* stream);
+int qw_moe_ep_recv_route(const int32_t* recv_meta, int64_t ranks, int64_t cap, int64_t experts,
+                         void* recv_workspace, void* stream);
+int qw_moe_ep_pack_out(const void* recv_workspace, const int32_t* recv_meta, int64_t ranks, int64_t cap,
+                       int64_t hidden, int64_t experts, int64_t inter, void* send_back, void* stream);
+int qw_moe_ep_scatter(void* workspace, const void* recv_back, int64_t tokens, int64_t hidden,
+                      int64_t experts, int64_t inter, int64_t top_k, int64_t ranks, int64_t cap,
+                      void* stream);
+
 /* Byte offset, inside a MoE workspace, of the int32 count of active routed experts
  * (valid after qw_moe_route_lists or an expert entry point; for measuring the experts
  * actually streamed). */

@@ -542,15 +542,21 @@ __global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ l
 // active experts in ascending id with their pair ranges (off), and in each range the
 // pairs in ascending token.  Called by every thread of a CTA; scratch holds 3E ints,
 // red 64 ints.  Outputs may live in shared or global memory.
-__device__ void build_route_lists(const int* idx, int T, int E, int k, int* scratch, int* red, int* n_active,
-                                  int* active, int* off, int* tok, int* slot) {
+__device__ void build_route_lists(const int* idx, int T, int E, int k, int lo, int* scratch, int* red,
+                                  int* n_active, int* active, int* off, int* tok, int* slot) {
   const int nthr = blockDim.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // experts [lo, lo + E) of the routing, as local ids 0 .. E-1; pairs of other experts
+  // (or invalid ids) are left out
+  auto local = [&](int e) { return (e >= lo && e < lo + E) ? e - lo : -1; };
   int* cnt = scratch;                                  // [E] pairs per expert
   int* apos = scratch + E;                             // [E] next free position of each list
   unsigned* bits = reinterpret_cast<unsigned*>(scratch + 2 * E);   // [E] token bits of one 32-token chunk
   for (int e = threadIdx.x; e < E; e += nthr) cnt[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < T * k; i += nthr) atomicAdd(&cnt[idx[i]], 1);
+  for (int i = threadIdx.x; i < T * k; i += nthr) {
+    const int e = local(idx[i]);
+    if (e >= 0) atomicAdd(&cnt[e], 1);
+  }
   __syncthreads();
   // exclusive scans of (active flag, count) over experts: thread i owns a contiguous run
   const int per = (E + nthr - 1) / nthr;
@@ -587,11 +593,15 @@ __device__ void build_route_lists(const int* idx, int T, int E, int k, int* scra
     const int tn = min(32, T - t0);
     for (int e = threadIdx.x; e < E; e += nthr) bits[e] = 0u;
     __syncthreads();
-    for (int i = threadIdx.x; i < tn * k; i += nthr) atomicOr(&bits[idx[t0 * k + i]], 1u << (i / k));
+    for (int i = threadIdx.x; i < tn * k; i += nthr) {
+      const int e = local(idx[t0 * k + i]);
+      if (e >= 0) atomicOr(&bits[e], 1u << (i / k));
+    }
     __syncthreads();
     for (int i = threadIdx.x; i < tn * k; i += nthr) {
       const int tl = i / k, s = i % k;
-      const int e = idx[t0 * k + i];
+      const int e = local(idx[t0 * k + i]);
+      if (e < 0) continue;
       const int at = apos[e] + __popc(bits[e] & ((1u << tl) - 1u));
       tok[at] = t0 + tl;
       slot[at] = s;
@@ -603,13 +613,14 @@ __device__ void build_route_lists(const int* idx, int T, int E, int k, int* scra
 }
 
 // Lists of the routing workspace (one CTA).  Dynamic smem: 3E + 64 ints.
-__global__ void __launch_bounds__(1024) route_lists_kernel(int T, int E, int k, void* ws) {
+// Lists of experts [lo, lo + ne) of a routing over E experts (local ids).
+__global__ void __launch_bounds__(1024) route_lists_kernel(int T, int E, int k, int lo, int ne, void* ws) {
   extern __shared__ __align__(16) uint8_t smem[];
   pdl_wait();
   pdl_trigger();
   RouteView rv = route_view(ws, T, E, k);
   int* scratch = reinterpret_cast<int*>(smem);
-  build_route_lists(rv.topk_idx, T, E, k, scratch, scratch + 3 * E, rv.n_active, rv.active, rv.pair_off,
+  build_route_lists(rv.topk_idx, T, ne, k, lo, scratch, scratch + 3 * E, rv.n_active, rv.active, rv.pair_off,
                     rv.pair_tok, rv.pair_slot);
 }
 
@@ -627,6 +638,7 @@ struct MoeArgs {
   ET* hbuf;                 // [T*k + T, I]
   float* part;              // [T, k+1, H] raw expert outputs
   int T, H, I, E, k, has_shared;
+  int e_lo, e_cnt;          // routed experts computed: [e_lo, e_lo + e_cnt) of the E, banks indexed e - e_lo
 };
 
 // Decode CTA slot -> (weights, number of pairs, pair list base); false if idle.
@@ -782,14 +794,11 @@ struct XtRoute {
 // memory).  With publish, the lists are also written to the routing workspace (for the
 // host and for kernels that read the workspace lists).
 __device__ __forceinline__ void xt_build_route(XtRoute& r, int* scratch, const RouteView& rv, int T, int E, int k,
-                                               bool publish) {
+                                               int lo, int ne, bool publish) {
   const int np = T * k;
-  for (int i = threadIdx.x; i < np; i += blockDim.x) {
-    const int e = rv.topk_idx[i];
-    r.idx[i] = (e >= 0 && e < E) ? e : 0;   // the route kernel writes valid ids; stay in bounds regardless
-  }
+  for (int i = threadIdx.x; i < np; i += blockDim.x) r.idx[i] = rv.topk_idx[i];
   __syncthreads();
-  build_route_lists(r.idx, T, E, k, scratch, scratch + 3 * E, &r.n_active, r.active, r.off, r.tok, r.slot);
+  build_route_lists(r.idx, T, ne, k, lo, scratch, scratch + 3 * E, &r.n_active, r.active, r.off, r.tok, r.slot);
   if (publish) {
     const int na = r.n_active;
     if (threadIdx.x == 0) *rv.n_active = na;
@@ -878,7 +887,7 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
     }
   }
   cp_async_commit();
-  xt_build_route(rt, scratch, rv, T, a.E, a.k, blockIdx.x == 0);
+  xt_build_route(rt, scratch, rv, T, a.E, a.k, a.e_lo, a.e_cnt, blockIdx.x == 0);
   __syncthreads();
   const int J = I / 16;
   const int nslots = a.has_shared + rt.n_active;
@@ -1022,7 +1031,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
     for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
   fence_barrier_init();
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
-  xt_build_route(rt, scratch, rv, T, a.E, a.k, false);
+  xt_build_route(rt, scratch, rv, T, a.E, a.k, a.e_lo, a.e_cnt, false);
   __syncthreads();
   const int nslots = a.has_shared + rt.n_active;
   const int nu = nslots * nrb;
@@ -1271,7 +1280,7 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   return QW_OK;
 }
 
-static int launch_route_lists(int T, int E, int k, void* ws, cudaStream_t s) {
+static int launch_route_lists(int T, int E, int k, int lo, int ne, void* ws, cudaStream_t s) {
   const size_t smem = (3 * static_cast<size_t>(E) + 64) * sizeof(int);
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
@@ -1279,7 +1288,7 @@ static int launch_route_lists(int T, int E, int k, void* ws, cudaStream_t s) {
     err = cudaFuncSetAttribute(route_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
   });
   if (err != cudaSuccess) return cuda_status(err, "route lists smem attribute");
-  QW_LAUNCH_PDL("moe route lists", route_lists_kernel, dim3(1), dim3(1024), smem, s, T, E, k, ws);
+  QW_LAUNCH_PDL("moe route lists", route_lists_kernel, dim3(1), dim3(1024), smem, s, T, E, k, lo, ne, ws);
   return QW_OK;
 }
 
@@ -1390,7 +1399,7 @@ static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bo
   if (p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);
   // the streaming kernels read the lists from the workspace (built once, before gate/up)
   if (up) {
-    const int rc = launch_route_lists(a.T, a.E, a.k, a.ws, s);
+    const int rc = launch_route_lists(a.T, a.E, a.k, a.e_lo, a.e_cnt, a.ws, s);
     if (rc != QW_OK) return rc;
   }
   // the arithmetic of the bulk kernels (raw-nibble gate/up, fp16 down): a token's expert
@@ -1481,14 +1490,18 @@ extern "C" int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t exper
   QW_CHECK_ARG(workspace, "moe_route_lists: null pointer");
   QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && experts >= 1 && experts <= 1024 && top_k >= 1 && top_k <= 16 &&
                    top_k <= experts, "moe_route_lists: invalid shape");
-  return launch_route_lists(static_cast<int>(tokens), static_cast<int>(experts), static_cast<int>(top_k), workspace,
+  return launch_route_lists(static_cast<int>(tokens), static_cast<int>(experts), static_cast<int>(top_k), 0,
+                            static_cast<int>(experts), workspace,
                             as_stream(stream));
 }
 
 static int experts_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
                       const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
-                      int64_t top_k, int32_t group, void* workspace, void* stream, bool up, bool dn) {
-  QW_CHECK_ARG(x && gate_up && down && workspace, "moe_experts: null pointer");
+                      int64_t top_k, int32_t group, void* workspace, void* stream, bool up, bool dn,
+                      int64_t expert_lo = 0, int64_t expert_count = -1) {
+  if (expert_count < 0) expert_count = experts;
+  QW_CHECK_ARG(x && workspace && (expert_count == 0 || (gate_up && down)), "moe_experts: null pointer");
+  QW_CHECK_ARG(expert_lo >= 0 && expert_lo + expert_count <= experts, "moe_experts: expert range outside [0, experts)");
   QW_CHECK_ARG((shared_gate_up == nullptr) == (shared_down == nullptr), "moe_experts: shared expert pointers");
   QW_CHECK_ARG(group == 32 || group == 64 || group == 128, "moe_experts: group must be 32, 64 or 128");
   QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && hidden % group == 0 && inter % group == 0 && inter % 16 == 0 &&
@@ -1510,6 +1523,8 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   a.part = w.part;
   a.T = T; a.H = H; a.I = I; a.E = E; a.k = k;
   a.has_shared = shared_gate_up != nullptr;
+  a.e_lo = static_cast<int>(expert_lo);
+  a.e_cnt = static_cast<int>(expert_count);
   cudaStream_t s = as_stream(stream);
   switch (group) {
     case 128: return launch_experts_w4<128>(a, s, up, dn);
@@ -1524,6 +1539,14 @@ extern "C" int qw_moe_experts_w4(const void* x, const void* gate_up, const void*
                                  int32_t group, void* workspace, void* stream) {
   return experts_w4(x, gate_up, down, shared_gate_up, shared_down, tokens, hidden, experts, inter, top_k, group,
                     workspace, stream, true, true);
+}
+
+extern "C" int qw_moe_experts_w4_range(const void* x, const void* gate_up, const void* down,
+                                       const void* shared_gate_up, const void* shared_down, int64_t tokens,
+                                       int64_t hidden, int64_t experts, int64_t inter, int64_t top_k, int32_t group,
+                                       int64_t expert_lo, int64_t expert_count, void* workspace, void* stream) {
+  return experts_w4(x, gate_up, down, shared_gate_up, shared_down, tokens, hidden, experts, inter, top_k, group,
+                    workspace, stream, true, true, expert_lo, expert_count);
 }
 
 extern "C" int qw_moe_up_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
@@ -1634,7 +1657,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     st = launch_route<__half>(w.logits, E, T, E, k, -1, 1, w.route, nullptr, 256, 32, s);
   }
   if (st) return st;
-  st = launch_route_lists(T, E, k, w.route, s);
+  st = launch_route_lists(T, E, k, 0, E, w.route, s);
   if (st) return st;
   if (dtype == QW_BF16) {
     MoeArgs<__nv_bfloat16> a{};
@@ -1644,7 +1667,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     a.gu_stride = 2LL * I * H * 2; a.dn_stride = 1LL * H * I * 2;
     a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
     a.ws = w.route; a.hbuf = static_cast<__nv_bfloat16*>(w.hbuf); a.part = w.part;
-    a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
+    a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0; a.e_lo = 0; a.e_cnt = E;
     st = launch_experts<RowFmt<__nv_bfloat16>, 2>(a, s, true, true);
     if (st) return st;
     moe_combine_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__nv_bfloat16*>(out), T, H, E, k, 0, 0);
@@ -1656,7 +1679,7 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     a.gu_stride = 2LL * I * H * 2; a.dn_stride = 1LL * H * I * 2;
     a.gu_ld = 2LL * H; a.dn_ld = 2LL * I;
     a.ws = w.route; a.hbuf = static_cast<__half*>(w.hbuf); a.part = w.part;
-    a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0;
+    a.T = T; a.H = H; a.I = I; a.E = E; a.k = k; a.has_shared = 0; a.e_lo = 0; a.e_cnt = E;
     st = launch_experts<RowFmt<__half>, 2>(a, s, true, true);
     if (st) return st;
     moe_combine_kernel<__half><<<T, 256, 0, s>>>(w.part, w.route, static_cast<__half*>(out), T, H, E, k, 0, 0);
@@ -1667,5 +1690,175 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
     cudaError_t e = cudaMemcpyAsync(topk_idx_out, rv.topk_idx, sizeof(int32_t) * T * k, cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return cuda_status(e, "moe topk copy");
   }
+  return QW_OK;
+}
+
+// ------------------------------------------------------------------ expert parallelism
+// Experts sharded over G ranks (rank g owns experts [g E/G, (g+1) E/G)): each rank routes
+// its own tokens over all E experts, sends every (token, slot) pair's activation row to
+// the owning rank, each rank runs its local experts on the rows it received, and the
+// results come back to the source rank's per-(token, slot) outputs, where the usual
+// combine reads them.  The exchanges are two all-to-alls of fixed-size segments (cap
+// rows per destination, cap >= tokens * top_k so nothing can overflow), made by the
+// host's collective library between these kernels.  Every expert output is computed by
+// the same kernels as on one GPU (they give a row the same bits whatever else is in the
+// launch) and crosses ranks as bf16, the precision the combine reads it at, so the
+// result is bit-identical to the single-GPU MoE.
+namespace qw {
+
+struct EpPair {
+  int dest, pos;
+};
+
+// Destination rank and position in its segment of pair p (pairs in index order).
+__device__ __forceinline__ EpPair ep_place(const int32_t* idx, int p, int el) {
+  const int d = idx[p] / el;
+  int pos = 0;
+  for (int q = 0; q < p; ++q) pos += idx[q] / el == d;
+  return EpPair{d, pos};
+}
+
+// One CTA per pair: its row to send_rows[dest][pos]; CTA 0 also writes the segment
+// headers.  meta[g][0] = rows for rank g, meta[g][1 + pos] = (pair << 8) | local expert.
+__global__ void ep_pack_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ x, int T, int H,
+                               int k, int G, int el, int cap, __nv_bfloat16* __restrict__ rows,
+                               int32_t* __restrict__ meta) {
+  pdl_wait();
+  pdl_trigger();
+  const int np = T * k;
+  if (blockIdx.x == 0) {
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+      int c = 0;
+      for (int q = 0; q < np; ++q) c += idx[q] / el == g;
+      meta[static_cast<int64_t>(g) * (cap + 1)] = c;
+    }
+  }
+  const int p = blockIdx.x;
+  if (p >= np) return;
+  const EpPair pl = ep_place(idx, p, el);
+  if (threadIdx.x == 0)
+    meta[static_cast<int64_t>(pl.dest) * (cap + 1) + 1 + pl.pos] = (p << 8) | (idx[p] - pl.dest * el);
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(p / k) * H);
+  uint4* dst = reinterpret_cast<uint4*>(rows + (static_cast<int64_t>(pl.dest) * cap + pl.pos) * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// The receiving rank's routing of its G * cap received rows: top-1 = the row's local
+// expert, invalid past each segment's count (left out by the expert kernels).
+__global__ void ep_recv_route_kernel(const int32_t* __restrict__ meta, int G, int cap, int el, void* ws) {
+  pdl_wait();
+  pdl_trigger();
+  const int T = G * cap;
+  const RouteView rv = route_view(ws, T, el, 1);
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < T; r += gridDim.x * blockDim.x) {
+    const int g = r / cap, j = r % cap;
+    const int32_t* m = meta + static_cast<int64_t>(g) * (cap + 1);
+    const bool valid = j < m[0];
+    rv.topk_idx[r] = valid ? (m[1 + j] & 0xFF) : -1;
+    rv.topk_w[r] = 1.f;
+    rv.shared_gate[r] = 0.f;
+  }
+}
+
+// Received rows' expert outputs (slot 0 of the receiving routing) -> bf16 send segments.
+__global__ void ep_pack_out_kernel(const float* __restrict__ part, const int32_t* __restrict__ meta, int G, int cap,
+                                   int H, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x, g = r / cap, j = r % cap;
+  if (j >= meta[static_cast<int64_t>(g) * (cap + 1)]) return;
+  const float* src = part + static_cast<int64_t>(r) * 2 * H;   // [T_r][k + 1 = 2][H], slot 0
+  __nv_bfloat16* dst = out + static_cast<int64_t>(r) * H;
+  for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
+    const float2 v = *reinterpret_cast<const float2*>(src + 2 * i);
+    *reinterpret_cast<__nv_bfloat162*>(dst + 2 * i) = __floats2bfloat162_rn(v.x, v.y);
+  }
+}
+
+// The results back into the source routing's per-(token, slot) outputs.
+__global__ void ep_scatter_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ back, int T,
+                                  int H, int k, int el, int cap, float* __restrict__ part) {
+  pdl_wait();
+  pdl_trigger();
+  const int p = blockIdx.x;
+  if (p >= T * k) return;
+  const EpPair pl = ep_place(idx, p, el);
+  const __nv_bfloat16* src = back + (static_cast<int64_t>(pl.dest) * cap + pl.pos) * H;
+  float* dst = part + (static_cast<int64_t>(p / k) * (k + 1) + p % k) * H;
+  for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
+    const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * i));
+    *reinterpret_cast<float2*>(dst + 2 * i) = v;
+  }
+}
+
+static int ep_check(int64_t tokens, int64_t hidden, int64_t experts, int64_t top_k, int64_t ranks, int64_t cap) {
+  QW_CHECK_ARG(tokens >= 1 && tokens * top_k <= 4096 && top_k >= 1 && top_k <= 16 && hidden % 8 == 0 && hidden > 0,
+               "moe_ep: invalid shape (tokens * top_k <= 4096, hidden % 8 == 0)");
+  QW_CHECK_ARG(ranks >= 1 && experts % ranks == 0 && experts / ranks <= 256, "moe_ep: experts must split evenly, <= 256 per rank");
+  QW_CHECK_ARG(cap >= tokens * top_k && cap < (1 << 22), "moe_ep: cap must be >= tokens * top_k");
+  return QW_OK;
+}
+
+}  // namespace qw
+
+extern "C" int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+                                                  int64_t inter) {
+  if (ranks <= 0 || cap <= 0 || experts % ranks) return -1;
+  return qw_moe_workspace_bytes(ranks * cap, hidden, experts / ranks, inter, 1);
+}
+
+extern "C" int qw_moe_ep_pack(const void* workspace, const void* x, int64_t tokens, int64_t hidden, int64_t experts,
+                              int64_t top_k, int64_t ranks, int64_t cap, void* send_rows, int32_t* send_meta,
+                              void* stream) {
+  QW_CHECK_ARG(workspace && x && send_rows && send_meta, "moe_ep_pack: null pointer");
+  const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
+  if (st) return st;
+  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(send_rows) & 15) == 0,
+               "moe_ep_pack: x and send_rows must be 16-byte aligned");
+  const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
+  const RouteView rv = route_view(const_cast<void*>(workspace), T, E, k);
+  QW_LAUNCH_PDL("moe ep pack", ep_pack_kernel, dim3(static_cast<unsigned>(T * k)), dim3(128), 0, as_stream(stream),
+                rv.topk_idx, static_cast<const __nv_bfloat16*>(x), T, static_cast<int>(hidden), k,
+                static_cast<int>(ranks), static_cast<int>(experts / ranks), static_cast<int>(cap),
+                static_cast<__nv_bfloat16*>(send_rows), send_meta);
+  return QW_OK;
+}
+
+extern "C" int qw_moe_ep_recv_route(const int32_t* recv_meta, int64_t ranks, int64_t cap, int64_t experts,
+                                    void* recv_workspace, void* stream) {
+  QW_CHECK_ARG(recv_meta && recv_workspace, "moe_ep_recv_route: null pointer");
+  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && experts / ranks <= 256, "moe_ep_recv_route: shape");
+  QW_LAUNCH_PDL("moe ep recv route", ep_recv_route_kernel, dim3(static_cast<unsigned>((ranks * cap + 255) / 256)),
+                dim3(256), 0, as_stream(stream), recv_meta, static_cast<int>(ranks), static_cast<int>(cap),
+                static_cast<int>(experts / ranks), recv_workspace);
+  return QW_OK;
+}
+
+extern "C" int qw_moe_ep_pack_out(const void* recv_workspace, const int32_t* recv_meta, int64_t ranks, int64_t cap,
+                                  int64_t hidden, int64_t experts, int64_t inter, void* send_back, void* stream) {
+  QW_CHECK_ARG(recv_workspace && recv_meta && send_back, "moe_ep_pack_out: null pointer");
+  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && hidden % 2 == 0, "moe_ep_pack_out: shape");
+  const int Tr = static_cast<int>(ranks * cap), H = static_cast<int>(hidden);
+  WsParts w = split_ws(const_cast<void*>(recv_workspace), Tr, H, static_cast<int>(experts / ranks),
+                       static_cast<int>(inter), 1);
+  QW_LAUNCH_PDL("moe ep pack out", ep_pack_out_kernel, dim3(static_cast<unsigned>(Tr)), dim3(256), 0,
+                as_stream(stream), w.part, recv_meta, static_cast<int>(ranks), static_cast<int>(cap), H,
+                static_cast<__nv_bfloat16*>(send_back));
+  return QW_OK;
+}
+
+extern "C" int qw_moe_ep_scatter(void* workspace, const void* recv_back, int64_t tokens, int64_t hidden,
+                                 int64_t experts, int64_t inter, int64_t top_k, int64_t ranks, int64_t cap,
+                                 void* stream) {
+  QW_CHECK_ARG(workspace && recv_back, "moe_ep_scatter: null pointer");
+  const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
+  if (st) return st;
+  const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
+            k = static_cast<int>(top_k);
+  const RouteView rv = route_view(workspace, T, E, k);
+  WsParts w = split_ws(workspace, T, H, E, static_cast<int>(inter), k);
+  QW_LAUNCH_PDL("moe ep scatter", ep_scatter_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0,
+                as_stream(stream), rv.topk_idx, static_cast<const __nv_bfloat16*>(recv_back), T, H, k,
+                static_cast<int>(experts / ranks), static_cast<int>(cap), w.part);
   return QW_OK;
 }
