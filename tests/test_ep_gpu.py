@@ -20,6 +20,7 @@ def _worker(rank, world, port, cases):
     import __graft_entry__
     __graft_entry__.load_package()
     from qwen35_dflash_b200 import ep, lib, w4
+    from oracle import ep_np
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
@@ -69,6 +70,13 @@ def _worker(rank, world, port, cases):
                 if not torch.equal(out1, out2):
                     bad = (out1 != out2).sum().item()
                     raise AssertionError(f"rank {rank} case {(t, h, e, k, inter, g)}: {bad} elements differ")
+            # the packed segments are the protocol's (oracle/ep_np.py)
+            topk = ws2[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
+            rows, meta = ep_np.pack(topk, x.float().cpu().numpy(), e, world, t * k)
+            assert (moe.send_meta.cpu().numpy() == meta).all()
+            for d in range(world):
+                n = int(meta[d, 0])
+                assert torch.equal(moe.send_rows[d, :n].float().cpu(), torch.from_numpy(rows[d, :n]))
         dist.barrier()
     finally:
         dist.destroy_process_group()
