@@ -208,7 +208,9 @@ def run_ours(args, rank, world, local_rank):
     capacity = (capacity + 15) // 16 * 16
     t_init = time.perf_counter()
     weights = E.weights_random(cfg, seed=2, device=dev)
-    eng = E.TargetEngine(cfg, weights, batch=B, block=S, capacity=capacity, device=dev)
+    ep = args.ep and world > 1
+    eng = E.TargetEngine(cfg, weights, batch=B, block=S, capacity=capacity, device=dev,
+                         ep_group=dist.group.WORLD if ep else None)
     eng.set_random_context(args.ctx, seed=3 + rank)
     torch.cuda.synchronize(dev)
     init_s = time.perf_counter() - t_init
@@ -303,10 +305,14 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random-init weights N(0,0.02) W4A16 g128, seeded KV/GDN context and proposals)",
-            "config": {"workload": "full target verify forward, 1 GPU per replica (benchmark config 4)",
+            "config": {"workload": ("full target verify forward, experts sharded over the GPUs "
+                                    "(benchmark config 4 per GPU, config 5's expert parallelism)") if ep else
+                                   "full target verify forward, 1 GPU per replica (benchmark config 4)",
                        "model": "Qwen3.5-35B-A3B target (40 layers: 30 GDN + 10 attention)",
                        "global_batch": B * world, "block": S, "ctx": args.ctx, "seq_len": args.ctx + S,
-                       "parallelism": f"dp{world} (independent replicas)",
+                       "parallelism": (f"ep{world} (experts {cfg.num_experts // world} per GPU, all-to-all "
+                                       "dispatch/combine; attention/GDN per request)") if ep else
+                                      f"dp{world} (independent replicas)",
                        "l2": "no flush: each step streams ~8.5 GB of weights, far above the 126 MB L2",
                        "step_alg_bytes": alg["total"], "alg_bytes_parts": alg,
                        "routed_experts_per_layer_mean": round(sum(active.values()) / len(active), 1),
@@ -473,6 +479,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ep", action="store_true",
+                    help="with --gpus > 1: shard the routed experts over the GPUs (all-to-all dispatch/combine) "
+                         "instead of running independent replicas")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
@@ -487,6 +496,8 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"   # the version banner would go to stdout, ahead of the JSON line
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:

@@ -233,24 +233,31 @@ int qw_moe_experts_w4_range(const void* x, const void* gate_up, const void* down
 
 /* ------------------------------------------------------------------------------
  * Expert parallelism (experts [g E/G, (g+1) E/G) on rank g; dispatch and combine by
- * the host's all-to-all): the source rank packs each routed (token, slot) pair's row
- * for its expert's rank (qw_moe_ep_pack: send_rows bf16 [ranks][cap][hidden],
- * send_meta int32 [ranks][cap + 1], cap >= tokens * top_k); after the all-to-all the
- * receiving rank routes what it got (qw_moe_ep_recv_route into a workspace of
- * qw_moe_ep_recv_workspace_bytes), runs qw_moe_experts_w4_range over ranks * cap rows
- * (top_k 1, its experts, no shared expert), packs the outputs (qw_moe_ep_pack_out) and
- * the all-to-all returns them; qw_moe_ep_scatter writes them into the source routing's
- * per-(token, slot) outputs for qw_moe_combine(_norm).  Bit-identical to the one-GPU
- * MoE.  No counterpart in the reference (its plan for multi-GPU serving).
+ * the host's all-to-all of fixed segments): the source rank packs each routed
+ * (token, slot) pair's row for its expert's rank (qw_moe_ep_pack into send segments
+ * bf16 [ranks][cap + 1][hidden]: row 0 of a segment is its header of int32 words
+ * [count, (pair << 8) | local expert, ...], rows 1.. the pairs' rows; cap >=
+ * tokens * top_k and (cap + 1) * 4 <= hidden * 2); after the all-to-all the receiving
+ * rank routes the ranks * (cap + 1) rows of its received segments as they lie (header
+ * rows and rows past a segment's count invalid) and builds its expert lists
+ * (qw_moe_ep_recv_route into a workspace of qw_moe_ep_recv_workspace_bytes), runs its
+ * experts over them (qw_moe_ep_experts: top_k 1, no shared expert; the lists are not
+ * rebuilt), packs the outputs into return segments of the same layout
+ * (qw_moe_ep_pack_out), and after the all-to-all
+ * back qw_moe_ep_scatter writes them into the source routing's per-(token, slot)
+ * outputs for qw_moe_combine(_norm).  Bit-identical to the one-GPU MoE.  No counterpart
+ * in the reference (its plan for multi-GPU serving).
  * ---------------------------------------------------------------------------- */
 int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                                        int64_t inter);
 int qw_moe_ep_pack(const void* workspace, const void* x, int64_t tokens, int64_t hidden, int64_t experts,
-                   int64_t top_k, int64_t ranks, int64_t cap, void* send_rows, int32_t* send_meta,
-                   void* stream);
-int qw_moe_ep_recv_route(const int32_t* recv_meta, int64_t ranks, int64_t cap, int64_t experts,
+                   int64_t top_k, int64_t ranks, int64_t cap, void* send_seg, void* stream);
+int qw_moe_ep_recv_route(const void* recv_seg, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                          void* recv_workspace, void* stream);
-int qw_moe_ep_pack_out(const void* recv_workspace, const int32_t* recv_meta, int64_t ranks, int64_t cap,
+int qw_moe_ep_experts(const void* recv_seg, const void* gate_up_local, const void* down_local, int64_t ranks,
+                      int64_t cap, int64_t hidden, int64_t experts, int64_t inter, int32_t group,
+                      void* recv_workspace, void* stream);
+int qw_moe_ep_pack_out(const void* recv_workspace, const void* recv_seg, int64_t ranks, int64_t cap,
                        int64_t hidden, int64_t experts, int64_t inter, void* send_back, void* stream);
 int qw_moe_ep_scatter(void* workspace, const void* recv_back, int64_t tokens, int64_t hidden,
                       int64_t experts, int64_t inter, int64_t top_k, int64_t ranks, int64_t cap,

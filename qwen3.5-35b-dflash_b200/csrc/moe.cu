@@ -1390,7 +1390,8 @@ static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p,
 }
 
 template <int G>
-static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bool up, bool down) {
+static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bool up, bool down,
+                             bool lists_ready) {
   const XtPlan p = xt_plan<G>(a);
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   int32_t* status = rv.n_active + 1;
@@ -1398,7 +1399,7 @@ static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bo
   // halves of one MoE always come from the same pair
   if (p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);
   // the streaming kernels read the lists from the workspace (built once, before gate/up)
-  if (up) {
+  if (up && !lists_ready) {
     const int rc = launch_route_lists(a.T, a.E, a.k, a.e_lo, a.e_cnt, a.ws, s);
     if (rc != QW_OK) return rc;
   }
@@ -1498,7 +1499,7 @@ extern "C" int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t exper
 static int experts_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
                       const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
                       int64_t top_k, int32_t group, void* workspace, void* stream, bool up, bool dn,
-                      int64_t expert_lo = 0, int64_t expert_count = -1) {
+                      int64_t expert_lo = 0, int64_t expert_count = -1, bool lists_ready = false) {
   if (expert_count < 0) expert_count = experts;
   QW_CHECK_ARG(x && workspace && (expert_count == 0 || (gate_up && down)), "moe_experts: null pointer");
   QW_CHECK_ARG(expert_lo >= 0 && expert_lo + expert_count <= experts, "moe_experts: expert range outside [0, experts)");
@@ -1527,9 +1528,9 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   a.e_cnt = static_cast<int>(expert_count);
   cudaStream_t s = as_stream(stream);
   switch (group) {
-    case 128: return launch_experts_w4<128>(a, s, up, dn);
-    case 64: return launch_experts_w4<64>(a, s, up, dn);
-    default: return launch_experts_w4<32>(a, s, up, dn);
+    case 128: return launch_experts_w4<128>(a, s, up, dn, lists_ready);
+    case 64: return launch_experts_w4<64>(a, s, up, dn, lists_ready);
+    default: return launch_experts_w4<32>(a, s, up, dn, lists_ready);
   }
 }
 
@@ -1706,69 +1707,85 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
 // result is bit-identical to the single-GPU MoE.
 namespace qw {
 
-struct EpPair {
-  int dest, pos;
-};
-
-// Destination rank and position in its segment of pair p (pairs in index order).
-__device__ __forceinline__ EpPair ep_place(const int32_t* idx, int p, int el) {
-  const int d = idx[p] / el;
+// Position of pair p in its destination's segment: the earlier pairs with the same
+// destination, counted by the whole CTA (every thread calls it with the same p).
+__device__ __forceinline__ int ep_pos(const int32_t* idx, int p, int d, int el) {
   int pos = 0;
-  for (int q = 0; q < p; ++q) pos += idx[q] / el == d;
-  return EpPair{d, pos};
+  for (int q0 = 0; q0 < p; q0 += blockDim.x) {
+    const int q = q0 + threadIdx.x;
+    pos += __syncthreads_count(q < p && idx[q] / el == d);
+  }
+  return pos;
 }
 
-// One CTA per pair: its row to send_rows[dest][pos]; CTA 0 also writes the segment
-// headers.  meta[g][0] = rows for rank g, meta[g][1 + pos] = (pair << 8) | local expert.
+// Segment g of the send buffer: cap + 1 rows of hidden bf16; row 0 is the header
+// (int32 words: [count, (pair << 8) | local expert, ...]), rows 1 .. the pairs' rows.
+// One CTA per pair writes its row and header word; CTA 0 also writes the counts.
 __global__ void ep_pack_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ x, int T, int H,
-                               int k, int G, int el, int cap, __nv_bfloat16* __restrict__ rows,
-                               int32_t* __restrict__ meta) {
+                               int k, int G, int el, int cap, __nv_bfloat16* __restrict__ seg) {
   pdl_wait();
   pdl_trigger();
   const int np = T * k;
+  const int64_t segw = static_cast<int64_t>(cap + 1) * H;   // elements per segment
   if (blockIdx.x == 0) {
-    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    for (int g = 0; g < G; ++g) {
       int c = 0;
-      for (int q = 0; q < np; ++q) c += idx[q] / el == g;
-      meta[static_cast<int64_t>(g) * (cap + 1)] = c;
+      for (int q0 = 0; q0 < np; q0 += blockDim.x) {
+        const int q = q0 + threadIdx.x;
+        c += __syncthreads_count(q < np && idx[q] / el == g);
+      }
+      if (threadIdx.x == 0) reinterpret_cast<int32_t*>(seg + g * segw)[0] = c;
     }
   }
   const int p = blockIdx.x;
   if (p >= np) return;
-  const EpPair pl = ep_place(idx, p, el);
-  if (threadIdx.x == 0)
-    meta[static_cast<int64_t>(pl.dest) * (cap + 1) + 1 + pl.pos] = (p << 8) | (idx[p] - pl.dest * el);
+  const int d = idx[p] / el;
+  const int pos = ep_pos(idx, p, d, el);
+  if (threadIdx.x == 0) reinterpret_cast<int32_t*>(seg + d * segw)[1 + pos] = (p << 8) | (idx[p] - d * el);
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(p / k) * H);
-  uint4* dst = reinterpret_cast<uint4*>(rows + (static_cast<int64_t>(pl.dest) * cap + pl.pos) * H);
+  uint4* dst = reinterpret_cast<uint4*>(seg + d * segw + static_cast<int64_t>(1 + pos) * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
 }
 
-// The receiving rank's routing of its G * cap received rows: top-1 = the row's local
-// expert, invalid past each segment's count (left out by the expert kernels).
-__global__ void ep_recv_route_kernel(const int32_t* __restrict__ meta, int G, int cap, int el, void* ws) {
+// The receiving rank's routing of the G (cap + 1) rows of its received segments, taken
+// as they lie (row r = segment r / (cap + 1), row r % (cap + 1) of it): top-1 = the
+// row's local expert; the header rows and the rows past each segment's count are
+// invalid (left out by the expert kernels).  Then, as qw_moe_route_lists, the expert
+// lists.  One CTA.  Dynamic smem: 3 el + 64 ints.
+__global__ void __launch_bounds__(1024) ep_recv_route_kernel(const __nv_bfloat16* __restrict__ seg, int G, int cap,
+                                                             int H, int el, void* ws) {
+  extern __shared__ __align__(16) uint8_t smem[];
   pdl_wait();
   pdl_trigger();
-  const int T = G * cap;
+  const int T = G * (cap + 1);
+  const int64_t segw = static_cast<int64_t>(cap + 1) * H;
   const RouteView rv = route_view(ws, T, el, 1);
-  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < T; r += gridDim.x * blockDim.x) {
-    const int g = r / cap, j = r % cap;
-    const int32_t* m = meta + static_cast<int64_t>(g) * (cap + 1);
-    const bool valid = j < m[0];
-    rv.topk_idx[r] = valid ? (m[1 + j] & 0xFF) : -1;
+  for (int r = threadIdx.x; r < T; r += blockDim.x) {
+    const int32_t* m = reinterpret_cast<const int32_t*>(seg + (r / (cap + 1)) * segw);
+    const int j = r % (cap + 1) - 1;
+    rv.topk_idx[r] = j >= 0 && j < m[0] ? (m[1 + j] & 0xFF) : -1;
     rv.topk_w[r] = 1.f;
     rv.shared_gate[r] = 0.f;
   }
+  __syncthreads();
+  int* scratch = reinterpret_cast<int*>(smem);
+  build_route_lists(rv.topk_idx, T, el, 1, 0, scratch, scratch + 3 * el, rv.n_active, rv.active, rv.pair_off,
+                    rv.pair_tok, rv.pair_slot);
 }
 
-// Received rows' expert outputs (slot 0 of the receiving routing) -> bf16 send segments.
-__global__ void ep_pack_out_kernel(const float* __restrict__ part, const int32_t* __restrict__ meta, int G, int cap,
-                                   int H, __nv_bfloat16* __restrict__ out) {
+// Received rows' expert outputs (slot 0 of the receiving routing) -> bf16 return
+// segments of the same layout (row 0 unused, row 1 + j the output of received row j).
+// One CTA per pair row (G cap CTAs).
+__global__ void ep_pack_out_kernel(const float* __restrict__ part, const __nv_bfloat16* __restrict__ seg_in, int G,
+                                   int cap, int H, __nv_bfloat16* __restrict__ seg_out) {
   pdl_wait();
   pdl_trigger();
-  const int r = blockIdx.x, g = r / cap, j = r % cap;
-  if (j >= meta[static_cast<int64_t>(g) * (cap + 1)]) return;
-  const float* src = part + static_cast<int64_t>(r) * 2 * H;   // [T_r][k + 1 = 2][H], slot 0
-  __nv_bfloat16* dst = out + static_cast<int64_t>(r) * H;
+  const int g = blockIdx.x / cap, j = blockIdx.x % cap;
+  const int64_t segw = static_cast<int64_t>(cap + 1) * H;
+  if (j >= reinterpret_cast<const int32_t*>(seg_in + g * segw)[0]) return;
+  const int64_t r = static_cast<int64_t>(g) * (cap + 1) + 1 + j;   // the receiving routing's row
+  const float* src = part + r * 2 * H;   // [T_r][k + 1 = 2][H], slot 0
+  __nv_bfloat16* dst = seg_out + r * H;
   for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
     const float2 v = *reinterpret_cast<const float2*>(src + 2 * i);
     *reinterpret_cast<__nv_bfloat162*>(dst + 2 * i) = __floats2bfloat162_rn(v.x, v.y);
@@ -1782,8 +1799,9 @@ __global__ void ep_scatter_kernel(const int32_t* __restrict__ idx, const __nv_bf
   pdl_trigger();
   const int p = blockIdx.x;
   if (p >= T * k) return;
-  const EpPair pl = ep_place(idx, p, el);
-  const __nv_bfloat16* src = back + (static_cast<int64_t>(pl.dest) * cap + pl.pos) * H;
+  const int d = idx[p] / el;
+  const int pos = ep_pos(idx, p, d, el);
+  const __nv_bfloat16* src = back + d * static_cast<int64_t>(cap + 1) * H + static_cast<int64_t>(1 + pos) * H;
   float* dst = part + (static_cast<int64_t>(p / k) * (k + 1) + p % k) * H;
   for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
     const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * i));
@@ -1795,7 +1813,9 @@ static int ep_check(int64_t tokens, int64_t hidden, int64_t experts, int64_t top
   QW_CHECK_ARG(tokens >= 1 && tokens * top_k <= 4096 && top_k >= 1 && top_k <= 16 && hidden % 8 == 0 && hidden > 0,
                "moe_ep: invalid shape (tokens * top_k <= 4096, hidden % 8 == 0)");
   QW_CHECK_ARG(ranks >= 1 && experts % ranks == 0 && experts / ranks <= 256, "moe_ep: experts must split evenly, <= 256 per rank");
-  QW_CHECK_ARG(cap >= tokens * top_k && cap < (1 << 22), "moe_ep: cap must be >= tokens * top_k");
+  QW_CHECK_ARG(cap >= tokens * top_k && ranks * (cap + 1) <= 4096, "moe_ep: cap must be >= tokens * top_k, "
+               "ranks * (cap + 1) <= 4096");
+  QW_CHECK_ARG((cap + 1) * 4 <= hidden * 2, "moe_ep: the segment header (cap + 1 words) must fit in one row");
   return QW_OK;
 }
 
@@ -1804,46 +1824,58 @@ static int ep_check(int64_t tokens, int64_t hidden, int64_t experts, int64_t top
 extern "C" int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                                                   int64_t inter) {
   if (ranks <= 0 || cap <= 0 || experts % ranks) return -1;
-  return qw_moe_workspace_bytes(ranks * cap, hidden, experts / ranks, inter, 1);
+  return qw_moe_workspace_bytes(ranks * (cap + 1), hidden, experts / ranks, inter, 1);
 }
 
 extern "C" int qw_moe_ep_pack(const void* workspace, const void* x, int64_t tokens, int64_t hidden, int64_t experts,
-                              int64_t top_k, int64_t ranks, int64_t cap, void* send_rows, int32_t* send_meta,
-                              void* stream) {
-  QW_CHECK_ARG(workspace && x && send_rows && send_meta, "moe_ep_pack: null pointer");
+                              int64_t top_k, int64_t ranks, int64_t cap, void* send_seg, void* stream) {
+  QW_CHECK_ARG(workspace && x && send_seg, "moe_ep_pack: null pointer");
   const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
   if (st) return st;
-  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(send_rows) & 15) == 0,
-               "moe_ep_pack: x and send_rows must be 16-byte aligned");
+  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(send_seg) & 15) == 0,
+               "moe_ep_pack: x and the segments must be 16-byte aligned");
   const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
   const RouteView rv = route_view(const_cast<void*>(workspace), T, E, k);
-  QW_LAUNCH_PDL("moe ep pack", ep_pack_kernel, dim3(static_cast<unsigned>(T * k)), dim3(128), 0, as_stream(stream),
+  QW_LAUNCH_PDL("moe ep pack", ep_pack_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0, as_stream(stream),
                 rv.topk_idx, static_cast<const __nv_bfloat16*>(x), T, static_cast<int>(hidden), k,
                 static_cast<int>(ranks), static_cast<int>(experts / ranks), static_cast<int>(cap),
-                static_cast<__nv_bfloat16*>(send_rows), send_meta);
+                static_cast<__nv_bfloat16*>(send_seg));
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_recv_route(const int32_t* recv_meta, int64_t ranks, int64_t cap, int64_t experts,
+extern "C" int qw_moe_ep_recv_route(const void* recv_seg, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                                     void* recv_workspace, void* stream) {
-  QW_CHECK_ARG(recv_meta && recv_workspace, "moe_ep_recv_route: null pointer");
-  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && experts / ranks <= 256, "moe_ep_recv_route: shape");
-  QW_LAUNCH_PDL("moe ep recv route", ep_recv_route_kernel, dim3(static_cast<unsigned>((ranks * cap + 255) / 256)),
-                dim3(256), 0, as_stream(stream), recv_meta, static_cast<int>(ranks), static_cast<int>(cap),
-                static_cast<int>(experts / ranks), recv_workspace);
+  QW_CHECK_ARG(recv_seg && recv_workspace, "moe_ep_recv_route: null pointer");
+  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && experts / ranks <= 256 &&
+                   ranks * (cap + 1) <= 4096 && (cap + 1) * 4 <= hidden * 2, "moe_ep_recv_route: shape");
+  const int el = static_cast<int>(experts / ranks);
+  const size_t smem = (3 * static_cast<size_t>(el) + 64) * sizeof(int);
+  QW_LAUNCH_PDL("moe ep recv route", ep_recv_route_kernel, dim3(1), dim3(1024), smem, as_stream(stream),
+                static_cast<const __nv_bfloat16*>(recv_seg), static_cast<int>(ranks), static_cast<int>(cap),
+                static_cast<int>(hidden), el, recv_workspace);
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_pack_out(const void* recv_workspace, const int32_t* recv_meta, int64_t ranks, int64_t cap,
+extern "C" int qw_moe_ep_experts(const void* recv_seg, const void* gate_up_local, const void* down_local,
+                                 int64_t ranks, int64_t cap, int64_t hidden, int64_t experts, int64_t inter,
+                                 int32_t group, void* recv_workspace, void* stream) {
+  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0, "moe_ep_experts: shape");
+  // the received segments as G (cap + 1) rows, routed (lists included) by qw_moe_ep_recv_route
+  return experts_w4(recv_seg, gate_up_local, down_local, nullptr, nullptr, ranks * (cap + 1), hidden,
+                    experts / ranks, inter, 1, group, recv_workspace, stream, true, true, 0, experts / ranks,
+                    true);
+}
+
+extern "C" int qw_moe_ep_pack_out(const void* recv_workspace, const void* recv_seg, int64_t ranks, int64_t cap,
                                   int64_t hidden, int64_t experts, int64_t inter, void* send_back, void* stream) {
-  QW_CHECK_ARG(recv_workspace && recv_meta && send_back, "moe_ep_pack_out: null pointer");
+  QW_CHECK_ARG(recv_workspace && recv_seg && send_back, "moe_ep_pack_out: null pointer");
   QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && hidden % 2 == 0, "moe_ep_pack_out: shape");
-  const int Tr = static_cast<int>(ranks * cap), H = static_cast<int>(hidden);
+  const int Tr = static_cast<int>(ranks * (cap + 1)), H = static_cast<int>(hidden);
   WsParts w = split_ws(const_cast<void*>(recv_workspace), Tr, H, static_cast<int>(experts / ranks),
                        static_cast<int>(inter), 1);
-  QW_LAUNCH_PDL("moe ep pack out", ep_pack_out_kernel, dim3(static_cast<unsigned>(Tr)), dim3(256), 0,
-                as_stream(stream), w.part, recv_meta, static_cast<int>(ranks), static_cast<int>(cap), H,
-                static_cast<__nv_bfloat16*>(send_back));
+  QW_LAUNCH_PDL("moe ep pack out", ep_pack_out_kernel, dim3(static_cast<unsigned>(ranks * cap)), dim3(256), 0,
+                as_stream(stream), w.part, static_cast<const __nv_bfloat16*>(recv_seg), static_cast<int>(ranks),
+                static_cast<int>(cap), H, static_cast<__nv_bfloat16*>(send_back));
   return QW_OK;
 }
 

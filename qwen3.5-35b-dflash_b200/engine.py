@@ -150,7 +150,7 @@ def weights_random(cfg: TargetConfig, seed: int = 2, std: float = 0.02, device="
 
 class TargetEngine:
     def __init__(self, cfg: TargetConfig, weights, *, batch: int, block: int = 16, capacity: int = 4096,
-                 page_size: int = 16, device="cuda"):
+                 page_size: int = 16, device="cuda", ep_group=None):
         if not 1 <= block <= lib.QW_MAX_BLOCK:
             raise ValueError(f"block must be in [1, {lib.QW_MAX_BLOCK}]")
         self.cfg, self.B, self.S, self.device = cfg, batch, block, torch.device(device)
@@ -189,6 +189,21 @@ class TargetEngine:
             T, H, c.num_experts, c.moe_intermediate_size, c.num_experts_per_tok), dtype=torch.uint8, device=dev)
         self.features = torch.zeros(T, c.feature_width, dtype=BF16, device=dev)
         self.vocab_pad = (c.vocab_size + 15) // 16 * 16
+        # expert parallelism: this rank keeps only its slice of every routed expert bank
+        # (the shared weights object is not modified) and exchanges rows with the group
+        self.ep_moe = None
+        if ep_group is not None:
+            from . import ep as _ep
+            import torch.distributed as dist
+            G, rank = dist.get_world_size(ep_group), dist.get_rank(ep_group)
+            E = c.num_experts
+            self.ep_gu = [_ep.local_expert_streams(lw.gate_up, E, G, rank) if lw.gate_up is not None else None
+                          for lw in self.layers]
+            self.ep_dn = [_ep.local_expert_streams(lw.down, E, G, rank) if lw.down is not None else None
+                          for lw in self.layers]
+            self.ep_moe = _ep.ExpertParallelMoE(ep_group, tokens=T, hidden=H, experts=E,
+                                                inter=c.moe_intermediate_size, top_k=c.num_experts_per_tok,
+                                                quant_group=c.quant_group, device=dev)
         self.nblk = self.lib.qw_lmhead_blocks(self.vocab_pad)
         self.keys = torch.zeros(self.nblk, T, dtype=torch.int64, device=dev)
         self.top1 = torch.zeros(T, dtype=torch.int32, device=dev)
@@ -234,7 +249,9 @@ class TargetEngine:
         lib.check(getattr(self.lib, name)(*args), name)
 
     # kernels each entry point launches (all others launch one)
-    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2}
+    # (expert-parallel MoE layer: shared expert 2, pack, receive routing, lists + gate/up +
+    # down of the received rows, output pack, scatter; the all-to-alls are the library's)
+    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2, "qw_moe_ep": 8}
 
     def launches_per_step(self) -> int:
         """Kernels of this library in the captured step (counted from the entry calls)."""
@@ -298,9 +315,15 @@ class TargetEngine:
             E, k, I = c.num_experts, c.num_experts_per_tok, c.moe_intermediate_size
             self._call("qw_moe_route_x", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
                        lib.QW_BF16, self.normed.data_ptr(), H, c.quant_group, self.moe_ws.data_ptr(), st)
-            self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
-                       lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
-                       self.moe_ws.data_ptr(), st)
+            if self.ep_moe is not None:
+                if self._recording is not None:
+                    self._recording["qw_moe_ep"] = self._recording.get("qw_moe_ep", 0) + 1
+                self.ep_moe.experts(self.normed, self.moe_ws, self.ep_gu[l], self.ep_dn[l], lw.shared_gu,
+                                    lw.shared_down, st)
+            else:
+                self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
+                           lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
+                           self.moe_ws.data_ptr(), st)
             if after_moe_route is not None:
                 after_moe_route(l)
             # residual add of the MoE output + the next RMSNorm (next layer's input norm, or
@@ -338,8 +361,13 @@ class TargetEngine:
         self.commit_states()
 
     def active_experts(self) -> int:
-        """Distinct routed experts of the last routed layer (reads the workspace; syncs)."""
+        """Distinct routed experts of the last routed layer (reads the workspace; syncs);
+        with expert parallelism, this rank's experts that received rows."""
         c = self.cfg
+        if self.ep_moe is not None:
+            m = self.ep_moe
+            off = self.lib.qw_moe_active_experts(None, m.G * (m.cap + 1), m.el, 1)
+            return int(m.ws_r[off:off + 4].view(torch.int32).item())
         off = self.lib.qw_moe_active_experts(None, self.T, c.num_experts, c.num_experts_per_tok)
         return int(self.moe_ws[off:off + 4].view(torch.int32).item())
 

@@ -12,9 +12,10 @@ each rank routes its own tokens over all E experts (``qw_moe_route``), then
    empty routed range);
 2. ``qw_moe_ep_pack``: each pair's activation row into the send segment of the rank
    owning its expert (fixed ``cap`` rows per destination, ``cap = tokens * top_k``, so a
-   segment cannot overflow), with a header of counts and local expert ids;
-3. all-to-all of the headers and of the rows;
-4. ``qw_moe_ep_recv_route`` + ``qw_moe_experts_w4_range``: the received rows through the
+   segment cannot overflow), behind a header row of counts and local expert ids;
+3. all-to-all of the segments (optionally with the shared expert of step 1 on a side
+   stream meanwhile);
+4. ``qw_moe_ep_recv_route`` + ``qw_moe_ep_experts``: the received rows through the
    rank's own experts (top-1 routing, one expert per row);
 5. ``qw_moe_ep_pack_out`` + all-to-all back + ``qw_moe_ep_scatter``: the outputs into the
    source rank's per-(token, slot) slots.
@@ -55,10 +56,14 @@ def local_expert_streams(stream: torch.Tensor, experts: int, ranks: int, rank: i
 class ExpertParallelMoE:
     """The routed experts of MoE layers of one shape, sharded over ``group``.
 
-    ``tokens`` is the rank's own token count per call (every rank the same)."""
+    ``tokens`` is the rank's own token count per call (every rank the same).  With
+    ``overlap_shared`` the shared expert runs on a side stream beside the exchange;
+    otherwise (the default, faster on B200 at 16 tokens per rank: the expert kernels are
+    persistent over every SM, so the side stream delays the collective instead of hiding
+    it) it runs first on the caller's stream."""
 
     def __init__(self, group, *, tokens: int, hidden: int, experts: int, inter: int, top_k: int,
-                 quant_group: int, device):
+                 quant_group: int, device, overlap_shared: bool = False):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -67,39 +72,56 @@ class ExpertParallelMoE:
         self.cap = tokens * top_k
         self.so = lib.load()
         G, cap, H = self.G, self.cap, hidden
-        self.send_rows = torch.zeros(G, cap, H, dtype=BF16, device=device)
-        self.recv_rows = torch.zeros(G, cap, H, dtype=BF16, device=device)
-        self.send_meta = torch.zeros(G, cap + 1, dtype=torch.int32, device=device)
-        self.recv_meta = torch.zeros(G, cap + 1, dtype=torch.int32, device=device)
-        self.send_back = torch.zeros(G, cap, H, dtype=BF16, device=device)
-        self.recv_back = torch.zeros(G, cap, H, dtype=BF16, device=device)
+        if (cap + 1) * 4 > H * 2:
+            raise ValueError("the segment header (cap + 1 int32 words) must fit in one row")
+        # segments [G][cap + 1][H]: row 0 the header, rows 1.. the pairs (qw_moe_ep_pack)
+        self.send_seg = torch.zeros(G, cap + 1, H, dtype=BF16, device=device)
+        self.recv_seg = torch.zeros(G, cap + 1, H, dtype=BF16, device=device)
+        self.send_back = torch.zeros(G, cap + 1, H, dtype=BF16, device=device)
+        self.recv_back = torch.zeros(G, cap + 1, H, dtype=BF16, device=device)
         nbytes = self.so.qw_moe_ep_recv_workspace_bytes(G, cap, H, experts, inter)
         self.ws_r = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.side = torch.cuda.Stream(device) if overlap_shared else None
+
+    def header(self, seg: torch.Tensor) -> torch.Tensor:
+        """int32 header words [G, cap + 1] of a segment buffer."""
+        return seg[:, 0].contiguous().view(torch.int32)[:, : self.cap + 1]
 
     def experts(self, x: torch.Tensor, ws: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor,
                 shared_gate_up: torch.Tensor | None, shared_down: torch.Tensor | None, stream=None):
         """Routed + shared expert outputs of this rank's tokens ``x`` [tokens, hidden] (bf16)
-        into ``ws`` (a MoE workspace already routed by qw_moe_route / qw_moe_route_x).
-        Every rank of the group calls it, with the same shapes, in the same order."""
-        so, st = self.so, stream if stream is not None else lib.stream_ptr()
+        into ``ws`` (a MoE workspace already routed by qw_moe_route / qw_moe_route_x) on the
+        current stream.  Every rank of the group calls it, with the same shapes, in the same
+        order."""
+        so = self.so
+        cur = torch.cuda.current_stream(x.device)
+        st = stream if stream is not None else cur.cuda_stream
         T, H, E, I, k, g, G, cap = self.T, self.H, self.E, self.I, self.k, self.qg, self.G, self.cap
         if tuple(x.shape) != (T, H) or x.dtype != BF16:
             raise ValueError(f"x must be bf16 [{T}, {H}]")
+        # the shared expert (no routed pairs)
+        if self.side is not None:
+            self.side.wait_stream(cur)
         sgu = shared_gate_up.data_ptr() if shared_gate_up is not None else None
         sdn = shared_down.data_ptr() if shared_down is not None else None
         lib.check(so.qw_moe_experts_w4_range(x.data_ptr(), gate_up_local.data_ptr(), down_local.data_ptr(), sgu, sdn,
-                                             T, H, E, I, k, g, 0, 0, ws.data_ptr(), st), "ep shared expert")
-        lib.check(so.qw_moe_ep_pack(ws.data_ptr(), x.data_ptr(), T, H, E, k, G, cap, self.send_rows.data_ptr(),
-                                    self.send_meta.data_ptr(), st), "ep pack")
-        dist.all_to_all_single(self.recv_meta, self.send_meta, group=self.group)
-        dist.all_to_all_single(self.recv_rows, self.send_rows, group=self.group)
-        lib.check(so.qw_moe_ep_recv_route(self.recv_meta.data_ptr(), G, cap, E, self.ws_r.data_ptr(), st),
+                                             T, H, E, I, k, g, 0, 0, ws.data_ptr(),
+                                             self.side.cuda_stream if self.side is not None else st),
+                  "ep shared expert")
+        # dispatch
+        lib.check(so.qw_moe_ep_pack(ws.data_ptr(), x.data_ptr(), T, H, E, k, G, cap, self.send_seg.data_ptr(), st),
+                  "ep pack")
+        dist.all_to_all_single(self.recv_seg, self.send_seg, group=self.group)
+        # this rank's experts on the rows it received
+        lib.check(so.qw_moe_ep_recv_route(self.recv_seg.data_ptr(), G, cap, H, E, self.ws_r.data_ptr(), st),
                   "ep receive routing")
-        lib.check(so.qw_moe_experts_w4_range(self.recv_rows.data_ptr(), gate_up_local.data_ptr(),
-                                             down_local.data_ptr(), None, None, G * cap, H, self.el, I, 1, g, 0,
-                                             self.el, self.ws_r.data_ptr(), st), "ep local experts")
-        lib.check(so.qw_moe_ep_pack_out(self.ws_r.data_ptr(), self.recv_meta.data_ptr(), G, cap, H, E, I,
+        lib.check(so.qw_moe_ep_experts(self.recv_seg.data_ptr(), gate_up_local.data_ptr(), down_local.data_ptr(),
+                                       G, cap, H, E, I, g, self.ws_r.data_ptr(), st), "ep local experts")
+        # combine
+        lib.check(so.qw_moe_ep_pack_out(self.ws_r.data_ptr(), self.recv_seg.data_ptr(), G, cap, H, E, I,
                                         self.send_back.data_ptr(), st), "ep pack outputs")
         dist.all_to_all_single(self.recv_back, self.send_back, group=self.group)
         lib.check(so.qw_moe_ep_scatter(ws.data_ptr(), self.recv_back.data_ptr(), T, H, E, I, k, G, cap, st),
                   "ep scatter")
+        if self.side is not None:
+            cur.wait_stream(self.side)

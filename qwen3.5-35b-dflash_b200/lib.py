@@ -58,8 +58,9 @@ SIGNATURES = {
     "qw_moe_route": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, P]),
     "qw_moe_experts_w4_range": (_c.c_int, [P, P, P, P, P, I64, I64, I64, I64, I64, I32, I64, I64, P, P]),
     "qw_moe_ep_recv_workspace_bytes": (I64, [I64, I64, I64, I64, I64]),
-    "qw_moe_ep_pack": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, P, P, P]),
-    "qw_moe_ep_recv_route": (_c.c_int, [P, I64, I64, I64, P, P]),
+    "qw_moe_ep_pack": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, P, P]),
+    "qw_moe_ep_recv_route": (_c.c_int, [P, I64, I64, I64, I64, P, P]),
+    "qw_moe_ep_experts": (_c.c_int, [P, P, P, I64, I64, I64, I64, I64, _c.c_int32, P, P]),
     "qw_moe_ep_pack_out": (_c.c_int, [P, P, I64, I64, I64, I64, I64, P, P]),
     "qw_moe_ep_scatter": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, I64, P]),
     "qw_moe_route_x": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, I64, I32, P, P]),

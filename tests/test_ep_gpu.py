@@ -55,28 +55,33 @@ def _worker(rank, world, port, cases):
             lib.check(so.qw_moe_combine(ws1.data_ptr(), out1.data_ptr(), 0, t, h, e, inter, k, 1, st))
 
             # experts sharded over the group
-            moe = ep.ExpertParallelMoE(dist.group.WORLD, tokens=t, hidden=h, experts=e, inter=inter, top_k=k,
-                                       quant_group=g, device="cuda")
             gu_l = ep.local_expert_streams(gu, e, world, rank)
             dn_l = ep.local_expert_streams(dn, e, world, rank)
-            ws2 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
-            out2 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
-            for _ in range(2):   # twice: the exchange buffers are reused
-                lib.check(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16,
-                                          ws2.data_ptr(), st))
-                moe.experts(x, ws2, gu_l, dn_l, shgu, shdn)
-                lib.check(so.qw_moe_combine(ws2.data_ptr(), out2.data_ptr(), 0, t, h, e, inter, k, 1, st))
-                torch.cuda.synchronize()
-                if not torch.equal(out1, out2):
-                    bad = (out1 != out2).sum().item()
-                    raise AssertionError(f"rank {rank} case {(t, h, e, k, inter, g)}: {bad} elements differ")
+            for overlap in (False, True):   # the shared expert in line, or on a side stream
+                moe = ep.ExpertParallelMoE(dist.group.WORLD, tokens=t, hidden=h, experts=e, inter=inter, top_k=k,
+                                           quant_group=g, device="cuda", overlap_shared=overlap)
+                ws2 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+                out2 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+                for _ in range(2):   # twice: the exchange buffers are reused
+                    lib.check(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16,
+                                              ws2.data_ptr(), st))
+                    moe.experts(x, ws2, gu_l, dn_l, shgu, shdn)
+                    lib.check(so.qw_moe_combine(ws2.data_ptr(), out2.data_ptr(), 0, t, h, e, inter, k, 1, st))
+                    torch.cuda.synchronize()
+                    if not torch.equal(out1, out2):
+                        bad = (out1 != out2).sum().item()
+                        raise AssertionError(f"rank {rank} case {(t, h, e, k, inter, g)} overlap {overlap}: "
+                                             f"{bad} elements differ")
             # the packed segments are the protocol's (oracle/ep_np.py)
             topk = ws2[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
-            rows, meta = ep_np.pack(topk, x.float().cpu().numpy(), e, world, t * k)
-            assert (moe.send_meta.cpu().numpy() == meta).all()
+            x16 = x.cpu().view(torch.int16).numpy().view("uint16")
+            want = ep_np.pack(topk, x16, e, world, t * k)
+            got = moe.send_seg.cpu().view(torch.int16).numpy().view("uint16")
+            ww, gw = ep_np.header_words(want, t * k), ep_np.header_words(got, t * k)
             for d in range(world):
-                n = int(meta[d, 0])
-                assert torch.equal(moe.send_rows[d, :n].float().cpu(), torch.from_numpy(rows[d, :n]))
+                n = int(ww[d, 0])
+                assert (gw[d, : 1 + n] == ww[d, : 1 + n]).all()
+                assert (got[d, 1:1 + n] == want[d, 1:1 + n]).all()
         dist.barrier()
     finally:
         dist.destroy_process_group()
