@@ -279,3 +279,60 @@ def test_paged_attention_layer_matches_oracle(cuda_lib, b, ctx):
         assert_close(got_k, new_k[i], what="k append")
         np.testing.assert_array_equal(to_np(vc)[perm[i][pos // page], :, pos % page].transpose(1, 0, 2), new_v[i])
     assert_close(to_np(out).reshape(b, s, h * dim), want, what="paged attention")
+
+
+@pytest.mark.parametrize("t,g,e,inter", [(16, 128, 256, 512), (16, 32, 64, 256), (7, 64, 32, 256)])
+def test_moe_ep_kernels_one_rank_bit_identical(cuda_lib, t, g, e, inter):
+    """The expert-parallel kernels with one rank (the all-to-all is then the identity:
+    the send segments are the receive segments): pack, receive routing, the receiving
+    experts (the streaming kernels, over the cap + 1 rows of the segment), pack-out and
+    scatter must give the one-GPU MoE (the bulk kernels at 16 tokens) bit for bit."""
+    from qwen35_dflash_b200 import lib, w4
+    from oracle import ep_np
+    torch.manual_seed(t + g + e)
+    h, k = 2048, 8
+    x = torch.randn(t, h, device="cuda").to(torch.bfloat16)
+    logits = torch.cat([_tie_heavy_logits(t, e, seed=t + e).cuda(),
+                        torch.randn(t, 1, device="cuda").to(torch.bfloat16)], 1).contiguous()
+
+    def bank(n, kk, *lead):
+        return w4.pack_w4(torch.randint(-8, 8, (*lead, n, kk), dtype=torch.int8, device="cuda"),
+                          (torch.rand(*lead, n, kk // g, device="cuda") * 0.015 + 0.005).to(torch.bfloat16), g)
+    gu, dn = bank(2 * inter, h, e), bank(h, inter, e)
+    sgu, sdn = bank(2 * inter, h), bank(h, inter)
+    st = lib.stream_ptr()
+    nbytes = cuda_lib.qw_moe_workspace_bytes(t, h, e, inter, k)
+
+    ws1 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    out1 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+    lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws1.data_ptr(), st)
+    lib.call("qw_moe_experts_w4", x.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(), sdn.data_ptr(),
+             t, h, e, inter, k, g, ws1.data_ptr(), st)
+    lib.call("qw_moe_combine", ws1.data_ptr(), out1.data_ptr(), 0, t, h, e, inter, k, 1, st)
+
+    cap = t * k
+    seg = torch.zeros(1, cap + 1, h, dtype=torch.bfloat16, device="cuda")
+    back = torch.zeros_like(seg)
+    ws_r = torch.zeros(cuda_lib.qw_moe_ep_recv_workspace_bytes(1, cap, h, e, inter), dtype=torch.uint8,
+                       device="cuda")
+    ws2 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    out2 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+    lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws2.data_ptr(), st)
+    lib.call("qw_moe_experts_w4_range", x.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(),
+             sdn.data_ptr(), t, h, e, inter, k, g, 0, 0, ws2.data_ptr(), st)
+    lib.call("qw_moe_ep_pack", ws2.data_ptr(), x.data_ptr(), t, h, e, k, 1, cap, seg.data_ptr(), st)
+    lib.call("qw_moe_ep_recv_route", seg.data_ptr(), 1, cap, h, e, ws_r.data_ptr(), st)
+    lib.call("qw_moe_ep_experts", seg.data_ptr(), gu.data_ptr(), dn.data_ptr(), 1, cap, h, e, inter, g,
+             ws_r.data_ptr(), st)
+    lib.call("qw_moe_ep_pack_out", ws_r.data_ptr(), seg.data_ptr(), 1, cap, h, e, inter, back.data_ptr(), st)
+    lib.call("qw_moe_ep_scatter", ws2.data_ptr(), back.data_ptr(), t, h, e, inter, k, 1, cap, st)
+    lib.call("qw_moe_combine", ws2.data_ptr(), out2.data_ptr(), 0, t, h, e, inter, k, 1, st)
+    torch.cuda.synchronize()
+    # the segment is the protocol's
+    topk = ws2[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
+    want = ep_np.pack(topk, x.cpu().view(torch.int16).numpy().view("uint16"), e, 1, cap)
+    got = seg.cpu().view(torch.int16).numpy().view("uint16")
+    assert (ep_np.header_words(got, cap) == ep_np.header_words(want, cap)).all()
+    assert (got[0, 1:] == want[0, 1:]).all()
+    if not torch.equal(out1, out2):
+        raise AssertionError(f"{(out1 != out2).sum().item()} elements differ")
