@@ -639,6 +639,7 @@ struct MoeArgs {
   float* part;              // [T, k+1, H] raw expert outputs
   int T, H, I, E, k, has_shared;
   int e_lo, e_cnt;          // routed experts computed: [e_lo, e_lo + e_cnt) of the E, banks indexed e - e_lo
+  int pairs_hint;           // expected routed pairs (0: T * k); picks the activation tile width
 };
 
 // Decode CTA slot -> (weights, number of pairs, pair list base); false if idle.
@@ -1310,7 +1311,8 @@ static int launch_experts_nt(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s,
 // block-verify case: 16 tokens x top-8 over 256 experts), else 16.
 template <class Fmt, int PF, class FmtUp = Fmt>
 static int launch_experts(const MoeArgs<typename Fmt::ET>& a, cudaStream_t s, bool up, bool down) {
-  if (static_cast<int64_t>(a.T) * a.k <= 2LL * a.E) return launch_experts_nt<Fmt, 1, PF, FmtUp>(a, s, up, down);
+  const int64_t pairs = a.pairs_hint > 0 ? a.pairs_hint : static_cast<int64_t>(a.T) * a.k;
+  if (pairs <= 2LL * a.E) return launch_experts_nt<Fmt, 1, PF, FmtUp>(a, s, up, down);
   return launch_experts_nt<Fmt, 2, PF, FmtUp>(a, s, up, down);
 }
 
@@ -1499,7 +1501,8 @@ extern "C" int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t exper
 static int experts_w4(const void* x, const void* gate_up, const void* down, const void* shared_gate_up,
                       const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
                       int64_t top_k, int32_t group, void* workspace, void* stream, bool up, bool dn,
-                      int64_t expert_lo = 0, int64_t expert_count = -1, bool lists_ready = false) {
+                      int64_t expert_lo = 0, int64_t expert_count = -1, bool lists_ready = false,
+                      int64_t pairs_hint = 0) {
   if (expert_count < 0) expert_count = experts;
   QW_CHECK_ARG(x && workspace && (expert_count == 0 || (gate_up && down)), "moe_experts: null pointer");
   QW_CHECK_ARG(expert_lo >= 0 && expert_lo + expert_count <= experts, "moe_experts: expert range outside [0, experts)");
@@ -1526,6 +1529,7 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   a.has_shared = shared_gate_up != nullptr;
   a.e_lo = static_cast<int>(expert_lo);
   a.e_cnt = static_cast<int>(expert_count);
+  a.pairs_hint = static_cast<int>(pairs_hint);
   cudaStream_t s = as_stream(stream);
   switch (group) {
     case 128: return launch_experts_w4<128>(a, s, up, dn, lists_ready);
@@ -1860,10 +1864,11 @@ extern "C" int qw_moe_ep_experts(const void* recv_seg, const void* gate_up_local
                                  int64_t ranks, int64_t cap, int64_t hidden, int64_t experts, int64_t inter,
                                  int32_t group, void* recv_workspace, void* stream) {
   QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0, "moe_ep_experts: shape");
-  // the received segments as G (cap + 1) rows, routed (lists included) by qw_moe_ep_recv_route
+  // the received segments as G (cap + 1) rows, routed (lists included) by qw_moe_ep_recv_route;
+  // a rank receives cap pairs on average (every rank sends cap), which sets the tile width
   return experts_w4(recv_seg, gate_up_local, down_local, nullptr, nullptr, ranks * (cap + 1), hidden,
                     experts / ranks, inter, 1, group, recv_workspace, stream, true, true, 0, experts / ranks,
-                    true);
+                    true, cap);
 }
 
 extern "C" int qw_moe_ep_pack_out(const void* recv_workspace, const void* recv_seg, int64_t ranks, int64_t cap,
