@@ -191,6 +191,37 @@ def cpu_reference_estimate(threads: int | None = None):
 
 
 # ---------------------------------------------------------------------------- GPU side
+def print_timeline(prof):
+    """Per kernel of one graph replay: launches, summed duration and the time it adds to
+    the step's critical path (its end minus the latest end before it, in start order)."""
+    import collections
+    evs = sorted(((e.name, e.time_range.start, e.time_range.end) for e in prof.events()
+                  if e.device_type.name == "CUDA"), key=lambda x: x[1])
+    steps, cur = [], []
+    for name, s, e in evs:   # replays are separated by the host-side token copies
+        if "qw::" not in name and "nccl" not in name:
+            if cur:
+                steps.append(cur)
+            cur = []
+            continue
+        cur.append((name, s, e))
+    if cur:
+        steps.append(cur)
+    st = steps[-1]
+    cnt, dur, marg = collections.Counter(), collections.Counter(), collections.Counter()
+    prev = st[0][1]
+    for name, s, e in st:
+        n = name.split("<")[0].split("(")[0].replace("void ", "")
+        cnt[n] += 1
+        dur[n] += e - s
+        marg[n] += max(e, prev) - prev
+        prev = max(prev, e)
+    print(f"timeline: {len(st)} launches, {st[-1][2] - st[0][1]:.1f} us from first start to last end")
+    print(f"{'kernel':40s} {'launches':>8s} {'dur us':>9s} {'added us':>9s} {'per launch':>10s}")
+    for n, m in marg.most_common():
+        print(f"{n:40s} {cnt[n]:8d} {dur[n]:9.1f} {m:9.1f} {m / cnt[n]:10.2f}")
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -237,6 +268,20 @@ def run_ours(args, rank, world, local_rank):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    if args.timeline:
+        # in-graph kernel timeline of the last of two steps (CUPTI through torch.profiler)
+        from torch.profiler import profile, ProfilerActivity
+        if world > 1:
+            dist.barrier()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(2):
+                step(args.warmup + i)
+            torch.cuda.synchronize(dev)
+        if rank == 0:
+            print_timeline(prof)
+        if world > 1:
+            dist.barrier()
+        return None
     if args.profile_step:
         # one step between cudaProfilerStart/Stop (ncu --profile-from-start off)
         torch.cuda.profiler.start()
@@ -484,6 +529,8 @@ def main():
                          "instead of running independent replicas")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="after warm-up, print the in-graph kernel timeline of one step (rank 0) and exit")
     ap.add_argument("--profile-step", action="store_true",
                     help="run warm-up then one step inside cudaProfilerStart/Stop and exit (for ncu)")
     ap.add_argument("--kernels", action="store_true",
