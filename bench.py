@@ -241,7 +241,7 @@ def run_ours(args, rank, world, local_rank):
     weights = E.weights_random(cfg, seed=2, device=dev)
     ep = args.ep and world > 1
     eng = E.TargetEngine(cfg, weights, batch=B, block=S, capacity=capacity, device=dev,
-                         ep_group=dist.group.WORLD if ep else None)
+                         ep_group=dist.group.WORLD if ep else None, ep_overlap_shared=not args.ep_serial)
     eng.set_random_context(args.ctx, seed=3 + rank)
     torch.cuda.synchronize(dev)
     init_s = time.perf_counter() - t_init
@@ -527,6 +527,8 @@ def main():
     ap.add_argument("--ep", action="store_true",
                     help="with --gpus > 1: shard the routed experts over the GPUs (all-to-all dispatch/combine) "
                          "instead of running independent replicas")
+    ap.add_argument("--ep-serial", action="store_true",
+                    help="with --ep: run the shared expert before the dispatch all-to-all instead of beside it")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--timeline", action="store_true",

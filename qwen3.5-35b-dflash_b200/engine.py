@@ -150,7 +150,8 @@ def weights_random(cfg: TargetConfig, seed: int = 2, std: float = 0.02, device="
 
 class TargetEngine:
     def __init__(self, cfg: TargetConfig, weights, *, batch: int, block: int = 16, capacity: int = 4096,
-                 page_size: int = 16, device="cuda", ep_group=None):
+                 page_size: int = 16, device="cuda", ep_group=None,
+                 ep_overlap_shared: bool = True):
         if not 1 <= block <= lib.QW_MAX_BLOCK:
             raise ValueError(f"block must be in [1, {lib.QW_MAX_BLOCK}]")
         self.cfg, self.B, self.S, self.device = cfg, batch, block, torch.device(device)
@@ -203,7 +204,8 @@ class TargetEngine:
                           for lw in self.layers]
             self.ep_moe = _ep.ExpertParallelMoE(ep_group, tokens=T, hidden=H, experts=E,
                                                 inter=c.moe_intermediate_size, top_k=c.num_experts_per_tok,
-                                                quant_group=c.quant_group, device=dev)
+                                                quant_group=c.quant_group, device=dev,
+                                                overlap_shared=ep_overlap_shared)
         self.nblk = self.lib.qw_lmhead_blocks(self.vocab_pad)
         self.keys = torch.zeros(self.nblk, T, dtype=torch.int64, device=dev)
         self.top1 = torch.zeros(T, dtype=torch.int32, device=dev)
