@@ -57,7 +57,7 @@ def _worker(rank, world, port, cases):
             # experts sharded over the group
             gu_l = ep.local_expert_streams(gu, e, world, rank)
             dn_l = ep.local_expert_streams(dn, e, world, rank)
-            for overlap in (False, True):   # the shared expert in line, or on a side stream
+            for overlap in (False, True):   # the shared expert first, or launched behind the dispatch
                 moe = ep.ExpertParallelMoE(dist.group.WORLD, tokens=t, hidden=h, experts=e, inter=inter, top_k=k,
                                            quant_group=g, device="cuda", overlap_shared=overlap)
                 ws2 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
