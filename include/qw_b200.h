@@ -350,7 +350,10 @@ typedef struct {
 
 /* Block verify of one layer (`layers_dev[layer]`, a device array): writes out[],
  * reads the banks, never writes them.  (dk,dv) in {(128,128),(64,64),(128,64)},
- * 1 <= seq <= QW_MAX_BLOCK; proj 16-byte aligned with ldp a multiple of 8. */
+ * 1 <= seq <= QW_MAX_BLOCK; proj 16-byte aligned with ldp a multiple of 8.  The kernel
+ * reads proj, the banks and the conv weights, and runs the conv and the q/k norms,
+ * before it waits for the launch ahead of it (the a/b projection, whose output `ab` it
+ * reads after the wait), so that launch must not be the one that wrote proj. */
 int qw_gdn_verify(const qw_gdn_dims* dims, const qw_gdn_layer* layers_dev, int layer,
                   void* stream);
 

@@ -230,69 +230,90 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   // per-thread constants of the gates and of the gated norm
   const float neg_a = -__expf(L.A_log[h]), dtb = L.dt_bias[h];
   const float norm_w = COMMIT ? 0.f : __bfloat162float(L.norm_w[vcol0 + tid % COLS]);
+  // the phases before the recurrence; verify runs conv and the q/k norms, which need
+  // only the projections (written before the launch ahead of this one), before its
+  // wait, and the gates, which read that launch's output, after it
+  auto conv_phase = [&]() {
+    // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns (taps and tails
+    // loaded above)
+    {
+#pragma unroll
+      for (int r = 0; r < CPT; ++r) {
+        const int i = tid + r * THREADS;
+        if (i >= nch) continue;
+        // q and k are stored with row j at kperm(j) (see the recurrence)
+        if (i < nq) {
+          conv_channel(hreg[r], wreg[r], &sm.xin[0][i], XS, ntok, &sm.q[0][kperm<DK>(i)], DK);
+        } else if (i < nq + DK) {
+          const int j = i - nq;
+          conv_channel(hreg[r], wreg[r], &sm.xin[0][DK + j], XS, ntok, &sm.k[0][kperm<DK>(j)], DK);
+        } else {
+          const int j = i - nq - DK;
+          conv_channel(hreg[r], wreg[r], &sm.xin[0][2 * DK + j], XS, ntok, &sm.v[0][j], COLS);
+        }
+      }
+    }
+  };
+  auto l2_phase = [&]() {
+    // ---- L2 norm of q and k per token (fused_ops.py:92-95); q also scaled by Dk^-1/2:
+    // 8 threads per token, all tokens at once
+    {
+      static_assert(THREADS >= 8 * QW_MAX_BLOCK, "the l2 norm needs 8 threads per token");
+      const int t = tid / 8, part = tid % 8;
+      float sk = 0.f, sq = 0.f;
+      if (t < ntok) {
+#pragma unroll
+        for (int i = part; i < DK; i += 8) {
+          sk += sm.k[t][i] * sm.k[t][i];
+          if (!COMMIT) sq += sm.q[t][i] * sm.q[t][i];
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        if (!COMMIT) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      }
+      if (t < ntok) {
+        const float ik = rsqrtf(sk + 1e-6f);
+        const float iq = COMMIT ? 0.f : rsqrtf(sq + 1e-6f) * rsqrtf(static_cast<float>(DK));
+#pragma unroll
+        for (int i = part; i < DK; i += 8) {
+          sm.k[t][i] *= ik;
+          if (!COMMIT) sm.q[t][i] *= iq;
+        }
+      }
+    }
+  };
+  auto gates_phase = [&]() {
+    // ---- gates (fused/model.py:243-253, fp32)
+    for (int t = tid; t < ntok; t += THREADS) {
+      const int64_t row = static_cast<int64_t>(b) * d.seq + t;
+      const float bl = L.ab[row * 2 * d.v_heads + h];
+      const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
+      sm.beta[t] = sigmoid_f(bl);
+      sm.g[t] = __expf(neg_a * softplus_f(al + dtb));   // the decay exp(g) of the recurrence
+    }
+  };
   if constexpr (!COMMIT) {
+    cp_async_wait<0>();
+    __syncthreads();
+    conv_phase();
+    __syncthreads();
+    l2_phase();
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
+    gates_phase();
+    __syncthreads();
+  } else {
+    gates_phase();
+    cp_async_wait<0>();
+    __syncthreads();
+    conv_phase();
+    __syncthreads();
+    l2_phase();
+    __syncthreads();
   }
-  // ---- gates (fused/model.py:243-253, fp32)
-  for (int t = tid; t < ntok; t += THREADS) {
-    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
-    const float bl = L.ab[row * 2 * d.v_heads + h];
-    const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
-    sm.beta[t] = sigmoid_f(bl);
-    sm.g[t] = __expf(neg_a * softplus_f(al + dtb));   // the decay exp(g) of the recurrence
-  }
-  cp_async_wait<0>();
-  __syncthreads();
-  // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns (taps and tails
-  // loaded above, before the wait)
-  {
-#pragma unroll
-    for (int r = 0; r < CPT; ++r) {
-      const int i = tid + r * THREADS;
-      if (i >= nch) continue;
-      // q and k are stored with row j at kperm(j) (see the recurrence)
-      if (i < nq) {
-        conv_channel(hreg[r], wreg[r], &sm.xin[0][i], XS, ntok, &sm.q[0][kperm<DK>(i)], DK);
-      } else if (i < nq + DK) {
-        const int j = i - nq;
-        conv_channel(hreg[r], wreg[r], &sm.xin[0][DK + j], XS, ntok, &sm.k[0][kperm<DK>(j)], DK);
-      } else {
-        const int j = i - nq - DK;
-        conv_channel(hreg[r], wreg[r], &sm.xin[0][2 * DK + j], XS, ntok, &sm.v[0][j], COLS);
-      }
-    }
-  }
-  __syncthreads();
-  // ---- L2 norm of q and k per token (fused_ops.py:92-95); q also scaled by Dk^-1/2:
-  // 8 threads per token, all tokens at once
-  {
-    static_assert(THREADS >= 8 * QW_MAX_BLOCK, "the l2 norm needs 8 threads per token");
-    const int t = tid / 8, part = tid % 8;
-    float sk = 0.f, sq = 0.f;
-    if (t < ntok) {
-#pragma unroll
-      for (int i = part; i < DK; i += 8) {
-        sk += sm.k[t][i] * sm.k[t][i];
-        if (!COMMIT) sq += sm.q[t][i] * sm.q[t][i];
-      }
-    }
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      sk += __shfl_xor_sync(0xffffffffu, sk, o);
-      if (!COMMIT) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    }
-    if (t < ntok) {
-      const float ik = rsqrtf(sk + 1e-6f);
-      const float iq = COMMIT ? 0.f : rsqrtf(sq + 1e-6f) * rsqrtf(static_cast<float>(DK));
-#pragma unroll
-      for (int i = part; i < DK; i += 8) {
-        sm.k[t][i] *= ik;
-        if (!COMMIT) sm.q[t][i] *= iq;
-      }
-    }
-  }
-  __syncthreads();
   // ---- the recurrence (fused_ops.py:98-106)
   for (int t = 0; t < ntok; ++t) {
     const float decay = sm.g[t];
