@@ -278,6 +278,72 @@ __device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, in
   return lm < rm ? lm : rm;
 }
 
+// The introselect loop below once [first, last) fits one warp (last - first <= 32): the
+// range is held one element per lane (lane j = position first + j at entry) and each
+// step runs in registers.  The median of three is chosen from shuffled values; the
+// partition's left stops (ascending) and right stops (descending) come from two ballots,
+// the m-th left stop is paired with the m-th right stop through two 32-entry rank
+// tables, the pairs with L[m] < R[m] (a prefix) swap by shuffles, and the cut is the
+// sequential algorithm's.  Every step makes the same exchanges as the shared-memory
+// code, so the arrangement is the same; the range goes back to q at exit, with first /
+// last / depth advanced.  Stops when the range is <= 3 or depth reaches 0.
+__device__ void warp_introselect_regs(const Q& q, int& first, int& last, int nth, int& depth, int16_t* slot_l,
+                                      int16_t* slot_r, int lane) {
+  const int base = first, wlen = last - first;
+  const unsigned lt = (1u << lane) - 1u, gt = ~((2u << lane) - 1u);
+  float rv = 0.f;
+  int32_t ri = 0;
+  if (lane < wlen) { rv = q.v[base + lane]; ri = q.i[base + lane]; }
+  while (last - first > 3 && depth > 0) {
+    --depth;
+    // __move_median_to_first(first, first + 1, mid, last - 1)
+    const int mid = first + (last - first) / 2;
+    const float va = __shfl_sync(0xffffffffu, rv, first + 1 - base);
+    const float vb = __shfl_sync(0xffffffffu, rv, mid - base);
+    const float vc = __shfl_sync(0xffffffffu, rv, last - 1 - base);
+    int m;
+    if (va > vb) m = vb > vc ? mid : (va > vc ? last - 1 : first + 1);
+    else m = va > vc ? first + 1 : (vb > vc ? last - 1 : mid);
+    {
+      const int rf = first - base, rm = m - base;
+      const int src = lane == rf ? rm : (lane == rm ? rf : lane);
+      rv = __shfl_sync(0xffffffffu, rv, src);
+      ri = __shfl_sync(0xffffffffu, ri, src);
+    }
+    // unguarded partition of [a, b) = [first + 1, last) around the pivot at first
+    const int a = first + 1, b = last, pos = base + lane;
+    const float p = __shfl_sync(0xffffffffu, rv, first - base);
+    const bool is_l = pos >= a && pos < b && !(rv > p);
+    const bool is_r = pos >= a - 1 && pos < b && !(p > rv);
+    const unsigned ml = __ballot_sync(0xffffffffu, is_l), mr = __ballot_sync(0xffffffffu, is_r);
+    const int nl = __popc(ml), nr = __popc(mr);
+    const int rl = __popc(ml & lt), rr = __popc(mr & gt);   // rank among left / right stops
+    if (is_l) slot_l[rl] = static_cast<int16_t>(lane);
+    if (is_r) slot_r[rr] = static_cast<int16_t>(lane);
+    __syncwarp();
+    const bool pair_l = is_l && rl < nr && lane < slot_r[rl];
+    const int mstar = __popc(__ballot_sync(0xffffffffu, pair_l));
+    int src = lane;
+    if (is_l && rl < mstar) src = slot_r[rl];
+    if (is_r && rr < mstar) src = slot_l[rr];
+    int cut;
+    if (mstar == 0) {
+      cut = base + slot_l[0];
+    } else {
+      const int lm = mstar < nl ? base + slot_l[mstar] : 1 << 30;
+      const int rm2 = base + slot_r[mstar - 1];
+      cut = lm < rm2 ? lm : rm2;
+    }
+    __syncwarp();   // the tables are rewritten by the next step
+    rv = __shfl_sync(0xffffffffu, rv, src);
+    ri = __shfl_sync(0xffffffffu, ri, src);
+    if (cut <= nth) first = cut;
+    else last = cut;
+  }
+  if (lane < wlen) { q.v[base + lane] = rv; q.i[base + lane] = ri; }
+  __syncwarp();
+}
+
 // libstdc++ __insertion_sort of [first, first + n) under a > b, n <= 32, in parallel: it
 // is a stable descending sort, so element i goes to the number of elements greater than
 // it plus the number of equal ones before it.
@@ -327,6 +393,10 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
       }
       heap_done = true;
       break;
+    }
+    if (last - first <= 32) {   // the rest of the loop in registers (same steps)
+      warp_introselect_regs(q, first, last, nth, depth, pos_l, pos_r, lane);
+      continue;
     }
     --depth;
     const int mid = first + (last - first) / 2;
