@@ -278,54 +278,102 @@ __device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, in
   return lm < rm ? lm : rm;
 }
 
-// The introselect loop below once [first, last) fits one warp (last - first <= 32): the
-// range is held one element per lane (lane j = position first + j at entry) and each
-// step runs in registers.  The median of three is chosen from shuffled values; the
-// partition's left stops (ascending) and right stops (descending) come from two ballots,
-// the m-th left stop is paired with the m-th right stop through two 32-entry rank
-// tables, the pairs with L[m] < R[m] (a prefix) swap by shuffles, and the cut is the
-// sequential algorithm's.  Every step makes the same exchanges as the shared-memory
-// code, so the arrangement is the same; the range goes back to q at exit, with first /
-// last / depth advanced.  Stops when the range is <= 3 or depth reaches 0.
+// The introselect loop below once [first, last) has at most 32 NR elements: the range is
+// held NR elements per lane (register j of lane l = position first + 32 j + l at entry)
+// and each step runs in registers.  The median of three comes from shuffled values; the
+// partition's left stops (ascending) and right stops (descending) come from ballots, the
+// m-th left stop is paired with the m-th right stop through two rank tables, the pairs
+// with L[m] < R[m] (a prefix) swap by shuffles, and the cut is the sequential
+// algorithm's.  Every step makes the same exchanges as the shared-memory code, so the
+// arrangement is the same; the range goes back to q at exit, with first / last / depth
+// advanced.  Stops when the range is <= 3 or depth reaches 0.  Registers are only ever
+// selected by warp-uniform or unrolled indices.
+template <int NR>
 __device__ void warp_introselect_regs(const Q& q, int& first, int& last, int nth, int& depth, int16_t* slot_l,
                                       int16_t* slot_r, int lane) {
   const int base = first, wlen = last - first;
   const unsigned lt = (1u << lane) - 1u, gt = ~((2u << lane) - 1u);
-  float rv = 0.f;
-  int32_t ri = 0;
-  if (lane < wlen) { rv = q.v[base + lane]; ri = q.i[base + lane]; }
+  float rv[NR];
+  int32_t ri[NR];
+#pragma unroll
+  for (int j = 0; j < NR; ++j) {
+    const int o = 32 * j + lane;
+    rv[j] = o < wlen ? q.v[base + o] : 0.f;
+    ri[j] = o < wlen ? q.i[base + o] : 0;
+  }
+  // value / index at the warp-uniform offset o of the range
+  auto v_at = [&](int o) {
+    float x = rv[0];
+#pragma unroll
+    for (int j = 1; j < NR; ++j) x = (o >> 5) == j ? rv[j] : x;
+    return __shfl_sync(0xffffffffu, x, o & 31);
+  };
+  auto i_at = [&](int o) {
+    int32_t x = ri[0];
+#pragma unroll
+    for (int j = 1; j < NR; ++j) x = (o >> 5) == j ? ri[j] : x;
+    return __shfl_sync(0xffffffffu, x, o & 31);
+  };
   while (last - first > 3 && depth > 0) {
     --depth;
     // __move_median_to_first(first, first + 1, mid, last - 1)
     const int mid = first + (last - first) / 2;
-    const float va = __shfl_sync(0xffffffffu, rv, first + 1 - base);
-    const float vb = __shfl_sync(0xffffffffu, rv, mid - base);
-    const float vc = __shfl_sync(0xffffffffu, rv, last - 1 - base);
+    const float va = v_at(first + 1 - base), vb = v_at(mid - base), vc = v_at(last - 1 - base);
     int m;
     if (va > vb) m = vb > vc ? mid : (va > vc ? last - 1 : first + 1);
     else m = va > vc ? first + 1 : (vb > vc ? last - 1 : mid);
-    {
+    if (m != first) {
       const int rf = first - base, rm = m - base;
-      const int src = lane == rf ? rm : (lane == rm ? rf : lane);
-      rv = __shfl_sync(0xffffffffu, rv, src);
-      ri = __shfl_sync(0xffffffffu, ri, src);
+      const float vf = v_at(rf), vm = v_at(rm);
+      const int32_t jf = i_at(rf), jm = i_at(rm);
+#pragma unroll
+      for (int j = 0; j < NR; ++j) {
+        const int o = 32 * j + lane;
+        if (o == rf) { rv[j] = vm; ri[j] = jm; }
+        if (o == rm) { rv[j] = vf; ri[j] = jf; }
+      }
     }
     // unguarded partition of [a, b) = [first + 1, last) around the pivot at first
-    const int a = first + 1, b = last, pos = base + lane;
-    const float p = __shfl_sync(0xffffffffu, rv, first - base);
-    const bool is_l = pos >= a && pos < b && !(rv > p);
-    const bool is_r = pos >= a - 1 && pos < b && !(p > rv);
-    const unsigned ml = __ballot_sync(0xffffffffu, is_l), mr = __ballot_sync(0xffffffffu, is_r);
-    const int nl = __popc(ml), nr = __popc(mr);
-    const int rl = __popc(ml & lt), rr = __popc(mr & gt);   // rank among left / right stops
-    if (is_l) slot_l[rl] = static_cast<int16_t>(lane);
-    if (is_r) slot_r[rr] = static_cast<int16_t>(lane);
+    const int a = first + 1, b = last;
+    const float p = v_at(first - base);
+    bool is_l[NR], is_r[NR];
+    int rl[NR], rr[NR];
+    unsigned ml[NR], mr[NR];
+    int nl = 0, nr = 0;
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+      const int pos = base + 32 * j + lane;
+      is_l[j] = pos >= a && pos < b && !(rv[j] > p);
+      is_r[j] = pos >= a - 1 && pos < b && !(p > rv[j]);
+      ml[j] = __ballot_sync(0xffffffffu, is_l[j]);
+      mr[j] = __ballot_sync(0xffffffffu, is_r[j]);
+      rl[j] = nl + __popc(ml[j] & lt);   // rank among the left stops, ascending
+      nl += __popc(ml[j]);
+      nr += __popc(mr[j]);
+    }
+    int above = 0;   // right stops in registers after j
+#pragma unroll
+    for (int j = NR - 1; j >= 0; --j) {
+      rr[j] = above + __popc(mr[j] & gt);   // rank among the right stops, descending
+      above += __popc(mr[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+      if (is_l[j]) slot_l[rl[j]] = static_cast<int16_t>(32 * j + lane);
+      if (is_r[j]) slot_r[rr[j]] = static_cast<int16_t>(32 * j + lane);
+    }
     __syncwarp();
-    const bool pair_l = is_l && rl < nr && lane < slot_r[rl];
-    const int mstar = __popc(__ballot_sync(0xffffffffu, pair_l));
-    int src = lane;
-    if (is_l && rl < mstar) src = slot_r[rl];
-    if (is_r && rr < mstar) src = slot_l[rr];
+    int mstar = 0;
+#pragma unroll
+    for (int j = 0; j < NR; ++j)
+      mstar += __popc(__ballot_sync(0xffffffffu, is_l[j] && rl[j] < nr && 32 * j + lane < slot_r[rl[j]]));
+    int src[NR];
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+      src[j] = 32 * j + lane;
+      if (is_l[j] && rl[j] < mstar) src[j] = slot_r[rl[j]];
+      if (is_r[j] && rr[j] < mstar) src[j] = slot_l[rr[j]];
+    }
     int cut;
     if (mstar == 0) {
       cut = base + slot_l[0];
@@ -335,12 +383,29 @@ __device__ void warp_introselect_regs(const Q& q, int& first, int& last, int nth
       cut = lm < rm2 ? lm : rm2;
     }
     __syncwarp();   // the tables are rewritten by the next step
-    rv = __shfl_sync(0xffffffffu, rv, src);
-    ri = __shfl_sync(0xffffffffu, ri, src);
+    float nv[NR];
+    int32_t ni[NR];
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+      nv[j] = 0.f;
+      ni[j] = 0;
+#pragma unroll
+      for (int jj = 0; jj < NR; ++jj) {
+        const float tv = __shfl_sync(0xffffffffu, rv[jj], src[j] & 31);
+        const int32_t ti = __shfl_sync(0xffffffffu, ri[jj], src[j] & 31);
+        if ((src[j] >> 5) == jj) { nv[j] = tv; ni[j] = ti; }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NR; ++j) { rv[j] = nv[j]; ri[j] = ni[j]; }
     if (cut <= nth) first = cut;
     else last = cut;
   }
-  if (lane < wlen) { q.v[base + lane] = rv; q.i[base + lane] = ri; }
+#pragma unroll
+  for (int j = 0; j < NR; ++j) {
+    const int o = 32 * j + lane;
+    if (o < wlen) { q.v[base + o] = rv[j]; q.i[base + o] = ri[j]; }
+  }
   __syncwarp();
 }
 
@@ -394,8 +459,9 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
       heap_done = true;
       break;
     }
-    if (last - first <= 32) {   // the rest of the loop in registers (same steps)
-      warp_introselect_regs(q, first, last, nth, depth, pos_l, pos_r, lane);
+    if (last - first <= 64) {   // the rest of the loop in registers (same steps)
+      if (last - first <= 32) warp_introselect_regs<1>(q, first, last, nth, depth, pos_l, pos_r, lane);
+      else warp_introselect_regs<2>(q, first, last, nth, depth, pos_l, pos_r, lane);
       continue;
     }
     --depth;
