@@ -479,6 +479,14 @@ def run_kernels(args):
     def gdn(gi):
         return lambda: chk(so.qw_gdn_verify(eng.gdn_dims, eng.gdn_desc.data_ptr(), gi, s))
 
+    def attn(ai):
+        D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        return lambda: chk(so.qw_attn_paged(eng.qout.data_ptr(), eng.k_cache[ai].data_ptr(),
+                                            eng.v_cache[ai].data_ptr(), eng.pages.data_ptr(), eng.max_pages, eng.P,
+                                            eng.qpos.data_ptr(), eng.capacity, eng.qkv.data_ptr() + D * 2, eng.ldq,
+                                            eng.attn_out.data_ptr(), eng.B, eng.S, Hq, Hkv, D, D ** -0.5,
+                                            eng.attn_ws.data_ptr(), s))
+
     with torch.cuda.stream(st):
         route()
         up(L[0])()
@@ -488,7 +496,9 @@ def run_kernels(args):
     cases = [("route", [route], 0), ("moe_up", [up(lw) for lw in L], (active + 1) * w4(2 * I, H)),
              ("moe_down", [down(lw) for lw in L], (active + 1) * w4(H, I)),
              ("w4_qkvz", [qkvz(lw) for lw in gl], w4(eng.ldp, H)),
-             ("gdn_verify", [gdn(i) for i in range(len(gl))], 0)]
+             ("gdn_verify", [gdn(i) for i in range(len(gl))], 0),
+             ("attn_paged", [attn(i) for i in range(len(eng.k_cache))],
+              2 * cfg.num_key_value_heads * (args.ctx + 16) * cfg.head_dim * 2)]
     out = {"kernels": {}, "active_experts": active, "ctx": args.ctx}
     for name, fns, nbytes in cases:
         with torch.cuda.stream(st):
