@@ -219,11 +219,12 @@ __device__ int warp_partition(const Q& q, int a, int b, int16_t* pos_l, int16_t*
   return lm < rm ? lm : rm;
 }
 
-// The same partition for ranges of at most 288 elements (b - (a - 1) <= 288, so every
-// router of <= 256 experts): all ballots first, then the stop positions from prefix
-// counts, then the pair scan unrolled, so no loop carries a memory dependency.
+// The same partition for ranges of at most 32 IT elements (b - (a - 1) <= 32 IT; IT = 9
+// covers every router of <= 256 experts): all ballots first, then the stop positions
+// from prefix counts, then the pair scan unrolled, so no loop carries a memory
+// dependency.
+template <int IT>
 __device__ int warp_partition_small(const Q& q, int a, int b, int16_t* pos_l, int16_t* pos_r, int lane) {
-  constexpr int IT = 9;
   const float p = q.v[a - 1];
   const unsigned lt = (1u << lane) - 1u;
   const int itn = (b - a + 32) / 32;   // 32-wide passes over [a - 1, b)
@@ -468,8 +469,9 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
     const int mid = first + (last - first) / 2;
     warp_move_median_to_first(q, first, first + 1, mid, last - 1, lane);
     __syncwarp();
-    const int cut = last - first <= 288 ? warp_partition_small(q, first + 1, last, pos_l, pos_r, lane)
-                                        : warp_partition(q, first + 1, last, pos_l, pos_r, lane);
+    const int cut = last - first <= 160   ? warp_partition_small<5>(q, first + 1, last, pos_l, pos_r, lane)
+                    : last - first <= 288 ? warp_partition_small<9>(q, first + 1, last, pos_l, pos_r, lane)
+                                          : warp_partition(q, first + 1, last, pos_l, pos_r, lane);
     if (cut <= nth) first = cut;
     else last = cut;
   }
