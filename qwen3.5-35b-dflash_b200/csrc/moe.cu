@@ -1144,7 +1144,7 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
 
 // Down.  Unit = (slot, block of XT_DN_WARPS * spw row tiles); the CTA's warps share the
 // unit, each streaming spw... stages of tiles; the unit's rows of h are staged in shared
-// memory (double-buffered across units).  Units go to CTAs round-robin.
+// memory (three buffers across units).  Units go to CTAs round-robin.
 template <int G>
 __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs args, int tiles_per_stage,
                                                                          int stages_per_warp) {
@@ -1158,7 +1158,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   const int HS = I + XT_PAD;
   __half* hs = reinterpret_cast<__half*>(smem + xt_head_bytes(a.E));
   const size_t hbytes = ((static_cast<size_t>(XT_MAXT) * HS * 2 + 127) / 128) * 128;
-  uint8_t* ring_base = reinterpret_cast<uint8_t*>(hs) + 2 * hbytes;
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(hs) + 3 * hbytes;
   const int cpt = I / G;                         // chunks per row tile
   const int tps = tiles_per_stage, spw = stages_per_warp;
   const uint32_t sbytes = tps * cpt * Fmt::CHB;
@@ -1186,14 +1186,15 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   };
   if (lane == 0)
     for (int q = 0; q < XT_NST && q < Q; ++q) ring.issue(q, src(q), sbytes);
-  // h rows of unit i -> buffer i & 1
+  // h rows of unit i -> buffer i % 3: it is restaged (for unit i + 3) only after every
+  // warp has passed the barrier of unit i + 1, so units need one barrier each
   auto stage_h = [&](int i) {
     const int u = blockIdx.x + i * gridDim.x;
     const uint8_t* w;
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
     const int64_t hb = pb < 0 ? static_cast<int64_t>(T) * a.k : pb;
-    __half* dst = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(hs) + (i & 1) * hbytes);
+    __half* dst = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(hs) + (i % 3) * hbytes);
     const __half* hsrc = reinterpret_cast<const __half*>(a.hbuf);
     for (int e = threadIdx.x; e < np * (I / 8); e += blockDim.x) {
       const int r = e / (I / 8), c = (e % (I / 8)) * 8;
@@ -1217,7 +1218,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
     const bool two = np > 8;
-    const __half* hbuf_s = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(hs) + (i & 1) * hbytes);
+    const __half* hbuf_s = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(hs) + (i % 3) * hbytes);
     const __half* xr[2];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) xr[nt] = hbuf_s + min(nt * 8 + gid, np - 1) * HS;
@@ -1250,8 +1251,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
       __syncwarp();
       if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
     }
-    // a warp that timed out keeps taking part in the CTA barriers until the end
-    __syncthreads();
+    // a warp that timed out keeps staging and taking part in the units' barriers
   }
   cp_async_wait<0>();
 }
@@ -1497,7 +1497,7 @@ static XtPlan xt_plan(const MoeArgs<__nv_bfloat16>& a) {
     p.down_spw = 0;
     for (int spw = 2; spw >= 1; --spw)
       if (tiles % (XT_DN_WARPS * spw * p.down_tps) == 0) { p.down_spw = spw; break; }
-    p.down_smem = xt_head_bytes(a.E) + 2 * ((static_cast<size_t>(XT_MAXT) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
+    p.down_smem = xt_head_bytes(a.E) + 3 * ((static_cast<size_t>(XT_MAXT) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
                   static_cast<size_t>(XT_DN_WARPS) * XT_NST * p.down_tps * cpt * CHB;
     p.down_ok = p.down_spw > 0 && p.down_smem <= XT_SMEM_LIMIT;
   }
