@@ -303,7 +303,10 @@ int qw_moe_partials(void* workspace, int64_t tokens, int64_t hidden, int64_t exp
 /* q/k RMSNorm (zero-centred weights, +1), partial RoPE on the first rotary_dim dims
  * (theta, fp32 angles), and the K/V append of the block (the CacheUpdate role,
  * reference/fused_ops.py:110-124).  qkv bf16 [B*S, ldq] holds per head [q | gate]
- * (heads*2*dim), then k (kv_heads*dim), then v.  q_out bf16 [B, heads, S, dim]. */
+ * (heads*2*dim), then k (kv_heads*dim), then v.  q_out bf16 [B, heads, S, dim].  The
+ * kernel reads the norm weights, qpos and the page table before it waits for the launch
+ * ahead of it (the projection writing qkv), so that launch must not be the one that
+ * wrote them. */
 int qw_attn_prep(const void* qkv, int64_t ldq, const void* q_norm_w, const void* k_norm_w,
                  float eps, float rope_theta, int32_t rotary_dim, const int32_t* qpos,
                  const int32_t* pages, int32_t max_pages, int32_t page_size, void* k_cache,

@@ -319,15 +319,15 @@ __global__ void attn_combine_kernel(const float* __restrict__ opart, const float
 
 // q/k RMSNorm + RoPE + KV append.  One CTA per (token, head slot): slots [0, H) are query
 // heads, [H, H + Hkv) key heads (which also copy their value head).
+constexpr int ATT_PREP_THREADS = 128;
+
 template <int D>
-__global__ void attn_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ldq,
-                                 const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
-                                 float eps, float theta, int rot, const int32_t* __restrict__ qpos,
-                                 const int32_t* __restrict__ pages, int max_pages, int P,
-                                 __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
-                                 __nv_bfloat16* __restrict__ qout, int S, int H, int Hkv) {
-  pdl_wait();   // qkv comes from the predecessor (the projection)
-  pdl_trigger();
+__global__ void __launch_bounds__(ATT_PREP_THREADS) attn_prep_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int64_t ldq, const __nv_bfloat16* __restrict__ qn_w,
+    const __nv_bfloat16* __restrict__ kn_w, float eps, float theta, int rot, const int32_t* __restrict__ qpos,
+    const int32_t* __restrict__ pages, int max_pages, int P, __nv_bfloat16* __restrict__ kc,
+    __nv_bfloat16* __restrict__ vc, __nv_bfloat16* __restrict__ qout, int S, int H, int Hkv) {
+  constexpr int NPT = (D + ATT_PREP_THREADS - 1) / ATT_PREP_THREADS;   // columns per thread
   __shared__ float red[32];
   __shared__ float xr[D];
   const int t = blockIdx.x;  // token row b*S + s
@@ -335,36 +335,57 @@ __global__ void attn_prep_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t 
   const int slot = blockIdx.y;
   const bool is_q = slot < H;
   const int head = is_q ? slot : slot - H;
-  const __nv_bfloat16* src = is_q ? qkv + t * ldq + head * 2 * D : qkv + t * ldq + H * 2 * D + head * D;
+  // before the wait: the norm weight, the rotary factors and the cache page, none of
+  // which the projection (the predecessor) writes
   const __nv_bfloat16* gw = is_q ? qn_w : kn_w;
-  float ss = 0.f;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    const float v = __bfloat162float(src[d]);
-    ss += v * v;
-  }
-  ss = block_sum(ss, red);
-  const float inv = rsqrtf(ss / D + eps);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    const float g = rbf(__bfloat162float(gw[d]) + 1.f);  // zero-centred weight + 1
-    xr[d] = rbf(rbf(__bfloat162float(src[d]) * inv) * g);
-  }
-  __syncthreads();
   const int pos = qpos[b] + s;
   const int half = rot / 2;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float y = xr[d];
+  float gpre[NPT], cpre[NPT], spre[NPT];
+#pragma unroll
+  for (int j = 0; j < NPT; ++j) {
+    const int d = threadIdx.x + j * ATT_PREP_THREADS;
+    gpre[j] = cpre[j] = spre[j] = 0.f;
+    if (d < D) gpre[j] = rbf(__bfloat162float(gw[d]) + 1.f);  // zero-centred weight + 1
     if (d < rot) {
       const int i = d % half;
       const float inv_freq = 1.0f / powf(theta, static_cast<float>(2 * i) / rot);
       const float ang = static_cast<float>(pos) * inv_freq;
-      const float c = rbf(cosf(ang)), sn = rbf(sinf(ang));
+      cpre[j] = rbf(cosf(ang));
+      spre[j] = rbf(sinf(ang));
+    }
+  }
+  const int page = is_q ? 0 : pages[b * max_pages + pos / P];
+  pdl_wait();   // qkv comes from the predecessor (the projection)
+  pdl_trigger();
+  const __nv_bfloat16* src = is_q ? qkv + t * ldq + head * 2 * D : qkv + t * ldq + H * 2 * D + head * D;
+  float xv[NPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NPT; ++j) {
+    const int d = threadIdx.x + j * ATT_PREP_THREADS;
+    xv[j] = d < D ? __bfloat162float(src[d]) : 0.f;
+    ss += xv[j] * xv[j];
+  }
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / D + eps);
+#pragma unroll
+  for (int j = 0; j < NPT; ++j) {
+    const int d = threadIdx.x + j * ATT_PREP_THREADS;
+    if (d < D) xr[d] = rbf(rbf(xv[j] * inv) * gpre[j]);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < NPT; ++j) {
+    const int d = threadIdx.x + j * ATT_PREP_THREADS;
+    if (d >= D) continue;
+    float y = xr[d];
+    if (d < rot) {
       const float other = d < half ? -xr[d + half] : xr[d - half];
-      y = rbf(rbf(xr[d] * c) + rbf(other * sn));
+      y = rbf(rbf(xr[d] * cpre[j]) + rbf(other * spre[j]));
     }
     if (is_q) {
       qout[((static_cast<int64_t>(b) * H + head) * S + s) * D + d] = __float2bfloat16_rn(y);
     } else {
-      const int page = pages[b * max_pages + pos / P];
       const int64_t off = ((static_cast<int64_t>(page) * Hkv + head) * P + pos % P) * D + d;
       kc[off] = __float2bfloat16_rn(y);
       vc[off] = qkv[t * ldq + H * 2 * D + Hkv * D + head * D + d];
@@ -490,7 +511,7 @@ extern "C" int qw_attn_prep(const void* qkv, int64_t ldq, const void* q_norm_w, 
   const dim3 grid(static_cast<unsigned>(batch * seq), static_cast<unsigned>(heads + kv_heads));
   cudaStream_t st = as_stream(stream);
 #define QW_PREP(DD)                                                                                     \
-  QW_LAUNCH_PDL("attn_prep", attn_prep_kernel<DD>, grid, dim3(128), 0, st,                              \
+  QW_LAUNCH_PDL("attn_prep", attn_prep_kernel<DD>, grid, dim3(ATT_PREP_THREADS), 0, st,                              \
       static_cast<const __nv_bfloat16*>(qkv), ldq, static_cast<const __nv_bfloat16*>(q_norm_w),        \
       static_cast<const __nv_bfloat16*>(k_norm_w), eps, rope_theta, rotary_dim, qpos, pages, max_pages, \
       page_size, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),            \
