@@ -272,10 +272,15 @@ __global__ void attn_combine_kernel(const float* __restrict__ opart, const float
                                     int S, int kc) {
   __shared__ float s_w[ATT_MAXSPLIT];
   __shared__ float s_l;
+  const int s = blockIdx.x % S, h = (blockIdx.x / S) % H, b = blockIdx.x / (S * H);
+  // before the wait: the positions and the output gate, which the split kernel (the
+  // predecessor) does not write; with dim <= 256 every thread owns one column
+  const int qpos = qposv ? qposv[b] : qpos_scalar;
+  constexpr bool ONE = D <= 256;
+  float gpre = 0.f;
+  if (ONE && gate && threadIdx.x < D) gpre = rnd<ET>(sigmoid_f(to_f(gate[b * gb + h * gh + s * gs + threadIdx.x])));
   pdl_wait();
   pdl_trigger();
-  const int s = blockIdx.x % S, h = (blockIdx.x / S) % H, b = blockIdx.x / (S * H);
-  const int qpos = qposv ? qposv[b] : qpos_scalar;
   const int nsp = (qpos + S + kc - 1) / kc;
   const int64_t row = (static_cast<int64_t>(b) * H + h) * S + s;   // row index within one split
   const int64_t split_stride = static_cast<int64_t>(B) * H * S;
@@ -312,7 +317,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ opart, const float
       if (w != 0.f) acc += w * v;
     }
     float y = rnd<ET>(acc / L);
-    if (gate) y = rnd<ET>(y * rnd<ET>(sigmoid_f(to_f(gate[b * gb + h * gh + s * gs + d]))));
+    if (gate) y = rnd<ET>(y * (ONE ? gpre : rnd<ET>(sigmoid_f(to_f(gate[b * gb + h * gh + s * gs + d])))));
     out[b * ob + h * oh + s * os + d] = from_f<ET>(y);
   }
 }
