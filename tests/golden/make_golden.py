@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Runs ONLY where the reference checkout is mounted (default ``/root/reference``,
-override with ``QW_REFERENCE``); the committed ``*.npz`` files are what the tests
-read, on any machine.  Nothing here is imported by the library.
+Runs ONLY where a checkout of the reference is present, named by the environment
+variable ``QW_REFERENCE`` (its root directory); the committed ``*.npz`` files are what
+the tests read, on any machine.  Nothing here is imported by the library.
 
 Fixtures:
   ops_fp32.npz        reference/fused_ops.py functions on seeded float32 inputs
@@ -12,7 +12,7 @@ Fixtures:
                       state) on the tiny configuration: greedy decode, then
                       block verify / commit rounds with seeded proposals.
 
-Usage:  python tests/golden/make_golden.py
+Usage:  QW_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -24,10 +24,12 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("QW_REFERENCE", "/root/reference")
+REF = os.environ.get("QW_REFERENCE", "")
 
 
 def _import_reference():
+    if not REF or not os.path.isdir(REF):
+        raise SystemExit("set QW_REFERENCE to the root of a checkout of the reference")
     for sub in ("model", "reference"):
         path = os.path.join(REF, sub)
         if path not in sys.path:
