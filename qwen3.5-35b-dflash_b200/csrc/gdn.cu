@@ -102,7 +102,7 @@ struct GdnSmem {
   float opart[QW_MAX_BLOCK][COLS][KSPLIT];   // per-thread partial outputs, reduced after the recurrence
   float g[QW_MAX_BLOCK];
   float beta[QW_MAX_BLOCK];
-  float sumsq[QW_MAX_BLOCK];
+  float sumsq[VSPLIT][QW_MAX_BLOCK];   // per-token sums of squares of each cluster rank
   float total[QW_MAX_BLOCK];
   // the block's projections of this CTA's channels: q [0, DK), k [DK, 2DK), v [2DK, 2DK+COLS)
   __align__(16) __nv_bfloat16 xin[QW_MAX_BLOCK][2 * DK + COLS];
@@ -370,25 +370,30 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     sm.o[t][c] = rbf(o);   // core tensor in the activation dtype
   }
   __syncthreads();
-  // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225)
+  // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225).  Each CTA
+  // stores its per-token sums of squares into row `rank` of every cluster CTA's table,
+  // so after one cluster barrier all reads are local (and no CTA touches another's
+  // shared memory once it may exit); the rows are added in rank order.
   for (int t = tid / 32; t < ntok; t += THREADS / 32) {
     float ss = 0.f;
     for (int c = tid % 32; c < COLS; c += 32) ss += sm.o[t][c] * sm.o[t][c];
     ss = warp_sum(ss);
-    if (tid % 32 == 0) sm.sumsq[t] = ss;
-  }
-  if constexpr (VSPLIT > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    for (int t = tid; t < ntok; t += THREADS) {
-      float tot = 0.f;
-      for (int r = 0; r < VSPLIT; ++r) tot += cluster.map_shared_rank(&sm.sumsq[0], r)[t];
-      sm.total[t] = tot;
+    if (tid % 32 == 0) {
+      if constexpr (VSPLIT > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+#pragma unroll
+        for (int r = 0; r < VSPLIT; ++r) cluster.map_shared_rank(&sm.sumsq[rank][t], r)[0] = ss;
+      } else {
+        sm.sumsq[0][t] = ss;
+      }
     }
-    cluster.sync();
-  } else {
-    __syncthreads();
-    for (int t = tid; t < ntok; t += THREADS) sm.total[t] = sm.sumsq[t];
+  }
+  if constexpr (VSPLIT > 1) cg::this_cluster().sync();
+  else __syncthreads();
+  for (int t = tid; t < ntok; t += THREADS) {
+    float tot = 0.f;
+    for (int r = 0; r < VSPLIT; ++r) tot += sm.sumsq[r][t];
+    sm.total[t] = tot;
   }
   __syncthreads();
   const int vw = d.v_heads * DV;
