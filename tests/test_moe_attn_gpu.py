@@ -44,7 +44,10 @@ def _tie_heavy_logits(t, e, seed):
 
 @pytest.mark.parametrize("t,e,k,dt", [(16, 256, 8, "bf16"), (256, 256, 8, "bf16"), (64, 16, 4, "bf16"),
                                       (33, 128, 8, "bf16"), (40, 256, 2, "bf16"), (48, 256, 8, "f16"),
-                                      (16, 256, 8, "f32")])
+                                      (16, 256, 8, "f32"),
+                                      # introselect ranges that start in registers: two per lane
+                                      # (64 experts), and part-filled lanes (40 experts)
+                                      (64, 64, 8, "bf16"), (48, 40, 6, "f16")])
 def test_routing_indices_bit_exact_vs_torch_topk(cuda_lib, t, e, k, dt):
     """Router selection equals torch.topk on CPU (the reference's call) element for element,
     ties included (integer-valued rows, and rows whose largest logits are +0.0 and -0.0)."""
