@@ -364,8 +364,9 @@ def run_ours(args, rank, world, local_rank):
                        "step_hbm_frac_of_measured": round(alg["total"] / (ms_max * 1e-3) / (hbm * 1e9), 4),
                        "init_s": round(init_s, 1)},
             "e2e": {"value": round(tok / (e2e_ms * 1e-3), 2), "unit": "tok/s", "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": 2 * B * 4,
-                    "api": "TargetEngine.serve_step (pinned host proposals -> graph -> accepted/next tokens)"},
+                    "h2d_bytes_per_step": B * S * 4, "d2h_bytes_per_step": eng.serve_d2h_bytes(),
+                    "api": "TargetEngine.serve_step (pinned host proposals -> graph -> accepted/next tokens "
+                           "+ device wait status)"},
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": "moe_up_bulk_kernel (routed + shared expert gate/up, W4A16)",
                          "achieved": round(rl_achieved, 1), "peak": hbm, "unit": "GB/s",

@@ -402,6 +402,31 @@ int qw_accept(const void* keys, int64_t nblk, const int32_t* proposals, int32_t*
 int qw_apply_commit(const int32_t* accepted, const int32_t* top1, int32_t* next_token,
                     int32_t* qpos, int64_t batch, int64_t seq, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Bounded device waits.  Kernels that wait on the TMA engine (the cluster linears,
+ * the bulk expert kernels) give up after a bounded time instead of hanging, record
+ * the expiry in a sticky status word of the library and return early: the outputs of
+ * that launch are then incomplete.  The reference fails fast on any backend error and
+ * never retries or falls back (model/qwen35_moe_dflash/fused/ops.py:133-136); these
+ * two calls are how that error reaches the host.
+ * ---------------------------------------------------------------------------- */
+
+/* Stream-ordered (graph-capturable) report: after every earlier kernel on the stream,
+ * writes QW_OK or QW_ERR_TIMEOUT into status (int32, device) and, with clear != 0,
+ * resets the sticky words. */
+int qw_wait_status(int32_t* status, int clear, void* stream);
+
+/* Synchronous check: synchronizes the stream, returns QW_ERR_TIMEOUT (with a message
+ * naming the kernel family) if a wait expired since the last clear, else QW_OK; with
+ * clear != 0 the sticky words are reset. */
+int qw_check_wait_status(int clear, void* stream);
+
+/* Test hook: every later cluster-linear launch from this process waits at most
+ * limit_cycles (0 = the default of about a second) and announces tx_excess_bytes more
+ * on each weight stage than it copies, so that its waits expire (no fault, no hang);
+ * MoE expert launches take the limit only.  (0, 0) restores normal operation. */
+int qw_debug_inject_wait_timeout(int64_t limit_cycles, int64_t tx_excess_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -158,13 +158,17 @@ def route(logits, top_k: int, dtype: str = "f32"):
 
 
 def moe(hidden, router_weight, gate_up, down, *, top_k: int, dtype: str = "f32",
-        emulate_rounding: bool = True, logits=None, return_routing: bool = False):
+        emulate_rounding: bool = True, logits=None, return_routing: bool = False,
+        return_magnitude: bool = False):
     """reference/fused_ops.py:148-173 — routed SwiGLU experts, ascending expert order.
 
     With ``emulate_rounding`` each intermediate is rounded to ``dtype`` where the
     reference's torch ops return ``dtype`` tensors; otherwise everything stays fp32
     and only the result is rounded.  ``logits`` replaces the router GEMV when given
-    (the W4A16 microbench feeds router logits directly).
+    (the W4A16 microbench feeds router logits directly).  ``return_magnitude`` appends
+    the elementwise largest |value| the accumulation passes through (each weighted
+    expert term and each running sum): one rounding step of the sum is one ulp of
+    that magnitude, which bounds how far two correct implementations can part.
     """
     hidden = np.asarray(hidden, np.float32)
     flat = hidden.reshape(-1, hidden.shape[-1])
@@ -174,6 +178,7 @@ def moe(hidden, router_weight, gate_up, down, *, top_k: int, dtype: str = "f32",
     logits = np.asarray(logits, np.float32).reshape(flat.shape[0], -1)
     selected, weights = route(logits, top_k, dtype)
     result = np.zeros_like(flat)
+    magnitude = np.zeros_like(flat)
     experts = logits.shape[-1]
     for expert in range(experts):
         tokens, slots = np.nonzero(selected == expert)
@@ -184,8 +189,14 @@ def moe(hidden, router_weight, gate_up, down, *, top_k: int, dtype: str = "f32",
         gate, up = gu[:, :inter], gu[:, inter:]
         act = r(r(silu(gate)) * up)
         values = r(act @ np.asarray(down[expert], np.float32).T)
-        result[tokens] = r(result[tokens] + r(values * weights[tokens, slots][:, None]))
+        term = r(values * weights[tokens, slots][:, None])
+        result[tokens] = r(result[tokens] + term)
+        if return_magnitude:
+            magnitude[tokens] = np.maximum(magnitude[tokens], np.maximum(np.abs(term), np.abs(result[tokens])))
     out = round_to(result, dtype).reshape(hidden.shape)
+    extra = ()
     if return_routing:
-        return out, selected, weights
-    return out
+        extra += (selected, weights)
+    if return_magnitude:
+        extra += (magnitude.reshape(hidden.shape),)
+    return (out,) + extra if extra else out

@@ -612,7 +612,10 @@ extern "C" int qw_attention_noalloc(const void* q, const void* k, const void* v,
                 static_cast<long long>(dim));
   SplitPlan p = plan_splits(static_cast<int>(batch), static_cast<int>(heads), static_cast<int>(kv_heads),
                             static_cast<int>(seq), static_cast<int>(total));
-  const int64_t need = static_cast<int64_t>(p.nsplit) * batch * heads * seq * (dim + 2) * 4;
+  // the same sizing as a caller workspace of qw_attention, so the bound cannot drift
+  // from the split plan or the opart / ml layout below
+  const int64_t need = qw_attn_workspace_bytes(batch, heads, kv_heads, seq, dim, total);
+  QW_CHECK_ARG(need >= 0, "attention_noalloc: no workspace size for this shape");
   QW_CHECK_ARG(need <= static_cast<int64_t>(QW_ATTN_NOALLOC_SCRATCH_BYTES),
                "attention_noalloc: this shape needs %lld scratch bytes, the static scratch holds %lld "
                "(use qw_attention with a caller workspace)",

@@ -4,7 +4,7 @@
 //    sequential recurrence, one CTA per (sequence, head), state in shared memory.
 //  * qw_gdn_verify / qw_gdn_commit — the block-verify form.  One thread-block cluster
 //    per (sequence, value head); each CTA of the cluster owns Dv/VSPLIT state columns
-//    and keeps them in registers (4 threads per column, Dk/4 rows each) across the
+//    and keeps them in registers (8 threads per column, Dk/8 rows each) across the
 //    block's tokens.  The prologue fuses conv_state_update + causal_conv1d + SiLU
 //    (fused/model.py:232-239), the q/k L2 norm and the gate math (:243-253); the
 //    epilogue fuses the gated RMSNorm x SiLU(z) (:219-225), with the row sum of squares
@@ -173,6 +173,10 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   const int vcol0 = rank * COLS;        // first state column of this CTA within the head
 
   if (COMMIT && ntok <= 0) return;      // nothing accepted: the state stays S0
+  // verify pushes its gated-norm sums into the peer CTAs' shared memory after the
+  // recurrence; the arrival here and the wait before those stores make sure every CTA
+  // of the cluster has started by then (the wait is hidden behind the recurrence)
+  if constexpr (!COMMIT && VSPLIT > 1) cluster_arrive_relaxed();
 
   // ---- state columns into registers (bank layout [slot][head][Dv][Dk], column-major);
   // issued first so their latency overlaps the staging below
@@ -374,6 +378,7 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   // stores its per-token sums of squares into row `rank` of every cluster CTA's table,
   // so after one cluster barrier all reads are local (and no CTA touches another's
   // shared memory once it may exit); the rows are added in rank order.
+  if constexpr (VSPLIT > 1) cluster_wait();   // every peer CTA is running (arrived above)
   for (int t = tid / 32; t < ntok; t += THREADS / 32) {
     float ss = 0.f;
     for (int c = tid % 32; c < COLS; c += 32) ss += sm.o[t][c] * sm.o[t][c];

@@ -27,8 +27,12 @@ struct LinArgs {
 
 // Argmax key of logit `v` (rounded to bf16, the reference's logits dtype) at row n:
 // larger value wins, then the lower index (torch argmax returns the first maximum).
+// -0 and +0 get one key, so a -0 logit ties with a +0 one and the lower index wins
+// (the stable top-1 rule, targets/cpro/ops/draft-top1/src/reference/top1_cpu.cpp:12-16).
 __device__ __forceinline__ unsigned long long argmax_key(float v, int n) {
-  return (static_cast<unsigned long long>(float_key(rbf(v))) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(n));
+  const float r = rbf(v);
+  return (static_cast<unsigned long long>(float_key(r == 0.f ? 0.f : r)) << 32) |
+         (0xFFFFFFFFu - static_cast<uint32_t>(n));
 }
 
 template <class Fmt, int NT, int PF, bool ARGMAX = false>
@@ -152,6 +156,14 @@ constexpr int CL_MAXS = 8;      // ring stages per warp, at most
 
 __device__ int32_t g_linear_wait_status;   // sticky: a bounded wait in a cluster linear expired
 
+static std::mutex g_lin_status_mu;
+static int32_t* g_lin_status_ptr[64] = {};
+
+int linear_wait_status_addr(int32_t** out) {
+  return symbol_addr_cached(g_linear_wait_status, g_lin_status_ptr, 64, g_lin_status_mu, out,
+                            "linear wait status address");
+}
+
 struct ClArgs {
   const __nv_bfloat16* x;
   const uint8_t* w;
@@ -161,6 +173,7 @@ struct ClArgs {
   int tpc;        // row tiles per cluster, at most (partials buffer)
   int nst;        // ring stages per warp
   long long limit;
+  unsigned tx_excess;   // 0 except under qw_debug_inject_wait_timeout
 };
 
 __host__ __device__ inline size_t cl_head_bytes(int tpc) {
@@ -204,7 +217,7 @@ __global__ void __launch_bounds__(CL_WARPS * 32, 1) cluster_linear_kernel(ClArgs
   auto issue = [&](int j) {
     uint64_t* b = wbar + (j % nst);
     fence_proxy_async();
-    mbar_arrive_expect_tx(b, wbytes);
+    mbar_arrive_expect_tx(b, wbytes + a.tx_excess);
     bulk_g2s(wring + (j % nst) * sbytes, src(j), wbytes, b);
   };
   if (lane == 0 && wbytes)
@@ -394,7 +407,9 @@ static int launch_linear_cluster(const LinArgs& l, cudaStream_t s) {
     if (res >= p.ncl) break;
     if (!cl_plan<Fmt>(l, res, p)) return QW_ERR_UNSUPPORTED;
   }
-  ClArgs a{l.x, l.w, l.y, l.ldy, l.tokens, l.n, l.k, l.mode, p.tpc, p.nst, QW_WAIT_LIMIT};
+  const WaitInjection inj = wait_injection();
+  ClArgs a{l.x, l.w, l.y, l.ldy, l.tokens, l.n, l.k, l.mode, p.tpc, p.nst,
+           inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT, inj.tx_excess};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.ncl * CL_SIZE);
   cfg.blockDim = dim3(CL_WARPS * 32);

@@ -38,7 +38,7 @@ struct RouteView {
   int32_t* topk_idx;    // [T*k]
   float* topk_w;        // [T*k]  (value of the activation dtype)
   float* shared_gate;   // [T]
-  int32_t* n_active;    // [4]: [0] active experts, [1] device status (sticky, bulk_ring.cuh)
+  int32_t* n_active;    // [4]: [0] active experts, [1..3] unused
   int32_t* active;      // [min(E, T*k)]
   int32_t* pair_off;    // [min(E, T*k) + 1]
   int32_t* pair_tok;    // [T*k]
@@ -972,9 +972,21 @@ __device__ __forceinline__ void xt_slot(const A& a, const XtRoute& r, int sl, bo
 
 struct XtArgs {
   MoeArgs<__nv_bfloat16> m;
-  int32_t* status;
+  int32_t* status;      // g_moe_wait_status on the launching device
   long long limit;
 };
+
+// Sticky status of the expert kernels' bounded waits (bulk_ring.cuh): set when a wait
+// expired, read and cleared by qw_wait_status / qw_check_wait_status.
+__device__ int32_t g_moe_wait_status;
+
+static std::mutex g_moe_status_mu;
+static int32_t* g_moe_status_ptr[64] = {};
+
+int moe_wait_status_addr(int32_t** out) {
+  return symbol_addr_cached(g_moe_wait_status, g_moe_status_ptr, 64, g_moe_status_mu, out,
+                            "moe wait status address");
+}
 
 // Gate/up.  Unit = (slot, intermediate tile j): the gate row tile j then the up row tile
 // I/16 + j, each cut into stages of up to XT_UP_CPS chunks; unit u goes to warp u mod (all
@@ -1517,7 +1529,8 @@ static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p,
                                  static_cast<int>(XT_SMEM_LIMIT));
   });
   if (err != cudaSuccess) return cuda_status(err, "moe bulk smem attribute");
-  XtArgs xa{a, status, QW_WAIT_LIMIT};
+  const WaitInjection inj = wait_injection();
+  XtArgs xa{a, status, inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT};
   const int grid = sm_count();
   if (up) {
     QW_LAUNCH_PDL("moe up (bulk)", moe_up_bulk_kernel<G>, dim3(grid), dim3(XT_UP_WARPS * 32), p.up_smem, s, xa);
@@ -1533,8 +1546,9 @@ template <int G>
 static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bool up, bool down,
                              bool lists_ready) {
   const XtPlan p = xt_plan<G>(a);
-  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
-  int32_t* status = rv.n_active + 1;
+  int32_t* status = nullptr;
+  const int src = moe_wait_status_addr(&status);
+  if (src != QW_OK) return src;
   // the bulk pair keeps h (the down input) in fp16, the streaming pair in bf16: both
   // halves of one MoE always come from the same pair
   if (p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);

@@ -1,6 +1,8 @@
 // Shared device/host helpers for the sm_100a kernels of libqw_b200.
 #pragma once
 
+#include <mutex>
+
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -17,6 +19,40 @@ namespace qw {
 void set_error(const char* fmt, ...);
 int fail(int status, const char* fmt, ...);
 int cuda_status(cudaError_t err, const char* what);
+
+// Bounded device waits (bulk-copy rings) record an expiry in a sticky word of their
+// translation unit; these return that word's device address on the current device.
+int linear_wait_status_addr(int32_t** out);
+int moe_wait_status_addr(int32_t** out);
+
+// Test-only injection into the cluster linear kernels' waits (qw_debug_inject_wait_timeout):
+// the wait limit in cycles (0: the default) and extra bytes announced on every stage's
+// barrier beyond the bytes copied, so that no stage completes and every wait expires.
+struct WaitInjection {
+  long long limit;
+  unsigned tx_excess;
+};
+WaitInjection wait_injection();
+
+// Device address of a __device__ variable on the current device, looked up once per
+// device (cudaGetSymbolAddress with that device current) and cached.  `sym` must be
+// named in the translation unit that defines it.
+template <typename T>
+int symbol_addr_cached(const T& sym, T** cache, int ncache, std::mutex& mu, T** out, const char* what) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_status(err, what);
+  if (dev < 0 || dev >= ncache) return fail(QW_ERR_UNSUPPORTED, "%s: device %d beyond the %d tracked", what, dev, ncache);
+  std::lock_guard<std::mutex> guard(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, sym);
+    if (err != cudaSuccess) return cuda_status(err, what);
+    cache[dev] = static_cast<T*>(p);
+  }
+  *out = cache[dev];
+  return QW_OK;
+}
 
 #define QW_CHECK_ARG(cond, ...)                                   \
   do {                                                            \
@@ -40,6 +76,14 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // Without a programmatic predecessor both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// Split cluster barrier.  Every thread of every CTA of the cluster arrives (relaxed: it
+// publishes no memory) and later waits; after the wait every CTA of the cluster is known
+// to be running, which distributed shared memory stores into a peer CTA require.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,

@@ -213,6 +213,9 @@ class TargetEngine:
         self.accepted = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.next_token = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.qpos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        # QW_OK / QW_ERR_TIMEOUT of the bounded device waits of the last forward
+        self.wait_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._wait_status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
         # state banks
         self.conv_hist = torch.zeros(max(ng, 1), batch, c.conv_channels, c.linear_conv_kernel_dim - 1,
@@ -336,6 +339,16 @@ class TargetEngine:
                        gamma.data_ptr(), self.normed.data_ptr(), eps, self._tap(l), c.feature_width, int(last), st)
         self._call("qw_lmhead_argmax", self.normed.data_ptr(), self.glob["lm_head"].data_ptr(), None,
                    self.keys.data_ptr(), T, self.vocab_pad, H, st)
+        # did a bounded wait of this block's kernels expire? (read back with the results)
+        self._call("qw_wait_status", self.wait_status.data_ptr(), 1, st)
+
+    def raise_on_wait_timeout(self, status: int | None = None):
+        """TimeoutError if a bounded device wait of the last forward expired (its outputs
+        are incomplete); ``status`` is an already-copied value of ``wait_status``."""
+        value = int(self.wait_status.item()) if status is None else int(status)
+        if value != lib.QW_OK:
+            raise TimeoutError("a bounded device wait expired during the verify forward: "
+                               "the block's outputs are incomplete")
 
     def accept(self, auto_commit: bool):
         self._call("qw_accept", self.keys.data_ptr(), self.nblk, self.tokens.data_ptr(), self.top1.data_ptr(),
@@ -410,8 +423,14 @@ class TargetEngine:
         self.graph.replay()
         host_out[: self.B].copy_(self.accepted, non_blocking=True)
         host_out[self.B: 2 * self.B].copy_(self.next_token, non_blocking=True)
+        self._wait_status_host.copy_(self.wait_status, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        self.raise_on_wait_timeout(self._wait_status_host[0])
         return host_out
+
+    def serve_d2h_bytes(self) -> int:
+        """Bytes ``serve_step`` copies back per step: accepted + next token + wait status."""
+        return 4 * (2 * self.B + 1)
 
     # ------------------------------------------------------------------ graph
     def capture(self):

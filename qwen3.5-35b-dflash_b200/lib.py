@@ -84,6 +84,9 @@ SIGNATURES = {
     "qw_lmhead_argmax": (_c.c_int, [P, P, P, P, I64, I64, I64, P]),
     "qw_accept": (_c.c_int, [P, I64, P, P, P, P, P, P, I64, I64, _c.c_int, P]),
     "qw_apply_commit": (_c.c_int, [P, P, P, P, I64, I64, P]),
+    "qw_wait_status": (_c.c_int, [P, _c.c_int, P]),
+    "qw_check_wait_status": (_c.c_int, [_c.c_int, P]),
+    "qw_debug_inject_wait_timeout": (_c.c_int, [I64, I64]),
 }
 
 _lock = threading.Lock()

@@ -96,6 +96,7 @@ class TargetSession:
         e.tokens.copy_(torch.tensor(padded, dtype=torch.int32))
         e.forward()
         e.accept(auto_commit=False)
+        e.raise_on_wait_timeout()   # no retry, no fallback (fused/ops.py:133-136)
         self._forward_id += 1
         return self._forward_id
 

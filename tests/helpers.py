@@ -13,14 +13,16 @@ from oracle.numerics import bf16_round
 ATOL, RTOL = 2e-2, 1e-2
 
 
-def assert_close(got, want, atol=ATOL, rtol=RTOL, what="", row_scale=False, strict_frac=None):
+def assert_close(got, want, atol=ATOL, rtol=RTOL, what="", row_scale=False, strict_frac=None, magnitude=None):
     """|got - want| <= atol + rtol * |want| elementwise.
 
     row_scale: the relative term uses max(|want|, RMS of want's last-axis row), for
     outputs that are sums of bf16-rounded partial sums (the reference's MoE accumulates
     experts in bf16, so a one-ulp difference in an expert's output carries the row's
-    scale into a small, cancelled result).  strict_frac: additionally require that
-    fraction of elements to meet the plain elementwise bound.
+    scale into a small, cancelled result).  magnitude: an explicit elementwise magnitude
+    for the relative term (e.g. the largest intermediate of a bf16 accumulation).
+    strict_frac: additionally require that fraction of elements to meet the plain
+    elementwise bound.
     """
     a = np.asarray(got, np.float64)
     b = np.asarray(want, np.float64)
@@ -31,6 +33,8 @@ def assert_close(got, want, atol=ATOL, rtol=RTOL, what="", row_scale=False, stri
         assert ok.mean() >= strict_frac, f"{what}: only {ok.mean():.5f} of elements within the strict bound"
     if row_scale:
         mag = np.maximum(mag, np.sqrt(np.mean(b * b, axis=-1, keepdims=True)))
+    if magnitude is not None:
+        mag = np.maximum(mag, np.asarray(magnitude, np.float64))
     excess = np.abs(a - b) - (atol + rtol * mag)
     worst = np.unravel_index(np.argmax(excess), excess.shape) if excess.size else ()
     assert excess.size == 0 or excess.max() <= 0, (

@@ -68,7 +68,7 @@ def test_gated_delta_rule_matches_reference(golden, cuda_lib, tag):
             assert_close(to_np(st), d[f"gdn_state_{norm}"], 1e-5, 1e-4, "state")
 
 
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 8, 32])
 def test_gated_delta_rule_config3_shapes(cuda_lib, batch):
     """Full head shape (32 heads x 128) with ragged effective lengths, fp32 in and out."""
     from qwen35_dflash_b200 import fused_ops as Q
@@ -179,11 +179,13 @@ def _gdn_device(case, batch, seq, k_heads, v_heads, dk, dv, slots):
     return dev, dims
 
 
-@pytest.mark.parametrize("batch,k_heads,v_heads,dk", [(1, 16, 32, 128), (3, 4, 8, 64), (8, 16, 32, 128)])
+@pytest.mark.parametrize("batch,k_heads,v_heads,dk", [(1, 16, 32, 128), (3, 4, 8, 64), (8, 16, 32, 128),
+                                                    (32, 16, 32, 128)])
 def test_gdn_verify_and_commit(cuda_lib, batch, k_heads, v_heads, dk):
     from qwen35_dflash_b200 import lib
     seq, dv = 16, dk
-    slots = [(5 * i + 2) % (2 * batch + 1) for i in range(batch)]
+    # distinct bank slots, scattered over twice the batch
+    slots = [int(i) for i in np.random.default_rng(batch + 100).permutation(2 * batch + 1)[:batch]]
     case = _gdn_case(batch, seq, k_heads, v_heads, dk, dv, slots, seed=batch)
     dev, dims = _gdn_device(case, batch, seq, k_heads, v_heads, dk, dv, slots)
     accepted = [(16, 0, 5, 1, 9, 16, 3, 12)[i % 8] for i in range(batch)]
@@ -209,3 +211,79 @@ def test_gdn_verify_and_commit(cuda_lib, batch, k_heads, v_heads, dk):
         want_hist = case["hist"][slots[i]] if r == 0 else commits[r][1][i]
         assert_close(bank[slots[i]], want_state, 1e-5, 1e-4, f"state seq {i} r={r}")
         np.testing.assert_array_equal(hist[slots[i]], want_hist)
+
+
+def _stable_top1_bits(logits_bf16: torch.Tensor) -> np.ndarray:
+    """Row argmax of bf16 logits by the stable top-1 rule of the reference
+    (targets/cpro/ops/draft-top1/src/reference/top1_cpu.cpp:12-46): the larger value
+    wins, -0 and +0 are equal, ties go to the lowest index."""
+    bits = logits_bf16.view(torch.int16).cpu().numpy().astype(np.int64) & 0xFFFF
+    bits = np.where((bits & 0x7FFF) == 0, 0, bits)
+    key = np.where(bits & 0x8000, (~bits) & 0xFFFF, bits ^ 0x8000)
+    return np.argmax(key, axis=-1).astype(np.int32)   # numpy: the first maximum
+
+
+@pytest.mark.parametrize("n", [32768, 248320])
+def test_lmhead_argmax_stable_ties(cuda_lib, n):
+    """qw_lmhead_argmax + qw_accept against the stable top-1 rule with planted ties:
+    rows 0-7 have an exact tie of three duplicated lm_head rows at their maximum, in
+    different CTAs (the lowest index must win); rows 8-11 have their maximum at 0 with a
+    -0 logit below a +0 one in index order (an activation pair whose products cancel to a
+    negative value under bf16's smallest subnormal, so the bf16 logit is -0); rows 12-15
+    have x = 0, every logit +0 (index 0 wins).  The kernel's logits come back too: its
+    top-1 must equal the rule applied to them, and the planted maxima must be where
+    they were planted."""
+    from qwen35_dflash_b200 import lib, w4
+    torch.manual_seed(n)
+    k, t = 2048, 16
+    dup = [17, n // 3 + 5, n - 40]          # three equal rows, far apart (different CTAs)
+    neg0, pos0 = 40, (41, 3001)              # the -0 row below the +0 rows
+    base = torch.randn(k, device="cuda")
+    x = torch.zeros(t, k, device="cuda")
+    x[:8] = base + 0.05 * torch.randn(8, k, device="cuda")
+    # rows 8-11: only k = 0 and k = 256 are nonzero (positive), bf16-exact
+    x[8:12, 0] = (1 + 2 ** -6) * 2.0 ** -62
+    x[8:12, 256] = (1 + 2 ** -7) * 2.0 ** -62
+    w = torch.randn(n, k, device="cuda") * 0.02
+    w[:, 0] = -w[:, 0].abs() - 0.01         # rows 8-11: every ordinary logit < 0
+    w[:, 256] = -w[:, 256].abs() - 0.01
+    best = base * 0.5
+    best[0] = best[256] = -1.0
+    for r in dup:
+        w[r] = best
+    w[neg0] = 0.0                             # products (1+2^-6)2^-125 and -(1+2^-7)^2 2^-125
+    w[neg0, 0] = 2.0 ** -63
+    w[neg0, 256] = -(1 + 2 ** -7) * 2.0 ** -63
+    for r in pos0:
+        w[r] = 0.0
+    x = x.to(torch.bfloat16)
+    w = w.to(torch.bfloat16)
+    assert float(x[8, 0]) == (1 + 2 ** -6) * 2.0 ** -62 and float(w[neg0, 256]) == -(1 + 2 ** -7) * 2.0 ** -63
+    stream = w4.pack_b16(w)
+    nblk = cuda_lib.qw_lmhead_blocks(n)
+    keys = torch.zeros(nblk, t, dtype=torch.int64, device="cuda")
+    logits = torch.empty(t, n, dtype=torch.bfloat16, device="cuda")
+    st = lib.stream_ptr()
+    lib.call("qw_lmhead_argmax", x.data_ptr(), stream.data_ptr(), logits.data_ptr(), keys.data_ptr(), t, n, k, st)
+    props = torch.zeros(t, dtype=torch.int32, device="cuda")
+    top1 = torch.empty(t, dtype=torch.int32, device="cuda")
+    maxacc = torch.empty(1, dtype=torch.int32, device="cuda")
+    nxt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    lib.call("qw_accept", keys.data_ptr(), nblk, props.data_ptr(), top1.data_ptr(), maxacc.data_ptr(),
+             nxt.data_ptr(), None, None, 1, t, 0, st)
+    torch.cuda.synchronize()
+    got = top1.cpu().numpy()
+    np.testing.assert_array_equal(got, _stable_top1_bits(logits))
+    lg = logits.float().cpu().numpy()
+    for i in range(8):       # the duplicated rows are the maximum, bit-equal
+        assert lg[i, dup[0]] == lg[i, dup[1]] == lg[i, dup[2]] == lg[i].max(), i
+    assert (got[:8] == dup[0]).all(), got[:8]
+    bits = logits.view(torch.int16).cpu().numpy().astype(np.int64) & 0xFFFF
+    for i in range(8, 12):   # maximum 0 with the -0 logit first; the rule takes the -0 row
+        # the planted row is -0 when the fp32 accumulator keeps the subnormal sum (it is
+        # +0 if the sum is flushed; either way the lowest index holds the maximum)
+        assert bits[i, neg0] in (0x8000, 0) and bits[i, pos0[0]] == 0 and bits[i, pos0[1]] == 0, i
+        assert lg[i].max() == 0.0, i
+    print(f"\nplanted -0 logit came out as 0x{int(bits[8, neg0]):04x}")
+    assert (got[8:12] == neg0).all(), got[8:12]
+    assert (got[12:] == 0).all(), got[12:]

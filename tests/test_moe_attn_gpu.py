@@ -107,9 +107,10 @@ class _LazyDequant:
         return (self.q[e].astype(np.float32) * np.repeat(self.s[e], self.group, -1)).astype(np.float32)
 
 
-@pytest.mark.parametrize("t", [16, 64])
+@pytest.mark.parametrize("t", [16, 64, 256])
 def test_moe_w4a16_matches_oracle(cuda_lib, t):
-    """Config-2 microbench shape: H 2048, 256 experts top-8 + shared, I 512, W4 g128."""
+    """Config-2 microbench shapes (T = 16, 64, 256): H 2048, 256 experts top-8 + shared,
+    I 512, W4 g128, scales U(0.005, 0.02)."""
     from qwen35_dflash_b200 import lib, w4
     torch.manual_seed(t)
     h, e, k, inter, g = 2048, 256, 8, 512, 128
@@ -137,9 +138,9 @@ def test_moe_w4a16_matches_oracle(cuda_lib, t):
     # oracle (bf16 rounding points of fused_ops.moe + the shared expert of fused/model.py:305-307)
     xn = to_np(x)
     ln = to_np(logits)
-    routed, sel, _ = F.moe(xn, None, _LazyDequant(qgu.cpu().numpy(), sgu.float().cpu().numpy(), g),
-                           _LazyDequant(qdn.cpu().numpy(), sdn.float().cpu().numpy(), g), top_k=k,
-                           dtype="bf16", logits=ln[:, :e], return_routing=True)
+    routed, sel, _, mag = F.moe(xn, None, _LazyDequant(qgu.cpu().numpy(), sgu.float().cpu().numpy(), g),
+                                _LazyDequant(qdn.cpu().numpy(), sdn.float().cpu().numpy(), g), top_k=k,
+                                dtype="bf16", logits=ln[:, :e], return_routing=True, return_magnitude=True)
     wsg = to_np(w4.dequantize(qsgu, ssgu, g))
     wsd = to_np(w4.dequantize(qsdn, ssdn, g))
     gate = bf16_round(xn @ wsg[:inter].T)
@@ -147,11 +148,18 @@ def test_moe_w4a16_matches_oracle(cuda_lib, t):
     act = bf16_round(bf16_round(F.silu(gate)) * up)
     shared = bf16_round(act @ wsd.T)
     sgate = bf16_round(F.sigmoid(ln[:, e:e + 1]))
-    want = bf16_round(routed + bf16_round(shared * sgate))
+    sterm = bf16_round(shared * sgate)
+    want = bf16_round(routed + sterm)
     idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
     np.testing.assert_array_equal(idx, sel)
     _check_lists(ws, t, e, k, sel)   # as the expert kernels built (and published) them
-    assert_close(to_np(out), want, what="moe w4a16", row_scale=True, strict_frac=0.999)
+    # BASELINE's bound, |got - want| <= 2e-2 + 1e-2 M, with M the largest magnitude the
+    # reference's bf16 expert accumulation passes through at that element (the routed
+    # terms and running sums, the shared term): the sum is rounded to bf16 after every
+    # add, so one ulp of a large term survives cancellation; >= 99.9 % of elements must
+    # also meet the plain elementwise bound
+    mag = np.maximum(mag, np.abs(sterm))
+    assert_close(to_np(out), want, what="moe w4a16", magnitude=mag, strict_frac=0.999)
 
 
 @pytest.mark.parametrize("t,g", [(16, 128), (5, 64), (16, 32)])
