@@ -17,10 +17,11 @@ e2e       the same metric through TargetEngine.serve_step (proposals from pinned
 roofline  the dominant kernel (routed-expert gate/up), achieved algorithmic bytes per
           launch / its CUDA-event duration against the measured HBM copy bandwidth.
 cpu_baseline / --impl reference
-          the reference's CPU algorithm (the numpy restatement of reference/fused_ops.py
-          and fused/model.py in oracle/) on the host cores: one GDN layer, one attention
-          layer and one MoE layer at the same shapes, and 1/8 of the lm_head, timed and
-          combined as 30*GDN + 10*attention + 40*MoE + lm_head.
+          the reference's CPU path (torch on every host core: the restatement of
+          reference/fused_ops.py and fused/model.py in oracle/ref_torch.py, bf16 weights):
+          one GDN layer, one attention layer and one MoE layer at the same shapes and 1/8
+          of the lm_head per sample, a verify step extrapolated as 30*GDN + 10*attention +
+          40*MoE + 8*(lm_head/8); the reference arm runs one sample per step.
 Multi-GPU (torchrun): every rank runs an independent replica of the same workload
 (requests are data-parallel); value sums the ranks ("scaling": "weak").
 """
@@ -111,83 +112,107 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- CPU side
-def cpu_reference_estimate(threads: int | None = None):
-    """The reference CPU algorithm (numpy restatement, oracle/) at the benchmark's shapes.
+def _host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-    Returns (step_seconds, sample description).  Weights are random N(0, 0.02) fp32
-    (the CPU path computes on dequantized weights); routed experts are materialized for
-    the experts the routing selects."""
-    import numpy as np
-    from oracle import fused_ops_np as F
-    from oracle.model_np import OracleTarget, LayerState
-    import __graft_entry__
-    __graft_entry__.load_package()
-    from qwen35_dflash_b200.config import QWEN35_35B_A3B, with_layers
 
-    cfg = QWEN35_35B_A3B
-    rng = np.random.default_rng(7)
-    H, E, I = cfg.hidden_size, cfg.num_experts, cfg.moe_intermediate_size
-    s, ctx = 16, 4096
+class CpuReference:
+    """The reference's CPU path (torch on the host cores: oracle/ref_torch.py restates
+    reference/fused_ops.py and the layer bodies of fused/model.py) at the benchmark's
+    config-4 shapes: one gated-DeltaNet layer, one attention layer over 4096 tokens of
+    context, one MoE layer (16 tokens, top-8 of 256 + shared) and 1/8 of the lm_head,
+    dense bf16 weights N(0, 0.02) (the W4 weights dequantized), fp32 GDN state.  A sample
+    times one of each; a verify step is extrapolated as 30 GDN + 10 attention + 40 MoE +
+    8 x (1/8 lm_head)."""
 
-    class LazyExperts:
-        def __init__(self, shape):
-            self.shape, self.cache = shape, {}
+    def __init__(self, ctx: int = 4096, seed: int = 7):
+        import torch
+        self.threads = _host_cores()
+        torch.set_num_threads(self.threads)   # torchrun exports OMP_NUM_THREADS=1
+        import __graft_entry__
+        __graft_entry__.load_package()
+        from qwen35_dflash_b200.config import QWEN35_35B_A3B
+        self.cfg = c = QWEN35_35B_A3B
+        self.ctx = ctx
+        gen = torch.Generator().manual_seed(seed)
+        bf = torch.bfloat16
 
-        def __getitem__(self, e):
-            if e not in self.cache:
-                self.cache[e] = rng.normal(0, 0.02, self.shape).astype(np.float32)
-            return self.cache[e]
+        def w(*shape, std=0.02):
+            return (torch.randn(*shape, generator=gen) * std).to(bf)
 
-    def w(*shape):
-        return rng.normal(0, 0.02, shape).astype(np.float32)
+        H, E, I = c.hidden_size, c.num_experts, c.moe_intermediate_size
+        D, Hq, Hkv = c.head_dim, c.num_attention_heads, c.num_key_value_heads
+        vh, dk, dv = c.linear_num_value_heads, c.linear_key_head_dim, c.linear_value_head_dim
+        self.gdn_w = {"qkv": w(c.conv_channels, H), "z": w(c.value_width, H), "b": w(vh, H), "a": w(vh, H),
+                      "A_log": torch.log(torch.arange(1, vh + 1, dtype=torch.float32)),
+                      "dt_bias": w(vh).float(), "conv": w(c.conv_channels, 1, c.linear_conv_kernel_dim),
+                      "norm": torch.ones(dv, dtype=bf), "out": w(H, c.value_width)}
+        self.conv_hist = torch.randn(1, c.conv_channels, c.linear_conv_kernel_dim - 1, generator=gen).to(bf)
+        self.state = torch.randn(1, vh, dk, dv, generator=gen) * 0.02
+        self.attn_w = {"q": w(Hq * 2 * D, H), "k": w(Hkv * D, H), "v": w(Hkv * D, H), "o": w(H, Hq * D),
+                       "q_norm": torch.zeros(D, dtype=bf), "k_norm": torch.zeros(D, dtype=bf)}
+        self.key = torch.randn(1, Hkv, ctx, D, generator=gen).to(bf)
+        self.value = torch.randn(1, Hkv, ctx, D, generator=gen).to(bf)
+        self.moe_w = {"router": w(E, H), "shared_gu": w(2 * c.shared_expert_intermediate_size, H),
+                      "shared_down": w(H, c.shared_expert_intermediate_size), "shared_gate": w(1, H)}
+        self._experts = {}
+        self._expert_seed = seed
+        self.lm = w(c.vocab_size // 8, H)
+        self.x = torch.randn(1, 16, H, generator=gen).to(bf)
 
-    weights = {}
-    p = "target.layers.0"
-    a = p + ".linear_attn"
-    weights.update({a + ".in_proj_qkv.weight": w(cfg.conv_channels, H), a + ".in_proj_z.weight": w(cfg.value_width, H),
-                    a + ".in_proj_b.weight": w(32, H), a + ".in_proj_a.weight": w(32, H),
-                    a + ".A_log": np.log(np.arange(1, 33, dtype=np.float32)), a + ".dt_bias": w(32),
-                    a + ".conv1d.weight": w(cfg.conv_channels, 1, 4), a + ".norm.weight": np.ones(128, np.float32),
-                    a + ".out_proj.weight": w(H, cfg.value_width)})
-    p3 = "target.layers.3"
-    t = p3 + ".self_attn"
-    D = cfg.head_dim
-    weights.update({t + ".q_proj.weight": w(16 * 2 * D, H), t + ".k_proj.weight": w(2 * D, H),
-                    t + ".v_proj.weight": w(2 * D, H), t + ".o_proj.weight": w(H, 16 * D),
-                    t + ".q_norm.weight": np.zeros(D, np.float32), t + ".k_norm.weight": np.zeros(D, np.float32)})
-    m = p + ".mlp"
-    weights.update({m + ".gate.weight": w(E, H), m + ".experts.gate_up_proj": LazyExperts((2 * I, H)),
-                    m + ".experts.down_proj": LazyExperts((H, I)), m + ".shared_expert.gate_proj.weight": w(I, H),
-                    m + ".shared_expert.up_proj.weight": w(I, H), m + ".shared_expert.down_proj.weight": w(H, I),
-                    m + ".shared_expert_gate.weight": w(1, H)})
-    small = with_layers(cfg, 4)
-    oc = small.to_hf_text_config()
-    model = OracleTarget(oc, {k: v for k, v in weights.items() if not isinstance(v, LazyExperts)},
-                         (0,), act="bf16", rope="f32")
-    model.w[m + ".experts.gate_up_proj"] = weights[m + ".experts.gate_up_proj"]
-    model.w[m + ".experts.down_proj"] = weights[m + ".experts.down_proj"]
-    x = rng.normal(0, 1, (1, s, H)).astype(np.float32)
-    gdn_cache = LayerState(conv=rng.normal(0, 1, (1, cfg.conv_channels, 3)).astype(np.float32),
-                           recurrent=rng.normal(0, 0.02, (1, 32, 128, 128)).astype(np.float32))
-    kv = LayerState(key=rng.normal(0, 1, (1, 2, ctx, D)).astype(np.float32),
-                    value=rng.normal(0, 1, (1, 2, ctx, D)).astype(np.float32))
-    lm = w(cfg.vocab_size // 8, H)
+    def _expert(self, e):
+        import torch
+        if e not in self._experts:
+            g = torch.Generator().manual_seed(self._expert_seed * 1000 + e)
+            H, I = self.cfg.hidden_size, self.cfg.moe_intermediate_size
+            self._experts[e] = ((torch.randn(2 * I, H, generator=g) * 0.02).to(torch.bfloat16),
+                                (torch.randn(H, I, generator=g) * 0.02).to(torch.bfloat16))
+        return self._experts[e]
 
-    def timed(fn):
-        fn()
-        t0 = time.perf_counter()
-        fn()
-        return time.perf_counter() - t0
+    def sample(self) -> dict:
+        """Seconds of one layer of each kind and of 1/8 of the lm_head."""
+        import torch
+        import torch.nn.functional as Fn
+        from oracle import ref_torch as R
+        c, x = self.cfg, self.x
+        t = {}
+        with torch.inference_mode():
+            t0 = time.perf_counter()
+            R.gdn_layer(x, self.gdn_w, self.conv_hist, self.state, kh=c.linear_num_key_heads,
+                        vh=c.linear_num_value_heads, dk=c.linear_key_head_dim, dv=c.linear_value_head_dim)
+            t["gdn"] = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            R.attention_layer(x, self.attn_w, self.key, self.value, self.ctx, heads=c.num_attention_heads,
+                              kv_heads=c.num_key_value_heads, dim=c.head_dim, rot=c.rotary_dim, theta=c.rope_theta)
+            t["attn"] = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            R.moe_layer(x, self.moe_w, self._expert, top_k=c.num_experts_per_tok)
+            t["moe"] = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            Fn.linear(x[0], self.lm)
+            t["lm8"] = time.perf_counter() - t0
+        t["sample"] = sum(t.values())
+        t["step"] = 30 * t["gdn"] + 10 * t["attn"] + 40 * t["moe"] + 8 * t["lm8"]
+        return t
 
-    t_gdn = timed(lambda: model.gdn(x, a, gdn_cache))
-    t_att = timed(lambda: model.attention(x, t, kv, ctx))
-    t_moe = timed(lambda: model.moe(x, m))
-    t_lm = timed(lambda: x[0] @ lm.T) * 8
-    step = 30 * t_gdn + 10 * t_att + 40 * t_moe + t_lm
-    sample = (f"numpy restatement of the reference CPU path; one GDN layer {t_gdn*1e3:.1f} ms, one attention "
-              f"layer (ctx {ctx}) {t_att*1e3:.1f} ms, one MoE layer (16 tokens, top-8 of 256) {t_moe*1e3:.1f} ms, "
-              f"1/8 lm_head x8 {t_lm*1e3:.1f} ms; step = 30 GDN + 10 attn + 40 MoE + lm_head")
-    return step, sample
+    def describe(self, t: dict) -> str:
+        return (f"torch CPU restatement of the reference path (oracle/ref_torch.py), bf16 weights, "
+                f"{self.threads} threads; per sample one GDN layer {t['gdn']*1e3:.1f} ms, one attention layer "
+                f"(ctx {self.ctx}) {t['attn']*1e3:.1f} ms, one MoE layer (16 tokens, top-8 of 256 + shared) "
+                f"{t['moe']*1e3:.1f} ms, 1/8 lm_head {t['lm8']*1e3:.1f} ms; verify step extrapolated as "
+                f"30 GDN + 10 attention + 40 MoE + 8 x lm_head/8 = {t['step']*1e3:.0f} ms")
+
+
+def cpu_baseline_leg(samples: int = 5) -> dict:
+    """cpu_baseline of the GPU arm: best of ``samples`` after one warm-up sample."""
+    ref = CpuReference()
+    ref.sample()
+    best = min((ref.sample() for _ in range(samples)), key=lambda t: t["step"])
+    return {"value": round(16 / best["step"], 4), "unit": "tok/s", "cores": ref.threads, "kind": "port",
+            "sample": ref.describe(best) + f" (best of {samples} after 1 warm-up)"}
 
 
 # ---------------------------------------------------------------------------- GPU side
@@ -418,18 +443,30 @@ def time_moe_up(eng, cfg, dev, iters: int = 50):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the reference's CPU path on the host cores, rank 0 only (other
+    ranks exit without work).  Each of the W + K steps runs one sample (one layer of each
+    kind + 1/8 lm_head; about a tenth of a second); ms_per_step is the timed sample's
+    wall time, value the verify tok/s of the step extrapolated from the K samples'
+    medians."""
     if rank != 0:
         return None
-    cores = os.cpu_count() or 1
-    step_s, sample = cpu_reference_estimate()
-    value = 16 / step_s
+    ref = CpuReference(ctx=args.ctx)
+    for _ in range(args.warmup):
+        ref.sample()
+    runs = [ref.sample() for _ in range(args.steps)]
+    med = {key: statistics.median(r[key] for r in runs) for key in runs[0]}
+    med["step"] = 30 * med["gdn"] + 10 * med["attn"] + 40 * med["moe"] + 8 * med["lm8"]
+    value = 16 / med["step"]
+    desc = ref.describe(med) + f" (medians of {args.steps} samples after {args.warmup} warm-up samples)"
     return {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "full target verify forward (benchmark config 4)",
-                                            "block": 16, "ctx": args.ctx, "global_batch": 1},
-            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": sample},
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med["sample"] * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init bf16 weights N(0,0.02), seeded context)",
+            "config": {"workload": "full target verify forward (benchmark config 4), extrapolated per step "
+                                   "from one layer of each kind", "block": 16, "ctx": args.ctx, "global_batch": 1,
+                       "ms_per_verify_step_extrapolated": round(med["step"] * 1e3, 1)},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": ref.threads, "kind": "port",
+                             "sample": desc},
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -560,6 +597,12 @@ def main():
         os.environ["NCCL_DEBUG"] = "WARN"   # the version banner would go to stdout, ahead of the JSON line
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # the CPU reference needs no process group: rank 0 measures, the others exit
+        out = run_reference(args, rank, world)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
     if world > 1:
         import datetime
         import torch
@@ -568,14 +611,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.impl == "reference":
-            out = run_reference(args, rank, world)
-        else:
-            out = run_ours(args, rank, world, local_rank)
-            if out is not None and world == 1 and not args.no_cpu_baseline:
-                step_s, sample = cpu_reference_estimate()
-                out["cpu_baseline"] = {"value": round(16 / step_s, 4), "unit": "tok/s", "cores": os.cpu_count(),
-                                       "kind": "port", "sample": sample}
+        out = run_ours(args, rank, world, local_rank)
+        if out is not None and world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline_leg()
         if out is not None:
             print(json.dumps(out), flush=True)
     finally:
