@@ -22,12 +22,15 @@ cpu_baseline / --impl reference
           one GDN layer, one attention layer and one MoE layer at the same shapes and 1/8
           of the lm_head per sample, a verify step extrapolated as 30*GDN + 10*attention +
           40*MoE + 8*(lm_head/8); the reference arm runs one sample per step.
-Multi-GPU (torchrun): every rank runs an independent replica of the same workload
-(requests are data-parallel); value sums the ranks ("scaling": "weak").
+Multi-GPU (torchrun): expert parallelism -- every rank serves its own requests (the
+same per-GPU workload as one GPU, "scaling": "weak") and holds E/N of the routed experts
+of every MoE layer; rows go to their experts' ranks and back by kernel stores into the
+peers' windows (NVLink), value sums the ranks.  --replicas runs independent replicas.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -41,10 +44,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "verify tok/s & step latency (block 16, W4 MoE+GDN); % HBM roofline"
 
-# DRAM bytes (read + write) of one moe_up_bulk_kernel launch from an ncu capture of the
-# same routing (16 tokens of N(0,1) router logits, seed 17 -> 103 active experts):
-# profiles/moe_up_bulk_T16.md
-MOE_UP_NCU_TRAFFIC = {"bytes": 112_579_584 + 3_767_552, "active": 103, "profile": "profiles/moe_up_bulk_T16.md"}
+# DRAM bytes (read + write) of one moe_up_bulk_kernel launch, from one ncu capture of the
+# same launch (16 tokens of N(0,1) router logits, seed 17 -> 103 active experts; metrics
+# dram__bytes_read.sum + dram__bytes_write.sum): ncu cannot run inside the timed bench
+MOE_UP_NCU_TRAFFIC = {"bytes": 112_579_584 + 3_767_552, "active": 103,
+                      "source": "ncu capture of moe_up_bulk_kernel on the bench routing (103 active experts), "
+                                "dram__bytes_read.sum + dram__bytes_write.sum"}
 
 
 def _peaks():
@@ -264,9 +269,9 @@ def run_ours(args, rank, world, local_rank):
     capacity = (capacity + 15) // 16 * 16
     t_init = time.perf_counter()
     weights = E.weights_random(cfg, seed=2, device=dev)
-    ep = args.ep and world > 1
+    ep = world > 1 and not args.replicas
     eng = E.TargetEngine(cfg, weights, batch=B, block=S, capacity=capacity, device=dev,
-                         ep_group=dist.group.WORLD if ep else None, ep_overlap_shared=not args.ep_serial)
+                         ep_group=dist.group.WORLD if ep else None)
     eng.set_random_context(args.ctx, seed=3 + rank)
     torch.cuda.synchronize(dev)
     init_s = time.perf_counter() - t_init
@@ -306,6 +311,7 @@ def run_ours(args, rank, world, local_rank):
             print_timeline(prof)
         if world > 1:
             dist.barrier()
+        eng.close()
         return None
     if args.profile_step:
         # one step between cudaProfilerStart/Stop (ncu --profile-from-start off)
@@ -313,6 +319,7 @@ def run_ours(args, rank, world, local_rank):
         step(args.warmup)
         torch.cuda.synchronize(dev)
         torch.cuda.profiler.stop()
+        eng.close()
         return None
     if world > 1:
         dist.barrier()
@@ -380,8 +387,9 @@ def run_ours(args, rank, world, local_rank):
                                    "full target verify forward, 1 GPU per replica (benchmark config 4)",
                        "model": "Qwen3.5-35B-A3B target (40 layers: 30 GDN + 10 attention)",
                        "global_batch": B * world, "block": S, "ctx": args.ctx, "seq_len": args.ctx + S,
-                       "parallelism": (f"ep{world} (experts {cfg.num_experts // world} per GPU, all-to-all "
-                                       "dispatch/combine; attention/GDN per request)") if ep else
+                       "parallelism": (f"ep{world} (experts {cfg.num_experts // world} per GPU; dispatch and "
+                                       "combine by kernel stores into the peers' windows over NVLink; "
+                                       "attention/GDN per request)") if ep else
                                       f"dp{world} (independent replicas)",
                        "l2": "no flush: each step streams ~8.5 GB of weights, far above the 126 MB L2",
                        "step_alg_bytes": alg["total"], "alg_bytes_parts": alg,
@@ -397,11 +405,12 @@ def run_ours(args, rank, world, local_rank):
                          "achieved": round(rl_achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(rl_achieved / hbm, 4), "peak_kind": f"{peak_kind} burst copy",
                          "traffic": MOE_UP_NCU_TRAFFIC["bytes"] if rl["active"] == MOE_UP_NCU_TRAFFIC["active"] else None,
-                         "traffic_source": MOE_UP_NCU_TRAFFIC["profile"],
+                         "traffic_source": MOE_UP_NCU_TRAFFIC["source"],
                          "bytes_per_launch": rl["bytes"], "us_per_launch": round(rl["us"], 2),
                          "active_experts": rl["active"]},
             "clocks": clocks.summary(),
         }
+    eng.close()
     return result
 
 
@@ -436,7 +445,8 @@ def time_moe_up(eng, cfg, dev, iters: int = 50):
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1) * 1e3)
-    active = eng.active_experts()
+    off = so.qw_moe_active_experts(None, T, E, k)
+    active = int(ws[off:off + 4].view(torch.int32).item())
     w4b = 2 * I * H // 2 + 2 * I * (H // g) * 2
     nbytes = (active + 1) * w4b + T * H * 2 + (T * k + T) * I * 2
     return {"us": statistics.median(times), "bytes": nbytes, "active": active}
@@ -564,6 +574,121 @@ def run_kernels(args):
     print(json.dumps(out), flush=True)
 
 
+def _event_times(fn, reps: int, flush) -> float:
+    """Median CUDA-event time (us) of fn() over reps launches, L2 flushed before each."""
+    import torch
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    return statistics.median(times)
+
+
+def run_micro(args):
+    """Benchmark configs 2 and 3 (one JSON line per point): the W4A16 grouped MoE
+    (router logits given, softmax top-8 + shared expert, H 2048, 256 experts, I 512, g128,
+    scales U(0.005, 0.02)) at T = 16, 64, 256 -- routing + experts + combine -- and the
+    gated-DeltaNet verify at B = 1, 8, 32 (16 QK / 32 V heads of 128, block 16) -- verify
+    + commit of all 16 tokens.  CUDA events around each launch group, L2 flushed (256 MB
+    write) before each; achieved = algorithmic bytes / time against the measured HBM
+    copy bandwidth."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from qwen35_dflash_b200 import lib, w4
+    hbm, peak_kind = _peaks()
+    so = lib.load()
+    dev = torch.device("cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    lines = []
+    # ---- config 2
+    H, E, k, I, g = 2048, 256, 8, 512, 128
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def bank(n, kk, experts):
+        q = torch.randint(-8, 8, (experts, n, kk), dtype=torch.int8, device=dev, generator=gen)
+        sc = (torch.rand(experts, n, kk // g, device=dev, generator=gen) * 0.015 + 0.005).to(torch.bfloat16)
+        return w4.pack_w4(q, sc, g)
+
+    gu, dn = bank(2 * I, H, E), bank(H, I, E)
+    sgu, sdn = bank(2 * I, H, 1), bank(H, I, 1)
+    w4b = lambda n, kk: n * kk // 2 + n * (kk // g) * 2   # noqa: E731
+    per_expert = w4b(2 * I, H) + w4b(H, I)
+    for T in (16, 64, 256):
+        x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
+        logits = torch.randn(T, E + 1, device=dev, generator=gen).to(torch.bfloat16)
+        ws = torch.zeros(so.qw_moe_workspace_bytes(T, H, E, I, k), dtype=torch.uint8, device=dev)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+
+        def moe():
+            lib.check(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, E + 1, T, E, k, E, lib.QW_BF16, ws.data_ptr(), st))
+            lib.check(so.qw_moe_experts_w4(x.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(), sdn.data_ptr(),
+                                           T, H, E, I, k, g, ws.data_ptr(), st))
+            lib.check(so.qw_moe_combine(ws.data_ptr(), out.data_ptr(), 0, T, H, E, I, k, 1, st))
+
+        moe()
+        torch.cuda.synchronize()
+        off = so.qw_moe_active_experts(None, T, E, k)
+        active = int(ws[off:off + 4].view(torch.int32).item())
+        us = _event_times(moe, args.kernel_reps, flush)
+        nbytes = (active + 1) * per_expert + T * H * 2 * 2 + T * (E + 1) * 2
+        lines.append({"config": "2: W4A16 grouped MoE (route + experts + combine)", "tokens": T,
+                      "active_experts": active, "us": round(us, 2), "alg_bytes": nbytes,
+                      "achieved_gbs": round(nbytes / us / 1e3, 1), "peak_gbs": hbm,
+                      "frac": round(nbytes / us / 1e3 / hbm, 4), "peak_kind": f"{peak_kind} burst copy",
+                      "tflops": round(2 * T * 9 * 3 * I * H / us / 1e6, 2)})
+    del gu, dn
+    # ---- config 3
+    kh, vh, d, S = 16, 32, 128, 16
+    kw, vw = kh * d, vh * d
+    C = 2 * kw + vw
+    ldp = C + vw
+    for B in (1, 8, 32):
+        proj = torch.randn(B * S, ldp, device=dev, generator=gen).to(torch.bfloat16)
+        ab = torch.randn(B * S, 2 * vh, device=dev, generator=gen)
+        hist = torch.randn(B, C, 3, device=dev, generator=gen).to(torch.bfloat16)
+        conv_w = (torch.randn(C, 4, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        a_log = torch.log(torch.arange(1, vh + 1, dtype=torch.float32, device=dev))
+        dt_bias = torch.randn(vh, device=dev, generator=gen) * 0.5
+        norm_w = torch.ones(d, device=dev).to(torch.bfloat16)
+        state = torch.randn(B, vh, d, d, device=dev, generator=gen) * 0.02
+        outp = torch.zeros(B * S, vw, dtype=torch.bfloat16, device=dev)
+        slots = torch.arange(B, dtype=torch.int32, device=dev)
+        accepted = torch.full((B,), S, dtype=torch.int32, device=dev)
+        layer = (lib.GdnLayer * 1)()
+        layer[0] = lib.GdnLayer(proj.data_ptr(), ab.data_ptr(), hist.data_ptr(), conv_w.data_ptr(), a_log.data_ptr(),
+                                dt_bias.data_ptr(), norm_w.data_ptr(), state.data_ptr(), outp.data_ptr())
+        desc = torch.frombuffer(bytearray(bytes(memoryview(layer).cast("B"))), dtype=torch.uint8).to(dev)
+        dims = lib.GdnDims(B, S, kh, vh, d, d, C, 4, ldp, 1e-6, slots.data_ptr(), accepted.data_ptr())
+
+        def gdn_verify():
+            lib.check(so.qw_gdn_verify(ctypes.byref(dims), desc.data_ptr(), 0, st))
+
+        def gdn_both():
+            lib.check(so.qw_gdn_verify(ctypes.byref(dims), desc.data_ptr(), 0, st))
+            lib.check(so.qw_gdn_commit(ctypes.byref(dims), desc.data_ptr(), 1, st))
+
+        gdn_both()
+        torch.cuda.synchronize()
+        us_v = _event_times(gdn_verify, args.kernel_reps, flush)
+        us_b = _event_times(gdn_both, args.kernel_reps, flush)
+        seq_alg = 2 * 2 * vh * d * d + S * C * 2 + 2 * C * 3 * 2 + S * 2 * vh * 4 + 3 * S * vw * 2
+        moved = (3 * vh * d * d * 4 + S * ldp * 2 + S * 2 * vh * 4 + 2 * C * 3 * 2 + S * vw * 2)
+        lines.append({"config": "3: gated-DeltaNet verify + commit (block 16)", "batch": B,
+                      "us_verify": round(us_v, 2), "us_verify_commit": round(us_b, 2),
+                      "alg_bytes": B * seq_alg, "bytes_moved": B * moved,
+                      "achieved_gbs": round(B * seq_alg / us_b / 1e3, 1), "peak_gbs": hbm,
+                      "frac": round(B * seq_alg / us_b / 1e3 / hbm, 4), "peak_kind": f"{peak_kind} burst copy"})
+    for line in lines:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -572,11 +697,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--ep", action="store_true",
-                    help="with --gpus > 1: shard the routed experts over the GPUs (all-to-all dispatch/combine) "
-                         "instead of running independent replicas")
-    ap.add_argument("--ep-serial", action="store_true",
-                    help="with --ep: run the shared expert before the dispatch all-to-all instead of beside it")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with --gpus > 1: run independent replicas instead of sharding the routed experts")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--timeline", action="store_true",
@@ -586,9 +708,15 @@ def main():
     ap.add_argument("--kernels", action="store_true",
                     help="per-kernel timings on a 4-layer model of the full width (the small case for ncu)")
     ap.add_argument("--kernel-reps", type=int, default=5)
+    ap.add_argument("--micro", action="store_true",
+                    help="benchmark configs 2 (W4A16 MoE, T 16/64/256) and 3 (GDN verify, B 1/8/32), one line each")
     args = ap.parse_args()
     if args.kernels:
         run_kernels(args)
+        return
+    if args.micro:
+        args.kernel_reps = max(args.kernel_reps, 20)
+        run_micro(args)
         return
     if args.warmup < 3:
         args.warmup = 3

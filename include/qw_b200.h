@@ -232,36 +232,56 @@ int qw_moe_experts_w4_range(const void* x, const void* gate_up, const void* down
                             void* stream);
 
 /* ------------------------------------------------------------------------------
- * Expert parallelism (experts [g E/G, (g+1) E/G) on rank g; dispatch and combine by
- * the host's all-to-all of fixed segments): the source rank packs each routed
- * (token, slot) pair's row for its expert's rank (qw_moe_ep_pack into send segments
- * bf16 [ranks][cap + 1][hidden]: row 0 of a segment is its header of int32 words
- * [count, (pair << 8) | local expert, ...], rows 1.. the pairs' rows; cap >=
- * tokens * top_k and (cap + 1) * 4 <= hidden * 2); after the all-to-all the receiving
- * rank routes the ranks * (cap + 1) rows of its received segments as they lie (header
- * rows and rows past a segment's count invalid) and builds its expert lists
- * (qw_moe_ep_recv_route into a workspace of qw_moe_ep_recv_workspace_bytes), runs its
- * experts over them (qw_moe_ep_experts: top_k 1, no shared expert; the lists are not
- * rebuilt), packs the outputs into return segments of the same layout
- * (qw_moe_ep_pack_out), and after the all-to-all
- * back qw_moe_ep_scatter writes them into the source routing's per-(token, slot)
- * outputs for qw_moe_combine(_norm).  Bit-identical to the one-GPU MoE.  No counterpart
- * in the reference (its plan for multi-GPU serving).
+ * Expert parallelism: experts [g E/G, (g+1) E/G) live on rank g (one process per GPU);
+ * attention, GDN and the shared expert stay with each rank's own requests.  The
+ * reference shards the routed MoE of reference/fused_ops.py:148-173 (its quantised
+ * chain model/qwen35_moe_dflash/fused/quantization.py:181-202) this way in its serving
+ * plan; it has no multi-GPU code, so these entry points have no direct counterpart.
+ *
+ * The exchange is device-initiated over NVLink: each rank allocates one window of
+ * qw_ep_window_bytes (qw_ep_window_alloc, which also returns its 64-byte IPC handle),
+ * the ranks swap handles on the host once, and each maps its peers' windows
+ * (qw_ep_window_open).  `peers` is then a device array of `ranks` uint64 window
+ * addresses, this rank's own window at index `rank`.  Per MoE layer, after routing the
+ * rank's `tokens` over all experts (qw_moe_route / qw_moe_route_x into `workspace`):
+ *   qw_moe_ep_dispatch    each routed (token, slot) pair's row into its expert owner's
+ *                         window (peer stores), then a release flag in every window;
+ *   qw_moe_ep_recv_route  waits (bounded) for every rank's dispatch, routes the rows it
+ *                         received (top-1 = their local expert) into a workspace of
+ *                         qw_moe_ep_recv_workspace_bytes;
+ *   qw_moe_ep_experts     this rank's experts over those rows (gate_up_local /
+ *                         down_local: the streams of its experts only);
+ *   qw_moe_ep_combine     the outputs as bf16 into their source ranks' windows, then a
+ *                         release flag in every window;
+ *   qw_moe_ep_scatter     waits (bounded) for every rank's combine, writes the returned
+ *                         rows into the routing's per-(token, slot) outputs for
+ *                         qw_moe_combine(_norm), and closes the exchange.
+ * cap = tokens * top_k (every rank the same tokens).  Every rank issues the same calls in
+ * the same order; calls are stream-ordered (graph-capturable), and the results equal
+ * the one-GPU MoE bit for bit.  A wait that expires (a lost peer) records
+ * QW_ERR_TIMEOUT for qw_wait_status / qw_check_wait_status.
  * ---------------------------------------------------------------------------- */
+int64_t qw_ep_window_bytes(int64_t ranks, int64_t cap, int64_t hidden);
+/* The window's allocation (cudaMalloc, zeroed) and IPC handle: the only allocating
+ * calls of the library, made once per engine. */
+int qw_ep_window_alloc(int64_t bytes, void** window, void* ipc_handle);
+int qw_ep_window_open(const void* ipc_handle, void** peer_window);
+int qw_ep_window_close(void* peer_window);
+int qw_ep_window_free(void* window);
 int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                                        int64_t inter);
-int qw_moe_ep_pack(const void* workspace, const void* x, int64_t tokens, int64_t hidden, int64_t experts,
-                   int64_t top_k, int64_t ranks, int64_t cap, void* send_seg, void* stream);
-int qw_moe_ep_recv_route(const void* recv_seg, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+int qw_moe_ep_dispatch(const void* workspace, const void* x, int64_t tokens, int64_t hidden,
+                       int64_t experts, int64_t top_k, int64_t ranks, int64_t rank, int64_t cap,
+                       const void* peers, void* window, void* stream);
+int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                          void* recv_workspace, void* stream);
-int qw_moe_ep_experts(const void* recv_seg, const void* gate_up_local, const void* down_local, int64_t ranks,
-                      int64_t cap, int64_t hidden, int64_t experts, int64_t inter, int32_t group,
-                      void* recv_workspace, void* stream);
-int qw_moe_ep_pack_out(const void* recv_workspace, const void* recv_seg, int64_t ranks, int64_t cap,
-                       int64_t hidden, int64_t experts, int64_t inter, void* send_back, void* stream);
-int qw_moe_ep_scatter(void* workspace, const void* recv_back, int64_t tokens, int64_t hidden,
-                      int64_t experts, int64_t inter, int64_t top_k, int64_t ranks, int64_t cap,
-                      void* stream);
+int qw_moe_ep_experts(const void* window, const void* gate_up_local, const void* down_local,
+                      int64_t ranks, int64_t cap, int64_t hidden, int64_t experts, int64_t inter,
+                      int32_t group, void* recv_workspace, void* stream);
+int qw_moe_ep_combine(const void* recv_workspace, void* window, int64_t ranks, int64_t rank, int64_t cap,
+                      int64_t hidden, int64_t experts, int64_t inter, const void* peers, void* stream);
+int qw_moe_ep_scatter(void* workspace, void* window, int64_t tokens, int64_t hidden, int64_t experts,
+                      int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, void* stream);
 
 /* Byte offset, inside a MoE workspace, of the int32 count of active routed experts
  * (valid after qw_moe_route_lists or an expert entry point; for measuring the experts

@@ -2,72 +2,68 @@
 ``oracle/__init__.py``).
 
 The reference plans multi-GPU serving with the routed experts sharded over the GPUs
-(rank g owns experts [g E/G, (g+1) E/G)) and dispatch/combine by all-to-all (its
-serving plan; there is no multi-GPU code in the reference to pin against, so this is
-the protocol the CUDA kernels of ``qw_moe_ep_*`` implement, stated plainly):
+(rank g owns experts [g E/G, (g+1) E/G)) and dispatch/combine between them (its serving
+plan; there is no multi-GPU code in the reference to pin against, so this is the
+protocol the ``qw_moe_ep_*`` kernels implement, stated plainly):
 
-* pack: pair p = t * k + s (token t, slot s) of expert e goes to rank d = e // (E/G),
-  at position = number of earlier pairs for d; segment d of the send buffer is cap + 1
-  rows [cap + 1, H]: row 0 the header, int32 words [count, (p << 8) | (e - d E/G), ...]
-  laid into the row's bytes, row 1 + position the pair's activation row;
-* the receiving rank runs local expert ``word & 0xFF`` on each received pair row;
-* the outputs return in the same rows of segments of the same layout and land in slot
-  (t, s).
+* dispatch: pair p = t * k + s (token t, slot s) of expert e goes to rank d = e // (E/G),
+  at position = number of earlier pairs for d; the source g writes, into d's window,
+  rows[g][position] = x[t] and meta[g][position] = (p << 8) | (e - d E/G), and
+  count[g] = its number of pairs for d;
+* the receiving rank takes the valid rows source by source (rows [s][0, count[s])) and
+  runs local expert ``meta & 0xFF`` on each;
+* combine: the output of received row (s, j) goes to source s's ``back`` row
+  ``meta[s][j] >> 8`` (its own pair index); the source's pair p output lands in slot
+  (p // k, p % k).
 """
 from __future__ import annotations
 
 import numpy as np
 
 
-def header_words(seg: np.ndarray, cap: int) -> np.ndarray:
-    """int32 header words [ranks, cap + 1] of 16-bit segments [ranks, cap + 1, H]."""
-    head = np.ascontiguousarray(seg[:, 0])
-    return head.view(np.int32)[:, : cap + 1]
-
-
-def pack(topk: np.ndarray, x16: np.ndarray, experts: int, ranks: int, cap: int) -> np.ndarray:
-    """topk int [T, k], x16 16-bit rows [T, H] (bf16 bits as uint16) -> send segments
-    uint16 [ranks, cap + 1, H]."""
+def dispatch(topk: np.ndarray, x16: np.ndarray, experts: int, ranks: int):
+    """topk int [T, k], x16 16-bit rows [T, H] -> per destination d the block this source
+    writes into d's window: (rows uint16 [cap, H], meta int32 [cap], count), cap = T k."""
     T, k = topk.shape
     H = x16.shape[1]
-    if (cap + 1) * 2 > H:
-        raise ValueError("the header does not fit in one row")
+    cap = T * k
     el = experts // ranks
-    seg = np.zeros((ranks, cap + 1, H), np.uint16)
-    words = np.zeros((ranks, cap + 1), np.int32)
+    rows = np.zeros((ranks, cap, H), np.uint16)
+    meta = np.zeros((ranks, cap), np.int32)
+    count = np.zeros(ranks, np.int64)
     for p in range(T * k):
         e = int(topk.flat[p])
         d = e // el
-        pos = int(words[d, 0])
-        if pos >= cap:
-            raise ValueError("segment overflow")
-        seg[d, 1 + pos] = x16[p // k]
-        words[d, 1 + pos] = (p << 8) | (e - d * el)
-        words[d, 0] += 1
-    seg[:, 0, : 2 * (cap + 1)] = words.view(np.uint16).reshape(ranks, 2 * (cap + 1))
-    return seg
+        pos = int(count[d])
+        rows[d, pos] = x16[p // k]
+        meta[d, pos] = (p << 8) | (e - d * el)
+        count[d] += 1
+    return [(rows[d], meta[d], int(count[d])) for d in range(ranks)]
 
 
-def recv_experts(seg: np.ndarray, cap: int) -> np.ndarray:
-    """Local expert of every received row, rows taken as they lie (-1 for the header rows
-    and past each segment's count): [ranks * (cap + 1)]."""
-    words = header_words(seg, cap)
-    ranks = seg.shape[0]
-    out = np.full((ranks, cap + 1), -1, np.int64)
-    for g in range(ranks):
-        n = int(words[g, 0])
-        out[g, 1:1 + n] = words[g, 1:1 + n] & 0xFF
-    return out.reshape(-1)
-
-
-def scatter(topk: np.ndarray, back: np.ndarray, experts: int, ranks: int) -> np.ndarray:
-    """Returned output segments [ranks, cap + 1, H] -> per-(token, slot) outputs [T, k, H]."""
-    T, k = topk.shape
-    el = experts // ranks
-    out = np.zeros((T, k, back.shape[2]), back.dtype)
-    filled = np.zeros(ranks, np.int64)
-    for p in range(T * k):
-        d = int(topk.flat[p]) // el
-        out[p // k, p % k] = back[d, 1 + filled[d]]
-        filled[d] += 1
+def received(blocks) -> list[tuple[int, int, int]]:
+    """The blocks a rank received, one per source s (rows, meta, count), as its valid rows
+    in order: (source, row j, local expert)."""
+    out = []
+    for s, (_, meta, count) in enumerate(blocks):
+        for j in range(count):
+            out.append((s, j, int(meta[j]) & 0xFF))
     return out
+
+
+def combine(blocks, outputs: dict, cap: int, H: int, dtype=np.uint16):
+    """Received rows' outputs {(s, j): row} -> per source s the rows written into its
+    ``back`` array [cap, H] (at the source's pair index) and the mask of rows written."""
+    ranks = len(blocks)
+    back = np.zeros((ranks, cap, H), dtype)
+    written = np.zeros((ranks, cap), bool)
+    for (s, j), row in outputs.items():
+        pair = int(blocks[s][1][j]) >> 8
+        back[s, pair] = row
+        written[s, pair] = True
+    return back, written
+
+
+def scatter(back: np.ndarray, T: int, k: int) -> np.ndarray:
+    """The source's ``back`` [cap, H] -> per-(token, slot) outputs [T, k, H]."""
+    return back[: T * k].reshape(T, k, back.shape[-1])

@@ -26,6 +26,7 @@
 // heap fallback) run on lane 0.  Values compared are the bf16 router logits, which
 // order exactly as torch's fp32 probabilities (exp is monotone; equal logits give
 // equal probabilities).
+#include <cstring>
 #include <mutex>
 
 #include "bulk_ring.cuh"
@@ -1660,7 +1661,7 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   QW_CHECK_ARG(expert_lo >= 0 && expert_lo + expert_count <= experts, "moe_experts: expert range outside [0, experts)");
   QW_CHECK_ARG((shared_gate_up == nullptr) == (shared_down == nullptr), "moe_experts: shared expert pointers");
   QW_CHECK_ARG(group == 32 || group == 64 || group == 128, "moe_experts: group must be 32, 64 or 128");
-  QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && hidden % group == 0 && inter % group == 0 && inter % 16 == 0 &&
+  QW_CHECK_ARG(tokens >= 1 && tokens <= 65536 && hidden % group == 0 && inter % group == 0 && inter % 16 == 0 &&
                    hidden % 16 == 0 && top_k >= 1 && top_k <= 16 && experts >= top_k,
                "moe_experts: invalid shape");
   const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
@@ -1855,15 +1856,112 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
 // its own tokens over all E experts, sends every (token, slot) pair's activation row to
 // the owning rank, each rank runs its local experts on the rows it received, and the
 // results come back to the source rank's per-(token, slot) outputs, where the usual
-// combine reads them.  The exchanges are two all-to-alls of fixed-size segments (cap
-// rows per destination, cap >= tokens * top_k so nothing can overflow), made by the
-// host's collective library between these kernels.  Every expert output is computed by
-// the same kernels as on one GPU (they give a row the same bits whatever else is in the
-// launch) and crosses ranks as bf16, the precision the combine reads it at, so the
-// result is bit-identical to the single-GPU MoE.
+// combine reads them.
+//
+// The exchange is device-initiated over NVLink: every rank holds one window (a device
+// allocation that every peer has mapped, qw_ep_window_*), and the kernels store straight
+// into the peers' windows -- rows and their descriptors on dispatch, results on
+// combine -- then raise a flag in each peer's window with a system-scope release; the
+// consumer's kernel waits (bounded) on the flags in its own window with acquire loads.
+// Only the routed rows travel (no fixed-size segments), there is no host round trip
+// and no collective library on the data path, and the kernels are stream-ordered, so a
+// whole verify step with its exchanges replays as one CUDA graph.  No TMA and no
+// multicast touches peer memory: plain 16-byte stores from SM threads.
+//
+// Window of rank g (identical layout on every rank):
+//   hdr   int32[64]   [0] epoch of the last finished exchange, [1..3] CTA tickets of the
+//                     dispatch / combine / scatter kernels, [4] broken (a wait expired)
+//   dflag int32[64]   dflag[s] = epoch of source s's last dispatch to g
+//   cflag int32[64]   cflag[d] = epoch of destination d's last combine back to g
+//   count int32[64]   count[s] = rows source s sent to g in its last dispatch
+//   meta  int32[G][cap]       (source pair index << 8) | local expert, per received row
+//   rows  bf16 [G][cap][H]    received rows (source s at rows [s][0, count[s]))
+//   back  bf16 [cap][H]       this rank's own pairs' expert outputs (pair p at row p)
+// Ordering: a rank's scatter of exchange n waits for every peer's combine of n, so its
+// dispatch of n + 1 cannot overwrite a window region a peer is still reading.
+//
+// Every expert output is computed by the same kernels as on one GPU (they give a row the
+// same bits whatever else is in the launch) and crosses ranks as bf16, the precision
+// the combine reads it at, so the result is bit-identical to the single-GPU MoE.
 namespace qw {
 
-// Position of pair p in its destination's segment: the earlier pairs with the same
+constexpr int EP_MAX_RANKS = 64;
+constexpr long long EP_PEER_WAIT_LIMIT = 1ll << 34;   // cycles (~9 s): a peer's host may lag in eager use
+
+struct EpWin {
+  int32_t* hdr;
+  int32_t* dflag;
+  int32_t* cflag;
+  int32_t* count;
+  int32_t* meta;
+  __nv_bfloat16* rows;
+  __nv_bfloat16* back;
+};
+
+__host__ __device__ inline int64_t ep_window_bytes(int G, int cap, int H) {
+  int64_t off = 1024;
+  off += align256(static_cast<int64_t>(G) * cap * 4);
+  off += align256(static_cast<int64_t>(G) * cap * H * 2);
+  off += align256(static_cast<int64_t>(cap) * H * 2);
+  return off;
+}
+
+__host__ __device__ inline EpWin ep_win(const void* base, int G, int cap, int H) {
+  uint8_t* p = static_cast<uint8_t*>(const_cast<void*>(base));
+  EpWin w;
+  w.hdr = reinterpret_cast<int32_t*>(p);
+  w.dflag = reinterpret_cast<int32_t*>(p + 256);
+  w.cflag = w.dflag + EP_MAX_RANKS;
+  w.count = w.cflag + EP_MAX_RANKS;
+  int64_t off = 1024;
+  w.meta = reinterpret_cast<int32_t*>(p + off);
+  off += align256(static_cast<int64_t>(G) * cap * 4);
+  w.rows = reinterpret_cast<__nv_bfloat16*>(p + off);
+  off += align256(static_cast<int64_t>(G) * cap * H * 2);
+  w.back = reinterpret_cast<__nv_bfloat16*>(p + off);
+  return w;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait (one thread) until a peer has raised *flag to `want`.  On expiry -- or
+// when an earlier wait of this window expired (hdr[4]) -- records the timeout in the
+// sticky status and returns false, so a lost peer costs one limit, not one per wait.
+__device__ bool ep_wait_flag(const int32_t* flag, int want, int32_t* hdr) {
+  if (ld_acquire_sys(flag) >= want) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_sys(flag) < want) {
+    if (*reinterpret_cast<volatile int32_t*>(hdr + 4) != 0 || clock64() - t0 > EP_PEER_WAIT_LIMIT) {
+      atomicOr(&g_moe_wait_status, QW_DEVICE_TIMEOUT);
+      *reinterpret_cast<volatile int32_t*>(hdr + 4) = 1;
+      return false;
+    }
+    __nanosleep(100);
+  }
+  return true;
+}
+
+// The CTA that finishes last (ticket wraps to 0 for the next launch): every thread
+// fences its own stores at system scope first.
+__device__ __forceinline__ bool ep_last_cta(int32_t* ticket) {
+  __shared__ int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    s_last = atomicInc(reinterpret_cast<unsigned*>(ticket), gridDim.x - 1) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last) __threadfence_system();
+  return s_last != 0;
+}
+
+// Position of pair p in its destination's rows: the earlier pairs with the same
 // destination, counted by the whole CTA (every thread calls it with the same p).
 __device__ __forceinline__ int ep_pos(const int32_t* idx, int p, int d, int el) {
   int pos = 0;
@@ -1874,172 +1972,258 @@ __device__ __forceinline__ int ep_pos(const int32_t* idx, int p, int d, int el) 
   return pos;
 }
 
-// Segment g of the send buffer: cap + 1 rows of hidden bf16; row 0 is the header
-// (int32 words: [count, (pair << 8) | local expert, ...]), rows 1 .. the pairs' rows.
-// One CTA per pair writes its row and header word; CTA 0 also writes the counts.
-__global__ void ep_pack_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ x, int T, int H,
-                               int k, int G, int el, int cap, __nv_bfloat16* __restrict__ seg) {
+// Dispatch (source rank): one CTA per routed pair stores its token's row and descriptor
+// into the owner's window; the last CTA stores the per-destination counts and raises
+// this rank's dispatch flag in every window (all ranks, rows or not).
+__global__ void ep_dispatch_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ x, int T, int H,
+                                   int k, int G, int rank, int el, int cap, const unsigned long long* __restrict__ peers,
+                                   void* own) {
   pdl_wait();
   pdl_trigger();
+  const EpWin me = ep_win(own, G, cap, H);
+  const int epoch = me.hdr[0] + 1;
   const int np = T * k;
-  const int64_t segw = static_cast<int64_t>(cap + 1) * H;   // elements per segment
-  if (blockIdx.x == 0) {
-    for (int g = 0; g < G; ++g) {
-      int c = 0;
-      for (int q0 = 0; q0 < np; q0 += blockDim.x) {
-        const int q = q0 + threadIdx.x;
-        c += __syncthreads_count(q < np && idx[q] / el == g);
-      }
-      if (threadIdx.x == 0) reinterpret_cast<int32_t*>(seg + g * segw)[0] = c;
-    }
-  }
   const int p = blockIdx.x;
-  if (p >= np) return;
   const int d = idx[p] / el;
   const int pos = ep_pos(idx, p, d, el);
-  if (threadIdx.x == 0) reinterpret_cast<int32_t*>(seg + d * segw)[1 + pos] = (p << 8) | (idx[p] - d * el);
+  const EpWin dst = ep_win(reinterpret_cast<const void*>(peers[d]), G, cap, H);
+  if (threadIdx.x == 0) dst.meta[rank * cap + pos] = (p << 8) | (idx[p] - d * el);
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(p / k) * H);
-  uint4* dst = reinterpret_cast<uint4*>(seg + d * segw + static_cast<int64_t>(1 + pos) * H);
-  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+  uint4* out = reinterpret_cast<uint4*>(dst.rows + (static_cast<int64_t>(rank) * cap + pos) * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) out[i] = src[i];
+  if (!ep_last_cta(me.hdr + 1)) return;
+  for (int g = 0; g < G; ++g) {
+    int c = 0;
+    for (int q0 = 0; q0 < np; q0 += blockDim.x) {
+      const int q = q0 + threadIdx.x;
+      c += __syncthreads_count(q < np && idx[q] / el == g);
+    }
+    if (threadIdx.x == 0) ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).count[rank] = c;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < G)
+    st_release_sys(ep_win(reinterpret_cast<const void*>(peers[threadIdx.x]), G, cap, H).dflag + rank, epoch);
 }
 
-// The receiving rank's routing of the G (cap + 1) rows of its received segments, taken
-// as they lie (row r = segment r / (cap + 1), row r % (cap + 1) of it): top-1 = the
-// row's local expert; the header rows and the rows past each segment's count are
-// invalid (left out by the expert kernels).  Then, as qw_moe_route_lists, the expert
-// lists.  One CTA.  Dynamic smem: 3 el + 64 ints.
-__global__ void __launch_bounds__(1024) ep_recv_route_kernel(const __nv_bfloat16* __restrict__ seg, int G, int cap,
-                                                             int H, int el, void* ws) {
+// Receiving rank: wait for every source's dispatch, then route the received rows
+// (top-1 = the row's local expert, weight 1) and build the expert lists over the valid
+// rows only (compacted), with each list entry naming the row's place in the window.
+// One CTA; dynamic smem: 3 el + 64 ints.
+__global__ void __launch_bounds__(1024) ep_recv_route_kernel(void* own, int G, int cap, int H, int el, void* ws) {
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int s_cnt[EP_MAX_RANKS], s_off[EP_MAX_RANKS + 1];
   pdl_wait();
   pdl_trigger();
-  const int T = G * (cap + 1);
-  const int64_t segw = static_cast<int64_t>(cap + 1) * H;
-  const RouteView rv = route_view(ws, T, el, 1);
-  for (int r = threadIdx.x; r < T; r += blockDim.x) {
-    const int32_t* m = reinterpret_cast<const int32_t*>(seg + (r / (cap + 1)) * segw);
-    const int j = r % (cap + 1) - 1;
-    rv.topk_idx[r] = j >= 0 && j < m[0] ? (m[1 + j] & 0xFF) : -1;
-    rv.topk_w[r] = 1.f;
-    rv.shared_gate[r] = 0.f;
+  const EpWin me = ep_win(own, G, cap, H);
+  const int epoch = me.hdr[0] + 1;
+  if (threadIdx.x < G) {
+    const bool ok = ep_wait_flag(me.dflag + threadIdx.x, epoch, me.hdr);
+    const int c = ok ? __ldcg(me.count + threadIdx.x) : 0;
+    s_cnt[threadIdx.x] = c < 0 ? 0 : (c > cap ? cap : c);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_off[0] = 0;
+    for (int g = 0; g < G; ++g) s_off[g + 1] = s_off[g] + s_cnt[g];
+  }
+  __syncthreads();
+  const int n = s_off[G];
+  const RouteView rv = route_view(ws, G * cap, el, 1);
+  int* phys = reinterpret_cast<int*>(rv.topk_w);   // [n] window row of each compacted row
+  for (int c = threadIdx.x; c < n; c += blockDim.x) {
+    int src = 0;
+    while (c >= s_off[src + 1]) ++src;
+    const int j = c - s_off[src];
+    const int le = __ldcg(me.meta + src * cap + j) & 0xFF;
+    rv.topk_idx[c] = le < el ? le : -1;
+    phys[c] = src * cap + j;
   }
   __syncthreads();
   int* scratch = reinterpret_cast<int*>(smem);
-  build_route_lists(rv.topk_idx, T, el, 1, 0, scratch, scratch + 3 * el, rv.n_active, rv.active, rv.pair_off,
+  build_route_lists(rv.topk_idx, n, el, 1, 0, scratch, scratch + 3 * el, rv.n_active, rv.active, rv.pair_off,
                     rv.pair_tok, rv.pair_slot);
+  __syncthreads();
+  const int listed = rv.pair_off[*rv.n_active];
+  for (int i = threadIdx.x; i < listed; i += blockDim.x) rv.pair_tok[i] = phys[rv.pair_tok[i]];
 }
 
-// Received rows' expert outputs (slot 0 of the receiving routing) -> bf16 return
-// segments of the same layout (row 0 unused, row 1 + j the output of received row j).
-// One CTA per pair row (G cap CTAs).
-__global__ void ep_pack_out_kernel(const float* __restrict__ part, const __nv_bfloat16* __restrict__ seg_in, int G,
-                                   int cap, int H, __nv_bfloat16* __restrict__ seg_out) {
+// Combine (receiving rank): each listed row's expert output (f32, slot 0 of the
+// receiving routing) as bf16 into its source's window, at the source's pair index; the
+// last CTA raises this rank's combine flag in every window.
+__global__ void ep_combine_kernel(const float* __restrict__ part, const void* ws, void* own, int G, int rank, int cap,
+                                  int H, int el, const unsigned long long* __restrict__ peers) {
   pdl_wait();
   pdl_trigger();
-  const int g = blockIdx.x / cap, j = blockIdx.x % cap;
-  const int64_t segw = static_cast<int64_t>(cap + 1) * H;
-  if (j >= reinterpret_cast<const int32_t*>(seg_in + g * segw)[0]) return;
-  const int64_t r = static_cast<int64_t>(g) * (cap + 1) + 1 + j;   // the receiving routing's row
-  const float* src = part + r * 2 * H;   // [T_r][k + 1 = 2][H], slot 0
-  __nv_bfloat16* dst = seg_out + r * H;
-  for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
-    const float2 v = *reinterpret_cast<const float2*>(src + 2 * i);
-    *reinterpret_cast<__nv_bfloat162*>(dst + 2 * i) = __floats2bfloat162_rn(v.x, v.y);
+  const EpWin me = ep_win(own, G, cap, H);
+  const int epoch = me.hdr[0] + 1;
+  const RouteView rv = route_view(const_cast<void*>(ws), G * cap, el, 1);
+  const int listed = rv.pair_off[*rv.n_active];
+  for (int i = blockIdx.x; i < listed; i += gridDim.x) {
+    const int r = rv.pair_tok[i];
+    const int src = r / cap;
+    const int pair = __ldcg(me.meta + r) >> 8;
+    const float* from = part + static_cast<int64_t>(r) * 2 * H;   // [rows][k + 1 = 2][H], slot 0
+    __nv_bfloat16* to = ep_win(reinterpret_cast<const void*>(peers[src]), G, cap, H).back + static_cast<int64_t>(pair) * H;
+    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+      const float4 a = *reinterpret_cast<const float4*>(from + c);
+      const float4 b = *reinterpret_cast<const float4*>(from + c + 4);
+      __nv_bfloat162 o[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                             __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+      *reinterpret_cast<uint4*>(to + c) = *reinterpret_cast<uint4*>(o);
+    }
   }
+  if (!ep_last_cta(me.hdr + 2)) return;
+  if (threadIdx.x < G)
+    st_release_sys(ep_win(reinterpret_cast<const void*>(peers[threadIdx.x]), G, cap, H).cflag + rank, epoch);
 }
 
-// The results back into the source routing's per-(token, slot) outputs.
-__global__ void ep_scatter_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ back, int T,
-                                  int H, int k, int el, int cap, float* __restrict__ part) {
+// Scatter (source rank): wait for every rank's combine, then the returned rows into the
+// source routing's per-(token, slot) outputs; the last CTA closes the exchange (epoch).
+__global__ void ep_scatter_kernel(const int32_t* __restrict__ idx, void* own, int T, int H, int k, int G, int el,
+                                  int cap, float* __restrict__ part) {
+  __shared__ int s_ok;
   pdl_wait();
   pdl_trigger();
+  const EpWin me = ep_win(own, G, cap, H);
+  const int epoch = me.hdr[0] + 1;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < G && !ep_wait_flag(me.cflag + threadIdx.x, epoch, me.hdr)) s_ok = 0;
+  __syncthreads();
   const int p = blockIdx.x;
-  if (p >= T * k) return;
-  const int d = idx[p] / el;
-  const int pos = ep_pos(idx, p, d, el);
-  const __nv_bfloat16* src = back + d * static_cast<int64_t>(cap + 1) * H + static_cast<int64_t>(1 + pos) * H;
-  float* dst = part + (static_cast<int64_t>(p / k) * (k + 1) + p % k) * H;
-  for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
-    const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + 2 * i));
-    *reinterpret_cast<float2*>(dst + 2 * i) = v;
+  if (s_ok) {
+    const __nv_bfloat16* src = me.back + static_cast<int64_t>(p) * H;
+    float* dst = part + (static_cast<int64_t>(p / k) * (k + 1) + p % k) * H;
+    for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
+      const unsigned u = __ldcg(reinterpret_cast<const unsigned*>(src) + i);
+      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
+      *reinterpret_cast<float2*>(dst + 2 * i) = v;
+    }
   }
+  (void)idx;
+  if (ep_last_cta(me.hdr + 3) && threadIdx.x == 0) me.hdr[0] = epoch;
 }
 
 static int ep_check(int64_t tokens, int64_t hidden, int64_t experts, int64_t top_k, int64_t ranks, int64_t cap) {
   QW_CHECK_ARG(tokens >= 1 && tokens * top_k <= 4096 && top_k >= 1 && top_k <= 16 && hidden % 8 == 0 && hidden > 0,
                "moe_ep: invalid shape (tokens * top_k <= 4096, hidden % 8 == 0)");
-  QW_CHECK_ARG(ranks >= 1 && experts % ranks == 0 && experts / ranks <= 256, "moe_ep: experts must split evenly, <= 256 per rank");
-  QW_CHECK_ARG(cap >= tokens * top_k && ranks * (cap + 1) <= 4096, "moe_ep: cap must be >= tokens * top_k, "
-               "ranks * (cap + 1) <= 4096");
-  QW_CHECK_ARG((cap + 1) * 4 <= hidden * 2, "moe_ep: the segment header (cap + 1 words) must fit in one row");
+  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && experts % ranks == 0 && experts / ranks <= 256,
+               "moe_ep: 1 <= ranks <= 64, experts must split evenly, <= 256 per rank");
+  QW_CHECK_ARG(cap == tokens * top_k, "moe_ep: cap must be tokens * top_k (the rows one source can send)");
   return QW_OK;
 }
 
 }  // namespace qw
 
+extern "C" int64_t qw_ep_window_bytes(int64_t ranks, int64_t cap, int64_t hidden) {
+  if (ranks <= 0 || ranks > EP_MAX_RANKS || cap <= 0 || hidden <= 0) return -1;
+  return ep_window_bytes(static_cast<int>(ranks), static_cast<int>(cap), static_cast<int>(hidden));
+}
+
+extern "C" int qw_ep_window_alloc(int64_t bytes, void** window, void* ipc_handle) {
+  QW_CHECK_ARG(bytes > 0 && window && ipc_handle, "ep_window_alloc: invalid argument");
+  void* p = nullptr;
+  cudaError_t err = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (err != cudaSuccess) return cuda_status(err, "ep_window_alloc: cudaMalloc");
+  err = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(err, "ep_window_alloc: clear / IPC handle");
+  }
+  *window = p;
+  return QW_OK;
+}
+
+extern "C" int qw_ep_window_open(const void* ipc_handle, void** peer_window) {
+  QW_CHECK_ARG(ipc_handle && peer_window, "ep_window_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(peer_window, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_status(err, "ep_window_open: cudaIpcOpenMemHandle");
+  return QW_OK;
+}
+
+extern "C" int qw_ep_window_close(void* peer_window) {
+  QW_CHECK_ARG(peer_window, "ep_window_close: null pointer");
+  const cudaError_t err = cudaIpcCloseMemHandle(peer_window);
+  if (err != cudaSuccess) return cuda_status(err, "ep_window_close");
+  return QW_OK;
+}
+
+extern "C" int qw_ep_window_free(void* window) {
+  QW_CHECK_ARG(window, "ep_window_free: null pointer");
+  const cudaError_t err = cudaFree(window);
+  if (err != cudaSuccess) return cuda_status(err, "ep_window_free");
+  return QW_OK;
+}
+
 extern "C" int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                                                   int64_t inter) {
   if (ranks <= 0 || cap <= 0 || experts % ranks) return -1;
-  return qw_moe_workspace_bytes(ranks * (cap + 1), hidden, experts / ranks, inter, 1);
+  return qw_moe_workspace_bytes(ranks * cap, hidden, experts / ranks, inter, 1);
 }
 
-extern "C" int qw_moe_ep_pack(const void* workspace, const void* x, int64_t tokens, int64_t hidden, int64_t experts,
-                              int64_t top_k, int64_t ranks, int64_t cap, void* send_seg, void* stream) {
-  QW_CHECK_ARG(workspace && x && send_seg, "moe_ep_pack: null pointer");
+extern "C" int qw_moe_ep_dispatch(const void* workspace, const void* x, int64_t tokens, int64_t hidden,
+                                  int64_t experts, int64_t top_k, int64_t ranks, int64_t rank, int64_t cap,
+                                  const void* peers, void* window, void* stream) {
+  QW_CHECK_ARG(workspace && x && peers && window, "moe_ep_dispatch: null pointer");
   const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
   if (st) return st;
-  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(send_seg) & 15) == 0,
-               "moe_ep_pack: x and the segments must be 16-byte aligned");
+  QW_CHECK_ARG(rank >= 0 && rank < ranks, "moe_ep_dispatch: rank outside [0, ranks)");
+  QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "moe_ep_dispatch: x must be 16-byte aligned");
   const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
   const RouteView rv = route_view(const_cast<void*>(workspace), T, E, k);
-  QW_LAUNCH_PDL("moe ep pack", ep_pack_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0, as_stream(stream),
-                rv.topk_idx, static_cast<const __nv_bfloat16*>(x), T, static_cast<int>(hidden), k,
-                static_cast<int>(ranks), static_cast<int>(experts / ranks), static_cast<int>(cap),
-                static_cast<__nv_bfloat16*>(send_seg));
+  QW_LAUNCH_PDL("moe ep dispatch", ep_dispatch_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0,
+                as_stream(stream), rv.topk_idx, static_cast<const __nv_bfloat16*>(x), T, static_cast<int>(hidden), k,
+                static_cast<int>(ranks), static_cast<int>(rank), static_cast<int>(experts / ranks),
+                static_cast<int>(cap), static_cast<const unsigned long long*>(peers), window);
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_recv_route(const void* recv_seg, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+extern "C" int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
                                     void* recv_workspace, void* stream) {
-  QW_CHECK_ARG(recv_seg && recv_workspace, "moe_ep_recv_route: null pointer");
-  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && experts / ranks <= 256 &&
-                   ranks * (cap + 1) <= 4096 && (cap + 1) * 4 <= hidden * 2, "moe_ep_recv_route: shape");
+  QW_CHECK_ARG(window && recv_workspace, "moe_ep_recv_route: null pointer");
+  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && experts % ranks == 0 && experts / ranks <= 256,
+               "moe_ep_recv_route: shape");
   const int el = static_cast<int>(experts / ranks);
   const size_t smem = (3 * static_cast<size_t>(el) + 64) * sizeof(int);
-  QW_LAUNCH_PDL("moe ep recv route", ep_recv_route_kernel, dim3(1), dim3(1024), smem, as_stream(stream),
-                static_cast<const __nv_bfloat16*>(recv_seg), static_cast<int>(ranks), static_cast<int>(cap),
-                static_cast<int>(hidden), el, recv_workspace);
+  QW_LAUNCH_PDL("moe ep recv route", ep_recv_route_kernel, dim3(1), dim3(1024), smem, as_stream(stream), window,
+                static_cast<int>(ranks), static_cast<int>(cap), static_cast<int>(hidden), el, recv_workspace);
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_experts(const void* recv_seg, const void* gate_up_local, const void* down_local,
+extern "C" int qw_moe_ep_experts(const void* window, const void* gate_up_local, const void* down_local,
                                  int64_t ranks, int64_t cap, int64_t hidden, int64_t experts, int64_t inter,
                                  int32_t group, void* recv_workspace, void* stream) {
-  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0, "moe_ep_experts: shape");
-  // the received segments as G (cap + 1) rows, routed (lists included) by qw_moe_ep_recv_route;
-  // a rank receives cap pairs on average (every rank sends cap), which sets the tile width
-  return experts_w4(recv_seg, gate_up_local, down_local, nullptr, nullptr, ranks * (cap + 1), hidden,
-                    experts / ranks, inter, 1, group, recv_workspace, stream, true, true, 0, experts / ranks,
-                    true, cap);
+  QW_CHECK_ARG(window && ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && experts % ranks == 0,
+               "moe_ep_experts: shape");
+  // the window's received rows as ranks * cap rows, routed (lists included) by
+  // qw_moe_ep_recv_route; a rank receives cap pairs on average (every rank sends cap),
+  // which sets the tile width
+  const EpWin w = ep_win(window, static_cast<int>(ranks), static_cast<int>(cap), static_cast<int>(hidden));
+  return experts_w4(w.rows, gate_up_local, down_local, nullptr, nullptr, ranks * cap, hidden, experts / ranks, inter,
+                    1, group, recv_workspace, stream, true, true, 0, experts / ranks, true, cap);
 }
 
-extern "C" int qw_moe_ep_pack_out(const void* recv_workspace, const void* recv_seg, int64_t ranks, int64_t cap,
-                                  int64_t hidden, int64_t experts, int64_t inter, void* send_back, void* stream) {
-  QW_CHECK_ARG(recv_workspace && recv_seg && send_back, "moe_ep_pack_out: null pointer");
-  QW_CHECK_ARG(ranks >= 1 && cap >= 1 && experts % ranks == 0 && hidden % 2 == 0, "moe_ep_pack_out: shape");
-  const int Tr = static_cast<int>(ranks * (cap + 1)), H = static_cast<int>(hidden);
-  WsParts w = split_ws(const_cast<void*>(recv_workspace), Tr, H, static_cast<int>(experts / ranks),
-                       static_cast<int>(inter), 1);
-  QW_LAUNCH_PDL("moe ep pack out", ep_pack_out_kernel, dim3(static_cast<unsigned>(ranks * cap)), dim3(256), 0,
-                as_stream(stream), w.part, static_cast<const __nv_bfloat16*>(recv_seg), static_cast<int>(ranks),
-                static_cast<int>(cap), H, static_cast<__nv_bfloat16*>(send_back));
+extern "C" int qw_moe_ep_combine(const void* recv_workspace, void* window, int64_t ranks, int64_t rank, int64_t cap,
+                                 int64_t hidden, int64_t experts, int64_t inter, const void* peers, void* stream) {
+  QW_CHECK_ARG(recv_workspace && window && peers, "moe_ep_combine: null pointer");
+  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && rank >= 0 && rank < ranks && cap >= 1 &&
+                   experts % ranks == 0 && hidden % 8 == 0, "moe_ep_combine: shape");
+  const int Tr = static_cast<int>(ranks * cap), H = static_cast<int>(hidden), el = static_cast<int>(experts / ranks);
+  WsParts w = split_ws(const_cast<void*>(recv_workspace), Tr, H, el, static_cast<int>(inter), 1);
+  const int grid = 2 * sm_count();
+  QW_LAUNCH_PDL("moe ep combine", ep_combine_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                as_stream(stream), w.part, w.route, window, static_cast<int>(ranks), static_cast<int>(rank),
+                static_cast<int>(cap), H, el, static_cast<const unsigned long long*>(peers));
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_scatter(void* workspace, const void* recv_back, int64_t tokens, int64_t hidden,
-                                 int64_t experts, int64_t inter, int64_t top_k, int64_t ranks, int64_t cap,
-                                 void* stream) {
-  QW_CHECK_ARG(workspace && recv_back, "moe_ep_scatter: null pointer");
+extern "C" int qw_moe_ep_scatter(void* workspace, void* window, int64_t tokens, int64_t hidden, int64_t experts,
+                                 int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, void* stream) {
+  QW_CHECK_ARG(workspace && window, "moe_ep_scatter: null pointer");
   const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
   if (st) return st;
   const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
@@ -2047,7 +2231,7 @@ extern "C" int qw_moe_ep_scatter(void* workspace, const void* recv_back, int64_t
   const RouteView rv = route_view(workspace, T, E, k);
   WsParts w = split_ws(workspace, T, H, E, static_cast<int>(inter), k);
   QW_LAUNCH_PDL("moe ep scatter", ep_scatter_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0,
-                as_stream(stream), rv.topk_idx, static_cast<const __nv_bfloat16*>(recv_back), T, H, k,
+                as_stream(stream), rv.topk_idx, window, T, H, k, static_cast<int>(ranks),
                 static_cast<int>(experts / ranks), static_cast<int>(cap), w.part);
   return QW_OK;
 }

@@ -150,8 +150,7 @@ def weights_random(cfg: TargetConfig, seed: int = 2, std: float = 0.02, device="
 
 class TargetEngine:
     def __init__(self, cfg: TargetConfig, weights, *, batch: int, block: int = 16, capacity: int = 4096,
-                 page_size: int = 16, device="cuda", ep_group=None,
-                 ep_overlap_shared: bool = True):
+                 page_size: int = 16, device="cuda", ep_group=None):
         if not 1 <= block <= lib.QW_MAX_BLOCK:
             raise ValueError(f"block must be in [1, {lib.QW_MAX_BLOCK}]")
         self.cfg, self.B, self.S, self.device = cfg, batch, block, torch.device(device)
@@ -204,8 +203,7 @@ class TargetEngine:
                           for lw in self.layers]
             self.ep_moe = _ep.ExpertParallelMoE(ep_group, tokens=T, hidden=H, experts=E,
                                                 inter=c.moe_intermediate_size, top_k=c.num_experts_per_tok,
-                                                quant_group=c.quant_group, device=dev,
-                                                overlap_shared=ep_overlap_shared)
+                                                quant_group=c.quant_group, device=dev)
         self.nblk = self.lib.qw_lmhead_blocks(self.vocab_pad)
         self.keys = torch.zeros(self.nblk, T, dtype=torch.int64, device=dev)
         self.top1 = torch.zeros(T, dtype=torch.int32, device=dev)
@@ -254,8 +252,8 @@ class TargetEngine:
         lib.check(getattr(self.lib, name)(*args), name)
 
     # kernels each entry point launches (all others launch one)
-    # (expert-parallel MoE layer: shared expert 2, pack, receive routing, lists + gate/up +
-    # down of the received rows, output pack, scatter; the all-to-alls are the library's)
+    # (expert-parallel MoE layer: dispatch, shared expert 2, receive routing, gate/up +
+    # down of the received rows, combine, scatter)
     KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2, "qw_moe_ep": 8}
 
     def launches_per_step(self) -> int:
@@ -324,7 +322,7 @@ class TargetEngine:
                 if self._recording is not None:
                     self._recording["qw_moe_ep"] = self._recording.get("qw_moe_ep", 0) + 1
                 self.ep_moe.experts(self.normed, self.moe_ws, self.ep_gu[l], self.ep_dn[l], lw.shared_gu,
-                                    lw.shared_down, st)
+                                    lw.shared_down)
             else:
                 self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                            lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
@@ -381,7 +379,7 @@ class TargetEngine:
         c = self.cfg
         if self.ep_moe is not None:
             m = self.ep_moe
-            off = self.lib.qw_moe_active_experts(None, m.G * (m.cap + 1), m.el, 1)
+            off = self.lib.qw_moe_active_experts(None, m.G * m.cap, m.el, 1)
             return int(m.ws_r[off:off + 4].view(torch.int32).item())
         off = self.lib.qw_moe_active_experts(None, self.T, c.num_experts, c.num_experts_per_tok)
         return int(self.moe_ws[off:off + 4].view(torch.int32).item())
@@ -457,6 +455,13 @@ class TargetEngine:
 
     def replay(self):
         self.graph.replay()
+
+    def close(self):
+        """Release the captured graph and, with expert parallelism, the exchange windows
+        (collective: every rank of the group)."""
+        self.graph = None
+        if self.ep_moe is not None:
+            self.ep_moe.close()
 
     # ------------------------------------------------------------------ state utilities
     def snapshot(self):

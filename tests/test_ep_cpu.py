@@ -1,8 +1,8 @@
-"""The expert-parallel exchange on CPU: two gloo ranks pack their routed pairs, swap
-segments with all_to_all_single, run their own experts on what they received, swap the
-outputs back and scatter them; every (token, slot) must end up with its expert's output
-of its token, as one process holding all experts computes it."""
-import os
+"""The expert-parallel exchange protocol on CPU: two gloo ranks dispatch their routed pairs
+(the blocks each would store into the owners' windows, swapped here with all_to_all),
+run their own experts on the rows they received, send the outputs back to the pairs'
+sources and scatter them; every (token, slot) must end up with its expert's output of
+its token, as one process holding all experts computes it."""
 import socket
 
 import numpy as np
@@ -31,13 +31,14 @@ def _expert(e, rows):
     return _bf16_bits(_from_bits(rows) * (1.0 + 0.25 * e) + e)
 
 
-def _swap(seg: np.ndarray) -> np.ndarray:
-    """all_to_all_single of 16-bit segments (as int32 words: gloo's types)."""
-    send = torch.from_numpy(np.ascontiguousarray(seg).view(np.int32))
-    recv = torch.empty_like(send)
+def _swap(arr: np.ndarray) -> np.ndarray:
+    """all_to_all over the leading (rank) axis of a 16- or 32-bit array (gloo: int32)."""
     import torch.distributed as dist
+    raw = np.ascontiguousarray(arr)
+    send = torch.from_numpy(raw.view(np.int32).copy())
+    recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send)
-    return recv.numpy().view(np.uint16)
+    return recv.numpy().view(raw.dtype).reshape(raw.shape)
 
 
 def _worker(rank, world, port, T, H, E, k):
@@ -47,16 +48,22 @@ def _worker(rank, world, port, T, H, E, k):
         rng = np.random.default_rng(10 + rank)
         topk = np.stack([rng.choice(E, k, replace=False) for _ in range(T)])   # distinct experts per token
         x16 = _bf16_bits(torch.from_numpy(rng.normal(0, 1, (T, H)).astype(np.float32)))
-        cap = T * k
-        recv = _swap(ep_np.pack(topk, x16, E, world, cap))
-        el = E // world
-        local = ep_np.recv_experts(recv, cap)
-        rows = recv.reshape(world * (cap + 1), H)
-        back = np.zeros_like(rows)
-        for i, e in enumerate(local):
-            if e >= 0:
-                back[i] = _expert(rank * el + int(e), rows[i])
-        got = ep_np.scatter(topk, _swap(back.reshape(world, cap + 1, H)), E, world)
+        cap, el = T * k, E // world
+        out_blocks = ep_np.dispatch(topk, x16, E, world)
+        # what lands in this rank's window: block s = what source s wrote for this rank
+        rows = _swap(np.stack([b[0] for b in out_blocks]))
+        meta = _swap(np.stack([b[1] for b in out_blocks]))
+        count = _swap(np.array([[b[2]] for b in out_blocks], np.int32))[:, 0]
+        blocks = [(rows[s], meta[s], int(count[s])) for s in range(world)]
+        outputs = {(s, j): _expert(rank * el + le, rows[s, j]) for s, j, le in ep_np.received(blocks)}
+        back_to, written = ep_np.combine(blocks, outputs, cap, H)
+        back = _swap(back_to)              # [d]: the rows rank d wrote into this rank's back
+        mask = _swap(written.astype(np.int32))
+        assert (mask.sum(0) == 1).all()    # every pair's output arrives exactly once
+        mine = np.zeros((cap, H), np.uint16)
+        for d in range(world):
+            mine[mask[d] == 1] = back[d][mask[d] == 1]
+        got = ep_np.scatter(mine, T, k)
         for t in range(T):
             for s in range(k):
                 np.testing.assert_array_equal(got[t, s], _expert(int(topk[t, s]), x16[t]))
@@ -71,15 +78,13 @@ def test_expert_parallel_exchange_gloo(T, E, k):
     mp.spawn(_worker, args=(2, _free_port(), T, 160, E, k), nprocs=2, join=True)
 
 
-def test_pack_layout():
+def test_dispatch_layout():
     topk = np.array([[0, 3], [2, 1]])
     x16 = np.arange(2 * 16, dtype=np.uint16).reshape(2, 16)
-    seg = ep_np.pack(topk, x16, experts=4, ranks=2, cap=4)
-    words = ep_np.header_words(seg, 4)
+    blocks = ep_np.dispatch(topk, x16, experts=4, ranks=2)
     # rank 0 owns experts 0, 1: pairs 0 (e0) and 3 (e1); rank 1 owns 2, 3: pairs 1 (e3) and 2 (e2)
-    assert words[0, 0] == 2 and list(words[0, 1:3]) == [(0 << 8) | 0, (3 << 8) | 1]
-    assert words[1, 0] == 2 and list(words[1, 1:3]) == [(1 << 8) | 1, (2 << 8) | 0]
-    np.testing.assert_array_equal(seg[0, 2], x16[1])    # pair 3 (token 1) is rank 0's second row
-    np.testing.assert_array_equal(ep_np.recv_experts(seg, 4).reshape(2, 5)[:, :3], [[-1, 0, 1], [-1, 1, 0]])
-    with pytest.raises(ValueError):
-        ep_np.pack(np.zeros((4, 1), int), np.zeros((4, 16), np.uint16), experts=4, ranks=2, cap=3)
+    (r0, m0, c0), (r1, m1, c1) = blocks
+    assert c0 == 2 and list(m0[:2]) == [(0 << 8) | 0, (3 << 8) | 1]
+    assert c1 == 2 and list(m1[:2]) == [(1 << 8) | 1, (2 << 8) | 0]
+    np.testing.assert_array_equal(r0[1], x16[1])    # pair 3 (token 1) is rank 0's second row
+    assert ep_np.received(blocks) == [(0, 0, 0), (0, 1, 1), (1, 0, 1), (1, 1, 0)]
