@@ -256,7 +256,10 @@ int qw_moe_experts_w4_range(const void* x, const void* gate_up, const void* down
  *   qw_moe_ep_scatter     waits (bounded) for every rank's combine, writes the returned
  *                         rows into the routing's per-(token, slot) outputs for
  *                         qw_moe_combine(_norm), and closes the exchange.
- * cap = tokens * top_k (every rank the same tokens).  Every rank issues the same calls in
+ * With shared = 1 the shared expert travels the same way: every rank holds it as local
+ * expert E/G, after its routed experts (gate_up_local / down_local carry E/G + 1
+ * experts), and each token sends it one more row, to its own rank.  local_experts =
+ * E/G + shared; cap = tokens * (top_k + shared) (every rank the same tokens).  Every rank issues the same calls in
  * the same order; calls are stream-ordered (graph-capturable), and the results equal
  * the one-GPU MoE bit for bit.  A wait that expires (a lost peer) records
  * QW_ERR_TIMEOUT for qw_wait_status / qw_check_wait_status.
@@ -268,20 +271,20 @@ int qw_ep_window_alloc(int64_t bytes, void** window, void* ipc_handle);
 int qw_ep_window_open(const void* ipc_handle, void** peer_window);
 int qw_ep_window_close(void* peer_window);
 int qw_ep_window_free(void* window);
-int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts,
                                        int64_t inter);
 int qw_moe_ep_dispatch(const void* workspace, const void* x, int64_t tokens, int64_t hidden,
                        int64_t experts, int64_t top_k, int64_t ranks, int64_t rank, int64_t cap,
-                       const void* peers, void* window, void* stream);
-int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+                       int shared, const void* peers, void* window, void* stream);
+int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts,
                          void* recv_workspace, void* stream);
 int qw_moe_ep_experts(const void* window, const void* gate_up_local, const void* down_local,
-                      int64_t ranks, int64_t cap, int64_t hidden, int64_t experts, int64_t inter,
+                      int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts, int64_t inter,
                       int32_t group, void* recv_workspace, void* stream);
 int qw_moe_ep_combine(const void* recv_workspace, void* window, int64_t ranks, int64_t rank, int64_t cap,
-                      int64_t hidden, int64_t experts, int64_t inter, const void* peers, void* stream);
+                      int64_t hidden, int64_t local_experts, int64_t inter, const void* peers, void* stream);
 int qw_moe_ep_scatter(void* workspace, void* window, int64_t tokens, int64_t hidden, int64_t experts,
-                      int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, void* stream);
+                      int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, int shared, void* stream);
 
 /* Byte offset, inside a MoE workspace, of the int32 count of active routed experts
  * (valid after qw_moe_route_lists or an expert entry point; for measuring the experts

@@ -1874,9 +1874,12 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
 //   dflag int32[64]   dflag[s] = epoch of source s's last dispatch to g
 //   cflag int32[64]   cflag[d] = epoch of destination d's last combine back to g
 //   count int32[64]   count[s] = rows source s sent to g in its last dispatch
-//   meta  int32[G][cap]       (source pair index << 8) | local expert, per received row
+//   meta  int32[G][cap]       (source pair index << 9) | local expert, per received row
 //   rows  bf16 [G][cap][H]    received rows (source s at rows [s][0, count[s]))
 //   back  bf16 [cap][H]       this rank's own pairs' expert outputs (pair p at row p)
+// With the shared expert exchanged too (shared = 1), every rank holds it as local expert
+// el = E/G after its routed ones, and each token sends one more pair (index T k + t) to
+// its own rank: the shared expert then runs in the same launches as the routed ones.
 // Ordering: a rank's scatter of exchange n waits for every peer's combine of n, so its
 // dispatch of n + 1 cannot overwrite a window region a peer is still reading.
 //
@@ -1948,16 +1951,19 @@ __device__ bool ep_wait_flag(const int32_t* flag, int want, int32_t* hdr) {
   return true;
 }
 
-// The CTA that finishes last (ticket wraps to 0 for the next launch): every thread
-// fences its own stores at system scope first.
+// The CTA that finishes last (ticket wraps to 0 for the next launch).  The CTA barrier
+// orders every thread's stores before thread 0's system-scope fence, which precedes
+// its ticket; the last CTA's thread 0 fences again after taking the last ticket, and
+// then alone stores the flags (with release), so every CTA's stores happen before them.
 __device__ __forceinline__ bool ep_last_cta(int32_t* ticket) {
   __shared__ int s_last;
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
+    __threadfence_system();
     s_last = atomicInc(reinterpret_cast<unsigned*>(ticket), gridDim.x - 1) == gridDim.x - 1;
+    if (s_last) __threadfence_system();
+  }
   __syncthreads();
-  if (s_last) __threadfence_system();
   return s_last != 0;
 }
 
@@ -1972,23 +1978,44 @@ __device__ __forceinline__ int ep_pos(const int32_t* idx, int p, int d, int el) 
   return pos;
 }
 
-// Dispatch (source rank): one CTA per routed pair stores its token's row and descriptor
-// into the owner's window; the last CTA stores the per-destination counts and raises
-// this rank's dispatch flag in every window (all ranks, rows or not).
+// Destination of routed pair p and its position among the pairs to that destination,
+// counted by the whole CTA.  Shared-expert pairs (p >= T k: token p - T k) stay on this
+// rank, after its routed pairs.
+__device__ __forceinline__ void ep_route_pair(const int32_t* idx, int p, int np, int el, int rank, int& d, int& pos) {
+  if (p < np) {
+    d = idx[p] / el;
+    pos = ep_pos(idx, p, d, el);
+  } else {
+    d = rank;
+    int before = 0;
+    for (int q0 = 0; q0 < np; q0 += blockDim.x) {
+      const int q = q0 + threadIdx.x;
+      before += __syncthreads_count(q < np && idx[q] / el == rank);
+    }
+    pos = before + (p - np);
+  }
+}
+
+// Dispatch (source rank): one CTA per pair -- the T k routed pairs, then (with the shared
+// expert, local expert el of every rank) one per token -- stores its token's row and
+// descriptor into the owner's window; the last CTA stores the per-destination counts and
+// raises this rank's dispatch flag in every window (all ranks, rows or not).
 __global__ void ep_dispatch_kernel(const int32_t* __restrict__ idx, const __nv_bfloat16* __restrict__ x, int T, int H,
-                                   int k, int G, int rank, int el, int cap, const unsigned long long* __restrict__ peers,
-                                   void* own) {
+                                   int k, int G, int rank, int el, int shared, int cap,
+                                   const unsigned long long* __restrict__ peers, void* own) {
   pdl_wait();
   pdl_trigger();
   const EpWin me = ep_win(own, G, cap, H);
   const int epoch = me.hdr[0] + 1;
   const int np = T * k;
   const int p = blockIdx.x;
-  const int d = idx[p] / el;
-  const int pos = ep_pos(idx, p, d, el);
+  int d, pos;
+  ep_route_pair(idx, p, np, el, rank, d, pos);
+  const int tok = p < np ? p / k : p - np;
+  const int local = p < np ? idx[p] - d * el : el;
   const EpWin dst = ep_win(reinterpret_cast<const void*>(peers[d]), G, cap, H);
-  if (threadIdx.x == 0) dst.meta[rank * cap + pos] = (p << 8) | (idx[p] - d * el);
-  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(p / k) * H);
+  if (threadIdx.x == 0) dst.meta[rank * cap + pos] = (p << 9) | local;
+  const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(tok) * H);
   uint4* out = reinterpret_cast<uint4*>(dst.rows + (static_cast<int64_t>(rank) * cap + pos) * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) out[i] = src[i];
   if (!ep_last_cta(me.hdr + 1)) return;
@@ -1998,12 +2025,13 @@ __global__ void ep_dispatch_kernel(const int32_t* __restrict__ idx, const __nv_b
       const int q = q0 + threadIdx.x;
       c += __syncthreads_count(q < np && idx[q] / el == g);
     }
-    if (threadIdx.x == 0) ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).count[rank] = c;
+    if (threadIdx.x == 0)
+      ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).count[rank] = c + (g == rank && shared ? T : 0);
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < G)
-    st_release_sys(ep_win(reinterpret_cast<const void*>(peers[threadIdx.x]), G, cap, H).dflag + rank, epoch);
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int g = 0; g < G; ++g) st_release_sys(ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).dflag + rank, epoch);
+  }
 }
 
 // Receiving rank: wait for every source's dispatch, then route the received rows
@@ -2035,7 +2063,7 @@ __global__ void __launch_bounds__(1024) ep_recv_route_kernel(void* own, int G, i
     int src = 0;
     while (c >= s_off[src + 1]) ++src;
     const int j = c - s_off[src];
-    const int le = __ldcg(me.meta + src * cap + j) & 0xFF;
+    const int le = __ldcg(me.meta + src * cap + j) & 0x1FF;
     rv.topk_idx[c] = le < el ? le : -1;
     phys[c] = src * cap + j;
   }
@@ -2062,7 +2090,7 @@ __global__ void ep_combine_kernel(const float* __restrict__ part, const void* ws
   for (int i = blockIdx.x; i < listed; i += gridDim.x) {
     const int r = rv.pair_tok[i];
     const int src = r / cap;
-    const int pair = __ldcg(me.meta + r) >> 8;
+    const int pair = __ldcg(me.meta + r) >> 9;
     const float* from = part + static_cast<int64_t>(r) * 2 * H;   // [rows][k + 1 = 2][H], slot 0
     __nv_bfloat16* to = ep_win(reinterpret_cast<const void*>(peers[src]), G, cap, H).back + static_cast<int64_t>(pair) * H;
     for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
@@ -2073,15 +2101,14 @@ __global__ void ep_combine_kernel(const float* __restrict__ part, const void* ws
       *reinterpret_cast<uint4*>(to + c) = *reinterpret_cast<uint4*>(o);
     }
   }
-  if (!ep_last_cta(me.hdr + 2)) return;
-  if (threadIdx.x < G)
-    st_release_sys(ep_win(reinterpret_cast<const void*>(peers[threadIdx.x]), G, cap, H).cflag + rank, epoch);
+  if (ep_last_cta(me.hdr + 2) && threadIdx.x == 0)
+    for (int g = 0; g < G; ++g) st_release_sys(ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).cflag + rank, epoch);
 }
 
 // Scatter (source rank): wait for every rank's combine, then the returned rows into the
-// source routing's per-(token, slot) outputs; the last CTA closes the exchange (epoch).
-__global__ void ep_scatter_kernel(const int32_t* __restrict__ idx, void* own, int T, int H, int k, int G, int el,
-                                  int cap, float* __restrict__ part) {
+// source routing's per-(token, slot) outputs (a shared-expert pair p >= T k into slot k
+// of token p - T k); the last CTA closes the exchange (epoch).
+__global__ void ep_scatter_kernel(void* own, int T, int H, int k, int G, int cap, float* __restrict__ part) {
   __shared__ int s_ok;
   pdl_wait();
   pdl_trigger();
@@ -2094,23 +2121,28 @@ __global__ void ep_scatter_kernel(const int32_t* __restrict__ idx, void* own, in
   const int p = blockIdx.x;
   if (s_ok) {
     const __nv_bfloat16* src = me.back + static_cast<int64_t>(p) * H;
-    float* dst = part + (static_cast<int64_t>(p / k) * (k + 1) + p % k) * H;
+    const int np = T * k;
+    const int64_t slot_row = p < np ? static_cast<int64_t>(p / k) * (k + 1) + p % k
+                                    : static_cast<int64_t>(p - np) * (k + 1) + k;
+    float* dst = part + slot_row * H;
     for (int i = threadIdx.x; i < H / 2; i += blockDim.x) {
       const unsigned u = __ldcg(reinterpret_cast<const unsigned*>(src) + i);
       const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
       *reinterpret_cast<float2*>(dst + 2 * i) = v;
     }
   }
-  (void)idx;
   if (ep_last_cta(me.hdr + 3) && threadIdx.x == 0) me.hdr[0] = epoch;
 }
 
-static int ep_check(int64_t tokens, int64_t hidden, int64_t experts, int64_t top_k, int64_t ranks, int64_t cap) {
+static int ep_check(int64_t tokens, int64_t hidden, int64_t experts, int64_t top_k, int64_t ranks, int64_t cap,
+                    int shared) {
   QW_CHECK_ARG(tokens >= 1 && tokens * top_k <= 4096 && top_k >= 1 && top_k <= 16 && hidden % 8 == 0 && hidden > 0,
                "moe_ep: invalid shape (tokens * top_k <= 4096, hidden % 8 == 0)");
   QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && experts % ranks == 0 && experts / ranks <= 256,
                "moe_ep: 1 <= ranks <= 64, experts must split evenly, <= 256 per rank");
-  QW_CHECK_ARG(cap == tokens * top_k, "moe_ep: cap must be tokens * top_k (the rows one source can send)");
+  QW_CHECK_ARG(shared == 0 || shared == 1, "moe_ep: shared must be 0 or 1");
+  QW_CHECK_ARG(cap == tokens * (top_k + shared),
+               "moe_ep: cap must be tokens * (top_k + shared) (the rows one source can send)");
   return QW_OK;
 }
 
@@ -2159,35 +2191,35 @@ extern "C" int qw_ep_window_free(void* window) {
   return QW_OK;
 }
 
-extern "C" int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+extern "C" int64_t qw_moe_ep_recv_workspace_bytes(int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts,
                                                   int64_t inter) {
-  if (ranks <= 0 || cap <= 0 || experts % ranks) return -1;
-  return qw_moe_workspace_bytes(ranks * cap, hidden, experts / ranks, inter, 1);
+  if (ranks <= 0 || cap <= 0 || local_experts <= 0) return -1;
+  return qw_moe_workspace_bytes(ranks * cap, hidden, local_experts, inter, 1);
 }
 
 extern "C" int qw_moe_ep_dispatch(const void* workspace, const void* x, int64_t tokens, int64_t hidden,
                                   int64_t experts, int64_t top_k, int64_t ranks, int64_t rank, int64_t cap,
-                                  const void* peers, void* window, void* stream) {
+                                  int shared, const void* peers, void* window, void* stream) {
   QW_CHECK_ARG(workspace && x && peers && window, "moe_ep_dispatch: null pointer");
-  const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
+  const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap, shared);
   if (st) return st;
   QW_CHECK_ARG(rank >= 0 && rank < ranks, "moe_ep_dispatch: rank outside [0, ranks)");
   QW_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "moe_ep_dispatch: x must be 16-byte aligned");
   const int T = static_cast<int>(tokens), E = static_cast<int>(experts), k = static_cast<int>(top_k);
   const RouteView rv = route_view(const_cast<void*>(workspace), T, E, k);
-  QW_LAUNCH_PDL("moe ep dispatch", ep_dispatch_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0,
+  QW_LAUNCH_PDL("moe ep dispatch", ep_dispatch_kernel, dim3(static_cast<unsigned>(cap)), dim3(256), 0,
                 as_stream(stream), rv.topk_idx, static_cast<const __nv_bfloat16*>(x), T, static_cast<int>(hidden), k,
-                static_cast<int>(ranks), static_cast<int>(rank), static_cast<int>(experts / ranks),
+                static_cast<int>(ranks), static_cast<int>(rank), static_cast<int>(experts / ranks), shared,
                 static_cast<int>(cap), static_cast<const unsigned long long*>(peers), window);
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t experts,
+extern "C" int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts,
                                     void* recv_workspace, void* stream) {
   QW_CHECK_ARG(window && recv_workspace, "moe_ep_recv_route: null pointer");
-  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && experts % ranks == 0 && experts / ranks <= 256,
+  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && local_experts >= 1 && local_experts <= 257,
                "moe_ep_recv_route: shape");
-  const int el = static_cast<int>(experts / ranks);
+  const int el = static_cast<int>(local_experts);
   const size_t smem = (3 * static_cast<size_t>(el) + 64) * sizeof(int);
   QW_LAUNCH_PDL("moe ep recv route", ep_recv_route_kernel, dim3(1), dim3(1024), smem, as_stream(stream), window,
                 static_cast<int>(ranks), static_cast<int>(cap), static_cast<int>(hidden), el, recv_workspace);
@@ -2195,24 +2227,24 @@ extern "C" int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, in
 }
 
 extern "C" int qw_moe_ep_experts(const void* window, const void* gate_up_local, const void* down_local,
-                                 int64_t ranks, int64_t cap, int64_t hidden, int64_t experts, int64_t inter,
+                                 int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts, int64_t inter,
                                  int32_t group, void* recv_workspace, void* stream) {
-  QW_CHECK_ARG(window && ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && experts % ranks == 0,
+  QW_CHECK_ARG(window && ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && local_experts >= 1 && local_experts <= 257,
                "moe_ep_experts: shape");
   // the window's received rows as ranks * cap rows, routed (lists included) by
   // qw_moe_ep_recv_route; a rank receives cap pairs on average (every rank sends cap),
   // which sets the tile width
   const EpWin w = ep_win(window, static_cast<int>(ranks), static_cast<int>(cap), static_cast<int>(hidden));
-  return experts_w4(w.rows, gate_up_local, down_local, nullptr, nullptr, ranks * cap, hidden, experts / ranks, inter,
-                    1, group, recv_workspace, stream, true, true, 0, experts / ranks, true, cap);
+  return experts_w4(w.rows, gate_up_local, down_local, nullptr, nullptr, ranks * cap, hidden, local_experts, inter,
+                    1, group, recv_workspace, stream, true, true, 0, local_experts, true, cap);
 }
 
 extern "C" int qw_moe_ep_combine(const void* recv_workspace, void* window, int64_t ranks, int64_t rank, int64_t cap,
-                                 int64_t hidden, int64_t experts, int64_t inter, const void* peers, void* stream) {
+                                 int64_t hidden, int64_t local_experts, int64_t inter, const void* peers, void* stream) {
   QW_CHECK_ARG(recv_workspace && window && peers, "moe_ep_combine: null pointer");
   QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && rank >= 0 && rank < ranks && cap >= 1 &&
-                   experts % ranks == 0 && hidden % 8 == 0, "moe_ep_combine: shape");
-  const int Tr = static_cast<int>(ranks * cap), H = static_cast<int>(hidden), el = static_cast<int>(experts / ranks);
+                   local_experts >= 1 && local_experts <= 257 && hidden % 8 == 0, "moe_ep_combine: shape");
+  const int Tr = static_cast<int>(ranks * cap), H = static_cast<int>(hidden), el = static_cast<int>(local_experts);
   WsParts w = split_ws(const_cast<void*>(recv_workspace), Tr, H, el, static_cast<int>(inter), 1);
   const int grid = 2 * sm_count();
   QW_LAUNCH_PDL("moe ep combine", ep_combine_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
@@ -2222,16 +2254,14 @@ extern "C" int qw_moe_ep_combine(const void* recv_workspace, void* window, int64
 }
 
 extern "C" int qw_moe_ep_scatter(void* workspace, void* window, int64_t tokens, int64_t hidden, int64_t experts,
-                                 int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, void* stream) {
+                                 int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, int shared, void* stream) {
   QW_CHECK_ARG(workspace && window, "moe_ep_scatter: null pointer");
-  const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap);
+  const int st = ep_check(tokens, hidden, experts, top_k, ranks, cap, shared);
   if (st) return st;
   const int T = static_cast<int>(tokens), H = static_cast<int>(hidden), E = static_cast<int>(experts),
             k = static_cast<int>(top_k);
-  const RouteView rv = route_view(workspace, T, E, k);
   WsParts w = split_ws(workspace, T, H, E, static_cast<int>(inter), k);
-  QW_LAUNCH_PDL("moe ep scatter", ep_scatter_kernel, dim3(static_cast<unsigned>(T * k)), dim3(256), 0,
-                as_stream(stream), rv.topk_idx, window, T, H, k, static_cast<int>(ranks),
-                static_cast<int>(experts / ranks), static_cast<int>(cap), w.part);
+  QW_LAUNCH_PDL("moe ep scatter", ep_scatter_kernel, dim3(static_cast<unsigned>(cap)), dim3(256), 0,
+                as_stream(stream), window, T, H, k, static_cast<int>(ranks), static_cast<int>(cap), w.part);
   return QW_OK;
 }

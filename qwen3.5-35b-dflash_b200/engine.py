@@ -197,13 +197,12 @@ class TargetEngine:
             import torch.distributed as dist
             G, rank = dist.get_world_size(ep_group), dist.get_rank(ep_group)
             E = c.num_experts
-            self.ep_gu = [_ep.local_expert_streams(lw.gate_up, E, G, rank) if lw.gate_up is not None else None
-                          for lw in self.layers]
-            self.ep_dn = [_ep.local_expert_streams(lw.down, E, G, rank) if lw.down is not None else None
-                          for lw in self.layers]
             self.ep_moe = _ep.ExpertParallelMoE(ep_group, tokens=T, hidden=H, experts=E,
                                                 inter=c.moe_intermediate_size, top_k=c.num_experts_per_tok,
                                                 quant_group=c.quant_group, device=dev)
+            banks = [self.ep_moe.local_banks(lw.gate_up, lw.down, lw.shared_gu, lw.shared_down) for lw in self.layers]
+            self.ep_gu = [b[0] for b in banks]
+            self.ep_dn = [b[1] for b in banks]
         self.nblk = self.lib.qw_lmhead_blocks(self.vocab_pad)
         self.keys = torch.zeros(self.nblk, T, dtype=torch.int64, device=dev)
         self.top1 = torch.zeros(T, dtype=torch.int32, device=dev)
@@ -252,9 +251,9 @@ class TargetEngine:
         lib.check(getattr(self.lib, name)(*args), name)
 
     # kernels each entry point launches (all others launch one)
-    # (expert-parallel MoE layer: dispatch, shared expert 2, receive routing, gate/up +
-    # down of the received rows, combine, scatter)
-    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2, "qw_moe_ep": 8}
+    # (expert-parallel MoE layer: dispatch, receive routing, gate/up + down of the received
+    # rows, combine, scatter)
+    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2, "qw_moe_ep": 6}
 
     def launches_per_step(self) -> int:
         """Kernels of this library in the captured step (counted from the entry calls)."""
@@ -321,8 +320,7 @@ class TargetEngine:
             if self.ep_moe is not None:
                 if self._recording is not None:
                     self._recording["qw_moe_ep"] = self._recording.get("qw_moe_ep", 0) + 1
-                self.ep_moe.experts(self.normed, self.moe_ws, self.ep_gu[l], self.ep_dn[l], lw.shared_gu,
-                                    lw.shared_down)
+                self.ep_moe.experts(self.normed, self.moe_ws, self.ep_gu[l], self.ep_dn[l])
             else:
                 self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                            lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
@@ -379,7 +377,7 @@ class TargetEngine:
         c = self.cfg
         if self.ep_moe is not None:
             m = self.ep_moe
-            off = self.lib.qw_moe_active_experts(None, m.G * m.cap, m.el, 1)
+            off = self.lib.qw_moe_active_experts(None, m.G * m.cap, m.local, 1)
             return int(m.ws_r[off:off + 4].view(torch.int32).item())
         off = self.lib.qw_moe_active_experts(None, self.T, c.num_experts, c.num_experts_per_tok)
         return int(self.moe_ws[off:off + 4].view(torch.int32).item())

@@ -8,14 +8,14 @@ each rank routes its own tokens over all E experts (``qw_moe_route``), then
 ``qw_moe_experts_w4`` would on one GPU holding all experts:
 
 1. ``qw_moe_ep_dispatch``: each pair's activation row straight into the window of the
-   rank owning its expert (stores over NVLink from the kernel), then a flag;
-2. the shared expert on the rank's own tokens (``qw_moe_experts_w4_range`` with an empty
-   routed range) while the peers' rows arrive;
-3. ``qw_moe_ep_recv_route`` (waits for every rank's rows) + ``qw_moe_ep_experts``: the
+   rank owning its expert (stores over NVLink from the kernel), then a flag; the shared
+   expert is every rank's last local expert, and each token sends it one more row, to
+   its own rank, so it runs in the same expert launches as the routed pairs;
+2. ``qw_moe_ep_recv_route`` (waits for every rank's rows) + ``qw_moe_ep_experts``: the
    received rows through the rank's own experts;
-4. ``qw_moe_ep_combine``: the outputs straight into the source ranks' windows, then a
+3. ``qw_moe_ep_combine``: the outputs straight into the source ranks' windows, then a
    flag; ``qw_moe_ep_scatter`` (waits for every rank's outputs) into the per-(token,
-   slot) slots.
+   slot) slots (the shared expert's into slot k).
 
 ``qw_moe_combine`` / ``qw_moe_combine_norm`` then run unchanged.  The expert kernels give
 a row the same bits whatever else is in their launch and outputs travel as bf16 (the
@@ -60,13 +60,15 @@ class ExpertParallelMoE:
     is collective (every rank of the group, same arguments); so is ``close()``."""
 
     def __init__(self, group, *, tokens: int, hidden: int, experts: int, inter: int, top_k: int,
-                 quant_group: int, device):
+                 quant_group: int, device, shared: bool = True):
         self.group = group
         self.G = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.T, self.H, self.E, self.I, self.k, self.qg = tokens, hidden, experts, inter, top_k, quant_group
         self.lo, self.el = expert_range(experts, self.G, self.rank)
-        self.cap = tokens * top_k
+        self.shared = int(bool(shared))
+        self.local = self.el + self.shared          # local experts (the shared one last)
+        self.cap = tokens * (top_k + self.shared)
         self.device = torch.device(device)
         self.so = lib.load()
         so, G = self.so, self.G
@@ -92,7 +94,7 @@ class ExpertParallelMoE:
                 self._opened.append(peer.value)
                 ptrs.append(peer.value)
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
-        nbytes = so.qw_moe_ep_recv_workspace_bytes(G, self.cap, hidden, experts, inter)
+        nbytes = so.qw_moe_ep_recv_workspace_bytes(G, self.cap, hidden, self.local, inter)
         self.ws_r = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         dist.barrier(group=group)
 
@@ -109,29 +111,36 @@ class ExpertParallelMoE:
         lib.check(self.so.qw_ep_window_free(self.window), "ep window free")
         self.window = None
 
-    def experts(self, x: torch.Tensor, ws: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor,
-                shared_gate_up: torch.Tensor | None, shared_down: torch.Tensor | None):
-        """Routed + shared expert outputs of this rank's tokens ``x`` [tokens, hidden] (bf16)
-        into ``ws`` (a MoE workspace already routed by qw_moe_route / qw_moe_route_x) on the
-        current stream.  Every rank of the group calls it, with the same shapes, in the same
+    def local_banks(self, gate_up: torch.Tensor, down: torch.Tensor, shared_gate_up: torch.Tensor | None = None,
+                    shared_down: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """This rank's expert streams from full W4 banks (every expert's stream, equal sizes,
+        concatenated): its E/G routed experts, then the shared expert when it is exchanged."""
+        gu = local_expert_streams(gate_up, self.E, self.G, self.rank)
+        dn = local_expert_streams(down, self.E, self.G, self.rank)
+        if self.shared:
+            if shared_gate_up is None or shared_down is None:
+                raise ValueError("the shared expert's streams are needed (shared=True)")
+            gu = torch.cat([gu.view(-1), shared_gate_up.reshape(-1)])
+            dn = torch.cat([dn.view(-1), shared_down.reshape(-1)])
+        return gu, dn
+
+    def experts(self, x: torch.Tensor, ws: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor):
+        """Routed (and shared) expert outputs of this rank's tokens ``x`` [tokens, hidden]
+        (bf16) into ``ws`` (a MoE workspace already routed by qw_moe_route /
+        qw_moe_route_x), on the current stream; ``gate_up_local`` / ``down_local`` come from
+        ``local_banks``.  Every rank of the group calls it, with the same shapes, in the same
         order."""
         so = self.so
         st = torch.cuda.current_stream(x.device).cuda_stream
         T, H, E, I, k, g, G, cap = self.T, self.H, self.E, self.I, self.k, self.qg, self.G, self.cap
         if tuple(x.shape) != (T, H) or x.dtype != BF16:
             raise ValueError(f"x must be bf16 [{T}, {H}]")
-        sgu = shared_gate_up.data_ptr() if shared_gate_up is not None else None
-        sdn = shared_down.data_ptr() if shared_down is not None else None
-        win, peers = self.window, self.peers.data_ptr()
-        lib.check(so.qw_moe_ep_dispatch(ws.data_ptr(), x.data_ptr(), T, H, E, k, G, self.rank, cap, peers, win, st),
-                  "ep dispatch")
-        # the shared expert (no routed pairs) while the peers' rows arrive
-        lib.check(so.qw_moe_experts_w4_range(x.data_ptr(), gate_up_local.data_ptr(), down_local.data_ptr(),
-                                             sgu, sdn, T, H, E, I, k, g, 0, 0, ws.data_ptr(), st),
-                  "ep shared expert")
-        lib.check(so.qw_moe_ep_recv_route(win, G, cap, H, E, self.ws_r.data_ptr(), st), "ep receive routing")
-        lib.check(so.qw_moe_ep_experts(win, gate_up_local.data_ptr(), down_local.data_ptr(), G, cap, H, E, I, g,
+        win, peers, L, sh = self.window, self.peers.data_ptr(), self.local, self.shared
+        lib.check(so.qw_moe_ep_dispatch(ws.data_ptr(), x.data_ptr(), T, H, E, k, G, self.rank, cap, sh, peers, win,
+                                        st), "ep dispatch")
+        lib.check(so.qw_moe_ep_recv_route(win, G, cap, H, L, self.ws_r.data_ptr(), st), "ep receive routing")
+        lib.check(so.qw_moe_ep_experts(win, gate_up_local.data_ptr(), down_local.data_ptr(), G, cap, H, L, I, g,
                                        self.ws_r.data_ptr(), st), "ep local experts")
-        lib.check(so.qw_moe_ep_combine(self.ws_r.data_ptr(), win, G, self.rank, cap, H, E, I, peers, st),
+        lib.check(so.qw_moe_ep_combine(self.ws_r.data_ptr(), win, G, self.rank, cap, H, L, I, peers, st),
                   "ep combine")
-        lib.check(so.qw_moe_ep_scatter(ws.data_ptr(), win, T, H, E, I, k, G, cap, st), "ep scatter")
+        lib.check(so.qw_moe_ep_scatter(ws.data_ptr(), win, T, H, E, I, k, G, cap, sh, st), "ep scatter")

@@ -36,10 +36,9 @@ def _moe_cases(rank, world, so, cases):
         dn = w4.pack_w4(qdn.cuda(), sdn.cuda(), g)
         shgu = w4.pack_w4(qsgu.cuda(), ssgu.cuda(), g)
         shdn = w4.pack_w4(qsdn.cuda(), ssdn.cuda(), g)
-        gu_l = ep.local_expert_streams(gu, e, world, rank)
-        dn_l = ep.local_expert_streams(dn, e, world, rank)
         moe = ep.ExpertParallelMoE(dist.group.WORLD, tokens=t, hidden=h, experts=e, inter=inter, top_k=k,
                                    quant_group=g, device="cuda")
+        gu_l, dn_l = moe.local_banks(gu, dn, shgu, shdn)
         st = lib.stream_ptr()
         nbytes = so.qw_moe_workspace_bytes(t, h, e, inter, k)
         try:
@@ -60,7 +59,7 @@ def _moe_cases(rank, world, so, cases):
                 out2 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
                 lib.check(so.qw_moe_route(logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16,
                                           ws2.data_ptr(), st))
-                moe.experts(x, ws2, gu_l, dn_l, shgu, shdn)
+                moe.experts(x, ws2, gu_l, dn_l)
                 lib.check(so.qw_moe_combine(ws2.data_ptr(), out2.data_ptr(), 0, t, h, e, inter, k, 1, st))
                 lib.check(so.qw_check_wait_status(1, st), "ep waits")
                 if not torch.equal(out1, out2):

@@ -294,10 +294,12 @@ def test_paged_attention_layer_matches_oracle(cuda_lib, b, ctx):
 
 @pytest.mark.parametrize("t,g,e,inter", [(16, 128, 256, 512), (16, 32, 64, 256), (7, 64, 32, 256)])
 def test_moe_ep_kernels_one_rank_bit_identical(cuda_lib, t, g, e, inter):
-    """The expert-parallel kernels with one rank (the all-to-all is then the identity:
-    the send segments are the receive segments): pack, receive routing, the receiving
-    experts (the streaming kernels, over the cap + 1 rows of the segment), pack-out and
-    scatter must give the one-GPU MoE (the bulk kernels at 16 tokens) bit for bit."""
+    """The expert-parallel kernels with one rank (the window is its own peer, allocated
+    here as a plain device tensor) and the shared expert exchanged as local expert E:
+    dispatch, receive routing, the receiving experts (the streaming kernels over the
+    window's rows), combine and scatter must give the one-GPU MoE (the bulk kernels at 16
+    tokens) bit for bit, twice in a row (the epoch advances), and the window must hold the
+    protocol's rows and descriptors (oracle/ep_np.py)."""
     from qwen35_dflash_b200 import lib, w4
     from oracle import ep_np
     torch.manual_seed(t + g + e)
@@ -321,29 +323,37 @@ def test_moe_ep_kernels_one_rank_bit_identical(cuda_lib, t, g, e, inter):
              t, h, e, inter, k, g, ws1.data_ptr(), st)
     lib.call("qw_moe_combine", ws1.data_ptr(), out1.data_ptr(), 0, t, h, e, inter, k, 1, st)
 
-    cap = t * k
-    seg = torch.zeros(1, cap + 1, h, dtype=torch.bfloat16, device="cuda")
-    back = torch.zeros_like(seg)
-    ws_r = torch.zeros(cuda_lib.qw_moe_ep_recv_workspace_bytes(1, cap, h, e, inter), dtype=torch.uint8,
+    cap = t * (k + 1)                      # routed pairs + one shared-expert row per token
+    window = torch.zeros(cuda_lib.qw_ep_window_bytes(1, cap, h), dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([window.data_ptr()], dtype=torch.int64, device="cuda")
+    ws_r = torch.zeros(cuda_lib.qw_moe_ep_recv_workspace_bytes(1, cap, h, e + 1, inter), dtype=torch.uint8,
                        device="cuda")
-    ws2 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
-    out2 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
-    lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws2.data_ptr(), st)
-    lib.call("qw_moe_experts_w4_range", x.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(),
-             sdn.data_ptr(), t, h, e, inter, k, g, 0, 0, ws2.data_ptr(), st)
-    lib.call("qw_moe_ep_pack", ws2.data_ptr(), x.data_ptr(), t, h, e, k, 1, cap, seg.data_ptr(), st)
-    lib.call("qw_moe_ep_recv_route", seg.data_ptr(), 1, cap, h, e, ws_r.data_ptr(), st)
-    lib.call("qw_moe_ep_experts", seg.data_ptr(), gu.data_ptr(), dn.data_ptr(), 1, cap, h, e, inter, g,
-             ws_r.data_ptr(), st)
-    lib.call("qw_moe_ep_pack_out", ws_r.data_ptr(), seg.data_ptr(), 1, cap, h, e, inter, back.data_ptr(), st)
-    lib.call("qw_moe_ep_scatter", ws2.data_ptr(), back.data_ptr(), t, h, e, inter, k, 1, cap, st)
-    lib.call("qw_moe_combine", ws2.data_ptr(), out2.data_ptr(), 0, t, h, e, inter, k, 1, st)
-    torch.cuda.synchronize()
-    # the segment is the protocol's
-    topk = ws2[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
-    want = ep_np.pack(topk, x.cpu().view(torch.int16).numpy().view("uint16"), e, 1, cap)
-    got = seg.cpu().view(torch.int16).numpy().view("uint16")
-    assert (ep_np.header_words(got, cap) == ep_np.header_words(want, cap)).all()
-    assert (got[0, 1:] == want[0, 1:]).all()
-    if not torch.equal(out1, out2):
-        raise AssertionError(f"{(out1 != out2).sum().item()} elements differ")
+    gu_l, dn_l = torch.cat([gu.view(-1), sgu.view(-1)]), torch.cat([dn.view(-1), sdn.view(-1)])
+    for rep in range(2):
+        ws2 = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        out2 = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+        lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws2.data_ptr(), st)
+        lib.call("qw_moe_ep_dispatch", ws2.data_ptr(), x.data_ptr(), t, h, e, k, 1, 0, cap, 1, peers.data_ptr(),
+                 window.data_ptr(), st)
+        lib.call("qw_moe_ep_recv_route", window.data_ptr(), 1, cap, h, e + 1, ws_r.data_ptr(), st)
+        lib.call("qw_moe_ep_experts", window.data_ptr(), gu_l.data_ptr(), dn_l.data_ptr(), 1, cap, h, e + 1, inter, g,
+                 ws_r.data_ptr(), st)
+        lib.call("qw_moe_ep_combine", ws_r.data_ptr(), window.data_ptr(), 1, 0, cap, h, e + 1, inter,
+                 peers.data_ptr(), st)
+        lib.call("qw_moe_ep_scatter", ws2.data_ptr(), window.data_ptr(), t, h, e, inter, k, 1, cap, 1, st)
+        lib.call("qw_moe_combine", ws2.data_ptr(), out2.data_ptr(), 0, t, h, e, inter, k, 1, st)
+        lib.call("qw_check_wait_status", 1, st)
+        torch.cuda.synchronize()
+        # the window holds the protocol's rows and descriptors
+        words = window.view(torch.int32).cpu().numpy()
+        assert words[0] == rep + 1                                    # epoch of the finished exchange
+        topk = ws2[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
+        rows_w, meta_w, count_w = ep_np.dispatch(topk, x.cpu().view(torch.int16).numpy().view("uint16"), e, 1, 0,
+                                                 shared=True)[0]
+        assert words[64 + 128] == count_w == cap                       # count[0]
+        assert (words[256:256 + count_w] == meta_w[:count_w]).all()   # meta [1][cap] at byte 1024
+        rows_off = 1024 + (cap * 4 + 255) // 256 * 256
+        got = window[rows_off: rows_off + cap * h * 2].view(torch.int16).cpu().numpy().view("uint16").reshape(cap, h)
+        assert (got[:count_w] == rows_w[:count_w]).all()
+        if not torch.equal(out1, out2):
+            raise AssertionError(f"rep {rep}: {(out1 != out2).sum().item()} elements differ")
