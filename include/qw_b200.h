@@ -250,12 +250,15 @@ int qw_moe_experts_w4_range(const void* x, const void* gate_up, const void* down
  *                         received (top-1 = their local expert) into a workspace of
  *                         qw_moe_ep_recv_workspace_bytes;
  *   qw_moe_ep_experts     this rank's experts over those rows (gate_up_local /
- *                         down_local: the streams of its experts only);
- *   qw_moe_ep_combine     the outputs as bf16 into their source ranks' windows, then a
- *                         release flag in every window;
- *   qw_moe_ep_scatter     waits (bounded) for every rank's combine, writes the returned
+ *                         down_local: the streams of its experts only); the down
+ *                         projection's epilogue stores the outputs, as bf16, into their
+ *                         source ranks' windows and raises a release flag in every
+ *                         window (the combine half of the exchange, inside the kernel);
+ *   qw_moe_ep_scatter     waits (bounded) for every rank's results, writes the returned
  *                         rows into the routing's per-(token, slot) outputs for
- *                         qw_moe_combine(_norm), and closes the exchange.
+ *                         qw_moe_combine(_norm), and closes the exchange -- or
+ *   qw_moe_ep_combine_norm  does the combine + next RMSNorm reading the returned rows
+ *                         directly (waits, then closes the exchange).
  * With shared = 1 the shared expert travels the same way: every rank holds it as local
  * expert E/G, after its routed experts (gate_up_local / down_local carry E/G + 1
  * experts), and each token sends it one more row, to its own rank.  local_experts =
@@ -278,13 +281,18 @@ int qw_moe_ep_dispatch(const void* workspace, const void* x, int64_t tokens, int
                        int shared, const void* peers, void* window, void* stream);
 int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts,
                          void* recv_workspace, void* stream);
-int qw_moe_ep_experts(const void* window, const void* gate_up_local, const void* down_local,
-                      int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts, int64_t inter,
-                      int32_t group, void* recv_workspace, void* stream);
-int qw_moe_ep_combine(const void* recv_workspace, void* window, int64_t ranks, int64_t rank, int64_t cap,
-                      int64_t hidden, int64_t local_experts, int64_t inter, const void* peers, void* stream);
+int qw_moe_ep_experts(void* window, const void* gate_up_local, const void* down_local, int64_t ranks,
+                      int64_t rank, int64_t cap, int64_t hidden, int64_t local_experts, int64_t inter,
+                      int32_t group, const void* peers, void* recv_workspace, void* stream);
 int qw_moe_ep_scatter(void* workspace, void* window, int64_t tokens, int64_t hidden, int64_t experts,
                       int64_t inter, int64_t top_k, int64_t ranks, int64_t cap, int shared, void* stream);
+/* qw_moe_combine_norm reading the expert outputs straight from the window (the returned
+ * bf16 rows) instead of the workspace: waits (bounded) for every rank's results, then
+ * closes the exchange (in place of qw_moe_ep_scatter + qw_moe_combine_norm). */
+int qw_moe_ep_combine_norm(void* workspace, void* window, int64_t ranks, int64_t cap, void* hidden,
+                           int64_t tokens, int64_t hidden_dim, int64_t experts, int64_t inter,
+                           int64_t top_k, int has_shared, const void* gamma, void* normed, float eps,
+                           void* tap, int64_t ldf, int tap_normed, void* stream);
 
 /* Byte offset, inside a MoE workspace, of the int32 count of active routed experts
  * (valid after qw_moe_route_lists or an expert entry point; for measuring the experts

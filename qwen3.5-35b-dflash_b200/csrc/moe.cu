@@ -1269,6 +1269,462 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   cp_async_wait<0>();
 }
 
+// ------------------------------------------------------------------ expert-parallel window
+// (the exchange itself is described with its kernels at the end of this file)
+constexpr int EP_MAX_RANKS = 64;
+constexpr long long EP_PEER_WAIT_LIMIT = 1ll << 34;   // cycles (~9 s): a peer's host may lag in eager use
+
+struct EpWin {
+  int32_t* hdr;
+  int32_t* dflag;
+  int32_t* cflag;
+  int32_t* count;
+  int32_t* meta;
+  __nv_bfloat16* rows;
+  __nv_bfloat16* back;
+};
+
+__host__ __device__ inline int64_t ep_window_bytes(int G, int cap, int H) {
+  int64_t off = 1024;
+  off += align256(static_cast<int64_t>(G) * cap * 4);
+  off += align256(static_cast<int64_t>(G) * cap * H * 2);
+  off += align256(static_cast<int64_t>(cap) * H * 2);
+  return off;
+}
+
+__host__ __device__ inline EpWin ep_win(const void* base, int G, int cap, int H) {
+  uint8_t* p = static_cast<uint8_t*>(const_cast<void*>(base));
+  EpWin w;
+  w.hdr = reinterpret_cast<int32_t*>(p);
+  w.dflag = reinterpret_cast<int32_t*>(p + 256);
+  w.cflag = w.dflag + EP_MAX_RANKS;
+  w.count = w.cflag + EP_MAX_RANKS;
+  int64_t off = 1024;
+  w.meta = reinterpret_cast<int32_t*>(p + off);
+  off += align256(static_cast<int64_t>(G) * cap * 4);
+  w.rows = reinterpret_cast<__nv_bfloat16*>(p + off);
+  off += align256(static_cast<int64_t>(G) * cap * H * 2);
+  w.back = reinterpret_cast<__nv_bfloat16*>(p + off);
+  return w;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait (one thread) until a peer has raised *flag to `want`.  On expiry -- or
+// when an earlier wait of this window expired (hdr[4]) -- records the timeout in the
+// sticky status and returns false, so a lost peer costs one limit, not one per wait.
+__device__ bool ep_wait_flag(const int32_t* flag, int want, int32_t* hdr) {
+  if (ld_acquire_sys(flag) >= want) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_sys(flag) < want) {
+    if (*reinterpret_cast<volatile int32_t*>(hdr + 4) != 0 || clock64() - t0 > EP_PEER_WAIT_LIMIT) {
+      atomicOr(&g_moe_wait_status, QW_DEVICE_TIMEOUT);
+      *reinterpret_cast<volatile int32_t*>(hdr + 4) = 1;
+      return false;
+    }
+    __nanosleep(100);
+  }
+  return true;
+}
+
+// The CTA that finishes last (ticket wraps to 0 for the next launch).  The CTA barrier
+// orders every thread's stores before thread 0's system-scope fence, which precedes
+// its ticket; the last CTA's thread 0 fences again after taking the last ticket, and
+// then alone stores the flags (with release), so every CTA's stores happen before them.
+__device__ __forceinline__ bool ep_last_cta(int32_t* ticket) {
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicInc(reinterpret_cast<unsigned*>(ticket), gridDim.x - 1) == gridDim.x - 1;
+    if (s_last) __threadfence_system();
+  }
+  __syncthreads();
+  return s_last != 0;
+}
+
+// ------------------------------------------------------------------ grouped bulk kernels
+// The bulk-copy gate/up and down kernels for any number of tokens (T > 16, and the rows an
+// expert-parallel rank receives): the expert lists come from the routing workspace
+// (qw_moe_route_lists or the receive routing), and an expert's tokens are taken in
+// chunks of at most 16.  Work is cut into items of whole weight-tile groups of one
+// (expert slot, token chunk) "segment"; a CTA takes a contiguous range of items and
+// stages a segment's activation rows in shared memory once, when the segment changes.
+// Per row tile and token the MMA sequence and the epilogue are those of the bulk
+// kernels, so every output has their bits.
+constexpr int GR_CHUNK = 16;          // tokens per segment, at most
+// dynamic shared memory of the grouped kernels, at most: the CTA limit less room for the
+// few bytes of static shared memory the expert-parallel epilogue uses
+constexpr size_t GR_SMEM_LIMIT = 227 * 1024 - 256;
+constexpr int GR_MAX_SLOTS = 1 + 512;  // shared expert + active experts
+
+// Segment table in shared memory: for every slot its pair count and the first item of
+// each slot, so an item index maps to (slot, chunk, tile block) by a binary search.
+struct GrTable {
+  int nslots, total;          // slots, items (or units) in all
+  int first[GR_MAX_SLOTS + 1];  // first item of slot s; first[nslots] = total
+};
+
+template <typename ET>
+__device__ __forceinline__ int gr_pairs(const MoeArgs<ET>& a, const RouteView& rv, int slot) {
+  if (a.has_shared && slot == 0) return a.T;
+  const int ai = slot - a.has_shared;
+  return rv.pair_off[ai + 1] - rv.pair_off[ai];
+}
+
+// Every thread: the table with `per` items per (slot, chunk).
+template <typename ET>
+__device__ void gr_build_table(GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int per) {
+  if (threadIdx.x == 0) {
+    const int ns = a.has_shared + *rv.n_active;
+    int acc = 0;
+    for (int sl = 0; sl < ns; ++sl) {
+      tb.first[sl] = acc;
+      acc += (gr_pairs(a, rv, sl) + GR_CHUNK - 1) / GR_CHUNK * per;
+    }
+    tb.first[ns] = acc;
+    tb.nslots = ns;
+    tb.total = acc;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ int gr_slot_of(const GrTable& tb, int item) {
+  int lo = 0, hi = tb.nslots - 1;   // the last slot whose first item <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tb.first[mid] <= item) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Segment of item `item`: slot, chunk, item within the (slot, chunk), the weights, the
+// segment's token count and the base of its pair list (-1: identity, shared expert).
+template <typename ET>
+__device__ __forceinline__ void gr_item(const GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int item,
+                                        int per, bool up, int& slot, int& chunk, int& sub, const uint8_t*& w,
+                                        int& np, int& pbase) {
+  slot = gr_slot_of(tb, item);
+  const int r = item - tb.first[slot];
+  chunk = r / per;
+  sub = r % per;
+  const int npairs = gr_pairs(a, rv, slot);
+  np = min(GR_CHUNK, npairs - chunk * GR_CHUNK);
+  if (a.has_shared && slot == 0) {
+    w = up ? a.sgu : a.sdn;
+    pbase = -1;
+  } else {
+    const int ai = slot - a.has_shared;
+    const int e = rv.active[ai];
+    w = up ? a.gu + e * a.gu_stride : a.dn + e * a.dn_stride;
+    pbase = rv.pair_off[ai];
+  }
+}
+
+// Gate/up.  Item = (slot, chunk, block of XT_UP_WARPS intermediate tiles): warp w takes
+// tile block * XT_UP_WARPS + w (I / 16 a multiple of the warp count).
+template <int G>
+__global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_grouped_kernel(XtArgs args) {
+  using Fmt = W4Fmt<G>;
+  const MoeArgs<__nv_bfloat16>& a = args.m;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  GrTable& tb = *reinterpret_cast<GrTable*>(smem + XT_BAR_BYTES);
+  const int H = a.H, I = a.I;
+  const int XS = H + XT_PAD;
+  const int nch = H / G, cps = nch < XT_UP_CPS ? nch : XT_UP_CPS;
+  __half* xs = reinterpret_cast<__half*>(smem + XT_BAR_BYTES + (sizeof(GrTable) + 127) / 128 * 128);
+  float* xsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) +
+                                         ((static_cast<size_t>(GR_CHUNK) * XS * 2 + 127) / 128) * 128);
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(xsum) + ((static_cast<size_t>(GR_CHUNK) * nch * 4 + 127) / 128) * 128;
+  const uint32_t sbytes = cps * Fmt::CHB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
+  if (lane == 0)
+    for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
+  fence_barrier_init();
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  pdl_wait();   // the lists (and the received rows) come from the predecessor
+  pdl_trigger();
+  const int J = I / 16, per = J / XT_UP_WARPS;
+  gr_build_table(tb, a, rv, per);
+  const int n_items = tb.total;
+  const int i0 = static_cast<int>(static_cast<int64_t>(n_items) * blockIdx.x / gridDim.x);
+  const int i1 = static_cast<int>(static_cast<int64_t>(n_items) * (blockIdx.x + 1) / gridDim.x);
+  const int hc = cps / 2, spu = nch / hc;
+  const uint32_t hbytes = hc * Fmt::CHB;
+  const int64_t tbytes = Fmt::tile_offset(1, H, 0);
+  const int Q = (i1 - i0) * spu;
+  // lane 0's copy cursor over this warp's units (one per item)
+  int cu_i = i0, cu_s = 0;
+  const uint8_t* cu_w = nullptr;
+  auto cursor_unit = [&]() {
+    int sl, ch, sub, np_, pb_;
+    gr_item(tb, a, rv, cu_i, per, true, sl, ch, sub, cu_w, np_, pb_);
+    cu_w += Fmt::tile_offset(sub * XT_UP_WARPS + warp, H, 0);
+  };
+  auto issue_next = [&](int qq) {
+    ring.issue2(qq, cu_w + cu_s * hbytes, cu_w + J * tbytes + cu_s * hbytes, hbytes);
+    if (++cu_s == spu) {
+      cu_s = 0;
+      if (++cu_i < i1) cursor_unit();
+    }
+  };
+  if (lane == 0 && i1 > i0) {
+    cursor_unit();
+    for (int qq = 0; qq < XT_NST && qq < Q; ++qq) issue_next(qq);
+  }
+  const int gid = lane >> 2, tig = lane & 3;
+  int q = 0, seg_slot = -1, seg_chunk = -1;
+  bool ok = true;
+  for (int it = i0; it < i1; ++it) {
+    int sl, ch, sub, np, pb;
+    const uint8_t* w;
+    gr_item(tb, a, rv, it, per, true, sl, ch, sub, w, np, pb);
+    if (sl != seg_slot || ch != seg_chunk) {
+      // a new segment: its rows as fp16 and their group sums (after every warp is done
+      // with the previous segment's)
+      __syncthreads();
+      for (int i = threadIdx.x; i < np * (H / 8); i += blockDim.x) {
+        const int r = i / (H / 8), c = (i % (H / 8)) * 8;
+        const int pi = ch * GR_CHUNK + r;
+        const int tok = pb < 0 ? pi : rv.pair_tok[pb + pi];
+        cp_async16(xs + r * XS + c, a.x + static_cast<int64_t>(tok) * H + c, true);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      if (H % 256 == 0) {
+        for (int i = threadIdx.x; i < np * (H / 8); i += blockDim.x) {
+          const int r = i / (H / 8), sg = i % (H / 8);
+          uint4* p = reinterpret_cast<uint4*>(xs + r * XS + sg * 8);
+          const uint4 v = bf16x8_to_f16x8(*p);
+          *p = v;
+          const float xg = warp_group_xsum_f16<G>(sum8_f16(v), lane);
+          if (sg % (G / 8) == 0) xsum[r * nch + sg / (G / 8)] = xg;
+        }
+        __syncthreads();
+      } else {
+        for (int i = threadIdx.x; i < np * (H / 8); i += blockDim.x) {
+          uint4* p = reinterpret_cast<uint4*>(xs + (i / (H / 8)) * XS + (i % (H / 8)) * 8);
+          *p = bf16x8_to_f16x8(*p);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < np * nch; i += blockDim.x)
+          xsum[i] = group_xsum_f16<G>(xs + (i / nch) * XS + (i % nch) * G);
+        __syncthreads();
+      }
+      seg_slot = sl;
+      seg_chunk = ch;
+    }
+    if (!ok) continue;   // a warp that timed out still takes part in the segment barriers
+    const int j = sub * XT_UP_WARPS + warp;
+    const bool two = np > 8;
+    const __half* xr[2];
+    const float* xq[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      xr[nt] = xs + min(nt * 8 + gid, np - 1) * XS;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) xq[nt][e] = xsum + min(nt * 8 + 2 * tig + e, np - 1) * nch;
+    }
+    float accg[2][4], accu[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) accg[nt][r] = accu[nt][r] = 0.f;
+    for (int s = 0; s < spu; ++s, ++q) {
+      if (!ring.wait(q, args.status)) {
+        if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
+        ok = false;
+        break;
+      }
+      const uint8_t* st = ring.stage(q);
+      for (int c = 0; c < hc; ++c)
+        w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[0], (s * hc + c) * G, xq[0][0], xq[0][1],
+                         s * hc + c, lane, accg[0], accu[0]);
+      if (two)
+        for (int c = 0; c < hc; ++c)
+          w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[1], (s * hc + c) * G, xq[1][0],
+                           xq[1][1], s * hc + c, lane, accg[1], accu[1]);
+      __syncwarp();
+      if (lane == 0 && q + XT_NST < Q) issue_next(q + XT_NST);
+    }
+    if (!ok) continue;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int tl = frag_tok(lane, nt, r);
+        if (tl < np) {
+          const float gr = rbf(accg[nt][r]), ur = rbf(accu[nt][r]);
+          const float h = rbf(rbf(silu_f(gr)) * ur);
+          const int pi = ch * GR_CHUNK + tl;
+          const int64_t hrow = pb < 0 ? static_cast<int64_t>(a.T) * a.k + pi : pb + pi;
+          reinterpret_cast<__half*>(a.hbuf)[hrow * I + j * 16 + frag_row(lane, r)] = __float2half_rn(h);
+        }
+      }
+  }
+}
+
+// Where an expert-parallel rank's down projection sends its results: row r of the
+// receiving routing came from rank r / cap (window meta[r] = (pair << 9) | expert); its
+// output goes, as bf16, to row `pair` of that rank's `back`.
+struct EpSend {
+  void* window;                      // this rank's window (null: plain f32 outputs)
+  const unsigned long long* peers;   // every rank's window
+  int G, rank, cap;
+};
+
+// Down.  Unit = (slot, chunk, block of XT_DN_WARPS * spw row tiles), as in the bulk down
+// kernel; units go to CTAs round-robin and the unit's h rows are staged per unit.  With
+// an EpSend window the unit's outputs are rounded to bf16 (the precision the combine
+// reads), gathered in shared memory and stored with 16-byte stores straight into the
+// source ranks' windows; the last CTA then raises this rank's combine flag in every
+// window.
+template <int G, bool EP>
+__global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(XtArgs args, int tiles_per_stage,
+                                                                            int stages_per_warp, EpSend ep) {
+  using Fmt = W4Fmt<G>;
+  const MoeArgs<__nv_bfloat16>& a = args.m;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  GrTable& tb = *reinterpret_cast<GrTable*>(smem + XT_BAR_BYTES);
+  const int H = a.H, I = a.I, T = a.T;
+  const int HS = I + XT_PAD;
+  __half* hs = reinterpret_cast<__half*>(smem + XT_BAR_BYTES + (sizeof(GrTable) + 127) / 128 * 128);
+  const size_t hbytes = ((static_cast<size_t>(GR_CHUNK) * HS * 2 + 127) / 128) * 128;
+  const int cpt = I / G;
+  const int tps = tiles_per_stage, spw = stages_per_warp;
+  const uint32_t sbytes = tps * cpt * Fmt::CHB;
+  const int rb_tiles = XT_DN_WARPS * spw * tps;
+  // EP: the unit's bf16 outputs [GR_CHUNK][rb_tiles * 16 (+8)] before they leave
+  const int OS = rb_tiles * 16 + 8;
+  __nv_bfloat16* osm = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(hs) + 3 * hbytes);
+  const size_t obytes = EP ? ((static_cast<size_t>(GR_CHUNK) * OS * 2 + 127) / 128) * 128 : 0;
+  uint8_t* ring_base = reinterpret_cast<uint8_t*>(hs) + 3 * hbytes + obytes;
+  const int nrb = (H / 16) / rb_tiles;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  WarpRing<XT_NST> ring{ring_base + warp * XT_NST * sbytes, bars + warp * XT_NST, sbytes, args.limit};
+  if (lane == 0)
+    for (int i = 0; i < XT_NST; ++i) mbar_init(ring.bar + i, 1);
+  fence_barrier_init();
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  pdl_wait();   // h comes from the predecessor (gate/up); the lists from earlier kernels
+  pdl_trigger();
+  gr_build_table(tb, a, rv, nrb);
+  const int nu = tb.total;
+  const int my_units = blockIdx.x < nu ? (nu - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int Q = my_units * spw;
+  auto src = [&](int q) -> const uint8_t* {
+    const int u = blockIdx.x + (q / spw) * gridDim.x, l = q % spw;
+    int sl, ch, sub, np, pb;
+    const uint8_t* w;
+    gr_item(tb, a, rv, u, nrb, false, sl, ch, sub, w, np, pb);
+    const int tile = sub * rb_tiles + (warp * spw + l) * tps;
+    return w + Fmt::tile_offset(tile, I, 0);
+  };
+  if (lane == 0)
+    for (int q = 0; q < XT_NST && q < Q; ++q) ring.issue(q, src(q), sbytes);
+  auto stage_h = [&](int i) {
+    const int u = blockIdx.x + i * gridDim.x;
+    int sl, ch, sub, np, pb;
+    const uint8_t* w;
+    gr_item(tb, a, rv, u, nrb, false, sl, ch, sub, w, np, pb);
+    const int64_t hb = (pb < 0 ? static_cast<int64_t>(T) * a.k : pb) + ch * GR_CHUNK;
+    __half* dst = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(hs) + (i % 3) * hbytes);
+    const __half* hsrc = reinterpret_cast<const __half*>(a.hbuf);
+    for (int e = threadIdx.x; e < np * (I / 8); e += blockDim.x) {
+      const int r = e / (I / 8), c = (e % (I / 8)) * 8;
+      cp_async16(dst + r * HS + c, hsrc + (hb + r) * I + c, true);
+    }
+  };
+  if (my_units > 0) stage_h(0);
+  cp_async_commit();
+  const int gid = lane >> 2;
+  int q = 0;
+  bool ok = true;
+  for (int i = 0; i < my_units; ++i) {
+    if (i + 1 < my_units) stage_h(i + 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int u = blockIdx.x + i * gridDim.x;
+    int sl, ch, sub, np, pb;
+    const uint8_t* w;
+    gr_item(tb, a, rv, u, nrb, false, sl, ch, sub, w, np, pb);
+    const bool two = np > 8;
+    const __half* hbuf_s = reinterpret_cast<const __half*>(reinterpret_cast<const uint8_t*>(hs) + (i % 3) * hbytes);
+    const __half* xr[2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) xr[nt] = hbuf_s + min(nt * 8 + gid, np - 1) * HS;
+    for (int l = 0; l < spw && ok; ++l, ++q) {
+      if (!ring.wait(q, args.status)) {
+        if (lane == 0) ring.drain(q + 1, min(q + XT_NST, Q));
+        ok = false;
+        break;
+      }
+      const uint8_t* st = ring.stage(q);
+      for (int t = 0; t < tps; ++t) {
+        float acc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        w4_smem_run<G>(st + t * cpt * Fmt::CHB, cpt, xr, 0, lane, two, acc);
+        const int row0 = (sub * rb_tiles + (warp * spw + l) * tps + t) * 16;
+        const int lrow0 = ((warp * spw + l) * tps + t) * 16;   // within the unit
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int tl = frag_tok(lane, nt, r);
+            if (tl < np) {
+              if constexpr (EP) {
+                osm[tl * OS + lrow0 + frag_row(lane, r)] = __float2bfloat16_rn(acc[nt][r]);
+              } else {
+                const int pi = ch * GR_CHUNK + tl;
+                int tok, slot;
+                if (pb < 0) { tok = pi; slot = a.k; }
+                else { tok = rv.pair_tok[pb + pi]; slot = rv.pair_slot[pb + pi]; }
+                a.part[(static_cast<int64_t>(tok) * (a.k + 1) + slot) * H + row0 + frag_row(lane, r)] = acc[nt][r];
+              }
+            }
+          }
+      }
+      __syncwarp();
+      if (lane == 0 && q + XT_NST < Q) ring.issue(q + XT_NST, src(q + XT_NST), sbytes);
+    }
+    if constexpr (EP) {
+      // the unit's rows to their sources: row tl of the unit is the received row
+      // pair_tok[pb + ch * 16 + tl] (no shared slot on the receiving side)
+      __syncthreads();
+      const int vec = rb_tiles * 16 / 8;   // 16-byte vectors per output row
+      for (int i = threadIdx.x; i < np * vec; i += blockDim.x) {
+        const int tl = i / vec, c = (i % vec) * 8;
+        const int r = rv.pair_tok[pb + ch * GR_CHUNK + tl];
+        const int srcr = r / ep.cap;
+        const int pair = __ldcg(ep_win(ep.window, ep.G, ep.cap, H).meta + r) >> 9;
+        __nv_bfloat16* to = ep_win(reinterpret_cast<const void*>(ep.peers[srcr]), ep.G, ep.cap, H).back +
+                            static_cast<int64_t>(pair) * H + sub * rb_tiles * 16 + c;
+        *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(osm + tl * OS + c);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if constexpr (EP) {
+    const EpWin me = ep_win(ep.window, ep.G, ep.cap, H);
+    const int epoch = me.hdr[0] + 1;
+    if (ep_last_cta(me.hdr + 2) && threadIdx.x == 0)
+      for (int g = 0; g < ep.G; ++g)
+        st_release_sys(ep_win(reinterpret_cast<const void*>(ep.peers[g]), ep.G, ep.cap, H).cflag + ep.rank, epoch);
+  }
+}
+
 // Combine (fused/model.py:296-307 with fused_ops.py:165-172): per token, the routed
 // experts in ascending id, each raw output rounded to the activation dtype, times its
 // weight (rounded), added with a rounding; then + round(round(shared) * gate) when a
@@ -1310,11 +1766,21 @@ __global__ void moe_combine_kernel(const float* __restrict__ part, void* ws, ET*
 // expert outputs, all k + 1 slots of a run issued before the ordered sum).
 constexpr int CN_THREADS = 512;
 
+// Expert-parallel form (ep.window set): the expert outputs are the bf16 rows the expert
+// owners stored into this rank's window (routed pair p = t k + s at back row p, the
+// shared expert's at row T k + t) -- the values the f32 path rounds to bf16 first, so the
+// sums have the same bits; every CTA waits (bounded) for every rank's combine flag
+// first, and the last CTA closes the exchange.
+struct EpRecv {
+  void* window;   // null: the f32 outputs of the workspace
+  int G, cap;
+};
+
 template <int KMAX>
 __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     const float* __restrict__ part, void* ws, __nv_bfloat16* __restrict__ hidden, int T, int H, int E, int k,
     int has_shared, const __nv_bfloat16* __restrict__ gamma, __nv_bfloat16* __restrict__ normed, float eps,
-    __nv_bfloat16* __restrict__ tap, int64_t ldf, int tap_normed) {
+    __nv_bfloat16* __restrict__ tap, int64_t ldf, int tap_normed, EpRecv ep) {
   __shared__ int s_slot[KMAX];
   __shared__ float s_w[KMAX];
   __shared__ float red[32];
@@ -1340,15 +1806,36 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
   }
   pdl_wait();
   pdl_trigger();
+  __shared__ int s_epoch;
+  EpWin me{};
+  if (ep.window) {
+    me = ep_win(ep.window, ep.G, ep.cap, H);
+    if (threadIdx.x == 0) s_epoch = me.hdr[0] + 1;
+    __syncthreads();
+    if (threadIdx.x < ep.G) ep_wait_flag(me.cflag + threadIdx.x, s_epoch, me.hdr);
+  }
   __syncthreads();
   const float* pt = part + static_cast<int64_t>(t) * (k + 1) * H;
   float ss = 0.f;
+  auto back4 = [&](int64_t row, int c) {
+    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(me.back + row * H + c));
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  };
   for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
     float4 y[KMAX + 1];
+    if (ep.window) {
 #pragma unroll
-    for (int j = 0; j < KMAX; ++j)
-      if (j < k) y[j] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(s_slot[j]) * H + c);
-    if (has_shared) y[KMAX] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(k) * H + c);
+      for (int j = 0; j < KMAX; ++j)
+        if (j < k) y[j] = back4(static_cast<int64_t>(t) * k + s_slot[j], c);
+      if (has_shared) y[KMAX] = back4(static_cast<int64_t>(T) * k + t, c);
+    } else {
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (j < k) y[j] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(s_slot[j]) * H + c);
+      if (has_shared) y[KMAX] = *reinterpret_cast<const float4*>(pt + static_cast<int64_t>(k) * H + c);
+    }
     const uint2 hraw = one ? h0 : *reinterpret_cast<const uint2*>(h + c);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -1399,6 +1886,7 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
       *reinterpret_cast<uint2*>(tap + static_cast<int64_t>(t) * ldf + c) = tap_normed ? yraw : hraw;
     }
   }
+  if (ep.window && ep_last_cta(me.hdr + 3) && threadIdx.x == 0) me.hdr[0] = s_epoch;
 }
 
 // Router logits of the fused-ops operator: dense [E, H] weights, one warp per (t, e),
@@ -1489,6 +1977,7 @@ struct XtPlan {
   bool up_ok, down_ok;
   int down_tps, down_spw;
   size_t up_smem, down_smem;
+  size_t down_ep_smem;   // grouped down kernel with the expert-parallel send
 };
 
 template <int G>
@@ -1543,21 +2032,88 @@ static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p,
   return QW_OK;
 }
 
+// Shapes the grouped kernels take: I / 16 a multiple of the gate/up warp count and the
+// bulk down kernel's stage geometry.
+template <int G>
+static bool grouped_plan(const MoeArgs<__nv_bfloat16>& a, XtPlan& p) {
+  constexpr int CHB = W4Fmt<G>::CHB;
+  const int nch = a.H / G;
+  const int cps = nch < XT_UP_CPS ? nch : XT_UP_CPS;
+  if ((a.I / 16) % XT_UP_WARPS || a.H % 8 || nch % cps || cps % 2 || (reinterpret_cast<uintptr_t>(a.x) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.hbuf) & 15) || a.has_shared + a.e_cnt > GR_MAX_SLOTS)
+    return false;
+  const size_t head = XT_BAR_BYTES + (sizeof(GrTable) + 127) / 128 * 128;
+  p.up_smem = head + (static_cast<size_t>(GR_CHUNK) * (a.H + XT_PAD) * 2 + 127) / 128 * 128 +
+              (static_cast<size_t>(GR_CHUNK) * nch * 4 + 127) / 128 * 128 +
+              static_cast<size_t>(XT_UP_WARPS) * XT_NST * cps * CHB;
+  const int cpt = a.I / G;
+  if (cpt < 1 || cpt > XT_DN_CPS || XT_DN_CPS % cpt) return false;
+  p.down_tps = XT_DN_CPS / cpt;
+  const int tiles = a.H / 16;
+  p.down_spw = 0;
+  for (int spw = 2; spw >= 1; --spw)
+    if (tiles % (XT_DN_WARPS * spw * p.down_tps) == 0) { p.down_spw = spw; break; }
+  p.down_smem = head + 3 * ((static_cast<size_t>(GR_CHUNK) * (a.I + XT_PAD) * 2 + 127) / 128 * 128) +
+                static_cast<size_t>(XT_DN_WARPS) * XT_NST * p.down_tps * cpt * CHB;
+  if (p.down_spw > 0) {   // room for the expert-parallel output tile
+    const int rb = XT_DN_WARPS * p.down_spw * p.down_tps * 16;
+    p.down_ep_smem = p.down_smem + (static_cast<size_t>(GR_CHUNK) * (rb + 8) * 2 + 127) / 128 * 128;
+  }
+  return p.down_spw > 0 && p.up_smem <= GR_SMEM_LIMIT && p.down_smem <= GR_SMEM_LIMIT;
+}
+
+template <int G>
+static int launch_experts_grouped(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p, cudaStream_t s, bool up,
+                                  bool down, int32_t* status, const EpSend* ep = nullptr) {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(moe_up_grouped_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(GR_SMEM_LIMIT));
+    if (err == cudaSuccess)
+      err = cudaFuncSetAttribute(moe_down_grouped_kernel<G, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(GR_SMEM_LIMIT));
+    if (err == cudaSuccess)
+      err = cudaFuncSetAttribute(moe_down_grouped_kernel<G, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(GR_SMEM_LIMIT));
+  });
+  if (err != cudaSuccess) return cuda_status(err, "moe grouped smem attribute");
+  const WaitInjection inj = wait_injection();
+  XtArgs xa{a, status, inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT};
+  const int grid = sm_count();
+  if (up) {
+    QW_LAUNCH_PDL("moe up (grouped)", moe_up_grouped_kernel<G>, dim3(grid), dim3(XT_UP_WARPS * 32), p.up_smem, s, xa);
+  }
+  if (down && ep) {
+    if (p.down_ep_smem > GR_SMEM_LIMIT) return fail(QW_ERR_UNSUPPORTED, "moe_ep_experts: output tile does not fit");
+    QW_LAUNCH_PDL("moe down (grouped, ep send)", moe_down_grouped_kernel<G, true>, dim3(grid), dim3(XT_DN_WARPS * 32),
+                  p.down_ep_smem, s, xa, p.down_tps, p.down_spw, *ep);
+  } else if (down) {
+    QW_LAUNCH_PDL("moe down (grouped)", moe_down_grouped_kernel<G, false>, dim3(grid), dim3(XT_DN_WARPS * 32),
+                  p.down_smem, s, xa, p.down_tps, p.down_spw, EpSend{});
+  }
+  return QW_OK;
+}
+
 template <int G>
 static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bool up, bool down,
-                             bool lists_ready) {
+                             bool lists_ready, const EpSend* ep = nullptr) {
   const XtPlan p = xt_plan<G>(a);
   int32_t* status = nullptr;
   const int src = moe_wait_status_addr(&status);
   if (src != QW_OK) return src;
   // the bulk pair keeps h (the down input) in fp16, the streaming pair in bf16: both
   // halves of one MoE always come from the same pair
-  if (p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);
-  // the streaming kernels read the lists from the workspace (built once, before gate/up)
+  if (!ep && p.up_ok && p.down_ok) return launch_experts_bulk<G>(a, p, s, up, down, status);
+  // the grouped and streaming kernels read the lists from the workspace (built once,
+  // before gate/up)
   if (up && !lists_ready) {
     const int rc = launch_route_lists(a.T, a.E, a.k, a.e_lo, a.e_cnt, a.ws, s);
     if (rc != QW_OK) return rc;
   }
+  XtPlan gp{};
+  if (grouped_plan<G>(a, gp)) return launch_experts_grouped<G>(a, gp, s, up, down, status, ep);
+  if (ep) return fail(QW_ERR_UNSUPPORTED, "moe_ep_experts: shape outside the grouped expert kernels");
   // the arithmetic of the bulk kernels (raw-nibble gate/up, fp16 down): a token's expert
   // outputs have the same bits whichever kernels (block size) compute them
   return launch_experts<W4Fmt<G, __half>, 4, W4NibFmt<G>>(a, s, up, down);
@@ -1655,7 +2211,7 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
                       const void* shared_down, int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
                       int64_t top_k, int32_t group, void* workspace, void* stream, bool up, bool dn,
                       int64_t expert_lo = 0, int64_t expert_count = -1, bool lists_ready = false,
-                      int64_t pairs_hint = 0) {
+                      int64_t pairs_hint = 0, const EpSend* ep = nullptr) {
   if (expert_count < 0) expert_count = experts;
   QW_CHECK_ARG(x && workspace && (expert_count == 0 || (gate_up && down)), "moe_experts: null pointer");
   QW_CHECK_ARG(expert_lo >= 0 && expert_lo + expert_count <= experts, "moe_experts: expert range outside [0, experts)");
@@ -1685,9 +2241,9 @@ static int experts_w4(const void* x, const void* gate_up, const void* down, cons
   a.pairs_hint = static_cast<int>(pairs_hint);
   cudaStream_t s = as_stream(stream);
   switch (group) {
-    case 128: return launch_experts_w4<128>(a, s, up, dn, lists_ready);
-    case 64: return launch_experts_w4<64>(a, s, up, dn, lists_ready);
-    default: return launch_experts_w4<32>(a, s, up, dn, lists_ready);
+    case 128: return launch_experts_w4<128>(a, s, up, dn, lists_ready, ep);
+    case 64: return launch_experts_w4<64>(a, s, up, dn, lists_ready, ep);
+    default: return launch_experts_w4<32>(a, s, up, dn, lists_ready, ep);
   }
 }
 
@@ -1755,10 +2311,9 @@ extern "C" int qw_moe_combine(void* workspace, void* out, int residual, int64_t 
   return QW_OK;
 }
 
-extern "C" int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens, int64_t hidden_dim,
-                                   int64_t experts, int64_t inter, int64_t top_k, int has_shared,
-                                   const void* gamma, void* normed, float eps, void* tap, int64_t ldf,
-                                   int tap_normed, void* stream) {
+static int combine_norm_entry(void* workspace, void* hidden, int64_t tokens, int64_t hidden_dim, int64_t experts,
+                              int64_t inter, int64_t top_k, int has_shared, const void* gamma, void* normed, float eps,
+                              void* tap, int64_t ldf, int tap_normed, void* stream, EpRecv ep_recv) {
   QW_CHECK_ARG(workspace && hidden && gamma && normed, "moe_combine_norm: null pointer");
   QW_CHECK_ARG(tokens >= 1 && top_k >= 1 && top_k <= 16 && hidden_dim > 0 && hidden_dim % 4 == 0 && eps > 0.f,
                "moe_combine_norm: invalid shape");
@@ -1779,11 +2334,31 @@ extern "C" int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens
   const float* part = w.part;
   if (k <= 8)
     QW_LAUNCH_PDL("moe combine_norm", moe_combine_norm_kernel<8>, dim3(T), dim3(CN_THREADS), 0, s, part, w.route, hp,
-                  T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed);
+                  T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed, ep_recv);
   else
     QW_LAUNCH_PDL("moe combine_norm", moe_combine_norm_kernel<16>, dim3(T), dim3(CN_THREADS), 0, s, part, w.route,
-                  hp, T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed);
+                  hp, T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed, ep_recv);
   return QW_OK;
+}
+
+extern "C" int qw_moe_combine_norm(void* workspace, void* hidden, int64_t tokens, int64_t hidden_dim,
+                                   int64_t experts, int64_t inter, int64_t top_k, int has_shared,
+                                   const void* gamma, void* normed, float eps, void* tap, int64_t ldf,
+                                   int tap_normed, void* stream) {
+  return combine_norm_entry(workspace, hidden, tokens, hidden_dim, experts, inter, top_k, has_shared, gamma, normed,
+                            eps, tap, ldf, tap_normed, stream, EpRecv{});
+}
+
+extern "C" int qw_moe_ep_combine_norm(void* workspace, void* window, int64_t ranks, int64_t cap, void* hidden,
+                                      int64_t tokens, int64_t hidden_dim, int64_t experts, int64_t inter,
+                                      int64_t top_k, int has_shared, const void* gamma, void* normed, float eps,
+                                      void* tap, int64_t ldf, int tap_normed, void* stream) {
+  QW_CHECK_ARG(window, "moe_ep_combine_norm: null window");
+  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && cap == tokens * (top_k + (has_shared ? 1 : 0)) &&
+                   hidden_dim % 8 == 0, "moe_ep_combine_norm: shape (cap = tokens * (top_k + shared))");
+  return combine_norm_entry(workspace, hidden, tokens, hidden_dim, experts, inter, top_k, has_shared, gamma, normed,
+                            eps, tap, ldf, tap_normed, stream,
+                            EpRecv{window, static_cast<int>(ranks), static_cast<int>(cap)});
 }
 
 extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_up, const void* down, void* out,
@@ -1887,85 +2462,6 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
 // same bits whatever else is in the launch) and crosses ranks as bf16, the precision
 // the combine reads it at, so the result is bit-identical to the single-GPU MoE.
 namespace qw {
-
-constexpr int EP_MAX_RANKS = 64;
-constexpr long long EP_PEER_WAIT_LIMIT = 1ll << 34;   // cycles (~9 s): a peer's host may lag in eager use
-
-struct EpWin {
-  int32_t* hdr;
-  int32_t* dflag;
-  int32_t* cflag;
-  int32_t* count;
-  int32_t* meta;
-  __nv_bfloat16* rows;
-  __nv_bfloat16* back;
-};
-
-__host__ __device__ inline int64_t ep_window_bytes(int G, int cap, int H) {
-  int64_t off = 1024;
-  off += align256(static_cast<int64_t>(G) * cap * 4);
-  off += align256(static_cast<int64_t>(G) * cap * H * 2);
-  off += align256(static_cast<int64_t>(cap) * H * 2);
-  return off;
-}
-
-__host__ __device__ inline EpWin ep_win(const void* base, int G, int cap, int H) {
-  uint8_t* p = static_cast<uint8_t*>(const_cast<void*>(base));
-  EpWin w;
-  w.hdr = reinterpret_cast<int32_t*>(p);
-  w.dflag = reinterpret_cast<int32_t*>(p + 256);
-  w.cflag = w.dflag + EP_MAX_RANKS;
-  w.count = w.cflag + EP_MAX_RANKS;
-  int64_t off = 1024;
-  w.meta = reinterpret_cast<int32_t*>(p + off);
-  off += align256(static_cast<int64_t>(G) * cap * 4);
-  w.rows = reinterpret_cast<__nv_bfloat16*>(p + off);
-  off += align256(static_cast<int64_t>(G) * cap * H * 2);
-  w.back = reinterpret_cast<__nv_bfloat16*>(p + off);
-  return w;
-}
-
-__device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded wait (one thread) until a peer has raised *flag to `want`.  On expiry -- or
-// when an earlier wait of this window expired (hdr[4]) -- records the timeout in the
-// sticky status and returns false, so a lost peer costs one limit, not one per wait.
-__device__ bool ep_wait_flag(const int32_t* flag, int want, int32_t* hdr) {
-  if (ld_acquire_sys(flag) >= want) return true;
-  const long long t0 = clock64();
-  while (ld_acquire_sys(flag) < want) {
-    if (*reinterpret_cast<volatile int32_t*>(hdr + 4) != 0 || clock64() - t0 > EP_PEER_WAIT_LIMIT) {
-      atomicOr(&g_moe_wait_status, QW_DEVICE_TIMEOUT);
-      *reinterpret_cast<volatile int32_t*>(hdr + 4) = 1;
-      return false;
-    }
-    __nanosleep(100);
-  }
-  return true;
-}
-
-// The CTA that finishes last (ticket wraps to 0 for the next launch).  The CTA barrier
-// orders every thread's stores before thread 0's system-scope fence, which precedes
-// its ticket; the last CTA's thread 0 fences again after taking the last ticket, and
-// then alone stores the flags (with release), so every CTA's stores happen before them.
-__device__ __forceinline__ bool ep_last_cta(int32_t* ticket) {
-  __shared__ int s_last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    s_last = atomicInc(reinterpret_cast<unsigned*>(ticket), gridDim.x - 1) == gridDim.x - 1;
-    if (s_last) __threadfence_system();
-  }
-  __syncthreads();
-  return s_last != 0;
-}
 
 // Position of pair p in its destination's rows: the earlier pairs with the same
 // destination, counted by the whole CTA (every thread calls it with the same p).
@@ -2074,35 +2570,6 @@ __global__ void __launch_bounds__(1024) ep_recv_route_kernel(void* own, int G, i
   __syncthreads();
   const int listed = rv.pair_off[*rv.n_active];
   for (int i = threadIdx.x; i < listed; i += blockDim.x) rv.pair_tok[i] = phys[rv.pair_tok[i]];
-}
-
-// Combine (receiving rank): each listed row's expert output (f32, slot 0 of the
-// receiving routing) as bf16 into its source's window, at the source's pair index; the
-// last CTA raises this rank's combine flag in every window.
-__global__ void ep_combine_kernel(const float* __restrict__ part, const void* ws, void* own, int G, int rank, int cap,
-                                  int H, int el, const unsigned long long* __restrict__ peers) {
-  pdl_wait();
-  pdl_trigger();
-  const EpWin me = ep_win(own, G, cap, H);
-  const int epoch = me.hdr[0] + 1;
-  const RouteView rv = route_view(const_cast<void*>(ws), G * cap, el, 1);
-  const int listed = rv.pair_off[*rv.n_active];
-  for (int i = blockIdx.x; i < listed; i += gridDim.x) {
-    const int r = rv.pair_tok[i];
-    const int src = r / cap;
-    const int pair = __ldcg(me.meta + r) >> 9;
-    const float* from = part + static_cast<int64_t>(r) * 2 * H;   // [rows][k + 1 = 2][H], slot 0
-    __nv_bfloat16* to = ep_win(reinterpret_cast<const void*>(peers[src]), G, cap, H).back + static_cast<int64_t>(pair) * H;
-    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-      const float4 a = *reinterpret_cast<const float4*>(from + c);
-      const float4 b = *reinterpret_cast<const float4*>(from + c + 4);
-      __nv_bfloat162 o[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                             __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-      *reinterpret_cast<uint4*>(to + c) = *reinterpret_cast<uint4*>(o);
-    }
-  }
-  if (ep_last_cta(me.hdr + 2) && threadIdx.x == 0)
-    for (int g = 0; g < G; ++g) st_release_sys(ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).cflag + rank, epoch);
 }
 
 // Scatter (source rank): wait for every rank's combine, then the returned rows into the
@@ -2226,31 +2693,19 @@ extern "C" int qw_moe_ep_recv_route(void* window, int64_t ranks, int64_t cap, in
   return QW_OK;
 }
 
-extern "C" int qw_moe_ep_experts(const void* window, const void* gate_up_local, const void* down_local,
-                                 int64_t ranks, int64_t cap, int64_t hidden, int64_t local_experts, int64_t inter,
-                                 int32_t group, void* recv_workspace, void* stream) {
-  QW_CHECK_ARG(window && ranks >= 1 && ranks <= EP_MAX_RANKS && cap >= 1 && local_experts >= 1 && local_experts <= 257,
-               "moe_ep_experts: shape");
+extern "C" int qw_moe_ep_experts(void* window, const void* gate_up_local, const void* down_local, int64_t ranks,
+                                 int64_t rank, int64_t cap, int64_t hidden, int64_t local_experts, int64_t inter,
+                                 int32_t group, const void* peers, void* recv_workspace, void* stream) {
+  QW_CHECK_ARG(window && peers && recv_workspace, "moe_ep_experts: null pointer");
+  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && rank >= 0 && rank < ranks && cap >= 1 && local_experts >= 1 &&
+                   local_experts <= 257, "moe_ep_experts: shape");
   // the window's received rows as ranks * cap rows, routed (lists included) by
-  // qw_moe_ep_recv_route; a rank receives cap pairs on average (every rank sends cap),
-  // which sets the tile width
+  // qw_moe_ep_recv_route; the down projection sends its outputs to their sources
   const EpWin w = ep_win(window, static_cast<int>(ranks), static_cast<int>(cap), static_cast<int>(hidden));
+  const EpSend ep{window, static_cast<const unsigned long long*>(peers), static_cast<int>(ranks),
+                  static_cast<int>(rank), static_cast<int>(cap)};
   return experts_w4(w.rows, gate_up_local, down_local, nullptr, nullptr, ranks * cap, hidden, local_experts, inter,
-                    1, group, recv_workspace, stream, true, true, 0, local_experts, true, cap);
-}
-
-extern "C" int qw_moe_ep_combine(const void* recv_workspace, void* window, int64_t ranks, int64_t rank, int64_t cap,
-                                 int64_t hidden, int64_t local_experts, int64_t inter, const void* peers, void* stream) {
-  QW_CHECK_ARG(recv_workspace && window && peers, "moe_ep_combine: null pointer");
-  QW_CHECK_ARG(ranks >= 1 && ranks <= EP_MAX_RANKS && rank >= 0 && rank < ranks && cap >= 1 &&
-                   local_experts >= 1 && local_experts <= 257 && hidden % 8 == 0, "moe_ep_combine: shape");
-  const int Tr = static_cast<int>(ranks * cap), H = static_cast<int>(hidden), el = static_cast<int>(local_experts);
-  WsParts w = split_ws(const_cast<void*>(recv_workspace), Tr, H, el, static_cast<int>(inter), 1);
-  const int grid = 2 * sm_count();
-  QW_LAUNCH_PDL("moe ep combine", ep_combine_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
-                as_stream(stream), w.part, w.route, window, static_cast<int>(ranks), static_cast<int>(rank),
-                static_cast<int>(cap), H, el, static_cast<const unsigned long long*>(peers));
-  return QW_OK;
+                    1, group, recv_workspace, stream, true, true, 0, local_experts, true, cap, &ep);
 }
 
 extern "C" int qw_moe_ep_scatter(void* workspace, void* window, int64_t tokens, int64_t hidden, int64_t experts,

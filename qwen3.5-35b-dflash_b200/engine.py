@@ -251,9 +251,9 @@ class TargetEngine:
         lib.check(getattr(self.lib, name)(*args), name)
 
     # kernels each entry point launches (all others launch one)
-    # (expert-parallel MoE layer: dispatch, receive routing, gate/up + down of the received
-    # rows, combine, scatter)
-    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2, "qw_moe_ep": 6}
+    # (expert-parallel MoE layer: dispatch, receive routing, gate/up + down-and-send of the
+    # received rows, and the combine + norm that reads the returned rows)
+    KERNELS_PER_CALL = {"qw_attn_paged": 2, "qw_moe_experts_w4": 2, "qw_gdn_commit": 2, "qw_moe_ep": 5}
 
     def launches_per_step(self) -> int:
         """Kernels of this library in the captured step (counted from the entry calls)."""
@@ -320,7 +320,7 @@ class TargetEngine:
             if self.ep_moe is not None:
                 if self._recording is not None:
                     self._recording["qw_moe_ep"] = self._recording.get("qw_moe_ep", 0) + 1
-                self.ep_moe.experts(self.normed, self.moe_ws, self.ep_gu[l], self.ep_dn[l])
+                self.ep_moe.experts(self.normed, self.moe_ws, self.ep_gu[l], self.ep_dn[l], scatter=False)
             else:
                 self._call("qw_moe_experts_w4", self.normed.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),
                            lw.shared_gu.data_ptr(), lw.shared_down.data_ptr(), T, H, E, I, k, c.quant_group,
@@ -331,8 +331,12 @@ class TargetEngine:
             # the final norm) + the feature tap of this layer (normed after the last layer)
             last = l == L - 1
             gamma = self.glob["final_norm"] if last else self.layers[l + 1].in_norm
-            self._call("qw_moe_combine_norm", self.moe_ws.data_ptr(), self.hidden.data_ptr(), T, H, E, I, k, 1,
-                       gamma.data_ptr(), self.normed.data_ptr(), eps, self._tap(l), c.feature_width, int(last), st)
+            if self.ep_moe is not None:
+                self.ep_moe.combine_norm(self.moe_ws, self.hidden, gamma, self.normed, eps, self._tap(l),
+                                         c.feature_width, int(last))
+            else:
+                self._call("qw_moe_combine_norm", self.moe_ws.data_ptr(), self.hidden.data_ptr(), T, H, E, I, k, 1,
+                           gamma.data_ptr(), self.normed.data_ptr(), eps, self._tap(l), c.feature_width, int(last), st)
         self._call("qw_lmhead_argmax", self.normed.data_ptr(), self.glob["lm_head"].data_ptr(), None,
                    self.keys.data_ptr(), T, self.vocab_pad, H, st)
         # did a bounded wait of this block's kernels expire? (read back with the results)

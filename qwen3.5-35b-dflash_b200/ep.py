@@ -12,12 +12,12 @@ each rank routes its own tokens over all E experts (``qw_moe_route``), then
    expert is every rank's last local expert, and each token sends it one more row, to
    its own rank, so it runs in the same expert launches as the routed pairs;
 2. ``qw_moe_ep_recv_route`` (waits for every rank's rows) + ``qw_moe_ep_experts``: the
-   received rows through the rank's own experts;
-3. ``qw_moe_ep_combine``: the outputs straight into the source ranks' windows, then a
-   flag; ``qw_moe_ep_scatter`` (waits for every rank's outputs) into the per-(token,
-   slot) slots (the shared expert's into slot k).
-
-``qw_moe_combine`` / ``qw_moe_combine_norm`` then run unchanged.  The expert kernels give
+   received rows through the rank's own experts, the down projection storing its
+   outputs straight into the source ranks' windows, then a flag;
+3. either ``qw_moe_ep_scatter`` (waits for every rank's outputs) into the per-(token,
+   slot) slots (the shared expert's into slot k), after which ``qw_moe_combine`` /
+   ``qw_moe_combine_norm`` run unchanged, or ``qw_moe_ep_combine_norm``, which reads the
+   returned rows directly (``combine_norm``).  The expert kernels give
 a row the same bits whatever else is in their launch and outputs travel as bf16 (the
 precision the combine reads), so the result equals the single-GPU MoE bit for bit.
 
@@ -124,12 +124,14 @@ class ExpertParallelMoE:
             dn = torch.cat([dn.view(-1), shared_down.reshape(-1)])
         return gu, dn
 
-    def experts(self, x: torch.Tensor, ws: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor):
+    def experts(self, x: torch.Tensor, ws: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor,
+                scatter: bool = True):
         """Routed (and shared) expert outputs of this rank's tokens ``x`` [tokens, hidden]
-        (bf16) into ``ws`` (a MoE workspace already routed by qw_moe_route /
+        (bf16) for the routing in ``ws`` (a MoE workspace already routed by qw_moe_route /
         qw_moe_route_x), on the current stream; ``gate_up_local`` / ``down_local`` come from
-        ``local_banks``.  Every rank of the group calls it, with the same shapes, in the same
-        order."""
+        ``local_banks``.  With ``scatter`` they land in ``ws``'s per-(token, slot) outputs;
+        without, they stay in the window for ``combine_norm``, which must follow.  Every
+        rank of the group calls it, with the same shapes, in the same order."""
         so = self.so
         st = torch.cuda.current_stream(x.device).cuda_stream
         T, H, E, I, k, g, G, cap = self.T, self.H, self.E, self.I, self.k, self.qg, self.G, self.cap
@@ -139,8 +141,20 @@ class ExpertParallelMoE:
         lib.check(so.qw_moe_ep_dispatch(ws.data_ptr(), x.data_ptr(), T, H, E, k, G, self.rank, cap, sh, peers, win,
                                         st), "ep dispatch")
         lib.check(so.qw_moe_ep_recv_route(win, G, cap, H, L, self.ws_r.data_ptr(), st), "ep receive routing")
-        lib.check(so.qw_moe_ep_experts(win, gate_up_local.data_ptr(), down_local.data_ptr(), G, cap, H, L, I, g,
-                                       self.ws_r.data_ptr(), st), "ep local experts")
-        lib.check(so.qw_moe_ep_combine(self.ws_r.data_ptr(), win, G, self.rank, cap, H, L, I, peers, st),
-                  "ep combine")
-        lib.check(so.qw_moe_ep_scatter(ws.data_ptr(), win, T, H, E, I, k, G, cap, sh, st), "ep scatter")
+        lib.check(so.qw_moe_ep_experts(win, gate_up_local.data_ptr(), down_local.data_ptr(), G, self.rank, cap, H, L,
+                                       I, g, peers, self.ws_r.data_ptr(), st), "ep local experts")
+        if scatter:
+            lib.check(so.qw_moe_ep_scatter(ws.data_ptr(), win, T, H, E, I, k, G, cap, sh, st), "ep scatter")
+
+    def combine_norm(self, ws: torch.Tensor, hidden: torch.Tensor, gamma: torch.Tensor, normed: torch.Tensor,
+                     eps: float, tap, ldf: int, tap_normed: int):
+        """``qw_moe_combine_norm`` over the rows the exchange returned (after
+        ``experts(..., scatter=False)``): hidden += MoE, normed = RMSNorm(hidden), the
+        optional tap."""
+        if not self.shared:
+            raise ValueError("combine_norm reads the shared expert's row from the exchange (shared=True)")
+        st = torch.cuda.current_stream(hidden.device).cuda_stream
+        lib.check(self.so.qw_moe_ep_combine_norm(ws.data_ptr(), self.window, self.G, self.cap, hidden.data_ptr(),
+                                                 self.T, self.H, self.E, self.I, self.k, 1, gamma.data_ptr(),
+                                                 normed.data_ptr(), eps, tap, ldf, tap_normed, st),
+                  "ep combine_norm")

@@ -65,8 +65,9 @@ SIGNATURES = {
     "qw_ep_window_free": (_c.c_int, [P]),
     "qw_moe_ep_dispatch": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, I64, _c.c_int, P, P, P]),
     "qw_moe_ep_recv_route": (_c.c_int, [P, I64, I64, I64, I64, P, P]),
-    "qw_moe_ep_experts": (_c.c_int, [P, P, P, I64, I64, I64, I64, I64, _c.c_int32, P, P]),
-    "qw_moe_ep_combine": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, P, P]),
+    "qw_moe_ep_experts": (_c.c_int, [P, P, P, I64, I64, I64, I64, I64, I64, _c.c_int32, P, P, P]),
+    "qw_moe_ep_combine_norm": (_c.c_int, [P, P, I64, I64, P, I64, I64, I64, I64, I64, _c.c_int, P, P, F32, P, I64,
+                                          _c.c_int, P]),
     "qw_moe_ep_scatter": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, I64, _c.c_int, P]),
     "qw_moe_route_x": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, I64, I32, P, P]),
     "qw_moe_route_lists": (_c.c_int, [P, I64, I64, I64, P]),
