@@ -1274,18 +1274,26 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
 constexpr int EP_MAX_RANKS = 64;
 constexpr long long EP_PEER_WAIT_LIMIT = 1ll << 34;   // cycles (~9 s): a peer's host may lag in eager use
 
+// Arrival counters: every exchange adds exactly EP_ROUND to the receiving counter of
+// each (sender, receiver) pair -- one per row as it lands, with release semantics, and
+// EP_ROUND - rows in one add from the sender, which knows the count -- so after exchange
+// n the counter is n * EP_ROUND, and no partial sum of exchange n reaches it.
+constexpr unsigned long long EP_ROUND = 1ull << 20;
+
 struct EpWin {
-  int32_t* hdr;
-  int32_t* dflag;
-  int32_t* cflag;
-  int32_t* count;
+  int32_t* hdr;                 // [0] epoch of the last closed exchange, [3] ticket, [4] broken
+  unsigned long long* dcnt;     // [64] rows (and count messages) arrived from source s
+  unsigned long long* ccnt;     // [64] results arrived from expert owner d
+  int32_t* count;               // [64] rows source s sent in the current exchange
   int32_t* meta;
   __nv_bfloat16* rows;
   __nv_bfloat16* back;
 };
 
+constexpr int EP_HEAD_BYTES = 2048;
+
 __host__ __device__ inline int64_t ep_window_bytes(int G, int cap, int H) {
-  int64_t off = 1024;
+  int64_t off = EP_HEAD_BYTES;
   off += align256(static_cast<int64_t>(G) * cap * 4);
   off += align256(static_cast<int64_t>(G) * cap * H * 2);
   off += align256(static_cast<int64_t>(cap) * H * 2);
@@ -1296,10 +1304,10 @@ __host__ __device__ inline EpWin ep_win(const void* base, int G, int cap, int H)
   uint8_t* p = static_cast<uint8_t*>(const_cast<void*>(base));
   EpWin w;
   w.hdr = reinterpret_cast<int32_t*>(p);
-  w.dflag = reinterpret_cast<int32_t*>(p + 256);
-  w.cflag = w.dflag + EP_MAX_RANKS;
-  w.count = w.cflag + EP_MAX_RANKS;
-  int64_t off = 1024;
+  w.dcnt = reinterpret_cast<unsigned long long*>(p + 256);
+  w.ccnt = w.dcnt + EP_MAX_RANKS;
+  w.count = reinterpret_cast<int32_t*>(p + 256 + 2 * EP_MAX_RANKS * 8);
+  int64_t off = EP_HEAD_BYTES;
   w.meta = reinterpret_cast<int32_t*>(p + off);
   off += align256(static_cast<int64_t>(G) * cap * 4);
   w.rows = reinterpret_cast<__nv_bfloat16*>(p + off);
@@ -1308,43 +1316,42 @@ __host__ __device__ inline EpWin ep_win(const void* base, int G, int cap, int H)
   return w;
 }
 
-__device__ __forceinline__ int ld_acquire_sys(const int32_t* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(int32_t* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+// Add to a (peer's) counter, ordered after every store this thread has observed.
+__device__ __forceinline__ void red_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
 
-// Bounded wait (one thread) until a peer has raised *flag to `want`.  On expiry -- or
-// when an earlier wait of this window expired (hdr[4]) -- records the timeout in the
-// sticky status and returns false, so a lost peer costs one limit, not one per wait.
-__device__ bool ep_wait_flag(const int32_t* flag, int want, int32_t* hdr) {
-  if (ld_acquire_sys(flag) >= want) return true;
+// Bounded wait (one thread) until *counter reaches `want` (added by peer GPUs).  On
+// expiry -- or when an earlier wait of this window expired (hdr[4]) -- records the
+// timeout in the sticky status and returns false, so a lost peer costs one limit, not
+// one per wait.
+__device__ bool ep_wait_count(const unsigned long long* counter, unsigned long long want, int32_t* hdr) {
+  if (ld_acquire_sys(counter) >= want) return true;
   const long long t0 = clock64();
-  while (ld_acquire_sys(flag) < want) {
+  while (ld_acquire_sys(counter) < want) {
     if (*reinterpret_cast<volatile int32_t*>(hdr + 4) != 0 || clock64() - t0 > EP_PEER_WAIT_LIMIT) {
       atomicOr(&g_moe_wait_status, QW_DEVICE_TIMEOUT);
       *reinterpret_cast<volatile int32_t*>(hdr + 4) = 1;
       return false;
     }
-    __nanosleep(100);
+    __nanosleep(64);
   }
   return true;
 }
 
-// The CTA that finishes last (ticket wraps to 0 for the next launch).  The CTA barrier
-// orders every thread's stores before thread 0's system-scope fence, which precedes
-// its ticket; the last CTA's thread 0 fences again after taking the last ticket, and
-// then alone stores the flags (with release), so every CTA's stores happen before them.
+// The CTA that finishes last (ticket wraps to 0 for the next launch); used to close an
+// exchange after every CTA of the kernel has read what it needs.
 __device__ __forceinline__ bool ep_last_cta(int32_t* ticket) {
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    __threadfence();
     s_last = atomicInc(reinterpret_cast<unsigned*>(ticket), gridDim.x - 1) == gridDim.x - 1;
-    if (s_last) __threadfence_system();
   }
   __syncthreads();
   return s_last != 0;
@@ -1379,19 +1386,33 @@ __device__ __forceinline__ int gr_pairs(const MoeArgs<ET>& a, const RouteView& r
   return rv.pair_off[ai + 1] - rv.pair_off[ai];
 }
 
-// Every thread: the table with `per` items per (slot, chunk).
+// Every thread: the table with `per` items per (slot, chunk).  The slots' item counts
+// load in parallel; warp 0 scans them 32 at a time.
 template <typename ET>
 __device__ void gr_build_table(GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int per) {
-  if (threadIdx.x == 0) {
-    const int ns = a.has_shared + *rv.n_active;
-    int acc = 0;
-    for (int sl = 0; sl < ns; ++sl) {
-      tb.first[sl] = acc;
-      acc += (gr_pairs(a, rv, sl) + GR_CHUNK - 1) / GR_CHUNK * per;
+  const int ns = a.has_shared + *rv.n_active;
+  for (int sl = threadIdx.x; sl < ns; sl += blockDim.x)
+    tb.first[sl] = (gr_pairs(a, rv, sl) + GR_CHUNK - 1) / GR_CHUNK * per;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int base = 0; base < ns; base += 32) {
+      const int v = base + lane < ns ? tb.first[base + lane] : 0;
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      if (base + lane < ns) tb.first[base + lane] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
     }
-    tb.first[ns] = acc;
-    tb.nslots = ns;
-    tb.total = acc;
+    if (lane == 0) {
+      tb.first[ns] = carry;
+      tb.nslots = ns;
+      tb.total = carry;
+    }
   }
   __syncthreads();
 }
@@ -1618,6 +1639,16 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(X
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   pdl_wait();   // h comes from the predecessor (gate/up); the lists from earlier kernels
   pdl_trigger();
+  if constexpr (EP) {
+    // every received row returns to its source as nrb pieces (one per unit), each
+    // counted on arrival; the complement to EP_ROUND goes now, from CTA 0
+    if (blockIdx.x == 0 && threadIdx.x < ep.G) {
+      const EpWin me = ep_win(ep.window, ep.G, ep.cap, H);
+      const unsigned long long pieces = static_cast<unsigned long long>(__ldcg(me.count + threadIdx.x)) * nrb;
+      red_release_sys(ep_win(reinterpret_cast<const void*>(ep.peers[threadIdx.x]), ep.G, ep.cap, H).ccnt + ep.rank,
+                      EP_ROUND - pieces);
+    }
+  }
   gr_build_table(tb, a, rv, nrb);
   const int nu = tb.total;
   const int my_units = blockIdx.x < nu ? (nu - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -1701,7 +1732,9 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(X
     }
     if constexpr (EP) {
       // the unit's rows to their sources: row tl of the unit is the received row
-      // pair_tok[pb + ch * 16 + tl] (no shared slot on the receiving side)
+      // pair_tok[pb + ch * 16 + tl] (no shared slot on the receiving side); each source's
+      // counter takes one release add per row piece, after the CTA barrier that follows
+      // the piece's stores
       __syncthreads();
       const int vec = rb_tiles * 16 / 8;   // 16-byte vectors per output row
       for (int i = threadIdx.x; i < np * vec; i += blockDim.x) {
@@ -1713,16 +1746,15 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(X
                             static_cast<int64_t>(pair) * H + sub * rb_tiles * 16 + c;
         *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(osm + tl * OS + c);
       }
+      __syncthreads();
+      if (threadIdx.x < np) {
+        const int r = rv.pair_tok[pb + ch * GR_CHUNK + threadIdx.x];
+        red_release_sys(ep_win(reinterpret_cast<const void*>(ep.peers[r / ep.cap]), ep.G, ep.cap, H).ccnt + ep.rank,
+                        1ull);
+      }
     }
   }
   cp_async_wait<0>();
-  if constexpr (EP) {
-    const EpWin me = ep_win(ep.window, ep.G, ep.cap, H);
-    const int epoch = me.hdr[0] + 1;
-    if (ep_last_cta(me.hdr + 2) && threadIdx.x == 0)
-      for (int g = 0; g < ep.G; ++g)
-        st_release_sys(ep_win(reinterpret_cast<const void*>(ep.peers[g]), ep.G, ep.cap, H).cflag + ep.rank, epoch);
-  }
 }
 
 // Combine (fused/model.py:296-307 with fused_ops.py:165-172): per token, the routed
@@ -1812,7 +1844,7 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     me = ep_win(ep.window, ep.G, ep.cap, H);
     if (threadIdx.x == 0) s_epoch = me.hdr[0] + 1;
     __syncthreads();
-    if (threadIdx.x < ep.G) ep_wait_flag(me.cflag + threadIdx.x, s_epoch, me.hdr);
+    if (threadIdx.x < ep.G) ep_wait_count(me.ccnt + threadIdx.x, s_epoch * EP_ROUND, me.hdr);
   }
   __syncthreads();
   const float* pt = part + static_cast<int64_t>(t) * (k + 1) * H;
@@ -2444,11 +2476,12 @@ extern "C" int qw_moe(const void* hidden, const void* router, const void* gate_u
 // multicast touches peer memory: plain 16-byte stores from SM threads.
 //
 // Window of rank g (identical layout on every rank):
-//   hdr   int32[64]   [0] epoch of the last finished exchange, [1..3] CTA tickets of the
-//                     dispatch / combine / scatter kernels, [4] broken (a wait expired)
-//   dflag int32[64]   dflag[s] = epoch of source s's last dispatch to g
-//   cflag int32[64]   cflag[d] = epoch of destination d's last combine back to g
-//   count int32[64]   count[s] = rows source s sent to g in its last dispatch
+//   hdr   int32[64]   [0] epoch of the last closed exchange, [3] CTA ticket of the
+//                     kernel that closes it, [4] broken (a wait expired)
+//   dcnt  u64[64]     rows arrived from source s (+ its count message), EP_ROUND each
+//                     exchange
+//   ccnt  u64[64]     result pieces arrived from expert owner d (+ its count message)
+//   count int32[64]   count[s] = rows source s sent to g in the current exchange
 //   meta  int32[G][cap]       (source pair index << 9) | local expert, per received row
 //   rows  bf16 [G][cap][H]    received rows (source s at rows [s][0, count[s]))
 //   back  bf16 [cap][H]       this rank's own pairs' expert outputs (pair p at row p)
@@ -2514,20 +2547,24 @@ __global__ void ep_dispatch_kernel(const int32_t* __restrict__ idx, const __nv_b
   const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(tok) * H);
   uint4* out = reinterpret_cast<uint4*>(dst.rows + (static_cast<int64_t>(rank) * cap + pos) * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) out[i] = src[i];
-  if (!ep_last_cta(me.hdr + 1)) return;
+  __syncthreads();
+  if (threadIdx.x == 0) red_release_sys(dst.dcnt + rank, 1ull);   // after the row and its descriptor
+  if (blockIdx.x != 0) return;
+  // CTA 0: the counts, then each destination's complement to EP_ROUND
   for (int g = 0; g < G; ++g) {
     int c = 0;
     for (int q0 = 0; q0 < np; q0 += blockDim.x) {
       const int q = q0 + threadIdx.x;
       c += __syncthreads_count(q < np && idx[q] / el == g);
     }
-    if (threadIdx.x == 0)
-      ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).count[rank] = c + (g == rank && shared ? T : 0);
+    if (threadIdx.x == 0) {
+      c += (g == rank && shared) ? T : 0;
+      const EpWin w = ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H);
+      w.count[rank] = c;
+      red_release_sys(w.dcnt + rank, EP_ROUND - static_cast<unsigned long long>(c));
+    }
   }
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int g = 0; g < G; ++g) st_release_sys(ep_win(reinterpret_cast<const void*>(peers[g]), G, cap, H).dflag + rank, epoch);
-  }
+  (void)epoch;
 }
 
 // Receiving rank: wait for every source's dispatch, then route the received rows
@@ -2542,7 +2579,7 @@ __global__ void __launch_bounds__(1024) ep_recv_route_kernel(void* own, int G, i
   const EpWin me = ep_win(own, G, cap, H);
   const int epoch = me.hdr[0] + 1;
   if (threadIdx.x < G) {
-    const bool ok = ep_wait_flag(me.dflag + threadIdx.x, epoch, me.hdr);
+    const bool ok = ep_wait_count(me.dcnt + threadIdx.x, static_cast<unsigned long long>(epoch) * EP_ROUND, me.hdr);
     const int c = ok ? __ldcg(me.count + threadIdx.x) : 0;
     s_cnt[threadIdx.x] = c < 0 ? 0 : (c > cap ? cap : c);
   }
@@ -2583,7 +2620,9 @@ __global__ void ep_scatter_kernel(void* own, int T, int H, int k, int G, int cap
   const int epoch = me.hdr[0] + 1;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
-  if (threadIdx.x < G && !ep_wait_flag(me.cflag + threadIdx.x, epoch, me.hdr)) s_ok = 0;
+  if (threadIdx.x < G && !ep_wait_count(me.ccnt + threadIdx.x, static_cast<unsigned long long>(epoch) * EP_ROUND,
+                                        me.hdr))
+    s_ok = 0;
   __syncthreads();
   const int p = blockIdx.x;
   if (s_ok) {

@@ -348,9 +348,11 @@ def test_moe_ep_kernels_one_rank_bit_identical(cuda_lib, t, g, e, inter):
         topk = ws2[: t * k * 4].view(torch.int32).view(t, k).cpu().numpy()
         rows_w, meta_w, count_w = ep_np.dispatch(topk, x.cpu().view(torch.int16).numpy().view("uint16"), e, 1, 0,
                                                  shared=True)[0]
-        assert words[64 + 128] == count_w == cap                       # count[0]
-        assert (words[256:256 + count_w] == meta_w[:count_w]).all()   # meta [1][cap] at byte 1024
-        rows_off = 1024 + (cap * 4 + 255) // 256 * 256
+        assert words[320] == count_w == cap                            # count[0] at byte 1280
+        counters = window[256:256 + 2 * 64 * 8].view(torch.int64).cpu().numpy()
+        assert counters[0] == counters[64] == (rep + 1) << 20          # dispatch / result arrivals
+        assert (words[512:512 + count_w] == meta_w[:count_w]).all()   # meta [1][cap] at byte 2048
+        rows_off = 2048 + (cap * 4 + 255) // 256 * 256
         got = window[rows_off: rows_off + cap * h * 2].view(torch.int16).cpu().numpy().view("uint16").reshape(cap, h)
         assert (got[:count_w] == rows_w[:count_w]).all()
         if not torch.equal(out1, out2):
