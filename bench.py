@@ -535,9 +535,19 @@ def run_kernels(args):
                                             eng.attn_out.data_ptr(), eng.B, eng.S, Hq, Hkv, D, D ** -0.5,
                                             eng.attn_ws.data_ptr(), s))
 
+    def lmhead():
+        return lambda: chk(so.qw_lmhead_argmax(x.data_ptr(), eng.glob["lm_head"].data_ptr(), None, eng.keys.data_ptr(),
+                                               T, eng.vocab_pad, H, s))
+
+    def combine_norm(lw):
+        return lambda: chk(so.qw_moe_combine_norm(ws.data_ptr(), eng.hidden.data_ptr(), T, H, Ex, I, k, 1,
+                                                  lw.in_norm.data_ptr(), eng.normed.data_ptr(), cfg.rms_norm_eps,
+                                                  None, 0, 0, s))
+
     with torch.cuda.stream(st):
         route()
         up(L[0])()
+        down(L[0])()
     torch.cuda.synchronize()
     active = eng.active_experts()
     w4 = lambda n, kk: n * kk // 2 + n * (kk // g) * 2
@@ -546,7 +556,9 @@ def run_kernels(args):
              ("w4_qkvz", [qkvz(lw) for lw in gl], w4(eng.ldp, H)),
              ("gdn_verify", [gdn(i) for i in range(len(gl))], 0),
              ("attn_paged", [attn(i) for i in range(len(eng.k_cache))],
-              2 * cfg.num_key_value_heads * (args.ctx + 16) * cfg.head_dim * 2)]
+              2 * cfg.num_key_value_heads * (args.ctx + 16) * cfg.head_dim * 2),
+             ("lm_head_argmax", [lmhead()], cfg.vocab_size * H * 2),
+             ("combine_norm", [combine_norm(lw) for lw in L], T * (k + 1) * H * 4 + 3 * T * H * 2)]
     out = {"kernels": {}, "active_experts": active, "ctx": args.ctx}
     for name, fns, nbytes in cases:
         with torch.cuda.stream(st):
