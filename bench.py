@@ -263,7 +263,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     cfg = QWEN35_35B_A3B
-    B, S = args.batch, 16
+    S = 16
+    if args.requests:
+        # benchmark config 5: the requests split evenly over the GPUs
+        if args.requests % world:
+            raise SystemExit(f"--requests {args.requests} does not split over {world} GPUs")
+        args.batch = args.requests // world
+    B = args.batch
     total_steps = args.warmup + args.steps
     capacity = args.ctx + S + (total_steps + args.e2e_steps + 8) * S
     capacity = (capacity + 15) // 16 * 16
@@ -273,6 +279,14 @@ def run_ours(args, rank, world, local_rank):
     eng = E.TargetEngine(cfg, weights, batch=B, block=S, capacity=capacity, device=dev,
                          ep_group=dist.group.WORLD if ep else None)
     eng.set_random_context(args.ctx, seed=3 + rank)
+    if args.zipf > 0:
+        # routing skew: a per-expert router-logit bias log p_e, p_e ~ rank^-s over a seeded
+        # permutation of the experts (the same on every GPU)
+        perm = torch.randperm(cfg.num_experts, generator=torch.Generator().manual_seed(3))
+        ranks = torch.empty(cfg.num_experts)
+        ranks[perm] = torch.arange(1, cfg.num_experts + 1, dtype=torch.float32)
+        p = ranks.pow(-args.zipf)
+        eng.router_bias = (p / p.sum()).log().to(torch.bfloat16).to(dev)
     torch.cuda.synchronize(dev)
     init_s = time.perf_counter() - t_init
 
@@ -382,9 +396,11 @@ def run_ours(args, rank, world, local_rank):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (random-init weights N(0,0.02) W4A16 g128, seeded KV/GDN context and proposals)",
-            "config": {"workload": ("full target verify forward, experts sharded over the GPUs "
-                                    "(benchmark config 4 per GPU, config 5's expert parallelism)") if ep else
-                                   "full target verify forward, 1 GPU per replica (benchmark config 4)",
+            "config": {"workload": (f"benchmark config 5: {B * world} requests ({B} per GPU), ctx {args.ctx}, "
+                                    f"Zipf({args.zipf}) routing skew" if args.requests else
+                                    ("full target verify forward, experts sharded over the GPUs "
+                                     "(benchmark config 4 per GPU, config 5's expert parallelism)") if ep else
+                                    "full target verify forward, 1 GPU per replica (benchmark config 4)"),
                        "model": "Qwen3.5-35B-A3B target (40 layers: 30 GDN + 10 attention)",
                        "global_batch": B * world, "block": S, "ctx": args.ctx, "seq_len": args.ctx + S,
                        "parallelism": (f"ep{world} (experts {cfg.num_experts // world} per GPU; dispatch and "
@@ -708,7 +724,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--ctx", type=int, default=4096)
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
+    ap.add_argument("--requests", type=int, default=0,
+                    help="total requests, split evenly over the GPUs (benchmark config 5: 64)")
+    ap.add_argument("--zipf", type=float, default=0.0,
+                    help="routing skew: router-logit bias log p_e, p_e ~ rank^-s (benchmark config 5: 1.1)")
+    ap.add_argument("--serving", action="store_true",
+                    help="benchmark config 5: --requests 64 --ctx 32768 --zipf 1.1")
     ap.add_argument("--replicas", action="store_true",
                     help="with --gpus > 1: run independent replicas instead of sharding the routed experts")
     ap.add_argument("--e2e-steps", type=int, default=30)
@@ -723,6 +745,10 @@ def main():
     ap.add_argument("--micro", action="store_true",
                     help="benchmark configs 2 (W4A16 MoE, T 16/64/256) and 3 (GDN verify, B 1/8/32), one line each")
     args = ap.parse_args()
+    if args.serving:
+        args.requests = args.requests or 64
+        args.ctx = 32768 if args.ctx == 4096 else args.ctx
+        args.zipf = args.zipf or 1.1
     if args.kernels:
         run_kernels(args)
         return

@@ -185,6 +185,9 @@ class TargetEngine:
             dtype=torch.uint8, device=dev)
         self.nrouter = (c.num_experts + 1 + 15) // 16 * 16
         self.router_logits = torch.zeros(T, self.nrouter, dtype=BF16, device=dev)
+        # optional per-expert router-logit bias (synthetic routing skew of a serving
+        # benchmark); None in the model
+        self.router_bias = None
         self.moe_ws = torch.zeros(self.lib.qw_moe_workspace_bytes(
             T, H, c.num_experts, c.moe_intermediate_size, c.num_experts_per_tok), dtype=torch.uint8, device=dev)
         self.features = torch.zeros(T, c.feature_width, dtype=BF16, device=dev)
@@ -315,6 +318,8 @@ class TargetEngine:
             self._call("qw_b16_linear", self.normed.data_ptr(), lw.router.data_ptr(),
                        self.router_logits.data_ptr(), lib.QW_OUT_BF16, self.nrouter, T, self.nrouter, H, st)
             E, k, I = c.num_experts, c.num_experts_per_tok, c.moe_intermediate_size
+            if self.router_bias is not None:
+                self.router_logits[:, :E].add_(self.router_bias)
             self._call("qw_moe_route_x", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
                        lib.QW_BF16, self.normed.data_ptr(), H, c.quant_group, self.moe_ws.data_ptr(), st)
             if self.ep_moe is not None:
