@@ -434,6 +434,50 @@ int qw_apply_commit(const int32_t* accepted, const int32_t* top1, int32_t* next_
                     int32_t* qpos, int64_t batch, int64_t seq, void* stream);
 
 /* ------------------------------------------------------------------------------
+ * The DFlash draft forward (model/qwen35_moe_dflash/model.py:102-522; block and context
+ * of the draft graph model/qwen35_moe_dflash/reference/graphs.py:63-97).  Its
+ * projections use qw_b16_linear, its norms qw_rms_norm (the draft stores effective
+ * norm weights), its attention qw_attn_paged_masked.
+ * ---------------------------------------------------------------------------- */
+
+/* qw_attn_paged without the output gate and with the draft's masks: block_full = 1
+ * lets every query row see the whole block (the draft's full-attention layer,
+ * model.py:134-141), window > 0 hides keys at or beyond `window` positions before the
+ * row (its sliding layers, model.py:170-175). */
+int qw_attn_paged_masked(const void* q, const void* k_cache, const void* v_cache, const int32_t* pages,
+                         int32_t max_pages, int32_t page_size, const int32_t* qpos, int64_t max_len,
+                         void* out, int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads,
+                         int64_t dim, float scale, int block_full, int32_t window, void* workspace,
+                         void* stream);
+
+/* q/k RMSNorm with effective weights (ops.py:66-71), rotary over the whole head
+ * (model.py:80-99, ops.py:75-90) and the append of k, v into the paged cache.  qkv rows
+ * [B*S, ldq] hold [q (heads*dim, when has_q) | k | v]; row (b, s) sits at position
+ * pos_base[b] - pos_sub[b] (pos_sub may be NULL) + s; with valid (int32 [B]) rows s >=
+ * valid[b] are skipped (the context rows of a partly accepted block).  q goes to q_out
+ * [B, heads, S, dim]. */
+int qw_draft_prep(const void* qkv, int64_t ldq, int has_q, const void* q_norm_w, const void* k_norm_w,
+                  float eps, float rope_theta, const int32_t* pos_base, const int32_t* pos_sub,
+                  const int32_t* valid, const int32_t* pages, int32_t max_pages, int32_t page_size,
+                  void* k_cache, void* v_cache, void* q_out, int64_t batch, int64_t seq, int64_t heads,
+                  int64_t kv_heads, int64_t dim, void* stream);
+
+/* out [T, inter] = bf16(bf16(silu(gate)) * up) from gate_up [T, 2 inter] = [gate | up]
+ * (the draft MLP, model.py:265-291). */
+int qw_swiglu(const void* gate_up, void* out, int64_t tokens, int64_t inter, void* stream);
+
+/* hidden [B*S, H] = embed[anchor[b]] for s = 0, embed[mask_id] otherwise (graphs.py:74-86,
+ * model.py:519-522 with the unit embedding scale). */
+int qw_draft_block_embed(const void* embed, const int32_t* anchor, int32_t mask_id, void* hidden,
+                         int64_t batch, int64_t seq, int64_t hidden_dim, void* stream);
+
+/* The next verify block from the draft's lm_head keys (qw_lmhead_argmax): tokens[b*S] =
+ * anchor[b], tokens[b*S + i] = stable arg-max of draft row i, i = 1 .. S-1
+ * (graphs.py:87-97, model.py:496-517). */
+int qw_draft_propose(const void* keys, int64_t nblk, const int32_t* anchor, int32_t* tokens,
+                     int64_t batch, int64_t seq, void* stream);
+
+/* ------------------------------------------------------------------------------
  * Bounded device waits.  Kernels that wait on the TMA engine (the cluster linears,
  * the bulk expert kernels) give up after a bounded time instead of hanging, record
  * the expiry in a sticky status word of the library and return early: the outputs of

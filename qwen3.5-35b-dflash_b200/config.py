@@ -155,3 +155,86 @@ def with_layers(config: TargetConfig, n_layers: int) -> TargetConfig:
     taps = tuple(i for i in config.feature_layers if i < n_layers) or (n_layers - 1,)
     return replace(config, num_hidden_layers=n_layers, layer_types=_interleaved(n_layers),
                    feature_layers=taps)
+
+
+@dataclass(frozen=True)
+class DraftConfig:
+    """The DFlash draft (model/qwen35_moe_dflash/config.py:11-140; the locked checkpoint
+    specs/draft-config.json): a dense Qwen3-style decoder over a 16-token block (anchor +
+    mask tokens) attending to the target's tapped features, sliding-window causal layers
+    and a last full-attention layer that is bidirectional over the block."""
+    hidden_size: int
+    intermediate_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    layer_types: tuple[str, ...]
+    target_layer_ids: tuple[int, ...]
+    mask_token_id: int
+    sliding_window: int
+    use_sliding_window: bool = True
+    block_size: int = 16
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10_000_000.0
+    input_embedding_scale: float = 1.0
+
+    def __post_init__(self):
+        if self.num_attention_heads % self.num_key_value_heads:
+            raise ValueError("attention heads must be divisible by KV heads")
+        if len(self.layer_types) != self.num_hidden_layers or set(self.layer_types) - {
+                "sliding_attention", "full_attention"}:
+            raise ValueError("layer_types must name one sliding_attention / full_attention per layer")
+        if not self.target_layer_ids or tuple(sorted(set(self.target_layer_ids))) != self.target_layer_ids:
+            raise ValueError("target_layer_ids must be sorted and unique")
+        if min(self.hidden_size, self.intermediate_size, self.head_dim, self.sliding_window, self.block_size) <= 0:
+            raise ValueError("DFlash configuration values must be positive")
+        if self.input_embedding_scale != 1.0:
+            raise ValueError("the draft block embedding is used unscaled (input_embedding_scale 1)")
+
+    @property
+    def feature_size(self) -> int:
+        return len(self.target_layer_ids) * self.hidden_size
+
+    def window(self, layer: int) -> int:
+        """Sliding window of a layer's causal mask (0: none)."""
+        sliding = self.layer_types[layer] == "sliding_attention"
+        return self.sliding_window if sliding and self.use_sliding_window else 0
+
+    def causal(self, layer: int) -> bool:
+        """Sliding layers are causal; the full-attention layer is bidirectional over the
+        block (model/qwen35_moe_dflash/model.py:134-141)."""
+        return self.layer_types[layer] == "sliding_attention"
+
+    def to_reference_dict(self, vocab_size: int, num_target_layers: int) -> dict:
+        """The config.json shape the reference's Qwen35DFlashConfig.from_dict reads."""
+        return {
+            "hidden_size": self.hidden_size, "intermediate_size": self.intermediate_size,
+            "vocab_size": vocab_size, "num_hidden_layers": self.num_hidden_layers,
+            "num_attention_heads": self.num_attention_heads, "num_key_value_heads": self.num_key_value_heads,
+            "head_dim": self.head_dim, "num_target_layers": num_target_layers,
+            "layer_types": list(self.layer_types), "rms_norm_eps": self.rms_norm_eps,
+            "rope_parameters": {"rope_theta": self.rope_theta, "rope_type": "default"},
+            "max_position_embeddings": 262144, "sliding_window": self.sliding_window,
+            "use_sliding_window": self.use_sliding_window, "attention_bias": False, "attention_dropout": 0.0,
+            "hidden_act": "silu", "dtype": "bfloat16",
+            "dflash_config": {"block_size": self.block_size, "mask_token_id": self.mask_token_id,
+                              "target_layer_ids": list(self.target_layer_ids)},
+        }
+
+
+# The Qwen3.5-35B-A3B DFlash draft (specs/draft-config.json).
+QWEN35_DFLASH_DRAFT = DraftConfig(
+    hidden_size=2048, intermediate_size=6144, num_hidden_layers=6, num_attention_heads=32,
+    num_key_value_heads=8, head_dim=128,
+    layer_types=("sliding_attention",) * 5 + ("full_attention",),
+    target_layer_ids=(1, 6, 11, 16, 22, 27, 32, 37), mask_token_id=248077, sliding_window=4096,
+)
+
+# The draft of the tiny configuration: 2 layers (sliding, full), a window of 8 positions
+# so that the window cuts into the context in tests; taps = TINY.feature_layers.
+TINY_DRAFT = DraftConfig(
+    hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+    num_key_value_heads=1, head_dim=64, layer_types=("sliding_attention", "full_attention"),
+    target_layer_ids=(1, 2), mask_token_id=4095, sliding_window=8,
+)

@@ -45,6 +45,8 @@ struct AttnArgs {
   float* opart;                // [nsplit, B, H, S, D]
   float* ml;                   // [nsplit, B, H, S, 2]
   int pgcap;                   // page indices a CTA may stage in shared memory
+  int block_full;              // 1: every query row sees the whole block (no causal order inside it)
+  int window;                  // > 0: row at position p sees keys > p - window only
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
@@ -134,11 +136,13 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   const int wrow = warp * 16;
-  int smax[2];  // last visible key for the lane's two rows
+  int smax[2], smin[2];  // last and first visible key for the lane's two rows
 #pragma unroll
   for (int h2 = 0; h2 < 2; ++h2) {
     const int rr = row0 + wrow + gid + 8 * h2;
-    smax[h2] = (wrow + gid + 8 * h2 < nrows) ? qpos + rr % a.S : -1;
+    const int qp = qpos + rr % a.S;
+    smax[h2] = (wrow + gid + 8 * h2 < nrows) ? (a.block_full ? qpos + a.S - 1 : qp) : -1;
+    smin[h2] = a.window > 0 ? qp - a.window + 1 : 0;
   }
   // ldmatrix row addresses
   const int qa_row = wrow + ((lane >> 3) & 1) * 8 + (lane & 7);
@@ -184,7 +188,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
       for (int r = 0; r < 4; ++r) {
         const int key = t0 + j * 8 + 2 * tig + (r & 1);
         const int h2 = r >> 1;
-        const bool ok = key < k1 && key <= smax[h2];
+        const bool ok = key < k1 && key <= smax[h2] && key >= smin[h2];
         const float s = ok ? sc[j][r] * a.scale : -INFINITY;
         sc[j][r] = s;
         tmax[h2] = fmaxf(tmax[h2], s);
@@ -533,10 +537,35 @@ extern "C" int qw_attn_prep(const void* qkv, int64_t ldq, const void* q_norm_w, 
   return QW_OK;
 }
 
+static int attn_paged_entry(const void* q, const void* k_cache, const void* v_cache, const int32_t* pages,
+                            int32_t max_pages, int32_t page_size, const int32_t* qpos, int64_t max_len,
+                            const void* gate, int64_t ldg, void* out, int64_t batch, int64_t seq, int64_t heads,
+                            int64_t kv_heads, int64_t dim, float scale, void* workspace, void* stream, int block_full,
+                            int window);
+
 extern "C" int qw_attn_paged(const void* q, const void* k_cache, const void* v_cache, const int32_t* pages,
                              int32_t max_pages, int32_t page_size, const int32_t* qpos, int64_t max_len,
                              const void* gate, int64_t ldg, void* out, int64_t batch, int64_t seq, int64_t heads,
                              int64_t kv_heads, int64_t dim, float scale, void* workspace, void* stream) {
+  return attn_paged_entry(q, k_cache, v_cache, pages, max_pages, page_size, qpos, max_len, gate, ldg, out, batch, seq,
+                          heads, kv_heads, dim, scale, workspace, stream, 0, 0);
+}
+
+extern "C" int qw_attn_paged_masked(const void* q, const void* k_cache, const void* v_cache, const int32_t* pages,
+                                    int32_t max_pages, int32_t page_size, const int32_t* qpos, int64_t max_len,
+                                    void* out, int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads,
+                                    int64_t dim, float scale, int block_full, int32_t window, void* workspace,
+                                    void* stream) {
+  QW_CHECK_ARG(window >= 0 && (block_full == 0 || block_full == 1), "attn_paged_masked: invalid mask");
+  return attn_paged_entry(q, k_cache, v_cache, pages, max_pages, page_size, qpos, max_len, nullptr, 0, out, batch,
+                          seq, heads, kv_heads, dim, scale, workspace, stream, block_full, window);
+}
+
+static int attn_paged_entry(const void* q, const void* k_cache, const void* v_cache, const int32_t* pages,
+                            int32_t max_pages, int32_t page_size, const int32_t* qpos, int64_t max_len,
+                            const void* gate, int64_t ldg, void* out, int64_t batch, int64_t seq, int64_t heads,
+                            int64_t kv_heads, int64_t dim, float scale, void* workspace, void* stream, int block_full,
+                            int window) {
   QW_CHECK_ARG(q && k_cache && v_cache && pages && qpos && out && workspace, "attn_paged: null pointer");
   QW_CHECK_ARG(batch >= 1 && seq >= 1 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0 && max_len >= seq &&
                    page_size >= 1 && max_pages * static_cast<int64_t>(page_size) >= max_len && scale > 0.f,
@@ -552,6 +581,8 @@ extern "C" int qw_attn_paged(const void* q, const void* k_cache, const void* v_c
   a.B = static_cast<int>(batch); a.H = static_cast<int>(heads); a.Hkv = static_cast<int>(kv_heads);
   a.S = static_cast<int>(seq); a.kc = p.kc; a.nsplit = p.nsplit; a.rowgroups = p.rowgroups;
   a.scale = scale;
+  a.block_full = block_full;
+  a.window = window;
   a.opart = static_cast<float*>(workspace);
   a.ml = a.opart + static_cast<int64_t>(p.nsplit) * batch * heads * seq * dim;
   // out [B*S, H*D]; gate element (b, h, s, d) at gate + (b*S + s)*ldg + h*2D + d

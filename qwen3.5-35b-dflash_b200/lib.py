@@ -90,6 +90,13 @@ SIGNATURES = {
     "qw_lmhead_argmax": (_c.c_int, [P, P, P, P, I64, I64, I64, P]),
     "qw_accept": (_c.c_int, [P, I64, P, P, P, P, P, P, I64, I64, _c.c_int, P]),
     "qw_apply_commit": (_c.c_int, [P, P, P, P, I64, I64, P]),
+    "qw_attn_paged_masked": (_c.c_int, [P, P, P, P, I32, I32, P, I64, P, I64, I64, I64, I64, I64, F32, _c.c_int,
+                                        I32, P, P]),
+    "qw_draft_prep": (_c.c_int, [P, I64, _c.c_int, P, P, F32, F32, P, P, P, P, I32, I32, P, P, P, I64, I64, I64,
+                                 I64, I64, P]),
+    "qw_swiglu": (_c.c_int, [P, P, I64, I64, P]),
+    "qw_draft_block_embed": (_c.c_int, [P, P, I32, P, I64, I64, I64, P]),
+    "qw_draft_propose": (_c.c_int, [P, I64, P, P, I64, I64, P]),
     "qw_wait_status": (_c.c_int, [P, _c.c_int, P]),
     "qw_check_wait_status": (_c.c_int, [_c.c_int, P]),
     "qw_debug_inject_wait_timeout": (_c.c_int, [I64, I64]),

@@ -102,3 +102,34 @@ def init_value(name: str, shape, seed: int, std: float = 0.02) -> np.ndarray:
 def init_weights(c: TargetConfig, seed: int = 17, std: float = 0.02) -> dict[str, np.ndarray]:
     """All target.* tensors as float32 numpy arrays (small configurations only)."""
     return {name: init_value(name, shape, seed, std) for name, shape in weight_shapes(c).items()}
+
+
+def draft_weight_shapes(d) -> dict[str, tuple[int, ...]]:
+    """Tensors of the DFlash draft by the reference's parameter names
+    (model/qwen35_moe_dflash/model.py:310-391): layers.*, norm, fc, hidden_norm."""
+    h, hd = d.hidden_size, d.head_dim
+    q, kv = d.num_attention_heads * hd, d.num_key_value_heads * hd
+    shapes = {"norm.weight": (h,), "fc.weight": (h, d.feature_size), "hidden_norm.weight": (h,)}
+    for i in range(d.num_hidden_layers):
+        p = f"layers.{i}"
+        shapes.update({p + ".input_layernorm.weight": (h,), p + ".post_attention_layernorm.weight": (h,),
+                       p + ".self_attn.q_proj.weight": (q, h), p + ".self_attn.k_proj.weight": (kv, h),
+                       p + ".self_attn.v_proj.weight": (kv, h), p + ".self_attn.o_proj.weight": (h, q),
+                       p + ".self_attn.q_norm.weight": (hd,), p + ".self_attn.k_norm.weight": (hd,),
+                       p + ".mlp.gate_proj.weight": (d.intermediate_size, h),
+                       p + ".mlp.up_proj.weight": (d.intermediate_size, h),
+                       p + ".mlp.down_proj.weight": (h, d.intermediate_size)})
+    return shapes
+
+
+def init_draft_weights(d, seed: int = 29, std: float = 0.04) -> dict[str, np.ndarray]:
+    """Seeded draft weights (bf16 values): matrices N(0, std), norm weights (stored as
+    the effective scale) 1 + N(0, 0.1)."""
+    out = {}
+    for name, shape in draft_weight_shapes(d).items():
+        if name.endswith("norm.weight"):
+            value = 1.0 + _rng(seed, name).normal(0.0, 0.1, shape)
+        else:
+            value = _rng(seed, name).normal(0.0, std, shape)
+        out[name] = _bf16(value.astype(np.float32))
+    return out

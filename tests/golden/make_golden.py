@@ -11,8 +11,12 @@ Fixtures:
   tiny_session.npz    FusedTargetModel + FusedTargetSession (fp16, fp32 recurrent
                       state) on the tiny configuration: greedy decode, then
                       block verify / commit rounds with seeded proposals.
+  draft.npz           the reference's DFlashDraftModel (bf16) of the tiny draft
+                      configuration: context features -> draft hidden rows and the
+                      proposals of the target's lm_head, for two context lengths.
 
 Usage:  QW_REFERENCE=<reference checkout> python tests/golden/make_golden.py
+        (QW_GOLDEN_ONLY=draft: only draft.npz)
 """
 from __future__ import annotations
 
@@ -198,12 +202,52 @@ def make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fuse
         final_position=np.int32(state.position), state_sums=np.asarray(sums, np.float64))
 
 
+def make_draft():
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from qwen35_dflash_b200 import config as qcfg, synthetic
+    from qwen35_moe_dflash.config import Qwen35DFlashConfig
+    from qwen35_moe_dflash.model import DFlashDraftModel
+
+    tc, dc = qcfg.TINY, qcfg.TINY_DRAFT
+    raw = dc.to_reference_dict(tc.vocab_size, tc.num_hidden_layers)
+    model = DFlashDraftModel(Qwen35DFlashConfig.from_dict(raw), dtype=torch.bfloat16).eval()
+    weights = synthetic.init_draft_weights(dc)
+    with torch.no_grad():
+        for name, param in model.named_parameters():
+            param.copy_(torch.from_numpy(weights[name]).to(torch.bfloat16))
+    target = synthetic.init_weights(tc, seed=17)
+    embed = torch.from_numpy(target["target.embed_tokens.weight"]).to(torch.bfloat16)
+    lm_head = torch.from_numpy(target["target.lm_head.weight"]).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(31)
+    out = {}
+    for case, ctx in enumerate((5, 20)):
+        feats = torch.randn(1, ctx, dc.feature_size, generator=g).to(torch.bfloat16)
+        anchor = int(torch.randint(0, tc.vocab_size, (1,), generator=g))
+        ids = torch.tensor([[anchor] + [dc.mask_token_id] * (dc.block_size - 1)])
+        positions = torch.arange(ctx + dc.block_size).view(1, -1)
+        with torch.inference_mode():
+            noise = model.embed_block(ids, embed)
+            hidden = model.draft_hidden(feats, noise, positions)
+            top1 = torch.argmax(torch.nn.functional.linear(hidden, lm_head), -1)
+        out[f"features_{case}"] = feats[0].float().numpy()
+        out[f"anchor_{case}"] = np.int32(anchor)
+        out[f"hidden_{case}"] = hidden[0].float().numpy()
+        out[f"top1_{case}"] = top1[0].numpy().astype(np.int32)
+    np.savez_compressed(os.path.join(HERE, "draft.npz"), **out)
+
+
 def main():
     fused_ops, ModuleFusedOps, FusedTargetModel, FusedTargetSession = _import_reference()
+    if os.environ.get("QW_GOLDEN_ONLY") == "draft":
+        make_draft()
+        return
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     make_ops(fused_ops)
     make_topk()
     make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops)
+    make_draft()
     for name in sorted(os.listdir(HERE)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(HERE, name)))

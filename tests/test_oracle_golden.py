@@ -148,3 +148,31 @@ def test_tiny_session_fp16_matches_reference(golden):
     assert agree >= 0.95 * total, (agree, total)
     assert same_acc >= 6, same_acc
     assert state.position == int(d["final_position"])
+
+
+def test_draft_oracle_matches_reference_draft_model(golden):
+    """The numpy draft forward against the reference's own DFlashDraftModel (bf16) on the
+    tiny draft configuration, with a context shorter and longer than the sliding window:
+    hidden rows within bf16 rounding drift, proposals equal except on near-ties."""
+    from qwen35_dflash_b200 import config as qcfg, synthetic
+    from oracle.draft_np import OracleDraft
+    d = golden("draft.npz")
+    tc, dc = qcfg.TINY, qcfg.TINY_DRAFT
+    target = synthetic.init_weights(tc, seed=17)
+    oracle = OracleDraft(dc, synthetic.init_draft_weights(dc))
+    for case in (0, 1):
+        feats = d[f"features_{case}"]
+        C = len(feats)
+        ctx = oracle.context(feats, np.arange(C))
+        ids = [int(d[f"anchor_{case}"])] + [dc.mask_token_id] * (dc.block_size - 1)
+        hidden = oracle.block(ids, C, ctx, target["target.embed_tokens.weight"])
+        want = d[f"hidden_{case}"]
+        diff = np.abs(hidden[1:] - want)
+        tol = 2e-2 + 1e-2 * np.abs(want)
+        assert (diff <= tol).mean() >= 0.995, (case, float(diff.max()))
+        top, logits = oracle.draft(feats, ids[0], target["target.embed_tokens.weight"],
+                                   target["target.lm_head.weight"], return_logits=True)
+        ref = d[f"top1_{case}"]
+        for i, (a, b) in enumerate(zip(top, ref)):
+            if a != b:   # only where the oracle's two candidates are within 4 bf16 ulps
+                assert abs(logits[i, a] - logits[i, b]) <= 4 * 2 ** -7 * max(1.0, abs(logits[i, b])), (case, i, a, b)
