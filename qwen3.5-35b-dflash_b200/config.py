@@ -150,6 +150,13 @@ TINY = TargetConfig(
 )
 
 
+# The tiny target shaped for an original group-256 checkpoint (every contraction
+# dimension a multiple of 256, every quantised projection a multiple of 16 rows):
+# expert FFN and shared expert 256, GDN 8 QK / 16 V heads, group 128.
+TINY_G256 = replace(TINY, moe_intermediate_size=256, shared_expert_intermediate_size=256, quant_group=128,
+                    linear_num_key_heads=8, linear_num_value_heads=16)
+
+
 def with_layers(config: TargetConfig, n_layers: int) -> TargetConfig:
     """Same architecture with fewer decoder layers (for tests), taps clipped."""
     taps = tuple(i for i in config.feature_layers if i < n_layers) or (n_layers - 1,)

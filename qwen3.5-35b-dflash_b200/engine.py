@@ -69,18 +69,26 @@ class LayerWeights:
     shared_down: torch.Tensor | None = None
 
 
-def pack_weights(cfg: TargetConfig, get, device) -> tuple[dict, list[LayerWeights]]:
+def pack_weights(cfg: TargetConfig, get, device, quantized=None) -> tuple[dict, list[LayerWeights]]:
     """Pack all target weights.  ``get(name) -> float tensor on `device``` (bf16-exact
-    values outside the W4 scope)."""
+    values outside the W4 scope).  ``quantized(name) -> (int8 q, bf16 scales)``, when
+    given, supplies the W4 projections already quantised (the original checkpoint's
+    values); otherwise ``get``'s values are quantised here."""
     g = cfg.quant_group
 
     def q4(*names):
+        if quantized is not None:
+            parts = [quantized(n) for n in names]
+            return w4.pack_w4(torch.cat([p[0] for p in parts], -2), torch.cat([p[1] for p in parts], -2), g)
         mats = [get(n).float() for n in names]
         mat = torch.cat(mats, -2) if len(mats) > 1 else mats[0]
         q, s = w4.quantize(mat, g)
         return w4.pack_w4(q, s, g)
 
     def experts(name):
+        if quantized is not None:
+            q, s = quantized(name)
+            return torch.cat([w4.pack_w4(q[e0:e0 + 64], s[e0:e0 + 64], g) for e0 in range(0, q.shape[0], 64)])
         t = get(name)
         out = []
         for e0 in range(0, t.shape[0], 64):

@@ -14,9 +14,14 @@ Fixtures:
   draft.npz           the reference's DFlashDraftModel (bf16) of the tiny draft
                       configuration: context features -> draft hidden rows and the
                       proposals of the target's lm_head, for two context lengths.
+  original/           two small shards in the original group-256 quantised layout
+                      (data-0000{1,2}.safetensors, written here) and what the
+                      reference's OriginalQuantWeights / canonicalkeys make of them
+                      (expect.json: key mapping, rejected names; expect.npz: the
+                      logical int4 values and scales of each tensor).
 
 Usage:  QW_REFERENCE=<reference checkout> python tests/golden/make_golden.py
-        (QW_GOLDEN_ONLY=draft: only draft.npz)
+        (QW_GOLDEN_ONLY=draft: only draft.npz; =original: only original/)
 """
 from __future__ import annotations
 
@@ -238,16 +243,73 @@ def make_draft():
     np.savez_compressed(os.path.join(HERE, "draft.npz"), **out)
 
 
+def make_original():
+    import json
+    sys.path.insert(0, os.path.dirname(HERE))
+    sys.path.insert(0, ROOT)
+    from original_fixture import quantize_g256, write_safetensors
+    from qwen35_moe_dflash.target.original_quant import OriginalQuantWeights, canonicalkeys
+
+    rng = np.random.default_rng(41)
+    d = os.path.join(HERE, "original")
+    os.makedirs(d, exist_ok=True)
+    tensors = [("target.layers.0.linear_attn.out_proj.weight", (32, 512), np.float16),
+               ("target.layers.3.self_attn.q_proj.weight", (48, 256), np.float32),
+               ("target.layers.1.mlp.experts.down_proj", (2, 32, 512), np.float16),
+               ("target.layers.2.mlp.gate.weight", (16, 256), np.float32),
+               ("target.lm_head.weight", (64, 256), np.float16)]
+    shards = [{}, {}]
+    for i, (name, shape, sdt) in enumerate(tensors):
+        w = rng.normal(0, 0.02, shape).astype(np.float32)
+        w[..., :256] *= 3.0
+        q, sc = quantize_g256(w)
+        wkey, skey = canonicalkeys(name)
+        shards[i % 2][wkey] = q
+        shards[i % 2][skey] = (sc if "experts" in name else sc[..., None]).astype(sdt)
+    for i, t in enumerate(shards):
+        write_safetensors(os.path.join(d, f"data-0000{i + 1}.safetensors"), t)
+    ref = OriginalQuantWeights(d)
+    arrays = {}
+    for i, (name, shape, _) in enumerate(tensors):
+        q, sc = ref.logical(name, shape)
+        arrays[f"q{i}"] = np.asarray(q)
+        arrays[f"s{i}"] = np.asarray(sc)
+    names = [t[0] for t in tensors] + [
+        "target.layers.7.linear_attn.in_proj_qkv.weight", "target.layers.7.linear_attn.in_proj_z.weight",
+        "target.layers.7.linear_attn.in_proj_b.weight", "target.layers.7.linear_attn.in_proj_a.weight",
+        "target.layers.39.self_attn.k_proj.weight", "target.layers.39.self_attn.v_proj.weight",
+        "target.layers.39.self_attn.o_proj.weight", "target.layers.5.mlp.experts.gate_up_proj",
+        "target.layers.5.mlp.shared_expert.gate_proj.weight", "target.layers.5.mlp.shared_expert.up_proj.weight",
+        "target.layers.5.mlp.shared_expert.down_proj.weight"]
+    rejected = {}
+    for name in ("target.embed_tokens.weight", "target.layers.0.input_layernorm.weight",
+                 "target.layers.5.mlp.shared_expert_gate.weight", "target.layers.0.linear_attn.A_log",
+                 "target.layers.5.mlp.experts.gate_up_proj.weight", "draft.fc.weight", "target.norm.weight"):
+        try:
+            canonicalkeys(name)
+        except ValueError as e:
+            rejected[name] = str(e)
+    exp = {"keys": {n: list(canonicalkeys(n)) for n in names}, "rejected_names": rejected,
+           "logical": [[n, list(s)] for n, s, _ in tensors]}
+    with open(os.path.join(d, "expect.json"), "w") as f:
+        json.dump(exp, f, indent=1)
+    np.savez_compressed(os.path.join(d, "expect.npz"), **arrays)
+
+
 def main():
     fused_ops, ModuleFusedOps, FusedTargetModel, FusedTargetSession = _import_reference()
     if os.environ.get("QW_GOLDEN_ONLY") == "draft":
         make_draft()
+        return
+    if os.environ.get("QW_GOLDEN_ONLY") == "original":
+        make_original()
         return
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     make_ops(fused_ops)
     make_topk()
     make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops)
     make_draft()
+    make_original()
     for name in sorted(os.listdir(HERE)):
         if name.endswith(".npz"):
             print(name, os.path.getsize(os.path.join(HERE, name)))
