@@ -26,11 +26,13 @@
 // heap fallback) run on lane 0.  Values compared are the bf16 router logits, which
 // order exactly as torch's fp32 probabilities (exp is monotone; equal logits give
 // equal probabilities).
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
 #include "bulk_ring.cuh"
 #include "stream_gemm.cuh"
+#include "umma.cuh"
 
 namespace qw {
 
@@ -975,6 +977,7 @@ struct XtArgs {
   MoeArgs<__nv_bfloat16> m;
   int32_t* status;      // g_moe_wait_status on the launching device
   long long limit;
+  int dense_min;        // slots with at least this many pairs go to the tcgen05 kernels (0: none)
 };
 
 // Sticky status of the expert kernels' bounded waits (bulk_ring.cuh): set when a wait
@@ -1386,13 +1389,19 @@ __device__ __forceinline__ int gr_pairs(const MoeArgs<ET>& a, const RouteView& r
   return rv.pair_off[ai + 1] - rv.pair_off[ai];
 }
 
-// Every thread: the table with `per` items per (slot, chunk).  The slots' item counts
-// load in parallel; warp 0 scans them 32 at a time.
+// Every thread: the table with `per` items per (slot, chunk of `chunk` pairs).  A slot
+// with at least dense_min pairs (dense_min > 0) belongs to the tcgen05 kernels: with
+// dense false it gets no items here, with dense true only such slots get items.  The
+// slots' item counts load in parallel; warp 0 scans them 32 at a time.
 template <typename ET>
-__device__ void gr_build_table(GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int per) {
+__device__ void gr_build_table(GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int per, int dense_min = 0,
+                               bool dense = false, int chunk = GR_CHUNK) {
   const int ns = a.has_shared + *rv.n_active;
-  for (int sl = threadIdx.x; sl < ns; sl += blockDim.x)
-    tb.first[sl] = (gr_pairs(a, rv, sl) + GR_CHUNK - 1) / GR_CHUNK * per;
+  for (int sl = threadIdx.x; sl < ns; sl += blockDim.x) {
+    const int np = gr_pairs(a, rv, sl);
+    const bool is_dense = dense_min > 0 && np >= dense_min;
+    tb.first[sl] = is_dense == dense ? (np + chunk - 1) / chunk * per : 0;
+  }
   __syncthreads();
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
@@ -1475,7 +1484,7 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_grouped_kernel(XtA
   pdl_wait();   // the lists (and the received rows) come from the predecessor
   pdl_trigger();
   const int J = I / 16, per = J / XT_UP_WARPS;
-  gr_build_table(tb, a, rv, per);
+  gr_build_table(tb, a, rv, per, args.dense_min);
   const int n_items = tb.total;
   const int i0 = static_cast<int>(static_cast<int64_t>(n_items) * blockIdx.x / gridDim.x);
   const int i1 = static_cast<int>(static_cast<int64_t>(n_items) * (blockIdx.x + 1) / gridDim.x);
@@ -1649,7 +1658,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(X
                       EP_ROUND - pieces);
     }
   }
-  gr_build_table(tb, a, rv, nrb);
+  gr_build_table(tb, a, rv, nrb, args.dense_min);
   const int nu = tb.total;
   const int my_units = blockIdx.x < nu ? (nu - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int Q = my_units * spw;
@@ -1755,6 +1764,347 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(X
     }
   }
   cp_async_wait<0>();
+}
+
+// ------------------------------------------------------------------ dense experts (tcgen05)
+// An expert that receives at least XtArgs::dense_min tokens is a real contraction: its
+// gate/up and down run on the 5th-generation tensor cores instead of the grouped
+// mma.sync kernels (which then skip it).  Item = (slot, token tile of up to TC_N pairs,
+// row block of 128 weight rows).  Per 128-wide K group (one quantisation group) the CTA
+// expands the rows' int4 values to fp16 integers in shared memory, converts the tile's
+// activation rows to fp16 beside them (both operands K-major, canonical no-swizzle
+// layout: umma.cuh), and one thread issues the group's eight K = 16 tcgen05.mma steps
+// into a fresh fp32 accumulator in tensor memory (M = 128 weight rows, N = the tile's
+// pairs rounded up to 16; two accumulators alternate).  While the tensor core works on
+// group g, every thread reads group g - 1's accumulator (tcgen05.ld) and adds it, times
+// its row's bf16 scale, into fp32 registers: the per-group partial sums and the scaling
+// of the grouped kernels, so the two paths round alike (a single accumulator chained
+// over all of K lost low bits in the tensor core's fp32 additions).  Shared-memory stages
+// form a ring of TC_ST; a stage is rewritten only after the MMAs that read it committed
+// to its mbarrier, an accumulator only after every thread read it (all waits bounded).
+// Epilogue: gate/up rows of one intermediate column meet through shared memory for
+// SiLU(gate) * up in the reference's rounding order; down writes the fp32 expert output
+// rows the combine reads.
+constexpr int TC_THREADS = 256;
+constexpr int TC_N = 128;                       // pairs per item, at most
+constexpr int TC_KS = 128;                      // K per stage (one quantisation group)
+constexpr int TC_ST = 3;                        // ring stages
+constexpr int TC_A_BYTES = 128 * TC_KS * 2;     // 128 weight rows x 128 K, fp16
+constexpr int TC_B_BYTES = TC_N * TC_KS * 2;    // TC_N rows x 128 K, fp16
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr int TC_HEAD = 1024 + (static_cast<int>(sizeof(GrTable)) + 1023) / 1024 * 1024;
+constexpr size_t TC_SMEM = TC_HEAD + static_cast<size_t>(TC_ST) * TC_STAGE_BYTES;
+constexpr uint32_t TC_TMEM_COLS = 2 * TC_N;     // two accumulators
+static_assert(TC_SMEM <= 227 * 1024, "tcgen05 expert stages exceed shared memory");
+
+// Byte offset of (row, K octet) in a canonical K-major tile of TC_KS columns.
+__device__ __forceinline__ int tc_off(int row, int octet) {
+  return ((row >> 3) * (TC_KS / 8) + octet) * 128 + (row & 7) * 16;
+}
+
+// Expand one W4 task of a 16-row stream tile's K group (16 bytes of nibbles: lane
+// `ln`'s steps 4v .. 4v + 3) to the fp16 integers q = u - 8 of rows row0 + gid and
+// row0 + gid + 8 of the A tile.  (0x6400 | u is the fp16 1024 + u; minus 1032 is exact.)
+__device__ __forceinline__ void tc_expand_task(uint8_t* As, const uint8_t* chunk, int v, int ln, int row0) {
+  const uint4 wv = ldg_stream(chunk + v * 512 + ln * 16);
+  const int gid = ln >> 2, tig = ln & 3;
+  const __half2 off = __half2half2(__ushort_as_half(0x6408));   // 1032
+  const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {           // steps (4v + 2p, 4v + 2p + 1): K octet 8v + 4p + tig
+    const int octet = 8 * v + 4 * p + tig;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {         // row gid (nibbles 0, 2, 4, 6) or gid + 8 (1, 3, 5, 7)
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t x = w[2 * p + e] >> (4 * h);
+        const uint32_t c01 = (x & 0x000F000Fu) | 0x64006400u;          // K 4e + 0, 4e + 1
+        const uint32_t c23 = ((x >> 8) & 0x000F000Fu) | 0x64006400u;   // K 4e + 2, 4e + 3
+        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&c01), off);
+        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&c23), off);
+        o[2 * e] = *reinterpret_cast<const uint32_t*>(&q01);
+        o[2 * e + 1] = *reinterpret_cast<const uint32_t*>(&q23);
+      }
+      *reinterpret_cast<uint4*>(As + tc_off(row0 + gid + 8 * h, octet)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// The item's slot, token tile and row block (table built with TC_N-pair chunks).
+template <typename ET>
+__device__ __forceinline__ void tc_item(const GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int item,
+                                        int per, bool up, int& slot, int& tt, int& rb, const uint8_t*& w, int& np,
+                                        int& pbase) {
+  slot = gr_slot_of(tb, item);
+  const int r = item - tb.first[slot];
+  tt = r / per;
+  rb = r % per;
+  np = min(TC_N, gr_pairs(a, rv, slot) - tt * TC_N);
+  if (a.has_shared && slot == 0) {
+    w = up ? a.sgu : a.sdn;
+    pbase = -1;
+  } else {
+    const int ai = slot - a.has_shared;
+    const int e = rv.active[ai];
+    w = up ? a.gu + e * a.gu_stride : a.dn + e * a.dn_stride;
+    pbase = rv.pair_off[ai];
+  }
+}
+
+struct TcRing {
+  uint8_t* stages;
+  uint64_t* done;     // TC_ST barriers: the MMAs that read the stage committed
+  uint64_t* full;     // 2 barriers: accumulator (g % 2) holds group g
+  uint32_t tmem;
+  int g;              // groups issued so far (all items of the CTA)
+};
+
+// Group kg of an item: the A tile (8 stream tiles: tile0 .. + 3 -> rows 0-63, tile1 ..
+// + 3 -> rows 64-127) and the B tile (pairs [0, nn), rows >= np zero) into the next
+// stage, then one thread issues the MMAs into accumulator g % 2.  False (for every
+// thread) when a bounded wait expired.
+template <bool UP>
+__device__ __forceinline__ bool tc_issue(TcRing& r, const XtArgs& args, const uint8_t* w, int kg, int tile0,
+                                         int tile1, int K, const int (&rows)[TC_N / 16], int np, int nn,
+                                         const void* src, int64_t src_ld, uint32_t idesc) {
+  using Fmt = W4Fmt<128>;
+  const int st = r.g % TC_ST;
+  const bool free_ok = r.g < TC_ST || mbar_wait(r.done + st, ((r.g / TC_ST) - 1) & 1, args.status, args.limit);
+  if (!__syncthreads_and(free_ok)) return false;
+  uint8_t* As = r.stages + st * TC_STAGE_BYTES;
+  uint8_t* Bs = As + TC_A_BYTES;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {           // A: 8 stream tiles x 64 tasks of 16 bytes
+    const int task = threadIdx.x + i * TC_THREADS;
+    const int t8 = task >> 6, v = (task >> 5) & 1, ln = task & 31;
+    const int tile = t8 < 4 ? tile0 + t8 : tile1 + (t8 - 4);
+    tc_expand_task(As, w + Fmt::tile_offset(tile, K, 0) + static_cast<int64_t>(kg) * Fmt::CHB, v, ln, t8 * 16);
+  }
+  const int octet = threadIdx.x & 15;     // B: pair row n = threadIdx.x / 16 + 16 i
+#pragma unroll
+  for (int i = 0; i < TC_N / 16; ++i) {
+    const int n = (threadIdx.x >> 4) + 16 * i;
+    if (n < nn) {
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (n < np) {
+        if constexpr (UP) {
+          v = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(
+              static_cast<const __nv_bfloat16*>(src) + static_cast<int64_t>(rows[i]) * src_ld + kg * TC_KS + octet * 8)));
+        } else {
+          v = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(src) +
+                                                   static_cast<int64_t>(rows[i]) * src_ld + kg * TC_KS + octet * 8));
+        }
+      }
+      *reinterpret_cast<uint4*>(Bs + tc_off(n, octet)) = v;
+    }
+  }
+  fence_proxy_async();   // the generic-proxy tile stores before the tensor core reads them
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    umma::fence_after_sync();
+    const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs);
+    const uint32_t d = r.tmem + (r.g & 1) * TC_N;
+#pragma unroll
+    for (int s = 0; s < TC_KS / 16; ++s)
+      umma::mma_f16(d, umma::smem_desc(a0 + s * 256, 128, (TC_KS / 8) * 128),
+                    umma::smem_desc(b0 + s * 256, 128, (TC_KS / 8) * 128), idesc, s > 0);
+    umma::commit(r.done + st);
+    umma::commit(r.full + (r.g & 1));
+  }
+  ++r.g;
+  return true;
+}
+
+// Every thread: wait (bounded) for group `g`'s accumulator and add its columns
+// [c0, c0 + 64) of this warp's 32 rows, times the row's scale, into acc.
+__device__ __forceinline__ bool tc_accumulate(const TcRing& r, const XtArgs& args, int g, int c0, int nn,
+                                              float scale, float (&acc)[64]) {
+  const bool ok = __syncthreads_and(mbar_wait(r.full + (g & 1), (g >> 1) & 1, args.status, args.limit));
+  if (!ok) return false;
+  umma::fence_after_sync();
+  const int q = (threadIdx.x >> 5) & 3;
+  const uint32_t base = r.tmem + (static_cast<uint32_t>(32 * q) << 16) + (g & 1) * TC_N + c0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    if (c0 + 16 * c < nn) {
+      float v[16];
+      umma::ld16(base + 16 * c, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[16 * c + j] = fmaf(scale, v[j], acc[16 * c + j]);
+    }
+  }
+  umma::fence_before_sync();
+  return true;
+}
+
+// The bf16 scale of A-tile row `row` in group kg (tile0 / tile1 as in tc_issue).
+__device__ __forceinline__ float tc_scale(const uint8_t* w, int kg, int tile0, int tile1, int K, int row) {
+  using Fmt = W4Fmt<128>;
+  const int t8 = row >> 4, rr = row & 15;
+  const int tile = t8 < 4 ? tile0 + t8 : tile1 + (t8 - 4);
+  const uint8_t* sc = w + Fmt::tile_offset(tile, K, 0) + static_cast<int64_t>(kg) * Fmt::CHB + 8 * 128;
+  const int p = 2 * (rr & 7) + (rr >> 3);   // position 2 gid + h <-> row gid + 8 h
+  return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(sc) + p));
+}
+
+// All groups of one item; acc = this thread's 64 fp32 sums (row 32 (warp % 4) + lane,
+// columns 64 (warp / 4) ..).  False when a bounded wait expired.
+template <bool UP>
+__device__ __forceinline__ bool tc_item_run(TcRing& r, const XtArgs& args, const uint8_t* w, int ngroups, int tile0,
+                                            int tile1, int K, const int (&rows)[TC_N / 16], int np, int nn,
+                                            const void* src, int64_t src_ld, float (&acc)[64]) {
+  const uint32_t idesc = umma::idesc_f16_f32(128, nn);
+  const int row = 32 * ((threadIdx.x >> 5) & 3) + (threadIdx.x & 31);
+  const int c0 = 64 * (threadIdx.x >> 7);
+#pragma unroll
+  for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+  for (int kg = 0; kg < ngroups; ++kg) {
+    if (!tc_issue<UP>(r, args, w, kg, tile0, tile1, K, rows, np, nn, src, src_ld, idesc)) return false;
+    if (kg > 0 && !tc_accumulate(r, args, r.g - 2, c0, nn, tc_scale(w, kg - 1, tile0, tile1, K, row), acc))
+      return false;
+  }
+  return tc_accumulate(r, args, r.g - 1, c0, nn, tc_scale(w, ngroups - 1, tile0, tile1, K, row), acc);
+}
+
+// Setup common to both kernels: barriers, the tensor-memory allocation (warp 0).
+__device__ __forceinline__ void tc_setup(uint8_t* smem, TcRing& r) {
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint32_t* tbase = reinterpret_cast<uint32_t*>(smem + 256);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < TC_ST + 2; ++i) mbar_init(bars + i, 1);
+  }
+  fence_barrier_init();
+  if (threadIdx.x < 32) umma::tmem_alloc(tbase, TC_TMEM_COLS);
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  r.stages = smem + TC_HEAD;
+  r.done = bars;
+  r.full = bars + TC_ST;
+  r.tmem = *tbase;
+  r.g = 0;
+}
+
+// Teardown: every MMA this CTA issued has completed (or a bounded wait gave up, after
+// which the last group's commit is waited for once more, bounded), then warp 0 frees the
+// columns.
+__device__ __forceinline__ void tc_teardown(TcRing& r, const XtArgs& args, bool ok) {
+  if (!ok && r.g > 0) {
+    const int last = r.g - 1;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(r.full + (last & 1), (last >> 1) & 1))
+      if (clock64() - t0 > args.limit) break;
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    umma::fence_after_sync();
+    umma::tmem_free(r.tmem, TC_TMEM_COLS);
+  }
+}
+
+// Gate/up of the dense slots.  Row block rb = intermediate columns [64 rb, 64 rb + 64):
+// A rows 0-63 are their gate rows (stream tiles 4 rb ..), rows 64-127 their up rows
+// (tiles I / 16 + 4 rb ..); h = round(round(SiLU(round(gate))) * round(up)) per pair,
+// stored as fp16 like the grouped kernel's.
+__global__ void __launch_bounds__(TC_THREADS, 1) moe_up_tc_kernel(XtArgs args) {
+  const MoeArgs<__nv_bfloat16>& a = args.m;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  GrTable& tb = *reinterpret_cast<GrTable*>(smem + 1024);
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  const int H = a.H, I = a.I, per = I / 64;
+  pdl_wait();   // the lists come from the predecessor
+  pdl_trigger();
+  gr_build_table(tb, a, rv, per, args.dense_min, true, TC_N);
+  if (blockIdx.x >= tb.total) return;
+  TcRing r;
+  tc_setup(smem, r);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, row = 32 * q + lane, c0 = 64 * (warp >> 2);
+  bool ok = true;
+  for (int it = blockIdx.x; it < tb.total && ok; it += gridDim.x) {
+    int sl, tt, rb, np, pb;
+    const uint8_t* w;
+    tc_item(tb, a, rv, it, per, true, sl, tt, rb, w, np, pb);
+    const int nn = (np + 15) & ~15;
+    int rows[TC_N / 16];
+#pragma unroll
+    for (int i = 0; i < TC_N / 16; ++i) {
+      const int n = min((threadIdx.x >> 4) + 16 * i, np - 1);
+      rows[i] = pb < 0 ? tt * TC_N + n : rv.pair_tok[pb + tt * TC_N + n];
+    }
+    float acc[64];
+    ok = tc_item_run<true>(r, args, w, H / TC_KS, 4 * rb, I / 16 + 4 * rb, H, rows, np, nn, a.x, H, acc);
+    if (!ok) break;
+    // the up rows (quarters 2, 3) go through the first stage (idle: every MMA is done)
+    float* ubuf = reinterpret_cast<float*>(r.stages);   // [64][TC_N + 1]
+    if (q >= 2) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (c0 + j < nn) ubuf[(row - 64) * (TC_N + 1) + c0 + j] = rbf(acc[j]);
+    }
+    __syncthreads();
+    if (q < 2) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const int n = c0 + j;
+        if (n < np) {
+          const float gr = rbf(acc[j]), ur = ubuf[row * (TC_N + 1) + n];
+          const float h = rbf(rbf(silu_f(gr)) * ur);
+          const int pi = tt * TC_N + n;
+          const int64_t hrow = pb < 0 ? static_cast<int64_t>(a.T) * a.k + pi : pb + pi;
+          reinterpret_cast<__half*>(a.hbuf)[hrow * I + rb * 64 + row] = __float2half_rn(h);
+        }
+      }
+    }
+    __syncthreads();   // ubuf free for the next item's stages
+  }
+  tc_teardown(r, args, ok);
+}
+
+// Down of the dense slots.  Row block rb = output columns [128 rb, 128 rb + 128) (stream
+// tiles 8 rb ..); K = I from the fp16 h rows; fp32 outputs to part[token][slot].
+__global__ void __launch_bounds__(TC_THREADS, 1) moe_down_tc_kernel(XtArgs args) {
+  const MoeArgs<__nv_bfloat16>& a = args.m;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  GrTable& tb = *reinterpret_cast<GrTable*>(smem + 1024);
+  const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
+  const int H = a.H, I = a.I, per = H / 128;
+  pdl_wait();   // h comes from the predecessors (gate/up)
+  pdl_trigger();
+  gr_build_table(tb, a, rv, per, args.dense_min, true, TC_N);
+  if (blockIdx.x >= tb.total) return;
+  TcRing r;
+  tc_setup(smem, r);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = 32 * (warp & 3) + lane, c0 = 64 * (warp >> 2);
+  bool ok = true;
+  for (int it = blockIdx.x; it < tb.total && ok; it += gridDim.x) {
+    int sl, tt, rb, np, pb;
+    const uint8_t* w;
+    tc_item(tb, a, rv, it, per, false, sl, tt, rb, w, np, pb);
+    const int nn = (np + 15) & ~15;
+    const int64_t hb = (pb < 0 ? static_cast<int64_t>(a.T) * a.k : pb) + tt * TC_N;
+    int rows[TC_N / 16];
+#pragma unroll
+    for (int i = 0; i < TC_N / 16; ++i) rows[i] = static_cast<int>(hb) + min((threadIdx.x >> 4) + 16 * i, np - 1);
+    float acc[64];
+    ok = tc_item_run<false>(r, args, w, I / TC_KS, 8 * rb, 8 * rb + 4, I, rows, np, nn, a.hbuf, I, acc);
+    if (!ok) break;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const int n = c0 + j;
+      if (n < np) {
+        const int pi = tt * TC_N + n;
+        int tok, slot;
+        if (pb < 0) { tok = pi; slot = a.k; }
+        else { tok = rv.pair_tok[pb + pi]; slot = rv.pair_slot[pb + pi]; }
+        a.part[(static_cast<int64_t>(tok) * (a.k + 1) + slot) * H + rb * 128 + row] = acc[j];
+      }
+    }
+  }
+  tc_teardown(r, args, ok);
 }
 
 // Combine (fused/model.py:296-307 with fused_ops.py:165-172): per token, the routed
@@ -2052,7 +2402,7 @@ static int launch_experts_bulk(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p,
   });
   if (err != cudaSuccess) return cuda_status(err, "moe bulk smem attribute");
   const WaitInjection inj = wait_injection();
-  XtArgs xa{a, status, inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT};
+  XtArgs xa{a, status, inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT, 0};
   const int grid = sm_count();
   if (up) {
     QW_LAUNCH_PDL("moe up (bulk)", moe_up_bulk_kernel<G>, dim3(grid), dim3(XT_UP_WARPS * 32), p.up_smem, s, xa);
@@ -2094,6 +2444,18 @@ static bool grouped_plan(const MoeArgs<__nv_bfloat16>& a, XtPlan& p) {
   return p.down_spw > 0 && p.up_smem <= GR_SMEM_LIMIT && p.down_smem <= GR_SMEM_LIMIT;
 }
 
+// Tokens per expert from which an expert runs on the tcgen05 kernels (0: never); see
+// qw_moe_dense_threshold.
+static std::atomic<int> g_dense_min{32};
+
+// The dense path's shape limits: group 128 (one quantisation group per K stage), K and
+// the row blocks whole, 16-byte aligned activation rows.
+template <int G>
+static int dense_min_for(const MoeArgs<__nv_bfloat16>& a, const EpSend* ep) {
+  if (G != 128 || ep || a.H % 128 || a.I % 128 || (reinterpret_cast<uintptr_t>(a.x) & 15)) return 0;
+  return g_dense_min.load(std::memory_order_relaxed);
+}
+
 template <int G>
 static int launch_experts_grouped(const MoeArgs<__nv_bfloat16>& a, const XtPlan& p, cudaStream_t s, bool up,
                                   bool down, int32_t* status, const EpSend* ep = nullptr) {
@@ -2110,11 +2472,25 @@ static int launch_experts_grouped(const MoeArgs<__nv_bfloat16>& a, const XtPlan&
                                  static_cast<int>(GR_SMEM_LIMIT));
   });
   if (err != cudaSuccess) return cuda_status(err, "moe grouped smem attribute");
+  const int dmin = dense_min_for<G>(a, ep);
+  if (dmin > 0) {
+    static std::once_flag once_tc;
+    static cudaError_t err_tc = cudaSuccess;
+    std::call_once(once_tc, [] {
+      err_tc = cudaFuncSetAttribute(moe_up_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(TC_SMEM));
+      if (err_tc == cudaSuccess)
+        err_tc = cudaFuncSetAttribute(moe_down_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(TC_SMEM));
+    });
+    if (err_tc != cudaSuccess) return cuda_status(err_tc, "moe dense smem attribute");
+  }
   const WaitInjection inj = wait_injection();
-  XtArgs xa{a, status, inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT};
+  XtArgs xa{a, status, inj.limit > 0 ? inj.limit : QW_WAIT_LIMIT, dmin};
   const int grid = sm_count();
   if (up) {
     QW_LAUNCH_PDL("moe up (grouped)", moe_up_grouped_kernel<G>, dim3(grid), dim3(XT_UP_WARPS * 32), p.up_smem, s, xa);
+    if (dmin > 0) QW_LAUNCH_PDL("moe up (dense)", moe_up_tc_kernel, dim3(grid), dim3(TC_THREADS), TC_SMEM, s, xa);
   }
   if (down && ep) {
     if (p.down_ep_smem > GR_SMEM_LIMIT) return fail(QW_ERR_UNSUPPORTED, "moe_ep_experts: output tile does not fit");
@@ -2123,6 +2499,7 @@ static int launch_experts_grouped(const MoeArgs<__nv_bfloat16>& a, const XtPlan&
   } else if (down) {
     QW_LAUNCH_PDL("moe down (grouped)", moe_down_grouped_kernel<G, false>, dim3(grid), dim3(XT_DN_WARPS * 32),
                   p.down_smem, s, xa, p.down_tps, p.down_spw, EpSend{});
+    if (dmin > 0) QW_LAUNCH_PDL("moe down (dense)", moe_down_tc_kernel, dim3(grid), dim3(TC_THREADS), TC_SMEM, s, xa);
   }
   return QW_OK;
 }
@@ -2154,6 +2531,11 @@ static int launch_experts_w4(const MoeArgs<__nv_bfloat16>& a, cudaStream_t s, bo
 }  // namespace qw
 
 using namespace qw;
+
+extern "C" int32_t qw_moe_dense_threshold(int32_t tokens) {
+  if (tokens < 0) return g_dense_min.load();
+  return g_dense_min.exchange(tokens);
+}
 
 extern "C" int64_t qw_moe_workspace_bytes(int64_t tokens, int64_t hidden, int64_t experts, int64_t inter,
                                           int64_t top_k) {

@@ -55,6 +55,7 @@ SIGNATURES = {
                                  F32, P, P]),
     "qw_moe": (_c.c_int, [P, P, P, P, P, _c.c_int, I64, I64, I64, I64, I64, P, P, P]),
     "qw_moe_workspace_bytes": (I64, [I64, I64, I64, I64, I64]),
+    "qw_moe_dense_threshold": (I32, [I32]),
     "qw_moe_route": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, P]),
     "qw_moe_experts_w4_range": (_c.c_int, [P, P, P, P, P, I64, I64, I64, I64, I64, I32, I64, I64, P, P]),
     "qw_moe_ep_recv_workspace_bytes": (I64, [I64, I64, I64, I64, I64]),

@@ -9,7 +9,7 @@ import torch
 from oracle import fused_ops_np as F
 from oracle.numerics import bf16_round
 
-# BASELINE tolerance for bf16 outputs after dequant: |a - b| <= 2e-2 + 1e-2 |b|
+# The stated tolerance for bf16 outputs after dequant: |a - b| <= 2e-2 + 1e-2 |b|
 ATOL, RTOL = 2e-2, 1e-2
 
 

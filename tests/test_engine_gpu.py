@@ -280,7 +280,7 @@ def test_greedy_dflash_free_running_matches_oracle(cuda_lib, golden):
     and both sides' accepted sequences (accepted drafts + correction/bonus token) are
     compared.
 
-    BASELINE's gate: identical accepted sequences on >= 99 % of rounds, where a round
+    The stated greedy gate: identical accepted sequences on >= 99 % of rounds, where a round
     whose first differing prediction sits on a near-tie of the oracle's logits (<= 4
     bf16 ulps) or behind a routing near-tie (k-th and (k+1)-th router logits within 4
     bf16 ulps) of a token at or before it counts as explained: such rounds are counted

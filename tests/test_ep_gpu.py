@@ -22,6 +22,9 @@ def _free_port():
 def _moe_cases(rank, world, so, cases):
     from qwen35_dflash_b200 import ep, lib, w4
     import torch.distributed as dist
+    # the expert-parallel receiver runs the grouped kernels only: compare with the
+    # one-GPU kernels without the tensor-core dense path (same bits)
+    prev = so.qw_moe_dense_threshold(0)
     for (t, h, e, k, inter, g) in cases:
         gen = torch.Generator().manual_seed(1000 + t + e)       # weights: the same on every rank
         qgu = torch.randint(-8, 8, (e, 2 * inter, h), dtype=torch.int8, generator=gen)
@@ -67,6 +70,7 @@ def _moe_cases(rank, world, so, cases):
                     raise AssertionError(f"rank {rank} case {(t, h, e, k, inter, g)} rep {rep}: {bad} elements differ")
         finally:
             moe.close()
+    so.qw_moe_dense_threshold(prev)
 
 
 def _engine_case(rank, world):
