@@ -620,7 +620,10 @@ def _event_times(fn, reps: int, flush) -> float:
 def run_micro(args):
     """Benchmark configs 2 and 3 (one JSON line per point): the W4A16 grouped MoE
     (router logits given, softmax top-8 + shared expert, H 2048, 256 experts, I 512, g128,
-    scales U(0.005, 0.02)) at T = 16, 64, 256 -- routing + experts + combine -- and the
+    scales U(0.005, 0.02)) at T = 16, 64, 256 -- routing + experts + combine; also with
+    skewed routing (config 5's Zipf bias at T = 256 and 1024, and 8 hot experts), each
+    timed with the default grouped kernels ("us") and with the tcgen05 dense-expert
+    kernels enabled at 128 pairs ("us_tcgen05_dense") -- and the
     gated-DeltaNet verify at B = 1, 8, 32 (16 QK / 32 V heads of 128, block 16) -- verify
     + commit of all 16 tokens.  CUDA events around each launch group, L2 flushed (256 MB
     write) before each; achieved = algorithmic bytes / time against the measured HBM
@@ -648,9 +651,28 @@ def run_micro(args):
     sgu, sdn = bank(2 * I, H, 1), bank(H, I, 1)
     w4b = lambda n, kk: n * kk // 2 + n * (kk // g) * 2   # noqa: E731
     per_expert = w4b(2 * I, H) + w4b(H, I)
-    for T in (16, 64, 256):
+    dense_default = so.qw_moe_dense_threshold(-1)
+    DENSE_ON = 128   # the tensor-core arm: routed experts with >= 128 pairs, when they fill the GPU
+    # (tokens, routing): "random" logits N(0, 1); "zipf" adds the per-expert bias log p_e,
+    # p_e ~ rank^-1.1 (benchmark config 5's skew); "hot8" adds +4 to 8 experts (every
+    # token's routed pairs land on them: all nine slots are dense contractions)
+    perm = torch.randperm(E, generator=torch.Generator().manual_seed(3))
+    ranks = torch.empty(E)
+    ranks[perm] = torch.arange(1, E + 1, dtype=torch.float32)
+    zipf = ranks.pow(-1.1)
+    zipf = (zipf / zipf.sum()).log().to(dev)
+    cases = ((16, "random"), (64, "random"), (256, "random"), (256, "zipf"), (1024, "zipf"), (256, "hot8"))
+    if args.moe_case:
+        tok, rt = args.moe_case.split(":")
+        cases = ((int(tok), rt),)
+    for T, routing in cases:
         x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
-        logits = torch.randn(T, E + 1, device=dev, generator=gen).to(torch.bfloat16)
+        logits = torch.randn(T, E + 1, device=dev, generator=gen)
+        if routing == "zipf":
+            logits[:, :E] += zipf
+        elif routing == "hot8":
+            logits[:, perm[:8].to(dev)] += 4.0
+        logits = logits.to(torch.bfloat16)
         ws = torch.zeros(so.qw_moe_workspace_bytes(T, H, E, I, k), dtype=torch.uint8, device=dev)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
 
@@ -664,14 +686,29 @@ def run_micro(args):
         torch.cuda.synchronize()
         off = so.qw_moe_active_experts(None, T, E, k)
         active = int(ws[off:off + 4].view(torch.int32).item())
+        na = min(E, T * k)   # room of the active list; the pair offsets follow it
+        pair_off = ws[off + 4 * (4 + na):off + 4 * (4 + na + active + 1)].view(torch.int32).cpu()
+        counts = (pair_off[1:] - pair_off[:-1]).tolist()
+        dense = [c for c in counts if T > 16 and c >= DENSE_ON]
+        if sum((c + 127) // 128 for c in dense) * (I // 64) < 128:   # the kernels' fill rule
+            dense = []
         us = _event_times(moe, args.kernel_reps, flush)
+        so.qw_moe_dense_threshold(DENSE_ON)
+        us_dense = _event_times(moe, args.kernel_reps, flush) if dense else us
+        so.qw_moe_dense_threshold(dense_default)
         nbytes = (active + 1) * per_expert + T * H * 2 * 2 + T * (E + 1) * 2
         lines.append({"config": "2: W4A16 grouped MoE (route + experts + combine)", "tokens": T,
-                      "active_experts": active, "us": round(us, 2), "alg_bytes": nbytes,
+                      "routing": routing, "active_experts": active, "max_pairs": max(counts),
+                      "dense_experts": len(dense), "dense_pairs": sum(dense), "us": round(us, 2),
+                      "us_tcgen05_dense": round(us_dense, 2), "alg_bytes": nbytes,
                       "achieved_gbs": round(nbytes / us / 1e3, 1), "peak_gbs": hbm,
                       "frac": round(nbytes / us / 1e3 / hbm, 4), "peak_kind": f"{peak_kind} burst copy",
                       "tflops": round(2 * T * 9 * 3 * I * H / us / 1e6, 2)})
     del gu, dn
+    if args.moe_case:
+        for line in lines:
+            print(json.dumps(line), flush=True)
+        return
     # ---- config 3
     kh, vh, d, S = 16, 32, 128, 16
     kw, vw = kh * d, vh * d
@@ -744,6 +781,8 @@ def main():
     ap.add_argument("--kernel-reps", type=int, default=5)
     ap.add_argument("--micro", action="store_true",
                     help="benchmark configs 2 (W4A16 MoE, T 16/64/256) and 3 (GDN verify, B 1/8/32), one line each")
+    ap.add_argument("--moe-case", default="",
+                    help="with --micro: only this config-2 case, TOKENS:ROUTING (e.g. 256:hot8; the small case for ncu)")
     args = ap.parse_args()
     if args.serving:
         args.requests = args.requests or 64

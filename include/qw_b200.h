@@ -212,14 +212,19 @@ int qw_moe_experts_w4(const void* x, const void* gate_up, const void* down,
                       int64_t hidden, int64_t experts, int64_t inter, int64_t top_k,
                       int32_t group, void* workspace, void* stream);
 
-/* Dense experts on the tensor cores.  With blocks of more than 16 tokens, an expert
- * (the shared one included) that receives at least `tokens` (token, slot) pairs runs on
- * the tcgen05 kernels (weights dequantised to fp16 in shared memory, fp32 accumulators
- * in tensor memory) instead of the grouped mma.sync kernels: group 128, hidden and
- * inter multiples of 128, not on the expert-parallel receiver.  Its outputs then differ
- * from the grouped kernels' in fp32 summation order only.  Process-wide; 0 disables;
- * default 32.  Returns the previous threshold (tokens < 0: query only).  The reference
- * computes every expert with one grouped matmul (quantization.py:181-202). */
+/* Dense experts on the tensor cores.  With blocks of more than 16 tokens, a routed
+ * expert that receives at least `tokens` (token, slot) pairs runs on the tcgen05
+ * kernels (int4 expanded to 16-bit integers in shared memory, one fp32 tensor-memory
+ * accumulator per quantisation group, scaled and summed in fp32) instead of the grouped
+ * mma.sync kernels -- when such experts make at least 128 gate/up work items (tiles of
+ * 128 pairs x 64-column blocks), decided on the device from the routing; group 128,
+ * hidden and inter multiples of 128, not on the expert-parallel receiver.  Their outputs
+ * then differ from the grouped kernels' in fp32 summation order only.  Process-wide;
+ * 0 disables; default 0 (off: measured no faster than the grouped kernels on random,
+ * Zipf(1.1) or 8-hot-expert routings); 128 is the tuned value when enabled.  Returns the
+ * previous threshold (tokens < 0: query only).
+ * The reference computes every expert with one grouped matmul
+ * (quantization.py:181-202). */
 int32_t qw_moe_dense_threshold(int32_t tokens);
 
 /* The two halves of qw_moe_experts_w4 (same arguments), for timing each launch:

@@ -1389,17 +1389,44 @@ __device__ __forceinline__ int gr_pairs(const MoeArgs<ET>& a, const RouteView& r
   return rv.pair_off[ai + 1] - rv.pair_off[ai];
 }
 
-// Every thread: the table with `per` items per (slot, chunk of `chunk` pairs).  A slot
-// with at least dense_min pairs (dense_min > 0) belongs to the tcgen05 kernels: with
+// The tcgen05 kernels take an expert's pairs in tiles of this many, and run at all only
+// when the routed experts with at least dense_min pairs make this many gate/up items
+// (tiles x 64-column blocks): fewer would run serially on a few SMs after the grouped
+// kernels and cost more than they save (measured).
+constexpr int TC_N = 128;
+constexpr int TC_MIN_ITEMS = 128;
+
+// Every thread (a CTA-wide vote): do the dense experts of this routing fill the GPU?
+// The grouped and the tcgen05 kernels decide alike from the same counts.
+template <typename ET>
+__device__ bool dense_path_fills(const MoeArgs<ET>& a, const RouteView& rv, int dense_min) {
+  __shared__ int tiles;
+  if (threadIdx.x == 0) tiles = 0;
+  __syncthreads();
+  const int ns = a.has_shared + *rv.n_active;
+  int mine = 0;
+  for (int sl = a.has_shared + threadIdx.x; sl < ns; sl += blockDim.x) {
+    const int np = gr_pairs(a, rv, sl);
+    if (np >= dense_min) mine += (np + TC_N - 1) / TC_N;
+  }
+  if (mine) atomicAdd(&tiles, mine);
+  __syncthreads();
+  return tiles * (a.I / 64) >= TC_MIN_ITEMS;
+}
+
+// Every thread: the table with `per` items per (slot, chunk of `chunk` pairs).  A routed
+// expert's slot with at least dense_min pairs (dense_min > 0, and the dense experts
+// filling the GPU) belongs to the tcgen05 kernels: with
 // dense false it gets no items here, with dense true only such slots get items.  The
 // slots' item counts load in parallel; warp 0 scans them 32 at a time.
 template <typename ET>
 __device__ void gr_build_table(GrTable& tb, const MoeArgs<ET>& a, const RouteView& rv, int per, int dense_min = 0,
                                bool dense = false, int chunk = GR_CHUNK) {
   const int ns = a.has_shared + *rv.n_active;
+  if (dense_min > 0 && !dense_path_fills(a, rv, dense_min)) dense_min = 0;
   for (int sl = threadIdx.x; sl < ns; sl += blockDim.x) {
     const int np = gr_pairs(a, rv, sl);
-    const bool is_dense = dense_min > 0 && np >= dense_min;
+    const bool is_dense = dense_min > 0 && !(a.has_shared && sl == 0) && np >= dense_min;
     tb.first[sl] = is_dense == dense ? (np + chunk - 1) / chunk * per : 0;
   }
   __syncthreads();
@@ -1770,45 +1797,52 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_grouped_kernel(X
 // An expert that receives at least XtArgs::dense_min tokens is a real contraction: its
 // gate/up and down run on the 5th-generation tensor cores instead of the grouped
 // mma.sync kernels (which then skip it).  Item = (slot, token tile of up to TC_N pairs,
-// row block of 128 weight rows).  Per 128-wide K group (one quantisation group) the CTA
-// expands the rows' int4 values to fp16 integers in shared memory, converts the tile's
-// activation rows to fp16 beside them (both operands K-major, canonical no-swizzle
-// layout: umma.cuh), and one thread issues the group's eight K = 16 tcgen05.mma steps
-// into a fresh fp32 accumulator in tensor memory (M = 128 weight rows, N = the tile's
-// pairs rounded up to 16; two accumulators alternate).  While the tensor core works on
-// group g, every thread reads group g - 1's accumulator (tcgen05.ld) and adds it, times
-// its row's bf16 scale, into fp32 registers: the per-group partial sums and the scaling
-// of the grouped kernels, so the two paths round alike (a single accumulator chained
-// over all of K lost low bits in the tensor core's fp32 additions).  Shared-memory stages
-// form a ring of TC_ST; a stage is rewritten only after the MMAs that read it committed
-// to its mbarrier, an accumulator only after every thread read it (all waits bounded).
-// Epilogue: gate/up rows of one intermediate column meet through shared memory for
-// SiLU(gate) * up in the reference's rounding order; down writes the fp32 expert output
-// rows the combine reads.
-constexpr int TC_THREADS = 256;
-constexpr int TC_N = 128;                       // pairs per item, at most
+// row block of 128 weight rows), K in groups of 128 (one quantisation group).
+//
+// Per group the CTA copies, asynchronously and two groups ahead (cp.async, a ring of
+// TC_ST stages), the row block's raw W4 chunks (8 stream tiles x 1056 bytes) and the
+// tile's activation rows straight into the canonical K-major operand layout
+// (umma.cuh); it expands the int4 values in shared memory to 16-bit integers q = u - 8
+// (exact in bf16 and fp16), and one thread issues the group's eight K = 16 tcgen05.mma
+// steps into a fresh fp32 accumulator in tensor memory (M = 128 weight rows, N = the
+// tile's pairs rounded up to 16; two accumulators alternate).  While the tensor core
+// works on group g, every thread reads group g - 1's accumulator (tcgen05.ld) and adds
+// it, times its row's bf16 scale, into fp32 registers: the per-group partial sums and
+// scaling of the grouped kernels, so both paths round alike (one accumulator chained
+// over all of K lost low bits in the tensor core's fp32 additions).  Gate/up multiplies
+// bf16 q by the bf16 activations as stored; down multiplies fp16 q by the fp16 h rows.
+// All waits are bounded.  Epilogue: gate/up rows of one intermediate column meet through
+// shared memory for SiLU(gate) * up in the reference's rounding order; down writes the
+// fp32 expert output rows the combine reads.
+constexpr int TC_THREADS = 512;
+constexpr int TC_COLS = TC_N / (TC_THREADS / 128);   // accumulator columns per thread
+constexpr int TC_ROWS_PT = TC_N * 16 / TC_THREADS;   // activation rows a thread copies per group
 constexpr int TC_KS = 128;                      // K per stage (one quantisation group)
 constexpr int TC_ST = 3;                        // ring stages
-constexpr int TC_A_BYTES = 128 * TC_KS * 2;     // 128 weight rows x 128 K, fp16
-constexpr int TC_B_BYTES = TC_N * TC_KS * 2;    // TC_N rows x 128 K, fp16
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr int TC_CHB = 8 * TC_KS + 32;          // one stream tile's group chunk (nibbles + scales)
+constexpr int TC_A_BYTES = 128 * TC_KS * 2;     // 128 weight rows x 128 K, 16-bit
+constexpr int TC_B_BYTES = TC_N * TC_KS * 2;    // TC_N rows x 128 K, 16-bit
+constexpr int TC_RAW_BYTES = 8 * TC_CHB;        // the row block's 8 raw chunks
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES + TC_RAW_BYTES;
 constexpr int TC_HEAD = 1024 + (static_cast<int>(sizeof(GrTable)) + 1023) / 1024 * 1024;
 constexpr size_t TC_SMEM = TC_HEAD + static_cast<size_t>(TC_ST) * TC_STAGE_BYTES;
 constexpr uint32_t TC_TMEM_COLS = 2 * TC_N;     // two accumulators
 static_assert(TC_SMEM <= 227 * 1024, "tcgen05 expert stages exceed shared memory");
+static_assert(TC_STAGE_BYTES % 128 == 0 && TC_CHB % 16 == 0, "stage alignment");
 
 // Byte offset of (row, K octet) in a canonical K-major tile of TC_KS columns.
 __device__ __forceinline__ int tc_off(int row, int octet) {
   return ((row >> 3) * (TC_KS / 8) + octet) * 128 + (row & 7) * 16;
 }
 
-// Expand one W4 task of a 16-row stream tile's K group (16 bytes of nibbles: lane
-// `ln`'s steps 4v .. 4v + 3) to the fp16 integers q = u - 8 of rows row0 + gid and
-// row0 + gid + 8 of the A tile.  (0x6400 | u is the fp16 1024 + u; minus 1032 is exact.)
+// Expand one W4 task of a raw chunk (16 bytes of nibbles: lane `ln`'s steps 4v .. 4v + 3)
+// to the 16-bit integers q = u - 8 of A-tile rows row0 + gid and row0 + gid + 8.
+// (MAGIC | u is 128 + u in bf16 or 1024 + u in fp16; subtracting OFF = MAGIC + 8 is exact.)
+template <bool BF16>
 __device__ __forceinline__ void tc_expand_task(uint8_t* As, const uint8_t* chunk, int v, int ln, int row0) {
-  const uint4 wv = ldg_stream(chunk + v * 512 + ln * 16);
+  const uint4 wv = *reinterpret_cast<const uint4*>(chunk + v * 512 + ln * 16);
   const int gid = ln >> 2, tig = ln & 3;
-  const __half2 off = __half2half2(__ushort_as_half(0x6408));   // 1032
+  constexpr uint32_t MAGIC = BF16 ? 0x43004300u : 0x64006400u;
   const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
   for (int p = 0; p < 2; ++p) {           // steps (4v + 2p, 4v + 2p + 1): K octet 8v + 4p + tig
@@ -1819,12 +1853,19 @@ __device__ __forceinline__ void tc_expand_task(uint8_t* As, const uint8_t* chunk
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const uint32_t x = w[2 * p + e] >> (4 * h);
-        const uint32_t c01 = (x & 0x000F000Fu) | 0x64006400u;          // K 4e + 0, 4e + 1
-        const uint32_t c23 = ((x >> 8) & 0x000F000Fu) | 0x64006400u;   // K 4e + 2, 4e + 3
-        const __half2 q01 = __hsub2(*reinterpret_cast<const __half2*>(&c01), off);
-        const __half2 q23 = __hsub2(*reinterpret_cast<const __half2*>(&c23), off);
-        o[2 * e] = *reinterpret_cast<const uint32_t*>(&q01);
-        o[2 * e + 1] = *reinterpret_cast<const uint32_t*>(&q23);
+        uint32_t c[2] = {lop3_and_or(x, 0x000F000Fu, MAGIC), lop3_and_or(x >> 8, 0x000F000Fu, MAGIC)};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if constexpr (BF16) {
+            const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&c[j]),
+                                             __bfloat162bfloat162(__ushort_as_bfloat16(0x4308)));
+            o[2 * e + j] = *reinterpret_cast<const uint32_t*>(&q);
+          } else {
+            const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&c[j]),
+                                      __half2half2(__ushort_as_half(0x6408)));
+            o[2 * e + j] = *reinterpret_cast<const uint32_t*>(&q);
+          }
+        }
       }
       *reinterpret_cast<uint4*>(As + tc_off(row0 + gid + 8 * h, octet)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
@@ -1854,79 +1895,100 @@ __device__ __forceinline__ void tc_item(const GrTable& tb, const MoeArgs<ET>& a,
 
 struct TcRing {
   uint8_t* stages;
-  uint64_t* done;     // TC_ST barriers: the MMAs that read the stage committed
   uint64_t* full;     // 2 barriers: accumulator (g % 2) holds group g
   uint32_t tmem;
   int g;              // groups issued so far (all items of the CTA)
 };
 
-// Group kg of an item: the A tile (8 stream tiles: tile0 .. + 3 -> rows 0-63, tile1 ..
-// + 3 -> rows 64-127) and the B tile (pairs [0, nn), rows >= np zero) into the next
-// stage, then one thread issues the MMAs into accumulator g % 2.  False (for every
-// thread) when a bounded wait expired.
-template <bool UP>
-__device__ __forceinline__ bool tc_issue(TcRing& r, const XtArgs& args, const uint8_t* w, int kg, int tile0,
-                                         int tile1, int K, const int (&rows)[TC_N / 16], int np, int nn,
-                                         const void* src, int64_t src_ld, uint32_t idesc) {
-  using Fmt = W4Fmt<128>;
-  const int st = r.g % TC_ST;
-  const bool free_ok = r.g < TC_ST || mbar_wait(r.done + st, ((r.g / TC_ST) - 1) & 1, args.status, args.limit);
-  if (!__syncthreads_and(free_ok)) return false;
-  uint8_t* As = r.stages + st * TC_STAGE_BYTES;
-  uint8_t* Bs = As + TC_A_BYTES;
+// What one item streams: 8 stream tiles (tile0 .. + 3 -> A rows 0-63, tile1 .. + 3 ->
+// rows 64-127) of a K-wide W4 matrix, and the activation rows src[rows[i]] (16-bit,
+// row stride src_ld elements) of the tile's pairs [0, np), zero up to nn.
+struct TcOperands {
+  const uint8_t* w;
+  int tile0, tile1, K;
+  const uint8_t* src;
+  int64_t src_ld;
+  int np, nn;
+};
+
+__device__ __forceinline__ uint8_t* tc_stage(const TcRing& r, int g) { return r.stages + (g % TC_ST) * TC_STAGE_BYTES; }
+
+// Copy task i of this thread: activation row n and K octet of the B tile.  Task t =
+// i * TC_THREADS + threadIdx.x covers row group t / 128, octets 4 ((t / 32) % 4) ..
+// + 3 (lane / 8) of rows (lane % 8).
+__device__ __forceinline__ void tc_copy_slot(int i, int& n, int& octet) {
+  const int t = i * TC_THREADS + threadIdx.x, lane = t & 31;
+  n = (t >> 7) * 8 + (lane & 7);
+  octet = ((t >> 5) & 3) * 4 + (lane >> 3);
+}
+
+// Every thread: its cp.async copies of group kg into stage g (one commit group).
+__device__ __forceinline__ void tc_load(const TcRing& r, const TcOperands& o, const int (&rows)[TC_ROWS_PT], int g,
+                                        int kg) {
+  uint8_t* st = tc_stage(r, g);
+  uint8_t* Bs = st + TC_A_BYTES;
+  uint8_t* raw = Bs + TC_B_BYTES;
+  for (int i = threadIdx.x; i < 8 * (TC_CHB / 16); i += TC_THREADS) {
+    const int t8 = i / (TC_CHB / 16), c = i % (TC_CHB / 16);
+    const int tile = t8 < 4 ? o.tile0 + t8 : o.tile1 + (t8 - 4);
+    cp_async16(raw + t8 * TC_CHB + c * 16,
+               o.w + W4Fmt<128>::tile_offset(tile, o.K, 0) + static_cast<int64_t>(kg) * TC_CHB + c * 16, true);
+  }
+  // a warp fills four whole core matrices (8 rows x 4 K octets, 512 contiguous bytes)
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {           // A: 8 stream tiles x 64 tasks of 16 bytes
+  for (int i = 0; i < TC_ROWS_PT; ++i) {
+    int n, octet;
+    tc_copy_slot(i, n, octet);
+    if (n < o.nn)
+      cp_async16(Bs + tc_off(n, octet), o.src + (static_cast<int64_t>(rows[i]) * o.src_ld + kg * TC_KS + octet * 8) * 2,
+                 n < o.np);
+  }
+  cp_async_commit();
+}
+
+// Group kg (in stage g = r.g, copies landed): expand A, then one thread issues the MMAs
+// into accumulator g % 2 and commits them to full[g % 2].
+template <bool BF16>
+__device__ __forceinline__ void tc_issue(TcRing& r, uint32_t idesc) {
+  uint8_t* As = tc_stage(r, r.g);
+  const uint8_t* raw = As + TC_A_BYTES + TC_B_BYTES;
+#pragma unroll
+  for (int i = 0; i < 512 / TC_THREADS; ++i) {   // 8 raw chunks x 64 tasks of 16 bytes
     const int task = threadIdx.x + i * TC_THREADS;
     const int t8 = task >> 6, v = (task >> 5) & 1, ln = task & 31;
-    const int tile = t8 < 4 ? tile0 + t8 : tile1 + (t8 - 4);
-    tc_expand_task(As, w + Fmt::tile_offset(tile, K, 0) + static_cast<int64_t>(kg) * Fmt::CHB, v, ln, t8 * 16);
+    tc_expand_task<BF16>(As, raw + t8 * TC_CHB, v, ln, t8 * 16);
   }
-  const int octet = threadIdx.x & 15;     // B: pair row n = threadIdx.x / 16 + 16 i
-#pragma unroll
-  for (int i = 0; i < TC_N / 16; ++i) {
-    const int n = (threadIdx.x >> 4) + 16 * i;
-    if (n < nn) {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (n < np) {
-        if constexpr (UP) {
-          v = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(
-              static_cast<const __nv_bfloat16*>(src) + static_cast<int64_t>(rows[i]) * src_ld + kg * TC_KS + octet * 8)));
-        } else {
-          v = __ldg(reinterpret_cast<const uint4*>(static_cast<const __half*>(src) +
-                                                   static_cast<int64_t>(rows[i]) * src_ld + kg * TC_KS + octet * 8));
-        }
-      }
-      *reinterpret_cast<uint4*>(Bs + tc_off(n, octet)) = v;
-    }
-  }
-  fence_proxy_async();   // the generic-proxy tile stores before the tensor core reads them
+  fence_proxy_async();   // the generic-proxy stores (and landed copies) before the tensor core reads them
   __syncthreads();
   if (threadIdx.x == 0) {
     umma::fence_after_sync();
-    const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs);
+    const uint32_t a0 = smem_u32(As), b0 = a0 + TC_A_BYTES;
     const uint32_t d = r.tmem + (r.g & 1) * TC_N;
 #pragma unroll
     for (int s = 0; s < TC_KS / 16; ++s)
       umma::mma_f16(d, umma::smem_desc(a0 + s * 256, 128, (TC_KS / 8) * 128),
                     umma::smem_desc(b0 + s * 256, 128, (TC_KS / 8) * 128), idesc, s > 0);
-    umma::commit(r.done + st);
     umma::commit(r.full + (r.g & 1));
   }
   ++r.g;
-  return true;
 }
 
-// Every thread: wait (bounded) for group `g`'s accumulator and add its columns
-// [c0, c0 + 64) of this warp's 32 rows, times the row's scale, into acc.
-__device__ __forceinline__ bool tc_accumulate(const TcRing& r, const XtArgs& args, int g, int c0, int nn,
-                                              float scale, float (&acc)[64]) {
+// Every thread: wait (bounded) for group g's accumulator and add its columns
+// [c0, c0 + TC_COLS) of this warp's 32 rows, times the row's scale (from the group's raw
+// chunk), into acc.
+__device__ __forceinline__ bool tc_accumulate(const TcRing& r, const XtArgs& args, int g, int c0, int nn, int row,
+                                              float (&acc)[TC_COLS]) {
   const bool ok = __syncthreads_and(mbar_wait(r.full + (g & 1), (g >> 1) & 1, args.status, args.limit));
   if (!ok) return false;
   umma::fence_after_sync();
+  const uint8_t* raw = tc_stage(r, g) + TC_A_BYTES + TC_B_BYTES;
+  const int rr = row & 15;   // scale position 2 gid + h <-> row gid + 8 h of the tile
+  const float scale = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(
+      raw + (row >> 4) * TC_CHB + 8 * TC_KS + 2 * (2 * (rr & 7) + (rr >> 3))));
   const int q = (threadIdx.x >> 5) & 3;
   const uint32_t base = r.tmem + (static_cast<uint32_t>(32 * q) << 16) + (g & 1) * TC_N + c0;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < TC_COLS / 16; ++c) {
     if (c0 + 16 * c < nn) {
       float v[16];
       umma::ld16(base + 16 * c, v);
@@ -1935,36 +1997,33 @@ __device__ __forceinline__ bool tc_accumulate(const TcRing& r, const XtArgs& arg
     }
   }
   umma::fence_before_sync();
+  __syncthreads();   // every thread is done with the group's stage and accumulator
   return true;
 }
 
-// The bf16 scale of A-tile row `row` in group kg (tile0 / tile1 as in tc_issue).
-__device__ __forceinline__ float tc_scale(const uint8_t* w, int kg, int tile0, int tile1, int K, int row) {
-  using Fmt = W4Fmt<128>;
-  const int t8 = row >> 4, rr = row & 15;
-  const int tile = t8 < 4 ? tile0 + t8 : tile1 + (t8 - 4);
-  const uint8_t* sc = w + Fmt::tile_offset(tile, K, 0) + static_cast<int64_t>(kg) * Fmt::CHB + 8 * 128;
-  const int p = 2 * (rr & 7) + (rr >> 3);   // position 2 gid + h <-> row gid + 8 h
-  return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(sc) + p));
-}
-
-// All groups of one item; acc = this thread's 64 fp32 sums (row 32 (warp % 4) + lane,
-// columns 64 (warp / 4) ..).  False when a bounded wait expired.
-template <bool UP>
-__device__ __forceinline__ bool tc_item_run(TcRing& r, const XtArgs& args, const uint8_t* w, int ngroups, int tile0,
-                                            int tile1, int K, const int (&rows)[TC_N / 16], int np, int nn,
-                                            const void* src, int64_t src_ld, float (&acc)[64]) {
-  const uint32_t idesc = umma::idesc_f16_f32(128, nn);
+// All groups of one item; acc = this thread's TC_COLS fp32 sums (row 32 (warp % 4) +
+// lane, columns TC_COLS (warp / 4) ..).  False when a bounded wait expired.
+template <bool BF16>
+__device__ __forceinline__ bool tc_item_run(TcRing& r, const XtArgs& args, const TcOperands& o, int ngroups,
+                                            const int (&rows)[TC_ROWS_PT], float (&acc)[TC_COLS]) {
+  const uint32_t idesc = umma::idesc_16(128, o.nn, BF16);
   const int row = 32 * ((threadIdx.x >> 5) & 3) + (threadIdx.x & 31);
-  const int c0 = 64 * (threadIdx.x >> 7);
+  const int c0 = TC_COLS * (threadIdx.x >> 7);
 #pragma unroll
-  for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+  for (int j = 0; j < TC_COLS; ++j) acc[j] = 0.f;
+  const int g0 = r.g;
+  tc_load(r, o, rows, g0, 0);
+  if (ngroups > 1) tc_load(r, o, rows, g0 + 1, 1); else cp_async_commit();
   for (int kg = 0; kg < ngroups; ++kg) {
-    if (!tc_issue<UP>(r, args, w, kg, tile0, tile1, K, rows, np, nn, src, src_ld, idesc)) return false;
-    if (kg > 0 && !tc_accumulate(r, args, r.g - 2, c0, nn, tc_scale(w, kg - 1, tile0, tile1, K, row), acc))
-      return false;
+    cp_async_wait<1>();    // this thread's copies of group kg landed
+    __syncthreads();       // everyone's
+    tc_issue<BF16>(r, idesc);
+    if (kg > 0 && !tc_accumulate(r, args, r.g - 2, c0, o.nn, row, acc)) return false;
+    // stage of group kg - 1 is free (its MMAs completed): copies of group kg + 2
+    if (kg + 2 < ngroups) tc_load(r, o, rows, g0 + kg + 2, kg + 2); else cp_async_commit();
   }
-  return tc_accumulate(r, args, r.g - 1, c0, nn, tc_scale(w, ngroups - 1, tile0, tile1, K, row), acc);
+  cp_async_wait<0>();
+  return tc_accumulate(r, args, r.g - 1, c0, o.nn, row, acc);
 }
 
 // Setup common to both kernels: barriers, the tensor-memory allocation (warp 0).
@@ -1972,7 +2031,7 @@ __device__ __forceinline__ void tc_setup(uint8_t* smem, TcRing& r) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint32_t* tbase = reinterpret_cast<uint32_t*>(smem + 256);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TC_ST + 2; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(bars + i, 1);
   }
   fence_barrier_init();
   if (threadIdx.x < 32) umma::tmem_alloc(tbase, TC_TMEM_COLS);
@@ -1980,15 +2039,14 @@ __device__ __forceinline__ void tc_setup(uint8_t* smem, TcRing& r) {
   __syncthreads();
   umma::fence_after_sync();
   r.stages = smem + TC_HEAD;
-  r.done = bars;
-  r.full = bars + TC_ST;
+  r.full = bars;
   r.tmem = *tbase;
   r.g = 0;
 }
 
 // Teardown: every MMA this CTA issued has completed (or a bounded wait gave up, after
-// which the last group's commit is waited for once more, bounded), then warp 0 frees the
-// columns.
+// which the last group's commit is waited for once more, bounded, and the copies in
+// flight drained), then warp 0 frees the columns.
 __device__ __forceinline__ void tc_teardown(TcRing& r, const XtArgs& args, bool ok) {
   if (!ok && r.g > 0) {
     const int last = r.g - 1;
@@ -1996,6 +2054,7 @@ __device__ __forceinline__ void tc_teardown(TcRing& r, const XtArgs& args, bool 
     while (!mbar_try_wait(r.full + (last & 1), (last >> 1) & 1))
       if (clock64() - t0 > args.limit) break;
   }
+  cp_async_wait<0>();
   umma::fence_before_sync();
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -2021,33 +2080,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_up_tc_kernel(XtArgs args) {
   TcRing r;
   tc_setup(smem, r);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = warp & 3, row = 32 * q + lane, c0 = 64 * (warp >> 2);
+  const int q = warp & 3, row = 32 * q + lane, c0 = TC_COLS * (warp >> 2);
   bool ok = true;
   for (int it = blockIdx.x; it < tb.total && ok; it += gridDim.x) {
     int sl, tt, rb, np, pb;
     const uint8_t* w;
     tc_item(tb, a, rv, it, per, true, sl, tt, rb, w, np, pb);
-    const int nn = (np + 15) & ~15;
-    int rows[TC_N / 16];
+    int rows[TC_ROWS_PT];
 #pragma unroll
-    for (int i = 0; i < TC_N / 16; ++i) {
-      const int n = min((threadIdx.x >> 4) + 16 * i, np - 1);
+    for (int i = 0; i < TC_ROWS_PT; ++i) {
+      int n, octet;
+      tc_copy_slot(i, n, octet);
+      n = min(n, np - 1);
       rows[i] = pb < 0 ? tt * TC_N + n : rv.pair_tok[pb + tt * TC_N + n];
     }
-    float acc[64];
-    ok = tc_item_run<true>(r, args, w, H / TC_KS, 4 * rb, I / 16 + 4 * rb, H, rows, np, nn, a.x, H, acc);
+    const TcOperands o{w, 4 * rb, I / 16 + 4 * rb, H, reinterpret_cast<const uint8_t*>(a.x), H, np,
+                       (np + 15) & ~15};
+    float acc[TC_COLS];
+    ok = tc_item_run<true>(r, args, o, H / TC_KS, rows, acc);
     if (!ok) break;
-    // the up rows (quarters 2, 3) go through the first stage (idle: every MMA is done)
+    // the up rows (quarters 2, 3) go through the first stage (idle: every MMA and copy is done)
     float* ubuf = reinterpret_cast<float*>(r.stages);   // [64][TC_N + 1]
     if (q >= 2) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j)
-        if (c0 + j < nn) ubuf[(row - 64) * (TC_N + 1) + c0 + j] = rbf(acc[j]);
+      for (int j = 0; j < TC_COLS; ++j)
+        if (c0 + j < o.nn) ubuf[(row - 64) * (TC_N + 1) + c0 + j] = rbf(acc[j]);
     }
     __syncthreads();
     if (q < 2) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
+      for (int j = 0; j < TC_COLS; ++j) {
         const int n = c0 + j;
         if (n < np) {
           const float gr = rbf(acc[j]), ur = ubuf[row * (TC_N + 1) + n];
@@ -2078,22 +2140,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_down_tc_kernel(XtArgs args)
   TcRing r;
   tc_setup(smem, r);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = 32 * (warp & 3) + lane, c0 = 64 * (warp >> 2);
+  const int row = 32 * (warp & 3) + lane, c0 = TC_COLS * (warp >> 2);
   bool ok = true;
   for (int it = blockIdx.x; it < tb.total && ok; it += gridDim.x) {
     int sl, tt, rb, np, pb;
     const uint8_t* w;
     tc_item(tb, a, rv, it, per, false, sl, tt, rb, w, np, pb);
-    const int nn = (np + 15) & ~15;
     const int64_t hb = (pb < 0 ? static_cast<int64_t>(a.T) * a.k : pb) + tt * TC_N;
-    int rows[TC_N / 16];
+    int rows[TC_ROWS_PT];
 #pragma unroll
-    for (int i = 0; i < TC_N / 16; ++i) rows[i] = static_cast<int>(hb) + min((threadIdx.x >> 4) + 16 * i, np - 1);
-    float acc[64];
-    ok = tc_item_run<false>(r, args, w, I / TC_KS, 8 * rb, 8 * rb + 4, I, rows, np, nn, a.hbuf, I, acc);
+    for (int i = 0; i < TC_ROWS_PT; ++i) {
+      int n, octet;
+      tc_copy_slot(i, n, octet);
+      rows[i] = static_cast<int>(hb) + min(n, np - 1);
+    }
+    const TcOperands o{w, 8 * rb, 8 * rb + 4, I, reinterpret_cast<const uint8_t*>(a.hbuf), I, np, (np + 15) & ~15};
+    float acc[TC_COLS];
+    ok = tc_item_run<false>(r, args, o, I / TC_KS, rows, acc);
     if (!ok) break;
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
+    for (int j = 0; j < TC_COLS; ++j) {
       const int n = c0 + j;
       if (n < np) {
         const int pi = tt * TC_N + n;
@@ -2444,9 +2510,10 @@ static bool grouped_plan(const MoeArgs<__nv_bfloat16>& a, XtPlan& p) {
   return p.down_spw > 0 && p.up_smem <= GR_SMEM_LIMIT && p.down_smem <= GR_SMEM_LIMIT;
 }
 
-// Tokens per expert from which an expert runs on the tcgen05 kernels (0: never); see
-// qw_moe_dense_threshold.
-static std::atomic<int> g_dense_min{32};
+// Tokens per expert from which a routed expert runs on the tcgen05 kernels (0: never,
+// the default: measured no faster than the grouped kernels on the benchmark's routings);
+// see qw_moe_dense_threshold.
+static std::atomic<int> g_dense_min{0};
 
 // The dense path's shape limits: group 128 (one quantisation group per K stage), K and
 // the row blocks whole, 16-byte aligned activation rows.

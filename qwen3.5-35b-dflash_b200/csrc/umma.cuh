@@ -1,7 +1,7 @@
 // Blackwell tensor-core (tcgen05) primitives: tensor-memory allocation, shared-memory
 // matrix descriptors, the single-thread MMA issue, its completion through an mbarrier,
 // and tensor-memory loads for the epilogue.  Only the forms the dense expert kernels use:
-// one CTA (cta_group::1), kind::f16 with fp16 operands and fp32 accumulators, K-major
+// one CTA (cta_group::1), kind::f16 with fp16 or bf16 operands and fp32 accumulators, K-major
 // operands in the canonical no-swizzle layout.
 //
 // Canonical K-major layout without swizzle, as the descriptor describes it: the matrix
@@ -29,12 +29,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;                               // base offset 0, layout type 0 (no swizzle)
 }
 
-// Instruction descriptor of kind::f16: fp16 A and B (both K-major), fp32 D, M x N.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
-  return (1u << 4)                                   // D format fp32
-         | (0u << 7) | (0u << 10)                    // A, B fp16
-         | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
-         | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
+// Instruction descriptor of kind::f16: A and B both fp16 or both bf16 (K-major), fp32
+// D, M x N.
+__host__ __device__ constexpr uint32_t idesc_16(int m, int n, bool bf16) {
+  return (1u << 4)                                              // D format fp32
+         | (static_cast<uint32_t>(bf16) << 7) | (static_cast<uint32_t>(bf16) << 10)   // A, B format
+         | (static_cast<uint32_t>(n >> 3) << 17)                // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);               // M / 16
 }
 
 // One warp: allocate `ncols` (power of two >= 32) tensor-memory columns; the base

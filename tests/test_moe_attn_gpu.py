@@ -107,15 +107,16 @@ class _LazyDequant:
         return (self.q[e].astype(np.float32) * np.repeat(self.s[e], self.group, -1)).astype(np.float32)
 
 
-@pytest.mark.parametrize("t,skew,dense", [(16, 0, 32), (64, 0, 32), (256, 0, 32), (256, 0, 0), (256, 12, 32),
-                                          (64, 5, 32), (200, 3, 32), (256, 12, 0)])
+@pytest.mark.parametrize("t,skew,dense", [(16, 0, 128), (64, 0, 128), (256, 0, 128), (256, 0, 0), (256, 12, 32),
+                                          (64, 5, 32), (200, 3, 32), (256, 12, 0), (512, 8, 128), (256, 16, 64)])
 def test_moe_w4a16_matches_oracle(cuda_lib, t, skew, dense):
     """Config-2 microbench shapes (T = 16, 64, 256): H 2048, 256 experts top-8 + shared,
     I 512, W4 g128, scales U(0.005, 0.02).  ``skew`` experts get +4 on every token's
     router logits (they receive nearly every token: dense contractions of up to 256
     pairs); ``dense`` is the tensor-core threshold (tokens per expert; 0 = grouped
-    mma.sync kernels only).  With T > 16 and the threshold 32 the shared expert (T pairs)
-    and the skewed experts run on the tcgen05 kernels."""
+    mma.sync kernels only).  With T > 16 the skewed routed experts with at least that
+    many pairs run on the tcgen05 kernels when they make at least 128 gate/up items
+    (cases 256/12/32, 512/8/128, 256/16/64); the others check the rule's fallback."""
     from qwen35_dflash_b200 import lib, w4
     torch.manual_seed(t)
     h, e, k, inter, g = 2048, 256, 8, 512, 128
@@ -172,7 +173,7 @@ def test_moe_w4a16_matches_oracle(cuda_lib, t, skew, dense):
     # k + 1 adds, so two kernels whose fp32 expert outputs differ in the last bits may
     # part by two flipped roundings: up to two bf16 ulps of M is allowed as well.
     mag = np.maximum(mag, np.abs(sterm))
-    ulp2 = 2.0 * np.exp2(np.floor(np.log2(np.maximum(mag, 2.0 ** -100))) - 7)
+    ulp2 = 2.0 * np.exp2(np.floor(np.log2(np.maximum(np.maximum(mag, np.abs(want)), 2.0 ** -100))) - 7)
     assert_close(to_np(out), want, what="moe w4a16", magnitude=np.maximum(mag, (ulp2 - 2e-2) / 1e-2),
                  strict_frac=0.999)
 
