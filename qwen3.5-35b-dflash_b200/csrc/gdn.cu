@@ -6,7 +6,9 @@
 //    per (sequence, value head); each CTA of the cluster owns Dv/VSPLIT state columns
 //    and keeps them in registers (8 threads per column, Dk/8 rows each) across the
 //    block's tokens.  The prologue fuses conv_state_update + causal_conv1d + SiLU
-//    (fused/model.py:232-239), the q/k L2 norm and the gate math (:243-253); the
+//    (fused/model.py:232-239; the head's q|k channels split over the cluster's CTAs and
+//    pushed to all of them through distributed shared memory), the q/k L2 norm and the
+//    gate math (:243-253); the
 //    epilogue fuses the gated RMSNorm x SiLU(z) (:219-225), with the row sum of squares
 //    exchanged through distributed shared memory.  Verify never writes the recurrent
 //    state: commit recomputes the first r tokens from the same inputs with the same
@@ -123,26 +125,24 @@ __device__ __forceinline__ int kperm(int j) {
 // conv + SiLU of one channel over the block's tokens, rounded to bf16 after the conv and
 // after the SiLU (the reference's activation tensors, fused/model.py:238-239).  hist /
 // w hold the channel's conv tail and taps, the block inputs come from shared memory
-// (src[t * sstride]).
+// (src[t * sstride]).  Every row of the block buffer is computed (rows past the block's
+// tokens hold stale, in-bounds values) so the unrolled tokens interleave; the caller
+// stores the real ones.
 constexpr int GDN_CONV_K = 4;  // conv taps of the block kernels
 
 __device__ __forceinline__ void conv_channel(const float (&hist)[GDN_CONV_K - 1], const float (&w)[GDN_CONV_K],
-                                             const __nv_bfloat16* src, int sstride, int ntok, float* dst,
-                                             int stride) {
+                                             const __nv_bfloat16* src, int sstride, float (&y)[QW_MAX_BLOCK]) {
   constexpr int K = GDN_CONV_K;
   float win[K];
 #pragma unroll
   for (int j = 0; j < K - 1; ++j) win[j] = hist[j];
-  // every row of the block buffer is computed (rows past ntok hold stale, in-bounds
-  // values) so the unrolled tokens interleave; only the real ones are stored
 #pragma unroll
   for (int t = 0; t < QW_MAX_BLOCK; ++t) {
     win[K - 1] = __bfloat162float(src[t * sstride]);
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < K; ++j) acc = fmaf(win[j], w[j], acc);
-    const float y = rbf(silu_f(rbf(acc)));
-    if (t < ntok) dst[t * stride] = y;
+    y[t] = rbf(silu_f(rbf(acc)));
 #pragma unroll
     for (int j = 0; j < K - 1; ++j) win[j] = win[j + 1];
   }
@@ -172,11 +172,11 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   const int kw = d.k_heads * DK;
   const int vcol0 = rank * COLS;        // first state column of this CTA within the head
 
-  if (COMMIT && ntok <= 0) return;      // nothing accepted: the state stays S0
-  // verify pushes its gated-norm sums into the peer CTAs' shared memory after the
-  // recurrence; the arrival here and the wait before those stores make sure every CTA
-  // of the cluster has started by then (the wait is hidden behind the recurrence)
-  if constexpr (!COMMIT && VSPLIT > 1) cluster_arrive_relaxed();
+  if (COMMIT && ntok <= 0) return;      // nothing accepted (the whole cluster): the state stays S0
+  // the conv outputs of q and k are pushed into the peer CTAs' shared memory; the
+  // arrival here and the wait before those stores make sure every CTA of the cluster has
+  // started by then (the wait is hidden behind the staging)
+  if constexpr (VSPLIT > 1) cluster_arrive_relaxed();
 
   // ---- state columns into registers (bank layout [slot][head][Dv][Dk], column-major);
   // issued first so their latency overlaps the staging below
@@ -209,20 +209,29 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     }
     cp_async_commit();
   }
-  // ---- each thread's conv channels: tails and taps (older than the predecessor)
+  // ---- each thread's conv channels: tails and taps (older than the predecessor).  The
+  // cluster's CTAs share the head's q and k: rank r convolves q|k channels
+  // [r * QKR, (r + 1) * QKR) for all of them (verify: q then k; commit: k only), and
+  // every CTA its own v columns.
   constexpr int K = GDN_CONV_K;
   constexpr int XS = 2 * DK + COLS;
-  constexpr int CPT = (2 * DK + COLS + THREADS - 1) / THREADS;  // channels per thread
+  constexpr int CPT = (2 * DK / VSPLIT + COLS + THREADS - 1) / THREADS;  // channels per thread
   const int nq = COMMIT ? 0 : DK;
-  const int nch = nq + DK + COLS;
+  const int qkr = (nq + DK) / VSPLIT;   // q|k channels this CTA convolves
+  const int nch = qkr + COLS;
   float hreg[CPT][K - 1], wreg[CPT][K];
-  int chan[CPT];
+  int chan[CPT], src_col[CPT];
 #pragma unroll
   for (int r = 0; r < CPT; ++r) {
     const int i = tid + r * THREADS;
-    if (i < nq) chan[r] = kh * DK + i;
-    else if (i < nq + DK) chan[r] = kw + kh * DK + (i - nq);
-    else chan[r] = 2 * kw + h * DV + vcol0 + (i - nq - DK);
+    if (i < qkr) {
+      const int j = rank * qkr + i + (DK - nq);   // 0 .. DK: q, DK .. 2DK: k
+      chan[r] = j < DK ? kh * DK + j : kw + kh * DK + (j - DK);
+      src_col[r] = j;
+    } else {
+      chan[r] = 2 * kw + h * DV + vcol0 + (i - qkr);
+      src_col[r] = 2 * DK + (i - qkr);
+    }
     if (i < nch) {
       const __nv_bfloat16* hist = L.conv_hist + (slot * d.channels + chan[r]) * (K - 1);
 #pragma unroll
@@ -238,25 +247,35 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   // only the projections (written before the launch ahead of this one), before its
   // wait, and the gates, which read that launch's output, after it
   auto conv_phase = [&]() {
-    // ---- conv + SiLU for q (commit skips q), k and this CTA's v columns (taps and tails
-    // loaded above)
-    {
+    // ---- conv + SiLU for this CTA's share of q|k (into every cluster CTA) and its v
+    // columns (taps and tails loaded above); q and k are stored with row j at kperm(j)
+    // (see the recurrence)
+    if constexpr (VSPLIT > 1) cluster_wait();   // every peer CTA is running (arrived above)
 #pragma unroll
-      for (int r = 0; r < CPT; ++r) {
-        const int i = tid + r * THREADS;
-        if (i >= nch) continue;
-        // q and k are stored with row j at kperm(j) (see the recurrence)
-        if (i < nq) {
-          conv_channel(hreg[r], wreg[r], &sm.xin[0][i], XS, ntok, &sm.q[0][kperm<DK>(i)], DK);
-        } else if (i < nq + DK) {
-          const int j = i - nq;
-          conv_channel(hreg[r], wreg[r], &sm.xin[0][DK + j], XS, ntok, &sm.k[0][kperm<DK>(j)], DK);
-        } else {
-          const int j = i - nq - DK;
-          conv_channel(hreg[r], wreg[r], &sm.xin[0][2 * DK + j], XS, ntok, &sm.v[0][j], COLS);
+    for (int r = 0; r < CPT; ++r) {
+      const int i = tid + r * THREADS;
+      if (i >= nch) continue;
+      float y[QW_MAX_BLOCK];
+      conv_channel(hreg[r], wreg[r], &sm.xin[0][src_col[r]], XS, y);
+      if (i < qkr) {
+        const int j = src_col[r];
+        float* dst = j < DK ? &sm.q[0][kperm<DK>(j)] : &sm.k[0][kperm<DK>(j - DK)];
+#pragma unroll
+        for (int pr = 0; pr < VSPLIT; ++pr) {
+          float* to = dst;
+          if constexpr (VSPLIT > 1) to = cg::this_cluster().map_shared_rank(dst, (rank + pr) % VSPLIT);
+#pragma unroll
+          for (int t = 0; t < QW_MAX_BLOCK; ++t)
+            if (t < ntok) to[t * DK] = y[t];
         }
+      } else {
+#pragma unroll
+        for (int t = 0; t < QW_MAX_BLOCK; ++t)
+          if (t < ntok) sm.v[t][i - qkr] = y[t];
       }
     }
+    // every CTA's share of q|k has landed everywhere
+    if constexpr (VSPLIT > 1) cg::this_cluster().sync();
   };
   auto l2_phase = [&]() {
     // ---- L2 norm of q and k per token (fused_ops.py:92-95); q also scaled by Dk^-1/2:
@@ -377,8 +396,9 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225).  Each CTA
   // stores its per-token sums of squares into row `rank` of every cluster CTA's table,
   // so after one cluster barrier all reads are local (and no CTA touches another's
-  // shared memory once it may exit); the rows are added in rank order.
-  if constexpr (VSPLIT > 1) cluster_wait();   // every peer CTA is running (arrived above)
+  // shared memory once it may exit); the rows are added in rank order.  (Every peer is
+  // running: they all passed the cluster barrier of the conv phase and wait at the one
+  // below before they exit.)
   for (int t = tid / 32; t < ntok; t += THREADS / 32) {
     float ss = 0.f;
     for (int c = tid % 32; c < COLS; c += 32) ss += sm.o[t][c] * sm.o[t][c];
