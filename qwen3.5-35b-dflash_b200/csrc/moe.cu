@@ -500,28 +500,50 @@ __device__ void warp_topk(const Q& q, int n, int k, int16_t* pos_l, int16_t* pos
 constexpr int ROUTE_MAXJ = 8;  // logits per lane on the fast path (E <= 256)
 
 // One token's row of x -> x16 and its group sums (warp, lanes = 8-element segments).
+// The row's loads are all issued before the first is used (8 per lane for H = 2048), so
+// the staging costs one load latency, not one per 256 columns.
 template <int G>
 __device__ __forceinline__ void stage_row(const __nv_bfloat16* xr, __half* dst, float* xs, int H, int lane) {
-  for (int b = 0; b < H / 256; ++b) {
-    const int seg = b * 32 + lane;
-    const uint4 v = bf16x8_to_f16x8(__ldg(reinterpret_cast<const uint4*>(xr + seg * 8)));
-    *reinterpret_cast<uint4*>(dst + seg * 8) = v;
-    const float xg = warp_group_xsum_f16<G>(sum8_f16(v), lane);
-    if (lane % (G / 8) == 0) xs[seg * 8 / G] = xg;
+  constexpr int NB = 8;
+  for (int b0 = 0; b0 < H / 256; b0 += NB) {
+    uint4 raw[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+      if (b0 + b < H / 256) raw[b] = __ldg(reinterpret_cast<const uint4*>(xr + ((b0 + b) * 32 + lane) * 8));
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (b0 + b < H / 256) {
+        const int seg = (b0 + b) * 32 + lane;
+        const uint4 v = bf16x8_to_f16x8(raw[b]);
+        *reinterpret_cast<uint4*>(dst + seg * 8) = v;
+        const float xg = warp_group_xsum_f16<G>(sum8_f16(v), lane);
+        if (lane % (G / 8) == 0) xs[seg * 8 / G] = xg;
+      }
+    }
   }
 }
 
+// ROUTE_TPB tokens per CTA (one warp each): few CTAs, so they fit beside the router
+// GEMV's clusters and stage x while it still runs.
+constexpr int ROUTE_TPB = 4;
+
+__host__ __device__ inline size_t route_warp_smem(int E) { return ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16; }
+
 template <typename LT>
-__global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ logits, int64_t ldl, int T, int E,
-                                                       int k, int shared_col, int act_is_f16, void* ws,
-                                                       const __nv_bfloat16* __restrict__ x, int H, int G) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int lane = threadIdx.x;
+__global__ void __launch_bounds__(32 * ROUTE_TPB) route_topk_kernel(const LT* __restrict__ logits, int64_t ldl,
+                                                                   int T, int E, int k, int shared_col,
+                                                                   int act_is_f16, void* ws,
+                                                                   const __nv_bfloat16* __restrict__ x, int H,
+                                                                   int G) {
+  extern __shared__ __align__(16) uint8_t smem_all[];
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * ROUTE_TPB + (threadIdx.x >> 5);   // this warp's token
+  if (t >= T) return;   // (another warp of the CTA waits for the predecessor)
+  uint8_t* smem = smem_all + (threadIdx.x >> 5) * route_warp_smem(E);
   // x (older than the router logits) is staged for the gate/up kernel before the wait;
   // the header is rewritten on every call so that nothing stale is taken for staged
   {
     const StageView sv = stage_view(ws, T, E, k, H);
-    const int t = blockIdx.x;
     if (x != nullptr) {
       const __nv_bfloat16* xr = x + static_cast<int64_t>(t) * H;
       __half* dst = sv.x16 + static_cast<int64_t>(t) * H;
@@ -541,7 +563,6 @@ __global__ void __launch_bounds__(32) route_topk_kernel(const LT* __restrict__ l
   Q q{reinterpret_cast<float*>(smem), reinterpret_cast<int32_t*>(smem + E * 4)};
   int16_t* pos_l = reinterpret_cast<int16_t*>(smem + E * 8);
   int16_t* pos_r = pos_l + E + 2;
-  const int t = blockIdx.x;
   const LT* row = logits + static_cast<int64_t>(t) * ldl;
   float sel_v = -INFINITY;   // lane r < k: value of the r-th selected expert
   int sel_i = 0;             //             and its index
@@ -2069,7 +2090,7 @@ __device__ __forceinline__ void tc_teardown(TcRing& r, const XtArgs& args, bool 
 // stored as fp16 like the grouped kernel's.
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_up_tc_kernel(XtArgs args) {
   const MoeArgs<__nv_bfloat16>& a = args.m;
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(16) uint8_t smem[];
   GrTable& tb = *reinterpret_cast<GrTable*>(smem + 1024);
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   const int H = a.H, I = a.I, per = I / 64;
@@ -2129,7 +2150,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_up_tc_kernel(XtArgs args) {
 // tiles 8 rb ..); K = I from the fp16 h rows; fp32 outputs to part[token][slot].
 __global__ void __launch_bounds__(TC_THREADS, 1) moe_down_tc_kernel(XtArgs args) {
   const MoeArgs<__nv_bfloat16>& a = args.m;
-  extern __shared__ __align__(1024) uint8_t smem[];
+  extern __shared__ __align__(16) uint8_t smem[];
   GrTable& tb = *reinterpret_cast<GrTable*>(smem + 1024);
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   const int H = a.H, I = a.I, per = H / 128;
@@ -2355,7 +2376,7 @@ __global__ void router_dense_kernel(const ET* __restrict__ x, const ET* __restri
 template <typename LT>
 static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, int shared_col,
                         int act_is_f16, void* ws, const void* x, int H, int G, cudaStream_t s) {
-  const size_t smem = ((E * 8 + 2 * (E + 2) * 2) + 15) / 16 * 16;
+  const size_t smem = ROUTE_TPB * route_warp_smem(E);
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
@@ -2363,8 +2384,9 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   });
   if (err != cudaSuccess) return cuda_status(err, "route smem attribute");
   if (smem > 64 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
-  QW_LAUNCH_PDL("moe route", route_topk_kernel<LT>, dim3(T), dim3(32), smem, s, static_cast<const LT*>(logits), ldl,
-                T, E, k, shared_col, act_is_f16, ws, static_cast<const __nv_bfloat16*>(x), H, G);
+  QW_LAUNCH_PDL("moe route", route_topk_kernel<LT>, dim3((T + ROUTE_TPB - 1) / ROUTE_TPB), dim3(32 * ROUTE_TPB), smem,
+                s, static_cast<const LT*>(logits), ldl, T, E, k, shared_col, act_is_f16, ws,
+                static_cast<const __nv_bfloat16*>(x), H, G);
   return QW_OK;
 }
 
