@@ -617,6 +617,50 @@ def _event_times(fn, reps: int, flush) -> float:
     return statistics.median(times)
 
 
+def run_prefill(args):
+    """Prompt prefill of the full target (1 GPU, random weights of the architecture): a
+    prompt of --prefill-tokens tokens committed in chunks of 64 tokens per forward (the
+    prefill engine) and, for comparison, in verify blocks of 16.  CUDA events around the
+    whole prefill (every chunk's forward + accept + commit); prefill tokens/s."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from qwen35_dflash_b200 import config, engine as E
+    dev = torch.device("cuda")
+    cfg = config.QWEN35_35B_A3B
+    n = args.prefill_tokens
+    te = E.TargetEngine(cfg, E.weights_random(cfg, seed=2, device=dev), batch=1, block=16, capacity=n + 128,
+                        device=dev)
+    gen = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, cfg.vocab_size, (n,), generator=gen, dtype=torch.int32).tolist()
+    out = {"metric": "prefill tok/s (1 GPU, Qwen3.5-35B-A3B target, random-init weights)", "prompt_tokens": n}
+    for block in (64, 16):
+        eng = te if block == 16 else te.prefill_engine(block)
+        chunks = [torch.tensor(prompt[i:i + block] + [0] * (block - len(prompt[i:i + block])), dtype=torch.int32)
+                  for i in range(0, n, block)]
+        counts = [min(block, n - i) for i in range(0, n, block)]
+
+        def run():
+            te.qpos.zero_(); te.state.zero_(); te.conv_hist.zero_()
+            for c, k in zip(chunks, counts):
+                eng.tokens.copy_(c, non_blocking=True)
+                eng.forward()
+                eng.accept(auto_commit=False)
+                eng.accepted.fill_(k)
+                eng.commit()
+        run()   # warm-up
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(); run(); e1.record(); e1.synchronize()
+            times.append(e0.elapsed_time(e1) / 1e3)
+        best = min(times)
+        eng.raise_on_wait_timeout()
+        out[f"chunk{block}"] = {"s": round(best, 4), "tok_s": round(n / best, 1), "forwards": len(chunks)}
+    print(json.dumps(out), flush=True)
+
+
 def run_micro(args):
     """Benchmark configs 2 and 3 (one JSON line per point): the W4A16 grouped MoE
     (router logits given, softmax top-8 + shared expert, H 2048, 256 experts, I 512, g128,
@@ -781,6 +825,9 @@ def main():
     ap.add_argument("--kernel-reps", type=int, default=5)
     ap.add_argument("--micro", action="store_true",
                     help="benchmark configs 2 (W4A16 MoE, T 16/64/256) and 3 (GDN verify, B 1/8/32), one line each")
+    ap.add_argument("--prefill", action="store_true",
+                    help="prompt prefill tok/s: 64-token chunks (prefill engine) against 16-token blocks")
+    ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--moe-case", default="",
                     help="with --micro: only this config-2 case, TOKENS:ROUTING (e.g. 256:hot8; the small case for ncu)")
     args = ap.parse_args()
@@ -794,6 +841,9 @@ def main():
     if args.micro:
         args.kernel_reps = max(args.kernel_reps, 20)
         run_micro(args)
+        return
+    if args.prefill:
+        run_prefill(args)
         return
     if args.warmup < 3:
         args.warmup = 3

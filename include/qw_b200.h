@@ -49,6 +49,8 @@ enum qw_status {
 enum qw_dtype { QW_F32 = 0, QW_F16 = 1, QW_BF16 = 2 };
 
 #define QW_MAX_BLOCK 16 /* tokens per sequence in one block verify (GDN kernels) */
+#define QW_MAX_SEQ 256  /* tokens per sequence in one forward: prefill chunks (taken by the
+                           GDN kernels in sub-blocks of QW_MAX_BLOCK) */
 #define QW_MAX_CONV 8   /* largest causal-conv kernel width */
 
 /* Mirrors FUSED_OPS_ABI = 1 (model/qwen35_moe_dflash/fused/ops.py:21). */
@@ -399,7 +401,8 @@ typedef struct {
 
 /* Block verify of one layer (`layers_dev[layer]`, a device array): writes out[],
  * reads the banks, never writes them.  (dk,dv) in {(128,128),(64,64),(128,64)},
- * 1 <= seq <= QW_MAX_BLOCK; proj 16-byte aligned with ldp a multiple of 8.  The kernel
+ * 1 <= seq <= QW_MAX_SEQ (a block verify: seq <= QW_MAX_BLOCK; a prefill chunk may be
+ * longer); proj 16-byte aligned with ldp a multiple of 8.  The kernel
  * reads proj, the banks and the conv weights, and runs the conv and the q/k norms,
  * before it waits for the launch ahead of it (the a/b projection, whose output `ab` it
  * reads after the wait), so that launch must not be the one that wrote proj. */

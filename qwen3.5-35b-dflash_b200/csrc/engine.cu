@@ -171,7 +171,7 @@ extern "C" int qw_accept(const void* keys, int64_t nblk, const int32_t* proposal
                          int64_t batch, int64_t seq, int auto_commit, void* stream) {
   QW_CHECK_ARG(keys && proposals && top1 && max_accepted && next_token, "accept: null pointer");
   QW_CHECK_ARG(!auto_commit || (accepted && qpos), "accept: auto commit needs accepted and qpos");
-  QW_CHECK_ARG(batch >= 1 && seq >= 1 && seq <= QW_MAX_BLOCK && batch * seq <= QW_MAX_BLOCK * 64 && nblk >= 1,
+  QW_CHECK_ARG(batch >= 1 && seq >= 1 && seq <= QW_MAX_SEQ && batch * seq <= QW_MAX_BLOCK * 64 && nblk >= 1,
                "accept: invalid shape");
   QW_LAUNCH_PDL("accept", accept_kernel, dim3(static_cast<unsigned>(batch * seq)), dim3(256), 0, as_stream(stream),
                 static_cast<const unsigned long long*>(keys), static_cast<int>(nblk),

@@ -5,7 +5,9 @@
 //  * qw_gdn_verify / qw_gdn_commit — the block-verify form.  One thread-block cluster
 //    per (sequence, value head); each CTA of the cluster owns Dv/VSPLIT state columns
 //    and keeps them in registers (8 threads per column, Dk/8 rows each) across the
-//    block's tokens.  The prologue fuses conv_state_update + causal_conv1d + SiLU
+//    block's tokens (a prefill chunk longer than QW_MAX_BLOCK is taken in sub-blocks of
+//    QW_MAX_BLOCK, the state staying in registers and each full sub-block's last inputs
+//    becoming the next one's conv tail).  The prologue fuses conv_state_update + causal_conv1d + SiLU
 //    (fused/model.py:232-239; the head's q|k channels split over the cluster's CTAs and
 //    pushed to all of them through distributed shared memory), the q/k L2 norm and the
 //    gate math (:243-253); the
@@ -165,18 +167,17 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     pdl_wait();
     pdl_trigger();
   }
-  const int ntok = COMMIT ? d.accepted[b] : d.seq;
+  // tokens of the sequence: the block (verify), or its accepted prefix (commit); taken in
+  // sub-blocks of QW_MAX_BLOCK with the state kept in registers (a prefill chunk is
+  // longer than one verify block)
+  const int total = COMMIT ? d.accepted[b] : d.seq;
   const int tid = threadIdx.x;
   const int col = tid / KSPLIT, kq = tid % KSPLIT;
   const int kh = h / (d.v_heads / d.k_heads);
   const int kw = d.k_heads * DK;
   const int vcol0 = rank * COLS;        // first state column of this CTA within the head
 
-  if (COMMIT && ntok <= 0) return;      // nothing accepted (the whole cluster): the state stays S0
-  // the conv outputs of q and k are pushed into the peer CTAs' shared memory; the
-  // arrival here and the wait before those stores make sure every CTA of the cluster has
-  // started by then (the wait is hidden behind the staging)
-  if constexpr (VSPLIT > 1) cluster_arrive_relaxed();
+  if (COMMIT && total <= 0) return;     // nothing accepted (the whole cluster): the state stays S0
 
   // ---- state columns into registers (bank layout [slot][head][Dv][Dk], column-major);
   // issued first so their latency overlaps the staging below
@@ -187,9 +188,10 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     float4 v4 = *reinterpret_cast<const float4*>(scol + i);
     st[i] = v4.x; st[i + 1] = v4.y; st[i + 2] = v4.z; st[i + 3] = v4.w;
   }
-  // ---- stage the block's projections of this CTA's channels (and z) in shared memory:
+  int t0 = 0, ntok = 0;   // the current sub-block: tokens [t0, t0 + ntok)
+  // ---- stage a sub-block's projections of this CTA's channels (and z) in shared memory:
   // per token 8-element vectors of the q, k, v (and z) segments, all loads in flight at once
-  {
+  auto stage = [&]() {
     const int vw = d.v_heads * DV;
     constexpr int QV = DK / 8, KV = DK / 8, VV = COLS / 8;
     constexpr int PER = QV + KV + VV + VV;
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
     for (int i = tid; i < ntok * PER; i += THREADS) {
       const int t = i / PER, v = i % PER;
       if (COMMIT && (v < QV || v >= QV + KV + VV)) continue;   // commit needs k and v only
-      const __nv_bfloat16* rowp = L.proj + (static_cast<int64_t>(b) * d.seq + t) * d.ldp;
+      const __nv_bfloat16* rowp = L.proj + (static_cast<int64_t>(b) * d.seq + t0 + t) * d.ldp;
       const __nv_bfloat16* src;
       __nv_bfloat16* dst;
       if (v < QV) { src = rowp + segq + v * 8; dst = &sm.xin[t][v * 8]; }
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
       cp_async16(dst, src, true);
     }
     cp_async_commit();
-  }
+  };
   // ---- each thread's conv channels: tails and taps (older than the predecessor).  The
   // cluster's CTAs share the head's q and k: rank r convolves q|k channels
   // [r * QKR, (r + 1) * QKR) for all of them (verify: q then k; commit: k only), and
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   auto conv_phase = [&]() {
     // ---- conv + SiLU for this CTA's share of q|k (into every cluster CTA) and its v
     // columns (taps and tails loaded above); q and k are stored with row j at kperm(j)
-    // (see the recurrence)
+    // (see the recurrence).  A full sub-block's last K - 1 inputs are the next one's tail.
     if constexpr (VSPLIT > 1) cluster_wait();   // every peer CTA is running (arrived above)
 #pragma unroll
     for (int r = 0; r < CPT; ++r) {
@@ -257,6 +259,11 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
       if (i >= nch) continue;
       float y[QW_MAX_BLOCK];
       conv_channel(hreg[r], wreg[r], &sm.xin[0][src_col[r]], XS, y);
+      if (ntok == QW_MAX_BLOCK) {
+#pragma unroll
+        for (int j = 0; j < K - 1; ++j)
+          hreg[r][j] = __bfloat162float(sm.xin[QW_MAX_BLOCK - (K - 1) + j][src_col[r]]);
+      }
       if (i < qkr) {
         const int j = src_col[r];
         float* dst = j < DK ? &sm.q[0][kperm<DK>(j)] : &sm.k[0][kperm<DK>(j - DK)];
@@ -310,127 +317,139 @@ __global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
   auto gates_phase = [&]() {
     // ---- gates (fused/model.py:243-253, fp32)
     for (int t = tid; t < ntok; t += THREADS) {
-      const int64_t row = static_cast<int64_t>(b) * d.seq + t;
+      const int64_t row = static_cast<int64_t>(b) * d.seq + t0 + t;
       const float bl = L.ab[row * 2 * d.v_heads + h];
       const float al = L.ab[row * 2 * d.v_heads + d.v_heads + h];
       sm.beta[t] = sigmoid_f(bl);
       sm.g[t] = __expf(neg_a * softplus_f(al + dtb));   // the decay exp(g) of the recurrence
     }
   };
-  if constexpr (!COMMIT) {
-    cp_async_wait<0>();
-    __syncthreads();
-    conv_phase();
-    __syncthreads();
-    l2_phase();
-    __syncthreads();
-    pdl_wait();
-    pdl_trigger();
-    gates_phase();
-    __syncthreads();
-  } else {
-    gates_phase();
-    cp_async_wait<0>();
-    __syncthreads();
-    conv_phase();
-    __syncthreads();
-    l2_phase();
-    __syncthreads();
-  }
-  // ---- the recurrence (fused_ops.py:98-106)
-  for (int t = 0; t < ntok; ++t) {
-    const float decay = sm.g[t];
-    const float* kt = &sm.k[t][kq * 4];
-    float kr[ROWS];
-    float p[4] = {0.f, 0.f, 0.f, 0.f};   // four chains: short dependent FMA sequences
-#pragma unroll
-    for (int i = 0; i < ROWS; i += 4) {
-      const float4 k4 = *reinterpret_cast<const float4*>(kt + (i / 4) * 4 * KSPLIT);
-      kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        st[i + e] *= decay;
-        p[e] = fmaf(st[i + e], kr[i + e], p[e]);
+  const int vw = d.v_heads * DV;
+  for (t0 = 0; t0 < total; t0 += QW_MAX_BLOCK) {
+    ntok = min(QW_MAX_BLOCK, total - t0);
+    // the conv outputs of q and k are pushed into the peer CTAs' shared memory; the
+    // arrival here and the wait before those stores make sure every CTA of the cluster
+    // has started (and finished the previous sub-block) by then
+    if constexpr (VSPLIT > 1) cluster_arrive_relaxed();
+    stage();
+    if constexpr (!COMMIT) {
+      cp_async_wait<0>();
+      __syncthreads();
+      conv_phase();
+      __syncthreads();
+      l2_phase();
+      __syncthreads();
+      if (t0 == 0) {
+        pdl_wait();
+        pdl_trigger();
       }
-    }
-    float pred = (p[0] + p[1]) + (p[2] + p[3]);
-#pragma unroll
-    for (int sh = 1; sh < KSPLIT; sh <<= 1) pred += __shfl_xor_sync(0xffffffffu, pred, sh);
-    const float delta = (sm.v[t][col] - pred) * sm.beta[t];
-    if (COMMIT) {
-#pragma unroll
-      for (int i = 0; i < ROWS; ++i) st[i] = fmaf(kr[i], delta, st[i]);
+      gates_phase();
+      __syncthreads();
     } else {
-      const float* qt = &sm.q[t][kq * 4];
-      float oo[4] = {0.f, 0.f, 0.f, 0.f};
+      gates_phase();
+      cp_async_wait<0>();
+      __syncthreads();
+      conv_phase();
+      __syncthreads();
+      l2_phase();
+      __syncthreads();
+    }
+    // ---- the recurrence (fused_ops.py:98-106)
+    for (int t = 0; t < ntok; ++t) {
+      const float decay = sm.g[t];
+      const float* kt = &sm.k[t][kq * 4];
+      float kr[ROWS];
+      float p[4] = {0.f, 0.f, 0.f, 0.f};   // four chains: short dependent FMA sequences
 #pragma unroll
       for (int i = 0; i < ROWS; i += 4) {
-        const float4 q4 = *reinterpret_cast<const float4*>(qt + (i / 4) * 4 * KSPLIT);
-        const float qr[4] = {q4.x, q4.y, q4.z, q4.w};
+        const float4 k4 = *reinterpret_cast<const float4*>(kt + (i / 4) * 4 * KSPLIT);
+        kr[i] = k4.x; kr[i + 1] = k4.y; kr[i + 2] = k4.z; kr[i + 3] = k4.w;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          st[i + e] = fmaf(kr[i + e], delta, st[i + e]);
-          oo[e] = fmaf(st[i + e], qr[e], oo[e]);
+          st[i + e] *= decay;
+          p[e] = fmaf(st[i + e], kr[i + e], p[e]);
         }
       }
-      // the output sum over the KSPLIT threads is not on the state's critical path:
-      // partials go to shared memory and are reduced after the loop
-      sm.opart[t][col][kq] = (oo[0] + oo[1]) + (oo[2] + oo[3]);
+      float pred = (p[0] + p[1]) + (p[2] + p[3]);
+#pragma unroll
+      for (int sh = 1; sh < KSPLIT; sh <<= 1) pred += __shfl_xor_sync(0xffffffffu, pred, sh);
+      const float delta = (sm.v[t][col] - pred) * sm.beta[t];
+      if (COMMIT) {
+#pragma unroll
+        for (int i = 0; i < ROWS; ++i) st[i] = fmaf(kr[i], delta, st[i]);
+      } else {
+        const float* qt = &sm.q[t][kq * 4];
+        float oo[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < ROWS; i += 4) {
+          const float4 q4 = *reinterpret_cast<const float4*>(qt + (i / 4) * 4 * KSPLIT);
+          const float qr[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            st[i + e] = fmaf(kr[i + e], delta, st[i + e]);
+            oo[e] = fmaf(st[i + e], qr[e], oo[e]);
+          }
+        }
+        // the output sum over the KSPLIT threads is not on the state's critical path:
+        // partials go to shared memory and are reduced after the loop
+        sm.opart[t][col][kq] = (oo[0] + oo[1]) + (oo[2] + oo[3]);
+      }
     }
+    if constexpr (!COMMIT) {
+      __syncthreads();
+      for (int i = tid; i < ntok * COLS; i += THREADS) {
+        const int t = i / COLS, c = i % COLS;
+        float o = 0.f;
+#pragma unroll
+        for (int q = 0; q < KSPLIT; ++q) o += sm.opart[t][c][q];
+        sm.o[t][c] = rbf(o);   // core tensor in the activation dtype
+      }
+      __syncthreads();
+      // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225).  Each CTA
+      // stores its per-token sums of squares into row `rank` of every cluster CTA's
+      // table, so after one cluster barrier all reads are local (and no CTA touches
+      // another's shared memory once it may exit); the rows are added in rank order.
+      // (Every peer is running: they all passed the cluster barrier of the conv phase and
+      // wait at the one below before they go on.)
+      for (int t = tid / 32; t < ntok; t += THREADS / 32) {
+        float ss = 0.f;
+        for (int c = tid % 32; c < COLS; c += 32) ss += sm.o[t][c] * sm.o[t][c];
+        ss = warp_sum(ss);
+        if (tid % 32 == 0) {
+          if constexpr (VSPLIT > 1) {
+            cg::cluster_group cluster = cg::this_cluster();
+#pragma unroll
+            for (int r = 0; r < VSPLIT; ++r) cluster.map_shared_rank(&sm.sumsq[rank][t], r)[0] = ss;
+          } else {
+            sm.sumsq[0][t] = ss;
+          }
+        }
+      }
+      if constexpr (VSPLIT > 1) cg::this_cluster().sync();
+      else __syncthreads();
+      for (int t = tid; t < ntok; t += THREADS) {
+        float tot = 0.f;
+        for (int r = 0; r < VSPLIT; ++r) tot += sm.sumsq[r][t];
+        sm.total[t] = tot;
+      }
+      __syncthreads();
+      for (int i = tid; i < ntok * COLS; i += THREADS) {
+        const int t = i / COLS, c = i % COLS;
+        const int64_t row = static_cast<int64_t>(b) * d.seq + t0 + t;
+        const int vc = h * DV + vcol0 + c;
+        const float inv = rsqrtf(sm.total[t] / DV + d.eps);
+        const float n = rbf(sm.o[t][c] * inv);
+        const float y = rbf(n * norm_w);   // c == tid % COLS for every i of this thread
+        const float z = __bfloat162float(sm.zin[t][c]);
+        L.out[row * vw + vc] = __float2bfloat16_rn(y * rbf(silu_f(z)));
+      }
+    }
+    __syncthreads();   // the sub-block's shared buffers are free for the next one
   }
-  if (COMMIT) {
+  if constexpr (COMMIT) {
 #pragma unroll
     for (int i = 0; i < ROWS; i += 4)
       *reinterpret_cast<float4*>(scol + i) = make_float4(st[i], st[i + 1], st[i + 2], st[i + 3]);
-    return;
-  }
-  __syncthreads();
-  for (int i = tid; i < ntok * COLS; i += THREADS) {
-    const int t = i / COLS, c = i % COLS;
-    float o = 0.f;
-#pragma unroll
-    for (int q = 0; q < KSPLIT; ++q) o += sm.opart[t][c][q];
-    sm.o[t][c] = rbf(o);   // core tensor in the activation dtype
-  }
-  __syncthreads();
-  // ---- gated RMSNorm over the head's Dv columns (fused/model.py:219-225).  Each CTA
-  // stores its per-token sums of squares into row `rank` of every cluster CTA's table,
-  // so after one cluster barrier all reads are local (and no CTA touches another's
-  // shared memory once it may exit); the rows are added in rank order.  (Every peer is
-  // running: they all passed the cluster barrier of the conv phase and wait at the one
-  // below before they exit.)
-  for (int t = tid / 32; t < ntok; t += THREADS / 32) {
-    float ss = 0.f;
-    for (int c = tid % 32; c < COLS; c += 32) ss += sm.o[t][c] * sm.o[t][c];
-    ss = warp_sum(ss);
-    if (tid % 32 == 0) {
-      if constexpr (VSPLIT > 1) {
-        cg::cluster_group cluster = cg::this_cluster();
-#pragma unroll
-        for (int r = 0; r < VSPLIT; ++r) cluster.map_shared_rank(&sm.sumsq[rank][t], r)[0] = ss;
-      } else {
-        sm.sumsq[0][t] = ss;
-      }
-    }
-  }
-  if constexpr (VSPLIT > 1) cg::this_cluster().sync();
-  else __syncthreads();
-  for (int t = tid; t < ntok; t += THREADS) {
-    float tot = 0.f;
-    for (int r = 0; r < VSPLIT; ++r) tot += sm.sumsq[r][t];
-    sm.total[t] = tot;
-  }
-  __syncthreads();
-  const int vw = d.v_heads * DV;
-  for (int i = tid; i < ntok * COLS; i += THREADS) {
-    const int t = i / COLS, c = i % COLS;
-    const int64_t row = static_cast<int64_t>(b) * d.seq + t;
-    const int vc = h * DV + vcol0 + c;
-    const float inv = rsqrtf(sm.total[t] / DV + d.eps);
-    const float n = rbf(sm.o[t][c] * inv);
-    const float y = rbf(n * norm_w);   // c == tid % COLS for every i of this thread
-    const float z = __bfloat162float(sm.zin[t][c]);
-    L.out[row * vw + vc] = __float2bfloat16_rn(y * rbf(silu_f(z)));
   }
 }
 
@@ -493,8 +512,8 @@ static int dispatch_block(const GdnDims& d, const GdnLayer* layers, int layer0, 
 }
 
 static int check_dims(const GdnDims& d) {
-  QW_CHECK_ARG(d.batch >= 1 && d.seq >= 1 && d.seq <= QW_MAX_BLOCK,
-               "gdn block: need 1 <= seq <= %d", QW_MAX_BLOCK);
+  QW_CHECK_ARG(d.batch >= 1 && d.seq >= 1 && d.seq <= QW_MAX_SEQ,
+               "gdn block: need 1 <= seq <= %d", QW_MAX_SEQ);
   QW_CHECK_ARG(d.v_heads >= 1 && d.k_heads >= 1 && d.v_heads % d.k_heads == 0,
                "gdn block: value heads must be a multiple of key heads");
   QW_CHECK_ARG(d.conv_k >= 2 && d.conv_k <= QW_MAX_CONV, "gdn block: conv kernel out of range");

@@ -39,34 +39,55 @@ class Generation:
     iterations: list[dict] = field(default_factory=list)
 
 
+PREFILL_BLOCK = 64   # prompt tokens per prefill forward
+
+
 class DFlash:
-    def __init__(self, target: TargetEngine, draft: DraftEngine):
+    def __init__(self, target: TargetEngine, draft: DraftEngine, prefill_block: int = PREFILL_BLOCK):
+        """``prefill_block``: prompt tokens per prefill forward (a multiple of the verify
+        block; the target's prefill engine shares its state)."""
         if target.B != 1:
             raise ValueError("DFlash.generate drives one sequence (engine batch 1)")
+        if prefill_block % target.S:
+            raise ValueError("the prefill block must be a multiple of the verify block")
         self.te, self.dr = target, draft
         self.graph = None
         self._host = torch.zeros(1 + target.S, dtype=torch.int32).pin_memory()
+        self.prefill_block = prefill_block
+        self._pe = None
+        self._valid = torch.zeros(1, dtype=torch.int32, device=target.device)
+        self._pos_sub = torch.zeros(1, dtype=torch.int32, device=target.device)
 
     def prefill(self, prompt: list[int]) -> None:
-        """Commit the prompt into the target (blocks of S) and the draft's context; the
-        target's next_token is then the first generated token (the first anchor)."""
-        te, S = self.te, self.te.S
+        """Commit the prompt into the target and the draft's context, ``prefill_block``
+        tokens per target forward; the target's next_token is then the first generated
+        token (the first anchor).  The draft's context takes each chunk's committed rows
+        one verify block of features at a time."""
+        te, S, P = self.te, self.te.S, self.prefill_block
         if not prompt:
             raise ValueError("nonempty prompt required")
         if any(type(t) is not int or not 0 <= t < te.cfg.vocab_size for t in prompt):
             raise ValueError("token ID outside vocabulary")
-        if len(prompt) + S > te.capacity:
+        if (len(prompt) + P - 1) // P * P + S > te.capacity:
             raise ValueError("prompt exceeds the engine's capacity")
+        if self._pe is None:
+            self._pe = te if P == S else te.prefill_engine(P)
+        pe = self._pe
         te.qpos.zero_()
         te.state.zero_()
         te.conv_hist.zero_()
-        for i in range(0, len(prompt), S):
-            chunk = prompt[i:i + S]
-            te.tokens.copy_(torch.tensor(chunk + [0] * (S - len(chunk)), dtype=torch.int32))
-            te.forward()
-            te.accept(auto_commit=False)
-            te.commit([len(chunk)])
-            self.dr.extend()
+        for i in range(0, len(prompt), P):
+            chunk = prompt[i:i + P]
+            n = len(chunk)
+            pe.tokens.copy_(torch.tensor(chunk + [0] * (P - n), dtype=torch.int32))
+            pe.forward()
+            pe.accept(auto_commit=False)
+            pe.commit([n])
+            pe.raise_on_wait_timeout()
+            for j in range(0, n, S):
+                self._valid.fill_(min(S, n - j))
+                self._pos_sub.fill_(n - j)
+                self.dr.extend(valid=self._valid, features=pe.features[j:j + S], pos_sub=self._pos_sub)
 
     def step(self) -> None:
         """One DFlash step on the current stream (device only)."""

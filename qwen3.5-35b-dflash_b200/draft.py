@@ -88,14 +88,21 @@ class DraftEngine:
         return torch.cuda.current_stream(self.dev).cuda_stream
 
     # ------------------------------------------------------------------ context
-    def extend(self, valid: torch.Tensor | None = None):
-        """Append the draft K/V of the last verify block's committed rows: row s of
-        sequence b (s < valid[b], default the target's accepted counts) at position
-        qpos[b] - valid[b] + s, the target's qpos already advanced past them."""
+    def extend(self, valid: torch.Tensor | None = None, features: torch.Tensor | None = None,
+               pos_sub: torch.Tensor | None = None):
+        """Append the draft K/V of committed rows: row s of sequence b (s < valid[b],
+        default the target's accepted counts) of ``features`` (default the target's
+        feature taps of the last verify block, [B * S, F]) at position
+        qpos[b] - pos_sub[b] + s (default pos_sub = valid: the rows are the last ones the
+        target committed, its qpos already advanced past them)."""
         te, d, st = self.te, self.d, self._st()
         valid = te.accepted if valid is None else valid
+        pos_sub = valid if pos_sub is None else pos_sub
+        features = te.features if features is None else features
+        if features.shape[0] != self.T or features.stride(-1) != 1:
+            raise ValueError("features: one row per block position, contiguous rows")
         T, H, Hkv, D = self.T, self.H, self.Hkv, self.D
-        self._call("qw_b16_linear", te.features.data_ptr(), self.fc.data_ptr(), self.ext.data_ptr(),
+        self._call("qw_b16_linear", features.data_ptr(), self.fc.data_ptr(), self.ext.data_ptr(),
                    lib.QW_OUT_BF16, H, T, H, d.feature_size, st)
         self._call("qw_rms_norm", self.ext.data_ptr(), lib.QW_BF16, self.hidden_norm.data_ptr(), lib.QW_BF16,
                    self.ext_n.data_ptr(), lib.QW_BF16, T, H, d.rms_norm_eps, st)
@@ -103,7 +110,7 @@ class DraftEngine:
             self._call("qw_b16_linear", self.ext_n.data_ptr(), lw["kv_ptr"], self.kvx.data_ptr(), lib.QW_OUT_BF16,
                        2 * Hkv * D, T, 2 * Hkv * D, H, st)
             self._call("qw_draft_prep", self.kvx.data_ptr(), 2 * Hkv * D, 0, None, lw["k_norm"].data_ptr(),
-                       d.rms_norm_eps, d.rope_theta, te.qpos.data_ptr(), valid.data_ptr(), valid.data_ptr(),
+                       d.rms_norm_eps, d.rope_theta, te.qpos.data_ptr(), pos_sub.data_ptr(), valid.data_ptr(),
                        te.pages.data_ptr(), te.max_pages, te.P, self.k_cache[i].data_ptr(),
                        self.v_cache[i].data_ptr(), None, self.B, self.S, self.Hq, Hkv, D, st)
 

@@ -158,9 +158,16 @@ def weights_random(cfg: TargetConfig, seed: int = 2, std: float = 0.02, device="
 
 class TargetEngine:
     def __init__(self, cfg: TargetConfig, weights, *, batch: int, block: int = 16, capacity: int = 4096,
-                 page_size: int = 16, device="cuda", ep_group=None):
-        if not 1 <= block <= lib.QW_MAX_BLOCK:
-            raise ValueError(f"block must be in [1, {lib.QW_MAX_BLOCK}]")
+                 page_size: int = 16, device="cuda", ep_group=None, share: "TargetEngine | None" = None):
+        """``share``: another engine of the same configuration, batch, capacity and page
+        size whose state (GDN and conv banks, paged KV cache, positions, next tokens) this
+        one works on -- a prefill engine with longer blocks beside a verify engine."""
+        if not 1 <= block <= lib.QW_MAX_SEQ:
+            raise ValueError(f"block must be in [1, {lib.QW_MAX_SEQ}]")
+        if share is not None and (share.cfg != cfg or share.B != batch or share.capacity != capacity
+                                  or share.P != page_size or ep_group is not None):
+            raise ValueError("a sharing engine needs the same configuration, batch, capacity and pages "
+                             "(and no expert parallelism)")
         self.cfg, self.B, self.S, self.device = cfg, batch, block, torch.device(device)
         self.T = batch * block
         self.capacity = capacity
@@ -219,22 +226,27 @@ class TargetEngine:
         self.top1 = torch.zeros(T, dtype=torch.int32, device=dev)
         self.max_accepted = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.accepted = torch.zeros(batch, dtype=torch.int32, device=dev)
-        self.next_token = torch.zeros(batch, dtype=torch.int32, device=dev)
-        self.qpos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.next_token = torch.zeros(batch, dtype=torch.int32, device=dev) if share is None else share.next_token
+        self.qpos = torch.zeros(batch, dtype=torch.int32, device=dev) if share is None else share.qpos
         # QW_OK / QW_ERR_TIMEOUT of the bounded device waits of the last forward
         self.wait_status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._wait_status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.slots = torch.arange(batch, dtype=torch.int32, device=dev)
-        # state banks
-        self.conv_hist = torch.zeros(max(ng, 1), batch, c.conv_channels, c.linear_conv_kernel_dim - 1,
-                                     dtype=BF16, device=dev)
-        self.state = torch.zeros(max(ng, 1), batch, c.linear_num_value_heads, c.linear_value_head_dim,
-                                 c.linear_key_head_dim, dtype=torch.float32, device=dev)
+        # state banks (a sharing engine works on the other engine's)
         self.max_pages = (capacity + page_size - 1) // page_size
-        self.pages = torch.arange(batch * self.max_pages, dtype=torch.int32, device=dev).view(batch, self.max_pages)
-        kv_shape = (max(na, 1), batch * self.max_pages, c.num_key_value_heads, page_size, c.head_dim)
-        self.k_cache = torch.zeros(kv_shape, dtype=BF16, device=dev)
-        self.v_cache = torch.zeros(kv_shape, dtype=BF16, device=dev)
+        if share is not None:
+            self.conv_hist, self.state = share.conv_hist, share.state
+            self.pages, self.k_cache, self.v_cache = share.pages, share.k_cache, share.v_cache
+        else:
+            self.conv_hist = torch.zeros(max(ng, 1), batch, c.conv_channels, c.linear_conv_kernel_dim - 1,
+                                         dtype=BF16, device=dev)
+            self.state = torch.zeros(max(ng, 1), batch, c.linear_num_value_heads, c.linear_value_head_dim,
+                                     c.linear_key_head_dim, dtype=torch.float32, device=dev)
+            self.pages = torch.arange(batch * self.max_pages, dtype=torch.int32, device=dev).view(batch,
+                                                                                                 self.max_pages)
+            kv_shape = (max(na, 1), batch * self.max_pages, c.num_key_value_heads, page_size, c.head_dim)
+            self.k_cache = torch.zeros(kv_shape, dtype=BF16, device=dev)
+            self.v_cache = torch.zeros(kv_shape, dtype=BF16, device=dev)
         # GDN layer descriptors (device array) and dims
         descs = (lib.GdnLayer * max(ng, 1))()
         for l, gi in self.gdn_idx.items():
@@ -477,6 +489,15 @@ class TargetEngine:
         self.graph = None
         if self.ep_moe is not None:
             self.ep_moe.close()
+
+    def prefill_engine(self, block: int = 64) -> "TargetEngine":
+        """An engine of ``block``-token blocks on this engine's weights and state: prompt
+        chunks of ``block`` tokens per forward (the reference prefills the whole prompt in
+        one forward, fused/session.py:282-296) instead of verify blocks of 16.  Its
+        ``forward`` + ``accept(False)`` + ``commit([n])`` commits the first n tokens of a
+        chunk into the shared banks and sets the shared next token."""
+        return TargetEngine(self.cfg, (self.glob, self.layers), batch=self.B, block=block, capacity=self.capacity,
+                            page_size=self.P, device=self.device, share=self)
 
     # ------------------------------------------------------------------ state utilities
     def snapshot(self):

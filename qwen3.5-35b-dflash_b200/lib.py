@@ -19,6 +19,7 @@ QW_OK, QW_ERR_ARG, QW_ERR_UNSUPPORTED, QW_ERR_CUDA, QW_ERR_TIMEOUT = range(5)
 QW_F32, QW_F16, QW_BF16 = 0, 1, 2
 QW_OUT_BF16, QW_OUT_F32, QW_OUT_RESID_BF16 = 0, 1, 2
 QW_MAX_BLOCK = 16
+QW_MAX_SEQ = 256   # tokens per sequence in one forward (prefill chunks)
 QW_ATTN_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024  # static scratch of qw_attention_noalloc
 
 _c = ctypes
