@@ -446,7 +446,7 @@ def time_moe_up(eng, cfg, dev, iters: int = 50):
     st = torch.cuda.current_stream(dev).cuda_stream
     so = eng.lib
     lib.check(so.qw_moe_route_x(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, E, k, E, lib.QW_BF16,
-                                x.data_ptr(), H, g, ws.data_ptr(), st))
+                                x.data_ptr(), H, g, ws.data_ptr(), st, 0))
     args = (x.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(), lw.shared_gu.data_ptr(),
             lw.shared_down.data_ptr(), T, H, E, I, k, g, ws.data_ptr(), st)
     for _ in range(5):
@@ -524,7 +524,7 @@ def run_kernels(args):
 
     def route():
         chk(so.qw_moe_route_x(logits.data_ptr(), lib.QW_BF16, eng.nrouter, T, Ex, k, Ex, lib.QW_BF16, x.data_ptr(), H,
-                              g, ws.data_ptr(), s))
+                              g, ws.data_ptr(), s, 0))
 
     def up(lw):
         return lambda: chk(so.qw_moe_up_w4(x.data_ptr(), lw.gate_up.data_ptr(), lw.down.data_ptr(),

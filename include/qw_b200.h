@@ -194,11 +194,17 @@ int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, int64_t token
  * gate/up kernel: fp16 copy and per-group sums, written once per block instead of by
  * every gate/up CTA.  hidden and group as in that call; staged only for blocks of
  * <= 16 tokens with hidden a multiple of 256 and x 16-byte aligned (otherwise this is
- * qw_moe_route and the expert call converts x itself).  No counterpart in the
- * reference: qw_moe_route's extra work, same outputs. */
+ * qw_moe_route and the expert call converts x itself).  tie_order 1: qw_moe_route's
+ * outputs exactly; 0: the same selected experts and weights, but experts whose logits
+ * tie inside the top k may be listed in ascending id instead of torch.topk's order
+ * (only a tie between the k-th and (k+1)-th logits runs the order emulation).  No
+ * consumer of the routing depends on that order (the combine adds experts in
+ * ascending id; equal weights renormalise to the same bits), so the MoE outputs are the
+ * same bits.  No counterpart in the reference: qw_moe_route's extra work. */
 int qw_moe_route_x(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens,
                    int64_t experts, int64_t top_k, int64_t shared_col, int act_dtype,
-                   const void* x, int64_t hidden, int32_t group, void* workspace, void* stream);
+                   const void* x, int64_t hidden, int32_t group, void* workspace, void* stream,
+                   int32_t tie_order);
 
 /* The per-expert lists of a routed block in the workspace: active experts in
  * ascending id, and for each its (token, slot) pairs in ascending token (the order in

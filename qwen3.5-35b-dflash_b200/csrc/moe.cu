@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(32 * ROUTE_TPB) route_topk_kernel(const LT* __
                                                                    int T, int E, int k, int shared_col,
                                                                    int act_is_f16, void* ws,
                                                                    const __nv_bfloat16* __restrict__ x, int H,
-                                                                   int G) {
+                                                                   int G, int tie_order) {
   extern __shared__ __align__(16) uint8_t smem_all[];
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * ROUTE_TPB + (threadIdx.x >> 5);   // this warp's token
@@ -600,7 +600,8 @@ __global__ void __launch_bounds__(32 * ROUTE_TPB) route_topk_kernel(const LT* __
           for (int j = 0; j < ROUTE_MAXJ; ++j) loc = max(loc, pk[j]);
           const uint32_t best = __reduce_max_sync(0xffffffffu, loc);
           // a tie anywhere among the k+1 largest: use the exact emulation
-          if (r > 0 && (best >> 12) == (prev >> 12)) { exact = true; break; }
+          // (tie_order 0: only a tie at the k / k+1 boundary changes the selected set)
+          if (r > 0 && (best >> 12) == (prev >> 12) && (tie_order || r == k)) { exact = true; break; }
           prev = best;
           const int e = 0xFFF - static_cast<int>(best & 0xFFFu);
           const uint32_t kv = best & 0xFFFFF000u;
@@ -635,7 +636,7 @@ __global__ void __launch_bounds__(32 * ROUTE_TPB) route_topk_kernel(const LT* __
           if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
         }
         // a tie (or a NaN) anywhere among the k+1 largest: use the exact emulation
-        if (r > 0 && !(prev > bv)) { exact = true; break; }
+        if (r > 0 && !(prev > bv) && (tie_order || r == k || isnan(bv) || isnan(prev))) { exact = true; break; }
         prev = bv;
         if (r < k && lane == r) { sel_v = bv; sel_i = bi; }
         if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
@@ -2375,7 +2376,7 @@ __global__ void router_dense_kernel(const ET* __restrict__ x, const ET* __restri
 // ------------------------------------------------------------------ host launchers
 template <typename LT>
 static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, int shared_col,
-                        int act_is_f16, void* ws, const void* x, int H, int G, cudaStream_t s) {
+                        int act_is_f16, void* ws, const void* x, int H, int G, cudaStream_t s, int tie_order = 1) {
   const size_t smem = ROUTE_TPB * route_warp_smem(E);
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
@@ -2386,7 +2387,7 @@ static int launch_route(const void* logits, int64_t ldl, int T, int E, int k, in
   if (smem > 64 * 1024) return fail(QW_ERR_UNSUPPORTED, "route: too many experts");
   QW_LAUNCH_PDL("moe route", route_topk_kernel<LT>, dim3((T + ROUTE_TPB - 1) / ROUTE_TPB), dim3(32 * ROUTE_TPB), smem,
                 s, static_cast<const LT*>(logits), ldl, T, E, k, shared_col, act_is_f16, ws,
-                static_cast<const __nv_bfloat16*>(x), H, G);
+                static_cast<const __nv_bfloat16*>(x), H, G, tie_order);
   return QW_OK;
 }
 
@@ -2661,8 +2662,9 @@ static WsParts split_ws(void* ws, int T, int H, int E, int I, int k) {
 
 static int route_entry(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
                        int64_t top_k, int64_t shared_col, int act_dtype, const void* x, int64_t hidden,
-                       int32_t group, void* workspace, void* stream) {
+                       int32_t group, void* workspace, void* stream, int tie_order = 1) {
   QW_CHECK_ARG(logits && workspace, "moe_route: null pointer");
+  QW_CHECK_ARG(tie_order == 0 || tie_order == 1, "moe_route: tie_order must be 0 or 1");
   QW_CHECK_ARG(tokens >= 1 && tokens <= 4096 && experts >= 1 && experts <= 1024 && top_k >= 1 &&
                    top_k <= 16 && top_k <= experts && ldl >= experts,
                "MoE needs compatible expert weights and a valid top_k");
@@ -2681,9 +2683,10 @@ static int route_entry(const void* logits, int logit_dtype, int64_t ldl, int64_t
   if (x == nullptr) H = 256, G = 32;   // header only
   cudaStream_t s = as_stream(stream);
   const int sc = static_cast<int>(shared_col), f16 = act_dtype == QW_F16;
-  if (logit_dtype == QW_BF16) return launch_route<__nv_bfloat16>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s);
-  if (logit_dtype == QW_F16) return launch_route<__half>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s);
-  if (logit_dtype == QW_F32) return launch_route<float>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s);
+  if (logit_dtype == QW_BF16)
+    return launch_route<__nv_bfloat16>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s, tie_order);
+  if (logit_dtype == QW_F16) return launch_route<__half>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s, tie_order);
+  if (logit_dtype == QW_F32) return launch_route<float>(logits, ldl, T, E, k, sc, f16, workspace, x, H, G, s, tie_order);
   return fail(QW_ERR_ARG, "moe_route: bad logit dtype");
 }
 
@@ -2695,10 +2698,10 @@ extern "C" int qw_moe_route(const void* logits, int logit_dtype, int64_t ldl, in
 
 extern "C" int qw_moe_route_x(const void* logits, int logit_dtype, int64_t ldl, int64_t tokens, int64_t experts,
                               int64_t top_k, int64_t shared_col, int act_dtype, const void* x, int64_t hidden,
-                              int32_t group, void* workspace, void* stream) {
+                              int32_t group, void* workspace, void* stream, int32_t tie_order) {
   QW_CHECK_ARG(x != nullptr, "moe_route_x: null x");
   return route_entry(logits, logit_dtype, ldl, tokens, experts, top_k, shared_col, act_dtype, x, hidden, group,
-                     workspace, stream);
+                     workspace, stream, tie_order);
 }
 
 extern "C" int qw_moe_route_lists(void* workspace, int64_t tokens, int64_t experts, int64_t top_k, void* stream) {

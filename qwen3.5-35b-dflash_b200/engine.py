@@ -341,7 +341,7 @@ class TargetEngine:
             if self.router_bias is not None:
                 self.router_logits[:, :E].add_(self.router_bias)
             self._call("qw_moe_route_x", self.router_logits.data_ptr(), lib.QW_BF16, self.nrouter, T, E, k, E,
-                       lib.QW_BF16, self.normed.data_ptr(), H, c.quant_group, self.moe_ws.data_ptr(), st)
+                       lib.QW_BF16, self.normed.data_ptr(), H, c.quant_group, self.moe_ws.data_ptr(), st, 0)
             if self.ep_moe is not None:
                 if self._recording is not None:
                     self._recording["qw_moe_ep"] = self._recording.get("qw_moe_ep", 0) + 1

@@ -71,7 +71,7 @@ SIGNATURES = {
     "qw_moe_ep_combine_norm": (_c.c_int, [P, P, I64, I64, P, I64, I64, I64, I64, I64, _c.c_int, P, P, F32, P, I64,
                                           _c.c_int, P]),
     "qw_moe_ep_scatter": (_c.c_int, [P, P, I64, I64, I64, I64, I64, I64, I64, _c.c_int, P]),
-    "qw_moe_route_x": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, I64, I32, P, P]),
+    "qw_moe_route_x": (_c.c_int, [P, _c.c_int, I64, I64, I64, I64, I64, _c.c_int, P, I64, I32, P, P, I32]),
     "qw_moe_route_lists": (_c.c_int, [P, I64, I64, I64, P]),
     "qw_moe_experts_w4": (_c.c_int, [P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P]),
     "qw_moe_up_w4": (_c.c_int, [P, P, P, P, P, I64, I64, I64, I64, I64, I32, P, P]),

@@ -206,7 +206,7 @@ def test_moe_route_x_staging_is_bit_identical(cuda_lib, t, g):
             lib.call("qw_moe_route", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16, ws.data_ptr(), st)
         else:
             lib.call("qw_moe_route_x", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16,
-                     stage_x.data_ptr(), h, g, ws.data_ptr(), st)
+                     stage_x.data_ptr(), h, g, ws.data_ptr(), st, 1)
         lib.call("qw_moe_experts_w4", x_in.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(),
                  sdn.data_ptr(), t, h, e, inter, k, g, ws.data_ptr(), st)
         lib.call("qw_moe_combine", ws.data_ptr(), out.data_ptr(), 0, t, h, e, inter, k, 1, st)
@@ -215,6 +215,62 @@ def test_moe_route_x_staging_is_bit_identical(cuda_lib, t, g):
 
     assert torch.equal(run(x, x), run(None, x))
     assert torch.equal(run(x, x2), run(None, x2))
+
+
+@pytest.mark.parametrize("t,e,k,combine", [(16, 256, 8, "norm"), (16, 64, 8, "plain"), (48, 40, 6, "plain")])
+def test_route_tie_order_zero_same_selection_and_outputs(cuda_lib, t, e, k, combine):
+    """qw_moe_route_x with tie_order 0 (the engine's routing) on tie-heavy logits: per
+    token the same selected experts with the same weights as torch.topk, ties at the
+    k / k+1 boundary resolved in torch's order, and the MoE output (experts + combine,
+    plain or fused with the next RMSNorm) bit-identical to the tie_order 1 routing."""
+    from qwen35_dflash_b200 import lib, w4
+    g, h, inter = 128, 2048, 256
+    gen = torch.Generator().manual_seed(t * 31 + e)
+    logits = _tie_heavy_logits(t, e, seed=t * 7 + e + 1).float()
+    logits[1::4] = torch.randint(-2, 3, (len(range(1, t, 4)), e), generator=gen).float() * 0.5
+    logits = torch.cat([logits, torch.randn(t, 1, generator=gen)], 1).to(torch.bfloat16).cuda()
+    probs = torch.softmax(logits[:, :e].cpu().float(), -1)
+    _, want = torch.topk(probs, k, dim=-1)
+    x = torch.randn(t, h, device="cuda").to(torch.bfloat16)
+    gu = w4.pack_w4(torch.randint(-8, 8, (e, 2 * inter, h), dtype=torch.int8, device="cuda"),
+                    (torch.rand(e, 2 * inter, h // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    dn = w4.pack_w4(torch.randint(-8, 8, (e, h, inter), dtype=torch.int8, device="cuda"),
+                    (torch.rand(e, h, inter // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    sgu = w4.pack_w4(torch.randint(-8, 8, (2 * inter, h), dtype=torch.int8, device="cuda"),
+                     (torch.rand(2 * inter, h // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    sdn = w4.pack_w4(torch.randint(-8, 8, (h, inter), dtype=torch.int8, device="cuda"),
+                     (torch.rand(h, inter // g, device="cuda") * 0.02).to(torch.bfloat16), g)
+    gamma = (torch.randn(h, device="cuda") * 0.1).to(torch.bfloat16)
+    resid = torch.randn(t, h, device="cuda").to(torch.bfloat16)
+    st = lib.stream_ptr()
+
+    def run(order):
+        ws = torch.zeros(cuda_lib.qw_moe_workspace_bytes(t, h, e, inter, k), dtype=torch.uint8, device="cuda")
+        lib.call("qw_moe_route_x", logits.data_ptr(), lib.QW_BF16, e + 1, t, e, k, e, lib.QW_BF16,
+                 x.data_ptr(), h, g, ws.data_ptr(), st, order)
+        lib.call("qw_moe_experts_w4", x.data_ptr(), gu.data_ptr(), dn.data_ptr(), sgu.data_ptr(),
+                 sdn.data_ptr(), t, h, e, inter, k, g, ws.data_ptr(), st)
+        hidden = resid.clone()
+        normed = torch.empty(t, h, dtype=torch.bfloat16, device="cuda")
+        if combine == "norm":
+            lib.call("qw_moe_combine_norm", ws.data_ptr(), hidden.data_ptr(), t, h, e, inter, k, 1,
+                     gamma.data_ptr(), normed.data_ptr(), 1e-6, None, 0, 0, st)
+        else:
+            lib.call("qw_moe_combine", ws.data_ptr(), normed.data_ptr(), 0, t, h, e, inter, k, 1, st)
+        torch.cuda.synchronize()
+        idx = ws[: t * k * 4].view(torch.int32).view(t, k).cpu()
+        w = ws[t * k * 4: 2 * t * k * 4].view(torch.float32).view(t, k).cpu()
+        return idx, w, hidden, normed
+
+    i1, w1, h1, n1 = run(1)
+    i0, w0, h0, n0 = run(0)
+    np.testing.assert_array_equal(i1.numpy(), want.numpy())
+    for r in range(t):
+        assert sorted(i0[r].tolist()) == sorted(want[r].tolist()), r
+        m1 = dict(zip(i1[r].tolist(), w1[r].tolist()))
+        m0 = dict(zip(i0[r].tolist(), w0[r].tolist()))
+        assert m0 == m1, r
+    assert torch.equal(h0, h1) and torch.equal(n0, n1)
 
 
 @pytest.mark.parametrize("tag", ["bf16", "f16"])
