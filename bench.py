@@ -221,9 +221,11 @@ def cpu_baseline_leg(samples: int = 5) -> dict:
 
 
 # ---------------------------------------------------------------------------- GPU side
-def print_timeline(prof):
+def print_timeline(prof, detail: bool = False):
     """Per kernel of one graph replay: launches, summed duration and the time it adds to
-    the step's critical path (its end minus the latest end before it, in start order)."""
+    the step's critical path (its end minus the latest end before it, in start order).
+    detail: also every launch of decoder layers 4-7 in order (start from the step's
+    first start, duration, added)."""
     import collections
     evs = sorted(((e.name, e.time_range.start, e.time_range.end) for e in prof.events()
                   if e.device_type.name == "CUDA"), key=lambda x: x[1])
@@ -240,12 +242,20 @@ def print_timeline(prof):
     st = steps[-1]
     cnt, dur, marg = collections.Counter(), collections.Counter(), collections.Counter()
     prev = st[0][1]
+    rows = []
     for name, s, e in st:
         n = name.split("<")[0].split("(")[0].replace("void ", "")
         cnt[n] += 1
         dur[n] += e - s
         marg[n] += max(e, prev) - prev
+        rows.append((n, s - st[0][1], e - s, max(e, prev) - prev))
         prev = max(prev, e)
+    if detail:
+        # the launches of layers 4-7: after the embedding norm, 10 per GDN layer and 11 per
+        # attention layer (layers 3, 7, ... are attention)
+        first = 1 + 4 * 10 + 1
+        for n, start, d, added in rows[first:first + 41]:
+            print(f"  {n:34s} start {start:9.1f} dur {d:7.2f} added {added:6.2f}")
     print(f"timeline: {len(st)} launches, {st[-1][2] - st[0][1]:.1f} us from first start to last end")
     print(f"{'kernel':40s} {'launches':>8s} {'dur us':>9s} {'added us':>9s} {'per launch':>10s}")
     for n, m in marg.most_common():
@@ -322,7 +332,7 @@ def run_ours(args, rank, world, local_rank):
                 step(args.warmup + i)
             torch.cuda.synchronize(dev)
         if rank == 0:
-            print_timeline(prof)
+            print_timeline(prof, detail=args.timeline_detail)
         if world > 1:
             dist.barrier()
         eng.close()
@@ -816,6 +826,8 @@ def main():
                     help="with --gpus > 1: run independent replicas instead of sharding the routed experts")
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--timeline-detail", action="store_true",
+                    help="with --timeline: also each launch of decoder layers 4-7 in order")
     ap.add_argument("--timeline", action="store_true",
                     help="after warm-up, print the in-graph kernel timeline of one step (rank 0) and exit")
     ap.add_argument("--profile-step", action="store_true",
