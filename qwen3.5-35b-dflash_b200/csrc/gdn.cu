@@ -150,8 +150,10 @@ __device__ __forceinline__ void conv_channel(const float (&hist)[GDN_CONV_K - 1]
   }
 }
 
+// Four CTAs per SM (64 registers, no spills; the shared memory allows four): at batch 8
+// and up the grid is several waves of clusters, and residency sets the throughput.
 template <int DK, int DV, int VSPLIT, bool COMMIT>
-__global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS)
+__global__ void __launch_bounds__(GdnTile<DK, DV, VSPLIT>::THREADS, 4)
     gdn_block_kernel(GdnDims d, const GdnLayer* __restrict__ layers, int layer0) {
   using Tile = GdnTile<DK, DV, VSPLIT>;
   constexpr int COLS = Tile::COLS, ROWS = Tile::ROWS, THREADS = Tile::THREADS;
