@@ -995,6 +995,21 @@ __device__ __forceinline__ void xt_slot(const A& a, const XtRoute& r, int sl, bo
   np = r.off[ai + 1] - pbase;
 }
 
+// Unit at position p of a round-robin deal of nu units over nw workers (worker w takes
+// positions w, w + nw, ...).  Units 0 .. nh-1 are heavy (the shared expert's: all T
+// tokens, two n-tiles of MMAs against one of a routed expert).  In natural order they
+// land on the first workers, which also take a unit of the partial last round, and the
+// launch waits for them; here they take the positions of the last full round whose
+// workers get no unit of the partial round.  Only the assignment changes, not what a
+// unit computes.
+__device__ __forceinline__ int xt_unit_at(int p, int nu, int nw, int nh) {
+  const int full = nu / nw, r0 = nu % nw;
+  if (nh == 0 || full == 0 || r0 == 0 || r0 + nh > nw) return p;
+  const int p0 = (full - 1) * nw + r0;
+  if (p >= p0 && p < p0 + nh) return p - p0;
+  return nh + (p < p0 ? p : p - nh);
+}
+
 struct XtArgs {
   MoeArgs<__nv_bfloat16> m;
   int32_t* status;      // g_moe_wait_status on the launching device
@@ -1015,8 +1030,9 @@ int moe_wait_status_addr(int32_t** out) {
 }
 
 // Gate/up.  Unit = (slot, intermediate tile j): the gate row tile j then the up row tile
-// I/16 + j, each cut into stages of up to XT_UP_CPS chunks; unit u goes to warp u mod (all
-// warps).  x [T, H] is staged once per CTA.  (Splitting a unit's K range over two warps
+// I/16 + j, each cut into stages of up to XT_UP_CPS chunks; units are dealt round-robin
+// to all warps (xt_unit_at: the shared expert's heavier units on warps with one unit
+// fewer).  x [T, H] is staged once per CTA.  (Splitting a unit's K range over two warps
 // was measured no faster, and would change the fp32 summation order against the
 // streaming kernels that serve larger blocks.)
 template <int G>
@@ -1042,9 +1058,45 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
   const RouteView rv = route_view(a.ws, a.T, a.E, a.k);
   pdl_wait();   // the top-k indices and the staged x come from the predecessor (route)
   pdl_trigger();
-  // x -> shared memory (cp.async), overlapped with the list building and the first
-  // weight stages below: as fp16 with its group sums when the route kernel staged this
-  // x (qw_moe_route_x), else as bf16, converted and summed here
+  // the lists first: the weight copies below depend on them and are the long pole (the
+  // activation copies issued ahead of them delayed the lists' loads)
+  xt_build_route(rt, scratch, rv, T, a.E, a.k, a.e_lo, a.e_cnt, blockIdx.x == 0);
+  __syncthreads();
+  const int J = I / 16;
+  const int nslots = a.has_shared + rt.n_active;
+  const int nu = nslots * J;
+  const int nh = a.has_shared && T > 8 ? J : 0;   // the shared expert's units: two n-tiles
+  const int gw = blockIdx.x * XT_UP_WARPS + warp, nw = gridDim.x * XT_UP_WARPS;
+  const int my_units = gw < nu ? (nu - 1 - gw) / nw + 1 : 0;
+  // stage s of a unit: the gate chunks [s * hc, s * hc + hc) and the up chunks of the
+  // same k range (two copies, the up half second); spu stages per unit
+  const int hc = cps / 2, spu = nch / hc;
+  const uint32_t hbytes = hc * Fmt::CHB;
+  const int64_t tbytes = Fmt::tile_offset(1, H, 0);   // one row tile, all chunks
+  const int Q = my_units * spu;
+  // lane 0's copy cursor: the warp's unit cu_i, its stage cu_s, the unit's gate tile
+  int cu_i = 0, cu_s = 0;
+  const uint8_t* cu_w = nullptr;
+  auto cursor_unit = [&]() {
+    const int u = xt_unit_at(gw + cu_i * nw, nu, nw, nh);
+    int np_, pb_;
+    xt_slot(a, rt, u / J, true, cu_w, np_, pb_);
+    cu_w += Fmt::tile_offset(u % J, H, 0);
+  };
+  auto issue_next = [&](int qq) {
+    ring.issue2(qq, cu_w + cu_s * hbytes, cu_w + J * tbytes + cu_s * hbytes, hbytes);
+    if (++cu_s == spu) {
+      cu_s = 0;
+      if (++cu_i < my_units) cursor_unit();
+    }
+  };
+  if (lane == 0 && my_units > 0) {
+    cursor_unit();
+    for (int qq = 0; qq < XT_NST && qq < Q; ++qq) issue_next(qq);
+  }
+  // x -> shared memory (cp.async) while the first weight stages stream: as fp16 with its
+  // group sums when the route kernel staged this x (qw_moe_route_x), else as bf16,
+  // converted and summed below
   const StageView sv = stage_view(a.ws, T, a.E, a.k, H);
   const bool staged = sv.tag[0] == reinterpret_cast<unsigned long long>(a.x) && sv.tag[1] == stage_key(T, H, G);
   if (staged) {
@@ -1064,39 +1116,6 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
     }
   }
   cp_async_commit();
-  xt_build_route(rt, scratch, rv, T, a.E, a.k, a.e_lo, a.e_cnt, blockIdx.x == 0);
-  __syncthreads();
-  const int J = I / 16;
-  const int nslots = a.has_shared + rt.n_active;
-  const int nu = nslots * J;
-  const int gw = blockIdx.x * XT_UP_WARPS + warp, nw = gridDim.x * XT_UP_WARPS;
-  const int my_units = gw < nu ? (nu - 1 - gw) / nw + 1 : 0;
-  // stage s of a unit: the gate chunks [s * hc, s * hc + hc) and the up chunks of the
-  // same k range (two copies, the up half second); spu stages per unit
-  const int hc = cps / 2, spu = nch / hc;
-  const uint32_t hbytes = hc * Fmt::CHB;
-  const int64_t tbytes = Fmt::tile_offset(1, H, 0);   // one row tile, all chunks
-  const int Q = my_units * spu;
-  // lane 0's copy cursor: the warp's unit cu_i, its stage cu_s, the unit's gate tile
-  int cu_i = 0, cu_s = 0;
-  const uint8_t* cu_w = nullptr;
-  auto cursor_unit = [&]() {
-    const int u = gw + cu_i * nw;
-    int np_, pb_;
-    xt_slot(a, rt, u / J, true, cu_w, np_, pb_);
-    cu_w += Fmt::tile_offset(u % J, H, 0);
-  };
-  auto issue_next = [&](int qq) {
-    ring.issue2(qq, cu_w + cu_s * hbytes, cu_w + J * tbytes + cu_s * hbytes, hbytes);
-    if (++cu_s == spu) {
-      cu_s = 0;
-      if (++cu_i < my_units) cursor_unit();
-    }
-  };
-  if (lane == 0 && my_units > 0) {
-    cursor_unit();
-    for (int qq = 0; qq < XT_NST && qq < Q; ++qq) issue_next(qq);
-  }
   cp_async_wait<0>();
   // unstaged x: bf16 -> fp16 in place (each thread converts the vectors it copied), and
   // the per (token, K group) activation sums of the nibble MMA's offset term: with H a
@@ -1125,7 +1144,7 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
   const int gid = lane >> 2, tig = lane & 3;
   int q = 0;
   for (int i = 0; i < my_units; ++i) {
-    const int u = gw + i * nw, j = u % J;
+    const int u = xt_unit_at(gw + i * nw, nu, nw, nh), j = u % J;
     const uint8_t* w;
     int np, pb;
     xt_slot(a, rt, u / J, true, w, np, pb);
@@ -1153,13 +1172,18 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
         return;
       }
       const uint8_t* st = ring.stage(q);
-      for (int c = 0; c < hc; ++c)
-        w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[0], (s * hc + c) * G, xq[0][0], xq[0][1],
-                         s * hc + c, lane, accg[0], accu[0]);
-      if (two)
-        for (int c = 0; c < hc; ++c)
-          w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[1], (s * hc + c) * G, xq[1][0],
-                           xq[1][1], s * hc + c, lane, accg[1], accu[1]);
+      // one n-tile of the stage, four chunk pairs at a time (eight independent MMA chains)
+      auto tile = [&](const __half* xrn, const float* q0, const float* q1, float(&ag)[4], float(&au)[4]) {
+        int c = 0;
+        for (; c + 4 <= hc; c += 4)
+          w4n_smem_pairs<G, 4>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xrn, (s * hc + c) * G, q0, q1,
+                               s * hc + c, lane, ag, au);
+        for (; c < hc; ++c)
+          w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xrn, (s * hc + c) * G, q0, q1, s * hc + c,
+                           lane, ag, au);
+      };
+      tile(xr[0], xq[0][0], xq[0][1], accg[0], accu[0]);
+      if (two) tile(xr[1], xq[1][0], xq[1][1], accg[1], accu[1]);
       __syncwarp();
       if (lane == 0 && q + XT_NST < Q) issue_next(q + XT_NST);
     }
@@ -1182,7 +1206,8 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_bulk_kernel(XtArgs
 
 // Down.  Unit = (slot, block of XT_DN_WARPS * spw row tiles); the CTA's warps share the
 // unit, each streaming spw... stages of tiles; the unit's rows of h are staged in shared
-// memory (three buffers across units).  Units go to CTAs round-robin.
+// memory (three buffers across units).  Units go to CTAs round-robin (xt_unit_at: the
+// shared expert's heavier units on CTAs with one unit fewer).
 template <int G>
 __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtArgs args, int tiles_per_stage,
                                                                          int stages_per_warp) {
@@ -1212,10 +1237,11 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   __syncthreads();
   const int nslots = a.has_shared + rt.n_active;
   const int nu = nslots * nrb;
+  const int nh = a.has_shared && T > 8 ? nrb : 0;   // the shared expert's units: two n-tiles
   const int my_units = blockIdx.x < nu ? (nu - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int Q = my_units * spw;
   auto src = [&](int q) -> const uint8_t* {
-    const int u = blockIdx.x + (q / spw) * gridDim.x, l = q % spw;
+    const int u = xt_unit_at(blockIdx.x + (q / spw) * gridDim.x, nu, gridDim.x, nh), l = q % spw;
     const uint8_t* w;
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
@@ -1227,7 +1253,7 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   // h rows of unit i -> buffer i % 3: it is restaged (for unit i + 3) only after every
   // warp has passed the barrier of unit i + 1, so units need one barrier each
   auto stage_h = [&](int i) {
-    const int u = blockIdx.x + i * gridDim.x;
+    const int u = xt_unit_at(blockIdx.x + i * gridDim.x, nu, gridDim.x, nh);
     const uint8_t* w;
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
@@ -1241,17 +1267,31 @@ __global__ void __launch_bounds__(XT_DN_WARPS * 32, 1) moe_down_bulk_kernel(XtAr
   };
   pdl_wait();   // h comes from the predecessor (gate/up); the lists and weights do not
   pdl_trigger();
-  if (my_units > 0) stage_h(0);
-  cp_async_commit();
+  // With at most three units (the usual case) every unit's h rows fit the three buffers:
+  // they are staged once, behind one barrier, and the warps then run their units
+  // without CTA barriers (a barrier per unit made each unit wait for the CTA's slowest
+  // weight copy).  Otherwise unit i + 1 is staged while unit i runs.
+  const bool h_once = my_units <= 3;
+  if (h_once) {
+    for (int i = 0; i < my_units; ++i) stage_h(i);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+  } else {
+    stage_h(0);
+    cp_async_commit();
+  }
   const int gid = lane >> 2;
   int q = 0;
   bool ok = true;
   for (int i = 0; i < my_units; ++i) {
-    if (i + 1 < my_units) stage_h(i + 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const int u = blockIdx.x + i * gridDim.x;
+    if (!h_once) {
+      if (i + 1 < my_units) stage_h(i + 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+      __syncthreads();
+    }
+    const int u = xt_unit_at(blockIdx.x + i * gridDim.x, nu, gridDim.x, nh);
     const uint8_t* w;
     int np, pb;
     xt_slot(a, rt, u / nrb, false, w, np, pb);
@@ -1625,13 +1665,18 @@ __global__ void __launch_bounds__(XT_UP_WARPS * 32, 1) moe_up_grouped_kernel(XtA
         break;
       }
       const uint8_t* st = ring.stage(q);
-      for (int c = 0; c < hc; ++c)
-        w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[0], (s * hc + c) * G, xq[0][0], xq[0][1],
-                         s * hc + c, lane, accg[0], accu[0]);
-      if (two)
-        for (int c = 0; c < hc; ++c)
-          w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xr[1], (s * hc + c) * G, xq[1][0],
-                           xq[1][1], s * hc + c, lane, accg[1], accu[1]);
+      // one n-tile of the stage, four chunk pairs at a time (eight independent MMA chains)
+      auto tile = [&](const __half* xrn, const float* q0, const float* q1, float(&ag)[4], float(&au)[4]) {
+        int c = 0;
+        for (; c + 4 <= hc; c += 4)
+          w4n_smem_pairs<G, 4>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xrn, (s * hc + c) * G, q0, q1,
+                               s * hc + c, lane, ag, au);
+        for (; c < hc; ++c)
+          w4n_smem_pair<G>(st + c * Fmt::CHB, st + hbytes + c * Fmt::CHB, xrn, (s * hc + c) * G, q0, q1, s * hc + c,
+                           lane, ag, au);
+      };
+      tile(xr[0], xq[0][0], xq[0][1], accg[0], accu[0]);
+      if (two) tile(xr[1], xq[1][0], xq[1][1], accg[1], accu[1]);
       __syncwarp();
       if (lane == 0 && q + XT_NST < Q) issue_next(q + XT_NST);
     }

@@ -460,6 +460,73 @@ __device__ __forceinline__ void w4n_smem_pair(const uint8_t* ca, const uint8_t* 
   accb[3] = fmaf(fmaf(pb[3], 0x1p20f, x1), s2b.y, accb[3]);
 }
 
+// NC consecutive chunk pairs (chunks cg .. cg + NC - 1 of both tiles, CHB apart) at once:
+// 2 NC independent MMA chains in flight.  Each chunk's MMA sequence and its epilogue, in
+// chunk order, are those of NC calls of w4n_smem_pair, so the results have the same bits.
+template <int G, int NC>
+__device__ __forceinline__ void w4n_smem_pairs(const uint8_t* ca, const uint8_t* cb, const __half* xr, int k0,
+                                               const float* xq0, const float* xq1, int cg, int lane,
+                                               float (&acca)[4], float (&accb)[4]) {
+  using Fmt = W4Fmt<G>;
+  uint32_t wa[NC][Fmt::WORDS], wb[NC][Fmt::WORDS];
+  uint32_t sca[NC], scb[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int v = 0; v < Fmt::NV; ++v) {
+      const int off = c * Fmt::CHB + v * (32 * Fmt::VW * 4) + lane * (Fmt::VW * 4);
+      if constexpr (Fmt::VW == 4) {
+        const uint4 u = *reinterpret_cast<const uint4*>(ca + off);
+        const uint4 t = *reinterpret_cast<const uint4*>(cb + off);
+        wa[c][v * 4 + 0] = u.x; wa[c][v * 4 + 1] = u.y; wa[c][v * 4 + 2] = u.z; wa[c][v * 4 + 3] = u.w;
+        wb[c][v * 4 + 0] = t.x; wb[c][v * 4 + 1] = t.y; wb[c][v * 4 + 2] = t.z; wb[c][v * 4 + 3] = t.w;
+      } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(ca + off);
+        const uint2 t = *reinterpret_cast<const uint2*>(cb + off);
+        wa[c][v * 2 + 0] = u.x; wa[c][v * 2 + 1] = u.y;
+        wb[c][v * 2 + 0] = t.x; wb[c][v * 2 + 1] = t.y;
+      }
+    }
+    sca[c] = *reinterpret_cast<const uint32_t*>(ca + c * Fmt::CHB + 8 * G + (lane >> 2) * 4);
+    scb[c] = *reinterpret_cast<const uint32_t*>(cb + c * Fmt::CHB + 8 * G + (lane >> 2) * 4);
+  }
+  const int tig = lane & 3;
+  float pa[NC][4], pb[NC][4];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) pa[c][r] = pb[c][r] = 0.f;
+#pragma unroll
+  for (int q = 0; q < G / 32; ++q) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + k0 + c * G + 32 * q + 8 * tig);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t b0 = h ? v.z : v.x, b1 = h ? v.w : v.y;
+        uint32_t a[4];
+        w4_nibbles_f16(wa[c][2 * q + h], a);
+        mma_f16_16816(pa[c], a, b0, b1);
+        w4_nibbles_f16(wb[c][2 * q + h], a);
+        mma_f16_16816(pb[c], a, b0, b1);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const float x0 = -8.f * xq0[cg + c], x1 = -8.f * xq1[cg + c];
+    const float2 s2a = bf162_to_f2(sca[c]), s2b = bf162_to_f2(scb[c]);
+    acca[0] = fmaf(fmaf(pa[c][0], 0x1p24f, x0), s2a.x, acca[0]);
+    acca[1] = fmaf(fmaf(pa[c][1], 0x1p24f, x1), s2a.x, acca[1]);
+    acca[2] = fmaf(fmaf(pa[c][2], 0x1p20f, x0), s2a.y, acca[2]);
+    acca[3] = fmaf(fmaf(pa[c][3], 0x1p20f, x1), s2a.y, acca[3]);
+    accb[0] = fmaf(fmaf(pb[c][0], 0x1p24f, x0), s2b.x, accb[0]);
+    accb[1] = fmaf(fmaf(pb[c][1], 0x1p24f, x1), s2b.x, accb[1]);
+    accb[2] = fmaf(fmaf(pb[c][2], 0x1p20f, x0), s2b.y, accb[2]);
+    accb[3] = fmaf(fmaf(pb[c][3], 0x1p20f, x1), s2b.y, accb[3]);
+  }
+}
+
 // n consecutive chunks (global chunk index cg0 + c) through w4n_smem_chunk; NT = 2 only
 // when the unit has > 8 tokens.
 template <int G>
