@@ -47,6 +47,7 @@ struct AttnArgs {
   int pgcap;                   // page indices a CTA may stage in shared memory
   int block_full;              // 1: every query row sees the whole block (no causal order inside it)
   int window;                  // > 0: row at position p sees keys > p - window only
+  int plog2;                   // log2(P) when P is a power of two, else -1
 };
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, bool f16) {
@@ -91,18 +92,28 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
   if (staged)
     for (int i = threadIdx.x; i < npg; i += blockDim.x) pg[i] = a.pages ? a.pages[b * a.max_pages + p0 + i] : b;
   __syncthreads();
+  // Rows are copied by warps, a row's 16-byte chunks by lanes: a lane's row offset is
+  // computed once per row, with a shift and a mask for a power-of-two page size (the
+  // row loops are unrolled, so the page-table reads of a warp's rows overlap).
+  constexpr int CPR = D / 8;      // 16-byte chunks of one row
+  constexpr int RPI = 32 / CPR;   // rows one warp instruction covers
+  const int rsub = lane / CPR, cc = (lane % CPR) * 8;
+  auto key_off = [&](int t) -> int64_t {
+    const int pi = a.plog2 >= 0 ? (t >> a.plog2) : t / a.P;
+    const int ps = t - pi * a.P;
+    const int page = staged ? pg[pi - p0] : (a.pages ? a.pages[b * a.max_pages + pi] : b);
+    return ((static_cast<int64_t>(page) * a.Hkv + kvh) * a.P + ps) * D;
+  };
   // K/V tile t0.. -> stage st (keys past k1 zero-filled)
   auto load_tile = [&](int st, int t0) {
     ET* kd = ksm + st * 2 * ATT_KT * XS;
     ET* vd = kd + ATT_KT * XS;
-    for (int i = threadIdx.x; i < ATT_KT * (D / 8); i += blockDim.x) {
-      const int r = i / (D / 8), c = (i % (D / 8)) * 8;
+#pragma unroll 8
+    for (int r = warp * RPI + rsub; r < ATT_KT; r += nwarps * RPI) {
       const bool valid = t0 + r < k1;
-      const int t = valid ? t0 + r : k0;
-      const int page = staged ? pg[t / a.P - p0] : (a.pages ? a.pages[b * a.max_pages + t / a.P] : b);
-      const int64_t off = ((static_cast<int64_t>(page) * a.Hkv + kvh) * a.P + t % a.P) * D + c;
-      cp_async16(kd + r * XS + c, a.k + off, valid);
-      cp_async16(vd + r * XS + c, a.v + off, valid);
+      const int64_t off = key_off(valid ? t0 + r : k0) + cc;
+      cp_async16(kd + r * XS + cc, a.k + off, valid);
+      cp_async16(vd + r * XS + cc, a.v + off, valid);
     }
   };
   const int ntiles = (k1 - k0 + ATT_KT - 1) / ATT_KT;
@@ -120,12 +131,12 @@ __global__ void __launch_bounds__(256) attn_split_kernel(AttnArgs<ET> a) {
     cp_async_commit();
   }
   // Q rows -> smem (row r: head kvh*G + (row0+r)/S, position (row0+r)%S)
-  for (int i = threadIdx.x; i < nwarps * 16 * (D / 8); i += blockDim.x) {
-    const int r = i / (D / 8), c = (i % (D / 8)) * 8;
+#pragma unroll 4
+  for (int r = warp * RPI + rsub; r < nwarps * 16; r += nwarps * RPI) {
     const bool valid = r < nrows;
     const int rr = row0 + (valid ? r : 0);
     const int h = kvh * G + rr / a.S, s = rr % a.S;
-    cp_async16(qsm + r * XS + c, a.q + b * a.qb + h * a.qh + s * a.qs + c, valid);
+    cp_async16(qsm + r * XS + cc, a.q + b * a.qb + h * a.qh + s * a.qs + cc, valid);
   }
   cp_async_commit();
   cp_async_wait<0>();
@@ -435,6 +446,7 @@ static int launch_attn(AttnArgs<ET> a, ET* out, int64_t ob, int64_t oh, int64_t 
   const size_t smem = (static_cast<size_t>(ATT_MAXROWS) + ATT_NST * 2 * ATT_KT) * (D + 8) * sizeof(ET) +
                      ATT_PGCAP * sizeof(int);
   a.pgcap = ATT_PGCAP;
+  a.plog2 = (a.P > 0 && (a.P & (a.P - 1)) == 0) ? __builtin_ctz(static_cast<unsigned>(a.P)) : -1;
   static std::once_flag once;
   static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
