@@ -299,6 +299,15 @@ __global__ void attn_combine_kernel(const float* __restrict__ opart, const float
   const int nsp = (qpos + S + kc - 1) / kc;
   const int64_t row = (static_cast<int64_t>(b) * H + h) * S + s;   // row index within one split
   const int64_t split_stride = static_cast<int64_t>(B) * H * S;
+  // the first PRE splits' partials of this thread's column, requested now, while warp 0
+  // turns the (max, sum) pairs into weights: one load round trip instead of several
+  constexpr int PRE = 32;
+  float pre[PRE];
+  if (ONE) {
+    const float* op = opart + row * D + threadIdx.x;
+#pragma unroll
+    for (int sp = 0; sp < PRE; ++sp) pre[sp] = (sp < nsp && threadIdx.x < D) ? op[sp * split_stride * D] : 0.f;
+  }
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float m[2], l[2];
@@ -325,8 +334,17 @@ __global__ void attn_combine_kernel(const float* __restrict__ opart, const float
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float acc = 0.f;
     const float* op = opart + row * D + d;
+    int sp0 = 0;
+    if (ONE) {   // d == threadIdx.x: the prefetched splits first, in split order
+#pragma unroll
+      for (int sp = 0; sp < PRE; ++sp) {
+        const float w = sp < nsp ? s_w[sp] : 0.f;
+        if (w != 0.f) acc += w * pre[sp];
+      }
+      sp0 = PRE;
+    }
 #pragma unroll 8
-    for (int sp = 0; sp < nsp; ++sp) {
+    for (int sp = sp0; sp < nsp; ++sp) {
       const float w = s_w[sp];
       const float v = op[sp * split_stride * D];
       if (w != 0.f) acc += w * v;
