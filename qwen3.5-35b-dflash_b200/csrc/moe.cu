@@ -26,6 +26,7 @@
 // heap fallback) run on lane 0.  Values compared are the bf16 router logits, which
 // order exactly as torch's fp32 probabilities (exp is monotone; equal logits give
 // equal probabilities).
+#include <cooperative_groups.h>
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -35,6 +36,8 @@
 #include "umma.cuh"
 
 namespace qw {
+
+namespace cg = cooperative_groups;
 
 // ------------------------------------------------------------------ route workspace
 struct RouteView {
@@ -2277,9 +2280,17 @@ __global__ void moe_combine_kernel(const float* __restrict__ part, void* ws, ET*
 // (ascending expert, rounding at each add, then the gated shared expert), then
 // normed[t] = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * bf16(gamma + 1)) as
 // residual_norm_kernel, and the optional feature tap (h, or the normed row).
-// One CTA per token; each thread owns runs of 4 columns (16-byte loads of the fp32
-// expert outputs, all k + 1 slots of a run issued before the ordered sum).
-constexpr int CN_THREADS = 512;
+// A cluster of CN_SPLIT CTAs per token (64 SMs at T = 16 instead of 16: one CTA per
+// token kept only 16 SMs' worth of loads in flight); thread g = rank * CN_THREADS + tid of
+// the token's cluster owns runs of 4 columns (16-byte loads of the fp32 expert outputs,
+// all k + 1 slots of a run issued before the ordered sum).  The sum of squares is reduced
+// as block_sum reduces one CN_TOTAL-thread block -- each warp's tree, then one tree over
+// the warp sums in warp order, gathered from the cluster through distributed shared
+// memory -- so the norm has the bits of a one-CTA-per-token kernel.
+constexpr int CN_THREADS = 128;
+constexpr int CN_SPLIT = 4;
+constexpr int CN_TOTAL = CN_THREADS * CN_SPLIT;
+static_assert(CN_TOTAL / 32 <= 32, "the warp sums of a token fit one warp");
 
 // Expert-parallel form (ep.window set): the expert outputs are the bf16 rows the expert
 // owners stored into this rank's window (routed pair p = t k + s at back row p, the
@@ -2298,12 +2309,15 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     __nv_bfloat16* __restrict__ tap, int64_t ldf, int tap_normed, EpRecv ep) {
   __shared__ int s_slot[KMAX];
   __shared__ float s_w[KMAX];
-  __shared__ float red[32];
+  __shared__ float red[CN_TOTAL / 32];
+  cluster_arrive_relaxed();   // the peers' shared memory is written only after every CTA started
+  const int rank = blockIdx.x % CN_SPLIT;
+  const int g = rank * CN_THREADS + threadIdx.x;   // thread index within the token's cluster
   // before the wait: everything but the expert outputs -- the routing (from the route
   // kernel), the residual row (from the mixer's projection) and the norm weight are
   // older than the predecessor (the down projection)
   const RouteView rv = route_view(ws, T, E, k);
-  const int t = blockIdx.x;
+  const int t = blockIdx.x / CN_SPLIT;
   if (threadIdx.x < k) {
     const int e = rv.topk_idx[t * k + threadIdx.x];
     int rank = 0;
@@ -2313,11 +2327,11 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
   }
   const float sg = has_shared ? rv.shared_gate[t] : 0.f;
   __nv_bfloat16* h = hidden + static_cast<int64_t>(t) * H;
-  const bool one = H <= 4 * CN_THREADS;   // each thread at most one 4-column chunk
+  const bool one = H <= 4 * CN_TOTAL;   // each thread at most one 4-column chunk
   uint2 h0 = make_uint2(0u, 0u), g0 = make_uint2(0u, 0u), n0 = make_uint2(0u, 0u);
-  if (one && 4 * static_cast<int>(threadIdx.x) < H) {
-    h0 = *reinterpret_cast<const uint2*>(h + 4 * threadIdx.x);
-    g0 = *reinterpret_cast<const uint2*>(gamma + 4 * threadIdx.x);
+  if (one && 4 * g < H) {
+    h0 = *reinterpret_cast<const uint2*>(h + 4 * g);
+    g0 = *reinterpret_cast<const uint2*>(gamma + 4 * g);
   }
   pdl_wait();
   pdl_trigger();
@@ -2338,7 +2352,7 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
     return make_float4(a.x, a.y, b.x, b.y);
   };
-  for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
+  for (int c = 4 * g; c < H; c += 4 * CN_TOTAL) {
     float4 y[KMAX + 1];
     if (ep.window) {
 #pragma unroll
@@ -2381,9 +2395,21 @@ __global__ void __launch_bounds__(CN_THREADS) moe_combine_norm_kernel(
     const float2 f01 = __bfloat1622float2(n01), f23 = __bfloat1622float2(n23);
     ss += f01.x * f01.x + f01.y * f01.y + f23.x * f23.x + f23.y * f23.y;
   }
-  ss = block_sum(ss, red);
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    ss = warp_sum(ss);
+    cluster_wait();
+    if (lane == 0) {
+      cg::cluster_group cl = cg::this_cluster();
+#pragma unroll
+      for (int r = 0; r < CN_SPLIT; ++r) cl.map_shared_rank(red, r)[rank * (CN_THREADS / 32) + warp] = ss;
+    }
+    cg::this_cluster().sync();   // every warp sum has landed; no peer writes after this
+    float tt = lane < CN_TOTAL / 32 ? red[lane] : 0.f;
+    ss = warp_sum(tt);
+  }
   const float inv = rsqrtf(ss / H + eps);
-  for (int c = 4 * threadIdx.x; c < H; c += 4 * CN_THREADS) {
+  for (int c = 4 * g; c < H; c += 4 * CN_TOTAL) {
     const uint2 hraw = one ? n0 : *reinterpret_cast<const uint2*>(h + c);
     const uint2 graw = one ? g0 : *reinterpret_cast<const uint2*>(gamma + c);
     const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&hraw);
@@ -2883,12 +2909,25 @@ static int combine_norm_entry(void* workspace, void* hidden, int64_t tokens, int
   auto* np_ = static_cast<__nv_bfloat16*>(normed);
   auto* tp = static_cast<__nv_bfloat16*>(tap);
   const float* part = w.part;
-  if (k <= 8)
-    QW_LAUNCH_PDL("moe combine_norm", moe_combine_norm_kernel<8>, dim3(T), dim3(CN_THREADS), 0, s, part, w.route, hp,
-                  T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed, ep_recv);
-  else
-    QW_LAUNCH_PDL("moe combine_norm", moe_combine_norm_kernel<16>, dim3(T), dim3(CN_THREADS), 0, s, part, w.route,
-                  hp, T, H, E, k, has_shared, gp, np_, eps, tp, ldf, tap_normed, ep_recv);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(T * CN_SPLIT);
+  cfg.blockDim = dim3(CN_THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CN_SPLIT;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = k <= 8 ? cudaLaunchKernelEx(&cfg, moe_combine_norm_kernel<8>, part, w.route, hp, T, H, E, k,
+                                                    has_shared, gp, np_, eps, tp, ldf, tap_normed, ep_recv)
+                               : cudaLaunchKernelEx(&cfg, moe_combine_norm_kernel<16>, part, w.route, hp, T, H, E, k,
+                                                    has_shared, gp, np_, eps, tp, ldf, tap_normed, ep_recv);
+  if (e != cudaSuccess) return cuda_status(e, "moe combine_norm");
   return QW_OK;
 }
 
