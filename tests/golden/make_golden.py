@@ -14,6 +14,11 @@ Fixtures:
   draft.npz           the reference's DFlashDraftModel (bf16) of the tiny draft
                       configuration: context features -> draft hidden rows and the
                       proposals of the target's lm_head, for two context lengths.
+  binding_trace.npz   every call the reference's FusedTargetModel makes through the
+                      reference's ModuleFusedOps on the tiny configuration (a 16-token
+                      prefill and one decode step), recorded at the adapter-module
+                      boundary: op name, arguments (weights by name) and the reference
+                      backend's outputs; replayed through qwen35_dflash_b200.fused_ops.
   original/           two small shards in the original group-256 quantised layout
                       (data-0000{1,2}.safetensors, written here) and what the
                       reference's OriginalQuantWeights / canonicalkeys make of them
@@ -21,7 +26,8 @@ Fixtures:
                       logical int4 values and scales of each tensor).
 
 Usage:  QW_REFERENCE=<reference checkout> python tests/golden/make_golden.py
-        (QW_GOLDEN_ONLY=draft: only draft.npz; =original: only original/)
+        (QW_GOLDEN_ONLY=draft: only draft.npz; =original: only original/;
+         =binding: only binding_trace.npz)
 """
 from __future__ import annotations
 
@@ -130,6 +136,73 @@ def make_topk():
         out[f"p_{e}_{k}"] = probs.numpy()
         out[f"i_{e}_{k}"] = idx.numpy().astype(np.int16)
     np.savez_compressed(os.path.join(HERE, "topk.npz"), **out)
+
+
+def tiny_weights():
+    """The tiny target's fp16 weights as the reference model takes them (W4 matrices
+    quantised and dequantised); tests/test_binding_replay_gpu.py rebuilds the same."""
+    sys.path.insert(0, ROOT)
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from qwen35_dflash_b200 import config as qcfg, synthetic
+    from oracle.numerics import quantize_w4, dequantize_w4
+    cfg = qcfg.TINY
+    raw = synthetic.init_weights(cfg, seed=17)
+    weights = {}
+    for name, value in raw.items():
+        if synthetic.is_w4(name):
+            q, s = quantize_w4(value, cfg.quant_group)
+            value = dequantize_w4(q, s, cfg.quant_group)
+        weights[name] = torch.from_numpy(value).to(torch.float16)
+    return cfg, weights
+
+
+def make_binding_trace(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops):
+    """Record the reference model's calls at the fused-ops module boundary."""
+    import json
+    import types
+    cfg, weights = tiny_weights()
+    calls, arrays, wmap = [], {}, {}
+
+    def enc(x):
+        if isinstance(x, torch.Tensor):
+            if id(x) in wmap:
+                return {"weight": wmap[id(x)]}
+            key = f"a{len(arrays):04d}"
+            arrays[key] = x.detach().cpu().float().numpy() if x.dtype == torch.bfloat16 else x.detach().cpu().numpy()
+            return {"array": key, "dtype": str(x.dtype).replace("torch.", "")}
+        if isinstance(x, (tuple, list)):
+            return {"seq": [enc(v) for v in x]}
+        if x is None or isinstance(x, (bool, int, float)):
+            return {"value": x}
+        raise TypeError(f"unrecorded argument type {type(x)}")
+
+    rec = types.ModuleType("recording_fused_ops")
+    rec.FUSED_OPS_ABI = fused_ops.FUSED_OPS_ABI
+    rec.BACKEND_ID = "reference-recorder"
+    rec.IS_REFERENCE_BACKEND = True
+    for name in ModuleFusedOps.required_operations:
+        def wrapper(*args, _fn=getattr(fused_ops, name), _name=name, **kwargs):
+            entry = {"op": _name, "args": [enc(a) for a in args], "kwargs": {k: enc(v) for k, v in kwargs.items()}}
+            out = _fn(*args, **kwargs)
+            entry["out"] = enc(out)
+            calls.append(entry)
+            return out
+        setattr(rec, name, wrapper)
+    ops = ModuleFusedOps(rec, allow_reference=True)
+    model = FusedTargetModel(cfg.to_hf_text_config(), weights, feature_layers=cfg.feature_layers,
+                             ops=ops, recurrent_dtype=torch.float32)
+    for name in model._weight_names:
+        wmap[id(model.weight(name))] = name
+    prompt = np.random.default_rng(23).integers(0, cfg.vocab_size, 16).tolist()
+    session = FusedTargetSession(model)
+    session.prefill(prompt)
+    first = session.next_token
+    session.step(first)
+    np.savez_compressed(os.path.join(HERE, "binding_trace.npz"), calls=np.asarray(json.dumps(calls)),
+                        prompt=np.asarray(prompt, np.int32),
+                        next_tokens=np.asarray([first, session.next_token], np.int32), **arrays)
+    print("binding trace:", len(calls), "calls,", len(arrays), "arrays")
 
 
 def make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops):
@@ -304,10 +377,14 @@ def main():
     if os.environ.get("QW_GOLDEN_ONLY") == "original":
         make_original()
         return
+    if os.environ.get("QW_GOLDEN_ONLY") == "binding":
+        make_binding_trace(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops)
+        return
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     make_ops(fused_ops)
     make_topk()
     make_tiny_session(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops)
+    make_binding_trace(ModuleFusedOps, FusedTargetModel, FusedTargetSession, fused_ops)
     make_draft()
     make_original()
     for name in sorted(os.listdir(HERE)):
