@@ -47,7 +47,7 @@ METRIC = "verify tok/s & step latency (block 16, W4 MoE+GDN); % HBM roofline"
 # DRAM bytes (read + write) of one moe_up_bulk_kernel launch, from one ncu capture of the
 # same launch (16 tokens of N(0,1) router logits, seed 17 -> 103 active experts; metrics
 # dram__bytes_read.sum + dram__bytes_write.sum): ncu cannot run inside the timed bench
-MOE_UP_NCU_TRAFFIC = {"bytes": 112_579_584 + 3_767_552, "active": 103,
+MOE_UP_NCU_TRAFFIC = {"bytes": 112_598_016 + 3_043_840, "active": 103,
                       "source": "ncu capture of moe_up_bulk_kernel on the bench routing (103 active experts), "
                                 "dram__bytes_read.sum + dram__bytes_write.sum"}
 
