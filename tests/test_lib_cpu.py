@@ -119,6 +119,51 @@ def test_fused_ops_module_binds_like_the_reference_adapter():
         assert callable(getattr(fused_ops, name))
 
 
+def test_binding_trace_fixture_is_complete(golden):
+    """The recorded reference calls (tests/golden/binding_trace.npz) that the GPU replay
+    test drives through the module: every operator of the adapter contract occurs, every
+    argument resolves (a recorded array, or a weight of the tiny target by name, with
+    the shape the call needs), and the decode step came after the prefill."""
+    import json
+    from qwen35_dflash_b200 import config as qcfg, synthetic
+    d = golden("binding_trace.npz")
+    calls = json.loads(str(d["calls"]))
+    ops = [c["op"] for c in calls]
+    assert set(ops) == {"rms_norm", "conv_state_update", "causal_conv1d", "chunk_gated_delta_rule",
+                        "cache_update", "attention", "moe"}
+    shapes = {k: v.shape for k, v in synthetic.init_weights(qcfg.TINY, seed=17).items()}
+    seen = set()
+
+    def check(e):
+        if "weight" in e:
+            assert e["weight"] in shapes, e["weight"]
+            seen.add(e["weight"])
+        elif "array" in e:
+            assert e["array"] in d.files and e["dtype"] in ("float16", "bfloat16", "float32", "int16", "int32", "int64")
+        elif "seq" in e:
+            for x in e["seq"]:
+                check(x)
+        else:
+            assert "value" in e
+    for c in calls:
+        for a in c["args"]:
+            check(a)
+        for v in c["kwargs"].values():
+            check(v)
+        check(c["out"])
+    # the MoE calls pass the router and expert banks of every MoE layer by name
+    moe = [c for c in calls if c["op"] == "moe"]
+    assert len(moe) == 2 * qcfg.TINY.num_hidden_layers
+    e, i, h = qcfg.TINY.num_experts, qcfg.TINY.moe_intermediate_size, qcfg.TINY.hidden_size
+    for c in moe:
+        assert shapes[c["args"][2]["weight"]] == (e, 2 * i, h)
+        assert shapes[c["args"][3]["weight"]] == (e, h, i)
+    # attention: the prefill sees keys from 0, the decode step after the 16 prompt tokens
+    starts = [c["kwargs"]["query_start"]["value"] for c in calls if c["op"] == "attention"]
+    assert starts == [0, 16]
+    assert len(d["next_tokens"]) == 2
+
+
 def test_fused_ops_rejects_cpu_tensors():
     from qwen35_dflash_b200 import fused_ops
     x = torch.zeros(2, 8)
