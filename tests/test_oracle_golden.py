@@ -1,5 +1,6 @@
 """Pin the CPU oracle to outputs of the reference itself (fixtures from make_golden.py)."""
 import numpy as np
+import torch
 import pytest
 
 from oracle import fused_ops_np as F
@@ -66,6 +67,25 @@ def test_topk_matches_torch(golden):
             _, e, k = key.split("_")
             got = topk_indices(d[key], int(k))
             np.testing.assert_array_equal(got, d[f"i_{e}_{k}"].astype(np.int64), err_msg=key)
+
+
+@pytest.mark.parametrize("n,k", [(16, 4), (40, 6), (64, 8), (128, 8), (256, 8), (257, 8), (256, 2),
+                                 (512, 8), (1024, 8), (96, 17)])
+def test_topk_matches_live_torch_topk(n, k):
+    """The oracle's restatement of torch.topk's CPU tie order against torch.topk itself
+    (this process's torch), on seeded rows dense in ties: small integers, bf16-rounded
+    normals and signed zeros; both of ATen's paths (nth_element + sort when k * 64 > n,
+    partial_sort otherwise)."""
+    g = torch.Generator().manual_seed(n * 31 + k)
+    rows = [torch.randint(-3, 4, (24, n), generator=g).float(),
+            torch.randn(24, n, generator=g).to(torch.bfloat16).float(),
+            torch.where(torch.rand(8, n, generator=g) < 0.3, torch.ones(8, n),
+                        torch.where(torch.rand(8, n, generator=g) < 0.5, torch.full((8, n), -0.0), torch.zeros(8, n)))]
+    assert torch.signbit(rows[2]).any() and (rows[2] == 0).any()
+    for x in rows:
+        want = torch.topk(x, k, dim=-1).indices.numpy()
+        got = topk_indices(x.numpy(), k)
+        np.testing.assert_array_equal(got, want, err_msg=f"n={n} k={k}")
 
 
 def test_quantizer_roundtrip():
