@@ -671,6 +671,57 @@ def run_prefill(args):
     print(json.dumps(out), flush=True)
 
 
+def run_dflash(args):
+    """The greedy DFlash loop on the full target and the full draft (1 GPU, random weights
+    of both architectures): a --ctx-token prompt prefilled in 64-token chunks, then the
+    DFlash step -- the draft's proposals, the target's block verify + accept + commit, the
+    draft's context extension -- captured as one CUDA graph and replayed --steps times
+    after --warmup replays, CUDA events around the replays; then the target's own verify
+    step (its graph) timed the same way, so that the difference is the draft's share.
+    With random weights the proposals are almost never accepted: the step latency is the
+    figure that carries over to trained weights, where a step emits 1 + accepted tokens."""
+    import torch
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from qwen35_dflash_b200 import config, engine as E, synthetic
+    from qwen35_dflash_b200.dflash import DFlash
+    from qwen35_dflash_b200.draft import DraftEngine
+    dev = torch.device("cuda")
+    cfg, dcfg = config.QWEN35_35B_A3B, config.QWEN35_DFLASH_DRAFT
+    n, k, w = args.ctx, args.steps, args.warmup
+    cap = n + 16 * (2 * (k + w) + 8) + 128
+    te = E.TargetEngine(cfg, E.weights_random(cfg, seed=2, device=dev), batch=1, block=16, capacity=cap, device=dev)
+    df = DFlash(te, DraftEngine(dcfg, te, synthetic.init_draft_weights(dcfg), device=dev))
+    gen = torch.Generator().manual_seed(5)
+    df.prefill(torch.randint(0, cfg.vocab_size, (n,), generator=gen, dtype=torch.int32).tolist())
+    df.capture()
+
+    def timed(replay):
+        for _ in range(w):
+            replay()
+        torch.cuda.synchronize()
+        q0 = int(te.qpos[0].item())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(k):
+            replay()
+        e1.record()
+        e1.synchronize()
+        te.raise_on_wait_timeout()
+        return e0.elapsed_time(e1) / k, (int(te.qpos[0].item()) - q0) / k
+
+    ms, tok = timed(df.graph.replay)
+    te.capture()
+    ms_verify, _ = timed(te.replay)
+    print(json.dumps({
+        "metric": "DFlash step latency (draft propose + target block verify/accept/commit + draft extend), 1 GPU",
+        "ctx": n, "steps": k, "warmup": w, "ms_per_dflash_step": round(ms, 4),
+        "tokens_per_step": round(tok, 3), "tok_s": round(tok / ms * 1e3, 1),
+        "ms_per_verify_step": round(ms_verify, 4), "draft_ms_per_step": round(ms - ms_verify, 4),
+        "data": "random-init weights of the target and draft architectures: proposals ~never accepted; "
+                "a trained draft emits 1 + accepted tokens per step"}), flush=True)
+
+
 def run_micro(args):
     """Benchmark configs 2 and 3 (one JSON line per point): the W4A16 grouped MoE
     (router logits given, softmax top-8 + shared expert, H 2048, 256 experts, I 512, g128,
@@ -837,6 +888,8 @@ def main():
     ap.add_argument("--kernel-reps", type=int, default=5)
     ap.add_argument("--micro", action="store_true",
                     help="benchmark configs 2 (W4A16 MoE, T 16/64/256) and 3 (GDN verify, B 1/8/32), one line each")
+    ap.add_argument("--dflash", action="store_true",
+                    help="time the DFlash step (draft + verify + extend) on the full target and draft (1 GPU)")
     ap.add_argument("--prefill", action="store_true",
                     help="prompt prefill tok/s: 64-token chunks (prefill engine) against 16-token blocks")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
@@ -856,6 +909,9 @@ def main():
         return
     if args.prefill:
         run_prefill(args)
+        return
+    if args.dflash:
+        run_dflash(args)
         return
     if args.warmup < 3:
         args.warmup = 3
